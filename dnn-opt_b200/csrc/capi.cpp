@@ -1,0 +1,564 @@
+// C ABI of libdnnopt_b200.so: argument validation, plan selection (with
+// optional autotune), workspace management, host-pointer staging and kernel
+// dispatch.  See include/dnnopt_b200.h for the contract of each entry point.
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "kernels.h"
+#include "plan.h"
+#include "runtime.h"
+
+using namespace dnnopt_b200;
+
+namespace {
+
+GemmArgs to_args(const dnnopt_gemm_desc* d, const void* A, const void* B, void* C) {
+    GemmArgs g;
+    g.M = d->M; g.N = d->N; g.K = d->K;
+    g.alpha = d->alpha; g.beta = d->beta;
+    g.A = A; g.lda = d->lda; g.a_trans = d->trans_a ? 1 : 0;
+    g.B = B; g.ldb = d->ldb; g.b_trans = d->trans_b ? 1 : 0;
+    g.C = C; g.ldc = d->ldc;
+    return g;
+}
+
+// B is always N x K for these kinds.
+bool b_is_nk(Kind k) { return k == Kind::S8S32 || k == Kind::E4M3BF16; }
+
+// Validates sizes, leading dimensions and pointers.  Returns SUCCESS with
+// *noop = true for the reference's silent early return (any of M, N, K == 0).
+int validate(Kind kind, const dnnopt_gemm_desc* d, const void* A, const void* B, const void* C,
+             bool* noop) {
+    *noop = false;
+    if (!d) return DNNOPT_STATUS_INVALID_VALUE;
+    if (d->M < 0 || d->N < 0 || d->K < 0) return DNNOPT_STATUS_INVALID_VALUE;
+    if (d->M == 0 || d->N == 0 || d->K == 0) { *noop = true; return DNNOPT_STATUS_SUCCESS; }
+    const bool ta = d->trans_a != 0;
+    const bool tb = b_is_nk(kind) ? true : d->trans_b != 0;
+    if (d->lda < (ta ? d->M : d->K)) return DNNOPT_STATUS_INVALID_VALUE;
+    if (d->ldb < (tb ? d->K : d->N)) return DNNOPT_STATUS_INVALID_VALUE;
+    if (d->ldc < d->N) return DNNOPT_STATUS_INVALID_VALUE;
+    if (!A || !B || !C) return DNNOPT_STATUS_INVALID_VALUE;
+    return DNNOPT_STATUS_SUCCESS;
+}
+
+DeviceInfo info_of(const DeviceContext* ctx) {
+    DeviceInfo i;
+    if (ctx) { i.num_sms = ctx->num_sms; i.have_device = true; }
+    return i;
+}
+
+int vec_of(const Plan& p) {
+    return p.kernel == KernelId::GemvKn ? p.kn.vec4 : p.nk.vec;
+}
+
+In in_a(Kind k) {
+    switch (k) {
+        case Kind::BF16F32: return In::BF16;
+        case Kind::F32BF16R: return In::F32R;
+        case Kind::RE4E5: return In::RE4;
+        case Kind::RE5E5: return In::RE5;
+        default: return In::F32;
+    }
+}
+In in_b(Kind k) {
+    switch (k) {
+        case Kind::BF16F32: return In::BF16;
+        case Kind::F32BF16R: return In::F32R;
+        case Kind::RE4E5:
+        case Kind::RE5E5: return In::RE5;
+        default: return In::F32;
+    }
+}
+DotKind dot_kind(Kind k) {
+    switch (k) {
+        case Kind::S8S32: return DotKind::S8S32;
+        case Kind::F32S8Q: return DotKind::S8DQ;
+        case Kind::E4M3BF16: return DotKind::E4M3;
+        default: return DotKind::F32;
+    }
+}
+
+// Launches one plan.  `scales`: per-row scales (e4m3) or {sA, sB} (int8 dequant).
+int launch_plan(Kind kind, const GemmArgs& g, const Plan& p, const float* scales,
+                DeviceContext* ctx, cudaStream_t s) {
+    int inj = check_injected_fault(2);
+    if (inj != DNNOPT_STATUS_SUCCESS) return set_status(inj);
+    cudaError_t e = cudaSuccess;
+    Workspace* w = nullptr;
+    int st;
+    switch (p.kernel) {
+        case KernelId::GemvKn: {
+            const size_t wsf = gemv_kn_ws_floats(p.kn, g.N);
+            st = ensure_workspace(ctx, s, wsf, static_cast<size_t>(gemv_kn_tiles(g.N)), 0, &w);
+            if (st != DNNOPT_STATUS_SUCCESS) return st;
+            e = launch_gemv_kn(in_a(kind), in_b(kind), g, p.kn, w->ws, w->counters, s);
+            note_launch();
+            break;
+        }
+        case KernelId::GemvNk:
+            e = launch_gemv_nk(dot_kind(kind), g, p.nk, scales, s);
+            note_launch();
+            break;
+        case KernelId::GemvNkRows: {
+            const size_t ea = static_cast<size_t>(elem_bytes_a(kind));
+            for (int m0 = 0; m0 < g.M && e == cudaSuccess; m0 += 8) {
+                GemmArgs r = g;
+                r.M = g.M - m0 < 8 ? g.M - m0 : 8;
+                r.A = static_cast<const char*>(g.A) +
+                      (g.a_trans ? static_cast<size_t>(m0) : static_cast<size_t>(m0) * g.lda) * ea;
+                const size_t ec = (kind == Kind::E4M3BF16) ? 2 : 4;
+                r.C = static_cast<char*>(g.C) + static_cast<size_t>(m0) * g.ldc * ec;
+                GemvNkPlan rp = p.nk;
+                rp.mt = r.M <= 1 ? 1 : (r.M <= 2 ? 2 : (r.M <= 4 ? 4 : 8));
+                e = launch_gemv_nk(dot_kind(kind), r, rp, scales, s);
+                note_launch();
+            }
+            break;
+        }
+        case KernelId::TileF32:
+            if (kind == Kind::E4M3BF16 || kind == Kind::S8S32 || kind == Kind::F32S8Q)
+                return set_status(DNNOPT_STATUS_NOT_SUPPORTED);
+            e = launch_gemm_tile_f32(in_a(kind), in_b(kind), g, s);
+            note_launch();
+            break;
+        case KernelId::TileS8:
+            e = launch_gemm_tile_s8(dot_kind(kind), g, scales, s);
+            note_launch();
+            break;
+        case KernelId::Bf16Tc:
+            st = ensure_workspace(ctx, s, 0, 0, 0, &w);
+            if (st != DNNOPT_STATUS_SUCCESS) return st;
+            e = launch_gemm_bf16_tc(g, ctx->num_sms, w->err, s);
+            note_launch();
+            break;
+    }
+    return cuda_status(e);
+}
+
+// Times one plan (beta forced to 0, output into `scratch`), microseconds.
+float time_plan(Kind kind, GemmArgs g, const Plan& p, const float* scales, DeviceContext* ctx,
+                cudaStream_t s, void* scratch) {
+    g.beta = 0.0f;
+    g.C = scratch;
+    g.ldc = g.N;
+    cudaEvent_t a, b;
+    if (cudaEventCreate(&a) != cudaSuccess) return 1e30f;
+    if (cudaEventCreate(&b) != cudaSuccess) { cudaEventDestroy(a); return 1e30f; }
+    float best = 1e30f;
+    if (launch_plan(kind, g, p, scales, ctx, s) == DNNOPT_STATUS_SUCCESS) {
+        for (int r = 0; r < 3; ++r) {
+            cudaEventRecord(a, s);
+            for (int i = 0; i < 4; ++i) launch_plan(kind, g, p, scales, ctx, s);
+            cudaEventRecord(b, s);
+            if (cudaEventSynchronize(b) != cudaSuccess) break;
+            float ms = 0.0f;
+            cudaEventElapsedTime(&ms, a, b);
+            if (ms * 250.0f < best) best = ms * 250.0f;
+        }
+    }
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    cudaGetLastError();
+    return best;
+}
+
+Plan get_plan(Kind kind, const GemmArgs& g, DeviceContext* ctx, cudaStream_t s,
+              const float* scales) {
+    const DeviceInfo info = info_of(ctx);
+    Plan h = heuristic_plan(kind, g, info);
+    const bool tunable = h.kernel == KernelId::GemvKn || h.kernel == KernelId::GemvNk;
+    if (!tunable) return h;
+    const uint64_t key = plan_key(kind, g, vec_of(h));
+    Plan c = h;
+    if (cache_lookup(key, &c) && c.kernel == h.kernel) {
+        // Layout-derived fields come from the current call.
+        if (c.kernel == KernelId::GemvKn) c.kn.vec4 = h.kn.vec4;
+        else c.nk.vec = h.nk.vec;
+        return c;
+    }
+    if (!autotune_enabled() || !ctx) return h;
+
+    // Candidates around the heuristic choice.
+    Plan cands[4];
+    int nc = 0;
+    if (h.kernel == KernelId::GemvKn) {
+        const int s0 = h.kn.splits;
+        const int tries[4] = {s0, s0 / 2, s0 * 2, 1};
+        for (int t : tries) {
+            if (t < 1) continue;
+            Plan q = h;
+            q.kn = kn_plan_for(kind, g, info, t);
+            bool dup = false;
+            for (int i = 0; i < nc; ++i) dup = dup || cands[i].kn.splits == q.kn.splits;
+            if (!dup) cands[nc++] = q;
+        }
+    } else {
+        const int g0 = h.nk.grid;
+        const int tries[3] = {g0, g0 / 2, g0 * 2};
+        for (int t : tries) {
+            if (t < 1) continue;
+            Plan q = h;
+            q.nk = nk_plan_for(kind, g, info, t);
+            bool dup = false;
+            for (int i = 0; i < nc; ++i) dup = dup || cands[i].nk.grid == q.nk.grid;
+            if (!dup) cands[nc++] = q;
+        }
+    }
+    const size_t out_bytes = static_cast<size_t>(g.M) * g.N * 4;
+    Workspace* w = nullptr;
+    if (ensure_workspace(ctx, s, 0, 0, out_bytes, &w) != DNNOPT_STATUS_SUCCESS) return h;
+    float best_t = 1e30f;
+    Plan best = h;
+    for (int i = 0; i < nc; ++i) {
+        float t = time_plan(kind, g, cands[i], scales, ctx, s, w->quant);
+        if (t < best_t) { best_t = t; best = cands[i]; }
+    }
+    best.tuned = true;
+    cache_store(key, best, best_t);
+    return best;
+}
+
+// Device-pointer dispatch for one call (validation already done, not a no-op).
+int run_device(Kind kind, const GemmArgs& g0, const float* scales, DeviceContext* ctx,
+               cudaStream_t s) {
+    GemmArgs g = g0;
+    if (b_is_nk(kind)) g.b_trans = 1;
+    if (kind == Kind::F32S8Q) {
+        // Quantise (absmax -> scales -> int8 copies), then the int8 GEMM with a
+        // dequantising epilogue.
+        const size_t qa = static_cast<size_t>(g.M) * g.K;
+        const size_t qb = static_cast<size_t>(g.N) * g.K;
+        Workspace* w = nullptr;
+        int st = ensure_workspace(ctx, s, 0, 0, qa + qb + 16, &w);
+        if (st != DNNOPT_STATUS_SUCCESS) return st;
+        int inj = check_injected_fault(2);
+        if (inj != DNNOPT_STATUS_SUCCESS) return set_status(inj);
+        int8_t* q = static_cast<int8_t*>(w->quant);
+        cudaError_t e = launch_absmax2(g, w->absmax, s);
+        note_launch();
+        if (e == cudaSuccess) { e = launch_quantize_s8(g, w->absmax, w->scales, q, q + qa, s); note_launch(); }
+        if (e != cudaSuccess) return cuda_status(e);
+        GemmArgs gq = g;
+        gq.A = q; gq.lda = g.K; gq.a_trans = 0;
+        gq.B = q + qa; gq.ldb = g.K; gq.b_trans = 1;
+        Plan p = get_plan(kind, gq, ctx, s, w->scales);
+        return launch_plan(kind, gq, p, w->scales, ctx, s);
+    }
+    Plan p = get_plan(kind, g, ctx, s, scales);
+    return launch_plan(kind, g, p, scales, ctx, s);
+}
+
+int device_entry(Kind kind, const dnnopt_gemm_desc* d, const void* A, const void* B, void* C,
+                 const float* scales, void* stream) {
+    bool noop;
+    int st = validate(kind, d, A, B, C, &noop);
+    if (st != DNNOPT_STATUS_SUCCESS || noop) return set_status(st);
+    if (kind == Kind::E4M3BF16 && !scales) return set_status(DNNOPT_STATUS_INVALID_VALUE);
+    DeviceContext* ctx = current_context(&st);
+    if (!ctx) return st;
+    return run_device(kind, to_args(d, A, B, C), scales, ctx, static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------------------
+// Host-signature entry points: host or device pointers, synchronous.
+// ---------------------------------------------------------------------------
+struct Operand {
+    const void* user;
+    size_t bytes;     // span of the stored matrix in bytes
+    bool in, out;     // copied to / from the device
+};
+
+size_t span_bytes(int rows, int cols, int ld, size_t eb) {
+    if (rows <= 0 || cols <= 0) return 0;
+    return (static_cast<size_t>(rows - 1) * ld + cols) * eb;
+}
+
+int host_entry(Kind kind, const dnnopt_gemm_desc* d, const void* A, const void* B, void* C,
+               const float* scales) {
+    bool noop;
+    int st = validate(kind, d, A, B, C, &noop);
+    if (st != DNNOPT_STATUS_SUCCESS || noop) return set_status(st);
+    if (kind == Kind::E4M3BF16 && !scales) return set_status(DNNOPT_STATUS_INVALID_VALUE);
+    DeviceContext* ctx = current_context(&st);
+    if (!ctx) return st;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    cudaStream_t s = ctx->user_stream_set ? ctx->user_stream : ctx->default_stream;
+
+    const bool ta = d->trans_a != 0, tb = b_is_nk(kind) || d->trans_b != 0;
+    const size_t ea = (kind == Kind::F32 || kind == Kind::F32BF16R || kind == Kind::F32S8Q) ? 4
+                      : (kind == Kind::BF16F32 || kind == Kind::E4M3BF16) ? 2 : 1;
+    const size_t eb = (kind == Kind::F32 || kind == Kind::F32BF16R || kind == Kind::F32S8Q) ? 4
+                      : (kind == Kind::BF16F32) ? 2 : 1;
+    const size_t ec = (kind == Kind::S8S32) ? 4 : (kind == Kind::E4M3BF16 ? 2 : 4);
+    const bool reads_c = kind != Kind::S8S32 && kind != Kind::E4M3BF16 && d->beta != 0.0f;
+    Operand ops[4] = {
+        {A, ta ? span_bytes(d->K, d->M, d->lda, ea) : span_bytes(d->M, d->K, d->lda, ea), true, false},
+        {B, tb ? span_bytes(d->N, d->K, d->ldb, eb) : span_bytes(d->K, d->N, d->ldb, eb), true, false},
+        {C, span_bytes(d->M, d->N, d->ldc, ec), reads_c, true},
+        {scales, kind == Kind::E4M3BF16 ? static_cast<size_t>(d->N) * 4 : 0, true, false},
+    };
+    const void* dev[4] = {A, B, C, scales};
+    for (int i = 0; i < 4; ++i) {
+        if (!ops[i].user || ops[i].bytes == 0) continue;
+        if (classify_pointer(ops[i].user) == PtrKind::Device) continue;
+        void* buf = nullptr;
+        st = ensure_stage(ctx, i, ops[i].bytes, &buf);
+        if (st != DNNOPT_STATUS_SUCCESS) return st;
+        dev[i] = buf;
+        if (ops[i].in) {
+            int inj = check_injected_fault(3);
+            if (inj != DNNOPT_STATUS_SUCCESS) return set_status(inj);
+            cudaError_t e = cudaMemcpyAsync(buf, ops[i].user, ops[i].bytes, cudaMemcpyHostToDevice, s);
+            if (e != cudaSuccess) return cuda_status(e);
+        }
+    }
+    GemmArgs g = to_args(d, dev[0], dev[1], const_cast<void*>(dev[2]));
+    st = run_device(kind, g, static_cast<const float*>(dev[3]), ctx, s);
+    if (st != DNNOPT_STATUS_SUCCESS) {
+        cudaStreamSynchronize(s);
+        return set_status(st);
+    }
+    if (dev[2] != C) {
+        cudaError_t e = cudaMemcpyAsync(C, dev[2], ops[2].bytes, cudaMemcpyDeviceToHost, s);
+        if (e != cudaSuccess) return cuda_status(e);
+    }
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_status(e);
+    // Bounded in-kernel waits report through the stream's error word.
+    auto it = ctx->ws.find(s);
+    if (it != ctx->ws.end() && it->second.err) {
+        uint32_t code = 0;
+        e = cudaMemcpy(&code, it->second.err, sizeof(code), cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) return cuda_status(e);
+        if (code != 0) {
+            cudaMemset(it->second.err, 0, sizeof(code));
+            return set_status(DNNOPT_STATUS_KERNEL_TIMEOUT);
+        }
+    }
+    return set_status(DNNOPT_STATUS_SUCCESS);
+}
+
+dnnopt_gemm_desc make_desc(int M, int N, int K, float alpha, int lda, int ldb, float beta,
+                           int ldc) {
+    dnnopt_gemm_desc d;
+    d.M = M; d.N = N; d.K = K;
+    d.lda = lda; d.ldb = ldb; d.ldc = ldc;
+    d.alpha = alpha; d.beta = beta;
+    d.trans_a = 0; d.trans_b = 0;
+    return d;
+}
+
+int g_num_threads = 0;
+
+}  // namespace
+
+extern "C" {
+
+// ---- reference-signature (host or device pointers, synchronous) ----------
+int dnnopt_gemm_fp32(int M, int N, int K, float alpha, const float* A, int lda, const float* B,
+                     int ldb, float beta, float* C, int ldc) {
+    dnnopt_gemm_desc d = make_desc(M, N, K, alpha, lda, ldb, beta, ldc);
+    return host_entry(Kind::F32, &d, A, B, C, nullptr);
+}
+
+int dnnopt_gemm_bf16(int M, int N, int K, float alpha, const float* A, int lda, const float* B,
+                     int ldb, float beta, float* C, int ldc) {
+    dnnopt_gemm_desc d = make_desc(M, N, K, alpha, lda, ldb, beta, ldc);
+    return host_entry(Kind::F32BF16R, &d, A, B, C, nullptr);
+}
+
+int dnnopt_gemm_bf16_bf16bf16f32(int M, int N, int K, float alpha, const uint16_t* A, int lda,
+                                 const uint16_t* B, int ldb, float beta, float* C, int ldc) {
+    dnnopt_gemm_desc d = make_desc(M, N, K, alpha, lda, ldb, beta, ldc);
+    return host_entry(Kind::BF16F32, &d, A, B, C, nullptr);
+}
+
+int dnnopt_gemm_int8(int M, int N, int K, float alpha, const float* A, int lda, const float* B,
+                     int ldb, float beta, float* C, int ldc) {
+    dnnopt_gemm_desc d = make_desc(M, N, K, alpha, lda, ldb, beta, ldc);
+    return host_entry(Kind::F32S8Q, &d, A, B, C, nullptr);
+}
+
+int dnnopt_gemm_int8_int8int8int32(int M, int N, int K, const int8_t* A, int lda, const int8_t* B,
+                                   int ldb, int32_t* C, int ldc) {
+    dnnopt_gemm_desc d = make_desc(M, N, K, 1.0f, lda, ldb, 0.0f, ldc);
+    return host_entry(Kind::S8S32, &d, A, B, C, nullptr);
+}
+
+int dnnopt_gemm_fp8_e4m3(int M, int N, int K, float alpha, const uint8_t* A, int lda,
+                         const uint8_t* B, int ldb, float beta, float* C, int ldc) {
+    dnnopt_gemm_desc d = make_desc(M, N, K, alpha, lda, ldb, beta, ldc);
+    return host_entry(Kind::RE4E5, &d, A, B, C, nullptr);
+}
+
+int dnnopt_gemm_fp8_e5m2(int M, int N, int K, float alpha, const uint8_t* A, int lda,
+                         const uint8_t* B, int ldb, float beta, float* C, int ldc) {
+    dnnopt_gemm_desc d = make_desc(M, N, K, alpha, lda, ldb, beta, ldc);
+    return host_entry(Kind::RE5E5, &d, A, B, C, nullptr);
+}
+
+int dnnopt_gemm_fp8(int M, int N, int K, float alpha, const float* A, int lda, const float* B,
+                    int ldb, float beta, float* C, int ldc) {
+    dnnopt_gemm_desc d = make_desc(M, N, K, alpha, lda, ldb, beta, ldc);
+    bool noop;
+    int st = validate(Kind::F32, &d, A, B, C, &noop);
+    if (st != DNNOPT_STATUS_SUCCESS || noop) return set_status(st);
+    // Quantise with the reference codecs on the device, then gemm_fp8_e4m3.
+    DeviceContext* ctx = current_context(&st);
+    if (!ctx) return st;
+    const size_t qa = static_cast<size_t>(M) * K, qb = static_cast<size_t>(K) * N;
+    void* dA = nullptr;
+    void* dB = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        cudaStream_t s = ctx->user_stream_set ? ctx->user_stream : ctx->default_stream;
+        const void* src[2] = {A, B};
+        const size_t bytes[2] = {span_bytes(M, K, lda, 4), span_bytes(K, N, ldb, 4)};
+        for (int i = 0; i < 2; ++i) {
+            if (classify_pointer(src[i]) == PtrKind::Device) {
+                (i == 0 ? dA : dB) = const_cast<void*>(src[i]);
+                continue;
+            }
+            void* buf = nullptr;
+            st = ensure_stage(ctx, i, bytes[i], &buf);
+            if (st != DNNOPT_STATUS_SUCCESS) return st;
+            cudaError_t e = cudaMemcpyAsync(buf, src[i], bytes[i], cudaMemcpyHostToDevice, s);
+            if (e != cudaSuccess) return cuda_status(e);
+            (i == 0 ? dA : dB) = buf;
+        }
+        void* q = nullptr;
+        st = ensure_stage(ctx, 3, qa + qb, &q);
+        if (st != DNNOPT_STATUS_SUCCESS) return st;
+        GemmArgs g = to_args(&d, dA, dB, C);
+        cudaError_t e = launch_quantize_ref_fp8(g, static_cast<uint8_t*>(q),
+                                                static_cast<uint8_t*>(q) + qa, s);
+        note_launch();
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return cuda_status(e);
+        dA = q;
+        dB = static_cast<uint8_t*>(q) + qa;
+    }
+    // dA/dB are device buffers now (stage slot 3); the call below only stages C.
+    dnnopt_gemm_desc dq = make_desc(M, N, K, alpha, K, N, beta, ldc);
+    return host_entry(Kind::RE4E5, &dq, dA, dB, C, nullptr);
+}
+
+int dnnopt_has_fp8_support(void) { return 1; }
+
+int dnnopt_gemm_f32_desc(const dnnopt_gemm_desc* d, const float* A, const float* B, float* C) {
+    return host_entry(Kind::F32, d, A, B, C, nullptr);
+}
+
+int dnnopt_saxpy(int N, float alpha, const float* X, int incX, float* Y, int incY) {
+    if (N <= 0 || alpha == 0.0f) return set_status(DNNOPT_STATUS_SUCCESS);   // reference early return
+    if (!X || !Y || incX < 0 || incY < 0) return set_status(DNNOPT_STATUS_INVALID_VALUE);
+    int st;
+    DeviceContext* ctx = current_context(&st);
+    if (!ctx) return st;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    cudaStream_t s = ctx->user_stream_set ? ctx->user_stream : ctx->default_stream;
+    const size_t xb = (static_cast<size_t>(N - 1) * incX + 1) * 4;
+    const size_t yb = (static_cast<size_t>(N - 1) * incY + 1) * 4;
+    const float* dx = X;
+    float* dy = Y;
+    if (classify_pointer(X) == PtrKind::Host) {
+        void* b = nullptr;
+        if ((st = ensure_stage(ctx, 0, xb, &b)) != DNNOPT_STATUS_SUCCESS) return st;
+        cudaError_t e = cudaMemcpyAsync(b, X, xb, cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) return cuda_status(e);
+        dx = static_cast<const float*>(b);
+    }
+    if (classify_pointer(Y) == PtrKind::Host) {
+        void* b = nullptr;
+        if ((st = ensure_stage(ctx, 2, yb, &b)) != DNNOPT_STATUS_SUCCESS) return st;
+        cudaError_t e = cudaMemcpyAsync(b, Y, yb, cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) return cuda_status(e);
+        dy = static_cast<float*>(b);
+    }
+    cudaError_t e = launch_saxpy(N, alpha, dx, incX, dy, incY, s);
+    note_launch();
+    if (e == cudaSuccess && dy != Y) e = cudaMemcpyAsync(Y, dy, yb, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    return cuda_status(e);
+}
+
+int dnnopt_gemm_e4m3_bf16(int M, int N, int K, const uint16_t* A, int lda, const uint8_t* W,
+                          int ldw, const float* scale, uint16_t* C, int ldc) {
+    dnnopt_gemm_desc d = make_desc(M, N, K, 1.0f, lda, ldw, 0.0f, ldc);
+    return host_entry(Kind::E4M3BF16, &d, A, W, C, scale);
+}
+
+void dnnopt_gemm_set_num_threads(int n) { g_num_threads = n < 0 ? 0 : n; }
+int dnnopt_gemm_get_num_threads(void) { return g_num_threads > 0 ? g_num_threads : 1; }
+
+// ---- device-pointer entry points ------------------------------------------
+int dnnopt_cuda_gemm_f32(const dnnopt_gemm_desc* d, const float* A, const float* B, float* C,
+                         void* stream) {
+    return device_entry(Kind::F32, d, A, B, C, nullptr, stream);
+}
+int dnnopt_cuda_gemm_bf16f32(const dnnopt_gemm_desc* d, const uint16_t* A, const uint16_t* B,
+                             float* C, void* stream) {
+    return device_entry(Kind::BF16F32, d, A, B, C, nullptr, stream);
+}
+int dnnopt_cuda_gemm_f32_bf16round(const dnnopt_gemm_desc* d, const float* A, const float* B,
+                                   float* C, void* stream) {
+    return device_entry(Kind::F32BF16R, d, A, B, C, nullptr, stream);
+}
+int dnnopt_cuda_gemm_f32_s8quant(const dnnopt_gemm_desc* d, const float* A, const float* B,
+                                 float* C, void* stream) {
+    return device_entry(Kind::F32S8Q, d, A, B, C, nullptr, stream);
+}
+int dnnopt_cuda_gemm_s8s32(const dnnopt_gemm_desc* d, const int8_t* A, const int8_t* B,
+                           int32_t* C, void* stream) {
+    return device_entry(Kind::S8S32, d, A, B, C, nullptr, stream);
+}
+int dnnopt_cuda_gemm_e4m3bf16(const dnnopt_gemm_desc* d, const uint16_t* A, const uint8_t* W,
+                              const float* scale, uint16_t* C, void* stream) {
+    return device_entry(Kind::E4M3BF16, d, A, W, C, scale, stream);
+}
+int dnnopt_cuda_gemm_refe4m3_e5m2(const dnnopt_gemm_desc* d, const uint8_t* A, const uint8_t* B,
+                                  float* C, void* stream) {
+    return device_entry(Kind::RE4E5, d, A, B, C, nullptr, stream);
+}
+int dnnopt_cuda_gemm_refe5m2_e5m2(const dnnopt_gemm_desc* d, const uint8_t* A, const uint8_t* B,
+                                  float* C, void* stream) {
+    return device_entry(Kind::RE5E5, d, A, B, C, nullptr, stream);
+}
+
+// ---- plan / autotune --------------------------------------------------------
+int dnnopt_plan_describe(int kind, const dnnopt_gemm_desc* d, char* buf, int len) {
+    if (!d || !buf || len <= 0 || kind < 0 || kind > 7) return set_status(DNNOPT_STATUS_INVALID_VALUE);
+    Kind k = static_cast<Kind>(kind);
+    GemmArgs g = to_args(d, nullptr, nullptr, nullptr);
+    if (b_is_nk(k)) g.b_trans = 1;
+    DeviceInfo info;
+    int dev = -1;
+    if (cudaGetDevice(&dev) == cudaSuccess) {
+        int st;
+        DeviceContext* ctx = current_context(&st);
+        if (ctx) info = info_of(ctx);
+    } else {
+        cudaGetLastError();
+    }
+    std::string s = describe_plan(k, g, heuristic_plan(k, g, info));
+    std::snprintf(buf, static_cast<size_t>(len), "%s", s.c_str());
+    return set_status(DNNOPT_STATUS_SUCCESS);
+}
+
+int dnnopt_autotune_enable(int on) {
+    set_autotune_enabled(on != 0);
+    return set_status(DNNOPT_STATUS_SUCCESS);
+}
+int dnnopt_autotune_save(const char* path) {
+    if (!path) return -1;
+    return cache_save(path);
+}
+int dnnopt_autotune_load(const char* path) {
+    if (!path) return -1;
+    return cache_load(path);
+}
+int dnnopt_autotune_entries(void) { return cache_entries(); }
+
+}  // extern "C"

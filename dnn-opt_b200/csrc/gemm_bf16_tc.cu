@@ -1,0 +1,322 @@
+// BF16 x BF16 -> FP32 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM)
+// for the tall-skinny class: large M, N <= 256, B small enough to stay resident
+// in shared memory.  This is the B200 replacement of the reference's BLIS
+// BFMMLA driver gemm_bf16_bf16bf16f32 (src/gemm/gemm_driver_bf16.cpp:134-218,
+// micro-kernel src/gemm/gemm_ukernel_bf16_neon.cpp:30-160) on its headline
+// shape (M=65536, N=64, K=256).
+//
+// Shape physics: at N=64, K=256 the GEMM does 43 flop per HBM byte, far below
+// the BF16 ridge (~250 flop/B), so the kernel streams A and C at HBM speed and
+// keeps the tensor cores a few percent busy.  Design:
+//   * persistent CTAs (one per SM) walk 128-row tiles of A;
+//   * warp 0 issues TMA loads of A in 128 x 64 K-blocks (128-byte swizzle)
+//     into an N-stage shared-memory ring (mbarrier full/empty pairs);
+//   * B (K x N) is gathered once per CTA into the same K-major swizzled layout;
+//   * warp 1 issues tcgen05.mma (M=128, N=n_pad, K=16) into one of two TMEM
+//     accumulators, so the epilogue of tile t overlaps the MMAs of tile t+1;
+//   * warps 2-5 drain TMEM with tcgen05.ld, apply alpha/beta (the reference
+//     epilogue: beta == 0 ? alpha*acc : fma(alpha, acc, beta*C)), stage the
+//     tile in swizzled shared memory and write it with TMA stores (rows >= M
+//     and columns >= N are clipped by the tensor map).
+// No cluster multicast is used anywhere.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace dnnopt_b200 {
+
+namespace {
+
+constexpr int BM = 128;                // rows per tile (UMMA M)
+constexpr int kKBlock = 64;            // bf16 elements per 128-byte swizzle row
+constexpr int kStageBytes = BM * 128;  // one A K-block
+constexpr int kThreads = 192;
+constexpr int kMaxStages = 8;
+constexpr size_t kSmemLimit = 227 * 1024;
+
+struct TcParams {
+    int M, N, K;
+    int n_pad, num_kb, num_tiles, stages, nbox;
+    float alpha, beta;
+    const uint16_t* B;
+    int64_t ldb;
+    int b_trans;
+    const float* C;    // read only when beta != 0
+    int64_t ldc;
+    uint32_t tmem_cols;
+    uint32_t* err;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmC,
+                    const TcParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    const int sb_bytes = p.num_kb * p.n_pad * 128;
+    uint8_t* sB = base;
+    uint8_t* sA = sB + sb_bytes;
+    uint8_t* sC = sA + p.stages * kStageBytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sC + 4 * p.nbox * 4096);
+    uint64_t* empty = full + p.stages;
+    uint64_t* tfull = empty + p.stages;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    if (tid == 0) {
+        for (int s = 0; s < p.stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int b = 0; b < 2; ++b) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], 4); }
+        *abort_flag = 0u;
+        fence_mbar_init();
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmC);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, p.tmem_cols);
+        tmem_relinquish();
+    }
+
+    // Gather B (K x N, or N x K when b_trans) into K-major 128B-swizzled rows:
+    // byte offset of (n, k) = kb*n_pad*128 + n*128 + ((c ^ (n&7))*16) + (k%8)*2,
+    // kb = k/64, c = (k%64)/8.  Consecutive threads take consecutive n.
+    {
+        const int total = p.num_kb * 8 * p.n_pad;
+        for (int idx = tid; idx < total; idx += kThreads) {
+            const int n = idx % p.n_pad, rest = idx / p.n_pad;
+            const int c = rest & 7, kb = rest >> 3;
+            const int k0 = kb * kKBlock + c * 8;
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+                uint32_t lo = 0, hi = 0;
+                if (n < p.N) {
+                    int ka = k0 + e, kb2 = k0 + e + 1;
+                    if (ka < p.K) lo = p.B[p.b_trans ? (int64_t)n * p.ldb + ka : (int64_t)ka * p.ldb + n];
+                    if (kb2 < p.K) hi = p.B[p.b_trans ? (int64_t)n * p.ldb + kb2 : (int64_t)kb2 * p.ldb + n];
+                }
+                w[e >> 1] = lo | (hi << 16);
+            }
+            uint8_t* dst = sB + kb * p.n_pad * 128 + n * 128 + ((c ^ (n & 7)) * 16);
+            *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            uint32_t it = 0;
+            for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
+                for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+                    const uint32_t s = it % p.stages, ph = (it / p.stages) & 1u;
+                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.err)) break;
+                    mbar_arrive_expect_tx(&full[s], kStageBytes);
+                    tma_load_2d(sA + s * kStageBytes, &tmA, &full[s], kb * kKBlock, tile * BM);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc_bf16_f32(BM, p.n_pad);
+            uint32_t it = 0, titer = 0;
+            for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x, ++titer) {
+                const uint32_t buf = titer & 1u, tph = (titer >> 1) & 1u;
+                if (!mbar_wait(&tempty[buf], tph ^ 1u, abort_flag, p.err)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + buf * p.n_pad;
+                bool ok = true;
+                for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+                    const uint32_t s = it % p.stages, ph = (it / p.stages) & 1u;
+                    if (!mbar_wait(&full[s], ph, abort_flag, p.err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sA + s * kStageBytes);
+                    const uint32_t b_addr = smem_u32(sB + kb * p.n_pad * 128);
+#pragma unroll
+                    for (int kk = 0; kk < kKBlock / 16; ++kk) {
+                        umma_f16_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32),
+                                    umma_desc_k_sw128(b_addr + kk * 32), idesc,
+                                    (kb | kk) != 0 ? 1u : 0u);
+                    }
+                    umma_commit(&empty[s]);   // stage is free once these MMAs retire
+                }
+                if (!ok) break;
+                umma_commit(&tfull[buf]);     // accumulator ready for the epilogue
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int q = warp & 3;                      // TMEM lane quadrant of this warp
+        uint8_t* stage = sC + (warp - 2) * p.nbox * 4096;
+        uint32_t titer = 0;
+        for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x, ++titer) {
+            const uint32_t buf = titer & 1u, tph = (titer >> 1) & 1u;
+            if (!mbar_wait(&tfull[buf], tph, abort_flag, p.err)) break;
+            tc_fence_after();
+            if (lane == 0) tma_store_wait_read<0>();  // staging buffer free again
+            __syncwarp();
+            const int row = tile * BM + q * 32 + lane;
+            const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * p.n_pad;
+            for (int cg = 0; cg < p.n_pad / 16; ++cg) {
+                uint32_t r[16];
+                tmem_ld_32x32b_x16(t_addr + cg * 16, r);
+                tmem_ld_wait();
+                float v[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    float acc = __uint_as_float(r[j]);
+                    int col = cg * 16 + j;
+                    if (p.beta == 0.0f) {
+                        v[j] = p.alpha * acc;
+                    } else {
+                        float cold = (row < p.M && col < p.N) ? p.C[(int64_t)row * p.ldc + col] : 0.0f;
+                        v[j] = fmaf(p.alpha, acc, p.beta * cold);
+                    }
+                }
+#pragma unroll
+                for (int j4 = 0; j4 < 4; ++j4) {
+                    const int col = cg * 16 + j4 * 4;
+                    const int box = col >> 5, chunk = (col & 31) >> 2;
+                    uint8_t* dst = stage + box * 4096 + lane * 128 + ((chunk ^ (lane & 7)) * 16);
+                    *reinterpret_cast<float4*>(dst) =
+                        make_float4(v[j4 * 4], v[j4 * 4 + 1], v[j4 * 4 + 2], v[j4 * 4 + 3]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);  // TMEM buffer may be overwritten
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                for (int box = 0; box < p.nbox; ++box)
+                    tma_store_2d(&tmC, stage + box * 4096, box * 32, tile * BM + q * 32);
+                tma_store_commit();
+            }
+        }
+        if (lane == 0) tma_store_wait_all<0>();
+        __syncwarp();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, p.tmem_cols);
+    }
+}
+
+// ---- host helpers ----------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+    static EncodeTiledFn fn = [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
+                                             cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<EncodeTiledFn>(nullptr);
+        return reinterpret_cast<EncodeTiledFn>(ptr);
+    }();
+    return fn;
+}
+
+struct Layout {
+    int n_pad, num_kb, nbox, stages;
+    size_t smem;
+};
+
+Layout plan_layout(const GemmArgs& g) {
+    Layout L;
+    L.n_pad = (g.N + 15) / 16 * 16;
+    L.num_kb = (g.K + kKBlock - 1) / kKBlock;
+    L.nbox = (L.n_pad + 31) / 32;
+    const size_t fixed = 1024 + static_cast<size_t>(L.num_kb) * L.n_pad * 128 +
+                         static_cast<size_t>(4) * L.nbox * 4096 + 256;
+    int st = 0;
+    if (fixed < kSmemLimit) st = static_cast<int>((kSmemLimit - fixed) / kStageBytes);
+    L.stages = st > kMaxStages ? kMaxStages : st;
+    L.smem = fixed + static_cast<size_t>(L.stages) * kStageBytes;
+    return L;
+}
+
+}  // namespace
+
+bool gemm_bf16_tc_supported(const GemmArgs& g) {
+    if (g.M < 1 || g.N < 1 || g.K < 1 || g.N > 256 || g.a_trans) return false;
+    if (reinterpret_cast<uintptr_t>(g.A) % 16 || g.lda % 8 || g.lda < g.K) return false;
+    if (reinterpret_cast<uintptr_t>(g.C) % 16 || g.ldc % 4 || g.ldc < g.N) return false;
+    if (get_encode_fn() == nullptr) return false;
+    return plan_layout(g).stages >= 2;
+}
+
+cudaError_t launch_gemm_bf16_tc(const GemmArgs& g, int num_sms, uint32_t* err, cudaStream_t s) {
+    if (!gemm_bf16_tc_supported(g)) return cudaErrorInvalidValue;
+    const Layout L = plan_layout(g);
+    EncodeTiledFn encode = get_encode_fn();
+
+    CUtensorMap tmA, tmC;
+    {
+        cuuint64_t dims[2] = {static_cast<cuuint64_t>(g.K), static_cast<cuuint64_t>(g.M)};
+        cuuint64_t strides[1] = {static_cast<cuuint64_t>(g.lda) * 2};
+        cuuint32_t box[2] = {kKBlock, BM};
+        cuuint32_t estr[2] = {1, 1};
+        if (encode(&tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(g.A), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    {
+        cuuint64_t dims[2] = {static_cast<cuuint64_t>(g.N), static_cast<cuuint64_t>(g.M)};
+        cuuint64_t strides[1] = {static_cast<cuuint64_t>(g.ldc) * 4};
+        cuuint32_t box[2] = {32, 32};
+        cuuint32_t estr[2] = {1, 1};
+        if (encode(&tmC, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, g.C, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+
+    TcParams p;
+    p.M = g.M; p.N = g.N; p.K = g.K;
+    p.n_pad = L.n_pad; p.num_kb = L.num_kb; p.nbox = L.nbox; p.stages = L.stages;
+    p.num_tiles = (g.M + BM - 1) / BM;
+    p.alpha = g.alpha; p.beta = g.beta;
+    p.B = static_cast<const uint16_t*>(g.B); p.ldb = g.ldb; p.b_trans = g.b_trans;
+    p.C = static_cast<const float*>(g.C); p.ldc = g.ldc;
+    uint32_t cols = 32;
+    while (cols < static_cast<uint32_t>(2 * L.n_pad)) cols <<= 1;
+    p.tmem_cols = cols;
+    p.err = err;
+
+    // The attribute is per device; set it once to the largest size requested
+    // so that launches under stream capture make no further attribute calls.
+    static thread_local int smem_set_dev = -1;
+    static thread_local size_t smem_set = 0;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev != smem_set_dev || L.smem > smem_set) {
+        e = cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kSmemLimit));
+        if (e != cudaSuccess) return e;
+        smem_set_dev = dev;
+        smem_set = kSmemLimit;
+    }
+    int grid = p.num_tiles < num_sms ? p.num_tiles : num_sms;
+    gemm_bf16_tc_kernel<<<grid, kThreads, L.smem, s>>>(tmA, tmC, p);
+    return cudaGetLastError();
+}
+
+}  // namespace dnnopt_b200

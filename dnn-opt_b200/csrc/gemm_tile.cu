@@ -1,0 +1,348 @@
+// General-shape SIMT kernels: any M, N, K, leading dimensions and
+// transpositions.  They cover the shapes outside the small-M and tall-skinny
+// classes (the reference's adaptive-tile / packed registry range,
+// src/gemm/gemm_adaptive_tile_fp32.cpp:664-784, src/gemm/gemm_driver_generic.cpp:27-248)
+// so that every call the reference accepts has a GPU path.  FP32 arithmetic is
+// FFMA only (no TF32), matching the reference's FP32 accumulation class.
+//
+// Also here: the FP32-API int8 quantisation (per-tensor absmax / 127,
+// lrintf, clamp to [-128, 127]) of reference src/gemm/gemm_smallm_int8.cpp:198-236
+// and src/gemm/gemm_driver_generic.cpp:49-67, bit-exact (IEEE division,
+// round-to-nearest-even conversion).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace dnnopt_b200 {
+
+namespace {
+
+constexpr int BM = 64, BN = 64, BK = 16, kThreads = 256;
+
+template <In I> struct ElemT;
+template <> struct ElemT<In::F32> { using T = float; };
+template <> struct ElemT<In::BF16> { using T = uint16_t; };
+template <> struct ElemT<In::F32R> { using T = float; };
+template <> struct ElemT<In::RE4> { using T = uint8_t; };
+template <> struct ElemT<In::RE5> { using T = uint8_t; };
+
+__device__ __forceinline__ float dre4(uint32_t b) {
+    uint32_t s = (b >> 7) & 1u, e = (b >> 3) & 0xFu, m = b & 7u;
+    float v;
+    if (e == 0) v = static_cast<float>(m) * 0.001953125f;
+    else if (e == 0xF && m == 7) v = 448.0f;
+    else v = __uint_as_float(((e + 119u) << 23) | (m << 20));
+    return s ? -v : v;
+}
+__device__ __forceinline__ float dre5(uint32_t b) {
+    uint32_t s = (b >> 7) & 1u, e = (b >> 2) & 0x1Fu, m = b & 3u;
+    if (e == 0) {
+        float v = static_cast<float>(m) * 1.52587890625e-05f;
+        return s ? -v : v;
+    }
+    if (e == 0x1F) return __uint_as_float((s << 31) | (0xFFu << 23) | (m << 21));
+    return __uint_as_float((s << 31) | ((e + 111u) << 23) | (m << 21));
+}
+
+template <In I>
+__device__ __forceinline__ float decode(typename ElemT<I>::T v) {
+    if constexpr (I == In::F32) return v;
+    else if constexpr (I == In::BF16) return bf16_bits_to_f32(v);
+    else if constexpr (I == In::F32R) return round_to_bf16(v);
+    else if constexpr (I == In::RE4) return dre4(v);
+    else return dre5(v);
+}
+
+// 64 x 64 output tile per CTA, 4 x 4 per thread, K staged 16 at a time.
+template <In IA, In IB>
+__global__ void __launch_bounds__(kThreads) gemm_tile_f32_kernel(const GemmArgs g) {
+    using TA = typename ElemT<IA>::T;
+    using TB = typename ElemT<IB>::T;
+    __shared__ float sA[BK][BM + 4];
+    __shared__ float sB[BK][BN + 4];
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const TA* A = static_cast<const TA*>(g.A);
+    const TB* B = static_cast<const TB*>(g.B);
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < g.K; k0 += BK) {
+        for (int idx = tid; idx < BM * BK; idx += kThreads) {
+            int i, k;
+            if (g.a_trans) { i = idx % BM; k = idx / BM; } else { k = idx % BK; i = idx / BK; }
+            int gi = m0 + i, gk = k0 + k;
+            float v = 0.0f;
+            if (gi < g.M && gk < g.K)
+                v = decode<IA>(A[g.a_trans ? (int64_t)gk * g.lda + gi : (int64_t)gi * g.lda + gk]);
+            sA[k][i] = v;
+        }
+        for (int idx = tid; idx < BK * BN; idx += kThreads) {
+            int j, k;
+            if (g.b_trans) { k = idx % BK; j = idx / BK; } else { j = idx % BN; k = idx / BN; }
+            int gj = n0 + j, gk = k0 + k;
+            float v = 0.0f;
+            if (gj < g.N && gk < g.K)
+                v = decode<IB>(B[g.b_trans ? (int64_t)gj * g.ldb + gk : (int64_t)gk * g.ldb + gj]);
+            sB[k][j] = v;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < BK; ++k) {
+            float a[4], b[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) a[r] = sA[k][ty * 4 + r];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) b[c] = sB[k][tx * 4 + c];
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) acc[r][c] = fmaf(a[r], b[c], acc[r][c]);
+        }
+        __syncthreads();
+    }
+    float* C = static_cast<float*>(g.C);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        int gi = m0 + ty * 4 + r;
+        if (gi >= g.M) continue;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            int gj = n0 + tx * 4 + c;
+            if (gj >= g.N) continue;
+            float* cp = C + (int64_t)gi * g.ldc + gj;
+            *cp = (g.beta == 0.0f) ? g.alpha * acc[r][c] : fmaf(g.alpha, acc[r][c], g.beta * *cp);
+        }
+    }
+}
+
+// int8 x int8 -> int32 (exact) with A [M, K] and B [N, K]; optional dequant epilogue.
+template <bool DQ>
+__global__ void __launch_bounds__(kThreads)
+gemm_tile_s8_kernel(const GemmArgs g, const float* scales) {
+    __shared__ int32_t sA[BK][BM + 4];
+    __shared__ int32_t sB[BK][BN + 4];
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int8_t* A = static_cast<const int8_t*>(g.A);
+    const int8_t* B = static_cast<const int8_t*>(g.B);
+    int32_t acc[4][4] = {};
+    for (int k0 = 0; k0 < g.K; k0 += BK) {
+        for (int idx = tid; idx < BM * BK; idx += kThreads) {
+            int k = idx % BK, i = idx / BK, gi = m0 + i, gk = k0 + k;
+            sA[k][i] = (gi < g.M && gk < g.K) ? A[(int64_t)gi * g.lda + gk] : 0;
+        }
+        for (int idx = tid; idx < BK * BN; idx += kThreads) {
+            int k = idx % BK, j = idx / BK, gj = n0 + j, gk = k0 + k;
+            sB[k][j] = (gj < g.N && gk < g.K) ? B[(int64_t)gj * g.ldb + gk] : 0;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < BK; ++k) {
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) acc[r][c] += sA[k][ty * 4 + r] * sB[k][tx * 4 + c];
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        int gi = m0 + ty * 4 + r;
+        if (gi >= g.M) continue;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            int gj = n0 + tx * 4 + c;
+            if (gj >= g.N) continue;
+            if constexpr (DQ) {
+                float* cp = static_cast<float*>(g.C) + (int64_t)gi * g.ldc + gj;
+                float scale = __fmul_rn(g.alpha, __fmul_rn(scales[0], scales[1]));
+                float c0 = (g.beta == 0.0f) ? 0.0f : __fmul_rn(g.beta, *cp);
+                *cp = __fadd_rn(c0, __fmul_rn(scale, static_cast<float>(acc[r][c])));
+            } else {
+                static_cast<int32_t*>(g.C)[(int64_t)gi * g.ldc + gj] = acc[r][c];
+            }
+        }
+    }
+}
+
+// Per-tensor absmax of op(A) (M x K) and B (K x N, or N x K when b_trans):
+// absmax_bits[0..1] hold the float bit patterns (non-negative floats order
+// like unsigned integers).  NaN never wins, as in the reference's `v > max`.
+__global__ void absmax2_kernel(const GemmArgs g, uint32_t* absmax_bits) {
+    const float* A = static_cast<const float*>(g.A);
+    const float* B = static_cast<const float*>(g.B);
+    const int64_t na = (int64_t)g.M * g.K, nb = (int64_t)g.K * g.N;
+    float ma = 0.0f, mb = 0.0f;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < na + nb; i += stride) {
+        if (i < na) {
+            int64_t m = i / g.K, k = i - m * g.K;
+            float v = fabsf(A[g.a_trans ? k * g.lda + m : m * g.lda + k]);
+            if (v > ma) ma = v;
+        } else {
+            int64_t j = i - na;
+            int64_t k = j / g.N, n = j - k * g.N;
+            float v = fabsf(B[g.b_trans ? n * g.ldb + k : k * g.ldb + n]);
+            if (v > mb) mb = v;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        ma = fmaxf(ma, __shfl_xor_sync(0xFFFFFFFFu, ma, o));
+        mb = fmaxf(mb, __shfl_xor_sync(0xFFFFFFFFu, mb, o));
+    }
+    if ((threadIdx.x & 31) == 0) {
+        if (ma > 0.0f) atomicMax(&absmax_bits[0], __float_as_uint(ma));
+        if (mb > 0.0f) atomicMax(&absmax_bits[1], __float_as_uint(mb));
+    }
+}
+
+__device__ __forceinline__ int8_t quant_s8(float x, float s) {
+    int q = __float2int_rn(__fdiv_rn(x, s));
+    q = q < -128 ? -128 : (q > 127 ? 127 : q);
+    return static_cast<int8_t>(q);
+}
+
+// qa: M x K dense; qb: N x K dense (B transposed so the dot-form kernels read
+// K-contiguous rows).  scales[0..1] = sA, sB.
+__global__ void quantize_s8_kernel(const GemmArgs g, const uint32_t* absmax_bits, float* scales,
+                                   int8_t* qa, int8_t* qb) {
+    float ma = __uint_as_float(absmax_bits[0]), mb = __uint_as_float(absmax_bits[1]);
+    float sa = (ma == 0.0f) ? 1.0f : __fdiv_rn(ma, 127.0f);
+    float sb = (mb == 0.0f) ? 1.0f : __fdiv_rn(mb, 127.0f);
+    if (blockIdx.x == 0 && threadIdx.x == 0) { scales[0] = sa; scales[1] = sb; }
+    const float* A = static_cast<const float*>(g.A);
+    const float* B = static_cast<const float*>(g.B);
+    const int64_t na = (int64_t)g.M * g.K, nb = (int64_t)g.K * g.N;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < na + nb; i += stride) {
+        if (i < na) {
+            int64_t m = i / g.K, k = i - m * g.K;
+            qa[i] = quant_s8(A[g.a_trans ? k * g.lda + m : m * g.lda + k], sa);
+        } else {
+            // Output-major order for qb (n, k) so writes are coalesced.
+            int64_t j = i - na;
+            int64_t n = j / g.K, k = j - n * g.K;
+            qb[j] = quant_s8(B[g.b_trans ? n * g.ldb + k : k * g.ldb + n], sb);
+        }
+    }
+}
+
+// Reference fp8_e4m3_t(float) / fp8_e5m2_t(float) encoders
+// (include/dnnopt/gemm/gemm_types.h:56-85, :131-157), bit for bit.
+__device__ __forceinline__ uint8_t enc_re4(float f) {
+    uint32_t u = __float_as_uint(f);
+    uint32_t sign = (u >> 31) & 1u;
+    int32_t ex = static_cast<int32_t>((u >> 23) & 0xFFu) - 127 + 8;
+    uint32_t mant = (u >> 20) & 0x7u;
+    if (ex > 7) { ex = 7; mant = 7; }
+    else if (ex < -6) { ex = 0; mant = 0; }
+    if (ex > 0) return static_cast<uint8_t>((sign << 7) | (static_cast<uint32_t>(ex & 0xF) << 3) | mant);
+    int shift = -ex;
+    if (shift >= 8) return 0;
+    mant = (mant >> shift) | (0x8u >> shift);
+    return static_cast<uint8_t>((sign << 7) | mant);
+}
+
+__device__ __forceinline__ uint8_t enc_re5(float f) {
+    uint32_t u = __float_as_uint(f);
+    uint32_t sign = (u >> 31) & 1u;
+    int32_t ex = static_cast<int32_t>((u >> 23) & 0xFFu) - 127 + 16;
+    uint32_t mant = (u >> 21) & 0x3u;
+    if (ex > 30) return static_cast<uint8_t>((sign << 7) | (0x1Fu << 2));
+    if (ex < -14) return static_cast<uint8_t>(sign << 7);
+    if (ex > 0) return static_cast<uint8_t>((sign << 7) | (static_cast<uint32_t>(ex & 0x1F) << 2) | mant);
+    int shift = -ex;
+    if (shift >= 4) return static_cast<uint8_t>(sign << 7);
+    mant = (mant >> shift) | (0x4u >> shift);
+    return static_cast<uint8_t>((sign << 7) | mant);
+}
+
+// gemm_fp8 (src/gemm/gemm_fp8.cpp:117-146): A -> e4m3 (dense M x K),
+// B -> e5m2 (dense K x N).
+__global__ void quantize_ref_fp8_kernel(const GemmArgs g, uint8_t* qa, uint8_t* qb) {
+    const float* A = static_cast<const float*>(g.A);
+    const float* B = static_cast<const float*>(g.B);
+    const int64_t na = (int64_t)g.M * g.K, nb = (int64_t)g.K * g.N;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < na + nb; i += stride) {
+        if (i < na) {
+            int64_t m = i / g.K, k = i - m * g.K;
+            qa[i] = enc_re4(A[g.a_trans ? k * g.lda + m : m * g.lda + k]);
+        } else {
+            int64_t j = i - na;
+            int64_t k = j / g.N, n = j - k * g.N;
+            qb[j] = enc_re5(B[g.b_trans ? n * g.ldb + k : k * g.ldb + n]);
+        }
+    }
+}
+
+template <In IA, In IB>
+const void* tile_fn() {
+    return reinterpret_cast<const void*>(&gemm_tile_f32_kernel<IA, IB>);
+}
+
+}  // namespace
+
+cudaError_t launch_gemm_tile_f32(In ia, In ib, const GemmArgs& g, cudaStream_t s) {
+    const void* fn = nullptr;
+    if (ia == In::F32 && ib == In::F32) fn = tile_fn<In::F32, In::F32>();
+    else if (ia == In::BF16 && ib == In::BF16) fn = tile_fn<In::BF16, In::BF16>();
+    else if (ia == In::F32R && ib == In::F32R) fn = tile_fn<In::F32R, In::F32R>();
+    else if (ia == In::RE4 && ib == In::RE5) fn = tile_fn<In::RE4, In::RE5>();
+    else if (ia == In::RE5 && ib == In::RE5) fn = tile_fn<In::RE5, In::RE5>();
+    if (!fn) return cudaErrorInvalidValue;
+    dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM);
+    GemmArgs a = g;
+    void* args[] = {&a};
+    return cudaLaunchKernel(fn, grid, dim3(kThreads), args, 0, s);
+}
+
+cudaError_t launch_gemm_tile_s8(DotKind kind, const GemmArgs& g, const float* scales,
+                                cudaStream_t s) {
+    dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM);
+    if (kind == DotKind::S8S32) gemm_tile_s8_kernel<false><<<grid, kThreads, 0, s>>>(g, scales);
+    else if (kind == DotKind::S8DQ) gemm_tile_s8_kernel<true><<<grid, kThreads, 0, s>>>(g, scales);
+    else return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
+cudaError_t launch_absmax2(const GemmArgs& g, uint32_t* absmax_bits, cudaStream_t s) {
+    cudaError_t e = cudaMemsetAsync(absmax_bits, 0, 2 * sizeof(uint32_t), s);
+    if (e != cudaSuccess) return e;
+    int64_t n = (int64_t)g.M * g.K + (int64_t)g.K * g.N;
+    int blocks = static_cast<int>(((n + 255) / 256) < 148 * 8 ? (n + 255) / 256 : 148 * 8);
+    absmax2_kernel<<<blocks, 256, 0, s>>>(g, absmax_bits);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_s8(const GemmArgs& g, const uint32_t* absmax_bits, float* scales,
+                               int8_t* qa, int8_t* qb_nk, cudaStream_t s) {
+    int64_t n = (int64_t)g.M * g.K + (int64_t)g.K * g.N;
+    int blocks = static_cast<int>(((n + 255) / 256) < 148 * 8 ? (n + 255) / 256 : 148 * 8);
+    quantize_s8_kernel<<<blocks, 256, 0, s>>>(g, absmax_bits, scales, qa, qb_nk);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_ref_fp8(const GemmArgs& g, uint8_t* qa, uint8_t* qb,
+                                    cudaStream_t s) {
+    int64_t n = (int64_t)g.M * g.K + (int64_t)g.K * g.N;
+    int blocks = static_cast<int>(((n + 255) / 256) < 148 * 8 ? (n + 255) / 256 : 148 * 8);
+    quantize_ref_fp8_kernel<<<blocks, 256, 0, s>>>(g, qa, qb);
+    return cudaGetLastError();
+}
+
+// cblas_saxpy (reference src/blas/cblas_saxpy.cpp:13-50): Y[i*incY] += alpha*X[i*incX].
+__global__ void saxpy_kernel(int n, float alpha, const float* x, int incx, float* y, int incy) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+        y[i * incy] = fmaf(alpha, x[i * incx], y[i * incy]);
+}
+
+cudaError_t launch_saxpy(int n, float alpha, const float* x, int incx, float* y, int incy,
+                         cudaStream_t s) {
+    int blocks = (n + 255) / 256;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    saxpy_kernel<<<blocks, 256, 0, s>>>(n, alpha, x, incx, y, incy);
+    return cudaGetLastError();
+}
+
+}  // namespace dnnopt_b200

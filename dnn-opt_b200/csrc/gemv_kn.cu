@@ -1,0 +1,308 @@
+// Small-M (M <= 8) GEMV-class kernel for a K x N row-major B (N contiguous):
+//   C[M,N] = alpha * op(A)[M,K] * B[K,N] + beta * C
+//
+// Replaces the reference's small-M FP32 drivers (gemm_1xn_fp32,
+// src/gemm/gemm_tiny_fp32.cpp:167-218; gemm_smallm_wide_driver_fp32,
+// src/gemm/gemm_smallm_wide_fp32.cpp:412-490) and serves the same shapes for
+// the bf16 / FP32-API bf16 / reference-fp8 entry points.
+//
+// B200 design: the op is HBM-bound (about 0.5*M flop per byte of B), so the
+// kernel is shaped for bytes in flight, not arithmetic.
+//   * A CTA owns a 128-column strip of B and one K-split; each warp streams
+//     rows of the strip with coalesced 16-byte loads (4-byte loads when the
+//     rows are not 16-byte aligned, e.g. prime N), U rows unrolled so every
+//     thread keeps U independent loads in flight.
+//   * The A panel for the split is staged transposed in shared memory so a
+//     row's M coefficients arrive with one broadcast vector load.
+//   * Warps reduce through shared memory in a fixed order; K-splits reduce
+//     through a global workspace by the last CTA of each strip (atomic
+//     ticket), again in split order, so results are deterministic.
+//   * The grid is sized by the host to one wave of resident CTAs over the
+//     148 SMs (splits = resident CTAs / strips).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace dnnopt_b200 {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kTileN = 128;
+constexpr int kStageK = 128;   // K rows of A staged per pass
+
+template <In I> struct Elem;
+template <> struct Elem<In::F32> { using T = float; };
+template <> struct Elem<In::BF16> { using T = uint16_t; };
+template <> struct Elem<In::F32R> { using T = float; };
+template <> struct Elem<In::RE4> { using T = uint8_t; };
+template <> struct Elem<In::RE5> { using T = uint8_t; };
+
+// Reference fp8_e4m3_t decode (include/dnnopt/gemm/gemm_types.h:88-115):
+// bias 8, subnormal step 2^-9, field 0x7F/0xFF decodes to +-448.
+__device__ __forceinline__ float decode_re4(uint32_t b) {
+    uint32_t s = (b >> 7) & 1u, e = (b >> 3) & 0xFu, m = b & 7u;
+    float v;
+    if (e == 0) v = static_cast<float>(m) * 0.001953125f;           // m * 2^-9
+    else if (e == 0xF && m == 7) v = 448.0f;
+    else v = __uint_as_float(((e + 119u) << 23) | (m << 20));      // 2^(e-8) * (1+m/8)
+    return s ? -v : v;
+}
+
+// Reference fp8_e5m2_t decode (gemm_types.h:160-191): bias 16,
+// subnormal step 2^-16, exponent field 31 is inf/nan.
+__device__ __forceinline__ float decode_re5(uint32_t b) {
+    uint32_t s = (b >> 7) & 1u, e = (b >> 2) & 0x1Fu, m = b & 3u;
+    if (e == 0) {
+        float v = static_cast<float>(m) * 1.52587890625e-05f;       // m * 2^-16
+        return s ? -v : v;
+    }
+    if (e == 0x1F) return __uint_as_float((s << 31) | (0xFFu << 23) | (m << 21));
+    return __uint_as_float((s << 31) | ((e + 111u) << 23) | (m << 21));
+}
+
+template <In I>
+__device__ __forceinline__ float dec(typename Elem<I>::T v) {
+    if constexpr (I == In::F32) return v;
+    else if constexpr (I == In::BF16) return bf16_bits_to_f32(v);
+    else if constexpr (I == In::F32R) return round_to_bf16(v);
+    else if constexpr (I == In::RE4) return decode_re4(v);
+    else return decode_re5(v);
+}
+
+// Four consecutive elements of one B row -> four floats (aligned vector load).
+template <In I>
+__device__ __forceinline__ void load4(const typename Elem<I>::T* p, float (&o)[4]) {
+    if constexpr (sizeof(typename Elem<I>::T) == 4) {
+        float4 v = __ldg(reinterpret_cast<const float4*>(p));
+        o[0] = dec<I>(v.x); o[1] = dec<I>(v.y); o[2] = dec<I>(v.z); o[3] = dec<I>(v.w);
+    } else if constexpr (sizeof(typename Elem<I>::T) == 2) {
+        uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
+        o[0] = dec<I>(static_cast<uint16_t>(v.x & 0xFFFFu));
+        o[1] = dec<I>(static_cast<uint16_t>(v.x >> 16));
+        o[2] = dec<I>(static_cast<uint16_t>(v.y & 0xFFFFu));
+        o[3] = dec<I>(static_cast<uint16_t>(v.y >> 16));
+    } else {
+        uint32_t v = __ldg(reinterpret_cast<const unsigned int*>(p));
+        o[0] = dec<I>(static_cast<uint8_t>(v & 0xFFu));
+        o[1] = dec<I>(static_cast<uint8_t>((v >> 8) & 0xFFu));
+        o[2] = dec<I>(static_cast<uint8_t>((v >> 16) & 0xFFu));
+        o[3] = dec<I>(static_cast<uint8_t>(v >> 24));
+    }
+}
+
+struct KnParams {
+    GemmArgs g;
+    int splits, kchunk, n_pad;
+    float* ws;
+    uint32_t* counters;
+};
+
+// Column (within the 128-wide strip) held in accumulator slot c of `lane`.
+template <bool VEC4>
+__device__ __forceinline__ int slot_col(int lane, int c) {
+    return VEC4 ? 4 * lane + c : lane + 32 * c;
+}
+
+template <In IA, In IB, int MT, bool VEC4>
+__global__ void __launch_bounds__(kThreads)
+gemv_kn_kernel(const KnParams p) {
+    using TA = typename Elem<IA>::T;
+    using TB = typename Elem<IB>::T;
+    constexpr int U = (MT >= 4) ? 4 : 8;   // rows in flight per warp iteration
+
+    // Shared memory: staged A panel (k-major, MT floats per row) during the
+    // K loop, then the per-warp partial strips for the reduction.
+    __shared__ __align__(16) float smem[(kStageK * MT > kWarps * MT * kTileN)
+                                            ? kStageK * MT
+                                            : kWarps * MT * kTileN];
+    __shared__ int s_last;
+
+    const GemmArgs& g = p.g;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n0 = blockIdx.x * kTileN;
+    const int split = blockIdx.y;
+    const int k_begin = split * p.kchunk;
+    const int k_end = min(g.K, k_begin + p.kchunk);
+    const bool full_tile = (n0 + kTileN) <= g.N;
+    const TA* A = static_cast<const TA*>(g.A);
+    const TB* B = static_cast<const TB*>(g.B);
+
+    float acc[MT][4];
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[m][c] = 0.0f;
+
+    for (int kb = k_begin; kb < k_end; kb += kStageK) {
+        const int kn = min(kStageK, k_end - kb);
+        // Stage A[0:MT, kb:kb+kn] as smem[r*MT + m] (zero for m >= M).
+        for (int idx = tid; idx < kn * MT; idx += kThreads) {
+            int r = idx / MT, m = idx - r * MT;
+            float v = 0.0f;
+            if (m < g.M) {
+                int64_t off = g.a_trans ? (int64_t)(kb + r) * g.lda + m
+                                        : (int64_t)m * g.lda + (kb + r);
+                v = dec<IA>(A[off]);
+            }
+            smem[idx] = v;
+        }
+        __syncthreads();
+
+        for (int r0 = warp; r0 < kn; r0 += kWarps * U) {
+            float b[U][4];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int r = r0 + u * kWarps;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) b[u][c] = 0.0f;
+                if (r < kn) {
+                    const TB* row = B + (int64_t)(kb + r) * g.ldb + n0;
+                    if (VEC4 && full_tile) {
+                        load4<IB>(row + 4 * lane, b[u]);
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            int col = slot_col<VEC4>(lane, c);
+                            if (n0 + col < g.N) b[u][c] = dec<IB>(row[col]);
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int r = r0 + u * kWarps;
+                if (r < kn) {
+                    float a[MT];
+                    if constexpr (MT % 4 == 0) {
+#pragma unroll
+                        for (int q = 0; q < MT / 4; ++q) {
+                            float4 v = *reinterpret_cast<const float4*>(&smem[r * MT + 4 * q]);
+                            a[4 * q] = v.x; a[4 * q + 1] = v.y; a[4 * q + 2] = v.z; a[4 * q + 3] = v.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int m = 0; m < MT; ++m) a[m] = smem[r * MT + m];
+                    }
+#pragma unroll
+                    for (int m = 0; m < MT; ++m)
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) acc[m][c] = fmaf(a[m], b[u][c], acc[m][c]);
+                }
+            }
+        }
+        __syncthreads();
+    }
+
+    // Cross-warp reduction: smem[(w*MT + m)*128 + col], summed in warp order.
+    float* red = smem;
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) red[(warp * MT + m) * kTileN + slot_col<VEC4>(lane, c)] = acc[m][c];
+    __syncthreads();
+
+    float* C = static_cast<float*>(g.C);
+    if (p.splits == 1) {
+        for (int idx = tid; idx < MT * kTileN; idx += kThreads) {
+            int m = idx / kTileN, j = idx - m * kTileN;
+            float s = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) s += red[(w * MT + m) * kTileN + j];
+            if (m < g.M && n0 + j < g.N) {
+                float* cp = C + (int64_t)m * g.ldc + n0 + j;
+                *cp = (g.beta == 0.0f) ? g.alpha * s : fmaf(g.alpha, s, g.beta * *cp);
+            }
+        }
+        return;
+    }
+
+    // Split-K: publish this split's strip, then the last CTA of the strip
+    // (ticket == splits-1) sums the splits in order and writes C.
+    for (int idx = tid; idx < MT * kTileN; idx += kThreads) {
+        int m = idx / kTileN, j = idx - m * kTileN;
+        float s = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) s += red[(w * MT + m) * kTileN + j];
+        __stcg(&p.ws[((int64_t)split * MT + m) * p.n_pad + n0 + j], s);
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        uint32_t ticket = atomicAdd(&p.counters[blockIdx.x], 1u);
+        s_last = (ticket == static_cast<uint32_t>(p.splits - 1));
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int idx = tid; idx < MT * kTileN; idx += kThreads) {
+        int m = idx / kTileN, j = idx - m * kTileN;
+        if (m < g.M && n0 + j < g.N) {
+            float s = 0.0f;
+            for (int sp = 0; sp < p.splits; ++sp)
+                s += __ldcg(&p.ws[((int64_t)sp * MT + m) * p.n_pad + n0 + j]);
+            float* cp = C + (int64_t)m * g.ldc + n0 + j;
+            *cp = (g.beta == 0.0f) ? g.alpha * s : fmaf(g.alpha, s, g.beta * *cp);
+        }
+    }
+    if (tid == 0) p.counters[blockIdx.x] = 0u;   // ready for the next launch on this stream
+}
+
+template <In IA, In IB, int MT, bool VEC4>
+const void* kn_fn() {
+    return reinterpret_cast<const void*>(&gemv_kn_kernel<IA, IB, MT, VEC4>);
+}
+
+template <In IA, In IB>
+const void* kn_select_mt(int mt, int vec4) {
+    switch (mt) {
+        case 1: return vec4 ? kn_fn<IA, IB, 1, true>() : kn_fn<IA, IB, 1, false>();
+        case 2: return vec4 ? kn_fn<IA, IB, 2, true>() : kn_fn<IA, IB, 2, false>();
+        case 4: return vec4 ? kn_fn<IA, IB, 4, true>() : kn_fn<IA, IB, 4, false>();
+        case 8: return vec4 ? kn_fn<IA, IB, 8, true>() : kn_fn<IA, IB, 8, false>();
+        default: return nullptr;
+    }
+}
+
+const void* kn_select(In ia, In ib, int mt, int vec4) {
+    if (ia == In::F32 && ib == In::F32) return kn_select_mt<In::F32, In::F32>(mt, vec4);
+    if (ia == In::BF16 && ib == In::BF16) return kn_select_mt<In::BF16, In::BF16>(mt, vec4);
+    if (ia == In::F32R && ib == In::F32R) return kn_select_mt<In::F32R, In::F32R>(mt, vec4);
+    if (ia == In::RE4 && ib == In::RE5) return kn_select_mt<In::RE4, In::RE5>(mt, vec4);
+    if (ia == In::RE5 && ib == In::RE5) return kn_select_mt<In::RE5, In::RE5>(mt, vec4);
+    return nullptr;
+}
+
+}  // namespace
+
+int gemv_kn_tiles(int N) { return (N + kTileN - 1) / kTileN; }
+
+size_t gemv_kn_ws_floats(const GemvKnPlan& p, int N) {
+    if (p.splits <= 1) return 0;
+    return static_cast<size_t>(p.splits) * p.mt * gemv_kn_tiles(N) * kTileN;
+}
+
+cudaError_t gemv_kn_occupancy(In ia, In ib, int mt, int vec4, int* blocks_per_sm) {
+    const void* fn = kn_select(ia, ib, mt, vec4);
+    if (!fn) return cudaErrorInvalidValue;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, fn, kThreads, 0);
+}
+
+cudaError_t launch_gemv_kn(In ia, In ib, const GemmArgs& g, const GemvKnPlan& p, float* ws,
+                           uint32_t* counters, cudaStream_t s) {
+    const void* fn = kn_select(ia, ib, p.mt, p.vec4);
+    if (!fn || g.M > p.mt || p.splits < 1 || p.kchunk < 1) return cudaErrorInvalidValue;
+    if (p.splits > 1 && (!ws || !counters)) return cudaErrorInvalidValue;
+    KnParams kp;
+    kp.g = g;
+    kp.splits = p.splits;
+    kp.kchunk = p.kchunk;
+    kp.n_pad = gemv_kn_tiles(g.N) * kTileN;
+    kp.ws = ws;
+    kp.counters = counters;
+    dim3 grid(gemv_kn_tiles(g.N), p.splits);
+    void* args[] = {&kp};
+    return cudaLaunchKernel(fn, grid, dim3(kThreads), args, 0, s);
+}
+
+}  // namespace dnnopt_b200

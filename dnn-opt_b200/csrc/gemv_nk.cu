@@ -1,0 +1,283 @@
+// Small-M (M <= 8) dot-form GEMV for a B stored N x K (K contiguous):
+//   C[m, n] = epilogue( sum_k A[m, k] * B[n, k] )
+//
+// Serves:
+//   * gemm_int8_int8int8int32 (reference src/gemm/gemm_int8_native.cpp:189-248,
+//     whose B is [N, K] with ldb >= K): exact int32 dot products via dp4a.
+//   * the FP32-API gemm_int8 after quantisation (reference
+//     src/gemm/gemm_smallm_int8.cpp:198-236, :355-390): int8 dot + dequant.
+//   * FP32 GEMM with op(B) = B^T (cblas_sgemm with TransB): fp32 FMA.
+//   * the config-5 decode-FFN weight GEMM: bf16 activations x OCP-e4m3
+//     weights with a per-row FP32 scale, bf16 output (CUDA-core variant).
+//
+// Each warp owns whole rows of B; lanes stride along K with 16-byte loads, so
+// a warp reads 512 contiguous bytes per step and each lane keeps several loads
+// in flight.  A (M x K, at most 8 rows) is staged once in shared memory and
+// read back with conflict-free 16-byte loads; per-row partial sums are reduced
+// with warp shuffles.  Integer accumulation is exact in any order, so the
+// int8 path is bit-identical to the reference's scalar loop.
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace dnnopt_b200 {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+
+struct NkParams {
+    GemmArgs g;
+    int rows_per_cta;
+    const float* scales;
+};
+
+template <DotKind K> struct Tr;
+
+template <> struct Tr<DotKind::F32> {
+    using TA = float; using TB = float; using Acc = float;
+    static constexpr int EPC = 4;   // B elements per 16-byte chunk
+    __device__ static void dot(const uint4& b, const TA* a, Acc& acc) {
+        const float4 av = *reinterpret_cast<const float4*>(a);
+        acc = fmaf(av.x, __uint_as_float(b.x), acc);
+        acc = fmaf(av.y, __uint_as_float(b.y), acc);
+        acc = fmaf(av.z, __uint_as_float(b.z), acc);
+        acc = fmaf(av.w, __uint_as_float(b.w), acc);
+    }
+    __device__ static Acc one(TA a, TB b) { return a * b; }
+};
+
+template <> struct Tr<DotKind::S8S32> {
+    using TA = int8_t; using TB = int8_t; using Acc = int32_t;
+    static constexpr int EPC = 16;
+    __device__ static void dot(const uint4& b, const TA* a, Acc& acc) {
+        const int4 av = *reinterpret_cast<const int4*>(a);
+        acc = __dp4a(av.x, static_cast<int>(b.x), acc);
+        acc = __dp4a(av.y, static_cast<int>(b.y), acc);
+        acc = __dp4a(av.z, static_cast<int>(b.z), acc);
+        acc = __dp4a(av.w, static_cast<int>(b.w), acc);
+    }
+    __device__ static Acc one(TA a, TB b) { return static_cast<int32_t>(a) * static_cast<int32_t>(b); }
+};
+
+template <> struct Tr<DotKind::S8DQ> : Tr<DotKind::S8S32> {};
+
+template <> struct Tr<DotKind::E4M3> {
+    using TA = uint16_t; using TB = uint8_t; using Acc = float;
+    static constexpr int EPC = 16;
+    __device__ static void dot(const uint4& b, const TA* a, Acc& acc) {
+        const uint4 a0 = *reinterpret_cast<const uint4*>(a);
+        const uint4 a1 = *reinterpret_cast<const uint4*>(a + 8);
+        const uint32_t aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            float2 lo = e4m3x2_to_f32x2(static_cast<uint16_t>(bw[q] & 0xFFFFu));
+            float2 hi = e4m3x2_to_f32x2(static_cast<uint16_t>(bw[q] >> 16));
+            uint32_t x0 = aw[2 * q], x1 = aw[2 * q + 1];
+            acc = fmaf(__uint_as_float(x0 << 16), lo.x, acc);
+            acc = fmaf(__uint_as_float(x0 & 0xFFFF0000u), lo.y, acc);
+            acc = fmaf(__uint_as_float(x1 << 16), hi.x, acc);
+            acc = fmaf(__uint_as_float(x1 & 0xFFFF0000u), hi.y, acc);
+        }
+    }
+    __device__ static Acc one(TA a, TB b) {
+        float2 v = e4m3x2_to_f32x2(static_cast<uint16_t>(b));
+        return bf16_bits_to_f32(a) * v.x;
+    }
+};
+
+template <typename T>
+__device__ __forceinline__ T warp_sum(T v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+
+template <DotKind KIND, int MT, bool VEC>
+__global__ void __launch_bounds__(kThreads)
+gemv_nk_kernel(const NkParams p) {
+    using T = Tr<KIND>;
+    using TA = typename T::TA;
+    using TB = typename T::TB;
+    using Acc = typename T::Acc;
+    constexpr int EPC = T::EPC;
+    constexpr int U = 4;   // 16-byte chunks in flight per lane
+
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    TA* sA = reinterpret_cast<TA*>(smem_raw);   // [MT][kpad]
+
+    const GemmArgs& g = p.g;
+    const int K = g.K;
+    const int kpad = (K + EPC - 1) / EPC * EPC;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const TA* A = static_cast<const TA*>(g.A);
+    const TB* B = static_cast<const TB*>(g.B);
+
+    // Stage A (rows >= M and the K tail are zero).
+    for (int idx = tid; idx < MT * kpad; idx += kThreads) {
+        int m = idx / kpad, k = idx - m * kpad;
+        TA v = TA(0);
+        if (m < g.M && k < K)
+            v = A[g.a_trans ? (int64_t)k * g.lda + m : (int64_t)m * g.lda + k];
+        sA[idx] = v;
+    }
+    __syncthreads();
+
+    const int row_begin = blockIdx.x * p.rows_per_cta;
+    const int row_end = min(g.N, row_begin + p.rows_per_cta);
+    const int nchunks = VEC ? K / EPC : 0;   // full 16-byte chunks
+
+    for (int n = row_begin + warp; n < row_end; n += kWarps) {
+        const TB* brow = B + (int64_t)n * g.ldb;
+        Acc acc[MT];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) acc[m] = Acc(0);
+
+        if constexpr (VEC) {
+            const uint4* b4 = reinterpret_cast<const uint4*>(brow);
+            for (int q0 = lane; q0 < nchunks; q0 += 32 * U) {
+                uint4 bv[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    int q = q0 + 32 * u;
+                    bv[u] = (q < nchunks) ? __ldg(b4 + q) : make_uint4(0u, 0u, 0u, 0u);
+                }
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    int q = q0 + 32 * u;
+                    if (q < nchunks) {
+#pragma unroll
+                        for (int m = 0; m < MT; ++m) T::dot(bv[u], sA + m * kpad + q * EPC, acc[m]);
+                    }
+                }
+            }
+        }
+        // Scalar remainder (the whole row when rows are not 16-byte aligned).
+        for (int k = nchunks * EPC + lane; k < K; k += 32) {
+            TB bk = brow[k];
+#pragma unroll
+            for (int m = 0; m < MT; ++m) acc[m] += T::one(sA[m * kpad + k], bk);
+        }
+
+#pragma unroll
+        for (int m = 0; m < MT; ++m) acc[m] = warp_sum(acc[m]);
+
+        if (lane < MT && lane < g.M) {
+            Acc s = acc[0];
+#pragma unroll
+            for (int m = 1; m < MT; ++m) if (lane == m) s = acc[m];
+            const int m = lane;
+            if constexpr (KIND == DotKind::F32) {
+                float* cp = static_cast<float*>(g.C) + (int64_t)m * g.ldc + n;
+                *cp = (g.beta == 0.0f) ? g.alpha * s : fmaf(g.alpha, s, g.beta * *cp);
+            } else if constexpr (KIND == DotKind::S8S32) {
+                static_cast<int32_t*>(g.C)[(int64_t)m * g.ldc + n] = s;
+            } else if constexpr (KIND == DotKind::S8DQ) {
+                // C = (beta == 0 ? 0 : beta*C) + (alpha*(sA*sB)) * float(acc), each op rounded.
+                float* cp = static_cast<float*>(g.C) + (int64_t)m * g.ldc + n;
+                float scale = __fmul_rn(g.alpha, __fmul_rn(p.scales[0], p.scales[1]));
+                float c0 = (g.beta == 0.0f) ? 0.0f : __fmul_rn(g.beta, *cp);
+                *cp = __fadd_rn(c0, __fmul_rn(scale, static_cast<float>(s)));
+            } else {
+                float v = s * p.scales[n];
+                static_cast<uint16_t*>(g.C)[(int64_t)m * g.ldc + n] =
+                    __bfloat16_as_ushort(__float2bfloat16_rn(v));
+            }
+        }
+    }
+}
+
+template <DotKind KIND, int MT, bool VEC>
+const void* nk_fn() {
+    return reinterpret_cast<const void*>(&gemv_nk_kernel<KIND, MT, VEC>);
+}
+
+template <DotKind KIND>
+const void* nk_select_mt(int mt, int vec) {
+    switch (mt) {
+        case 1: return vec ? nk_fn<KIND, 1, true>() : nk_fn<KIND, 1, false>();
+        case 2: return vec ? nk_fn<KIND, 2, true>() : nk_fn<KIND, 2, false>();
+        case 4: return vec ? nk_fn<KIND, 4, true>() : nk_fn<KIND, 4, false>();
+        case 8: return vec ? nk_fn<KIND, 8, true>() : nk_fn<KIND, 8, false>();
+        default: return nullptr;
+    }
+}
+
+const void* nk_select(DotKind kind, int mt, int vec) {
+    switch (kind) {
+        case DotKind::F32: return nk_select_mt<DotKind::F32>(mt, vec);
+        case DotKind::S8S32: return nk_select_mt<DotKind::S8S32>(mt, vec);
+        case DotKind::S8DQ: return nk_select_mt<DotKind::S8DQ>(mt, vec);
+        case DotKind::E4M3: return nk_select_mt<DotKind::E4M3>(mt, vec);
+    }
+    return nullptr;
+}
+
+size_t elem_a_bytes(DotKind kind) {
+    switch (kind) {
+        case DotKind::F32: return 4;
+        case DotKind::E4M3: return 2;
+        default: return 1;
+    }
+}
+
+int epc(DotKind kind) { return kind == DotKind::F32 ? 4 : 16; }
+
+}  // namespace
+
+size_t gemv_nk_smem_bytes(DotKind kind, int mt, int K) {
+    int e = epc(kind);
+    size_t kpad = (static_cast<size_t>(K) + e - 1) / e * e;
+    return static_cast<size_t>(mt) * kpad * elem_a_bytes(kind);
+}
+
+// Raises the kernel's dynamic shared-memory limit once per (device, kernel)
+// to the library maximum, so later launches (including under stream capture)
+// make no attribute calls.
+static cudaError_t prepare_nk(const void* fn, size_t smem) {
+    if (smem <= 48 * 1024) return cudaSuccess;
+    static std::mutex mu;
+    static std::set<std::pair<int, const void*>> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(mu);
+    if (done.count({dev, fn})) return cudaSuccess;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kGemvNkMaxSmem));
+    if (e == cudaSuccess) done.insert({dev, fn});
+    return e;
+}
+
+cudaError_t gemv_nk_occupancy(DotKind kind, int mt, int vec, int K, int* blocks_per_sm) {
+    const void* fn = nk_select(kind, mt, vec);
+    if (!fn) return cudaErrorInvalidValue;
+    size_t smem = gemv_nk_smem_bytes(kind, mt, K);
+    cudaError_t e = prepare_nk(fn, smem);
+    if (e != cudaSuccess) return e;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, fn, kThreads, smem);
+}
+
+cudaError_t launch_gemv_nk(DotKind kind, const GemmArgs& g, const GemvNkPlan& p,
+                           const float* scales, cudaStream_t s) {
+    const void* fn = nk_select(kind, p.mt, p.vec);
+    if (!fn || g.M > p.mt || p.grid < 1) return cudaErrorInvalidValue;
+    size_t smem = gemv_nk_smem_bytes(kind, p.mt, g.K);
+    if (smem > kGemvNkMaxSmem) return cudaErrorInvalidValue;
+    cudaError_t e = prepare_nk(fn, smem);
+    if (e != cudaSuccess) return e;
+    NkParams kp;
+    kp.g = g;
+    kp.rows_per_cta = (g.N + p.grid - 1) / p.grid;
+    kp.scales = scales;
+    int grid = (g.N + kp.rows_per_cta - 1) / kp.rows_per_cta;
+    void* args[] = {&kp};
+    return cudaLaunchKernel(fn, dim3(grid), dim3(kThreads), args, smem, s);
+}
+
+}  // namespace dnnopt_b200

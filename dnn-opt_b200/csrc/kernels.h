@@ -1,0 +1,97 @@
+// Host-side launch interface of the sm_100a kernels (internal to the library).
+// The public boundary is include/dnnopt_b200.h; these entry points take plain
+// device pointers and a stream and return cudaError_t.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace dnnopt_b200 {
+
+// Element encodings an FP32-accumulating kernel can read.
+enum class In : int {
+    F32 = 0,    // float
+    BF16 = 1,   // bfloat16 bits (uint16_t)
+    F32R = 2,   // float, rounded to bf16 (RNE) on load: the FP32-API gemm_bf16
+    RE4 = 3,    // reference fp8_e4m3_t byte (bias-8 codec, gemm_types.h:51-121)
+    RE5 = 4,    // reference fp8_e5m2_t byte (bias-16 codec, gemm_types.h:127-197)
+};
+
+// op(A)[M,K] * op(B)[K,N]: row-major views with optional transposition.
+// a_trans: A is stored K x M (element (m,k) at A[k*lda + m]).
+// b_trans: B is stored N x K (element (k,n) at B[n*ldb + k]).
+struct GemmArgs {
+    int M, N, K;
+    float alpha, beta;
+    const void* A;
+    int64_t lda;
+    int a_trans;
+    const void* B;
+    int64_t ldb;
+    int b_trans;
+    void* C;
+    int64_t ldc;
+};
+
+// ---- small-M FP32-output GEMV, B is K x N (N contiguous) -------------------
+// Split-K over gridDim.y with a deterministic last-CTA reduction through
+// `ws` (splits * MT * n_pad floats) and `counters` (one per 128-column tile,
+// zero on entry, left zero on exit).
+struct GemvKnPlan {
+    int mt;        // 1, 2, 4 or 8 (M <= mt)
+    int vec4;      // 1: 4-wide vector loads of B rows (aligned rows)
+    int splits;    // K splits (gridDim.y)
+    int kchunk;    // rows of K per split
+};
+int gemv_kn_tiles(int N);
+size_t gemv_kn_ws_floats(const GemvKnPlan& p, int N);
+cudaError_t gemv_kn_occupancy(In ia, In ib, int mt, int vec4, int* blocks_per_sm);
+cudaError_t launch_gemv_kn(In ia, In ib, const GemmArgs& g, const GemvKnPlan& p, float* ws,
+                           uint32_t* counters, cudaStream_t s);
+
+// ---- small-M dot-form GEMV, B is N x K (K contiguous) ----------------------
+enum class DotKind : int {
+    F32 = 0,     // fp32 x fp32 -> fp32, alpha/beta epilogue
+    S8S32 = 1,   // int8 x int8 -> int32 (exact), C overwritten
+    E4M3 = 2,    // bf16 x OCP e4m3 * scale[n] -> bf16
+    S8DQ = 3,    // int8 x int8 -> fp32 dequant: C = (alpha*sA*sB)*acc + beta*C
+};
+struct GemvNkPlan {
+    int mt;       // 1, 2, 4 or 8
+    int vec;      // 1: 16-byte vector loads of B rows
+    int grid;     // CTAs (rows are split evenly across them)
+};
+// The whole A panel (mt x K) is staged in shared memory, so K is bounded by
+// kGemvNkMaxSmem / (mt * sizeof(A element)).
+constexpr size_t kGemvNkMaxSmem = 200 * 1024;
+size_t gemv_nk_smem_bytes(DotKind kind, int mt, int K);
+cudaError_t launch_gemv_nk(DotKind kind, const GemmArgs& g, const GemvNkPlan& p,
+                           const float* scales, cudaStream_t s);
+cudaError_t gemv_nk_occupancy(DotKind kind, int mt, int vec, int K, int* blocks_per_sm);
+
+// ---- general tiled SIMT kernels (any M, N, K, strides, transposes) ----------
+cudaError_t launch_gemm_tile_f32(In ia, In ib, const GemmArgs& g, cudaStream_t s);
+// int8: A is M x K (lda), B is N x K (ldb); kind S8S32 or S8DQ (scales = {sA, sB} on device).
+cudaError_t launch_gemm_tile_s8(DotKind kind, const GemmArgs& g, const float* scales,
+                                cudaStream_t s);
+
+// ---- FP32-API int8 quantisation (per-tensor absmax / 127, lrintf, clamp) ----
+// scales[0..1] receive sA, sB; absmax[0..1] is scratch (zeroed by this call).
+cudaError_t launch_absmax2(const GemmArgs& g, uint32_t* absmax_bits, cudaStream_t s);
+cudaError_t launch_quantize_s8(const GemmArgs& g, const uint32_t* absmax_bits, float* scales,
+                               int8_t* qa, int8_t* qb_nk, cudaStream_t s);
+
+// gemm_fp8 FP32 API: encode A with the reference e4m3 codec (dense M x K) and
+// B with the reference e5m2 codec (dense K x N).
+cudaError_t launch_quantize_ref_fp8(const GemmArgs& g, uint8_t* qa, uint8_t* qb, cudaStream_t s);
+
+cudaError_t launch_saxpy(int n, float alpha, const float* x, int incx, float* y, int incy,
+                         cudaStream_t s);
+
+// ---- BF16 tall-skinny tcgen05 GEMM (A row-major K-contiguous, TMA) ----------
+bool gemm_bf16_tc_supported(const GemmArgs& g);
+// err: device word that receives a KernelErrorCode when a bounded wait gives up.
+cudaError_t launch_gemm_bf16_tc(const GemmArgs& g, int num_sms, uint32_t* err, cudaStream_t s);
+
+
+}  // namespace dnnopt_b200

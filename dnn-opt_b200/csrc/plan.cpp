@@ -1,0 +1,336 @@
+// Plan selector and autotune cache.
+//
+// Dispatch rules (B200 re-statement of src/gemm/gemm.cpp:168-455, where the
+// reference routes by M < small_m_bound (8), N >= wide_n_bound and K):
+//   * M <= 8 and B stored K x N      -> GemvKn  (split-K streaming GEMV)
+//   * M <= 8 and B stored N x K      -> GemvNk  (dot-form GEMV; all int8 calls)
+//   * BF16, large M, N <= 256        -> Bf16Tc  (tcgen05 tall-skinny)
+//   * config-5 e4m3 with M > 8       -> GemvNkRows (dot form per 8-row block)
+//   * anything else                  -> TileF32 / TileS8 (general SIMT tiles)
+// The split-K factor of GemvKn is chosen so that the grid is one wave of
+// resident CTAs (strips x splits ~= occupancy x SMs), never below 32 K-rows
+// per split; autotune times {s/2, s, 2s} and keeps the fastest.
+#include "plan.h"
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+
+namespace dnnopt_b200 {
+
+namespace {
+
+int mt_for(int M) { return M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8)); }
+
+In in_a(Kind k) {
+    switch (k) {
+        case Kind::BF16F32: return In::BF16;
+        case Kind::F32BF16R: return In::F32R;
+        case Kind::RE4E5: return In::RE4;
+        case Kind::RE5E5: return In::RE5;
+        default: return In::F32;
+    }
+}
+In in_b(Kind k) {
+    switch (k) {
+        case Kind::BF16F32: return In::BF16;
+        case Kind::F32BF16R: return In::F32R;
+        case Kind::RE4E5:
+        case Kind::RE5E5: return In::RE5;
+        default: return In::F32;
+    }
+}
+
+DotKind dot_kind(Kind k) {
+    switch (k) {
+        case Kind::S8S32: return DotKind::S8S32;
+        case Kind::F32S8Q: return DotKind::S8DQ;
+        case Kind::E4M3BF16: return DotKind::E4M3;
+        default: return DotKind::F32;
+    }
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int kn_occupancy(Kind kind, int mt, int vec4, const DeviceInfo& info) {
+    if (!info.have_device) return 3;
+    static std::mutex mu;
+    static std::map<int, int> memo;
+    int key = static_cast<int>(kind) * 100 + mt * 10 + vec4;
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = memo.find(key);
+    if (it != memo.end()) return it->second;
+    int occ = 0;
+    if (gemv_kn_occupancy(in_a(kind), in_b(kind), mt, vec4, &occ) != cudaSuccess || occ < 1) {
+        cudaGetLastError();
+        occ = 1;
+    }
+    memo[key] = occ;
+    return occ;
+}
+
+int nk_occupancy(DotKind kind, int mt, int vec, int K, const DeviceInfo& info) {
+    if (!info.have_device) return 2;
+    int occ = 0;
+    if (gemv_nk_occupancy(kind, mt, vec, K, &occ) != cudaSuccess || occ < 1) {
+        cudaGetLastError();
+        occ = 1;
+    }
+    return occ;
+}
+
+}  // namespace
+
+int elem_bytes_a(Kind k) {
+    switch (k) {
+        case Kind::BF16F32:
+        case Kind::E4M3BF16: return 2;
+        case Kind::S8S32:
+        case Kind::RE4E5:
+        case Kind::RE5E5: return 1;
+        case Kind::F32S8Q: return 1;   // after quantisation
+        default: return 4;
+    }
+}
+
+int elem_bytes_b(Kind k) {
+    switch (k) {
+        case Kind::BF16F32: return 2;
+        case Kind::S8S32:
+        case Kind::F32S8Q:
+        case Kind::E4M3BF16:
+        case Kind::RE4E5:
+        case Kind::RE5E5: return 1;
+        default: return 4;
+    }
+}
+
+const char* kernel_name(KernelId k) {
+    switch (k) {
+        case KernelId::GemvKn: return "gemv_kn_splitk";
+        case KernelId::GemvNk: return "gemv_nk_dot";
+        case KernelId::TileF32: return "gemm_tile_f32";
+        case KernelId::TileS8: return "gemm_tile_s8";
+        case KernelId::Bf16Tc: return "gemm_bf16_tcgen05";
+        case KernelId::GemvNkRows: return "gemv_nk_dot_rowblocks";
+    }
+    return "?";
+}
+
+GemvKnPlan kn_plan_for(Kind kind, const GemmArgs& g, const DeviceInfo& info, int splits_hint) {
+    GemvKnPlan p;
+    p.mt = mt_for(g.M);
+    const size_t eb = static_cast<size_t>(elem_bytes_b(kind));
+    p.vec4 = (aligned(g.B, 4 * eb) && g.ldb % 4 == 0) ? 1 : 0;
+    const int tiles = gemv_kn_tiles(g.N);
+    int splits = splits_hint;
+    if (splits <= 0) {
+        const int occ = kn_occupancy(kind, p.mt, p.vec4, info);
+        splits = (occ * info.num_sms) / tiles;
+    }
+    const int max_splits = g.K / 32 > 1 ? g.K / 32 : 1;
+    if (splits > max_splits) splits = max_splits;
+    if (splits < 1) splits = 1;
+    int kchunk = (g.K + splits - 1) / splits;
+    kchunk = (kchunk + 7) / 8 * 8;
+    p.kchunk = kchunk;
+    p.splits = (g.K + kchunk - 1) / kchunk;
+    return p;
+}
+
+GemvNkPlan nk_plan_for(Kind kind, const GemmArgs& g, const DeviceInfo& info, int grid_hint) {
+    GemvNkPlan p;
+    p.mt = mt_for(g.M < 8 ? g.M : 8);
+    const size_t eb = static_cast<size_t>(elem_bytes_b(kind));
+    p.vec = (aligned(g.B, 16) && (static_cast<size_t>(g.ldb) * eb) % 16 == 0) ? 1 : 0;
+    int grid = grid_hint;
+    if (grid <= 0) grid = nk_occupancy(dot_kind(kind), p.mt, p.vec, g.K, info) * info.num_sms;
+    if (grid > g.N) grid = g.N;
+    if (grid < 1) grid = 1;
+    p.grid = grid;
+    return p;
+}
+
+Plan heuristic_plan(Kind kind, const GemmArgs& g, const DeviceInfo& info) {
+    Plan p;
+    const bool dot_fits = gemv_nk_smem_bytes(dot_kind(kind), mt_for(g.M < 8 ? g.M : 8), g.K) <=
+                          kGemvNkMaxSmem;
+    switch (kind) {
+        case Kind::S8S32:
+        case Kind::F32S8Q:
+            if (g.M <= 8 && dot_fits) {
+                p.kernel = KernelId::GemvNk;
+                p.nk = nk_plan_for(kind, g, info, 0);
+            } else {
+                p.kernel = KernelId::TileS8;
+            }
+            return p;
+        case Kind::E4M3BF16:
+            p.kernel = (g.M <= 8) ? KernelId::GemvNk : KernelId::GemvNkRows;
+            p.nk = nk_plan_for(kind, g, info, 0);
+            if (!dot_fits) p.kernel = KernelId::TileF32;   // rejected by the caller (no tile path)
+            return p;
+        default:
+            break;
+    }
+    if (g.M <= 8 && !g.b_trans) {
+        p.kernel = KernelId::GemvKn;
+        p.kn = kn_plan_for(kind, g, info, 0);
+        return p;
+    }
+    if (kind == Kind::F32 && g.M <= 8 && g.b_trans && dot_fits) {
+        p.kernel = KernelId::GemvNk;
+        p.nk = nk_plan_for(kind, g, info, 0);
+        return p;
+    }
+    if (kind == Kind::BF16F32 && g.M > 8 && info.have_device && gemm_bf16_tc_supported(g)) {
+        p.kernel = KernelId::Bf16Tc;
+        return p;
+    }
+    p.kernel = KernelId::TileF32;
+    return p;
+}
+
+std::string describe_plan(Kind, const GemmArgs&, const Plan& p) {
+    char buf[160];
+    switch (p.kernel) {
+        case KernelId::GemvKn:
+            std::snprintf(buf, sizeof(buf), "%s mt=%d vec4=%d splits=%d kchunk=%d%s",
+                          kernel_name(p.kernel), p.kn.mt, p.kn.vec4, p.kn.splits, p.kn.kchunk,
+                          p.tuned ? " tuned" : "");
+            break;
+        case KernelId::GemvNk:
+        case KernelId::GemvNkRows:
+            std::snprintf(buf, sizeof(buf), "%s mt=%d vec=%d grid=%d%s", kernel_name(p.kernel),
+                          p.nk.mt, p.nk.vec, p.nk.grid, p.tuned ? " tuned" : "");
+            break;
+        default:
+            std::snprintf(buf, sizeof(buf), "%s", kernel_name(p.kernel));
+    }
+    return buf;
+}
+
+// ---------------------------------------------------------------------------
+// Autotune cache
+// ---------------------------------------------------------------------------
+namespace {
+
+struct Entry {
+    int32_t kernel, p0, p1, mt;
+    float time_us;
+};
+
+std::mutex g_cache_mu;
+std::map<uint64_t, Entry> g_cache;
+int g_autotune = -1;   // -1: read DNNOPT_AUTOTUNE on first query
+
+uint64_t fnv1a(const void* data, size_t n) {
+    const unsigned char* p = static_cast<const unsigned char*>(data);
+    uint64_t h = 1469598103934665603ull;
+    for (size_t i = 0; i < n; ++i) { h ^= p[i]; h *= 1099511628211ull; }
+    return h;
+}
+
+constexpr char kMagic[8] = {'D', 'N', 'N', 'A', 'U', 'T', 'O', '\0'};
+constexpr uint32_t kVersion = 4;   // reference files are v1-v3 (CPU blocking choices)
+
+}  // namespace
+
+bool autotune_enabled() {
+    std::lock_guard<std::mutex> lk(g_cache_mu);
+    if (g_autotune < 0) {
+        const char* e = std::getenv("DNNOPT_AUTOTUNE");
+        g_autotune = (e && (e[0] == '1' || e[0] == 'y' || e[0] == 'Y')) ? 1 : 0;
+    }
+    return g_autotune == 1;
+}
+
+void set_autotune_enabled(bool on) {
+    std::lock_guard<std::mutex> lk(g_cache_mu);
+    g_autotune = on ? 1 : 0;
+}
+
+uint64_t plan_key(Kind kind, const GemmArgs& g, int vec) {
+    int64_t k[10] = {static_cast<int64_t>(kind), g.M, g.N, g.K, g.lda, g.ldb, g.ldc,
+                     g.a_trans, g.b_trans, vec};
+    return fnv1a(k, sizeof(k));
+}
+
+bool cache_lookup(uint64_t key, Plan* out) {
+    std::lock_guard<std::mutex> lk(g_cache_mu);
+    auto it = g_cache.find(key);
+    if (it == g_cache.end()) return false;
+    const Entry& e = it->second;
+    out->kernel = static_cast<KernelId>(e.kernel);
+    out->tuned = true;
+    if (out->kernel == KernelId::GemvKn) {
+        out->kn.splits = e.p0;
+        out->kn.kchunk = e.p1;
+        out->kn.mt = e.mt;
+    } else {
+        out->nk.grid = e.p0;
+        out->nk.mt = e.mt;
+    }
+    return true;
+}
+
+void cache_store(uint64_t key, const Plan& p, float time_us) {
+    Entry e;
+    e.kernel = static_cast<int32_t>(p.kernel);
+    if (p.kernel == KernelId::GemvKn) { e.p0 = p.kn.splits; e.p1 = p.kn.kchunk; e.mt = p.kn.mt; }
+    else { e.p0 = p.nk.grid; e.p1 = 0; e.mt = p.nk.mt; }
+    e.time_us = time_us;
+    std::lock_guard<std::mutex> lk(g_cache_mu);
+    if (g_cache.size() >= 4096) g_cache.erase(g_cache.begin());
+    g_cache[key] = e;
+}
+
+int cache_save(const char* path) {
+    std::lock_guard<std::mutex> lk(g_cache_mu);
+    FILE* f = std::fopen(path, "wb");
+    if (!f) return -1;
+    uint32_t n = static_cast<uint32_t>(g_cache.size());
+    bool ok = std::fwrite(kMagic, 1, 8, f) == 8 && std::fwrite(&kVersion, 4, 1, f) == 1 &&
+              std::fwrite(&n, 4, 1, f) == 1;
+    for (const auto& kv : g_cache) {
+        ok = ok && std::fwrite(&kv.first, 8, 1, f) == 1 && std::fwrite(&kv.second, sizeof(Entry), 1, f) == 1;
+    }
+    ok = (std::fclose(f) == 0) && ok;
+    return ok ? static_cast<int>(n) : -1;
+}
+
+int cache_load(const char* path) {
+    FILE* f = std::fopen(path, "rb");
+    if (!f) return -1;
+    char magic[8];
+    uint32_t ver = 0, n = 0;
+    if (std::fread(magic, 1, 8, f) != 8 || std::memcmp(magic, kMagic, 8) != 0 ||
+        std::fread(&ver, 4, 1, f) != 1 || ver != kVersion || std::fread(&n, 4, 1, f) != 1 ||
+        n > 1000000u) {
+        std::fclose(f);
+        return -1;
+    }
+    std::map<uint64_t, Entry> loaded;
+    for (uint32_t i = 0; i < n; ++i) {
+        uint64_t key;
+        Entry e;
+        if (std::fread(&key, 8, 1, f) != 1 || std::fread(&e, sizeof(Entry), 1, f) != 1) {
+            std::fclose(f);
+            return -1;
+        }
+        loaded[key] = e;
+    }
+    std::fclose(f);
+    std::lock_guard<std::mutex> lk(g_cache_mu);
+    for (const auto& kv : loaded) g_cache[kv.first] = kv.second;
+    return static_cast<int>(loaded.size());
+}
+
+int cache_entries() {
+    std::lock_guard<std::mutex> lk(g_cache_mu);
+    return static_cast<int>(g_cache.size());
+}
+
+}  // namespace dnnopt_b200

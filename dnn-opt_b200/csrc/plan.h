@@ -1,0 +1,70 @@
+// Plan selector: the B200 replacement of the reference's shape dispatcher
+// (src/gemm/gemm.cpp:168-455) and CPU autotuner (src/gemm/gemm_autotune.cpp,
+// src/autotune/shape_cache.cpp).  For each (kind, shape, layout) it picks a
+// kernel family and its launch shape (split-K factor or grid), optionally by
+// timing candidates (autotune), and caches the choice.
+#pragma once
+
+#include <cstdint>
+#include <string>
+
+#include "kernels.h"
+
+namespace dnnopt_b200 {
+
+enum class Kind : int {
+    F32 = 0,        // gemm_fp32
+    BF16F32 = 1,    // gemm_bf16_bf16bf16f32
+    F32BF16R = 2,   // gemm_bf16 (FP32 API)
+    F32S8Q = 3,     // gemm_int8 (FP32 API)
+    S8S32 = 4,      // gemm_int8_int8int8int32
+    E4M3BF16 = 5,   // config-5 decode-FFN weight GEMM
+    RE4E5 = 6,      // gemm_fp8_e4m3
+    RE5E5 = 7,      // gemm_fp8_e5m2
+};
+
+enum class KernelId : int {
+    GemvKn = 0,     // small-M split-K, B K x N
+    GemvNk = 1,     // small-M dot form, B N x K
+    TileF32 = 2,    // general SIMT FP32-accumulate tile
+    TileS8 = 3,     // general SIMT int8 tile
+    Bf16Tc = 4,     // tcgen05 tall-skinny BF16
+    GemvNkRows = 5, // dot form over 8-row blocks of A (M > 8)
+};
+
+struct Plan {
+    KernelId kernel = KernelId::TileF32;
+    GemvKnPlan kn{};
+    GemvNkPlan nk{};
+    bool tuned = false;
+};
+
+struct DeviceInfo {
+    int num_sms = 148;
+    bool have_device = false;
+};
+
+GemvKnPlan kn_plan_for(Kind kind, const GemmArgs& g, const DeviceInfo& info, int splits_hint);
+GemvNkPlan nk_plan_for(Kind kind, const GemmArgs& g, const DeviceInfo& info, int grid_hint);
+
+// Heuristic plan (no timing).  Needs no device when info.have_device is false
+// (occupancy is then estimated).
+Plan heuristic_plan(Kind kind, const GemmArgs& g, const DeviceInfo& info);
+const char* kernel_name(KernelId k);
+std::string describe_plan(Kind kind, const GemmArgs& g, const Plan& p);
+
+// Autotune cache (FNV-1a keyed, persisted as "DNNAUTO" version 4).
+bool autotune_enabled();
+void set_autotune_enabled(bool on);
+uint64_t plan_key(Kind kind, const GemmArgs& g, int vec);
+bool cache_lookup(uint64_t key, Plan* out);
+void cache_store(uint64_t key, const Plan& p, float time_us);
+int cache_save(const char* path);
+int cache_load(const char* path);
+int cache_entries();
+
+// Element sizes of A and B for a kind (bytes).
+int elem_bytes_a(Kind k);
+int elem_bytes_b(Kind k);
+
+}  // namespace dnnopt_b200

@@ -1,0 +1,196 @@
+/*
+ * dnnopt_b200.h -- C ABI of the B200-native small-M / irregular-N /
+ * tall-skinny GEMM library (libdnnopt_b200.so).
+ *
+ * Drop-in boundary for the GEMM hot path of xuefenghao5121/DNN-Opt.  Plain C
+ * types only (no CUDA, torch or C++ types), so cgo / JNI / ctypes / N-API can
+ * bind it directly.  Two families of entry points:
+ *
+ *   dnnopt_gemm_*       Same arguments as the reference's public C++ API
+ *                       (include/dnnopt/gemm/gemm.h:10-102): row-major,
+ *                       C = alpha*A*B + beta*C, pointers may be host memory
+ *                       (pageable or pinned) or device memory.  Synchronous:
+ *                       results are in C when the call returns.  They run on
+ *                       the stream set with dnnopt_set_stream (default: a
+ *                       library-owned stream of the current device).
+ *
+ *   dnnopt_cuda_gemm_*  Device pointers only, asynchronous on `stream` (a
+ *                       cudaStream_t passed as void*; NULL is the legacy
+ *                       default stream).  Nothing is copied or synchronised.
+ *
+ * Error behaviour: the reference's functions return void and silently return
+ * on M, N or K <= 0 (src/gemm/gemm.cpp:180).  Here every function returns a
+ * dnnopt_status; M, N or K == 0 is a successful no-op exactly as in the
+ * reference, while negative sizes, too-small leading dimensions and NULL
+ * operands are DNNOPT_STATUS_INVALID_VALUE.  The C++ mirror (libdnnopt_b200.so
+ * also exports dnnopt::gemm_fp32 etc. with the reference's void signatures)
+ * records the status for dnnopt_get_last_error().
+ *
+ * Matrix conventions: A is M x K, B is K x N, C is M x N, all row-major with
+ * leading dimensions lda, ldb, ldc (elements), except where an entry point
+ * says otherwise (the int8 entry points read B as N x K, K contiguous, exactly
+ * as the reference implementation does: src/gemm/gemm_int8_native.cpp:217).
+ */
+#ifndef DNNOPT_B200_H
+#define DNNOPT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DNNOPT_B200_ABI_VERSION 1
+
+typedef enum dnnopt_status {
+    DNNOPT_STATUS_SUCCESS = 0,
+    DNNOPT_STATUS_INVALID_VALUE = 1,   /* negative size, ld too small, NULL operand */
+    DNNOPT_STATUS_NOT_SUPPORTED = 2,   /* no GPU path for this combination */
+    DNNOPT_STATUS_CUDA_ERROR = 3,      /* a CUDA runtime call failed */
+    DNNOPT_STATUS_ALLOC_FAILED = 4,    /* device or pinned allocation failed */
+    DNNOPT_STATUS_NO_DEVICE = 5,       /* no CUDA device visible */
+    DNNOPT_STATUS_KERNEL_TIMEOUT = 6,  /* a bounded in-kernel wait gave up */
+    DNNOPT_STATUS_INJECTED_FAULT = 7   /* host-side fault injection (tests) */
+} dnnopt_status;
+
+/* Shape and epilogue of one GEMM call for the dnnopt_cuda_* entry points.
+ * trans_a: A is stored K x M (op(A) = A^T).  trans_b: B is stored N x K
+ * (op(B) = B^T).  Leading dimensions refer to the stored matrices. */
+typedef struct dnnopt_gemm_desc {
+    int M, N, K;
+    int lda, ldb, ldc;
+    float alpha, beta;
+    int trans_a, trans_b;
+} dnnopt_gemm_desc;
+
+/* ------------------------------------------------------------------------
+ * Reference-signature entry points (host or device pointers, synchronous)
+ * ---------------------------------------------------------------------- */
+
+/* Replaces dnnopt::gemm_fp32 (include/dnnopt/gemm/gemm.h:14-17,
+ * src/gemm/gemm.cpp:168-377).  FP32 FMA accumulation (never TF32). */
+int dnnopt_gemm_fp32(int M, int N, int K, float alpha, const float* A, int lda,
+                     const float* B, int ldb, float beta, float* C, int ldc);
+
+/* Replaces dnnopt::gemm_bf16 (gemm.h:28-31, src/gemm/gemm.cpp:379-416): FP32
+ * in/out, operands rounded to bf16 (round-to-nearest-even, gemm_types.h:18-24),
+ * FP32 accumulation. */
+int dnnopt_gemm_bf16(int M, int N, int K, float alpha, const float* A, int lda,
+                     const float* B, int ldb, float beta, float* C, int ldc);
+
+/* Replaces dnnopt::gemm_bf16_bf16bf16f32 (gemm.h:36-39,
+ * src/gemm/gemm_driver_bf16.cpp:134-218).  A, B are bf16 bit patterns. */
+int dnnopt_gemm_bf16_bf16bf16f32(int M, int N, int K, float alpha, const uint16_t* A, int lda,
+                                 const uint16_t* B, int ldb, float beta, float* C, int ldc);
+
+/* Replaces dnnopt::gemm_int8 (gemm.h:44-47, src/gemm/gemm.cpp:418-455) on its
+ * I8MM path: per-tensor absmax/127 scales, lrintf quantisation clamped to
+ * [-128, 127], exact int32 accumulation, C = (alpha*sA*sB)*acc + beta*C
+ * (src/gemm/gemm_smallm_int8.cpp:198-236, :355-390). */
+int dnnopt_gemm_int8(int M, int N, int K, float alpha, const float* A, int lda,
+                     const float* B, int ldb, float beta, float* C, int ldc);
+
+/* Replaces dnnopt::gemm_int8_int8int8int32 (gemm.h:55-58,
+ * src/gemm/gemm_int8_native.cpp:189-248).  B is N x K (K contiguous,
+ * ldb >= K), C is overwritten with exact int32 dot products. */
+int dnnopt_gemm_int8_int8int8int32(int M, int N, int K, const int8_t* A, int lda,
+                                   const int8_t* B, int ldb, int32_t* C, int ldc);
+
+/* Replace dnnopt::gemm_fp8_e4m3 / gemm_fp8_e5m2 / gemm_fp8 / has_fp8_support
+ * (gemm.h:70-93, src/gemm/gemm_fp8.cpp:32-146).  Operands use the reference's
+ * own fp8_e4m3_t / fp8_e5m2_t codecs (include/dnnopt/gemm/gemm_types.h:51-200),
+ * decoded exactly; FP32 accumulation.  dnnopt_gemm_fp8 quantises FP32 inputs
+ * with those codecs first (the reference's FP8-hardware branch). */
+int dnnopt_gemm_fp8_e4m3(int M, int N, int K, float alpha, const uint8_t* A, int lda,
+                         const uint8_t* B, int ldb, float beta, float* C, int ldc);
+int dnnopt_gemm_fp8_e5m2(int M, int N, int K, float alpha, const uint8_t* A, int lda,
+                         const uint8_t* B, int ldb, float beta, float* C, int ldc);
+int dnnopt_gemm_fp8(int M, int N, int K, float alpha, const float* A, int lda, const float* B,
+                    int ldb, float beta, float* C, int ldc);
+int dnnopt_has_fp8_support(void);
+
+/* Decode-FFN weight GEMM (the reference has only the
+ * FP32 stub above): C[m,n] = bf16_rne(scale[n] * sum_k A[m,k] * W[n,k]),
+ * A bf16 M x K, W OCP-E4M3FN N x K (K contiguous, ldw >= K), scale FP32[N],
+ * FP32 accumulation, C bf16 M x N. */
+int dnnopt_gemm_e4m3_bf16(int M, int N, int K, const uint16_t* A, int lda, const uint8_t* W,
+                          int ldw, const float* scale, uint16_t* C, int ldc);
+
+/* FP32 GEMM with transposition flags (host or device pointers, synchronous):
+ * the row-major core that cblas_sgemm / sgemm_ reduce to (reference
+ * src/blas/cblas_sgemm.cpp:67-99), without materialising transposes. */
+int dnnopt_gemm_f32_desc(const dnnopt_gemm_desc* d, const float* A, const float* B, float* C);
+
+/* Replaces cblas_saxpy (reference src/blas/cblas_saxpy.cpp:13-50):
+ * Y[i*incY] += alpha * X[i*incX] for i < N; N <= 0 or alpha == 0 is a no-op;
+ * negative increments are rejected. */
+int dnnopt_saxpy(int N, float alpha, const float* X, int incX, float* Y, int incY);
+
+/* Replaces dnnopt::gemm_set_num_threads / gemm_get_num_threads
+ * (gemm.h:97-100).  The value is stored and reported; GPU parallelism is
+ * chosen by the plan selector. */
+void dnnopt_gemm_set_num_threads(int n);
+int dnnopt_gemm_get_num_threads(void);
+
+/* ------------------------------------------------------------------------
+ * Device-pointer entry points (asynchronous on `stream`)
+ * ---------------------------------------------------------------------- */
+int dnnopt_cuda_gemm_f32(const dnnopt_gemm_desc* d, const float* A, const float* B, float* C,
+                         void* stream);
+int dnnopt_cuda_gemm_bf16f32(const dnnopt_gemm_desc* d, const uint16_t* A, const uint16_t* B,
+                             float* C, void* stream);
+/* FP32 operands rounded to bf16 on load (dnnopt_gemm_bf16 semantics). */
+int dnnopt_cuda_gemm_f32_bf16round(const dnnopt_gemm_desc* d, const float* A, const float* B,
+                                   float* C, void* stream);
+/* FP32-API int8 (dnnopt_gemm_int8 semantics). */
+int dnnopt_cuda_gemm_f32_s8quant(const dnnopt_gemm_desc* d, const float* A, const float* B,
+                                 float* C, void* stream);
+/* B is N x K (d->trans_b is ignored); alpha/beta are ignored. */
+int dnnopt_cuda_gemm_s8s32(const dnnopt_gemm_desc* d, const int8_t* A, const int8_t* B,
+                           int32_t* C, void* stream);
+/* W is N x K with leading dimension d->ldb; scale has N entries. */
+int dnnopt_cuda_gemm_e4m3bf16(const dnnopt_gemm_desc* d, const uint16_t* A, const uint8_t* W,
+                              const float* scale, uint16_t* C, void* stream);
+/* Reference fp8 codecs: A e4m3 (or e5m2) bytes, B e5m2 bytes. */
+int dnnopt_cuda_gemm_refe4m3_e5m2(const dnnopt_gemm_desc* d, const uint8_t* A, const uint8_t* B,
+                                  float* C, void* stream);
+int dnnopt_cuda_gemm_refe5m2_e5m2(const dnnopt_gemm_desc* d, const uint8_t* A, const uint8_t* B,
+                                  float* C, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Runtime control
+ * ---------------------------------------------------------------------- */
+/* Stream used by the dnnopt_gemm_* (host-signature) entry points on the
+ * current device; NULL restores the library-owned stream. */
+int dnnopt_set_stream(void* stream);
+/* Status of the last call made by this thread (for the void C++ mirror). */
+int dnnopt_get_last_error(void);
+const char* dnnopt_status_string(int status);
+/* Number of library kernel launches issued by this process so far. */
+uint64_t dnnopt_launch_count(void);
+/* Name of the kernel the plan selector picks for a call (diagnostics):
+ * kind 0 = f32, 1 = bf16f32, 2 = f32_bf16round, 3 = f32_s8quant, 4 = s8s32,
+ * 5 = e4m3bf16, 6 = refe4m3_e5m2, 7 = refe5m2_e5m2.  Writes a NUL-terminated
+ * string into buf (at most len bytes); needs no device for the name. */
+int dnnopt_plan_describe(int kind, const dnnopt_gemm_desc* d, char* buf, int len);
+
+/* Plan autotuning (replaces src/gemm/gemm_autotune.cpp's CPU blocking
+ * autotune; enabled like the reference with DNNOPT_AUTOTUNE=1 or this call):
+ * candidate split-K / grid choices are timed with CUDA events on first use of
+ * a shape and cached; the cache persists in a "DNNAUTO" v4 file. */
+int dnnopt_autotune_enable(int on);
+int dnnopt_autotune_save(const char* path);
+int dnnopt_autotune_load(const char* path);
+int dnnopt_autotune_entries(void);
+
+/* Host-side fault injection for failure-path tests: the next `count` calls
+ * that reach `site` fail with DNNOPT_STATUS_INJECTED_FAULT before touching the
+ * GPU.  site 1 = workspace allocation, 2 = kernel launch, 3 = host staging
+ * copy.  count 0 clears.  Also settable with DNNOPT_FAULT_INJECT=site:count. */
+int dnnopt_debug_inject_fault(int site, int count);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DNNOPT_B200_H */

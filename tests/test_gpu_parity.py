@@ -1,0 +1,414 @@
+"""GPU parity: the CUDA path through the C ABI against the reference's golden
+outputs and the CPU oracle.
+
+Tolerances (written here):
+  * FP32:   max|gpu - ref| <= 1e-5 * K          (reference test uses K*2e-5)
+  * BF16:   |gpu - fp64| <= 1e-2 * max(1, |ref|) (and a much tighter FP32 check)
+  * INT8 -> INT32 and the FP32-API int8 path: bit-exact
+  * FP8 (config 5): |gpu - fp64| <= 2^-7 |ref| + 1e-4 max|ref| (one bf16 ulp)
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from oracle.oracle import bf16_bits, bf16_to_f32, int8_uniform, ref_uniform
+
+pytestmark = pytest.mark.gpu
+
+GEMM_SHAPES = [(1, 1, 1), (4, 4, 4), (8, 8, 8), (16, 16, 16), (32, 32, 32), (64, 64, 64),
+               (1, 128, 64), (7, 13, 5), (3, 3, 1000), (128, 1, 768), (1, 1000, 2048),
+               (5, 7, 11), (13, 17, 19), (127, 127, 127)]
+CBLAS_SIZES = [(4, 4, 4), (16, 16, 16), (32, 64, 48), (7, 13, 11), (1, 64, 32)]
+C2_SHAPES = [(m, n, 1024) for m in (2, 3, 5, 7) for n in (1009, 2039, 4093)]
+INT8_SHAPES = [(1, 1, 1), (4, 37, 67), (3, 129, 1000), (8, 64, 4096), (5, 7, 11), (13, 17, 19)]
+
+
+def fp32_tol(K):
+    return 1e-5 * K
+
+
+@pytest.fixture(scope="module")
+def gpu(torch_cuda, dn):
+    return torch_cuda
+
+
+# ------------------------------------------------------------------ FP32 ----
+@pytest.mark.parametrize("shape", GEMM_SHAPES)
+def test_fp32_reference_shapes(gpu, dn, golden, shape):
+    M, N, K = shape
+    A, B = ref_uniform(M * K, 42), ref_uniform(K * N, 42)
+    C = np.zeros(M * N, np.float32)
+    dn.check(dn.gemm_fp32(M, N, K, 1.0, A, K, B, N, 0.0, C, N))
+    assert np.max(np.abs(C - golden[f"fp32_{M}x{N}x{K}"])) <= fp32_tol(K)
+
+
+def test_fp32_alpha_beta(gpu, dn, golden):
+    M, N, K = 32, 48, 64
+    A, B = ref_uniform(M * K, 42), ref_uniform(K * N, 43)
+    C = np.zeros(M * N, np.float32)
+    dn.check(dn.gemm_fp32(M, N, K, 2.0, A, K, B, N, 0.0, C, N))
+    assert np.max(np.abs(C - golden["fp32_alpha2"])) <= fp32_tol(K)
+    C = ref_uniform(M * N, 44)
+    dn.check(dn.gemm_fp32(M, N, K, 1.0, A, K, B, N, 0.5, C, N))
+    assert np.max(np.abs(C - golden["fp32_beta05"])) <= fp32_tol(K)
+
+
+def test_config1_host_and_device(gpu, dn, golden):
+    torch = gpu
+    M, N, K = 1, 4096, 4096
+    A, B = ref_uniform(M * K, 42), ref_uniform(K * N, 123)
+    C = np.zeros(M * N, np.float32)
+    dn.check(dn.gemm_fp32(M, N, K, 1.0, A, K, B, N, 0.0, C, N))
+    assert np.max(np.abs(C - golden["config1"])) <= fp32_tol(K)
+    dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    dC = torch.zeros(M * N, device="cuda")
+    s = torch.cuda.current_stream()
+    dn.check(dn.cuda_gemm("f32", dn.desc(M, N, K, K, N, N), dA, dB, dC, s))
+    torch.cuda.synchronize()
+    assert np.max(np.abs(dC.cpu().numpy() - golden["config1"])) <= fp32_tol(K)
+
+
+@pytest.mark.parametrize("shape", C2_SHAPES)
+def test_config2(gpu, dn, golden, shape):
+    M, N, K = shape
+    A, B, C = ref_uniform(M * K, 42), ref_uniform(K * N, 123), ref_uniform(M * N, 77)
+    dn.check(dn.gemm_fp32(M, N, K, 1.0, A, K, B, N, 0.5, C, N))
+    assert np.max(np.abs(C - golden[f"config2_{M}x{N}x{K}"])) <= fp32_tol(K)
+
+
+def test_config2_device_api_deterministic(gpu, dn, golden):
+    torch = gpu
+    M, N, K = 7, 4093, 1024
+    A, B, C0 = ref_uniform(M * K, 42), ref_uniform(K * N, 123), ref_uniform(M * N, 77)
+    dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    outs = []
+    for _ in range(3):
+        dC = torch.from_numpy(C0.copy()).cuda()
+        dn.check(dn.cuda_gemm("f32", dn.desc(M, N, K, K, N, N, 1.0, 0.5), dA, dB, dC,
+                              torch.cuda.current_stream()))
+        torch.cuda.synchronize()
+        outs.append(dC.cpu().numpy())
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    assert np.array_equal(outs[0].view(np.uint32), outs[2].view(np.uint32))
+    assert np.max(np.abs(outs[0] - golden[f"config2_{M}x{N}x{K}"])) <= fp32_tol(K)
+
+
+@pytest.mark.parametrize("M", range(1, 9))
+@pytest.mark.parametrize("N,K", [(1009, 1000), (33, 1023), (128, 7), (257, 4099)])
+def test_fp32_small_m_edges(gpu, dn, orc, M, N, K):
+    A, B, C = ref_uniform(M * K, 1), ref_uniform(K * N, 2), ref_uniform(M * N, 3)
+    ref = C.copy()
+    orc.gemm_f32(M, N, K, 1.5, A, K, B, N, -0.25, ref, N)
+    dn.check(dn.gemm_fp32(M, N, K, 1.5, A, K, B, N, -0.25, C, N))
+    assert np.max(np.abs(C - ref)) <= fp32_tol(K)
+
+
+def test_fp32_strides_unaligned_and_nan_c(gpu, dn, orc):
+    torch = gpu
+    M, N, K = 5, 300, 513
+    lda, ldb, ldc = K + 3, N + 5, N + 7
+    A = ref_uniform(M * lda, 4)
+    Bbig = ref_uniform(K * ldb + 1, 5)
+    dA = torch.from_numpy(A).cuda()
+    dB = torch.from_numpy(Bbig).cuda()[1:]            # 4-byte aligned only: scalar path
+    dC = torch.full((M * ldc,), float("nan"), device="cuda")   # beta == 0 never reads C
+    dn.check(dn.cuda_gemm("f32", dn.desc(M, N, K, lda, ldb, ldc), dA, dB, dC,
+                          torch.cuda.current_stream()))
+    torch.cuda.synchronize()
+    ref = np.zeros(M * ldc, np.float32)
+    orc.gemm_f32(M, N, K, 1.0, A, lda, np.ascontiguousarray(Bbig[1:]), ldb, 0.0, ref, ldc)
+    got = dC.cpu().numpy().reshape(M, ldc)
+    assert np.max(np.abs(got[:, :N] - ref.reshape(M, ldc)[:, :N])) <= fp32_tol(K)
+    assert np.all(np.isnan(got[:, N:]))               # padding columns untouched
+
+
+def cblas(dn):
+    lib = ctypes.CDLL(dn.BLAS_PATH)
+    lib.cblas_sgemm.argtypes = [ctypes.c_int] * 6 + [ctypes.c_float, ctypes.c_void_p, ctypes.c_int,
+                                                     ctypes.c_void_p, ctypes.c_int, ctypes.c_float,
+                                                     ctypes.c_void_p, ctypes.c_int]
+    lib.sgemm_.argtypes = [ctypes.c_void_p] * 13
+    return lib
+
+
+def cblas_operands(order, ta, tb, M, N, K):
+    if order == 101:
+        a_rows, a_cols = (K, M) if ta == 112 else (M, K)
+        b_rows, b_cols = (N, K) if tb == 112 else (K, N)
+        return a_rows, a_cols, b_rows, b_cols, a_cols, b_cols, N
+    a_rows, a_cols = (M, K) if ta == 112 else (K, M)
+    b_rows, b_cols = (K, N) if tb == 112 else (N, K)
+    return a_rows, a_cols, b_rows, b_cols, a_cols, b_cols, M
+
+
+@pytest.mark.parametrize("size", CBLAS_SIZES)
+def test_cblas_against_reference(gpu, dn, golden, size):
+    lib = cblas(dn)
+    M, N, K = size
+    for order in (101, 102):
+        for ta in (111, 112):
+            for tb in (111, 112):
+                a_rows, a_cols, b_rows, b_cols, lda, ldb, ldc = cblas_operands(order, ta, tb, M, N, K)
+                A = ref_uniform(a_rows * a_cols, 42)
+                B = ref_uniform(b_rows * b_cols, 123)
+                C = ref_uniform(M * N, 77)
+                lib.cblas_sgemm(order, ta, tb, M, N, K, 1.0, A.ctypes.data, lda, B.ctypes.data,
+                                ldb, 0.5, C.ctypes.data, ldc)
+                exp = golden[f"cblas_{order}_{ta}_{tb}_{M}x{N}x{K}"]
+                assert np.max(np.abs(C - exp)) <= fp32_tol(K), (order, ta, tb)
+    A, B, C = ref_uniform(M * K, 42), ref_uniform(K * N, 123), ref_uniform(M * N, 77)
+    lib.cblas_sgemm(101, 111, 111, M, N, K, 2.5, A.ctypes.data, K, B.ctypes.data, N, -0.3,
+                    C.ctypes.data, N)
+    assert np.max(np.abs(C - golden[f"cblas_ab_{M}x{N}x{K}"])) <= K * 5e-5
+    A, B = ref_uniform(M * K, 42), ref_uniform(K * N, 123)
+    C = np.zeros(M * N, np.float32)
+    ta, tb = ctypes.c_char(b"N"), ctypes.c_char(b"N")
+    m_, n_, k_ = ctypes.c_int(M), ctypes.c_int(N), ctypes.c_int(K)
+    al, be = ctypes.c_float(1.0), ctypes.c_float(0.0)
+    lda_, ldb_, ldc_ = ctypes.c_int(M), ctypes.c_int(K), ctypes.c_int(M)
+    lib.sgemm_(*(ctypes.addressof(x) for x in (ta, tb, m_, n_, k_, al)), A.ctypes.data,
+               ctypes.addressof(lda_), B.ctypes.data, ctypes.addressof(ldb_),
+               ctypes.addressof(be), C.ctypes.data, ctypes.addressof(ldc_))
+    assert np.max(np.abs(C - golden[f"fortran_{M}x{N}x{K}"])) <= fp32_tol(K)
+
+
+def test_cblas_256_all_orders(gpu, dn, orc):
+    from tests.test_oracle_golden import cblas_by_oracle
+    lib = cblas(dn)
+    M = N = K = 256
+    for order in (101, 102):
+        for ta in (111, 112):
+            for tb in (111, 112):
+                a_rows, a_cols, b_rows, b_cols, lda, ldb, ldc = cblas_operands(order, ta, tb, M, N, K)
+                A = ref_uniform(a_rows * a_cols, 42)
+                B = ref_uniform(b_rows * b_cols, 123)
+                C = ref_uniform(M * N, 77)
+                ref = C.copy()
+                cblas_by_oracle(orc, order, ta, tb, M, N, K, 1.0, A, lda, B, ldb, 0.5, ref, ldc)
+                lib.cblas_sgemm(order, ta, tb, M, N, K, 1.0, A.ctypes.data, lda, B.ctypes.data,
+                                ldb, 0.5, C.ctypes.data, ldc)
+                assert np.max(np.abs(C - ref)) <= fp32_tol(K), (order, ta, tb)
+
+
+def test_saxpy(gpu, dn):
+    X, Y = ref_uniform(1000, 1), ref_uniform(2000, 2)
+    exp = Y.copy()
+    exp[::2] = exp[::2] + np.float32(0.75) * X[:1000]
+    dn.check(dn.saxpy(1000, 0.75, X, 1, Y, 2))
+    assert np.max(np.abs(Y - exp)) <= 1e-6
+
+
+# ------------------------------------------------------------------ INT8 ----
+@pytest.mark.parametrize("shape", INT8_SHAPES + [(4, 11008, 4096)])
+def test_int8_native_bitexact(gpu, dn, golden, shape):
+    M, N, K = shape
+    A, B = int8_uniform(M * K, 42), int8_uniform(N * K, 123)
+    C = np.zeros(M * N, np.int32)
+    dn.check(dn.gemm_int8_int8int8int32(M, N, K, A, K, B, K, C, N))
+    key = "config3" if shape == (4, 11008, 4096) else f"s8_{M}x{N}x{K}"
+    assert np.array_equal(C, golden[key])
+
+
+def test_int8_edges_bitexact(gpu, dn, orc):
+    torch = gpu
+    for (M, N, K, lda, ldb, ldc, off) in [(1, 1009, 4096, 4096, 4096, 1009, 0),
+                                          (7, 513, 300, 301, 305, 520, 1),
+                                          (8, 64, 16, 16, 16, 64, 0),
+                                          (12, 200, 777, 777, 777, 200, 0),
+                                          (2, 5000, 127, 128, 127, 5000, 3)]:
+        A = int8_uniform(M * lda, 7)
+        Bb = int8_uniform(N * ldb + off, 8)
+        ref = np.zeros(M * ldc, np.int32)
+        orc.gemm_s8s32(M, N, K, A, lda, np.ascontiguousarray(Bb[off:]), ldb, ref, ldc)
+        dA = torch.from_numpy(A).cuda()
+        dB = torch.from_numpy(Bb).cuda()[off:]
+        dC = torch.zeros(M * ldc, dtype=torch.int32, device="cuda")
+        dn.check(dn.cuda_gemm("s8s32", dn.desc(M, N, K, lda, ldb, ldc), dA, dB, dC,
+                              torch.cuda.current_stream()))
+        torch.cuda.synchronize()
+        got = dC.cpu().numpy().reshape(M, ldc)[:, :N]
+        assert np.array_equal(got, ref.reshape(M, ldc)[:, :N]), (M, N, K)
+
+
+@pytest.mark.parametrize("shape", [(1, 128, 64), (7, 13, 5), (5, 7, 11), (4, 1009, 1024),
+                                   (8, 4096, 512), (32, 48, 64), (13, 17, 19)])
+def test_int8_fp32_api_bitexact(gpu, dn, orc, shape):
+    M, N, K = shape
+    for alpha, beta in [(1.0, 0.0), (1.5, 0.5)]:
+        A, B, C = ref_uniform(M * K, 42), ref_uniform(K * N, 43), ref_uniform(M * N, 44)
+        ref = C.copy()
+        orc.gemm_int8_f32api(M, N, K, alpha, A, K, B, N, beta, ref, N)
+        dn.check(dn.gemm_int8(M, N, K, alpha, A, K, B, N, beta, C, N))
+        assert np.array_equal(C.view(np.uint32), ref.view(np.uint32)), (alpha, beta)
+        Cf = np.zeros(M * N, np.float32)
+        orc.gemm_f32(M, N, K, alpha, A, K, B, N, 0.0, Cf, N)
+        if beta == 0.0:
+            assert np.max(np.abs(C - Cf)) < K * 2e-2   # reference test bound
+
+
+# ------------------------------------------------------------------ BF16 ----
+def _bf16_case(dn, orc, torch, M, N, K, alpha=1.0, beta=0.0, ldc=None, seed=42):
+    ldc = ldc or N
+    A32 = np.random.default_rng(seed).standard_normal(M * K).astype(np.float32)
+    B32 = np.random.default_rng(seed + 81).standard_normal(K * N).astype(np.float32)
+    A, B = bf16_bits(A32), bf16_bits(B32)
+    C0 = ref_uniform(M * ldc, 5)
+    ref = C0.copy()
+    ref64 = orc.gemm_bf16f32(M, N, K, alpha, A, K, B, N, beta, ref, ldc, want64=True)
+    dA = torch.from_numpy(A.view(np.int16)).cuda()
+    dB = torch.from_numpy(B.view(np.int16)).cuda()
+    dC = torch.from_numpy(C0.copy()).cuda()
+    dn.check(dn.cuda_gemm("bf16f32", dn.desc(M, N, K, K, N, ldc, alpha, beta), dA, dB, dC,
+                          torch.cuda.current_stream()))
+    torch.cuda.synchronize()
+    got = dC.cpu().numpy().reshape(M, ldc)
+    r64 = ref64.reshape(M, N)
+    err = np.abs(got[:, :N] - r64)
+    assert np.all(err <= 1e-2 * np.maximum(1.0, np.abs(r64)))        # BASELINE bound
+    assert np.max(err) <= 2e-6 * K * max(1.0, float(np.max(np.abs(r64))))  # FP32 accumulation
+    if ldc > N:
+        assert np.array_equal(got[:, N:], C0.reshape(M, ldc)[:, N:])
+    return got
+
+
+def test_bf16_config4_full(gpu, dn, orc):
+    d = dn.desc(65536, 64, 256, 256, 64, 64)
+    assert dn.plan_describe(dn.KIND_BF16F32, d) == "gemm_bf16_tcgen05"
+    _bf16_case(dn, orc, gpu, 65536, 64, 256)
+
+
+@pytest.mark.parametrize("M,N,K,alpha,beta,ldc", [
+    (128, 64, 256, 1.0, 0.0, None), (200, 64, 256, 1.0, 0.0, None), (1000, 16, 64, 2.0, 0.0, None),
+    (333, 48, 100, 1.0, 0.5, None), (4096, 256, 128, 0.5, 0.0, None), (257, 128, 320, 1.0, -1.0, 132),
+    (129, 80, 8, 1.0, 0.0, None), (9, 64, 256, 1.0, 0.0, None)])
+def test_bf16_tcgen05_shapes(gpu, dn, orc, M, N, K, alpha, beta, ldc):
+    _bf16_case(dn, orc, gpu, M, N, K, alpha, beta, ldc)
+
+
+@pytest.mark.parametrize("shape", [(1, 4096, 512), (7, 1009, 1024), (8, 64, 256), (65, 300, 77),
+                                   (300, 300, 300)])
+def test_bf16_other_paths(gpu, dn, orc, shape):
+    M, N, K = shape
+    _bf16_case(dn, orc, gpu, M, N, K, 1.0, 0.25)
+
+
+@pytest.mark.parametrize("shape", GEMM_SHAPES)
+def test_bf16_fp32_api(gpu, dn, orc, golden, shape):
+    M, N, K = shape
+    A, B = ref_uniform(M * K, 42), ref_uniform(K * N, 42)
+    C = np.zeros(M * N, np.float32)
+    dn.check(dn.gemm_bf16(M, N, K, 1.0, A, K, B, N, 0.0, C, N))
+    assert np.max(np.abs(C - golden[f"fp32_{M}x{N}x{K}"])) < K * 2e-3     # reference bound
+    ref = np.zeros(M * N, np.float32)
+    r64 = orc.gemm_bf16f32(M, N, K, 1.0, bf16_bits(A), K, bf16_bits(B), N, 0.0, ref, N,
+                           want64=True)
+    assert np.max(np.abs(C - r64)) <= 1e-5 * K
+
+
+# ------------------------------------------------------------------- FP8 ----
+def test_fp8_reference_codec_api(gpu, dn, orc, golden):
+    M, N, K = 5, 37, 64
+    enc4 = lambda x: orc.table("refe4m3", "from_f32", x)  # noqa: E731
+    enc5 = lambda x: orc.table("refe5m2", "from_f32", x)  # noqa: E731
+    A4, A5, B5 = enc4(ref_uniform(M * K, 42)), enc5(ref_uniform(M * K, 42)), enc5(ref_uniform(K * N, 123))
+    C = np.zeros(M * N, np.float32)
+    dn.check(dn.gemm_fp8_e4m3(M, N, K, 1.0, A4, K, B5, N, 0.0, C, N))
+    assert np.max(np.abs(C - golden["fp8_e4m3_5x37x64"])) <= fp32_tol(K)
+    C = np.zeros(M * N, np.float32)
+    dn.check(dn.gemm_fp8_e5m2(M, N, K, 1.0, A5, K, B5, N, 0.0, C, N))
+    assert np.max(np.abs(C - golden["fp8_e5m2_5x37x64"])) <= fp32_tol(K)
+    # gemm_fp8 (FP32 API): the reference's FP8-hardware branch = encode, then e4m3 GEMM.
+    for (M, N, K) in [(5, 37, 64), (33, 70, 90)]:
+        A, B = ref_uniform(M * K, 1), ref_uniform(K * N, 2)
+        ref = np.zeros(M * N, np.float32)
+        orc.gemm_refe4m3_e5m2(M, N, K, 1.0, enc4(A), K, enc5(B), N, 0.0, ref, N)
+        C = np.zeros(M * N, np.float32)
+        dn.check(dn.gemm_fp8(M, N, K, 1.0, A, K, B, N, 0.0, C, N))
+        assert np.max(np.abs(C - ref)) <= fp32_tol(K)
+
+
+def e4m3_problem(orc, M, N, K, seed_a=42, seed_w=123):
+    A = bf16_bits(np.random.default_rng(seed_a).standard_normal(M * K).astype(np.float32))
+    W = (np.random.default_rng(seed_w).standard_normal(N * K) * 0.02).astype(np.float32)
+    q, s = orc.quantize_e4m3_rows(N, K, W, K)
+    return A, q, s
+
+
+def check_e4m3(got_bits, ref64):
+    got = bf16_to_f32(got_bits).astype(np.float64)
+    err = np.abs(got - ref64)
+    assert np.all(err <= 2.0 ** -7 * np.abs(ref64) + 1e-4 * np.max(np.abs(ref64)))
+
+
+@pytest.mark.parametrize("shape", [(8, 512, 1024), (1, 300, 8192), (3, 1000, 1000), (8, 28672, 8192),
+                                   (16, 256, 512), (20, 64, 96)])
+def test_e4m3_decode_ffn(gpu, dn, orc, shape):
+    torch = gpu
+    M, N, K = shape
+    A, q, s = e4m3_problem(orc, M, N, K)
+    C = np.zeros(M * N, np.uint16)
+    ref64 = orc.gemm_e4m3bf16(M, N, K, A, K, q, K, s, C, N)
+    dA = torch.from_numpy(A.view(np.int16)).cuda()
+    dW = torch.from_numpy(q).cuda()
+    ds = torch.from_numpy(s).cuda()
+    dC = torch.zeros(M * N, dtype=torch.int16, device="cuda")
+    dn.check(dn.cuda_gemm("e4m3bf16", dn.desc(M, N, K, K, K, N), dA, dW, dC,
+                          torch.cuda.current_stream(), scale=ds))
+    torch.cuda.synchronize()
+    check_e4m3(dC.cpu().numpy().view(np.uint16), ref64)
+    # Host API on a small case.
+    if M * N <= 8192:
+        Ch = np.zeros(M * N, np.uint16)
+        dn.check(dn.gemm_e4m3_bf16(M, N, K, A, K, q, K, s, Ch, N))
+        check_e4m3(Ch, ref64)
+
+
+# -------------------------------------------------------- runtime paths ----
+def test_plan_selection_on_device(gpu, dn):
+    assert dn.plan_describe(dn.KIND_F32, dn.desc(1, 4096, 4096, 4096, 4096, 4096)).startswith(
+        "gemv_kn_splitk mt=1 vec4=1")
+    assert dn.plan_describe(dn.KIND_S8S32, dn.desc(4, 11008, 4096, 4096, 4096, 11008)).startswith(
+        "gemv_nk_dot mt=4 vec=1")
+
+
+def test_autotune_roundtrip(gpu, dn, orc, tmp_path):
+    M, N, K = 3, 2039, 1024
+    A, B, C = ref_uniform(M * K, 42), ref_uniform(K * N, 123), ref_uniform(M * N, 77)
+    ref = C.copy()
+    orc.gemm_f32(M, N, K, 1.0, A, K, B, N, 0.5, ref, N)
+    dn.check(dn.lib.dnnopt_autotune_enable(1))
+    try:
+        before = dn.lib.dnnopt_autotune_entries()
+        dn.check(dn.gemm_fp32(M, N, K, 1.0, A, K, B, N, 0.5, C, N))
+        assert dn.lib.dnnopt_autotune_entries() == before + 1
+        assert np.max(np.abs(C - ref)) <= fp32_tol(K)
+        path = str(tmp_path / "tune.bin").encode()
+        n = dn.lib.dnnopt_autotune_save(path)
+        assert n >= 1 and dn.lib.dnnopt_autotune_load(path) == n
+    finally:
+        dn.lib.dnnopt_autotune_enable(0)
+
+
+def test_injected_faults_leave_device_usable(gpu, dn, orc):
+    M, N, K = 2, 1009, 1024
+    A, B = ref_uniform(M * K, 1), ref_uniform(K * N, 2)
+    for site in (1, 2, 3):
+        C = np.zeros(M * N, np.float32)
+        dn.check(dn.lib.dnnopt_debug_inject_fault(site, 1))
+        assert dn.gemm_fp32(M, N, K, 1.0, A, K, B, N, 0.0, C, N) == dn.INJECTED_FAULT
+        assert dn.lib.dnnopt_get_last_error() == dn.INJECTED_FAULT
+        dn.check(dn.gemm_fp32(M, N, K, 1.0, A, K, B, N, 0.0, C, N))
+        ref = np.zeros(M * N, np.float32)
+        orc.gemm_f32(M, N, K, 1.0, A, K, B, N, 0.0, ref, N)
+        assert np.max(np.abs(C - ref)) <= fp32_tol(K)
+
+
+def test_launch_counter_counts_kernels(gpu, dn):
+    A, B = ref_uniform(4 * 64, 1), ref_uniform(64 * 512, 2)
+    C = np.zeros(4 * 512, np.float32)
+    n0 = dn.launch_count()
+    dn.check(dn.gemm_fp32(4, 512, 64, 1.0, A, 64, B, 512, 0.0, C, 512))
+    assert dn.launch_count() == n0 + 1
