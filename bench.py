@@ -363,6 +363,67 @@ def per_config(torch, dn, stream, pk, world, rank, dist):
     return out
 
 
+def run_profile(args):
+    """Runs one config's kernel `--reps` times on rotating inputs and exits
+    (the command that ncu captures; prints no bench line)."""
+    import torch
+    from oracle.oracle import bf16_bits, int8_uniform, ref_uniform
+    dn = load_dnnopt()
+    torch.cuda.set_device(0)
+    s = torch.cuda.current_stream()
+    name = args.profile
+    calls = []
+    if name == "c2":
+        for items in make_sweep_sets(torch, torch.device("cuda", 0)):
+            for (M, N, K, A, B, C) in items:
+                d = dn.desc(M, N, K, K, N, N, 1.0, 0.5)
+                calls.append(lambda d=d, A=A, B=B, C=C: dn.cuda_gemm("f32", d, A, B, C, s))
+    elif name == "c1":
+        M, N, K = 1, 4096, 4096
+        d = dn.desc(M, N, K, K, N, N)
+        for i in range(N_SETS):
+            A = torch.from_numpy(ref_uniform(M * K, 42 + i)).cuda()
+            B = torch.from_numpy(ref_uniform(K * N, 123 + i)).cuda()
+            C = torch.zeros(M * N, device="cuda")
+            calls.append(lambda A=A, B=B, C=C: dn.cuda_gemm("f32", d, A, B, C, s))
+    elif name == "c3":
+        M, N, K = 4, 11008, 4096
+        d = dn.desc(M, N, K, K, K, N)
+        for i in range(N_SETS):
+            A = torch.from_numpy(int8_uniform(M * K, 42 + i)).cuda()
+            B = torch.from_numpy(int8_uniform(N * K, 123 + i)).cuda()
+            C = torch.zeros(M * N, dtype=torch.int32, device="cuda")
+            calls.append(lambda A=A, B=B, C=C: dn.cuda_gemm("s8s32", d, A, B, C, s))
+    elif name == "c4":
+        M, N, K = 65536, 64, 256
+        d = dn.desc(M, N, K, K, N, N)
+        rng = np.random.default_rng(42)
+        for i in range(N_SETS):
+            A = torch.from_numpy(bf16_bits(rng.standard_normal(M * K).astype(np.float32)).view(np.int16)).cuda()
+            B = torch.from_numpy(bf16_bits(rng.standard_normal(K * N).astype(np.float32)).view(np.int16)).cuda()
+            C = torch.zeros(M * N, device="cuda")
+            calls.append(lambda A=A, B=B, C=C: dn.cuda_gemm("bf16f32", d, A, B, C, s))
+    elif name == "c5":
+        M, N, K = 8, 28672, 8192
+        d = dn.desc(M, N, K, K, K, N)
+        A = torch.from_numpy(bf16_bits(np.random.default_rng(42).standard_normal(M * K)
+                                       .astype(np.float32)).view(np.int16)).cuda()
+        g = torch.Generator(device="cuda").manual_seed(123)
+        Wf = torch.randn((N, K), device="cuda", generator=g) * 0.02
+        scale = (Wf.abs().amax(dim=1) / 448.0).clamp_min(1e-30)
+        W = (Wf / scale[:, None]).to(torch.float8_e4m3fn).view(torch.uint8).contiguous()
+        del Wf
+        C = torch.zeros(M * N, dtype=torch.int16, device="cuda")
+        calls.append(lambda: dn.cuda_gemm("e4m3bf16", d, A, W, C, s, scale=scale))
+    else:
+        raise SystemExit(f"unknown profile config {name}")
+    for r in range(args.reps):
+        for c in calls:
+            dn.check(c(), name)
+    torch.cuda.synchronize()
+    print(f"profile {name}: {args.reps} x {len(calls)} calls ok")
+
+
 def run_gpu_arm(args):
     import torch
     import torch.distributed as dist
@@ -487,8 +548,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["dnnopt", "reference"], default="dnnopt")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", choices=["c1", "c2", "c3", "c4", "c5"],
+                    help="run one config's kernel --reps times for an ncu capture, no bench line")
+    ap.add_argument("--reps", type=int, default=3)
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.profile:
+        run_profile(args)
+    elif args.impl == "reference":
         run_reference_arm(args)
     else:
         run_gpu_arm(args)
