@@ -29,6 +29,7 @@ ALLOC_FAILED = 4
 NO_DEVICE = 5
 KERNEL_TIMEOUT = 6
 INJECTED_FAULT = 7
+EXCEEDS_SCRATCH = 8
 
 # dnnopt_plan_describe kinds
 KIND_F32, KIND_BF16F32, KIND_F32_BF16ROUND, KIND_F32_S8QUANT = 0, 1, 2, 3
@@ -73,7 +74,8 @@ lib.dnnopt_gemm_f32_desc.argtypes = [ctypes.POINTER(GemmDesc), _P, _P, _P]
 lib.dnnopt_saxpy.argtypes = [_I, _F, _P, _I, _P, _I]
 for _name in ("dnnopt_cuda_gemm_f32", "dnnopt_cuda_gemm_bf16f32", "dnnopt_cuda_gemm_f32_bf16round",
               "dnnopt_cuda_gemm_f32_s8quant", "dnnopt_cuda_gemm_s8s32",
-              "dnnopt_cuda_gemm_refe4m3_e5m2", "dnnopt_cuda_gemm_refe5m2_e5m2"):
+              "dnnopt_cuda_gemm_refe4m3_e5m2", "dnnopt_cuda_gemm_refe5m2_e5m2",
+              "dnnopt_cuda_gemm_f32_noalloc"):
     getattr(lib, _name).argtypes = [ctypes.POINTER(GemmDesc), _P, _P, _P, _P]
     getattr(lib, _name).restype = _I
 lib.dnnopt_cuda_gemm_e4m3bf16.argtypes = [ctypes.POINTER(GemmDesc), _P, _P, _P, _P, _P]
@@ -175,7 +177,7 @@ def has_fp8_support() -> bool:
 # ---- device-pointer entry points (asynchronous on `stream`) -----------------
 def cuda_gemm(kind: str, d: GemmDesc, A, B, C, stream=None, scale=None) -> int:
     """kind: f32 | bf16f32 | f32_bf16round | f32_s8quant | s8s32 | e4m3bf16 |
-    refe4m3_e5m2 | refe5m2_e5m2."""
+    refe4m3_e5m2 | refe5m2_e5m2 | f32_noalloc."""
     s = ptr(stream) if not hasattr(stream, "cuda_stream") else stream.cuda_stream
     fn = getattr(lib, f"dnnopt_cuda_gemm_{kind}")
     if kind == "e4m3bf16":

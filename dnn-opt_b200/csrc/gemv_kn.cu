@@ -19,7 +19,10 @@
 //     ticket), again in split order, so results are deterministic.
 //   * The grid is sized by the host to one wave of resident CTAs over the
 //     148 SMs (splits = resident CTAs / strips).
+#include <mutex>
+
 #include "common.cuh"
+#include "dnnopt_b200.h"
 #include "kernels.h"
 
 namespace dnnopt_b200 {
@@ -306,3 +309,134 @@ cudaError_t launch_gemv_kn(In ia, In ib, const GemmArgs& g, const GemvKnPlan& p,
 }
 
 }  // namespace dnnopt_b200
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point: dnnopt_cuda_gemm_f32_noalloc.
+//
+// Some callers cannot call cudaMalloc: code whose device memory is owned by a
+// framework's caching allocator (allocating behind its back breaks the pool's
+// accounting and out-of-memory handling), serving loops that forbid any
+// allocation after warm-up because cudaMalloc can synchronise the device, and
+// runtimes that fix their memory budget at start-up.  For them this entry
+// point runs the same small-M split-K GEMV kernel as dnnopt_cuda_gemm_f32
+// but takes its scratch (split-K partial strips and the per-strip tickets)
+// from the file-scope device array below instead of the per-stream workspace.
+//
+// * Capacity: kNoAllocTicketWords strips of 128 columns (N <= 131072) and
+//   kNoAllocPartialFloats partial floats (4 MiB); larger requests are
+//   rejected with DNNOPT_STATUS_EXCEEDS_SCRATCH.  The array (4 MiB + 4 KiB)
+//   is held by every GPU that loads the library until the process exits.
+// * The first call on a device looks up the array's device address with
+//   cudaGetSymbolAddress (host code cannot use the symbol itself: on the host
+//   it names a stand-in, not device memory); make that first call before any
+//   stream capture.
+// * Every call shares the array and it keeps the last call's contents: the
+//   tickets are cleared on the call's stream before each launch, the partials
+//   are fully rewritten before they are read.  Calls that overlap on the GPU
+//   (different streams, or several host threads) race on the array and must
+//   be serialised by the caller.
+// * No cudaMalloc, cudaFree or allocating library routine is called.
+// ---------------------------------------------------------------------------
+namespace dnnopt_b200 {
+namespace {
+
+constexpr size_t kNoAllocTicketWords = 1024;
+constexpr size_t kNoAllocPartialFloats = static_cast<size_t>(1) << 20;
+constexpr size_t kNoAllocScratchBytes = kNoAllocTicketWords * 4 + kNoAllocPartialFloats * 4;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+int g_noalloc_sms[kNoAllocMaxDevices] = {};
+
+int noalloc_mt(int M) { return M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8)); }
+
+}  // namespace
+}  // namespace dnnopt_b200
+
+extern "C" __attribute__((visibility("default"))) int dnnopt_cuda_gemm_f32_noalloc(
+    const dnnopt_gemm_desc* d, const float* A, const float* B, float* C, void* stream) {
+    using namespace dnnopt_b200;
+    if (!d || d->M < 0 || d->N < 0 || d->K < 0) return DNNOPT_STATUS_INVALID_VALUE;
+    if (d->M == 0 || d->N == 0 || d->K == 0) return DNNOPT_STATUS_SUCCESS;
+    if (!A || !B || !C) return DNNOPT_STATUS_INVALID_VALUE;
+    if (d->lda < (d->trans_a ? d->M : d->K) || d->ldc < d->N) return DNNOPT_STATUS_INVALID_VALUE;
+    if (d->trans_b || d->M > 8) return DNNOPT_STATUS_NOT_SUPPORTED;   // small-M, B K x N only
+    if (d->ldb < d->N) return DNNOPT_STATUS_INVALID_VALUE;
+    const int tiles = gemv_kn_tiles(d->N);
+    if (static_cast<size_t>(tiles) > kNoAllocTicketWords) return DNNOPT_STATUS_EXCEEDS_SCRATCH;
+
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return DNNOPT_STATUS_NO_DEVICE;
+    }
+    if (dev < 0 || dev >= kNoAllocMaxDevices) return DNNOPT_STATUS_NOT_SUPPORTED;
+    void* scratch = nullptr;
+    int sms = 0;
+    {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (!g_noalloc_ptr[dev]) {
+            void* p = nullptr;
+            if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
+                cudaGetLastError();
+                return DNNOPT_STATUS_CUDA_ERROR;
+            }
+            int n = 0;
+            if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+                cudaGetLastError();
+                return DNNOPT_STATUS_CUDA_ERROR;
+            }
+            g_noalloc_ptr[dev] = p;
+            g_noalloc_sms[dev] = n;
+        }
+        scratch = g_noalloc_ptr[dev];
+        sms = g_noalloc_sms[dev];
+    }
+
+    GemmArgs g;
+    g.M = d->M; g.N = d->N; g.K = d->K;
+    g.alpha = d->alpha; g.beta = d->beta;
+    g.A = A; g.lda = d->lda; g.a_trans = d->trans_a ? 1 : 0;
+    g.B = B; g.ldb = d->ldb; g.b_trans = 0;
+    g.C = C; g.ldc = d->ldc;
+
+    // Same split-K choice as the allocating path, capped by the scratch size.
+    GemvKnPlan p;
+    p.mt = noalloc_mt(g.M);
+    p.vec4 = (reinterpret_cast<uintptr_t>(B) % 16 == 0 && g.ldb % 4 == 0) ? 1 : 0;
+    int occ = 1;
+    if (gemv_kn_occupancy(In::F32, In::F32, p.mt, p.vec4, &occ) != cudaSuccess || occ < 1) {
+        cudaGetLastError();
+        occ = 1;
+    }
+    int splits = (occ * sms) / tiles;
+    const int max_splits = g.K / 32 > 1 ? g.K / 32 : 1;
+    splits = splits > max_splits ? max_splits : splits;
+    splits = splits < 1 ? 1 : splits;
+    const size_t per_split = static_cast<size_t>(p.mt) * tiles * 128;
+    while (splits > 1 && static_cast<size_t>(splits) * per_split > kNoAllocPartialFloats) --splits;
+    int kchunk = (g.K + splits - 1) / splits;
+    kchunk = (kchunk + 7) / 8 * 8;
+    p.kchunk = kchunk;
+    p.splits = (g.K + kchunk - 1) / kchunk;
+    if (p.splits > 1 && static_cast<size_t>(p.splits) * per_split > kNoAllocPartialFloats)
+        return DNNOPT_STATUS_EXCEEDS_SCRATCH;
+
+    uint32_t* tickets = static_cast<uint32_t*>(scratch);
+    float* partials = reinterpret_cast<float*>(static_cast<unsigned char*>(scratch) +
+                                               kNoAllocTicketWords * 4);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (p.splits > 1 &&
+        cudaMemsetAsync(tickets, 0, static_cast<size_t>(tiles) * sizeof(uint32_t), s) != cudaSuccess) {
+        cudaGetLastError();
+        return DNNOPT_STATUS_CUDA_ERROR;
+    }
+    if (launch_gemv_kn(In::F32, In::F32, g, p, partials, tickets, s) != cudaSuccess) {
+        cudaGetLastError();
+        return DNNOPT_STATUS_CUDA_ERROR;
+    }
+    return DNNOPT_STATUS_SUCCESS;
+}

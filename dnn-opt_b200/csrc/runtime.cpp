@@ -170,6 +170,7 @@ const char* dnnopt_status_string(int s) {
         case DNNOPT_STATUS_NO_DEVICE: return "no CUDA device";
         case DNNOPT_STATUS_KERNEL_TIMEOUT: return "in-kernel wait timed out";
         case DNNOPT_STATUS_INJECTED_FAULT: return "injected fault";
+        case DNNOPT_STATUS_EXCEEDS_SCRATCH: return "request exceeds the fixed scratch area";
         default: return "unknown status";
     }
 }

@@ -51,7 +51,8 @@ typedef enum dnnopt_status {
     DNNOPT_STATUS_ALLOC_FAILED = 4,    /* device or pinned allocation failed */
     DNNOPT_STATUS_NO_DEVICE = 5,       /* no CUDA device visible */
     DNNOPT_STATUS_KERNEL_TIMEOUT = 6,  /* a bounded in-kernel wait gave up */
-    DNNOPT_STATUS_INJECTED_FAULT = 7   /* host-side fault injection (tests) */
+    DNNOPT_STATUS_INJECTED_FAULT = 7,  /* host-side fault injection (tests) */
+    DNNOPT_STATUS_EXCEEDS_SCRATCH = 8  /* request larger than a fixed scratch area */
 } dnnopt_status;
 
 /* Shape and epilogue of one GEMM call for the dnnopt_cuda_* entry points.
@@ -157,6 +158,19 @@ int dnnopt_cuda_gemm_refe4m3_e5m2(const dnnopt_gemm_desc* d, const uint8_t* A, c
                                   float* C, void* stream);
 int dnnopt_cuda_gemm_refe5m2_e5m2(const dnnopt_gemm_desc* d, const uint8_t* A, const uint8_t* B,
                                   float* C, void* stream);
+
+/* Allocation-free FP32 small-M GEMM (no counterpart in the reference).  For
+ * callers that cannot call cudaMalloc -- code whose device memory belongs to
+ * a framework's caching allocator, serving loops that allow no allocation
+ * after warm-up, runtimes with a memory budget fixed at start-up.  Same
+ * arithmetic and kernel as dnnopt_cuda_gemm_f32 for M <= 8 with B stored
+ * K x N (otherwise DNNOPT_STATUS_NOT_SUPPORTED); its split-K scratch is a
+ * fixed 4 MiB device array inside the library (N <= 131072, larger requests
+ * return DNNOPT_STATUS_EXCEEDS_SCRATCH).  The first call on a device looks up
+ * that array; make it before any stream capture.  All calls share the array:
+ * calls that overlap on the GPU race and must be serialised by the caller. */
+int dnnopt_cuda_gemm_f32_noalloc(const dnnopt_gemm_desc* d, const float* A, const float* B,
+                                 float* C, void* stream);
 
 /* ------------------------------------------------------------------------
  * Runtime control
