@@ -49,8 +49,10 @@ DeviceInfo info_of(const DeviceContext* ctx) {
     return i;
 }
 
+bool is_kn(KernelId k) { return k == KernelId::GemvKn || k == KernelId::GemvKnCluster; }
+
 int vec_of(const Plan& p) {
-    return p.kernel == KernelId::GemvKn ? p.kn.vec4 : p.nk.vec;
+    return is_kn(p.kernel) ? p.kn.vec4 : p.nk.vec;
 }
 
 In in_a(Kind k) {
@@ -97,8 +99,16 @@ int launch_plan(Kind kind, const GemmArgs& g, const Plan& p, const float* scales
             note_launch();
             break;
         }
+        case KernelId::GemvKnCluster:
+            e = launch_gemv_kn_cluster(in_a(kind), in_b(kind), g, p.kn, s);
+            note_launch();
+            break;
         case KernelId::GemvNk:
             e = launch_gemv_nk(dot_kind(kind), g, p.nk, scales, s);
+            note_launch();
+            break;
+        case KernelId::GemvRows:
+            e = launch_gemv_rows(dot_kind(kind), g, p.nk.mt, p.nk.grid, scales, s);
             note_launch();
             break;
         case KernelId::GemvNkRows: {
@@ -168,31 +178,37 @@ Plan get_plan(Kind kind, const GemmArgs& g, DeviceContext* ctx, cudaStream_t s,
               const float* scales) {
     const DeviceInfo info = info_of(ctx);
     Plan h = heuristic_plan(kind, g, info);
-    const bool tunable = h.kernel == KernelId::GemvKn || h.kernel == KernelId::GemvNk;
+    const bool tunable = is_kn(h.kernel) || h.kernel == KernelId::GemvNk;
     if (!tunable) return h;
     const uint64_t key = plan_key(kind, g, vec_of(h));
     Plan c = h;
-    if (cache_lookup(key, &c) && c.kernel == h.kernel) {
+    if (cache_lookup(key, &c) && (c.kernel == h.kernel || (is_kn(c.kernel) && is_kn(h.kernel)))) {
         // Layout-derived fields come from the current call.
-        if (c.kernel == KernelId::GemvKn) c.kn.vec4 = h.kn.vec4;
+        if (is_kn(c.kernel)) c.kn.vec4 = h.kn.vec4;
         else c.nk.vec = h.nk.vec;
         return c;
     }
     if (!autotune_enabled() || !ctx) return h;
 
     // Candidates around the heuristic choice.
-    Plan cands[4];
+    Plan cands[12];
     int nc = 0;
-    if (h.kernel == KernelId::GemvKn) {
-        const int s0 = h.kn.splits;
-        const int tries[4] = {s0, s0 / 2, s0 * 2, 1};
+    if (is_kn(h.kernel)) {
+        const GemvKnPlan ws_plan = kn_plan_for(kind, g, info, 0, false);
+        const int tries[6] = {h.kn.splits, h.kn.splits / 2, h.kn.splits * 2, 1,
+                              ws_plan.splits, ws_plan.splits * 2};
         for (int t : tries) {
             if (t < 1) continue;
-            Plan q = h;
-            q.kn = kn_plan_for(kind, g, info, t);
-            bool dup = false;
-            for (int i = 0; i < nc; ++i) dup = dup || cands[i].kn.splits == q.kn.splits;
-            if (!dup) cands[nc++] = q;
+            for (int cl = 0; cl < 2; ++cl) {
+                Plan q = h;
+                q.kn = kn_plan_for(kind, g, info, t, cl == 1);
+                if ((cl == 1) != (q.kn.cluster == 1)) continue;
+                q.kernel = q.kn.cluster ? KernelId::GemvKnCluster : KernelId::GemvKn;
+                bool dup = false;
+                for (int i = 0; i < nc; ++i)
+                    dup = dup || (cands[i].kn.splits == q.kn.splits && cands[i].kernel == q.kernel);
+                if (!dup && nc < 12) cands[nc++] = q;
+            }
         }
     } else {
         const int g0 = h.nk.grid;

@@ -11,7 +11,8 @@
 //   * persistent CTAs (one per SM) walk 128-row tiles of A;
 //   * warp 0 issues TMA loads of A in 128 x 64 K-blocks (128-byte swizzle)
 //     into an N-stage shared-memory ring (mbarrier full/empty pairs);
-//   * B (K x N) is gathered once per CTA into the same K-major swizzled layout;
+//   * the first ring of A loads is issued before B (K x N) is gathered once
+//     per CTA into the same K-major swizzled layout (16-byte row loads);
 //   * warp 1 issues tcgen05.mma (M=128, N=n_pad, K=16) into one of two TMEM
 //     accumulators, so the epilogue of tile t overlaps the MMAs of tile t+1;
 //   * warps 2-5 drain TMEM with tcgen05.ld, apply alpha/beta (the reference
@@ -42,6 +43,7 @@ struct TcParams {
     const uint16_t* B;
     int64_t ldb;
     int b_trans;
+    int b_vec;         // B is K x N with 16-byte aligned rows (vector gather)
     const float* C;    // read only when beta != 0
     int64_t ldc;
     uint32_t tmem_cols;
@@ -67,6 +69,21 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
+    // Tiles of this CTA: blockIdx.x, +gridDim.x, ...; producer iteration i
+    // loads K-block (i % num_kb) of the (i / num_kb)-th of them.
+    const int my_tiles = (p.num_tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                         static_cast<int>(gridDim.x);
+    const uint32_t total_iters = static_cast<uint32_t>(my_tiles > 0 ? my_tiles : 0) * p.num_kb;
+    auto issue_load = [&](uint32_t i) {
+        const uint32_t s = i % p.stages;
+        const int tile = static_cast<int>(blockIdx.x) + static_cast<int>(i / p.num_kb) * static_cast<int>(gridDim.x);
+        const int kb = static_cast<int>(i % p.num_kb);
+        mbar_arrive_expect_tx(&full[s], kStageBytes);
+        tma_load_2d(sA + s * kStageBytes, &tmA, &full[s], kb * kKBlock, tile * BM);
+    };
+    const uint32_t pre = total_iters < static_cast<uint32_t>(p.stages) ? total_iters
+                                                                       : static_cast<uint32_t>(p.stages);
+
     if (tid == 0) {
         for (int s = 0; s < p.stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         for (int b = 0; b < 2; ++b) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], 4); }
@@ -74,16 +91,48 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         fence_mbar_init();
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmC);
+        // The first ring of A loads goes out before B is gathered: every stage
+        // starts empty, so these need no wait.
+        for (uint32_t i = 0; i < pre; ++i) issue_load(i);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, p.tmem_cols);
         tmem_relinquish();
     }
 
-    // Gather B (K x N, or N x K when b_trans) into K-major 128B-swizzled rows:
+    // Gather B into K-major 128B-swizzled rows (the UMMA B operand):
     // byte offset of (n, k) = kb*n_pad*128 + n*128 + ((c ^ (n&7))*16) + (k%8)*2,
-    // kb = k/64, c = (k%64)/8.  Consecutive threads take consecutive n.
-    {
+    // kb = k/64, c = (k%64)/8.
+    if (p.b_vec) {
+        // B is K x N with 16-byte aligned rows: one 16-byte load brings 8
+        // consecutive n of row k; consecutive threads take consecutive k so
+        // the 2-byte shared stores of a warp fall in distinct banks.
+        const int kpad = p.num_kb * kKBlock;
+        const int n8s = p.n_pad / 8;
+        for (int idx = tid; idx < kpad * n8s; idx += kThreads) {
+            const int k = idx % kpad, n8 = idx / kpad;
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (k < p.K) {
+                if (n8 * 8 + 8 <= p.N) {
+                    v = __ldg(reinterpret_cast<const uint4*>(p.B + (int64_t)k * p.ldb + n8 * 8));
+                } else {
+                    uint32_t w[4] = {0u, 0u, 0u, 0u};
+                    for (int j = 0; j < 8 && n8 * 8 + j < p.N; ++j)
+                        w[j >> 1] |= static_cast<uint32_t>(p.B[(int64_t)k * p.ldb + n8 * 8 + j]) << ((j & 1) * 16);
+                    v = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+            }
+            const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+            const int kb = k >> 6, c = (k & 63) >> 3;
+            uint8_t* base_kb = sB + kb * p.n_pad * 128 + (k & 7) * 2;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int n = n8 * 8 + j;
+                const uint16_t val = static_cast<uint16_t>(w4[j >> 1] >> ((j & 1) * 16));
+                *reinterpret_cast<uint16_t*>(base_kb + n * 128 + ((c ^ (n & 7)) * 16)) = val;
+            }
+        }
+    } else {
         const int total = p.num_kb * 8 * p.n_pad;
         for (int idx = tid; idx < total; idx += kThreads) {
             const int n = idx % p.n_pad, rest = idx / p.n_pad;
@@ -113,14 +162,10 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
-            uint32_t it = 0;
-            for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
-                for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
-                    const uint32_t s = it % p.stages, ph = (it / p.stages) & 1u;
-                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.err)) break;
-                    mbar_arrive_expect_tx(&full[s], kStageBytes);
-                    tma_load_2d(sA + s * kStageBytes, &tmA, &full[s], kb * kKBlock, tile * BM);
-                }
+            for (uint32_t i = pre; i < total_iters && !*abort_flag; ++i) {
+                const uint32_t s = i % p.stages, ph = (i / p.stages) & 1u;
+                if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.err)) break;
+                issue_load(i);
             }
         }
     } else if (warp == 1) {
@@ -294,6 +339,7 @@ cudaError_t launch_gemm_bf16_tc(const GemmArgs& g, int num_sms, uint32_t* err, c
     p.num_tiles = (g.M + BM - 1) / BM;
     p.alpha = g.alpha; p.beta = g.beta;
     p.B = static_cast<const uint16_t*>(g.B); p.ldb = g.ldb; p.b_trans = g.b_trans;
+    p.b_vec = (!g.b_trans && reinterpret_cast<uintptr_t>(g.B) % 16 == 0 && g.ldb % 8 == 0) ? 1 : 0;
     p.C = static_cast<const float*>(g.C); p.ldc = g.ldc;
     uint32_t cols = 32;
     while (cols < static_cast<uint32_t>(2 * L.n_pad)) cols <<= 1;

@@ -20,6 +20,8 @@
 //   * The grid is sized by the host to one wave of resident CTAs over the
 //     148 SMs (splits = resident CTAs / strips).
 #include <mutex>
+#include <set>
+#include <utility>
 
 #include "common.cuh"
 #include "dnnopt_b200.h"
@@ -251,6 +253,208 @@ gemv_kn_kernel(const KnParams p) {
     if (tid == 0) p.counters[blockIdx.x] = 0u;   // ready for the next launch on this stream
 }
 
+// ---------------------------------------------------------------------------
+// Cluster variant: the K-splits of one strip form a thread-block cluster
+// (gridDim.y == cluster size S <= 16) and reduce through distributed shared
+// memory instead of the global workspace.  Each CTA:
+//   1. waits for the previous grid (programmatic dependent launch) and lets
+//      the next one start launching;
+//   2. issues its first batch of B loads, then stages its whole A chunk
+//      (<= kClusterMaxChunk rows) while those loads are in flight;
+//   3. streams the rest of its rows with register double-buffering;
+//   4. reduces its 8 warps in shared memory into a [MT][128] partial strip;
+//   5. after a cluster barrier, CTA rank r sums column j (j % S == r) over the
+//      S partials in rank order (deterministic), applies alpha/beta and writes
+//      C; a second cluster barrier keeps every partial alive until read.
+// ---------------------------------------------------------------------------
+constexpr int kClusterMaxChunk = 1024;   // K rows per CTA in the cluster variant
+
+template <In IA, In IB, int MT, bool VEC4>
+__global__ void __launch_bounds__(kThreads)
+gemv_kn_cluster_kernel(const KnParams p) {
+    using TA = typename Elem<IA>::T;
+    using TB = typename Elem<IB>::T;
+    constexpr int U = (MT >= 4) ? 4 : 8;          // rows per warp per batch
+    constexpr int kRowsPerBatch = kWarps * U;
+
+    extern __shared__ __align__(16) float dsm[];
+    // [0, max(chunk*MT, 8*MT*128)) staged A, then per-warp partials;
+    // [red_floats, +MT*128) the CTA's partial strip read by the cluster.
+    const int stage_floats = p.kchunk * MT;
+    const int red_floats = stage_floats > kWarps * MT * kTileN ? stage_floats : kWarps * MT * kTileN;
+    float* sA = dsm;
+    float* red = dsm;
+    float* part = dsm + red_floats;
+
+    pdl_wait();
+    pdl_launch_dependents();
+
+    const GemmArgs& g = p.g;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n0 = blockIdx.x * kTileN;
+    const int split = blockIdx.y;
+    const int k_begin = split * p.kchunk;
+    const int kn = max(0, min(g.K, k_begin + p.kchunk) - k_begin);
+    const bool full_tile = (n0 + kTileN) <= g.N;
+    const TA* A = static_cast<const TA*>(g.A);
+    const TB* B = static_cast<const TB*>(g.B);
+    const int nb = (kn + kRowsPerBatch - 1) / kRowsPerBatch;
+
+    auto load_batch = [&](float (&b)[U][4], int it) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int r = it * kRowsPerBatch + u * kWarps + warp;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) b[u][c] = 0.0f;
+            if (r < kn) {
+                const TB* row = B + (int64_t)(k_begin + r) * g.ldb + n0;
+                if (VEC4 && full_tile) {
+                    load4<IB>(row + 4 * lane, b[u]);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        int col = slot_col<VEC4>(lane, c);
+                        if (n0 + col < g.N) b[u][c] = dec<IB>(row[col]);
+                    }
+                }
+            }
+        }
+    };
+
+    float acc[MT][4];
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[m][c] = 0.0f;
+
+    auto compute_batch = [&](const float (&b)[U][4], int it) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int r = it * kRowsPerBatch + u * kWarps + warp;
+            if (r < kn) {
+                float a[MT];
+                if constexpr (MT % 4 == 0) {
+#pragma unroll
+                    for (int q = 0; q < MT / 4; ++q) {
+                        float4 v = *reinterpret_cast<const float4*>(&sA[r * MT + 4 * q]);
+                        a[4 * q] = v.x; a[4 * q + 1] = v.y; a[4 * q + 2] = v.z; a[4 * q + 3] = v.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int m = 0; m < MT; ++m) a[m] = sA[r * MT + m];
+                }
+#pragma unroll
+                for (int m = 0; m < MT; ++m)
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) acc[m][c] = fmaf(a[m], b[u][c], acc[m][c]);
+            }
+        }
+    };
+
+    float b0[U][4], b1[U][4];
+    if (nb > 0) load_batch(b0, 0);
+
+    // Stage A[0:MT, k_begin:k_begin+kn] as sA[r*MT + m] while B is in flight.
+    for (int idx = tid; idx < kn * MT; idx += kThreads) {
+        int r = idx / MT, m = idx - r * MT;
+        float v = 0.0f;
+        if (m < g.M) {
+            int64_t off = g.a_trans ? (int64_t)(k_begin + r) * g.lda + m
+                                    : (int64_t)m * g.lda + (k_begin + r);
+            v = dec<IA>(A[off]);
+        }
+        sA[idx] = v;
+    }
+    __syncthreads();
+
+    for (int it = 0; it < nb; it += 2) {
+        if (it + 1 < nb) load_batch(b1, it + 1);
+        compute_batch(b0, it);
+        if (it + 1 < nb) {
+            if (it + 2 < nb) load_batch(b0, it + 2);
+            compute_batch(b1, it + 1);
+        }
+    }
+    __syncthreads();   // sA is reused for the warp partials below
+
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) red[(warp * MT + m) * kTileN + slot_col<VEC4>(lane, c)] = acc[m][c];
+    __syncthreads();
+    for (int idx = tid; idx < MT * kTileN; idx += kThreads) {
+        int m = idx / kTileN, j = idx - m * kTileN;
+        float sum = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) sum += red[(w * MT + m) * kTileN + j];
+        part[idx] = sum;
+    }
+
+    float* C = static_cast<float*>(g.C);
+    const int S = p.splits;
+    if (S == 1) {
+        __syncthreads();
+        for (int idx = tid; idx < MT * kTileN; idx += kThreads) {
+            int m = idx / kTileN, j = idx - m * kTileN;
+            if (m < g.M && n0 + j < g.N) {
+                float* cp = C + (int64_t)m * g.ldc + n0 + j;
+                float s = part[idx];
+                *cp = (g.beta == 0.0f) ? g.alpha * s : fmaf(g.alpha, s, g.beta * *cp);
+            }
+        }
+        return;
+    }
+    cluster_sync_all();
+    const uint32_t rank = cluster_ctarank();
+    const uint32_t part_addr = smem_u32(part);
+    // Columns j with j % S == rank, all MT rows: MT * ceil(128 / S) outputs.
+    const int ncol = (kTileN - static_cast<int>(rank) + S - 1) / S;
+    for (int idx = tid; idx < MT * ncol; idx += kThreads) {
+        int m = idx / ncol, jj = idx - m * ncol;
+        int j = static_cast<int>(rank) + jj * S;
+        float sum = 0.0f;
+        for (int q = 0; q < S; ++q)
+            sum += ld_dsmem_f32(map_to_cta(part_addr + static_cast<uint32_t>((m * kTileN + j) * 4),
+                                           static_cast<uint32_t>(q)));
+        if (m < g.M && n0 + j < g.N) {
+            float* cp = C + (int64_t)m * g.ldc + n0 + j;
+            *cp = (g.beta == 0.0f) ? g.alpha * sum : fmaf(g.alpha, sum, g.beta * *cp);
+        }
+    }
+    cluster_sync_all();
+}
+
+template <In IA, In IB, int MT, bool VEC4>
+const void* kn_cluster_fn() {
+    return reinterpret_cast<const void*>(&gemv_kn_cluster_kernel<IA, IB, MT, VEC4>);
+}
+
+template <In IA, In IB>
+const void* kn_cluster_select_mt(int mt, int vec4) {
+    switch (mt) {
+        case 1: return vec4 ? kn_cluster_fn<IA, IB, 1, true>() : kn_cluster_fn<IA, IB, 1, false>();
+        case 2: return vec4 ? kn_cluster_fn<IA, IB, 2, true>() : kn_cluster_fn<IA, IB, 2, false>();
+        case 4: return vec4 ? kn_cluster_fn<IA, IB, 4, true>() : kn_cluster_fn<IA, IB, 4, false>();
+        case 8: return vec4 ? kn_cluster_fn<IA, IB, 8, true>() : kn_cluster_fn<IA, IB, 8, false>();
+        default: return nullptr;
+    }
+}
+
+const void* kn_cluster_select(In ia, In ib, int mt, int vec4) {
+    if (ia == In::F32 && ib == In::F32) return kn_cluster_select_mt<In::F32, In::F32>(mt, vec4);
+    if (ia == In::BF16 && ib == In::BF16) return kn_cluster_select_mt<In::BF16, In::BF16>(mt, vec4);
+    if (ia == In::F32R && ib == In::F32R) return kn_cluster_select_mt<In::F32R, In::F32R>(mt, vec4);
+    if (ia == In::RE4 && ib == In::RE5) return kn_cluster_select_mt<In::RE4, In::RE5>(mt, vec4);
+    if (ia == In::RE5 && ib == In::RE5) return kn_cluster_select_mt<In::RE5, In::RE5>(mt, vec4);
+    return nullptr;
+}
+
+size_t cluster_smem_bytes(int mt, int kchunk) {
+    size_t stage = static_cast<size_t>(kchunk) * mt;
+    size_t red = static_cast<size_t>(kWarps) * mt * kTileN;
+    return ((stage > red ? stage : red) + static_cast<size_t>(mt) * kTileN) * sizeof(float);
+}
+
 template <In IA, In IB, int MT, bool VEC4>
 const void* kn_fn() {
     return reinterpret_cast<const void*>(&gemv_kn_kernel<IA, IB, MT, VEC4>);
@@ -289,6 +493,59 @@ cudaError_t gemv_kn_occupancy(In ia, In ib, int mt, int vec4, int* blocks_per_sm
     const void* fn = kn_select(ia, ib, mt, vec4);
     if (!fn) return cudaErrorInvalidValue;
     return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, fn, kThreads, 0);
+}
+
+int gemv_kn_cluster_max_chunk() { return kClusterMaxChunk; }
+
+cudaError_t gemv_kn_cluster_occupancy(In ia, In ib, int mt, int vec4, int kchunk, int* blocks_per_sm) {
+    const void* fn = kn_cluster_select(ia, ib, mt, vec4);
+    if (!fn) return cudaErrorInvalidValue;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, fn, kThreads,
+                                                         cluster_smem_bytes(mt, kchunk));
+}
+
+cudaError_t launch_gemv_kn_cluster(In ia, In ib, const GemmArgs& g, const GemvKnPlan& p,
+                                   cudaStream_t s) {
+    const void* fn = kn_cluster_select(ia, ib, p.mt, p.vec4);
+    if (!fn || g.M > p.mt || p.splits < 1 || p.splits > 16 || p.kchunk < 1 ||
+        p.kchunk > kClusterMaxChunk)
+        return cudaErrorInvalidValue;
+    if (p.splits > 8) {
+        static std::mutex mu;
+        static std::set<std::pair<int, const void*>> done;
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        std::lock_guard<std::mutex> lk(mu);
+        if (!done.count({dev, fn})) {
+            e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            if (e != cudaSuccess) return e;
+            done.insert({dev, fn});
+        }
+    }
+    KnParams kp;
+    kp.g = g;
+    kp.splits = p.splits;
+    kp.kchunk = p.kchunk;
+    kp.n_pad = gemv_kn_tiles(g.N) * kTileN;
+    kp.ws = nullptr;
+    kp.counters = nullptr;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(gemv_kn_tiles(g.N), p.splits, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = cluster_smem_bytes(p.mt, p.kchunk);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = static_cast<unsigned>(p.splits);
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    void* args[] = {&kp};
+    return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
 cudaError_t launch_gemv_kn(In ia, In ib, const GemmArgs& g, const GemvKnPlan& p, float* ws,

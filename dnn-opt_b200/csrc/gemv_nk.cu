@@ -16,6 +16,7 @@
 // read back with conflict-free 16-byte loads; per-row partial sums are reduced
 // with warp shuffles.  Integer accumulation is exact in any order, so the
 // int8 path is bit-identical to the reference's scalar loop.
+#include <cstring>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -192,6 +193,175 @@ gemv_nk_kernel(const NkParams p) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// Register-resident variant for 16-byte aligned rows and K <= 2 * 256 chunks:
+// the CTA's 256 lanes own fixed 16-byte K-chunks (lane L: chunks L and L+256),
+// so each lane keeps its slice of A in registers for every row instead of
+// re-reading it from shared memory.  A CTA walks its contiguous row range R
+// rows at a time (R independent 16-byte loads in flight per chunk and lane),
+// accumulates MT x R partial dot products, and reduces them with a
+// 31-shuffle transpose-reduce (lane l ends with the warp total of value l),
+// then across the 8 warps through shared memory in warp order.
+// ---------------------------------------------------------------------------
+template <DotKind KIND> struct Chunk;
+template <> struct Chunk<DotKind::F32> {
+    using Acc = float;
+    __device__ static Acc dot(const uint4& b, const uint4& a, Acc acc) {
+        acc = fmaf(__uint_as_float(a.x), __uint_as_float(b.x), acc);
+        acc = fmaf(__uint_as_float(a.y), __uint_as_float(b.y), acc);
+        acc = fmaf(__uint_as_float(a.z), __uint_as_float(b.z), acc);
+        acc = fmaf(__uint_as_float(a.w), __uint_as_float(b.w), acc);
+        return acc;
+    }
+    static constexpr int EPC = 4;
+};
+template <> struct Chunk<DotKind::S8S32> {
+    using Acc = int32_t;
+    __device__ static Acc dot(const uint4& b, const uint4& a, Acc acc) {
+        acc = __dp4a(static_cast<int>(a.x), static_cast<int>(b.x), acc);
+        acc = __dp4a(static_cast<int>(a.y), static_cast<int>(b.y), acc);
+        acc = __dp4a(static_cast<int>(a.z), static_cast<int>(b.z), acc);
+        acc = __dp4a(static_cast<int>(a.w), static_cast<int>(b.w), acc);
+        return acc;
+    }
+    static constexpr int EPC = 16;
+};
+template <> struct Chunk<DotKind::S8DQ> : Chunk<DotKind::S8S32> {};
+
+struct RowsParams {
+    GemmArgs g;
+    int rows_per_cta;   // multiple of R
+    const float* scales;
+};
+
+// 16 bytes of A row m starting at element k (zero-filled past K; any alignment).
+template <typename TA>
+__device__ __forceinline__ uint4 load_a_chunk(const TA* A, int64_t lda, int a_trans, int m, int k,
+                                              int K) {
+    constexpr int E = 16 / sizeof(TA);
+    if (!a_trans && k + E <= K && (reinterpret_cast<uintptr_t>(A + (int64_t)m * lda + k) & 15u) == 0)
+        return *reinterpret_cast<const uint4*>(A + (int64_t)m * lda + k);
+    TA v[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e)
+        v[e] = (k + e < K) ? A[a_trans ? (int64_t)(k + e) * lda + m : (int64_t)m * lda + k + e] : TA(0);
+    uint4 r;
+    memcpy(&r, v, 16);
+    return r;
+}
+
+template <DotKind KIND, int MT, int R, int KCH>
+__global__ void __launch_bounds__(kThreads)
+gemv_rows_kernel(const RowsParams p) {
+    using C = Chunk<KIND>;
+    using Acc = typename C::Acc;
+    using TA = typename Tr<KIND>::TA;
+    static_assert(MT * R == 32, "one value per lane after the transpose-reduce");
+    __shared__ Acc red[2][kWarps][32];
+
+    pdl_wait();
+    pdl_launch_dependents();
+
+    const GemmArgs& g = p.g;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nchunks = g.K / C::EPC;                 // K % EPC == 0 on this path
+    const TA* A = static_cast<const TA*>(g.A);
+
+    uint4 a[KCH][MT];
+#pragma unroll
+    for (int j = 0; j < KCH; ++j) {
+        const int ch = tid + j * kThreads;
+#pragma unroll
+        for (int m = 0; m < MT; ++m)
+            a[j][m] = (m < g.M && ch < nchunks)
+                          ? load_a_chunk<TA>(A, g.lda, g.a_trans, m, ch * C::EPC, g.K)
+                          : make_uint4(0u, 0u, 0u, 0u);
+    }
+
+    const int row_begin = blockIdx.x * p.rows_per_cta;
+    const int row_end = min(g.N, row_begin + p.rows_per_cta);
+    const uint4* B = static_cast<const uint4*>(g.B);
+    const int64_t ldb_chunks = g.ldb / C::EPC;
+    int buf = 0;
+    for (int r0 = row_begin; r0 < row_end; r0 += R, buf ^= 1) {
+        uint4 b[KCH][R];
+#pragma unroll
+        for (int j = 0; j < KCH; ++j) {
+            const int ch = tid + j * kThreads;
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+                b[j][r] = (ch < nchunks && r0 + r < row_end) ? __ldg(B + (int64_t)(r0 + r) * ldb_chunks + ch)
+                                                            : make_uint4(0u, 0u, 0u, 0u);
+        }
+        Acc v[32];
+#pragma unroll
+        for (int m = 0; m < MT; ++m)
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                Acc acc = Acc(0);
+#pragma unroll
+                for (int j = 0; j < KCH; ++j) acc = C::dot(b[j][r], a[j][m], acc);
+                v[m * R + r] = acc;
+            }
+        // Transpose-reduce: after the step with offset s, a lane keeps the half
+        // selected by its bit s; lane l ends with the warp sum of value l.
+#pragma unroll
+        for (int s = 16; s >= 1; s >>= 1) {
+            const bool upper = (lane & s) != 0;
+#pragma unroll
+            for (int i = 0; i < s; ++i) {
+                Acc send = upper ? v[i] : v[i + s];
+                Acc keep = upper ? v[i + s] : v[i];
+                v[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, s);
+            }
+        }
+        red[buf][warp][lane] = v[0];
+        __syncthreads();
+        if (warp == 0) {
+            Acc t = red[buf][0][lane];
+#pragma unroll
+            for (int w = 1; w < kWarps; ++w) t += red[buf][w][lane];
+            const int m = lane / R, n = r0 + (lane % R);
+            if (m < g.M && n < row_end) {
+                if constexpr (KIND == DotKind::F32) {
+                    float* cp = static_cast<float*>(g.C) + (int64_t)m * g.ldc + n;
+                    *cp = (g.beta == 0.0f) ? g.alpha * t : fmaf(g.alpha, t, g.beta * *cp);
+                } else if constexpr (KIND == DotKind::S8S32) {
+                    static_cast<int32_t*>(g.C)[(int64_t)m * g.ldc + n] = t;
+                } else {
+                    float* cp = static_cast<float*>(g.C) + (int64_t)m * g.ldc + n;
+                    float scale = __fmul_rn(g.alpha, __fmul_rn(p.scales[0], p.scales[1]));
+                    float c0 = (g.beta == 0.0f) ? 0.0f : __fmul_rn(g.beta, *cp);
+                    *cp = __fadd_rn(c0, __fmul_rn(scale, static_cast<float>(t)));
+                }
+            }
+        }
+        // red[buf] is rewritten two iterations later, after the next barrier.
+    }
+}
+
+template <DotKind KIND, int KCH>
+const void* rows_select_mt(int mt) {
+    switch (mt) {
+        case 1:
+        case 2: return reinterpret_cast<const void*>(&gemv_rows_kernel<KIND, 2, 16, KCH>);
+        case 4: return reinterpret_cast<const void*>(&gemv_rows_kernel<KIND, 4, 8, KCH>);
+        case 8: return reinterpret_cast<const void*>(&gemv_rows_kernel<KIND, 8, 4, KCH>);
+        default: return nullptr;
+    }
+}
+
+const void* rows_select(DotKind kind, int mt, int kch) {
+    switch (kind) {
+        case DotKind::F32: return kch == 1 ? rows_select_mt<DotKind::F32, 1>(mt) : rows_select_mt<DotKind::F32, 2>(mt);
+        case DotKind::S8S32: return kch == 1 ? rows_select_mt<DotKind::S8S32, 1>(mt) : rows_select_mt<DotKind::S8S32, 2>(mt);
+        case DotKind::S8DQ: return kch == 1 ? rows_select_mt<DotKind::S8DQ, 1>(mt) : rows_select_mt<DotKind::S8DQ, 2>(mt);
+        default: return nullptr;
+    }
+}
+
+int rows_r(int mt) { return mt <= 2 ? 16 : (mt == 4 ? 8 : 4); }
+
 template <DotKind KIND, int MT, bool VEC>
 const void* nk_fn() {
     return reinterpret_cast<const void*>(&gemv_nk_kernel<KIND, MT, VEC>);
@@ -278,6 +448,51 @@ cudaError_t launch_gemv_nk(DotKind kind, const GemmArgs& g, const GemvNkPlan& p,
     int grid = (g.N + kp.rows_per_cta - 1) / kp.rows_per_cta;
     void* args[] = {&kp};
     return cudaLaunchKernel(fn, dim3(grid), dim3(kThreads), args, smem, s);
+}
+
+bool gemv_rows_supported(DotKind kind, const GemmArgs& g) {
+    if (kind == DotKind::E4M3 || g.M < 1 || g.M > 8) return false;
+    const int epc_ = epc(kind);
+    const size_t eb = kind == DotKind::F32 ? 4 : 1;
+    if (g.K % epc_ != 0 || g.K / epc_ > 2 * kThreads) return false;
+    return reinterpret_cast<uintptr_t>(g.B) % 16 == 0 && (static_cast<size_t>(g.ldb) * eb) % 16 == 0;
+}
+
+cudaError_t gemv_rows_occupancy(DotKind kind, int mt, int K, int* blocks_per_sm) {
+    const int kch = (K / epc(kind) + kThreads - 1) / kThreads;
+    const void* fn = rows_select(kind, mt, kch <= 1 ? 1 : 2);
+    if (!fn) return cudaErrorInvalidValue;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, fn, kThreads, 0);
+}
+
+cudaError_t launch_gemv_rows(DotKind kind, const GemmArgs& g, int mt, int grid, const float* scales,
+                             cudaStream_t s) {
+    if (!gemv_rows_supported(kind, g) || g.M > mt) return cudaErrorInvalidValue;
+    const int kch = (g.K / epc(kind) + kThreads - 1) / kThreads;
+    const void* fn = rows_select(kind, mt, kch <= 1 ? 1 : 2);
+    if (!fn) return cudaErrorInvalidValue;
+    const int R = rows_r(mt);
+    const int groups = (g.N + R - 1) / R;
+    if (grid < 1) grid = 1;
+    if (grid > groups) grid = groups;
+    const int per = (groups + grid - 1) / grid;
+    RowsParams rp;
+    rp.g = g;
+    rp.rows_per_cta = per * R;
+    rp.scales = scales;
+    const int blocks = (g.N + rp.rows_per_cta - 1) / rp.rows_per_cta;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void* args[] = {&rp};
+    return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
 }  // namespace dnnopt_b200

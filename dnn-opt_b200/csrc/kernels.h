@@ -42,12 +42,21 @@ struct GemvKnPlan {
     int vec4;      // 1: 4-wide vector loads of B rows (aligned rows)
     int splits;    // K splits (gridDim.y)
     int kchunk;    // rows of K per split
+    int cluster;   // 1: splits form a cluster (DSMEM reduction, no workspace)
 };
 int gemv_kn_tiles(int N);
 size_t gemv_kn_ws_floats(const GemvKnPlan& p, int N);
 cudaError_t gemv_kn_occupancy(In ia, In ib, int mt, int vec4, int* blocks_per_sm);
 cudaError_t launch_gemv_kn(In ia, In ib, const GemmArgs& g, const GemvKnPlan& p, float* ws,
                            uint32_t* counters, cudaStream_t s);
+// Cluster variant: splits <= 16 form one thread-block cluster per strip and
+// reduce through distributed shared memory (no workspace); kchunk must not
+// exceed gemv_kn_cluster_max_chunk().  Launched with programmatic dependent
+// launch so its prologue overlaps the previous kernel on the stream.
+int gemv_kn_cluster_max_chunk();
+cudaError_t gemv_kn_cluster_occupancy(In ia, In ib, int mt, int vec4, int kchunk, int* blocks_per_sm);
+cudaError_t launch_gemv_kn_cluster(In ia, In ib, const GemmArgs& g, const GemvKnPlan& p,
+                                   cudaStream_t s);
 
 // ---- small-M dot-form GEMV, B is N x K (K contiguous) ----------------------
 enum class DotKind : int {
@@ -68,6 +77,14 @@ size_t gemv_nk_smem_bytes(DotKind kind, int mt, int K);
 cudaError_t launch_gemv_nk(DotKind kind, const GemmArgs& g, const GemvNkPlan& p,
                            const float* scales, cudaStream_t s);
 cudaError_t gemv_nk_occupancy(DotKind kind, int mt, int vec, int K, int* blocks_per_sm);
+
+// Register-resident dot form (F32 / S8S32 / S8DQ): B rows 16-byte aligned,
+// K a multiple of the 16-byte chunk and at most 512 chunks.  `grid` CTAs split
+// the rows evenly in groups of R (32 / mt) rows.
+bool gemv_rows_supported(DotKind kind, const GemmArgs& g);
+cudaError_t gemv_rows_occupancy(DotKind kind, int mt, int K, int* blocks_per_sm);
+cudaError_t launch_gemv_rows(DotKind kind, const GemmArgs& g, int mt, int grid, const float* scales,
+                             cudaStream_t s);
 
 // ---- general tiled SIMT kernels (any M, N, K, strides, transposes) ----------
 cudaError_t launch_gemm_tile_f32(In ia, In ib, const GemmArgs& g, cudaStream_t s);

@@ -2,14 +2,17 @@
 //
 // Dispatch rules (B200 re-statement of src/gemm/gemm.cpp:168-455, where the
 // reference routes by M < small_m_bound (8), N >= wide_n_bound and K):
-//   * M <= 8 and B stored K x N      -> GemvKn  (split-K streaming GEMV)
+//   * M <= 8 and B stored K x N      -> GemvKnCluster (split-K streaming GEMV,
+//                                      splits reduced in a thread-block cluster)
+//                                      or GemvKn (more than 16 splits of at most
+//                                      1024 rows: workspace + ticket reduction)
 //   * M <= 8 and B stored N x K      -> GemvNk  (dot-form GEMV; all int8 calls)
 //   * BF16, large M, N <= 256        -> Bf16Tc  (tcgen05 tall-skinny)
 //   * config-5 e4m3 with M > 8       -> GemvNkRows (dot form per 8-row block)
 //   * anything else                  -> TileF32 / TileS8 (general SIMT tiles)
-// The split-K factor of GemvKn is chosen so that the grid is one wave of
-// resident CTAs (strips x splits ~= occupancy x SMs), never below 32 K-rows
-// per split; autotune times {s/2, s, 2s} and keeps the fastest.
+// The split-K factor is chosen so that the grid is one wave of resident CTAs
+// (strips x splits ~= occupancy x SMs), never below 32 K-rows per split;
+// autotune times {s, s/2, 2s, 1} in both variants and keeps the fastest.
 #include "plan.h"
 
 #include <cstdio>
@@ -71,6 +74,16 @@ int kn_occupancy(Kind kind, int mt, int vec4, const DeviceInfo& info) {
     return occ;
 }
 
+int rows_occupancy(DotKind kind, int mt, int K, const DeviceInfo& info) {
+    if (!info.have_device) return 4;
+    int occ = 0;
+    if (gemv_rows_occupancy(kind, mt, K, &occ) != cudaSuccess || occ < 1) {
+        cudaGetLastError();
+        occ = 1;
+    }
+    return occ;
+}
+
 int nk_occupancy(DotKind kind, int mt, int vec, int K, const DeviceInfo& info) {
     if (!info.have_device) return 2;
     int occ = 0;
@@ -115,24 +128,37 @@ const char* kernel_name(KernelId k) {
         case KernelId::TileS8: return "gemm_tile_s8";
         case KernelId::Bf16Tc: return "gemm_bf16_tcgen05";
         case KernelId::GemvNkRows: return "gemv_nk_dot_rowblocks";
+        case KernelId::GemvKnCluster: return "gemv_kn_cluster";
+        case KernelId::GemvRows: return "gemv_rows_dot";
     }
     return "?";
 }
 
-GemvKnPlan kn_plan_for(Kind kind, const GemmArgs& g, const DeviceInfo& info, int splits_hint) {
+GemvKnPlan kn_plan_for(Kind kind, const GemmArgs& g, const DeviceInfo& info, int splits_hint,
+                       bool allow_cluster) {
     GemvKnPlan p;
     p.mt = mt_for(g.M);
     const size_t eb = static_cast<size_t>(elem_bytes_b(kind));
     p.vec4 = (aligned(g.B, 4 * eb) && g.ldb % 4 == 0) ? 1 : 0;
+    p.cluster = 0;
     const int tiles = gemv_kn_tiles(g.N);
+    const int max_splits = g.K / 32 > 1 ? g.K / 32 : 1;
+    const int cmax = gemv_kn_cluster_max_chunk();
     int splits = splits_hint;
     if (splits <= 0) {
         const int occ = kn_occupancy(kind, p.mt, p.vec4, info);
         splits = (occ * info.num_sms) / tiles;
     }
-    const int max_splits = g.K / 32 > 1 ? g.K / 32 : 1;
     if (splits > max_splits) splits = max_splits;
     if (splits < 1) splits = 1;
+    if (allow_cluster) {
+        // Cluster variant: at most 16 splits, each at most cmax rows.
+        int cs = splits > 16 ? 16 : splits;
+        if ((g.K + cs - 1) / cs <= cmax) {
+            splits = cs;
+            p.cluster = 1;
+        }
+    }
     int kchunk = (g.K + splits - 1) / splits;
     kchunk = (kchunk + 7) / 8 * 8;
     p.kchunk = kchunk;
@@ -160,7 +186,12 @@ Plan heuristic_plan(Kind kind, const GemmArgs& g, const DeviceInfo& info) {
     switch (kind) {
         case Kind::S8S32:
         case Kind::F32S8Q:
-            if (g.M <= 8 && dot_fits) {
+            if (g.M <= 8 && gemv_rows_supported(dot_kind(kind), g)) {
+                p.kernel = KernelId::GemvRows;
+                p.nk.mt = mt_for(g.M);
+                p.nk.vec = 1;
+                p.nk.grid = rows_occupancy(dot_kind(kind), p.nk.mt, g.K, info) * info.num_sms;
+            } else if (g.M <= 8 && dot_fits) {
                 p.kernel = KernelId::GemvNk;
                 p.nk = nk_plan_for(kind, g, info, 0);
             } else {
@@ -176,8 +207,15 @@ Plan heuristic_plan(Kind kind, const GemmArgs& g, const DeviceInfo& info) {
             break;
     }
     if (g.M <= 8 && !g.b_trans) {
-        p.kernel = KernelId::GemvKn;
         p.kn = kn_plan_for(kind, g, info, 0);
+        p.kernel = p.kn.cluster ? KernelId::GemvKnCluster : KernelId::GemvKn;
+        return p;
+    }
+    if (kind == Kind::F32 && g.M <= 8 && g.b_trans && gemv_rows_supported(DotKind::F32, g)) {
+        p.kernel = KernelId::GemvRows;
+        p.nk.mt = mt_for(g.M);
+        p.nk.vec = 1;
+        p.nk.grid = rows_occupancy(DotKind::F32, p.nk.mt, g.K, info) * info.num_sms;
         return p;
     }
     if (kind == Kind::F32 && g.M <= 8 && g.b_trans && dot_fits) {
@@ -197,12 +235,14 @@ std::string describe_plan(Kind, const GemmArgs&, const Plan& p) {
     char buf[160];
     switch (p.kernel) {
         case KernelId::GemvKn:
+        case KernelId::GemvKnCluster:
             std::snprintf(buf, sizeof(buf), "%s mt=%d vec4=%d splits=%d kchunk=%d%s",
                           kernel_name(p.kernel), p.kn.mt, p.kn.vec4, p.kn.splits, p.kn.kchunk,
                           p.tuned ? " tuned" : "");
             break;
         case KernelId::GemvNk:
         case KernelId::GemvNkRows:
+        case KernelId::GemvRows:
             std::snprintf(buf, sizeof(buf), "%s mt=%d vec=%d grid=%d%s", kernel_name(p.kernel),
                           p.nk.mt, p.nk.vec, p.nk.grid, p.tuned ? " tuned" : "");
             break;
@@ -265,10 +305,11 @@ bool cache_lookup(uint64_t key, Plan* out) {
     const Entry& e = it->second;
     out->kernel = static_cast<KernelId>(e.kernel);
     out->tuned = true;
-    if (out->kernel == KernelId::GemvKn) {
+    if (out->kernel == KernelId::GemvKn || out->kernel == KernelId::GemvKnCluster) {
         out->kn.splits = e.p0;
         out->kn.kchunk = e.p1;
         out->kn.mt = e.mt;
+        out->kn.cluster = out->kernel == KernelId::GemvKnCluster ? 1 : 0;
     } else {
         out->nk.grid = e.p0;
         out->nk.mt = e.mt;
@@ -279,7 +320,9 @@ bool cache_lookup(uint64_t key, Plan* out) {
 void cache_store(uint64_t key, const Plan& p, float time_us) {
     Entry e;
     e.kernel = static_cast<int32_t>(p.kernel);
-    if (p.kernel == KernelId::GemvKn) { e.p0 = p.kn.splits; e.p1 = p.kn.kchunk; e.mt = p.kn.mt; }
+    if (p.kernel == KernelId::GemvKn || p.kernel == KernelId::GemvKnCluster) {
+        e.p0 = p.kn.splits; e.p1 = p.kn.kchunk; e.mt = p.kn.mt;
+    }
     else { e.p0 = p.nk.grid; e.p1 = 0; e.mt = p.nk.mt; }
     e.time_us = time_us;
     std::lock_guard<std::mutex> lk(g_cache_mu);

@@ -30,6 +30,8 @@ enum class KernelId : int {
     TileS8 = 3,     // general SIMT int8 tile
     Bf16Tc = 4,     // tcgen05 tall-skinny BF16
     GemvNkRows = 5, // dot form over 8-row blocks of A (M > 8)
+    GemvKnCluster = 6,  // small-M split-K, splits reduced in a thread-block cluster
+    GemvRows = 7,   // small-M dot form with A in registers (aligned B rows, K <= 512 chunks)
 };
 
 struct Plan {
@@ -44,7 +46,10 @@ struct DeviceInfo {
     bool have_device = false;
 };
 
-GemvKnPlan kn_plan_for(Kind kind, const GemmArgs& g, const DeviceInfo& info, int splits_hint);
+// splits_hint <= 0: heuristic.  allow_cluster: may choose the cluster variant
+// (splits <= 16, kchunk <= gemv_kn_cluster_max_chunk()).
+GemvKnPlan kn_plan_for(Kind kind, const GemmArgs& g, const DeviceInfo& info, int splits_hint,
+                       bool allow_cluster = true);
 GemvNkPlan nk_plan_for(Kind kind, const GemmArgs& g, const DeviceInfo& info, int grid_hint);
 
 // Heuristic plan (no timing).  Needs no device when info.have_device is false

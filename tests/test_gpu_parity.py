@@ -97,7 +97,7 @@ def test_config2_device_api_deterministic(gpu, dn, golden):
 
 
 @pytest.mark.parametrize("M", range(1, 9))
-@pytest.mark.parametrize("N,K", [(1009, 1000), (33, 1023), (128, 7), (257, 4099)])
+@pytest.mark.parametrize("N,K", [(1009, 1000), (33, 1023), (128, 7), (257, 4099), (200, 40000)])
 def test_fp32_small_m_edges(gpu, dn, orc, M, N, K):
     A, B, C = ref_uniform(M * K, 1), ref_uniform(K * N, 2), ref_uniform(M * N, 3)
     ref = C.copy()
@@ -193,6 +193,23 @@ def test_cblas_256_all_orders(gpu, dn, orc):
                 assert np.max(np.abs(C - ref)) <= fp32_tol(K), (order, ta, tb)
 
 
+@pytest.mark.parametrize("M,N,K,beta", [(5, 777, 1024, 0.5), (1, 4096, 4096, 0.0), (8, 300, 8000, -1.0),
+                                         (3, 64, 30, 0.0)])
+def test_fp32_transposed_b_small_m(gpu, dn, orc, M, N, K, beta):
+    """op(B) = B^T (B stored N x K): the dot-form kernels."""
+    torch = gpu
+    A, Bt, C0 = ref_uniform(M * K, 21), ref_uniform(N * K, 22), ref_uniform(M * N, 23)
+    ref = C0.copy()
+    orc.gemm_f32(M, N, K, 1.0, A, K, np.ascontiguousarray(Bt.reshape(N, K).T).ravel(), N, beta,
+                 ref, N)
+    dC = torch.from_numpy(C0.copy()).cuda()
+    dn.check(dn.cuda_gemm("f32", dn.desc(M, N, K, K, K, N, 1.0, beta, trans_b=1),
+                          torch.from_numpy(A).cuda(), torch.from_numpy(Bt).cuda(), dC,
+                          torch.cuda.current_stream()))
+    torch.cuda.synchronize()
+    assert np.max(np.abs(dC.cpu().numpy() - ref)) <= fp32_tol(K)
+
+
 def test_saxpy(gpu, dn):
     X, Y = ref_uniform(1000, 1), ref_uniform(2000, 2)
     exp = Y.copy()
@@ -218,7 +235,10 @@ def test_int8_edges_bitexact(gpu, dn, orc):
                                           (7, 513, 300, 301, 305, 520, 1),
                                           (8, 64, 16, 16, 16, 64, 0),
                                           (12, 200, 777, 777, 777, 200, 0),
-                                          (2, 5000, 127, 128, 127, 5000, 3)]:
+                                          (2, 5000, 127, 128, 127, 5000, 3),
+                                          (8, 1000, 8192, 8192, 8192, 1000, 0),
+                                          (3, 3001, 4112, 4112, 4128, 3001, 0),
+                                          (6, 17, 64, 80, 64, 17, 0)]:
         A = int8_uniform(M * lda, 7)
         Bb = int8_uniform(N * ldb + off, 8)
         ref = np.zeros(M * ldc, np.int32)
@@ -369,9 +389,9 @@ def test_e4m3_decode_ffn(gpu, dn, orc, shape):
 # -------------------------------------------------------- runtime paths ----
 def test_plan_selection_on_device(gpu, dn):
     assert dn.plan_describe(dn.KIND_F32, dn.desc(1, 4096, 4096, 4096, 4096, 4096)).startswith(
-        "gemv_kn_splitk mt=1 vec4=1")
+        "gemv_kn_cluster mt=1 vec4=1")
     assert dn.plan_describe(dn.KIND_S8S32, dn.desc(4, 11008, 4096, 4096, 4096, 11008)).startswith(
-        "gemv_nk_dot mt=4 vec=1")
+        "gemv_rows_dot mt=4 vec=1")
 
 
 def test_autotune_roundtrip(gpu, dn, orc, tmp_path):
