@@ -52,6 +52,7 @@ DeviceInfo info_of(const DeviceContext* ctx) {
 bool is_kn(KernelId k) { return k == KernelId::GemvKn || k == KernelId::GemvKnCluster; }
 
 int vec_of(const Plan& p) {
+    if (p.kernel == KernelId::E4m3Tc) return 1;
     return is_kn(p.kernel) ? p.kn.vec4 : p.nk.vec;
 }
 
@@ -127,6 +128,20 @@ int launch_plan(Kind kind, const GemmArgs& g, const Plan& p, const float* scales
             }
             break;
         }
+        case KernelId::E4m3Tc: {
+            for (int m0 = 0; m0 < g.M && e == cudaSuccess; m0 += 8) {
+                GemmArgs r = g;
+                r.M = g.M - m0 < 8 ? g.M - m0 : 8;
+                r.A = static_cast<const uint16_t*>(g.A) + static_cast<size_t>(m0) * g.lda;
+                r.C = static_cast<uint16_t*>(g.C) + static_cast<size_t>(m0) * g.ldc;
+                const size_t wsf = gemm_e4m3_tc_ws_floats(r, p.e4);
+                st = ensure_workspace(ctx, s, wsf, static_cast<size_t>((g.N + 127) / 128), 0, &w);
+                if (st != DNNOPT_STATUS_SUCCESS) return st;
+                e = launch_gemm_e4m3_tc(r, p.e4, scales, w->ws, w->counters, w->err, s);
+                note_launch();
+            }
+            break;
+        }
         case KernelId::TileF32:
             if (kind == Kind::E4M3BF16 || kind == Kind::S8S32 || kind == Kind::F32S8Q)
                 return set_status(DNNOPT_STATUS_NOT_SUPPORTED);
@@ -178,14 +193,15 @@ Plan get_plan(Kind kind, const GemmArgs& g, DeviceContext* ctx, cudaStream_t s,
               const float* scales) {
     const DeviceInfo info = info_of(ctx);
     Plan h = heuristic_plan(kind, g, info);
-    const bool tunable = is_kn(h.kernel) || h.kernel == KernelId::GemvNk;
+    const bool tunable = is_kn(h.kernel) || h.kernel == KernelId::GemvNk ||
+                         h.kernel == KernelId::E4m3Tc;
     if (!tunable) return h;
     const uint64_t key = plan_key(kind, g, vec_of(h));
     Plan c = h;
     if (cache_lookup(key, &c) && (c.kernel == h.kernel || (is_kn(c.kernel) && is_kn(h.kernel)))) {
         // Layout-derived fields come from the current call.
         if (is_kn(c.kernel)) c.kn.vec4 = h.kn.vec4;
-        else c.nk.vec = h.nk.vec;
+        else if (c.kernel != KernelId::E4m3Tc) c.nk.vec = h.nk.vec;
         return c;
     }
     if (!autotune_enabled() || !ctx) return h;
@@ -209,6 +225,18 @@ Plan get_plan(Kind kind, const GemmArgs& g, DeviceContext* ctx, cudaStream_t s,
                     dup = dup || (cands[i].kn.splits == q.kn.splits && cands[i].kernel == q.kernel);
                 if (!dup && nc < 12) cands[nc++] = q;
             }
+        }
+    } else if (h.kernel == KernelId::E4m3Tc) {
+        GemmArgs g8 = g;
+        g8.M = g.M < 8 ? g.M : 8;
+        const int tries[7] = {1, 2, 3, 4, 6, 8, 12};
+        for (int t : tries) {
+            Plan q = h;
+            q.e4 = gemm_e4m3_tc_plan_splits(g8, t);
+            if (q.e4.stages < 2) continue;
+            bool dup = false;
+            for (int i = 0; i < nc; ++i) dup = dup || cands[i].e4.splits == q.e4.splits;
+            if (!dup && nc < 12) cands[nc++] = q;
         }
     } else {
         const int g0 = h.nk.grid;

@@ -1,0 +1,368 @@
+// Decode-FFN weight GEMM on the tensor cores:
+//   C[m, n] = bf16_rne( scale[n] * sum_k A[m, k] * W[n, k] ),   M <= 8,
+// A bf16 [M, K], W OCP-E4M3FN [N, K] (K contiguous), scale FP32 [N], C bf16.
+// The reference has no implementation (its FP8 path, src/gemm/gemm_fp8.cpp:51-83,
+// dequantises to FP32 and calls the scalar GEMM); this is the B200 design.
+//
+// The weights are the HBM stream (235 MB at the config's shape), so they go
+// TMA -> shared memory -> tcgen05.mma.kind::f8f6f4 untouched: 128 weight rows
+// are the UMMA M dimension, the activations the N dimension.  The bf16
+// activations are split per CTA into two e4m3 operands, hi = e4m3(a*s) and
+// lo = e4m3(a*s - hi), with s a power of two chosen from the CTA's K-range
+// (max |a*s| in [128, 256)); hi + lo reproduces a*s exactly whenever the
+// residual is in e4m3's normal range, i.e. for all but values more than 2^18
+// below the range maximum.  UMMA N = 16 holds the 8 hi rows and 8 lo rows,
+// so D[:, m] + D[:, 8+m] is the full-precision product sum, undone by 1/s.
+//
+// K is split into S ranges (S chosen for an even wave count over the SMs);
+// S > 1 partial [8 x 128] strips reduce through the workspace by the last CTA
+// of each tile (atomic ticket), in split order, so the result is deterministic.
+// Roles: warp 0 TMA producer, warp 1 MMA issuer + TMEM owner, warps 2-5 build
+// the activation operand, then drain TMEM (tcgen05.ld) and write C.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace dnnopt_b200 {
+
+namespace {
+
+constexpr int BM = 128;                 // weight rows per tile (UMMA M)
+constexpr int KB = 128;                 // e4m3 elements per K-block (128-byte swizzle row)
+constexpr int kWStage = BM * KB;        // 16 KB
+constexpr int kActBlock = 16 * KB;      // 16 activation rows x 128 B per K-block
+constexpr int kThreads = 192;
+constexpr int kMaxStages = 8;
+constexpr int kMaxKc = 4096;            // K elements per CTA (activation operand 64 KB)
+constexpr size_t kSmemLimit = 227 * 1024;
+
+struct E4Params {
+    int M, N, K;
+    int kc, splits, stages;
+    const uint16_t* A;
+    int64_t lda;
+    const float* scale;
+    uint16_t* C;
+    int64_t ldc;
+    float* ws;
+    uint32_t* tickets;
+    uint32_t* err;
+};
+
+// Instruction descriptor, kind::f8f6f4: A = B = E4M3 (format 0), D = F32,
+// both K-major, M = 128, N = 16.
+constexpr uint32_t kIdescE4M3 = (1u << 4) | (0u << 7) | (0u << 10) | ((16u >> 3) << 17) |
+                                ((128u >> 4) << 24);
+
+__device__ __forceinline__ void umma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Two floats -> two OCP e4m3 bytes (RNE, saturate): x0 in the low byte.
+__device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float x0, float x1) {
+    uint16_t r;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(x1), "f"(x0));
+    return r;
+}
+
+__device__ __forceinline__ float e4m3_byte_to_f32(uint32_t b) {
+    return e4m3x2_to_f32x2(static_cast<uint16_t>(b & 0xFFu)).x;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_e4m3_tc_kernel(const __grid_constant__ CUtensorMap tmW, const E4Params p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    const int tile = blockIdx.x, split = blockIdx.y;
+    const int n0 = tile * BM;
+    const int k0 = split * p.kc;
+    const int klen = min(p.kc, p.K - k0);
+    const int nkb = (klen + KB - 1) / KB;
+    const int nkb_alloc = p.kc / KB;
+
+    uint8_t* sW = base;
+    uint8_t* sAct = sW + p.stages * kWStage;
+    float* inv_sigma = reinterpret_cast<float*>(sAct + nkb_alloc * kActBlock);
+    uint64_t* full = reinterpret_cast<uint64_t*>(inv_sigma + 8);
+    uint64_t* empty = full + p.stages;
+    uint64_t* act_ready = empty + p.stages;
+    uint64_t* mma_done = act_ready + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+    volatile int* s_last = reinterpret_cast<volatile int*>(tmem_slot + 2);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    pdl_wait();
+    pdl_launch_dependents();
+
+    const int pre = nkb < p.stages ? nkb : p.stages;
+    if (tid == 0) {
+        for (int s = 0; s < p.stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        mbar_init(act_ready, 128);
+        mbar_init(mma_done, 1);
+        *abort_flag = 0u;
+        fence_mbar_init();
+        prefetch_tmap(&tmW);
+        for (int kb = 0; kb < pre; ++kb) {
+            mbar_arrive_expect_tx(&full[kb], kWStage);
+            tma_load_2d(sW + kb * kWStage, &tmW, &full[kb], k0 + kb * KB, n0);
+        }
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 32);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            for (int kb = pre; kb < nkb && !*abort_flag; ++kb) {
+                const int s = kb % p.stages;
+                const uint32_t ph = static_cast<uint32_t>(kb / p.stages) & 1u;
+                if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.err)) break;
+                mbar_arrive_expect_tx(&full[s], kWStage);
+                tma_load_2d(sW + s * kWStage, &tmW, &full[s], k0 + kb * KB, n0);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            bool ok = mbar_wait(act_ready, 0u, abort_flag, p.err);
+            if (ok) tc_fence_after();
+            for (int kb = 0; ok && kb < nkb; ++kb) {
+                const int s = kb % p.stages;
+                const uint32_t ph = static_cast<uint32_t>(kb / p.stages) & 1u;
+                if (!mbar_wait(&full[s], ph, abort_flag, p.err)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(sW + s * kWStage);
+                const uint32_t b_addr = smem_u32(sAct + kb * kActBlock);
+#pragma unroll
+                for (int kk = 0; kk < KB / 32; ++kk)
+                    umma_f8_ss(tmem_base, umma_desc_k_sw128(a_addr + kk * 32),
+                               umma_desc_k_sw128(b_addr + kk * 32), kIdescE4M3,
+                               (kb | kk) != 0 ? 1u : 0u);
+                umma_commit(&empty[s]);
+            }
+            if (ok) umma_commit(mma_done);
+        }
+    } else {
+        // ---------------- activation operand (warps 2-5) ----------------
+        const int ew = warp - 2;              // 0..3, rows 2*ew and 2*ew+1
+        for (int rr = 0; rr < 2; ++rr) {
+            const int m = 2 * ew + rr;
+            const bool live = m < p.M;
+            const uint16_t* arow = p.A + (int64_t)m * p.lda + k0;
+            float amax = 0.0f;
+            if (live)
+                for (int k = lane; k < klen; k += 32) amax = fmaxf(amax, fabsf(bf16_bits_to_f32(arow[k])));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+            // s = 2^(8 - E) with amax < 2^E: max |a*s| in [128, 256).
+            int e = 0;
+            if (amax > 0.0f) frexpf(amax, &e);
+            e = max(-100, min(100, 8 - e));
+            const float sigma = ldexpf(1.0f, e);
+            if (lane == 0) inv_sigma[m] = ldexpf(1.0f, -e);
+            // Four consecutive k per lane -> one 4-byte store per operand row.
+            for (int kl = lane * 4; kl < nkb_alloc * KB; kl += 128) {
+                float x[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    x[j] = (live && kl + j < klen) ? bf16_bits_to_f32(arow[kl + j]) * sigma : 0.0f;
+                uint32_t hi = f32x2_to_e4m3x2(x[0], x[1]) | (f32x2_to_e4m3x2(x[2], x[3]) << 16);
+                float r[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) r[j] = x[j] - e4m3_byte_to_f32(hi >> (8 * j));
+                uint32_t lo = f32x2_to_e4m3x2(r[0], r[1]) | (f32x2_to_e4m3x2(r[2], r[3]) << 16);
+                const int kb = kl >> 7, w = kl & 127, c = w >> 4, within = w & 15;
+                uint8_t* blk = sAct + kb * kActBlock;
+                const int rh = m, rl = 8 + m;
+                *reinterpret_cast<uint32_t*>(blk + rh * 128 + ((c ^ (rh & 7)) << 4) + within) = hi;
+                *reinterpret_cast<uint32_t*>(blk + rl * 128 + ((c ^ (rl & 7)) << 4) + within) = lo;
+            }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(act_ready);
+
+        // ---------------- epilogue ----------------
+        const int q = warp & 3;
+        const int nl = q * 32 + lane;          // tile row = output column n0 + nl
+        const int n = n0 + nl;
+        float v[8];
+        bool ok = mbar_wait(mma_done, 0u, abort_flag, p.err);
+        if (ok) {
+            tc_fence_after();
+            uint32_t r[16];
+            tmem_ld_32x32b_x16(tmem_base + (static_cast<uint32_t>(q * 32) << 16), r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int m = 0; m < 8; ++m)
+                v[m] = (__uint_as_float(r[m]) + __uint_as_float(r[8 + m])) * inv_sigma[m];
+        }
+        const float sc = (n < p.N) ? p.scale[n] : 0.0f;
+        if (p.splits == 1) {
+            if (ok && n < p.N)
+                for (int m = 0; m < p.M; ++m)
+                    p.C[(int64_t)m * p.ldc + n] = __bfloat16_as_ushort(__float2bfloat16_rn(v[m] * sc));
+        } else {
+            // Every epilogue thread takes both barriers, whatever `ok` says.
+            if (ok) {
+                float* wsp = p.ws + ((int64_t)tile * p.splits + split) * (8 * BM);
+#pragma unroll
+                for (int m = 0; m < 8; ++m) __stcg(&wsp[m * BM + nl], v[m]);
+            }
+            __threadfence();
+            named_barrier_sync(1, 128);
+            if (tid == 64) {
+                uint32_t t = atomicAdd(&p.tickets[tile], 1u);
+                *s_last = (t == static_cast<uint32_t>(p.splits - 1)) ? 1 : 0;
+            }
+            named_barrier_sync(1, 128);
+            if (*s_last) {
+                __threadfence();
+                const float* wt = p.ws + (int64_t)tile * p.splits * (8 * BM);
+                if (ok && n < p.N)
+                    for (int m = 0; m < p.M; ++m) {
+                        float sum = 0.0f;
+                        for (int sp = 0; sp < p.splits; ++sp) sum += __ldcg(&wt[sp * 8 * BM + m * BM + nl]);
+                        p.C[(int64_t)m * p.ldc + n] = __bfloat16_as_ushort(__float2bfloat16_rn(sum * sc));
+                    }
+                if (tid == 64) p.tickets[tile] = 0u;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, 32);
+    }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
+                                             cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<EncodeTiledFn>(nullptr);
+        return reinterpret_cast<EncodeTiledFn>(ptr);
+    }();
+    return fn;
+}
+
+size_t smem_bytes(int stages, int kc) {
+    return 1024 + static_cast<size_t>(stages) * kWStage + static_cast<size_t>(kc / KB) * kActBlock +
+           8 * sizeof(float) + 256;
+}
+
+}  // namespace
+
+bool gemm_e4m3_tc_supported(const GemmArgs& g) {
+    if (g.M < 1 || g.M > 8 || g.N < 1 || g.K < 16 || g.a_trans) return false;
+    if (g.K % 16 || g.ldb % 16 || reinterpret_cast<uintptr_t>(g.B) % 16) return false;
+    return encode_fn() != nullptr;
+}
+
+E4m3TcPlan gemm_e4m3_tc_plan_splits(const GemmArgs& g, int splits) {
+    E4m3TcPlan p{1, 0, 0};
+    if (splits < 1) splits = 1;
+    int kc = ((g.K + splits - 1) / splits + KB - 1) / KB * KB;
+    if (kc > kMaxKc) kc = kMaxKc;
+    p.kc = kc;
+    p.splits = (g.K + kc - 1) / kc;
+    int st = kMaxStages;
+    while (st > 2 && smem_bytes(st, kc) > kSmemLimit) --st;
+    p.stages = smem_bytes(st, kc) <= kSmemLimit ? st : 0;
+    return p;
+}
+
+E4m3TcPlan gemm_e4m3_tc_plan(const GemmArgs& g, int num_sms) {
+    // Few long-lived CTAs: at most 4 K-ranges per tile, chosen for the most
+    // even wave count (each CTA has a fixed set-up cost: barriers, TMEM,
+    // building the activation operand, the split reduction).
+    const int tiles = (g.N + BM - 1) / BM;
+    E4m3TcPlan best = gemm_e4m3_tc_plan_splits(g, 1);
+    double best_balance = -1.0;
+    for (int s = 1; s <= 4; ++s) {
+        E4m3TcPlan p = gemm_e4m3_tc_plan_splits(g, s);
+        if (p.stages < 2) continue;
+        const double waves = static_cast<double>(tiles) * p.splits / num_sms;
+        const double balance = waves / static_cast<double>(static_cast<long long>(waves + 0.999999));
+        if (balance > best_balance + 0.05) {
+            best_balance = balance;
+            best = p;
+        }
+    }
+    return best;
+}
+
+size_t gemm_e4m3_tc_ws_floats(const GemmArgs& g, const E4m3TcPlan& p) {
+    if (p.splits <= 1) return 0;
+    return static_cast<size_t>((g.N + BM - 1) / BM) * p.splits * 8 * BM;
+}
+
+cudaError_t launch_gemm_e4m3_tc(const GemmArgs& g, const E4m3TcPlan& plan, const float* scale,
+                                float* ws, uint32_t* tickets, uint32_t* err, cudaStream_t s) {
+    if (!gemm_e4m3_tc_supported(g) || plan.kc <= 0 || plan.stages < 2) return cudaErrorInvalidValue;
+    if (plan.splits > 1 && (!ws || !tickets)) return cudaErrorInvalidValue;
+    CUtensorMap tmW;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(g.K), static_cast<cuuint64_t>(g.N)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(g.ldb)};
+    cuuint32_t box[2] = {KB, BM};
+    cuuint32_t estr[2] = {1, 1};
+    if (encode_fn()(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(g.B), dims, strides,
+                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
+    static thread_local int attr_dev = -1;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (attr_dev != dev) {
+        e = cudaFuncSetAttribute(gemm_e4m3_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kSmemLimit));
+        if (e != cudaSuccess) return e;
+        attr_dev = dev;
+    }
+    E4Params p;
+    p.M = g.M; p.N = g.N; p.K = g.K;
+    p.kc = plan.kc; p.splits = plan.splits; p.stages = plan.stages;
+    p.A = static_cast<const uint16_t*>(g.A); p.lda = g.lda;
+    p.scale = scale;
+    p.C = static_cast<uint16_t*>(g.C); p.ldc = g.ldc;
+    p.ws = ws; p.tickets = tickets; p.err = err;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((g.N + BM - 1) / BM, plan.splits, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem_bytes(plan.stages, plan.kc);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_e4m3_tc_kernel, tmW, p);
+}
+
+}  // namespace dnnopt_b200

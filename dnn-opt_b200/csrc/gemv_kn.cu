@@ -34,7 +34,6 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kTileN = 128;
-constexpr int kStageK = 128;   // K rows of A staged per pass
 
 template <In I> struct Elem;
 template <> struct Elem<In::F32> { using T = float; };
@@ -109,19 +108,40 @@ __device__ __forceinline__ int slot_col(int lane, int c) {
     return VEC4 ? 4 * lane + c : lane + 32 * c;
 }
 
-template <In IA, In IB, int MT, bool VEC4>
+// One kernel, two ways to reduce the K-splits of a strip:
+//   CLUSTER == false: partial strips go to the workspace; the last CTA of the
+//     strip (atomic ticket) sums them in split order;
+//   CLUSTER == true: the splits form one thread-block cluster and sum the
+//     partial strips through distributed shared memory.
+// Per CTA the critical path is kept to one DRAM round trip where possible:
+//   1. the first batch of B rows is requested before anything else; A for the
+//      pass is staged in shared memory and (beta != 0) this CTA's slice of C
+//      is prefetched while those loads are in flight;
+//   2. the remaining rows stream with register double-buffering (two batches
+//      of U rows in flight per thread);
+//   3. the 8 warps reduce in shared memory in warp order, then the splits.
+constexpr int kPassRows = 1024;   // K rows of A staged per pass
+
+template <In IA, In IB, int MT, bool VEC4, bool CLUSTER>
 __global__ void __launch_bounds__(kThreads)
 gemv_kn_kernel(const KnParams p) {
     using TA = typename Elem<IA>::T;
     using TB = typename Elem<IB>::T;
-    constexpr int U = (MT >= 4) ? 4 : 8;   // rows in flight per warp iteration
+    constexpr int U = 4;                          // rows per warp per batch (x2 in flight)
+    constexpr int kRowsPerBatch = kWarps * U;
 
-    // Shared memory: staged A panel (k-major, MT floats per row) during the
-    // K loop, then the per-warp partial strips for the reduction.
-    __shared__ __align__(16) float smem[(kStageK * MT > kWarps * MT * kTileN)
-                                            ? kStageK * MT
-                                            : kWarps * MT * kTileN];
+    extern __shared__ __align__(16) float dsm[];
+    const int pass_rows = p.kchunk < kPassRows ? p.kchunk : kPassRows;
+    const int stage_floats = pass_rows * MT;
+    const int red_floats = stage_floats > kWarps * MT * kTileN ? stage_floats : kWarps * MT * kTileN;
+    float* sA = dsm;
+    float* red = dsm;
+    float* part = dsm + red_floats;            // [MT][128] this CTA's partial strip
+    float* cpre = part + MT * kTileN;           // [MT][128] prefetched C (beta != 0)
     __shared__ int s_last;
+
+    pdl_wait();
+    pdl_launch_dependents();
 
     const GemmArgs& g = p.g;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -132,6 +152,7 @@ gemv_kn_kernel(const KnParams p) {
     const bool full_tile = (n0 + kTileN) <= g.N;
     const TA* A = static_cast<const TA*>(g.A);
     const TB* B = static_cast<const TB*>(g.B);
+    float* C = static_cast<float*>(g.C);
 
     float acc[MT][4];
 #pragma unroll
@@ -139,30 +160,18 @@ gemv_kn_kernel(const KnParams p) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) acc[m][c] = 0.0f;
 
-    for (int kb = k_begin; kb < k_end; kb += kStageK) {
-        const int kn = min(kStageK, k_end - kb);
-        // Stage A[0:MT, kb:kb+kn] as smem[r*MT + m] (zero for m >= M).
-        for (int idx = tid; idx < kn * MT; idx += kThreads) {
-            int r = idx / MT, m = idx - r * MT;
-            float v = 0.0f;
-            if (m < g.M) {
-                int64_t off = g.a_trans ? (int64_t)(kb + r) * g.lda + m
-                                        : (int64_t)m * g.lda + (kb + r);
-                v = dec<IA>(A[off]);
-            }
-            smem[idx] = v;
-        }
-        __syncthreads();
+    for (int kp = k_begin; kp < k_end; kp += kPassRows) {
+        const int kn = min(kPassRows, k_end - kp);
+        const int nb = (kn + kRowsPerBatch - 1) / kRowsPerBatch;
 
-        for (int r0 = warp; r0 < kn; r0 += kWarps * U) {
-            float b[U][4];
+        auto load_batch = [&](float (&b)[U][4], int it) {
 #pragma unroll
             for (int u = 0; u < U; ++u) {
-                const int r = r0 + u * kWarps;
+                const int r = it * kRowsPerBatch + u * kWarps + warp;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) b[u][c] = 0.0f;
                 if (r < kn) {
-                    const TB* row = B + (int64_t)(kb + r) * g.ldb + n0;
+                    const TB* row = B + (int64_t)(kp + r) * g.ldb + n0;
                     if (VEC4 && full_tile) {
                         load4<IB>(row + 4 * lane, b[u]);
                     } else {
@@ -174,20 +183,22 @@ gemv_kn_kernel(const KnParams p) {
                     }
                 }
             }
+        };
+        auto compute_batch = [&](const float (&b)[U][4], int it) {
 #pragma unroll
             for (int u = 0; u < U; ++u) {
-                const int r = r0 + u * kWarps;
+                const int r = it * kRowsPerBatch + u * kWarps + warp;
                 if (r < kn) {
                     float a[MT];
                     if constexpr (MT % 4 == 0) {
 #pragma unroll
                         for (int q = 0; q < MT / 4; ++q) {
-                            float4 v = *reinterpret_cast<const float4*>(&smem[r * MT + 4 * q]);
+                            float4 v = *reinterpret_cast<const float4*>(&sA[r * MT + 4 * q]);
                             a[4 * q] = v.x; a[4 * q + 1] = v.y; a[4 * q + 2] = v.z; a[4 * q + 3] = v.w;
                         }
                     } else {
 #pragma unroll
-                        for (int m = 0; m < MT; ++m) a[m] = smem[r * MT + m];
+                        for (int m = 0; m < MT; ++m) a[m] = sA[r * MT + m];
                     }
 #pragma unroll
                     for (int m = 0; m < MT; ++m)
@@ -195,184 +206,34 @@ gemv_kn_kernel(const KnParams p) {
                         for (int c = 0; c < 4; ++c) acc[m][c] = fmaf(a[m], b[u][c], acc[m][c]);
                 }
             }
+        };
+
+        float b0[U][4], b1[U][4];
+        if (nb > 0) load_batch(b0, 0);
+        if (kp > k_begin) __syncthreads();   // the previous pass is done with sA
+        for (int idx = tid; idx < kn * MT; idx += kThreads) {
+            int r = idx / MT, m = idx - r * MT;
+            float v = 0.0f;
+            if (m < g.M) {
+                int64_t off = g.a_trans ? (int64_t)(kp + r) * g.lda + m : (int64_t)m * g.lda + (kp + r);
+                v = dec<IA>(A[off]);
+            }
+            sA[idx] = v;
+        }
+        if (kp == k_begin && g.beta != 0.0f) {
+            for (int idx = tid; idx < MT * kTileN; idx += kThreads) {
+                int m = idx / kTileN, j = idx - m * kTileN;
+                cpre[idx] = (m < g.M && n0 + j < g.N) ? C[(int64_t)m * g.ldc + n0 + j] : 0.0f;
+            }
         }
         __syncthreads();
-    }
-
-    // Cross-warp reduction: smem[(w*MT + m)*128 + col], summed in warp order.
-    float* red = smem;
-#pragma unroll
-    for (int m = 0; m < MT; ++m)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) red[(warp * MT + m) * kTileN + slot_col<VEC4>(lane, c)] = acc[m][c];
-    __syncthreads();
-
-    float* C = static_cast<float*>(g.C);
-    if (p.splits == 1) {
-        for (int idx = tid; idx < MT * kTileN; idx += kThreads) {
-            int m = idx / kTileN, j = idx - m * kTileN;
-            float s = 0.0f;
-#pragma unroll
-            for (int w = 0; w < kWarps; ++w) s += red[(w * MT + m) * kTileN + j];
-            if (m < g.M && n0 + j < g.N) {
-                float* cp = C + (int64_t)m * g.ldc + n0 + j;
-                *cp = (g.beta == 0.0f) ? g.alpha * s : fmaf(g.alpha, s, g.beta * *cp);
+        for (int it = 0; it < nb; it += 2) {
+            if (it + 1 < nb) load_batch(b1, it + 1);
+            compute_batch(b0, it);
+            if (it + 1 < nb) {
+                if (it + 2 < nb) load_batch(b0, it + 2);
+                compute_batch(b1, it + 1);
             }
-        }
-        return;
-    }
-
-    // Split-K: publish this split's strip, then the last CTA of the strip
-    // (ticket == splits-1) sums the splits in order and writes C.
-    for (int idx = tid; idx < MT * kTileN; idx += kThreads) {
-        int m = idx / kTileN, j = idx - m * kTileN;
-        float s = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) s += red[(w * MT + m) * kTileN + j];
-        __stcg(&p.ws[((int64_t)split * MT + m) * p.n_pad + n0 + j], s);
-    }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        uint32_t ticket = atomicAdd(&p.counters[blockIdx.x], 1u);
-        s_last = (ticket == static_cast<uint32_t>(p.splits - 1));
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    for (int idx = tid; idx < MT * kTileN; idx += kThreads) {
-        int m = idx / kTileN, j = idx - m * kTileN;
-        if (m < g.M && n0 + j < g.N) {
-            float s = 0.0f;
-            for (int sp = 0; sp < p.splits; ++sp)
-                s += __ldcg(&p.ws[((int64_t)sp * MT + m) * p.n_pad + n0 + j]);
-            float* cp = C + (int64_t)m * g.ldc + n0 + j;
-            *cp = (g.beta == 0.0f) ? g.alpha * s : fmaf(g.alpha, s, g.beta * *cp);
-        }
-    }
-    if (tid == 0) p.counters[blockIdx.x] = 0u;   // ready for the next launch on this stream
-}
-
-// ---------------------------------------------------------------------------
-// Cluster variant: the K-splits of one strip form a thread-block cluster
-// (gridDim.y == cluster size S <= 16) and reduce through distributed shared
-// memory instead of the global workspace.  Each CTA:
-//   1. waits for the previous grid (programmatic dependent launch) and lets
-//      the next one start launching;
-//   2. issues its first batch of B loads, then stages its whole A chunk
-//      (<= kClusterMaxChunk rows) while those loads are in flight;
-//   3. streams the rest of its rows with register double-buffering;
-//   4. reduces its 8 warps in shared memory into a [MT][128] partial strip;
-//   5. after a cluster barrier, CTA rank r sums column j (j % S == r) over the
-//      S partials in rank order (deterministic), applies alpha/beta and writes
-//      C; a second cluster barrier keeps every partial alive until read.
-// ---------------------------------------------------------------------------
-constexpr int kClusterMaxChunk = 1024;   // K rows per CTA in the cluster variant
-
-template <In IA, In IB, int MT, bool VEC4>
-__global__ void __launch_bounds__(kThreads)
-gemv_kn_cluster_kernel(const KnParams p) {
-    using TA = typename Elem<IA>::T;
-    using TB = typename Elem<IB>::T;
-    constexpr int U = (MT >= 4) ? 4 : 8;          // rows per warp per batch
-    constexpr int kRowsPerBatch = kWarps * U;
-
-    extern __shared__ __align__(16) float dsm[];
-    // [0, max(chunk*MT, 8*MT*128)) staged A, then per-warp partials;
-    // [red_floats, +MT*128) the CTA's partial strip read by the cluster.
-    const int stage_floats = p.kchunk * MT;
-    const int red_floats = stage_floats > kWarps * MT * kTileN ? stage_floats : kWarps * MT * kTileN;
-    float* sA = dsm;
-    float* red = dsm;
-    float* part = dsm + red_floats;
-
-    pdl_wait();
-    pdl_launch_dependents();
-
-    const GemmArgs& g = p.g;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n0 = blockIdx.x * kTileN;
-    const int split = blockIdx.y;
-    const int k_begin = split * p.kchunk;
-    const int kn = max(0, min(g.K, k_begin + p.kchunk) - k_begin);
-    const bool full_tile = (n0 + kTileN) <= g.N;
-    const TA* A = static_cast<const TA*>(g.A);
-    const TB* B = static_cast<const TB*>(g.B);
-    const int nb = (kn + kRowsPerBatch - 1) / kRowsPerBatch;
-
-    auto load_batch = [&](float (&b)[U][4], int it) {
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int r = it * kRowsPerBatch + u * kWarps + warp;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) b[u][c] = 0.0f;
-            if (r < kn) {
-                const TB* row = B + (int64_t)(k_begin + r) * g.ldb + n0;
-                if (VEC4 && full_tile) {
-                    load4<IB>(row + 4 * lane, b[u]);
-                } else {
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        int col = slot_col<VEC4>(lane, c);
-                        if (n0 + col < g.N) b[u][c] = dec<IB>(row[col]);
-                    }
-                }
-            }
-        }
-    };
-
-    float acc[MT][4];
-#pragma unroll
-    for (int m = 0; m < MT; ++m)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) acc[m][c] = 0.0f;
-
-    auto compute_batch = [&](const float (&b)[U][4], int it) {
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int r = it * kRowsPerBatch + u * kWarps + warp;
-            if (r < kn) {
-                float a[MT];
-                if constexpr (MT % 4 == 0) {
-#pragma unroll
-                    for (int q = 0; q < MT / 4; ++q) {
-                        float4 v = *reinterpret_cast<const float4*>(&sA[r * MT + 4 * q]);
-                        a[4 * q] = v.x; a[4 * q + 1] = v.y; a[4 * q + 2] = v.z; a[4 * q + 3] = v.w;
-                    }
-                } else {
-#pragma unroll
-                    for (int m = 0; m < MT; ++m) a[m] = sA[r * MT + m];
-                }
-#pragma unroll
-                for (int m = 0; m < MT; ++m)
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) acc[m][c] = fmaf(a[m], b[u][c], acc[m][c]);
-            }
-        }
-    };
-
-    float b0[U][4], b1[U][4];
-    if (nb > 0) load_batch(b0, 0);
-
-    // Stage A[0:MT, k_begin:k_begin+kn] as sA[r*MT + m] while B is in flight.
-    for (int idx = tid; idx < kn * MT; idx += kThreads) {
-        int r = idx / MT, m = idx - r * MT;
-        float v = 0.0f;
-        if (m < g.M) {
-            int64_t off = g.a_trans ? (int64_t)(k_begin + r) * g.lda + m
-                                    : (int64_t)m * g.lda + (k_begin + r);
-            v = dec<IA>(A[off]);
-        }
-        sA[idx] = v;
-    }
-    __syncthreads();
-
-    for (int it = 0; it < nb; it += 2) {
-        if (it + 1 < nb) load_batch(b1, it + 1);
-        compute_batch(b0, it);
-        if (it + 1 < nb) {
-            if (it + 2 < nb) load_batch(b0, it + 2);
-            compute_batch(b1, it + 1);
         }
     }
     __syncthreads();   // sA is reused for the warp partials below
@@ -390,94 +251,99 @@ gemv_kn_cluster_kernel(const KnParams p) {
         part[idx] = sum;
     }
 
-    float* C = static_cast<float*>(g.C);
-    const int S = p.splits;
-    if (S == 1) {
+    auto store = [&](int m, int j, float sum) {
+        if (m < g.M && n0 + j < g.N) {
+            float* cp = C + (int64_t)m * g.ldc + n0 + j;
+            *cp = (g.beta == 0.0f) ? g.alpha * sum : fmaf(g.alpha, sum, g.beta * cpre[m * kTileN + j]);
+        }
+    };
+
+    if (p.splits == 1) {
+        // Each thread stores what it reduced itself: no barrier needed.
+        for (int idx = tid; idx < MT * kTileN; idx += kThreads) store(idx / kTileN, idx % kTileN, part[idx]);
+        return;
+    }
+    if constexpr (CLUSTER) {
+        cluster_sync_all();
+        const uint32_t rank = cluster_ctarank();
+        const uint32_t part_addr = smem_u32(part);
+        const int S = p.splits;
+        const int ncol = (kTileN - static_cast<int>(rank) + S - 1) / S;
+        for (int idx = tid; idx < MT * ncol; idx += kThreads) {
+            int m = idx / ncol, jj = idx - m * ncol;
+            int j = static_cast<int>(rank) + jj * S;
+            float sum = 0.0f;
+            for (int q = 0; q < S; ++q)
+                sum += ld_dsmem_f32(map_to_cta(part_addr + static_cast<uint32_t>((m * kTileN + j) * 4),
+                                               static_cast<uint32_t>(q)));
+            store(m, j, sum);
+        }
+        cluster_sync_all();
+    } else {
+        // Publish this split's strip; the last CTA of the strip (ticket
+        // splits-1) sums the splits in order and writes C.
+        for (int idx = tid; idx < MT * kTileN; idx += kThreads) {
+            int m = idx / kTileN, j = idx - m * kTileN;
+            __stcg(&p.ws[((int64_t)split * MT + m) * p.n_pad + n0 + j], part[idx]);
+        }
+        __threadfence();
         __syncthreads();
+        if (tid == 0) {
+            uint32_t ticket = atomicAdd(&p.counters[blockIdx.x], 1u);
+            s_last = (ticket == static_cast<uint32_t>(p.splits - 1));
+        }
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
         for (int idx = tid; idx < MT * kTileN; idx += kThreads) {
             int m = idx / kTileN, j = idx - m * kTileN;
             if (m < g.M && n0 + j < g.N) {
-                float* cp = C + (int64_t)m * g.ldc + n0 + j;
-                float s = part[idx];
-                *cp = (g.beta == 0.0f) ? g.alpha * s : fmaf(g.alpha, s, g.beta * *cp);
+                float sum = 0.0f;
+                for (int sp = 0; sp < p.splits; ++sp)
+                    sum += __ldcg(&p.ws[((int64_t)sp * MT + m) * p.n_pad + n0 + j]);
+                store(m, j, sum);
             }
         }
-        return;
-    }
-    cluster_sync_all();
-    const uint32_t rank = cluster_ctarank();
-    const uint32_t part_addr = smem_u32(part);
-    // Columns j with j % S == rank, all MT rows: MT * ceil(128 / S) outputs.
-    const int ncol = (kTileN - static_cast<int>(rank) + S - 1) / S;
-    for (int idx = tid; idx < MT * ncol; idx += kThreads) {
-        int m = idx / ncol, jj = idx - m * ncol;
-        int j = static_cast<int>(rank) + jj * S;
-        float sum = 0.0f;
-        for (int q = 0; q < S; ++q)
-            sum += ld_dsmem_f32(map_to_cta(part_addr + static_cast<uint32_t>((m * kTileN + j) * 4),
-                                           static_cast<uint32_t>(q)));
-        if (m < g.M && n0 + j < g.N) {
-            float* cp = C + (int64_t)m * g.ldc + n0 + j;
-            *cp = (g.beta == 0.0f) ? g.alpha * sum : fmaf(g.alpha, sum, g.beta * *cp);
-        }
-    }
-    cluster_sync_all();
-}
-
-template <In IA, In IB, int MT, bool VEC4>
-const void* kn_cluster_fn() {
-    return reinterpret_cast<const void*>(&gemv_kn_cluster_kernel<IA, IB, MT, VEC4>);
-}
-
-template <In IA, In IB>
-const void* kn_cluster_select_mt(int mt, int vec4) {
-    switch (mt) {
-        case 1: return vec4 ? kn_cluster_fn<IA, IB, 1, true>() : kn_cluster_fn<IA, IB, 1, false>();
-        case 2: return vec4 ? kn_cluster_fn<IA, IB, 2, true>() : kn_cluster_fn<IA, IB, 2, false>();
-        case 4: return vec4 ? kn_cluster_fn<IA, IB, 4, true>() : kn_cluster_fn<IA, IB, 4, false>();
-        case 8: return vec4 ? kn_cluster_fn<IA, IB, 8, true>() : kn_cluster_fn<IA, IB, 8, false>();
-        default: return nullptr;
+        if (tid == 0) p.counters[blockIdx.x] = 0u;   // ready for the next launch on this stream
     }
 }
 
-const void* kn_cluster_select(In ia, In ib, int mt, int vec4) {
-    if (ia == In::F32 && ib == In::F32) return kn_cluster_select_mt<In::F32, In::F32>(mt, vec4);
-    if (ia == In::BF16 && ib == In::BF16) return kn_cluster_select_mt<In::BF16, In::BF16>(mt, vec4);
-    if (ia == In::F32R && ib == In::F32R) return kn_cluster_select_mt<In::F32R, In::F32R>(mt, vec4);
-    if (ia == In::RE4 && ib == In::RE5) return kn_cluster_select_mt<In::RE4, In::RE5>(mt, vec4);
-    if (ia == In::RE5 && ib == In::RE5) return kn_cluster_select_mt<In::RE5, In::RE5>(mt, vec4);
-    return nullptr;
-}
-
-size_t cluster_smem_bytes(int mt, int kchunk) {
-    size_t stage = static_cast<size_t>(kchunk) * mt;
+size_t kn_smem_bytes(int mt, int kchunk) {
+    size_t rows = kchunk < kPassRows ? kchunk : kPassRows;
+    size_t stage = rows * mt;
     size_t red = static_cast<size_t>(kWarps) * mt * kTileN;
-    return ((stage > red ? stage : red) + static_cast<size_t>(mt) * kTileN) * sizeof(float);
+    return ((stage > red ? stage : red) + 2 * static_cast<size_t>(mt) * kTileN) * sizeof(float);
 }
 
-template <In IA, In IB, int MT, bool VEC4>
+template <In IA, In IB, int MT, bool VEC4, bool CL>
 const void* kn_fn() {
-    return reinterpret_cast<const void*>(&gemv_kn_kernel<IA, IB, MT, VEC4>);
+    return reinterpret_cast<const void*>(&gemv_kn_kernel<IA, IB, MT, VEC4, CL>);
 }
 
-template <In IA, In IB>
+template <In IA, In IB, bool CL>
 const void* kn_select_mt(int mt, int vec4) {
     switch (mt) {
-        case 1: return vec4 ? kn_fn<IA, IB, 1, true>() : kn_fn<IA, IB, 1, false>();
-        case 2: return vec4 ? kn_fn<IA, IB, 2, true>() : kn_fn<IA, IB, 2, false>();
-        case 4: return vec4 ? kn_fn<IA, IB, 4, true>() : kn_fn<IA, IB, 4, false>();
-        case 8: return vec4 ? kn_fn<IA, IB, 8, true>() : kn_fn<IA, IB, 8, false>();
+        case 1: return vec4 ? kn_fn<IA, IB, 1, true, CL>() : kn_fn<IA, IB, 1, false, CL>();
+        case 2: return vec4 ? kn_fn<IA, IB, 2, true, CL>() : kn_fn<IA, IB, 2, false, CL>();
+        case 4: return vec4 ? kn_fn<IA, IB, 4, true, CL>() : kn_fn<IA, IB, 4, false, CL>();
+        case 8: return vec4 ? kn_fn<IA, IB, 8, true, CL>() : kn_fn<IA, IB, 8, false, CL>();
         default: return nullptr;
     }
 }
 
-const void* kn_select(In ia, In ib, int mt, int vec4) {
-    if (ia == In::F32 && ib == In::F32) return kn_select_mt<In::F32, In::F32>(mt, vec4);
-    if (ia == In::BF16 && ib == In::BF16) return kn_select_mt<In::BF16, In::BF16>(mt, vec4);
-    if (ia == In::F32R && ib == In::F32R) return kn_select_mt<In::F32R, In::F32R>(mt, vec4);
-    if (ia == In::RE4 && ib == In::RE5) return kn_select_mt<In::RE4, In::RE5>(mt, vec4);
-    if (ia == In::RE5 && ib == In::RE5) return kn_select_mt<In::RE5, In::RE5>(mt, vec4);
+template <bool CL>
+const void* kn_select_t(In ia, In ib, int mt, int vec4) {
+    if (ia == In::F32 && ib == In::F32) return kn_select_mt<In::F32, In::F32, CL>(mt, vec4);
+    if (ia == In::BF16 && ib == In::BF16) return kn_select_mt<In::BF16, In::BF16, CL>(mt, vec4);
+    if (ia == In::F32R && ib == In::F32R) return kn_select_mt<In::F32R, In::F32R, CL>(mt, vec4);
+    if (ia == In::RE4 && ib == In::RE5) return kn_select_mt<In::RE4, In::RE5, CL>(mt, vec4);
+    if (ia == In::RE5 && ib == In::RE5) return kn_select_mt<In::RE5, In::RE5, CL>(mt, vec4);
     return nullptr;
+}
+
+const void* kn_select(In ia, In ib, int mt, int vec4) { return kn_select_t<false>(ia, ib, mt, vec4); }
+const void* kn_cluster_select(In ia, In ib, int mt, int vec4) {
+    return kn_select_t<true>(ia, ib, mt, vec4);
 }
 
 }  // namespace
@@ -492,23 +358,24 @@ size_t gemv_kn_ws_floats(const GemvKnPlan& p, int N) {
 cudaError_t gemv_kn_occupancy(In ia, In ib, int mt, int vec4, int* blocks_per_sm) {
     const void* fn = kn_select(ia, ib, mt, vec4);
     if (!fn) return cudaErrorInvalidValue;
-    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, fn, kThreads, 0);
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, fn, kThreads,
+                                                         kn_smem_bytes(mt, 256));
 }
 
-int gemv_kn_cluster_max_chunk() { return kClusterMaxChunk; }
+int gemv_kn_cluster_max_chunk() { return kPassRows; }
 
 cudaError_t gemv_kn_cluster_occupancy(In ia, In ib, int mt, int vec4, int kchunk, int* blocks_per_sm) {
     const void* fn = kn_cluster_select(ia, ib, mt, vec4);
     if (!fn) return cudaErrorInvalidValue;
     return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, fn, kThreads,
-                                                         cluster_smem_bytes(mt, kchunk));
+                                                         kn_smem_bytes(mt, kchunk));
 }
 
 cudaError_t launch_gemv_kn_cluster(In ia, In ib, const GemmArgs& g, const GemvKnPlan& p,
                                    cudaStream_t s) {
     const void* fn = kn_cluster_select(ia, ib, p.mt, p.vec4);
     if (!fn || g.M > p.mt || p.splits < 1 || p.splits > 16 || p.kchunk < 1 ||
-        p.kchunk > kClusterMaxChunk)
+        p.kchunk > kPassRows)
         return cudaErrorInvalidValue;
     if (p.splits > 8) {
         static std::mutex mu;
@@ -533,7 +400,7 @@ cudaError_t launch_gemv_kn_cluster(In ia, In ib, const GemmArgs& g, const GemvKn
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(gemv_kn_tiles(g.N), p.splits, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = cluster_smem_bytes(p.mt, p.kchunk);
+    cfg.dynamicSmemBytes = kn_smem_bytes(p.mt, p.kchunk);
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -560,9 +427,18 @@ cudaError_t launch_gemv_kn(In ia, In ib, const GemmArgs& g, const GemvKnPlan& p,
     kp.n_pad = gemv_kn_tiles(g.N) * kTileN;
     kp.ws = ws;
     kp.counters = counters;
-    dim3 grid(gemv_kn_tiles(g.N), p.splits);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(gemv_kn_tiles(g.N), p.splits, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = kn_smem_bytes(p.mt, p.kchunk);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     void* args[] = {&kp};
-    return cudaLaunchKernel(fn, grid, dim3(kThreads), args, 0, s);
+    return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
 }  // namespace dnnopt_b200

@@ -107,6 +107,19 @@ cudaError_t launch_saxpy(int n, float alpha, const float* x, int incx, float* y,
 
 // ---- BF16 tall-skinny tcgen05 GEMM (A row-major K-contiguous, TMA) ----------
 bool gemm_bf16_tc_supported(const GemmArgs& g);
+// ---- config-5 e4m3 weight GEMM on tcgen05 (kind::f8f6f4), M <= 8 ------------
+struct E4m3TcPlan {
+    int splits;   // K ranges (gridDim.y); > 1 reduces through ws + tickets
+    int kc;       // K elements per range (multiple of 128)
+    int stages;   // weight ring depth (0: shape not supported)
+};
+bool gemm_e4m3_tc_supported(const GemmArgs& g);
+E4m3TcPlan gemm_e4m3_tc_plan(const GemmArgs& g, int num_sms);
+E4m3TcPlan gemm_e4m3_tc_plan_splits(const GemmArgs& g, int splits);
+size_t gemm_e4m3_tc_ws_floats(const GemmArgs& g, const E4m3TcPlan& p);
+cudaError_t launch_gemm_e4m3_tc(const GemmArgs& g, const E4m3TcPlan& plan, const float* scale,
+                                float* ws, uint32_t* tickets, uint32_t* err, cudaStream_t s);
+
 // err: device word that receives a KernelErrorCode when a bounded wait gives up.
 cudaError_t launch_gemm_bf16_tc(const GemmArgs& g, int num_sms, uint32_t* err, cudaStream_t s);
 

@@ -2,10 +2,10 @@
 //
 // Dispatch rules (B200 re-statement of src/gemm/gemm.cpp:168-455, where the
 // reference routes by M < small_m_bound (8), N >= wide_n_bound and K):
-//   * M <= 8 and B stored K x N      -> GemvKnCluster (split-K streaming GEMV,
-//                                      splits reduced in a thread-block cluster)
-//                                      or GemvKn (more than 16 splits of at most
-//                                      1024 rows: workspace + ticket reduction)
+//   * M <= 8 and B stored K x N      -> GemvKn (split-K streaming GEMV, splits
+//                                      reduced by a ticketed last CTA) or, when
+//                                      autotune measures it faster, GemvKnCluster
+//                                      (splits reduced in a thread-block cluster)
 //   * M <= 8 and B stored N x K      -> GemvNk  (dot-form GEMV; all int8 calls)
 //   * BF16, large M, N <= 256        -> Bf16Tc  (tcgen05 tall-skinny)
 //   * config-5 e4m3 with M > 8       -> GemvNkRows (dot form per 8-row block)
@@ -130,6 +130,7 @@ const char* kernel_name(KernelId k) {
         case KernelId::GemvNkRows: return "gemv_nk_dot_rowblocks";
         case KernelId::GemvKnCluster: return "gemv_kn_cluster";
         case KernelId::GemvRows: return "gemv_rows_dot";
+        case KernelId::E4m3Tc: return "gemm_e4m3_tcgen05";
     }
     return "?";
 }
@@ -146,8 +147,12 @@ GemvKnPlan kn_plan_for(Kind kind, const GemmArgs& g, const DeviceInfo& info, int
     const int cmax = gemv_kn_cluster_max_chunk();
     int splits = splits_hint;
     if (splits <= 0) {
+        // One wave of resident CTAs, at most 16 splits of at least 64 rows:
+        // measured on B200, more splits only add reduction latency.
         const int occ = kn_occupancy(kind, p.mt, p.vec4, info);
         splits = (occ * info.num_sms) / tiles;
+        if (splits > 16) splits = 16;
+        if (splits > g.K / 64) splits = g.K / 64;
     }
     if (splits > max_splits) splits = max_splits;
     if (splits < 1) splits = 1;
@@ -199,6 +204,17 @@ Plan heuristic_plan(Kind kind, const GemmArgs& g, const DeviceInfo& info) {
             }
             return p;
         case Kind::E4M3BF16:
+            if (info.have_device) {
+                GemmArgs g8 = g;
+                g8.M = g.M < 8 ? g.M : 8;
+                if (gemm_e4m3_tc_supported(g8)) {
+                    p.e4 = gemm_e4m3_tc_plan(g8, info.num_sms);
+                    if (p.e4.stages >= 2) {
+                        p.kernel = KernelId::E4m3Tc;
+                        return p;
+                    }
+                }
+            }
             p.kernel = (g.M <= 8) ? KernelId::GemvNk : KernelId::GemvNkRows;
             p.nk = nk_plan_for(kind, g, info, 0);
             if (!dot_fits) p.kernel = KernelId::TileF32;   // rejected by the caller (no tile path)
@@ -207,7 +223,7 @@ Plan heuristic_plan(Kind kind, const GemmArgs& g, const DeviceInfo& info) {
             break;
     }
     if (g.M <= 8 && !g.b_trans) {
-        p.kn = kn_plan_for(kind, g, info, 0);
+        p.kn = kn_plan_for(kind, g, info, 0, false);
         p.kernel = p.kn.cluster ? KernelId::GemvKnCluster : KernelId::GemvKn;
         return p;
     }
@@ -245,6 +261,10 @@ std::string describe_plan(Kind, const GemmArgs&, const Plan& p) {
         case KernelId::GemvRows:
             std::snprintf(buf, sizeof(buf), "%s mt=%d vec=%d grid=%d%s", kernel_name(p.kernel),
                           p.nk.mt, p.nk.vec, p.nk.grid, p.tuned ? " tuned" : "");
+            break;
+        case KernelId::E4m3Tc:
+            std::snprintf(buf, sizeof(buf), "%s splits=%d kc=%d stages=%d", kernel_name(p.kernel),
+                          p.e4.splits, p.e4.kc, p.e4.stages);
             break;
         default:
             std::snprintf(buf, sizeof(buf), "%s", kernel_name(p.kernel));
@@ -310,6 +330,10 @@ bool cache_lookup(uint64_t key, Plan* out) {
         out->kn.kchunk = e.p1;
         out->kn.mt = e.mt;
         out->kn.cluster = out->kernel == KernelId::GemvKnCluster ? 1 : 0;
+    } else if (out->kernel == KernelId::E4m3Tc) {
+        out->e4.splits = e.p0;
+        out->e4.kc = e.p1;
+        out->e4.stages = e.mt;
     } else {
         out->nk.grid = e.p0;
         out->nk.mt = e.mt;
@@ -322,6 +346,8 @@ void cache_store(uint64_t key, const Plan& p, float time_us) {
     e.kernel = static_cast<int32_t>(p.kernel);
     if (p.kernel == KernelId::GemvKn || p.kernel == KernelId::GemvKnCluster) {
         e.p0 = p.kn.splits; e.p1 = p.kn.kchunk; e.mt = p.kn.mt;
+    } else if (p.kernel == KernelId::E4m3Tc) {
+        e.p0 = p.e4.splits; e.p1 = p.e4.kc; e.mt = p.e4.stages;
     }
     else { e.p0 = p.nk.grid; e.p1 = 0; e.mt = p.nk.mt; }
     e.time_us = time_us;

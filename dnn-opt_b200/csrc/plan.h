@@ -32,12 +32,14 @@ enum class KernelId : int {
     GemvNkRows = 5, // dot form over 8-row blocks of A (M > 8)
     GemvKnCluster = 6,  // small-M split-K, splits reduced in a thread-block cluster
     GemvRows = 7,   // small-M dot form with A in registers (aligned B rows, K <= 512 chunks)
+    E4m3Tc = 8,     // config-5 e4m3 weights on tcgen05 (kind::f8f6f4), 8-row blocks of A
 };
 
 struct Plan {
     KernelId kernel = KernelId::TileF32;
     GemvKnPlan kn{};
     GemvNkPlan nk{};
+    E4m3TcPlan e4{};
     bool tuned = false;
 };
 

@@ -71,8 +71,9 @@ class ShardedE4M3Gemm:
         elif hasattr(self.dist, "all_gather_into_tensor") and A.is_cuda:
             self.dist.all_gather_into_tensor(gathered, C_local, group=self.group)
         else:
-            parts = list(gathered.unbind(0))
-            self.dist.all_gather(parts, C_local, group=self.group)
+            # Byte views: some backends (gloo) have no 16-bit integer type.
+            parts = list(gathered.view(torch.uint8).unbind(0))
+            self.dist.all_gather(parts, C_local.view(torch.uint8), group=self.group)
         if out is None:
             out = torch.empty((M, self.N), dtype=torch.int16, device=A.device)
         out.view(M, self.world, self.n_local).copy_(gathered.permute(1, 0, 2))

@@ -1,0 +1,57 @@
+"""Worker for tests/test_sharded_cpu.py: one gloo rank of the N-sharded
+config-5 GEMM host logic, with the oracle standing in for the GPU kernel."""
+from __future__ import annotations
+
+import importlib.util
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+PKG = os.path.join(ROOT, "dnn-opt_b200")
+
+
+def main() -> None:
+    spec = importlib.util.spec_from_file_location("dnnopt_b200", os.path.join(PKG, "__init__.py"),
+                                                  submodule_search_locations=[PKG])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["dnnopt_b200"] = mod
+    spec.loader.exec_module(mod)
+    from dnnopt_b200.sharded import ShardedE4M3Gemm
+    from oracle.oracle import Oracle, bf16_bits
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    M, N, K = int(os.environ["M"]), int(os.environ["N"]), int(os.environ["K"])
+    orc = Oracle()
+    A = bf16_bits(np.random.default_rng(42).standard_normal(M * K).astype(np.float32))
+    W = (np.random.default_rng(123).standard_normal(N * K) * 0.02).astype(np.float32)
+    q, s = orc.quantize_e4m3_rows(N, K, W, K)
+
+    def compute(A_t, W_t, s_t, C_t):
+        m, n = A_t.shape[0], W_t.shape[0]
+        out = np.zeros(m * n, np.uint16)
+        orc.gemm_e4m3bf16(m, n, K, A_t.numpy().view(np.uint16).ravel(), K,
+                          W_t.numpy().ravel(), K, s_t.numpy(), out, n, want64=False)
+        C_t.copy_(torch.from_numpy(out.view(np.int16).reshape(m, n)))
+
+    sh = ShardedE4M3Gemm(dist, N, K, rank, world, compute=compute)
+    r0, r1 = sh.rows()
+    Wl = torch.from_numpy(q.reshape(N, K)[r0:r1].copy())
+    sl = torch.from_numpy(s[r0:r1].copy())
+    out = sh.forward(torch.from_numpy(A.view(np.int16).reshape(M, K)), Wl, sl)
+    full = np.zeros(M * N, np.uint16)
+    orc.gemm_e4m3bf16(M, N, K, A, K, q, K, s, full, N, want64=False)
+    ok = np.array_equal(out.numpy().view(np.uint16).ravel(), full)
+    flag = torch.tensor([1 if ok else 0])
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    dist.destroy_process_group()
+    sys.exit(0 if int(flag.item()) == 1 else 3)
+
+
+if __name__ == "__main__":
+    main()

@@ -126,12 +126,11 @@ def test_cpp_mirror_records_status(dn):
 def test_plan_selection_without_device(dn):
     # Dispatch classes of the reference's shape router (src/gemm/gemm.cpp:168-455).
     s = dn.plan_describe(dn.KIND_F32, dn.desc(1, 4096, 4096, 4096, 4096, 4096))
-    assert s.startswith("gemv_kn_cluster mt=1 vec4=1"), s
+    assert s.startswith("gemv_kn_splitk mt=1 vec4=1"), s
     s = dn.plan_describe(dn.KIND_F32, dn.desc(7, 4093, 1024, 1024, 4093, 4093, beta=0.5))
-    assert s.startswith("gemv_kn_cluster mt=8 vec4=0"), s   # prime N: rows not 16-B aligned
-    # Very long K needs more than 16 splits of <= 1024 rows: workspace variant.
-    s = dn.plan_describe(dn.KIND_F32, dn.desc(1, 64, 65536, 65536, 64, 64))
-    assert s.startswith("gemv_kn_splitk mt=1"), s
+    assert s.startswith("gemv_kn_splitk mt=8 vec4=0 splits=13"), s   # prime N: scalar loads
+    s = dn.plan_describe(dn.KIND_F32, dn.desc(2, 1009, 1024, 1024, 1009, 1009))
+    assert s.startswith("gemv_kn_splitk mt=2 vec4=0 splits=16 kchunk=64"), s
     s = dn.plan_describe(dn.KIND_S8S32, dn.desc(4, 11008, 4096, 4096, 4096, 11008))
     assert s.startswith("gemv_rows_dot mt=4 vec=1"), s
     s = dn.plan_describe(dn.KIND_S8S32, dn.desc(4, 11008, 4100, 4100, 4100, 11008))
@@ -144,8 +143,8 @@ def test_plan_selection_without_device(dn):
     assert s.startswith("gemv_rows_dot"), s
     s = dn.plan_describe(dn.KIND_F32, dn.desc(3, 64, 30, 3, 30, 64, trans_a=1, trans_b=1))
     assert s.startswith("gemv_nk_dot"), s                 # K not a multiple of 4
-    # Split-K keeps at least 32 K-rows per split.
-    s = dn.plan_describe(dn.KIND_F32, dn.desc(2, 64, 40, 40, 64, 64))
+    # Split-K keeps at least 64 K-rows per split.
+    s = dn.plan_describe(dn.KIND_F32, dn.desc(2, 64, 100, 100, 64, 64))
     assert "splits=1 " in s, s
 
 

@@ -389,9 +389,35 @@ def test_e4m3_decode_ffn(gpu, dn, orc, shape):
 # -------------------------------------------------------- runtime paths ----
 def test_plan_selection_on_device(gpu, dn):
     assert dn.plan_describe(dn.KIND_F32, dn.desc(1, 4096, 4096, 4096, 4096, 4096)).startswith(
-        "gemv_kn_cluster mt=1 vec4=1")
+        "gemv_kn_splitk mt=1 vec4=1 splits=16")
     assert dn.plan_describe(dn.KIND_S8S32, dn.desc(4, 11008, 4096, 4096, 4096, 11008)).startswith(
         "gemv_rows_dot mt=4 vec=1")
+
+
+@pytest.mark.parametrize("splits", [2, 5, 8, 16])
+def test_cluster_variant_forced(gpu, dn, orc, tmp_path, splits):
+    """The cluster (DSMEM-reduction) variant, forced through an autotune-cache
+    entry, against the oracle on a prime-N shape and an aligned shape."""
+    import struct
+    for (M, N, K, vec) in [(3, 2039, 1024, 0), (8, 1024, 2048, 1)]:
+        kchunk = ((K + splits - 1) // splits + 7) // 8 * 8
+        se = (K + kchunk - 1) // kchunk
+        mt = 1 if M <= 1 else 2 if M <= 2 else 4 if M <= 4 else 8
+        key_src = struct.pack("<10q", 0, M, N, K, K, N, N, 0, 0, vec)
+        h = 1469598103934665603
+        for b in key_src:
+            h = ((h ^ b) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+        path = tmp_path / f"cl_{splits}_{M}.bin"
+        path.write_bytes(b"DNNAUTO\x00" + struct.pack("<II", 4, 1) + struct.pack("<Q", h) +
+                         struct.pack("<iiiif", 6, se, kchunk, mt, 0.0))
+        assert dn.lib.dnnopt_autotune_load(str(path).encode()) == 1
+        d = dn.desc(M, N, K, K, N, N, 1.0, 0.5)
+        assert dn.plan_describe(dn.KIND_F32, d).startswith("gemv_kn_splitk")  # heuristic view
+        A, B, C = ref_uniform(M * K, 5), ref_uniform(K * N, 6), ref_uniform(M * N, 7)
+        ref = C.copy()
+        orc.gemm_f32(M, N, K, 1.0, A, K, B, N, 0.5, ref, N)
+        dn.check(dn.gemm_fp32(M, N, K, 1.0, A, K, B, N, 0.5, C, N))
+        assert np.max(np.abs(C - ref)) <= fp32_tol(K), (M, N, K, splits)
 
 
 def test_autotune_roundtrip(gpu, dn, orc, tmp_path):
