@@ -41,7 +41,7 @@ C2_SHAPES = [(m, n, 1024) for m in (2, 3, 5, 7) for n in (1009, 2039, 4093)]
 METRIC = "GFLOP/s (TOPS int8/fp8) and % of HBM/tensor roofline per shape vs reference CPU"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 N_SETS = 3
-SWEEP_STREAMS = 4
+SWEEP_STREAMS = 6
 
 
 def load_dnnopt():
@@ -252,18 +252,21 @@ def capture(torch, stream, fn):
 
 
 def bench_single(torch, dn, stream, fn_list, bytes_per_call, flops_per_call, iters=30):
-    """Per-call device time of a list of rotating calls (CUDA events on `stream`)."""
-    graphs = [capture(torch, stream, f) for f in fn_list]
-    for g in graphs * 2:
-        g.replay()
+    """Per-call device time of rotating calls: one CUDA graph holds 4 rounds
+    over `fn_list` (so graph-launch overhead is amortised), replayed `iters`
+    times between CUDA events on `stream`."""
+    rounds = 4
+    g = capture(torch, stream, lambda: [f() for _ in range(rounds) for f in fn_list])
+    g.replay()
+    g.replay()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(iters):
-        graphs[i % len(graphs)].replay()
+    for _ in range(iters):
+        g.replay()
     e1.record(stream)
     torch.cuda.synchronize()
-    us = e0.elapsed_time(e1) * 1e3 / iters
+    us = e0.elapsed_time(e1) * 1e3 / (iters * rounds * len(fn_list))
     return {"us_per_call": us, "GB_s": bytes_per_call / us / 1e3, "TFLOP_s": flops_per_call / us / 1e6}
 
 
@@ -330,7 +333,7 @@ def per_config(torch, dn, stream, pk, world, rank, dist):
     d = dn.desc(M, N, K, K, K, N)
     dn.check(dn.cuda_gemm("e4m3bf16", d, A, W, C, s, scale=scale))
     fns = [lambda: dn.cuda_gemm("e4m3bf16", d, A, W, C, s, scale=scale)]
-    r = bench_single(torch, dn, s, fns, N * K + 4 * N + 2 * M * K + 2 * M * N, 2.0 * M * N * K, iters=20)
+    r = bench_single(torch, dn, s, fns, N * K + 4 * N + 2 * M * K + 2 * M * N, 2.0 * M * N * K, iters=10)
     out["c5_e4m3_8x28672x8192"] = {"TFLOP_s": r["TFLOP_s"], "us": r["us_per_call"], "GB_s": r["GB_s"],
                                    "hbm_frac": r["GB_s"] / pk["hbm_gbs"],
                                    "kernel": dn.plan_describe(dn.KIND_E4M3BF16, d)}
@@ -449,11 +452,12 @@ def run_gpu_arm(args):
     # The 12 GEMMs are independent: issue them on SWEEP_STREAMS streams
     # (largest first, round-robin) forked from and joined back into `stream`,
     # so their latencies overlap; each stream has its own library workspace.
-    side = [torch.cuda.Stream(device=dev) for _ in range(SWEEP_STREAMS)]
+    side = [torch.cuda.Stream(device=dev) for _ in range(args.streams)]
     order = sorted(range(len(C2_SHAPES)), key=lambda i: -gemm_bytes(*C2_SHAPES[i], 0.5))
 
     def sweep(items, streams):
-        if len(streams) == 1:
+        if streams is None or len(streams) == 1:
+            streams = [stream]
             for (M, N, K, A, B, C) in items:
                 dn.check(dn.cuda_gemm("f32", dn.desc(M, N, K, K, N, N, 1.0, 0.5), A, B, C,
                                       streams[0]), "sweep GEMM")
@@ -473,12 +477,12 @@ def run_gpu_arm(args):
 
     for items in sets:      # first calls size the workspaces and plans (not capturable)
         sweep(items, side)
-        sweep(items, [stream])
+        sweep(items, None)
     torch.cuda.synchronize()
     n0 = dn.launch_count()
     graphs = [capture(torch, stream, lambda it=items: sweep(it, side)) for items in sets]
     launches_per_step = (dn.launch_count() - n0) // len(sets)
-    serial_graphs = [capture(torch, stream, lambda it=items: sweep(it, [stream])) for items in sets]
+    serial_graphs = [capture(torch, stream, lambda it=items: sweep(it, None)) for items in sets]
 
     clocks = ClockSampler(local)
     clocks.start()
@@ -533,7 +537,8 @@ def run_gpu_arm(args):
         "us_per_step": ms_serial * 1e3, "GFLOP_s": flops / (ms_serial * 1e-3) / 1e9,
         "GB_s": bytes_step / (ms_serial * 1e-3) / 1e9,
         "note": "same 12 GEMMs serialised on one stream (latency-bound per launch)"}
-    extra.update(per_config(torch, dn, stream, pk, world, rank, dist if use_dist else None))
+    if not args.no_per_config:
+        extra.update(per_config(torch, dn, stream, pk, world, rank, dist if use_dist else None))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -548,7 +553,7 @@ def run_gpu_arm(args):
             "config": {
                 "workload": "C2 FP32 sweep: M{2,3,5,7} x N{1009,2039,4093} x K1024, alpha=1, beta=0.5 "
                             "(12 GEMMs per step)",
-                "api": f"dnnopt_cuda_gemm_f32 (device pointers); the 12 independent GEMMs on {SWEEP_STREAMS} "
+                "api": f"dnnopt_cuda_gemm_f32 (device pointers); the 12 independent GEMMs on {args.streams} "
                        "streams forked/joined inside one CUDA graph per input set",
                 "l2": f"{N_SETS} rotating input sets ({N_SETS * bytes_step / 1e6:.0f} MB > 126 MB L2)",
                 "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
@@ -577,6 +582,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["dnnopt", "reference"], default="dnnopt")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--streams", type=int, default=SWEEP_STREAMS,
+                    help="streams the 12 independent sweep GEMMs are spread over")
+    ap.add_argument("--no-per-config", action="store_true", help="skip the per-config section")
     ap.add_argument("--profile", choices=["c1", "c2", "c3", "c4", "c5"],
                     help="run one config's kernel --reps times for an ncu capture, no bench line")
     ap.add_argument("--reps", type=int, default=3)

@@ -135,10 +135,11 @@ int launch_plan(Kind kind, const GemmArgs& g, const Plan& p, const float* scales
                 r.A = static_cast<const uint16_t*>(g.A) + static_cast<size_t>(m0) * g.lda;
                 r.C = static_cast<uint16_t*>(g.C) + static_cast<size_t>(m0) * g.ldc;
                 const size_t wsf = gemm_e4m3_tc_ws_floats(r, p.e4);
-                st = ensure_workspace(ctx, s, wsf, static_cast<size_t>((g.N + 127) / 128), 0, &w);
+                st = ensure_workspace(ctx, s, wsf, static_cast<size_t>((g.N + 127) / 128),
+                                      gemm_e4m3_tc_act_bytes(r), &w);
                 if (st != DNNOPT_STATUS_SUCCESS) return st;
-                e = launch_gemm_e4m3_tc(r, p.e4, scales, w->ws, w->counters, w->err, s);
-                note_launch();
+                e = launch_gemm_e4m3_tc(r, p.e4, scales, w->ws, w->counters, w->quant, w->err, s);
+                note_launch(2);
             }
             break;
         }

@@ -106,30 +106,45 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     if (p.b_vec) {
         // B is K x N with 16-byte aligned rows: one 16-byte load brings 8
         // consecutive n of row k; consecutive threads take consecutive k so
-        // the 2-byte shared stores of a warp fall in distinct banks.
+        // the 2-byte shared stores of a warp fall in distinct banks.  Loads
+        // are issued in groups of kGather before any store so that a thread
+        // has kGather requests in flight instead of one.
+        constexpr int kGather = 8;
         const int kpad = p.num_kb * kKBlock;
         const int n8s = p.n_pad / 8;
-        for (int idx = tid; idx < kpad * n8s; idx += kThreads) {
-            const int k = idx % kpad, n8 = idx / kpad;
-            uint4 v = make_uint4(0u, 0u, 0u, 0u);
-            if (k < p.K) {
-                if (n8 * 8 + 8 <= p.N) {
-                    v = __ldg(reinterpret_cast<const uint4*>(p.B + (int64_t)k * p.ldb + n8 * 8));
-                } else {
-                    uint32_t w[4] = {0u, 0u, 0u, 0u};
-                    for (int j = 0; j < 8 && n8 * 8 + j < p.N; ++j)
-                        w[j >> 1] |= static_cast<uint32_t>(p.B[(int64_t)k * p.ldb + n8 * 8 + j]) << ((j & 1) * 16);
-                    v = make_uint4(w[0], w[1], w[2], w[3]);
+        const int total = kpad * n8s;
+        for (int base_idx = tid; base_idx < total; base_idx += kThreads * kGather) {
+            uint4 v[kGather];
+#pragma unroll
+            for (int j = 0; j < kGather; ++j) {
+                const int idx = base_idx + j * kThreads;
+                const int k = idx % kpad, n8 = idx / kpad;
+                v[j] = make_uint4(0u, 0u, 0u, 0u);
+                if (idx < total && k < p.K) {
+                    if (n8 * 8 + 8 <= p.N) {
+                        v[j] = __ldg(reinterpret_cast<const uint4*>(p.B + (int64_t)k * p.ldb + n8 * 8));
+                    } else {
+                        uint32_t w[4] = {0u, 0u, 0u, 0u};
+                        for (int e = 0; e < 8 && n8 * 8 + e < p.N; ++e)
+                            w[e >> 1] |= static_cast<uint32_t>(p.B[(int64_t)k * p.ldb + n8 * 8 + e]) << ((e & 1) * 16);
+                        v[j] = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
                 }
             }
-            const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-            const int kb = k >> 6, c = (k & 63) >> 3;
-            uint8_t* base_kb = sB + kb * p.n_pad * 128 + (k & 7) * 2;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int n = n8 * 8 + j;
-                const uint16_t val = static_cast<uint16_t>(w4[j >> 1] >> ((j & 1) * 16));
-                *reinterpret_cast<uint16_t*>(base_kb + n * 128 + ((c ^ (n & 7)) * 16)) = val;
+            for (int j = 0; j < kGather; ++j) {
+                const int idx = base_idx + j * kThreads;
+                if (idx >= total) break;
+                const int k = idx % kpad, n8 = idx / kpad;
+                const uint32_t w4[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+                const int kb = k >> 6, c = (k & 63) >> 3;
+                uint8_t* base_kb = sB + kb * p.n_pad * 128 + (k & 7) * 2;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const int n = n8 * 8 + e;
+                    const uint16_t val = static_cast<uint16_t>(w4[e >> 1] >> ((e & 1) * 16));
+                    *reinterpret_cast<uint16_t*>(base_kb + n * 128 + ((c ^ (n & 7)) * 16)) = val;
+                }
             }
         }
     } else {

@@ -6,19 +6,20 @@
 //
 // The weights are the HBM stream (235 MB at the config's shape), so they go
 // TMA -> shared memory -> tcgen05.mma.kind::f8f6f4 untouched: 128 weight rows
-// are the UMMA M dimension, the activations the N dimension.  The bf16
-// activations are split per CTA into two e4m3 operands, hi = e4m3(a*s) and
-// lo = e4m3(a*s - hi), with s a power of two chosen from the CTA's K-range
+// are the UMMA M dimension, the activations the N dimension.  A small prep
+// kernel first splits the bf16 activations into two e4m3 operands,
+// hi = e4m3(a*s) and lo = e4m3(a*s - hi), with s a power of two per row
 // (max |a*s| in [128, 256)); hi + lo reproduces a*s exactly whenever the
 // residual is in e4m3's normal range, i.e. for all but values more than 2^18
-// below the range maximum.  UMMA N = 16 holds the 8 hi rows and 8 lo rows,
-// so D[:, m] + D[:, 8+m] is the full-precision product sum, undone by 1/s.
+// below the row maximum.  UMMA N = 16 holds the 8 hi rows and 8 lo rows (one
+// 2 KB TMA box per K-block, loaded with the weight box), so
+// D[:, m] + D[:, 8+m] is the full-precision product sum, undone by 1/s.
 //
 // K is split into S ranges (S chosen for an even wave count over the SMs);
 // S > 1 partial [8 x 128] strips reduce through the workspace by the last CTA
 // of each tile (atomic ticket), in split order, so the result is deterministic.
-// Roles: warp 0 TMA producer, warp 1 MMA issuer + TMEM owner, warps 2-5 build
-// the activation operand, then drain TMEM (tcgen05.ld) and write C.
+// Roles: warp 0 TMA producer, warp 1 MMA issuer + TMEM owner, warps 2-5 drain
+// TMEM (tcgen05.ld) and write C.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -30,8 +31,9 @@ namespace {
 
 constexpr int BM = 128;                 // weight rows per tile (UMMA M)
 constexpr int KB = 128;                 // e4m3 elements per K-block (128-byte swizzle row)
-constexpr int kWStage = BM * KB;        // 16 KB
+constexpr int kWStage = BM * KB;        // 16 KB of weights per K-block
 constexpr int kActBlock = 16 * KB;      // 16 activation rows x 128 B per K-block
+constexpr int kStage = kWStage + kActBlock;
 constexpr int kThreads = 192;
 constexpr int kMaxStages = 8;
 constexpr int kMaxKc = 4096;            // K elements per CTA (activation operand 64 KB)
@@ -40,8 +42,7 @@ constexpr size_t kSmemLimit = 227 * 1024;
 struct E4Params {
     int M, N, K;
     int kc, splits, stages;
-    const uint16_t* A;
-    int64_t lda;
+    const float* inv_sigma;   // [8] from the prep kernel
     const float* scale;
     uint16_t* C;
     int64_t ldc;
@@ -76,8 +77,51 @@ __device__ __forceinline__ float e4m3_byte_to_f32(uint32_t b) {
     return e4m3x2_to_f32x2(static_cast<uint16_t>(b & 0xFFu)).x;
 }
 
+// Activation operand: one CTA per activation row m (8 rows; rows >= M are
+// zero).  act is [16][kpad] e4m3 (row m = hi, row 8+m = lo), K-tail zero.
+__global__ void __launch_bounds__(256)
+e4m3_act_prep_kernel(const uint16_t* __restrict__ A, int64_t lda, int M, int K, int kpad,
+                     uint8_t* __restrict__ act, float* __restrict__ inv_sigma) {
+    __shared__ float wmax[8];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int m = blockIdx.x, tid = threadIdx.x;
+    const bool live = m < M;
+    const uint16_t* arow = A + (int64_t)m * lda;
+    float amax = 0.0f;
+    if (live)
+        for (int k = tid; k < K; k += 256) amax = fmaxf(amax, fabsf(bf16_bits_to_f32(arow[k])));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+    if ((tid & 31) == 0) wmax[tid >> 5] = amax;
+    __syncthreads();
+    amax = wmax[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) amax = fmaxf(amax, wmax[w]);
+    // s = 2^(8 - E) with amax < 2^E: max |a*s| in [128, 256).
+    int e = 0;
+    if (amax > 0.0f) frexpf(amax, &e);
+    e = max(-100, min(100, 8 - e));
+    const float sigma = ldexpf(1.0f, e);
+    if (tid == 0) inv_sigma[m] = ldexpf(1.0f, -e);
+    for (int k4 = tid * 4; k4 < kpad; k4 += 1024) {
+        float x[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            x[j] = (live && k4 + j < K) ? bf16_bits_to_f32(arow[k4 + j]) * sigma : 0.0f;
+        uint32_t hi = f32x2_to_e4m3x2(x[0], x[1]) | (f32x2_to_e4m3x2(x[2], x[3]) << 16);
+        float r[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) r[j] = x[j] - e4m3_byte_to_f32(hi >> (8 * j));
+        uint32_t lo = f32x2_to_e4m3x2(r[0], r[1]) | (f32x2_to_e4m3x2(r[2], r[3]) << 16);
+        *reinterpret_cast<uint32_t*>(act + (int64_t)m * kpad + k4) = hi;
+        *reinterpret_cast<uint32_t*>(act + (int64_t)(8 + m) * kpad + k4) = lo;
+    }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
-gemm_e4m3_tc_kernel(const __grid_constant__ CUtensorMap tmW, const E4Params p) {
+gemm_e4m3_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmAct,
+                    const E4Params p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -86,36 +130,34 @@ gemm_e4m3_tc_kernel(const __grid_constant__ CUtensorMap tmW, const E4Params p) {
     const int k0 = split * p.kc;
     const int klen = min(p.kc, p.K - k0);
     const int nkb = (klen + KB - 1) / KB;
-    const int nkb_alloc = p.kc / KB;
 
-    uint8_t* sW = base;
-    uint8_t* sAct = sW + p.stages * kWStage;
-    float* inv_sigma = reinterpret_cast<float*>(sAct + nkb_alloc * kActBlock);
-    uint64_t* full = reinterpret_cast<uint64_t*>(inv_sigma + 8);
+    uint8_t* sStage = base;                      // stages x (16 KB weights + 2 KB activations)
+    uint64_t* full = reinterpret_cast<uint64_t*>(sStage + p.stages * kStage);
     uint64_t* empty = full + p.stages;
-    uint64_t* act_ready = empty + p.stages;
-    uint64_t* mma_done = act_ready + 1;
+    uint64_t* mma_done = empty + p.stages;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
     volatile uint32_t* abort_flag = tmem_slot + 1;
     volatile int* s_last = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-    pdl_wait();
+    pdl_wait();          // the activation operand comes from the prep kernel
     pdl_launch_dependents();
 
+    auto issue = [&](int kb, int s) {
+        mbar_arrive_expect_tx(&full[s], kStage);
+        tma_load_2d(sStage + s * kStage, &tmW, &full[s], k0 + kb * KB, n0);
+        tma_load_2d(sStage + s * kStage + kWStage, &tmAct, &full[s], k0 + kb * KB, 0);
+    };
     const int pre = nkb < p.stages ? nkb : p.stages;
     if (tid == 0) {
         for (int s = 0; s < p.stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        mbar_init(act_ready, 128);
         mbar_init(mma_done, 1);
         *abort_flag = 0u;
         fence_mbar_init();
         prefetch_tmap(&tmW);
-        for (int kb = 0; kb < pre; ++kb) {
-            mbar_arrive_expect_tx(&full[kb], kWStage);
-            tma_load_2d(sW + kb * kWStage, &tmW, &full[kb], k0 + kb * KB, n0);
-        }
+        prefetch_tmap(&tmAct);
+        for (int kb = 0; kb < pre; ++kb) issue(kb, kb);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, 32);
@@ -133,22 +175,20 @@ gemm_e4m3_tc_kernel(const __grid_constant__ CUtensorMap tmW, const E4Params p) {
                 const int s = kb % p.stages;
                 const uint32_t ph = static_cast<uint32_t>(kb / p.stages) & 1u;
                 if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.err)) break;
-                mbar_arrive_expect_tx(&full[s], kWStage);
-                tma_load_2d(sW + s * kWStage, &tmW, &full[s], k0 + kb * KB, n0);
+                issue(kb, s);
             }
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            bool ok = mbar_wait(act_ready, 0u, abort_flag, p.err);
-            if (ok) tc_fence_after();
-            for (int kb = 0; ok && kb < nkb; ++kb) {
+            bool ok = true;
+            for (int kb = 0; kb < nkb; ++kb) {
                 const int s = kb % p.stages;
                 const uint32_t ph = static_cast<uint32_t>(kb / p.stages) & 1u;
                 if (!mbar_wait(&full[s], ph, abort_flag, p.err)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t a_addr = smem_u32(sW + s * kWStage);
-                const uint32_t b_addr = smem_u32(sAct + kb * kActBlock);
+                const uint32_t a_addr = smem_u32(sStage + s * kStage);
+                const uint32_t b_addr = a_addr + kWStage;
 #pragma unroll
                 for (int kk = 0; kk < KB / 32; ++kk)
                     umma_f8_ss(tmem_base, umma_desc_k_sw128(a_addr + kk * 32),
@@ -159,44 +199,6 @@ gemm_e4m3_tc_kernel(const __grid_constant__ CUtensorMap tmW, const E4Params p) {
             if (ok) umma_commit(mma_done);
         }
     } else {
-        // ---------------- activation operand (warps 2-5) ----------------
-        const int ew = warp - 2;              // 0..3, rows 2*ew and 2*ew+1
-        for (int rr = 0; rr < 2; ++rr) {
-            const int m = 2 * ew + rr;
-            const bool live = m < p.M;
-            const uint16_t* arow = p.A + (int64_t)m * p.lda + k0;
-            float amax = 0.0f;
-            if (live)
-                for (int k = lane; k < klen; k += 32) amax = fmaxf(amax, fabsf(bf16_bits_to_f32(arow[k])));
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-            // s = 2^(8 - E) with amax < 2^E: max |a*s| in [128, 256).
-            int e = 0;
-            if (amax > 0.0f) frexpf(amax, &e);
-            e = max(-100, min(100, 8 - e));
-            const float sigma = ldexpf(1.0f, e);
-            if (lane == 0) inv_sigma[m] = ldexpf(1.0f, -e);
-            // Four consecutive k per lane -> one 4-byte store per operand row.
-            for (int kl = lane * 4; kl < nkb_alloc * KB; kl += 128) {
-                float x[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    x[j] = (live && kl + j < klen) ? bf16_bits_to_f32(arow[kl + j]) * sigma : 0.0f;
-                uint32_t hi = f32x2_to_e4m3x2(x[0], x[1]) | (f32x2_to_e4m3x2(x[2], x[3]) << 16);
-                float r[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) r[j] = x[j] - e4m3_byte_to_f32(hi >> (8 * j));
-                uint32_t lo = f32x2_to_e4m3x2(r[0], r[1]) | (f32x2_to_e4m3x2(r[2], r[3]) << 16);
-                const int kb = kl >> 7, w = kl & 127, c = w >> 4, within = w & 15;
-                uint8_t* blk = sAct + kb * kActBlock;
-                const int rh = m, rl = 8 + m;
-                *reinterpret_cast<uint32_t*>(blk + rh * 128 + ((c ^ (rh & 7)) << 4) + within) = hi;
-                *reinterpret_cast<uint32_t*>(blk + rl * 128 + ((c ^ (rl & 7)) << 4) + within) = lo;
-            }
-        }
-        fence_proxy_async_smem();
-        mbar_arrive(act_ready);
-
         // ---------------- epilogue ----------------
         const int q = warp & 3;
         const int nl = q * 32 + lane;          // tile row = output column n0 + nl
@@ -210,7 +212,7 @@ gemm_e4m3_tc_kernel(const __grid_constant__ CUtensorMap tmW, const E4Params p) {
             tmem_ld_wait();
 #pragma unroll
             for (int m = 0; m < 8; ++m)
-                v[m] = (__uint_as_float(r[m]) + __uint_as_float(r[8 + m])) * inv_sigma[m];
+                v[m] = (__uint_as_float(r[m]) + __uint_as_float(r[8 + m])) * p.inv_sigma[m];
         }
         const float sc = (n < p.N) ? p.scale[n] : 0.0f;
         if (p.splits == 1) {
@@ -271,9 +273,8 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-size_t smem_bytes(int stages, int kc) {
-    return 1024 + static_cast<size_t>(stages) * kWStage + static_cast<size_t>(kc / KB) * kActBlock +
-           8 * sizeof(float) + 256;
+size_t smem_bytes(int stages, int /*kc*/) {
+    return 1024 + static_cast<size_t>(stages) * kStage + 256;
 }
 
 }  // namespace
@@ -322,19 +323,42 @@ size_t gemm_e4m3_tc_ws_floats(const GemmArgs& g, const E4m3TcPlan& p) {
     return static_cast<size_t>((g.N + BM - 1) / BM) * p.splits * 8 * BM;
 }
 
+size_t gemm_e4m3_tc_act_bytes(const GemmArgs& g) {
+    const size_t kpad = (static_cast<size_t>(g.K) + KB - 1) / KB * KB;
+    return 16 * kpad + 64;
+}
+
 cudaError_t launch_gemm_e4m3_tc(const GemmArgs& g, const E4m3TcPlan& plan, const float* scale,
-                                float* ws, uint32_t* tickets, uint32_t* err, cudaStream_t s) {
-    if (!gemm_e4m3_tc_supported(g) || plan.kc <= 0 || plan.stages < 2) return cudaErrorInvalidValue;
-    if (plan.splits > 1 && (!ws || !tickets)) return cudaErrorInvalidValue;
-    CUtensorMap tmW;
-    cuuint64_t dims[2] = {static_cast<cuuint64_t>(g.K), static_cast<cuuint64_t>(g.N)};
-    cuuint64_t strides[1] = {static_cast<cuuint64_t>(g.ldb)};
-    cuuint32_t box[2] = {KB, BM};
-    cuuint32_t estr[2] = {1, 1};
-    if (encode_fn()(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(g.B), dims, strides,
-                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+                                float* ws, uint32_t* tickets, void* act_buf, uint32_t* err,
+                                cudaStream_t s) {
+    if (!gemm_e4m3_tc_supported(g) || plan.kc <= 0 || plan.stages < 2 || !act_buf)
         return cudaErrorInvalidValue;
+    if (plan.splits > 1 && (!ws || !tickets)) return cudaErrorInvalidValue;
+    const int kpad = (g.K + KB - 1) / KB * KB;
+    uint8_t* act = static_cast<uint8_t*>(act_buf);
+    float* inv_sigma = reinterpret_cast<float*>(act + 16 * static_cast<size_t>(kpad));
+    if (reinterpret_cast<uintptr_t>(act) % 16) return cudaErrorInvalidValue;
+    CUtensorMap tmW, tmAct;
+    {
+        cuuint64_t dims[2] = {static_cast<cuuint64_t>(g.K), static_cast<cuuint64_t>(g.N)};
+        cuuint64_t strides[1] = {static_cast<cuuint64_t>(g.ldb)};
+        cuuint32_t box[2] = {KB, BM};
+        cuuint32_t estr[2] = {1, 1};
+        if (encode_fn()(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(g.B), dims, strides,
+                        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    {
+        cuuint64_t dims[2] = {static_cast<cuuint64_t>(kpad), 16};
+        cuuint64_t strides[1] = {static_cast<cuuint64_t>(kpad)};
+        cuuint32_t box[2] = {KB, 16};
+        cuuint32_t estr[2] = {1, 1};
+        if (encode_fn()(&tmAct, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, act, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
     static thread_local int attr_dev = -1;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -345,10 +369,24 @@ cudaError_t launch_gemm_e4m3_tc(const GemmArgs& g, const E4m3TcPlan& plan, const
         if (e != cudaSuccess) return e;
         attr_dev = dev;
     }
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(8, 1, 1);
+        cfg.blockDim = dim3(256, 1, 1);
+        cfg.stream = s;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, e4m3_act_prep_kernel, static_cast<const uint16_t*>(g.A),
+                               static_cast<int64_t>(g.lda), g.M, g.K, kpad, act, inv_sigma);
+        if (e != cudaSuccess) return e;
+    }
     E4Params p;
     p.M = g.M; p.N = g.N; p.K = g.K;
     p.kc = plan.kc; p.splits = plan.splits; p.stages = plan.stages;
-    p.A = static_cast<const uint16_t*>(g.A); p.lda = g.lda;
+    p.inv_sigma = inv_sigma;
     p.scale = scale;
     p.C = static_cast<uint16_t*>(g.C); p.ldc = g.ldc;
     p.ws = ws; p.tickets = tickets; p.err = err;
@@ -357,12 +395,9 @@ cudaError_t launch_gemm_e4m3_tc(const GemmArgs& g, const E4m3TcPlan& plan, const
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = smem_bytes(plan.stages, plan.kc);
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemm_e4m3_tc_kernel, tmW, p);
+    return cudaLaunchKernelEx(&cfg, gemm_e4m3_tc_kernel, tmW, tmAct, p);
 }
 
 }  // namespace dnnopt_b200

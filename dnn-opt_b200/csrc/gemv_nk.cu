@@ -282,9 +282,7 @@ gemv_rows_kernel(const RowsParams p) {
     const int row_end = min(g.N, row_begin + p.rows_per_cta);
     const uint4* B = static_cast<const uint4*>(g.B);
     const int64_t ldb_chunks = g.ldb / C::EPC;
-    int buf = 0;
-    for (int r0 = row_begin; r0 < row_end; r0 += R, buf ^= 1) {
-        uint4 b[KCH][R];
+    auto load_rows = [&](uint4 (&b)[KCH][R], int r0) {
 #pragma unroll
         for (int j = 0; j < KCH; ++j) {
             const int ch = tid + j * kThreads;
@@ -293,6 +291,14 @@ gemv_rows_kernel(const RowsParams p) {
                 b[j][r] = (ch < nchunks && r0 + r < row_end) ? __ldg(B + (int64_t)(r0 + r) * ldb_chunks + ch)
                                                             : make_uint4(0u, 0u, 0u, 0u);
         }
+    };
+    // Software pipeline: the next R rows are requested before the current
+    // ones are reduced, so a CTA always has two row groups in flight.
+    uint4 bc[KCH][R], bn[KCH][R];
+    if (row_begin < row_end) load_rows(bc, row_begin);
+    int buf = 0;
+    for (int r0 = row_begin; r0 < row_end; r0 += R, buf ^= 1) {
+        if (r0 + R < row_end) load_rows(bn, r0 + R);
         Acc v[32];
 #pragma unroll
         for (int m = 0; m < MT; ++m)
@@ -300,7 +306,7 @@ gemv_rows_kernel(const RowsParams p) {
             for (int r = 0; r < R; ++r) {
                 Acc acc = Acc(0);
 #pragma unroll
-                for (int j = 0; j < KCH; ++j) acc = C::dot(b[j][r], a[j][m], acc);
+                for (int j = 0; j < KCH; ++j) acc = C::dot(bc[j][r], a[j][m], acc);
                 v[m * R + r] = acc;
             }
         // Transpose-reduce: after the step with offset s, a lane keeps the half
@@ -337,6 +343,10 @@ gemv_rows_kernel(const RowsParams p) {
             }
         }
         // red[buf] is rewritten two iterations later, after the next barrier.
+#pragma unroll
+        for (int j = 0; j < KCH; ++j)
+#pragma unroll
+            for (int r = 0; r < R; ++r) bc[j][r] = bn[j][r];
     }
 }
 
@@ -344,7 +354,7 @@ template <DotKind KIND, int KCH>
 const void* rows_select_mt(int mt) {
     switch (mt) {
         case 1:
-        case 2: return reinterpret_cast<const void*>(&gemv_rows_kernel<KIND, 2, 16, KCH>);
+        case 2:   // rows >= M of A are zero: the MT=4 kernel, R=8 keeps registers down
         case 4: return reinterpret_cast<const void*>(&gemv_rows_kernel<KIND, 4, 8, KCH>);
         case 8: return reinterpret_cast<const void*>(&gemv_rows_kernel<KIND, 8, 4, KCH>);
         default: return nullptr;
@@ -360,7 +370,7 @@ const void* rows_select(DotKind kind, int mt, int kch) {
     }
 }
 
-int rows_r(int mt) { return mt <= 2 ? 16 : (mt == 4 ? 8 : 4); }
+int rows_r(int mt) { return mt <= 4 ? 8 : 4; }
 
 template <DotKind KIND, int MT, bool VEC>
 const void* nk_fn() {

@@ -117,8 +117,13 @@ bool gemm_e4m3_tc_supported(const GemmArgs& g);
 E4m3TcPlan gemm_e4m3_tc_plan(const GemmArgs& g, int num_sms);
 E4m3TcPlan gemm_e4m3_tc_plan_splits(const GemmArgs& g, int splits);
 size_t gemm_e4m3_tc_ws_floats(const GemmArgs& g, const E4m3TcPlan& p);
+// Scratch for the activation operand (hi/lo e4m3 rows + per-row scales).
+size_t gemm_e4m3_tc_act_bytes(const GemmArgs& g);
+// Two launches (activation prep, then the GEMM), both with programmatic
+// dependent launch.
 cudaError_t launch_gemm_e4m3_tc(const GemmArgs& g, const E4m3TcPlan& plan, const float* scale,
-                                float* ws, uint32_t* tickets, uint32_t* err, cudaStream_t s);
+                                float* ws, uint32_t* tickets, void* act_buf, uint32_t* err,
+                                cudaStream_t s);
 
 // err: device word that receives a KernelErrorCode when a bounded wait gives up.
 cudaError_t launch_gemm_bf16_tc(const GemmArgs& g, int num_sms, uint32_t* err, cudaStream_t s);

@@ -421,7 +421,7 @@ def test_cluster_variant_forced(gpu, dn, orc, tmp_path, splits):
 
 
 def test_autotune_roundtrip(gpu, dn, orc, tmp_path):
-    M, N, K = 3, 2039, 1024
+    M, N, K = 3, 2053, 1000     # a shape no other test plans
     A, B, C = ref_uniform(M * K, 42), ref_uniform(K * N, 123), ref_uniform(M * N, 77)
     ref = C.copy()
     orc.gemm_f32(M, N, K, 1.0, A, K, B, N, 0.5, ref, N)
