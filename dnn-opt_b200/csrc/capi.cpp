@@ -230,15 +230,18 @@ Plan get_plan(Kind kind, const GemmArgs& g, DeviceContext* ctx, cudaStream_t s,
     } else if (h.kernel == KernelId::E4m3Tc) {
         GemmArgs g8 = g;
         g8.M = g.M < 8 ? g.M : 8;
-        const int tries[7] = {1, 2, 3, 4, 6, 8, 12};
-        for (int t : tries) {
-            Plan q = h;
-            q.e4 = gemm_e4m3_tc_plan_splits(g8, t);
-            if (q.e4.stages < 2) continue;
-            bool dup = false;
-            for (int i = 0; i < nc; ++i) dup = dup || cands[i].e4.splits == q.e4.splits;
-            if (!dup && nc < 12) cands[nc++] = q;
-        }
+        const int tries[4] = {1, 2, 3, 4};
+        const int depths[3] = {2, 3, 4};
+        for (int t : tries)
+            for (int d : depths) {
+                Plan q = h;
+                q.e4 = gemm_e4m3_tc_plan_splits(g8, t, d);
+                if (q.e4.stages < 2) continue;
+                bool dup = false;
+                for (int i = 0; i < nc; ++i)
+                    dup = dup || (cands[i].e4.splits == q.e4.splits && cands[i].e4.stages == q.e4.stages);
+                if (!dup && nc < 12) cands[nc++] = q;
+            }
     } else {
         const int g0 = h.nk.grid;
         const int tries[3] = {g0, g0 / 2, g0 * 2};

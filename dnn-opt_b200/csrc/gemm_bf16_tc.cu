@@ -8,7 +8,7 @@
 // Shape physics: at N=64, K=256 the GEMM does 43 flop per HBM byte, far below
 // the BF16 ridge (~250 flop/B), so the kernel streams A and C at HBM speed and
 // keeps the tensor cores a few percent busy.  Design:
-//   * persistent CTAs (one per SM) walk 128-row tiles of A;
+//   * persistent CTAs walk 128-row tiles of A;
 //   * warp 0 issues TMA loads of A in 128 x 64 K-blocks (128-byte swizzle)
 //     into an N-stage shared-memory ring (mbarrier full/empty pairs);
 //   * the first ring of A loads is issued before B (K x N) is gathered once
@@ -16,9 +16,9 @@
 //   * warp 1 issues tcgen05.mma (M=128, N=n_pad, K=16) into one of two TMEM
 //     accumulators, so the epilogue of tile t overlaps the MMAs of tile t+1;
 //   * warps 2-5 drain TMEM with tcgen05.ld, apply alpha/beta (the reference
-//     epilogue: beta == 0 ? alpha*acc : fma(alpha, acc, beta*C)), stage the
-//     tile in swizzled shared memory and write it with TMA stores (rows >= M
-//     and columns >= N are clipped by the tensor map).
+//     epilogue: beta == 0 ? alpha*acc : fma(alpha, acc, beta*C)) and store
+//     each thread's row with 16-byte stores;
+//   * two CTAs per SM when B leaves room (a shallow 4-stage ring each).
 // No cluster multicast is used anywhere.
 #include <cuda.h>
 
@@ -38,29 +38,27 @@ constexpr size_t kSmemLimit = 227 * 1024;
 
 struct TcParams {
     int M, N, K;
-    int n_pad, num_kb, num_tiles, stages, nbox;
+    int n_pad, num_kb, num_tiles, stages;
     float alpha, beta;
     const uint16_t* B;
     int64_t ldb;
     int b_trans;
     int b_vec;         // B is K x N with 16-byte aligned rows (vector gather)
-    const float* C;    // read only when beta != 0
+    float* C;
     int64_t ldc;
     uint32_t tmem_cols;
     uint32_t* err;
 };
 
-__global__ void __launch_bounds__(kThreads, 1)
-gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmC,
-                    const TcParams p) {
+__global__ void __launch_bounds__(kThreads, 2)
+gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const TcParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     const int sb_bytes = p.num_kb * p.n_pad * 128;
     uint8_t* sB = base;
     uint8_t* sA = sB + sb_bytes;
-    uint8_t* sC = sA + p.stages * kStageBytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sC + 4 * p.nbox * 4096);
+    uint64_t* full = reinterpret_cast<uint64_t*>(sA + p.stages * kStageBytes);
     uint64_t* empty = full + p.stages;
     uint64_t* tfull = empty + p.stages;
     uint64_t* tempty = tfull + 2;
@@ -90,7 +88,6 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         *abort_flag = 0u;
         fence_mbar_init();
         prefetch_tmap(&tmA);
-        prefetch_tmap(&tmC);
         // The first ring of A loads goes out before B is gathered: every stage
         // starts empty, so these need no wait.
         for (uint32_t i = 0; i < pre; ++i) issue_load(i);
@@ -214,55 +211,54 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         }
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
+        // Each thread owns one output row: 16-column groups come out of TMEM
+        // and go straight to global memory as 16-byte stores (a thread's
+        // consecutive stores complete each 32-byte sector of its row).
         const int q = warp & 3;                      // TMEM lane quadrant of this warp
-        uint8_t* stage = sC + (warp - 2) * p.nbox * 4096;
         uint32_t titer = 0;
         for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x, ++titer) {
             const uint32_t buf = titer & 1u, tph = (titer >> 1) & 1u;
             if (!mbar_wait(&tfull[buf], tph, abort_flag, p.err)) break;
             tc_fence_after();
-            if (lane == 0) tma_store_wait_read<0>();  // staging buffer free again
-            __syncwarp();
             const int row = tile * BM + q * 32 + lane;
+            const bool row_ok = row < p.M;
             const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * p.n_pad;
+            float* crow = p.C + (int64_t)row * p.ldc;
             for (int cg = 0; cg < p.n_pad / 16; ++cg) {
                 uint32_t r[16];
                 tmem_ld_32x32b_x16(t_addr + cg * 16, r);
                 tmem_ld_wait();
-                float v[16];
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    float acc = __uint_as_float(r[j]);
-                    int col = cg * 16 + j;
-                    if (p.beta == 0.0f) {
-                        v[j] = p.alpha * acc;
-                    } else {
-                        float cold = (row < p.M && col < p.N) ? p.C[(int64_t)row * p.ldc + col] : 0.0f;
-                        v[j] = fmaf(p.alpha, acc, p.beta * cold);
-                    }
-                }
+                if (!row_ok) continue;
+                const int c0 = cg * 16;
 #pragma unroll
                 for (int j4 = 0; j4 < 4; ++j4) {
-                    const int col = cg * 16 + j4 * 4;
-                    const int box = col >> 5, chunk = (col & 31) >> 2;
-                    uint8_t* dst = stage + box * 4096 + lane * 128 + ((chunk ^ (lane & 7)) * 16);
-                    *reinterpret_cast<float4*>(dst) =
-                        make_float4(v[j4 * 4], v[j4 * 4 + 1], v[j4 * 4 + 2], v[j4 * 4 + 3]);
+                    const int col = c0 + j4 * 4;
+                    float v[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) v[j] = p.alpha * __uint_as_float(r[j4 * 4 + j]);
+                    if (col + 4 <= p.N) {
+                        float4* dst = reinterpret_cast<float4*>(crow + col);
+                        if (p.beta != 0.0f) {
+                            const float4 old = *dst;
+                            v[0] = fmaf(p.alpha, __uint_as_float(r[j4 * 4 + 0]), p.beta * old.x);
+                            v[1] = fmaf(p.alpha, __uint_as_float(r[j4 * 4 + 1]), p.beta * old.y);
+                            v[2] = fmaf(p.alpha, __uint_as_float(r[j4 * 4 + 2]), p.beta * old.z);
+                            v[3] = fmaf(p.alpha, __uint_as_float(r[j4 * 4 + 3]), p.beta * old.w);
+                        }
+                        *dst = make_float4(v[0], v[1], v[2], v[3]);
+                    } else {
+                        for (int j = 0; j < 4 && col + j < p.N; ++j) {
+                            float o = v[j];
+                            if (p.beta != 0.0f) o = fmaf(p.alpha, __uint_as_float(r[j4 * 4 + j]), p.beta * crow[col + j]);
+                            crow[col + j] = o;
+                        }
+                    }
                 }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[buf]);  // TMEM buffer may be overwritten
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-                for (int box = 0; box < p.nbox; ++box)
-                    tma_store_2d(&tmC, stage + box * 4096, box * 32, tile * BM + q * 32);
-                tma_store_commit();
-            }
         }
-        if (lane == 0) tma_store_wait_all<0>();
-        __syncwarp();
     }
 
     tc_fence_before();
@@ -293,20 +289,28 @@ EncodeTiledFn get_encode_fn() {
 }
 
 struct Layout {
-    int n_pad, num_kb, nbox, stages;
+    int n_pad, num_kb, stages, ctas_per_sm;
     size_t smem;
 };
 
+// Measured on B200: two CTAs per SM with a 4-stage ring stream A faster than
+// one CTA with a deep ring.  Fall back to one CTA per SM (up to 8 stages)
+// when B does not leave room for two.
 Layout plan_layout(const GemmArgs& g) {
     Layout L;
     L.n_pad = (g.N + 15) / 16 * 16;
     L.num_kb = (g.K + kKBlock - 1) / kKBlock;
-    L.nbox = (L.n_pad + 31) / 32;
-    const size_t fixed = 1024 + static_cast<size_t>(L.num_kb) * L.n_pad * 128 +
-                         static_cast<size_t>(4) * L.nbox * 4096 + 256;
-    int st = 0;
-    if (fixed < kSmemLimit) st = static_cast<int>((kSmemLimit - fixed) / kStageBytes);
-    L.stages = st > kMaxStages ? kMaxStages : st;
+    const size_t fixed = 1024 + static_cast<size_t>(L.num_kb) * L.n_pad * 128 + 256;
+    const size_t half = kSmemLimit / 2 - 1024;
+    int st2 = fixed < half ? static_cast<int>((half - fixed) / kStageBytes) : 0;
+    if (st2 >= 3) {
+        L.stages = st2 > 4 ? 4 : st2;
+        L.ctas_per_sm = 2;
+    } else {
+        int st = fixed < kSmemLimit ? static_cast<int>((kSmemLimit - fixed) / kStageBytes) : 0;
+        L.stages = st > kMaxStages ? kMaxStages : st;
+        L.ctas_per_sm = 1;
+    }
     L.smem = fixed + static_cast<size_t>(L.stages) * kStageBytes;
     return L;
 }
@@ -326,7 +330,7 @@ cudaError_t launch_gemm_bf16_tc(const GemmArgs& g, int num_sms, uint32_t* err, c
     const Layout L = plan_layout(g);
     EncodeTiledFn encode = get_encode_fn();
 
-    CUtensorMap tmA, tmC;
+    CUtensorMap tmA;
     {
         cuuint64_t dims[2] = {static_cast<cuuint64_t>(g.K), static_cast<cuuint64_t>(g.M)};
         cuuint64_t strides[1] = {static_cast<cuuint64_t>(g.lda) * 2};
@@ -337,25 +341,15 @@ cudaError_t launch_gemm_bf16_tc(const GemmArgs& g, int num_sms, uint32_t* err, c
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return cudaErrorInvalidValue;
     }
-    {
-        cuuint64_t dims[2] = {static_cast<cuuint64_t>(g.N), static_cast<cuuint64_t>(g.M)};
-        cuuint64_t strides[1] = {static_cast<cuuint64_t>(g.ldc) * 4};
-        cuuint32_t box[2] = {32, 32};
-        cuuint32_t estr[2] = {1, 1};
-        if (encode(&tmC, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, g.C, dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return cudaErrorInvalidValue;
-    }
 
     TcParams p;
     p.M = g.M; p.N = g.N; p.K = g.K;
-    p.n_pad = L.n_pad; p.num_kb = L.num_kb; p.nbox = L.nbox; p.stages = L.stages;
+    p.n_pad = L.n_pad; p.num_kb = L.num_kb; p.stages = L.stages;
     p.num_tiles = (g.M + BM - 1) / BM;
     p.alpha = g.alpha; p.beta = g.beta;
     p.B = static_cast<const uint16_t*>(g.B); p.ldb = g.ldb; p.b_trans = g.b_trans;
     p.b_vec = (!g.b_trans && reinterpret_cast<uintptr_t>(g.B) % 16 == 0 && g.ldb % 8 == 0) ? 1 : 0;
-    p.C = static_cast<const float*>(g.C); p.ldc = g.ldc;
+    p.C = static_cast<float*>(g.C); p.ldc = g.ldc;
     uint32_t cols = 32;
     while (cols < static_cast<uint32_t>(2 * L.n_pad)) cols <<= 1;
     p.tmem_cols = cols;
@@ -375,8 +369,9 @@ cudaError_t launch_gemm_bf16_tc(const GemmArgs& g, int num_sms, uint32_t* err, c
         smem_set_dev = dev;
         smem_set = kSmemLimit;
     }
-    int grid = p.num_tiles < num_sms ? p.num_tiles : num_sms;
-    gemm_bf16_tc_kernel<<<grid, kThreads, L.smem, s>>>(tmA, tmC, p);
+    const int slots = num_sms * L.ctas_per_sm;
+    int grid = p.num_tiles < slots ? p.num_tiles : slots;
+    gemm_bf16_tc_kernel<<<grid, kThreads, L.smem, s>>>(tmA, p);
     return cudaGetLastError();
 }
 

@@ -35,7 +35,6 @@ constexpr int kWStage = BM * KB;        // 16 KB of weights per K-block
 constexpr int kActBlock = 16 * KB;      // 16 activation rows x 128 B per K-block
 constexpr int kStage = kWStage + kActBlock;
 constexpr int kThreads = 192;
-constexpr int kMaxStages = 8;
 constexpr int kMaxKc = 4096;            // K elements per CTA (activation operand 64 KB)
 constexpr size_t kSmemLimit = 227 * 1024;
 
@@ -119,7 +118,7 @@ e4m3_act_prep_kernel(const uint16_t* __restrict__ A, int64_t lda, int M, int K, 
     }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 4)
 gemm_e4m3_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmAct,
                     const E4Params p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -285,37 +284,27 @@ bool gemm_e4m3_tc_supported(const GemmArgs& g) {
     return encode_fn() != nullptr;
 }
 
-E4m3TcPlan gemm_e4m3_tc_plan_splits(const GemmArgs& g, int splits) {
+E4m3TcPlan gemm_e4m3_tc_plan_splits(const GemmArgs& g, int splits, int stages) {
     E4m3TcPlan p{1, 0, 0};
     if (splits < 1) splits = 1;
     int kc = ((g.K + splits - 1) / splits + KB - 1) / KB * KB;
     if (kc > kMaxKc) kc = kMaxKc;
     p.kc = kc;
     p.splits = (g.K + kc - 1) / kc;
-    int st = kMaxStages;
+    int st = stages < 2 ? 2 : stages;
     while (st > 2 && smem_bytes(st, kc) > kSmemLimit) --st;
     p.stages = smem_bytes(st, kc) <= kSmemLimit ? st : 0;
     return p;
 }
 
 E4m3TcPlan gemm_e4m3_tc_plan(const GemmArgs& g, int num_sms) {
-    // Few long-lived CTAs: at most 4 K-ranges per tile, chosen for the most
-    // even wave count (each CTA has a fixed set-up cost: barriers, TMEM,
-    // building the activation operand, the split reduction).
+    // Measured on B200: several CTAs per SM with a shallow ring (3 stages,
+    // 56 KB -> 4 CTAs per SM) stream the weights faster than one CTA with a
+    // deep ring, so split K until every SM holds at least two CTAs, no more.
     const int tiles = (g.N + BM - 1) / BM;
-    E4m3TcPlan best = gemm_e4m3_tc_plan_splits(g, 1);
-    double best_balance = -1.0;
-    for (int s = 1; s <= 4; ++s) {
-        E4m3TcPlan p = gemm_e4m3_tc_plan_splits(g, s);
-        if (p.stages < 2) continue;
-        const double waves = static_cast<double>(tiles) * p.splits / num_sms;
-        const double balance = waves / static_cast<double>(static_cast<long long>(waves + 0.999999));
-        if (balance > best_balance + 0.05) {
-            best_balance = balance;
-            best = p;
-        }
-    }
-    return best;
+    int s = (2 * num_sms + tiles - 1) / tiles;
+    if (s < 1) s = 1;
+    return gemm_e4m3_tc_plan_splits(g, s, 3);
 }
 
 size_t gemm_e4m3_tc_ws_floats(const GemmArgs& g, const E4m3TcPlan& p) {

@@ -115,7 +115,7 @@ struct E4m3TcPlan {
 };
 bool gemm_e4m3_tc_supported(const GemmArgs& g);
 E4m3TcPlan gemm_e4m3_tc_plan(const GemmArgs& g, int num_sms);
-E4m3TcPlan gemm_e4m3_tc_plan_splits(const GemmArgs& g, int splits);
+E4m3TcPlan gemm_e4m3_tc_plan_splits(const GemmArgs& g, int splits, int stages);
 size_t gemm_e4m3_tc_ws_floats(const GemmArgs& g, const E4m3TcPlan& p);
 // Scratch for the activation operand (hi/lo e4m3 rows + per-row scales).
 size_t gemm_e4m3_tc_act_bytes(const GemmArgs& g);
