@@ -8,17 +8,23 @@
 // Shape physics: at N=64, K=256 the GEMM does 43 flop per HBM byte, far below
 // the BF16 ridge (~250 flop/B), so the kernel streams A and C at HBM speed and
 // keeps the tensor cores a few percent busy.  Design:
-//   * persistent CTAs walk 128-row tiles of A;
-//   * warp 0 issues TMA loads of A in 128 x 64 K-blocks (128-byte swizzle)
-//     into an N-stage shared-memory ring (mbarrier full/empty pairs);
-//   * the first ring of A loads is issued before B (K x N) is gathered once
-//     per CTA into the same K-major swizzled layout (16-byte row loads);
-//   * warp 1 issues tcgen05.mma (M=128, N=n_pad, K=16) into one of two TMEM
+//   * persistent CTAs walk 128-row tiles of A; two CTAs per SM when shared
+//     memory and TMEM allow (a shallow ring each: measured faster than one CTA
+//     with a deep ring);
+//   * one thread issues every TMA load: B once per CTA, straight into the UMMA
+//     operand layout (MN-major 128-byte swizzle when B is K x N, K-major when B
+//     is N x K; an element gather only when B's rows are not 16-byte aligned),
+//     then A in 128 x 64 K-blocks into the shared-memory ring (mbarrier
+//     full/empty pairs);
+//   * warp 1 issues tcgen05.mma (M=128, N=n_mma, K=16) into one of two TMEM
 //     accumulators, so the epilogue of tile t overlaps the MMAs of tile t+1;
 //   * warps 2-5 drain TMEM with tcgen05.ld, apply alpha/beta (the reference
-//     epilogue: beta == 0 ? alpha*acc : fma(alpha, acc, beta*C)) and store
-//     each thread's row with 16-byte stores;
-//   * two CTAs per SM when B leaves room (a shallow 4-stage ring each).
+//     epilogue: beta == 0 ? alpha*acc : fma(alpha, acc, beta*C)), stage 32 x 32
+//     float blocks in 128-byte-swizzled shared memory and write them with TMA
+//     stores (rows >= M and columns >= N are clipped by the tensor map);
+//   * programmatic dependent launch: the prologue (barrier init, TMEM
+//     allocation, descriptor prefetch) overlaps the previous kernel's tail and
+//     every global access waits for it (griddepcontrol.wait).
 // No cluster multicast is used anywhere.
 #include <cuda.h>
 
@@ -34,35 +40,60 @@ constexpr int kKBlock = 64;            // bf16 elements per 128-byte swizzle row
 constexpr int kStageBytes = BM * 128;  // one A K-block
 constexpr int kThreads = 192;
 constexpr int kMaxStages = 8;
+constexpr int kStageCBytes = 32 * 128;           // one 32 x 32 FP32 store block
+constexpr int kCStagingBytes = 4 * 2 * kStageCBytes;  // 4 warps x 2 buffers
 constexpr size_t kSmemLimit = 227 * 1024;
+constexpr size_t kSmemPerSm = 228 * 1024;        // per SM, 1 KB of it reserved per CTA
+
+enum BMode : int {
+    kBGather = 0,    // element gather into the K-major swizzled layout
+    kBTmaMN = 1,     // B is K x N: TMA boxes of 64 n x 64 k, MN-major operand
+    kBTmaK = 2,      // B is N x K: TMA boxes of 64 k x n_mma rows, K-major operand
+};
 
 struct TcParams {
     int M, N, K;
-    int n_pad, num_kb, num_tiles, stages;
+    int n_mma, num_kb, kpad, n_chunks, num_tiles, stages, b_mode;
+    uint32_t sb_bytes;
     float alpha, beta;
     const uint16_t* B;
     int64_t ldb;
     int b_trans;
-    int b_vec;         // B is K x N with 16-byte aligned rows (vector gather)
-    float* C;
+    const float* C;     // read for beta != 0
     int64_t ldc;
     uint32_t tmem_cols;
     uint32_t* err;
 };
 
-__global__ void __launch_bounds__(kThreads, 2)
-gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const TcParams p) {
+// Shared-memory descriptor of an MN-major operand in the canonical 128-byte
+// swizzled layout: 64 elements along N per 128-byte row, eight K rows per
+// 1024-byte atom, atoms of one 64-column chunk stacked densely along K (SBO =
+// 1024 B) and chunks `lbo` bytes apart (LBO).
+__device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t smem_addr, uint32_t lbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>(1024u >> 4) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    d |= static_cast<uint64_t>(2u) << 61;
+    return d;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmC, const TcParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    const int sb_bytes = p.num_kb * p.n_pad * 128;
     uint8_t* sB = base;
-    uint8_t* sA = sB + sb_bytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sA + p.stages * kStageBytes);
+    uint8_t* sA = sB + p.sb_bytes;
+    uint8_t* sC = sA + p.stages * kStageBytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sC + kCStagingBytes);
     uint64_t* empty = full + p.stages;
     uint64_t* tfull = empty + p.stages;
     uint64_t* tempty = tfull + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    uint64_t* bfull = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bfull + 1);
     volatile uint32_t* abort_flag = tmem_slot + 1;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -85,69 +116,40 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const TcParams p) {
     if (tid == 0) {
         for (int s = 0; s < p.stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         for (int b = 0; b < 2; ++b) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], 4); }
+        mbar_init(bfull, 1);
         *abort_flag = 0u;
         fence_mbar_init();
         prefetch_tmap(&tmA);
-        // The first ring of A loads goes out before B is gathered: every stage
-        // starts empty, so these need no wait.
-        for (uint32_t i = 0; i < pre; ++i) issue_load(i);
+        prefetch_tmap(&tmC);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, p.tmem_cols);
         tmem_relinquish();
     }
-
-    // Gather B into K-major 128B-swizzled rows (the UMMA B operand):
-    // byte offset of (n, k) = kb*n_pad*128 + n*128 + ((c ^ (n&7))*16) + (k%8)*2,
-    // kb = k/64, c = (k%64)/8.
-    if (p.b_vec) {
-        // B is K x N with 16-byte aligned rows: one 16-byte load brings 8
-        // consecutive n of row k; consecutive threads take consecutive k so
-        // the 2-byte shared stores of a warp fall in distinct banks.  Loads
-        // are issued in groups of kGather before any store so that a thread
-        // has kGather requests in flight instead of one.
-        constexpr int kGather = 8;
-        const int kpad = p.num_kb * kKBlock;
-        const int n8s = p.n_pad / 8;
-        const int total = kpad * n8s;
-        for (int base_idx = tid; base_idx < total; base_idx += kThreads * kGather) {
-            uint4 v[kGather];
-#pragma unroll
-            for (int j = 0; j < kGather; ++j) {
-                const int idx = base_idx + j * kThreads;
-                const int k = idx % kpad, n8 = idx / kpad;
-                v[j] = make_uint4(0u, 0u, 0u, 0u);
-                if (idx < total && k < p.K) {
-                    if (n8 * 8 + 8 <= p.N) {
-                        v[j] = __ldg(reinterpret_cast<const uint4*>(p.B + (int64_t)k * p.ldb + n8 * 8));
-                    } else {
-                        uint32_t w[4] = {0u, 0u, 0u, 0u};
-                        for (int e = 0; e < 8 && n8 * 8 + e < p.N; ++e)
-                            w[e >> 1] |= static_cast<uint32_t>(p.B[(int64_t)k * p.ldb + n8 * 8 + e]) << ((e & 1) * 16);
-                        v[j] = make_uint4(w[0], w[1], w[2], w[3]);
-                    }
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < kGather; ++j) {
-                const int idx = base_idx + j * kThreads;
-                if (idx >= total) break;
-                const int k = idx % kpad, n8 = idx / kpad;
-                const uint32_t w4[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-                const int kb = k >> 6, c = (k & 63) >> 3;
-                uint8_t* base_kb = sB + kb * p.n_pad * 128 + (k & 7) * 2;
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const int n = n8 * 8 + e;
-                    const uint16_t val = static_cast<uint16_t>(w4[e >> 1] >> ((e & 1) * 16));
-                    *reinterpret_cast<uint16_t*>(base_kb + n * 128 + ((c ^ (n & 7)) * 16)) = val;
-                }
-            }
+    pdl_wait();   // inputs and C may be written by the preceding kernel
+    if (tid == 0) {
+        // B first (the first MMA needs all of it), then the first ring of A:
+        // every stage starts empty, so these loads need no wait.
+        if (p.b_mode == kBTmaMN) {
+            mbar_arrive_expect_tx(bfull, p.sb_bytes);
+            for (int j = 0; j < p.n_chunks; ++j)
+                for (int kb = 0; kb < p.num_kb; ++kb)
+                    tma_load_2d(sB + (j * p.kpad + kb * kKBlock) * 128, &tmB, bfull, j * 64, kb * kKBlock);
+        } else if (p.b_mode == kBTmaK) {
+            mbar_arrive_expect_tx(bfull, p.sb_bytes);
+            for (int kb = 0; kb < p.num_kb; ++kb)
+                tma_load_2d(sB + kb * p.n_mma * 128, &tmB, bfull, kb * kKBlock, 0);
         }
-    } else {
-        const int total = p.num_kb * 8 * p.n_pad;
+        for (uint32_t i = 0; i < pre; ++i) issue_load(i);
+    }
+
+    if (p.b_mode == kBGather) {
+        // B rows are not 16-byte aligned: gather element pairs into the
+        // K-major 128B-swizzled layout, byte offset of (n, k) =
+        // kb*n_mma*128 + n*128 + ((c ^ (n&7))*16) + (k%8)*2, kb = k/64, c = (k%64)/8.
+        const int total = p.num_kb * 8 * p.n_mma;
         for (int idx = tid; idx < total; idx += kThreads) {
-            const int n = idx % p.n_pad, rest = idx / p.n_pad;
+            const int n = idx % p.n_mma, rest = idx / p.n_mma;
             const int c = rest & 7, kb = rest >> 3;
             const int k0 = kb * kKBlock + c * 8;
             uint32_t w[4];
@@ -161,15 +163,18 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const TcParams p) {
                 }
                 w[e >> 1] = lo | (hi << 16);
             }
-            uint8_t* dst = sB + kb * p.n_pad * 128 + n * 128 + ((c ^ (n & 7)) * 16);
+            uint8_t* dst = sB + kb * p.n_mma * 128 + n * 128 + ((c ^ (n & 7)) * 16);
             *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
         }
+        fence_proxy_async_smem();
     }
-    fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Dependent kernels may start once every CTA holds its TMEM: one that
+    // allocated first could otherwise leave this grid waiting on it.
+    pdl_launch_dependents();
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
@@ -183,24 +188,31 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const TcParams p) {
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            const uint32_t idesc = umma_idesc_bf16_f32(BM, p.n_pad);
+            uint32_t idesc = umma_idesc_bf16_f32(BM, p.n_mma);
+            if (p.b_mode == kBTmaMN) idesc |= 1u << 16;          // B operand MN-major
+            const uint32_t sb_addr = smem_u32(sB);
+            const uint32_t lbo = static_cast<uint32_t>(p.kpad) * 128u;
+            bool ok = p.b_mode == kBGather || mbar_wait(bfull, 0, abort_flag, p.err);
             uint32_t it = 0, titer = 0;
-            for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x, ++titer) {
+            for (int tile = blockIdx.x; ok && tile < p.num_tiles && !*abort_flag; tile += gridDim.x, ++titer) {
                 const uint32_t buf = titer & 1u, tph = (titer >> 1) & 1u;
                 if (!mbar_wait(&tempty[buf], tph ^ 1u, abort_flag, p.err)) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + buf * p.n_pad;
-                bool ok = true;
+                const uint32_t d_tmem = tmem_base + buf * p.n_mma;
                 for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
                     const uint32_t s = it % p.stages, ph = (it / p.stages) & 1u;
                     if (!mbar_wait(&full[s], ph, abort_flag, p.err)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(sA + s * kStageBytes);
-                    const uint32_t b_addr = smem_u32(sB + kb * p.n_pad * 128);
 #pragma unroll
                     for (int kk = 0; kk < kKBlock / 16; ++kk) {
-                        umma_f16_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32),
-                                    umma_desc_k_sw128(b_addr + kk * 32), idesc,
+                        // K step of 16: 32 bytes along a K-major row, or two
+                        // 1024-byte 8-row atoms down an MN-major chunk.
+                        const uint64_t bdesc =
+                            p.b_mode == kBTmaMN
+                                ? umma_desc_mn_sw128(sb_addr + (kb * 8 + kk * 2) * 1024, lbo)
+                                : umma_desc_k_sw128(sb_addr + kb * p.n_mma * 128 + kk * 32);
+                        umma_f16_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32), bdesc, idesc,
                                     (kb | kk) != 0 ? 1u : 0u);
                     }
                     umma_commit(&empty[s]);   // stage is free once these MMAs retire
@@ -211,54 +223,73 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const TcParams p) {
         }
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
-        // Each thread owns one output row: 16-column groups come out of TMEM
-        // and go straight to global memory as 16-byte stores (a thread's
-        // consecutive stores complete each 32-byte sector of its row).
-        const int q = warp & 3;                      // TMEM lane quadrant of this warp
-        uint32_t titer = 0;
+        // Warp q owns TMEM lanes / tile rows [32q, 32q+32).  Columns go out in
+        // 32-wide groups through two 4 KB staging buffers per warp: lane l
+        // writes row l as eight 16-byte chunks at ((c ^ (l&7))*16), the
+        // 128-byte swizzle the C tensor map uses, so a warp's shared stores
+        // are conflict-free; lane 0 then issues one TMA store per group.
+        const int q = warp & 3;
+        uint8_t* stg = sC + q * 2 * kStageCBytes;
+        const int n_groups = (p.N + 31) / 32;
+        uint32_t titer = 0, gcount = 0;
         for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x, ++titer) {
             const uint32_t buf = titer & 1u, tph = (titer >> 1) & 1u;
             if (!mbar_wait(&tfull[buf], tph, abort_flag, p.err)) break;
             tc_fence_after();
             const int row = tile * BM + q * 32 + lane;
-            const bool row_ok = row < p.M;
-            const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * p.n_pad;
-            float* crow = p.C + (int64_t)row * p.ldc;
-            for (int cg = 0; cg < p.n_pad / 16; ++cg) {
-                uint32_t r[16];
-                tmem_ld_32x32b_x16(t_addr + cg * 16, r);
-                tmem_ld_wait();
-                if (!row_ok) continue;
-                const int c0 = cg * 16;
+            const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * p.n_mma;
+            for (int g0 = 0; g0 < n_groups; g0 += 2) {
+                uint32_t r[2][32];
+                const int ng = n_groups - g0 < 2 ? n_groups - g0 : 2;
 #pragma unroll
-                for (int j4 = 0; j4 < 4; ++j4) {
-                    const int col = c0 + j4 * 4;
-                    float v[4];
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) v[j] = p.alpha * __uint_as_float(r[j4 * 4 + j]);
-                    if (col + 4 <= p.N) {
-                        float4* dst = reinterpret_cast<float4*>(crow + col);
-                        if (p.beta != 0.0f) {
-                            const float4 old = *dst;
-                            v[0] = fmaf(p.alpha, __uint_as_float(r[j4 * 4 + 0]), p.beta * old.x);
-                            v[1] = fmaf(p.alpha, __uint_as_float(r[j4 * 4 + 1]), p.beta * old.y);
-                            v[2] = fmaf(p.alpha, __uint_as_float(r[j4 * 4 + 2]), p.beta * old.z);
-                            v[3] = fmaf(p.alpha, __uint_as_float(r[j4 * 4 + 3]), p.beta * old.w);
-                        }
-                        *dst = make_float4(v[0], v[1], v[2], v[3]);
-                    } else {
-                        for (int j = 0; j < 4 && col + j < p.N; ++j) {
-                            float o = v[j];
-                            if (p.beta != 0.0f) o = fmaf(p.alpha, __uint_as_float(r[j4 * 4 + j]), p.beta * crow[col + j]);
-                            crow[col + j] = o;
-                        }
+                for (int h = 0; h < 2; ++h) {
+                    if (h < ng) {
+                        tmem_ld_32x32b_x16(t_addr + (g0 + h) * 32, *reinterpret_cast<uint32_t(*)[16]>(&r[h][0]));
+                        tmem_ld_32x32b_x16(t_addr + (g0 + h) * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[h][16]));
                     }
                 }
+                tmem_ld_wait();
+                if (g0 + 2 >= n_groups) {
+                    // Every column of this tile is in registers: release the
+                    // accumulator so the next tile's MMAs can start.
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[buf]);
+                }
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    if (h >= ng) break;
+                    const int col0 = (g0 + h) * 32;
+                    uint8_t* sbuf = stg + (gcount & 1u) * kStageCBytes;
+                    if (lane == 0) tma_store_wait_read<1>();   // this buffer's previous store has read it
+                    __syncwarp();
+                    const float* crow = p.C + (int64_t)row * p.ldc;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        float v[4];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) v[j] = p.alpha * __uint_as_float(r[h][c * 4 + j]);
+                        if (p.beta != 0.0f && row < p.M) {
+                            const int col = col0 + c * 4;
+#pragma unroll
+                            for (int j = 0; j < 4; ++j)
+                                if (col + j < p.N)
+                                    v[j] = fmaf(p.alpha, __uint_as_float(r[h][c * 4 + j]), p.beta * crow[col + j]);
+                        }
+                        *reinterpret_cast<float4*>(sbuf + lane * 128 + ((c ^ (lane & 7)) * 16)) =
+                            make_float4(v[0], v[1], v[2], v[3]);
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmC, sbuf, col0, tile * BM + q * 32);
+                        tma_store_commit();
+                    }
+                    ++gcount;
+                }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[buf]);  // TMEM buffer may be overwritten
         }
+        if (lane == 0) tma_store_wait_all<0>();   // staging must outlive the stores' reads
     }
 
     tc_fence_before();
@@ -289,30 +320,58 @@ EncodeTiledFn get_encode_fn() {
 }
 
 struct Layout {
-    int n_pad, num_kb, stages, ctas_per_sm;
+    int b_mode, n_mma, num_kb, kpad, n_chunks, stages, ctas_per_sm;
+    uint32_t sb_bytes, tmem_cols;
     size_t smem;
 };
 
-// Measured on B200: two CTAs per SM with a 4-stage ring stream A faster than
-// one CTA with a deep ring.  Fall back to one CTA per SM (up to 8 stages)
-// when B does not leave room for two.
+// B operand mode, shared-memory plan and CTAs per SM.  Measured on B200: two
+// CTAs per SM with a 2-4 stage ring stream A faster than one CTA with a deep
+// ring; one CTA per SM (up to 8 stages) when B or TMEM leaves no room for two.
 Layout plan_layout(const GemmArgs& g) {
     Layout L;
-    L.n_pad = (g.N + 15) / 16 * 16;
+    const bool b_aligned = reinterpret_cast<uintptr_t>(g.B) % 16 == 0 && g.ldb % 8 == 0;
     L.num_kb = (g.K + kKBlock - 1) / kKBlock;
-    const size_t fixed = 1024 + static_cast<size_t>(L.num_kb) * L.n_pad * 128 + 256;
-    const size_t half = kSmemLimit / 2 - 1024;
-    int st2 = fixed < half ? static_cast<int>((half - fixed) / kStageBytes) : 0;
-    if (st2 >= 3) {
+    L.kpad = L.num_kb * kKBlock;
+    if (b_aligned && !g.b_trans && L.kpad * 128 < (1 << 18)) {
+        L.b_mode = kBTmaMN;
+        L.n_mma = (g.N + 63) / 64 * 64;
+        L.n_chunks = L.n_mma / 64;
+        L.sb_bytes = static_cast<uint32_t>(L.n_chunks * L.kpad * 128);
+    } else {
+        L.b_mode = b_aligned && g.b_trans ? kBTmaK : kBGather;
+        L.n_mma = (g.N + 15) / 16 * 16;
+        L.n_chunks = 0;
+        L.sb_bytes = static_cast<uint32_t>(L.num_kb * L.n_mma * 128);
+    }
+    uint32_t cols = 32;
+    while (cols < static_cast<uint32_t>(2 * L.n_mma)) cols <<= 1;
+    L.tmem_cols = cols;
+    const size_t fixed = 1024 + static_cast<size_t>(L.sb_bytes) + kCStagingBytes + 256;
+    const size_t per_cta2 = kSmemPerSm / 2 - 1024;
+    const int st2 = fixed < per_cta2 ? static_cast<int>((per_cta2 - fixed) / kStageBytes) : 0;
+    if (st2 >= 2 && 2 * L.tmem_cols <= 512) {
         L.stages = st2 > 4 ? 4 : st2;
         L.ctas_per_sm = 2;
     } else {
-        int st = fixed < kSmemLimit ? static_cast<int>((kSmemLimit - fixed) / kStageBytes) : 0;
+        const int st = fixed < kSmemLimit ? static_cast<int>((kSmemLimit - fixed) / kStageBytes) : 0;
         L.stages = st > kMaxStages ? kMaxStages : st;
         L.ctas_per_sm = 1;
     }
     L.smem = fixed + static_cast<size_t>(L.stages) * kStageBytes;
     return L;
+}
+
+bool encode_2d(CUtensorMap* m, CUtensorMapDataType t, const void* ptr, uint64_t d0, uint64_t d1,
+               uint64_t row_bytes, uint32_t b0, uint32_t b1) {
+    cuuint64_t dims[2] = {d0, d1};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {b0, b1};
+    cuuint32_t estr[2] = {1, 1};
+    return get_encode_fn()(m, t, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
@@ -328,51 +387,63 @@ bool gemm_bf16_tc_supported(const GemmArgs& g) {
 cudaError_t launch_gemm_bf16_tc(const GemmArgs& g, int num_sms, uint32_t* err, cudaStream_t s) {
     if (!gemm_bf16_tc_supported(g)) return cudaErrorInvalidValue;
     const Layout L = plan_layout(g);
-    EncodeTiledFn encode = get_encode_fn();
 
-    CUtensorMap tmA;
-    {
-        cuuint64_t dims[2] = {static_cast<cuuint64_t>(g.K), static_cast<cuuint64_t>(g.M)};
-        cuuint64_t strides[1] = {static_cast<cuuint64_t>(g.lda) * 2};
-        cuuint32_t box[2] = {kKBlock, BM};
-        cuuint32_t estr[2] = {1, 1};
-        if (encode(&tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(g.A), dims, strides,
-                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    // Inner dimension first; every row stride is a multiple of 16 bytes and
+    // every box's inner extent is 128 bytes (the swizzle span).
+    CUtensorMap tmA, tmB, tmC;
+    if (!encode_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, g.A, g.K, g.M,
+                   static_cast<uint64_t>(g.lda) * 2, kKBlock, BM))
+        return cudaErrorInvalidValue;
+    if (!encode_2d(&tmC, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, g.C, g.N, g.M,
+                   static_cast<uint64_t>(g.ldc) * 4, 32, 32))
+        return cudaErrorInvalidValue;
+    if (L.b_mode == kBTmaMN) {
+        if (!encode_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, g.B, g.N, g.K,
+                       static_cast<uint64_t>(g.ldb) * 2, 64, kKBlock))
             return cudaErrorInvalidValue;
+    } else if (L.b_mode == kBTmaK) {
+        if (!encode_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, g.B, g.K, g.N,
+                       static_cast<uint64_t>(g.ldb) * 2, kKBlock, static_cast<uint32_t>(L.n_mma)))
+            return cudaErrorInvalidValue;
+    } else {
+        tmB = tmA;   // unused
     }
 
     TcParams p;
     p.M = g.M; p.N = g.N; p.K = g.K;
-    p.n_pad = L.n_pad; p.num_kb = L.num_kb; p.stages = L.stages;
+    p.n_mma = L.n_mma; p.num_kb = L.num_kb; p.kpad = L.kpad; p.n_chunks = L.n_chunks;
     p.num_tiles = (g.M + BM - 1) / BM;
+    p.stages = L.stages; p.b_mode = L.b_mode; p.sb_bytes = L.sb_bytes;
     p.alpha = g.alpha; p.beta = g.beta;
     p.B = static_cast<const uint16_t*>(g.B); p.ldb = g.ldb; p.b_trans = g.b_trans;
-    p.b_vec = (!g.b_trans && reinterpret_cast<uintptr_t>(g.B) % 16 == 0 && g.ldb % 8 == 0) ? 1 : 0;
-    p.C = static_cast<float*>(g.C); p.ldc = g.ldc;
-    uint32_t cols = 32;
-    while (cols < static_cast<uint32_t>(2 * L.n_pad)) cols <<= 1;
-    p.tmem_cols = cols;
+    p.C = static_cast<const float*>(g.C); p.ldc = g.ldc;
+    p.tmem_cols = L.tmem_cols;
     p.err = err;
 
-    // The attribute is per device; set it once to the largest size requested
-    // so that launches under stream capture make no further attribute calls.
+    // The attribute is per device; set it once so that launches under stream
+    // capture make no further attribute calls.
     static thread_local int smem_set_dev = -1;
-    static thread_local size_t smem_set = 0;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    if (dev != smem_set_dev || L.smem > smem_set) {
+    if (dev != smem_set_dev) {
         e = cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(kSmemLimit));
         if (e != cudaSuccess) return e;
         smem_set_dev = dev;
-        smem_set = kSmemLimit;
     }
     const int slots = num_sms * L.ctas_per_sm;
-    int grid = p.num_tiles < slots ? p.num_tiles : slots;
-    gemm_bf16_tc_kernel<<<grid, kThreads, L.smem, s>>>(tmA, p);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(p.num_tiles < slots ? p.num_tiles : slots));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = L.smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_bf16_tc_kernel, tmA, tmB, tmC, p);
 }
 
 }  // namespace dnnopt_b200

@@ -141,7 +141,6 @@ gemm_e4m3_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     pdl_wait();          // the activation operand comes from the prep kernel
-    pdl_launch_dependents();
 
     auto issue = [&](int kb, int s) {
         mbar_arrive_expect_tx(&full[s], kStage);
@@ -166,6 +165,9 @@ gemm_e4m3_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Dependent kernels may start once every CTA holds its TMEM: one that
+    // allocated first could otherwise leave this grid waiting on it.
+    pdl_launch_dependents();
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------

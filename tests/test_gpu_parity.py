@@ -270,7 +270,9 @@ def test_int8_fp32_api_bitexact(gpu, dn, orc, shape):
 
 
 # ------------------------------------------------------------------ BF16 ----
-def _bf16_case(dn, orc, torch, M, N, K, alpha=1.0, beta=0.0, ldc=None, seed=42):
+def _bf16_case(dn, orc, torch, M, N, K, alpha=1.0, beta=0.0, ldc=None, seed=42, b_layout="kn"):
+    """b_layout: "kn" (B is K x N, ldb = N), "nk" (B is N x K, trans_b, ldb = K),
+    "kn_pad1" (K x N with ldb = N + 1: rows not 16-byte aligned)."""
     ldc = ldc or N
     A32 = np.random.default_rng(seed).standard_normal(M * K).astype(np.float32)
     B32 = np.random.default_rng(seed + 81).standard_normal(K * N).astype(np.float32)
@@ -278,10 +280,18 @@ def _bf16_case(dn, orc, torch, M, N, K, alpha=1.0, beta=0.0, ldc=None, seed=42):
     C0 = ref_uniform(M * ldc, 5)
     ref = C0.copy()
     ref64 = orc.gemm_bf16f32(M, N, K, alpha, A, K, B, N, beta, ref, ldc, want64=True)
+    if b_layout == "nk":
+        Bdev, ldb, tb = np.ascontiguousarray(B.reshape(K, N).T).reshape(-1), K, 1
+    elif b_layout == "kn_pad1":
+        Bp = np.zeros((K, N + 1), np.uint16)
+        Bp[:, :N] = B.reshape(K, N)
+        Bdev, ldb, tb = Bp.reshape(-1), N + 1, 0
+    else:
+        Bdev, ldb, tb = B, N, 0
     dA = torch.from_numpy(A.view(np.int16)).cuda()
-    dB = torch.from_numpy(B.view(np.int16)).cuda()
+    dB = torch.from_numpy(Bdev.view(np.int16)).cuda()
     dC = torch.from_numpy(C0.copy()).cuda()
-    dn.check(dn.cuda_gemm("bf16f32", dn.desc(M, N, K, K, N, ldc, alpha, beta), dA, dB, dC,
+    dn.check(dn.cuda_gemm("bf16f32", dn.desc(M, N, K, K, ldb, ldc, alpha, beta, 0, tb), dA, dB, dC,
                           torch.cuda.current_stream()))
     torch.cuda.synchronize()
     got = dC.cpu().numpy().reshape(M, ldc)
@@ -306,6 +316,20 @@ def test_bf16_config4_full(gpu, dn, orc):
     (129, 80, 8, 1.0, 0.0, None), (9, 64, 256, 1.0, 0.0, None)])
 def test_bf16_tcgen05_shapes(gpu, dn, orc, M, N, K, alpha, beta, ldc):
     _bf16_case(dn, orc, gpu, M, N, K, alpha, beta, ldc)
+
+
+# B operand paths of the tcgen05 kernel: MN-major TMA (1-4 chunks of 64
+# columns, ragged N), K-major TMA (trans_b) and the element gather (B rows not
+# 16-byte aligned).
+@pytest.mark.parametrize("M,N,K,beta,b_layout", [
+    (1000, 40, 256, 0.0, "kn"), (777, 200, 192, 0.5, "kn"), (512, 256, 64, 0.0, "kn"),
+    (300, 24, 136, 0.0, "kn"), (4096, 64, 256, 0.0, "nk"), (333, 48, 104, 0.5, "nk"),
+    (257, 200, 64, 0.0, "nk"), (2000, 64, 256, 0.0, "kn_pad1"), (129, 36, 72, 0.5, "kn_pad1")])
+def test_bf16_tcgen05_b_layouts(gpu, dn, orc, M, N, K, beta, b_layout):
+    ldb = {"kn": N, "nk": K, "kn_pad1": N + 1}[b_layout]
+    d = dn.desc(M, N, K, K, ldb, N, 1.0, beta, 0, int(b_layout == "nk"))
+    assert dn.plan_describe(dn.KIND_BF16F32, d) == "gemm_bf16_tcgen05"
+    _bf16_case(dn, orc, gpu, M, N, K, 1.0, beta, b_layout=b_layout)
 
 
 @pytest.mark.parametrize("shape", [(1, 4096, 512), (7, 1009, 1024), (8, 64, 256), (65, 300, 77),
