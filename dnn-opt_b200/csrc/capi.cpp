@@ -49,7 +49,10 @@ DeviceInfo info_of(const DeviceContext* ctx) {
     return i;
 }
 
-bool is_kn(KernelId k) { return k == KernelId::GemvKn || k == KernelId::GemvKnCluster; }
+// Kernels for a K x N B with M <= 8 (one plan family: interchangeable under autotune).
+bool is_kn(KernelId k) {
+    return k == KernelId::GemvKn || k == KernelId::GemvKnCluster || k == KernelId::GemvSlab;
+}
 
 int vec_of(const Plan& p) {
     if (p.kernel == KernelId::E4m3Tc) return 1;
@@ -102,6 +105,10 @@ int launch_plan(Kind kind, const GemmArgs& g, const Plan& p, const float* scales
         }
         case KernelId::GemvKnCluster:
             e = launch_gemv_kn_cluster(in_a(kind), in_b(kind), g, p.kn, s);
+            note_launch();
+            break;
+        case KernelId::GemvSlab:
+            e = launch_gemv_slab(in_a(kind), in_b(kind), g, p.kn.mt, s);
             note_launch();
             break;
         case KernelId::GemvNk:
@@ -208,9 +215,14 @@ Plan get_plan(Kind kind, const GemmArgs& g, DeviceContext* ctx, cudaStream_t s,
     if (!autotune_enabled() || !ctx) return h;
 
     // Candidates around the heuristic choice.
-    Plan cands[12];
+    constexpr int kMaxCands = 16;
+    Plan cands[kMaxCands];
     int nc = 0;
     if (is_kn(h.kernel)) {
+        Plan slab = h;
+        slab.kernel = KernelId::GemvSlab;
+        slab.kn = kn_plan_for(kind, g, info, 0, false);
+        cands[nc++] = slab;
         const GemvKnPlan ws_plan = kn_plan_for(kind, g, info, 0, false);
         const int tries[6] = {h.kn.splits, h.kn.splits / 2, h.kn.splits * 2, 1,
                               ws_plan.splits, ws_plan.splits * 2};
@@ -224,7 +236,7 @@ Plan get_plan(Kind kind, const GemmArgs& g, DeviceContext* ctx, cudaStream_t s,
                 bool dup = false;
                 for (int i = 0; i < nc; ++i)
                     dup = dup || (cands[i].kn.splits == q.kn.splits && cands[i].kernel == q.kernel);
-                if (!dup && nc < 12) cands[nc++] = q;
+                if (!dup && nc < kMaxCands) cands[nc++] = q;
             }
         }
     } else if (h.kernel == KernelId::E4m3Tc) {
@@ -240,7 +252,7 @@ Plan get_plan(Kind kind, const GemmArgs& g, DeviceContext* ctx, cudaStream_t s,
                 bool dup = false;
                 for (int i = 0; i < nc; ++i)
                     dup = dup || (cands[i].e4.splits == q.e4.splits && cands[i].e4.stages == q.e4.stages);
-                if (!dup && nc < 12) cands[nc++] = q;
+                if (!dup && nc < kMaxCands) cands[nc++] = q;
             }
     } else {
         const int g0 = h.nk.grid;

@@ -25,6 +25,7 @@
 
 #include "common.cuh"
 #include "dnnopt_b200.h"
+#include "elem.cuh"
 #include "kernels.h"
 
 namespace dnnopt_b200 {
@@ -34,66 +35,6 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kTileN = 128;
-
-template <In I> struct Elem;
-template <> struct Elem<In::F32> { using T = float; };
-template <> struct Elem<In::BF16> { using T = uint16_t; };
-template <> struct Elem<In::F32R> { using T = float; };
-template <> struct Elem<In::RE4> { using T = uint8_t; };
-template <> struct Elem<In::RE5> { using T = uint8_t; };
-
-// Reference fp8_e4m3_t decode (include/dnnopt/gemm/gemm_types.h:88-115):
-// bias 8, subnormal step 2^-9, field 0x7F/0xFF decodes to +-448.
-__device__ __forceinline__ float decode_re4(uint32_t b) {
-    uint32_t s = (b >> 7) & 1u, e = (b >> 3) & 0xFu, m = b & 7u;
-    float v;
-    if (e == 0) v = static_cast<float>(m) * 0.001953125f;           // m * 2^-9
-    else if (e == 0xF && m == 7) v = 448.0f;
-    else v = __uint_as_float(((e + 119u) << 23) | (m << 20));      // 2^(e-8) * (1+m/8)
-    return s ? -v : v;
-}
-
-// Reference fp8_e5m2_t decode (gemm_types.h:160-191): bias 16,
-// subnormal step 2^-16, exponent field 31 is inf/nan.
-__device__ __forceinline__ float decode_re5(uint32_t b) {
-    uint32_t s = (b >> 7) & 1u, e = (b >> 2) & 0x1Fu, m = b & 3u;
-    if (e == 0) {
-        float v = static_cast<float>(m) * 1.52587890625e-05f;       // m * 2^-16
-        return s ? -v : v;
-    }
-    if (e == 0x1F) return __uint_as_float((s << 31) | (0xFFu << 23) | (m << 21));
-    return __uint_as_float((s << 31) | ((e + 111u) << 23) | (m << 21));
-}
-
-template <In I>
-__device__ __forceinline__ float dec(typename Elem<I>::T v) {
-    if constexpr (I == In::F32) return v;
-    else if constexpr (I == In::BF16) return bf16_bits_to_f32(v);
-    else if constexpr (I == In::F32R) return round_to_bf16(v);
-    else if constexpr (I == In::RE4) return decode_re4(v);
-    else return decode_re5(v);
-}
-
-// Four consecutive elements of one B row -> four floats (aligned vector load).
-template <In I>
-__device__ __forceinline__ void load4(const typename Elem<I>::T* p, float (&o)[4]) {
-    if constexpr (sizeof(typename Elem<I>::T) == 4) {
-        float4 v = __ldg(reinterpret_cast<const float4*>(p));
-        o[0] = dec<I>(v.x); o[1] = dec<I>(v.y); o[2] = dec<I>(v.z); o[3] = dec<I>(v.w);
-    } else if constexpr (sizeof(typename Elem<I>::T) == 2) {
-        uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
-        o[0] = dec<I>(static_cast<uint16_t>(v.x & 0xFFFFu));
-        o[1] = dec<I>(static_cast<uint16_t>(v.x >> 16));
-        o[2] = dec<I>(static_cast<uint16_t>(v.y & 0xFFFFu));
-        o[3] = dec<I>(static_cast<uint16_t>(v.y >> 16));
-    } else {
-        uint32_t v = __ldg(reinterpret_cast<const unsigned int*>(p));
-        o[0] = dec<I>(static_cast<uint8_t>(v & 0xFFu));
-        o[1] = dec<I>(static_cast<uint8_t>((v >> 8) & 0xFFu));
-        o[2] = dec<I>(static_cast<uint8_t>((v >> 16) & 0xFFu));
-        o[3] = dec<I>(static_cast<uint8_t>(v >> 24));
-    }
-}
 
 struct KnParams {
     GemmArgs g;
@@ -113,17 +54,20 @@ __device__ __forceinline__ int slot_col(int lane, int c) {
 //     strip (atomic ticket) sums them in split order;
 //   CLUSTER == true: the splits form one thread-block cluster and sum the
 //     partial strips through distributed shared memory.
-// Per CTA the critical path is kept to one DRAM round trip where possible:
+// Per CTA the critical path is kept to as few memory round trips as possible:
 //   1. the first batch of B rows is requested before anything else; A for the
-//      pass is staged in shared memory and (beta != 0) this CTA's slice of C
-//      is prefetched while those loads are in flight;
+//      pass is staged in shared memory while those loads are in flight;
 //   2. the remaining rows stream with register double-buffering (two batches
 //      of U rows in flight per thread);
-//   3. the 8 warps reduce in shared memory in warp order, then the splits.
+//   3. the 8 warps reduce in shared memory in warp order, then the splits:
+//      the last CTA of a strip loads every split's partial (8-16 splits
+//      per round of independent loads, vector width matched to MT so that all
+//      256 threads take part) and the C values it needs, and sums the splits
+//      in order.
 constexpr int kPassRows = 1024;   // K rows of A staged per pass
 
 template <In IA, In IB, int MT, bool VEC4, bool CLUSTER>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 1)
 gemv_kn_kernel(const KnParams p) {
     using TA = typename Elem<IA>::T;
     using TB = typename Elem<IB>::T;
@@ -137,7 +81,6 @@ gemv_kn_kernel(const KnParams p) {
     float* sA = dsm;
     float* red = dsm;
     float* part = dsm + red_floats;            // [MT][128] this CTA's partial strip
-    float* cpre = part + MT * kTileN;           // [MT][128] prefetched C (beta != 0)
     __shared__ int s_last;
 
     pdl_wait();
@@ -212,19 +155,13 @@ gemv_kn_kernel(const KnParams p) {
         if (nb > 0) load_batch(b0, 0);
         if (kp > k_begin) __syncthreads();   // the previous pass is done with sA
         for (int idx = tid; idx < kn * MT; idx += kThreads) {
-            int r = idx / MT, m = idx - r * MT;
+            const int r = idx / MT, m = idx - r * MT;
             float v = 0.0f;
             if (m < g.M) {
-                int64_t off = g.a_trans ? (int64_t)(kp + r) * g.lda + m : (int64_t)m * g.lda + (kp + r);
+                const int64_t off = g.a_trans ? (int64_t)(kp + r) * g.lda + m : (int64_t)m * g.lda + (kp + r);
                 v = dec<IA>(A[off]);
             }
             sA[idx] = v;
-        }
-        if (kp == k_begin && g.beta != 0.0f) {
-            for (int idx = tid; idx < MT * kTileN; idx += kThreads) {
-                int m = idx / kTileN, j = idx - m * kTileN;
-                cpre[idx] = (m < g.M && n0 + j < g.N) ? C[(int64_t)m * g.ldc + n0 + j] : 0.0f;
-            }
         }
         __syncthreads();
         for (int it = 0; it < nb; it += 2) {
@@ -251,10 +188,12 @@ gemv_kn_kernel(const KnParams p) {
         part[idx] = sum;
     }
 
+    // C = beta == 0 ? alpha*sum : fma(alpha, sum, beta*C), the reference's
+    // epilogue; C is read only where it is written.
     auto store = [&](int m, int j, float sum) {
         if (m < g.M && n0 + j < g.N) {
             float* cp = C + (int64_t)m * g.ldc + n0 + j;
-            *cp = (g.beta == 0.0f) ? g.alpha * sum : fmaf(g.alpha, sum, g.beta * cpre[m * kTileN + j]);
+            *cp = (g.beta == 0.0f) ? g.alpha * sum : fmaf(g.alpha, sum, g.beta * *cp);
         }
     };
 
@@ -280,11 +219,17 @@ gemv_kn_kernel(const KnParams p) {
         }
         cluster_sync_all();
     } else {
-        // Publish this split's strip; the last CTA of the strip (ticket
+        // Publish this split's strip (16-byte stores; the workspace rows are
+        // n_pad floats, a multiple of 128); the last CTA of the strip (ticket
         // splits-1) sums the splits in order and writes C.
-        for (int idx = tid; idx < MT * kTileN; idx += kThreads) {
-            int m = idx / kTileN, j = idx - m * kTileN;
-            __stcg(&p.ws[((int64_t)split * MT + m) * p.n_pad + n0 + j], part[idx]);
+        float4* ws4 = reinterpret_cast<float4*>(p.ws);
+        const int q_per_split = MT * kTileN / 4;           // float4 groups of one strip
+        const int row4 = p.n_pad / 4;
+        __syncthreads();   // part[] was written by other threads
+        for (int q = tid; q < q_per_split; q += kThreads) {
+            const int m = q / (kTileN / 4), j4 = q - m * (kTileN / 4);
+            __stcg(&ws4[((int64_t)split * MT + m) * row4 + n0 / 4 + j4],
+                   *reinterpret_cast<const float4*>(&part[m * kTileN + 4 * j4]));
         }
         __threadfence();
         __syncthreads();
@@ -295,14 +240,54 @@ gemv_kn_kernel(const KnParams p) {
         __syncthreads();
         if (!s_last) return;
         __threadfence();
-        for (int idx = tid; idx < MT * kTileN; idx += kThreads) {
-            int m = idx / kTileN, j = idx - m * kTileN;
-            if (m < g.M && n0 + j < g.N) {
-                float sum = 0.0f;
-                for (int sp = 0; sp < p.splits; ++sp)
-                    sum += __ldcg(&p.ws[((int64_t)sp * MT + m) * p.n_pad + n0 + j]);
-                store(m, j, sum);
+        // Each thread owns VW consecutive columns of one row m (every thread
+        // of the CTA when MT >= 2) and issues all its split loads in rounds of
+        // kSumRound before adding them in split order.
+        constexpr int VW = MT >= 8 ? 4 : (MT >= 4 ? 2 : 1);
+        constexpr int kGroupsPerRow = kTileN / VW;
+        constexpr int kSumRound = VW == 4 ? 8 : 16;
+        const float* wsf = p.ws;
+        for (int q = tid; q < MT * kGroupsPerRow; q += kThreads) {
+            const int m = q / kGroupsPerRow, j0 = (q - m * kGroupsPerRow) * VW;
+            if (m >= g.M || n0 + j0 >= g.N) continue;
+            float* crow = C + (int64_t)m * g.ldc + n0 + j0;
+            float cv[VW];
+#pragma unroll
+            for (int u = 0; u < VW; ++u)
+                cv[u] = (g.beta != 0.0f && n0 + j0 + u < g.N) ? crow[u] : 0.0f;
+            float sum[VW];
+#pragma unroll
+            for (int u = 0; u < VW; ++u) sum[u] = 0.0f;
+            const float* src = wsf + (int64_t)m * p.n_pad + n0 + j0;
+            const int64_t sstride = (int64_t)MT * p.n_pad;
+            for (int sp0 = 0; sp0 < p.splits; sp0 += kSumRound) {
+                float v[kSumRound][VW];
+#pragma unroll
+                for (int r = 0; r < kSumRound; ++r) {
+                    if (sp0 + r < p.splits) {
+                        const float* ps = src + (sp0 + r) * sstride;
+                        if constexpr (VW == 4) {
+                            const float4 t = __ldcg(reinterpret_cast<const float4*>(ps));
+                            v[r][0] = t.x; v[r][1] = t.y; v[r][2] = t.z; v[r][3] = t.w;
+                        } else if constexpr (VW == 2) {
+                            const float2 t = __ldcg(reinterpret_cast<const float2*>(ps));
+                            v[r][0] = t.x; v[r][1] = t.y;
+                        } else {
+                            v[r][0] = __ldcg(ps);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int r = 0; r < kSumRound; ++r)
+                    if (sp0 + r < p.splits) {
+#pragma unroll
+                        for (int u = 0; u < VW; ++u) sum[u] += v[r][u];
+                    }
             }
+#pragma unroll
+            for (int u = 0; u < VW; ++u)
+                if (n0 + j0 + u < g.N)
+                    crow[u] = (g.beta == 0.0f) ? g.alpha * sum[u] : fmaf(g.alpha, sum[u], g.beta * cv[u]);
         }
         if (tid == 0) p.counters[blockIdx.x] = 0u;   // ready for the next launch on this stream
     }
@@ -312,7 +297,7 @@ size_t kn_smem_bytes(int mt, int kchunk) {
     size_t rows = kchunk < kPassRows ? kchunk : kPassRows;
     size_t stage = rows * mt;
     size_t red = static_cast<size_t>(kWarps) * mt * kTileN;
-    return ((stage > red ? stage : red) + 2 * static_cast<size_t>(mt) * kTileN) * sizeof(float);
+    return ((stage > red ? stage : red) + static_cast<size_t>(mt) * kTileN) * sizeof(float);
 }
 
 template <In IA, In IB, int MT, bool VEC4, bool CL>

@@ -2,10 +2,14 @@
 //
 // Dispatch rules (B200 re-statement of src/gemm/gemm.cpp:168-455, where the
 // reference routes by M < small_m_bound (8), N >= wide_n_bound and K):
-//   * M <= 8 and B stored K x N      -> GemvKn (split-K streaming GEMV, splits
-//                                      reduced by a ticketed last CTA) or, when
-//                                      autotune measures it faster, GemvKnCluster
-//                                      (splits reduced in a thread-block cluster)
+//   * M <= 8 and B stored K x N      -> GemvSlab (whole K per 8-column CTA) for
+//                                      K <= 2048 and 512 <= N <= 8192, where a
+//                                      split-K reduction costs more than the B
+//                                      stream; else GemvKn (split-K streaming
+//                                      GEMV, splits reduced by a ticketed last
+//                                      CTA) or, when autotune measures it faster,
+//                                      GemvKnCluster (splits reduced in a
+//                                      thread-block cluster) or GemvSlab
 //   * M <= 8 and B stored N x K      -> GemvNk  (dot-form GEMV; all int8 calls)
 //   * BF16, large M, N <= 256        -> Bf16Tc  (tcgen05 tall-skinny)
 //   * config-5 e4m3 with M > 8       -> GemvNkRows (dot form per 8-row block)
@@ -131,6 +135,7 @@ const char* kernel_name(KernelId k) {
         case KernelId::GemvKnCluster: return "gemv_kn_cluster";
         case KernelId::GemvRows: return "gemv_rows_dot";
         case KernelId::E4m3Tc: return "gemm_e4m3_tcgen05";
+        case KernelId::GemvSlab: return "gemv_kn_slab";
     }
     return "?";
 }
@@ -225,6 +230,9 @@ Plan heuristic_plan(Kind kind, const GemmArgs& g, const DeviceInfo& info) {
     if (g.M <= 8 && !g.b_trans) {
         p.kn = kn_plan_for(kind, g, info, 0, false);
         p.kernel = p.kn.cluster ? KernelId::GemvKnCluster : KernelId::GemvKn;
+        // Measured on B200 (M <= 8, K = 1024, prime N of 1009-4093): the slab
+        // form finishes in 0.4-0.8x the split-K time; at K = 4096 split-K wins.
+        if (g.K <= 2048 && g.N >= 512 && g.N <= 8192) p.kernel = KernelId::GemvSlab;
         return p;
     }
     if (kind == Kind::F32 && g.M <= 8 && g.b_trans && gemv_rows_supported(DotKind::F32, g)) {
@@ -247,7 +255,7 @@ Plan heuristic_plan(Kind kind, const GemmArgs& g, const DeviceInfo& info) {
     return p;
 }
 
-std::string describe_plan(Kind, const GemmArgs&, const Plan& p) {
+std::string describe_plan(Kind, const GemmArgs& g, const Plan& p) {
     char buf[160];
     switch (p.kernel) {
         case KernelId::GemvKn:
@@ -265,6 +273,10 @@ std::string describe_plan(Kind, const GemmArgs&, const Plan& p) {
         case KernelId::E4m3Tc:
             std::snprintf(buf, sizeof(buf), "%s splits=%d kc=%d stages=%d", kernel_name(p.kernel),
                           p.e4.splits, p.e4.kc, p.e4.stages);
+            break;
+        case KernelId::GemvSlab:
+            std::snprintf(buf, sizeof(buf), "%s mt=%d ctas=%d%s", kernel_name(p.kernel), p.kn.mt,
+                          gemv_slab_ctas(g.N), p.tuned ? " tuned" : "");
             break;
         default:
             std::snprintf(buf, sizeof(buf), "%s", kernel_name(p.kernel));
@@ -325,7 +337,8 @@ bool cache_lookup(uint64_t key, Plan* out) {
     const Entry& e = it->second;
     out->kernel = static_cast<KernelId>(e.kernel);
     out->tuned = true;
-    if (out->kernel == KernelId::GemvKn || out->kernel == KernelId::GemvKnCluster) {
+    if (out->kernel == KernelId::GemvKn || out->kernel == KernelId::GemvKnCluster ||
+        out->kernel == KernelId::GemvSlab) {
         out->kn.splits = e.p0;
         out->kn.kchunk = e.p1;
         out->kn.mt = e.mt;
@@ -344,7 +357,8 @@ bool cache_lookup(uint64_t key, Plan* out) {
 void cache_store(uint64_t key, const Plan& p, float time_us) {
     Entry e;
     e.kernel = static_cast<int32_t>(p.kernel);
-    if (p.kernel == KernelId::GemvKn || p.kernel == KernelId::GemvKnCluster) {
+    if (p.kernel == KernelId::GemvKn || p.kernel == KernelId::GemvKnCluster ||
+        p.kernel == KernelId::GemvSlab) {
         e.p0 = p.kn.splits; e.p1 = p.kn.kchunk; e.mt = p.kn.mt;
     } else if (p.kernel == KernelId::E4m3Tc) {
         e.p0 = p.e4.splits; e.p1 = p.e4.kc; e.mt = p.e4.stages;

@@ -33,6 +33,7 @@ enum class KernelId : int {
     GemvKnCluster = 6,  // small-M split-K, splits reduced in a thread-block cluster
     GemvRows = 7,   // small-M dot form with A in registers (aligned B rows, K <= 512 chunks)
     E4m3Tc = 8,     // config-5 e4m3 weights on tcgen05 (kind::f8f6f4), 8-row blocks of A
+    GemvSlab = 9,   // small-M column slab, B K x N: whole K per CTA, no split-K reduction
 };
 
 struct Plan {

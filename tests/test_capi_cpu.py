@@ -127,10 +127,16 @@ def test_plan_selection_without_device(dn):
     # Dispatch classes of the reference's shape router (src/gemm/gemm.cpp:168-455).
     s = dn.plan_describe(dn.KIND_F32, dn.desc(1, 4096, 4096, 4096, 4096, 4096))
     assert s.startswith("gemv_kn_splitk mt=1 vec4=1"), s
+    # The irregular-N sweep (K = 1024): whole-K column slabs, no split-K reduction.
     s = dn.plan_describe(dn.KIND_F32, dn.desc(7, 4093, 1024, 1024, 4093, 4093, beta=0.5))
-    assert s.startswith("gemv_kn_splitk mt=8 vec4=0 splits=13"), s   # prime N: scalar loads
+    assert s == "gemv_kn_slab mt=8 ctas=512", s
     s = dn.plan_describe(dn.KIND_F32, dn.desc(2, 1009, 1024, 1024, 1009, 1009))
-    assert s.startswith("gemv_kn_splitk mt=2 vec4=0 splits=16 kchunk=64"), s
+    assert s == "gemv_kn_slab mt=2 ctas=127", s
+    # Deeper K: split-K, one wave of resident CTAs, at most 16 splits.
+    s = dn.plan_describe(dn.KIND_F32, dn.desc(7, 4093, 4096, 4096, 4093, 4093, beta=0.5))
+    assert s.startswith("gemv_kn_splitk mt=8 vec4=0 splits=13 kchunk=320"), s   # prime N: scalar loads
+    s = dn.plan_describe(dn.KIND_F32, dn.desc(2, 1009, 4096, 4096, 1009, 1009))
+    assert s.startswith("gemv_kn_splitk mt=2 vec4=0 splits=16 kchunk=256"), s
     s = dn.plan_describe(dn.KIND_S8S32, dn.desc(4, 11008, 4096, 4096, 4096, 11008))
     assert s.startswith("gemv_rows_dot mt=4 vec=1"), s
     s = dn.plan_describe(dn.KIND_S8S32, dn.desc(4, 11008, 4100, 4100, 4100, 11008))

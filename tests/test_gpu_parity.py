@@ -436,12 +436,61 @@ def test_cluster_variant_forced(gpu, dn, orc, tmp_path, splits):
                          struct.pack("<iiiif", 6, se, kchunk, mt, 0.0))
         assert dn.lib.dnnopt_autotune_load(str(path).encode()) == 1
         d = dn.desc(M, N, K, K, N, N, 1.0, 0.5)
-        assert dn.plan_describe(dn.KIND_F32, d).startswith("gemv_kn_splitk")  # heuristic view
+        assert dn.plan_describe(dn.KIND_F32, d).startswith("gemv_kn_")  # heuristic view
         A, B, C = ref_uniform(M * K, 5), ref_uniform(K * N, 6), ref_uniform(M * N, 7)
         ref = C.copy()
         orc.gemm_f32(M, N, K, 1.0, A, K, B, N, 0.5, ref, N)
         dn.check(dn.gemm_fp32(M, N, K, 1.0, A, K, B, N, 0.5, C, N))
         assert np.max(np.abs(C - ref)) <= fp32_tol(K), (M, N, K, splits)
+
+
+def _force_plan(dn, tmp_path, name, kind, M, N, K, lda, ldb, ldc, ta, tb, vec, entry):
+    """Load an autotune-cache file holding one plan for this exact call."""
+    import struct
+    key_src = struct.pack("<10q", kind, M, N, K, lda, ldb, ldc, ta, tb, vec)
+    h = 1469598103934665603
+    for b in key_src:
+        h = ((h ^ b) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+    path = tmp_path / name
+    path.write_bytes(b"DNNAUTO\x00" + struct.pack("<II", 4, 1) + struct.pack("<Q", h) +
+                     struct.pack("<iiiif", *entry, 0.0))
+    assert dn.lib.dnnopt_autotune_load(str(path).encode()) == 1
+
+
+# Column-slab kernel: heuristic shapes and, through a forced plan, shapes
+# outside its heuristic range (tiny N, K over several 1024-row passes, K not a
+# multiple of the 32-row step, transposed A, padded C).
+@pytest.mark.parametrize("M,N,K,alpha,beta,ta,ldc,force", [
+    (2, 1009, 1024, 1.0, 0.5, 0, None, False), (7, 4093, 1024, 1.0, 0.5, 0, None, False),
+    (5, 2039, 1000, 2.0, 0.0, 0, None, False), (8, 600, 2048, 1.0, -1.0, 0, 604, False),
+    (1, 7, 5, 1.0, 0.5, 0, None, True), (3, 100, 3000, 1.0, 0.25, 0, None, True),
+    (4, 520, 1030, 0.5, 0.5, 1, None, True), (6, 9000, 33, 1.0, 0.0, 0, None, True),
+    (1, 1024, 4097, 1.0, 0.5, 1, 1030, True)])
+def test_slab_kernel(gpu, dn, orc, tmp_path, M, N, K, alpha, beta, ta, ldc, force):
+    ldc = ldc or N
+    lda = M if ta else K
+    mt = 1 if M <= 1 else 2 if M <= 2 else 4 if M <= 4 else 8
+    vec = 1 if N % 4 == 0 else 0
+    if force:
+        _force_plan(dn, tmp_path, f"slab_{M}_{N}_{K}.bin", 0, M, N, K, lda, N, ldc, ta, 0, vec,
+                    (9, 0, 0, mt))
+    else:
+        assert dn.plan_describe(dn.KIND_F32, dn.desc(M, N, K, lda, N, ldc, alpha, beta, ta, 0)) \
+            == f"gemv_kn_slab mt={mt} ctas={(N + 7) // 8}"
+    A, B = ref_uniform(M * K, 11), ref_uniform(K * N, 12)   # A is K x M when ta
+    C0 = ref_uniform(M * ldc, 13)
+    Ar = np.ascontiguousarray(A.reshape(K, M).T).reshape(-1) if ta else A
+    ref_full = C0.reshape(M, ldc).copy()
+    tmp = ref_full[:, :N].copy().reshape(-1)
+    orc.gemm_f32(M, N, K, alpha, Ar, K, B, N, beta, tmp, N)
+    ref_full[:, :N] = tmp.reshape(M, N)
+    dA, dB, dC = (gpu.from_numpy(x).cuda() for x in (A, B, C0.copy()))
+    dn.check(dn.cuda_gemm("f32", dn.desc(M, N, K, lda, N, ldc, alpha, beta, ta, 0), dA, dB, dC,
+                          gpu.cuda.current_stream()))
+    gpu.cuda.synchronize()
+    got = dC.cpu().numpy().reshape(M, ldc)
+    assert np.max(np.abs(got[:, :N] - ref_full[:, :N])) <= fp32_tol(K), (M, N, K)
+    assert np.array_equal(got[:, N:], C0.reshape(M, ldc)[:, N:])
 
 
 def test_autotune_roundtrip(gpu, dn, orc, tmp_path):
