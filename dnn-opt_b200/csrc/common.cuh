@@ -121,7 +121,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
 }
 
 // ---------------------------------------------------------------------------
-// TMA (cp.async.bulk.tensor), no multicast anywhere in this library.
+// TMA (cp.async.bulk.tensor): every load lands in the issuing CTA's shared memory.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, uint64_t* bar,
                                             int32_t x, int32_t y) {

@@ -25,7 +25,7 @@
 //   * programmatic dependent launch: the prologue (barrier init, TMEM
 //     allocation, descriptor prefetch) overlaps the previous kernel's tail and
 //     every global access waits for it (griddepcontrol.wait).
-// No cluster multicast is used anywhere.
+// Every TMA load targets this CTA's own shared memory.
 #include <cuda.h>
 
 #include "common.cuh"
