@@ -55,6 +55,18 @@ def desc(M, N, K, lda, ldb, ldc, alpha=1.0, beta=0.0, trans_a=0, trans_b=0) -> G
     return GemmDesc(M, N, K, lda, ldb, ldc, alpha, beta, int(trans_a), int(trans_b))
 
 
+MAX_RANKS = 8
+
+
+class AllGatherDesc(ctypes.Structure):
+    _fields_ = [
+        ("world", ctypes.c_int), ("rank", ctypes.c_int),
+        ("out", ctypes.c_void_p * MAX_RANKS),
+        ("flags", ctypes.c_void_p * MAX_RANKS),
+        ("epoch", ctypes.c_uint),
+    ]
+
+
 if not os.path.exists(LIB_PATH):
     raise ImportError(f"{LIB_PATH} is missing: build it with `make -C dnn-opt_b200` "
                       "(there is no CPU fallback)")
@@ -93,6 +105,15 @@ lib.dnnopt_autotune_enable.argtypes = [_I]
 lib.dnnopt_autotune_save.argtypes = [ctypes.c_char_p]
 lib.dnnopt_autotune_load.argtypes = [ctypes.c_char_p]
 lib.dnnopt_debug_inject_fault.argtypes = [_I, _I]
+lib.dnnopt_peer_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]
+lib.dnnopt_peer_free.argtypes = [_P]
+lib.dnnopt_ipc_handle.argtypes = [_P, ctypes.c_char_p]
+lib.dnnopt_ipc_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]
+lib.dnnopt_ipc_close.argtypes = [_P]
+lib.dnnopt_cuda_gemm_e4m3bf16_allgather.argtypes = [ctypes.POINTER(GemmDesc), _P, _P, _P,
+                                                    ctypes.POINTER(AllGatherDesc), _P]
+lib.dnnopt_cuda_peer_wait.argtypes = [_P, _I, ctypes.c_uint, ctypes.c_uint, _P]
+lib.dnnopt_stream_status.argtypes = [_P]
 
 
 def ptr(x) -> int | None:
@@ -183,6 +204,52 @@ def cuda_gemm(kind: str, d: GemmDesc, A, B, C, stream=None, scale=None) -> int:
     if kind == "e4m3bf16":
         return fn(ctypes.byref(d), ptr(A), ptr(B), ptr(scale), ptr(C), s)
     return fn(ctypes.byref(d), ptr(A), ptr(B), ptr(C), s)
+
+
+def _stream(stream):
+    return stream.cuda_stream if hasattr(stream, "cuda_stream") else ptr(stream)
+
+
+# ---- multi-GPU (one process per GPU) ----------------------------------------
+def peer_alloc(nbytes: int) -> int:
+    p = ctypes.c_void_p()
+    check(lib.dnnopt_peer_alloc(nbytes, ctypes.byref(p)), "peer_alloc")
+    return int(p.value)
+
+
+def peer_free(address: int) -> None:
+    check(lib.dnnopt_peer_free(address), "peer_free")
+
+
+def ipc_handle(address: int) -> bytes:
+    buf = ctypes.create_string_buffer(64)
+    check(lib.dnnopt_ipc_handle(address, buf), "ipc_handle")
+    return buf.raw
+
+
+def ipc_open(handle: bytes) -> int:
+    if len(handle) != 64:
+        raise ValueError("CUDA IPC handles are 64 bytes")
+    p = ctypes.c_void_p()
+    check(lib.dnnopt_ipc_open(handle, ctypes.byref(p)), "ipc_open")
+    return int(p.value)
+
+
+def ipc_close(address: int) -> None:
+    check(lib.dnnopt_ipc_close(address), "ipc_close")
+
+
+def cuda_gemm_e4m3bf16_allgather(d: GemmDesc, A, W, scale, ag: AllGatherDesc, stream=None) -> int:
+    return lib.dnnopt_cuda_gemm_e4m3bf16_allgather(ctypes.byref(d), ptr(A), ptr(W), ptr(scale),
+                                                   ctypes.byref(ag), _stream(stream))
+
+
+def cuda_peer_wait(flags, world: int, epoch: int, timeout_us: int, stream=None) -> int:
+    return lib.dnnopt_cuda_peer_wait(ptr(flags), world, epoch, timeout_us, _stream(stream))
+
+
+def stream_status(stream=None) -> int:
+    return lib.dnnopt_stream_status(_stream(stream))
 
 
 def plan_describe(kind: int, d: GemmDesc) -> str:

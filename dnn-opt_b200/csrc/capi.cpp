@@ -242,10 +242,12 @@ Plan get_plan(Kind kind, const GemmArgs& g, DeviceContext* ctx, cudaStream_t s,
     } else if (h.kernel == KernelId::E4m3Tc) {
         GemmArgs g8 = g;
         g8.M = g.M < 8 ? g.M : 8;
-        const int tries[4] = {1, 2, 3, 4};
-        const int depths[3] = {2, 3, 4};
+        const int s0 = h.e4.splits;
+        const int tries[6] = {s0, s0 / 2, s0 * 2, 1, 2, 4};
+        const int depths[2] = {2, 3};
         for (int t : tries)
             for (int d : depths) {
+                if (t < 1 || t > 32) continue;
                 Plan q = h;
                 q.e4 = gemm_e4m3_tc_plan_splits(g8, t, d);
                 if (q.e4.stages < 2) continue;
@@ -585,6 +587,138 @@ int dnnopt_cuda_gemm_refe4m3_e5m2(const dnnopt_gemm_desc* d, const uint8_t* A, c
 int dnnopt_cuda_gemm_refe5m2_e5m2(const dnnopt_gemm_desc* d, const uint8_t* A, const uint8_t* B,
                                   float* C, void* stream) {
     return device_entry(Kind::RE5E5, d, A, B, C, nullptr, stream);
+}
+
+// ---- multi-GPU --------------------------------------------------------------
+int dnnopt_peer_alloc(size_t bytes, void** ptr) {
+    if (!ptr || bytes == 0) return set_status(DNNOPT_STATUS_INVALID_VALUE);
+    *ptr = nullptr;
+    int st;
+    if (!current_context(&st)) return st;
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return set_status(DNNOPT_STATUS_ALLOC_FAILED);
+    }
+    e = cudaMemset(p, 0, bytes);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return cuda_status(e);
+    }
+    *ptr = p;
+    return set_status(DNNOPT_STATUS_SUCCESS);
+}
+
+int dnnopt_peer_free(void* ptr) {
+    if (!ptr) return set_status(DNNOPT_STATUS_SUCCESS);
+    return cuda_status(cudaFree(ptr));
+}
+
+int dnnopt_ipc_handle(const void* ptr, unsigned char handle[64]) {
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+    if (!ptr || !handle) return set_status(DNNOPT_STATUS_INVALID_VALUE);
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+    if (e != cudaSuccess) return cuda_status(e);
+    std::memcpy(handle, &h, sizeof(h));
+    return set_status(DNNOPT_STATUS_SUCCESS);
+}
+
+int dnnopt_ipc_open(const unsigned char handle[64], void** ptr) {
+    if (!handle || !ptr) return set_status(DNNOPT_STATUS_INVALID_VALUE);
+    *ptr = nullptr;
+    int st;
+    if (!current_context(&st)) return st;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    return cuda_status(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int dnnopt_ipc_close(void* ptr) {
+    if (!ptr) return set_status(DNNOPT_STATUS_INVALID_VALUE);
+    return cuda_status(cudaIpcCloseMemHandle(ptr));
+}
+
+int dnnopt_cuda_gemm_e4m3bf16_allgather(const dnnopt_gemm_desc* d, const uint16_t* A,
+                                        const uint8_t* W, const float* scale,
+                                        const dnnopt_allgather_desc* ag, void* stream) {
+    if (!ag || ag->world < 1 || ag->world > DNNOPT_MAX_RANKS || ag->rank < 0 || ag->rank >= ag->world)
+        return set_status(DNNOPT_STATUS_INVALID_VALUE);
+    for (int q = 0; q < ag->world; ++q)
+        if (!ag->out[q] || !ag->flags[q]) return set_status(DNNOPT_STATUS_INVALID_VALUE);
+    bool noop;
+    int st = validate(Kind::E4M3BF16, d, A, W, ag->out[ag->rank], &noop);
+    if (st != DNNOPT_STATUS_SUCCESS) return set_status(st);
+    if (noop || !scale || static_cast<int64_t>(d->ldc) < static_cast<int64_t>(ag->world) * d->N)
+        return set_status(DNNOPT_STATUS_INVALID_VALUE);
+    if (d->M > 8) return set_status(DNNOPT_STATUS_NOT_SUPPORTED);
+    DeviceContext* ctx = current_context(&st);
+    if (!ctx) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    GemmArgs g = to_args(d, A, W, ag->out[ag->rank]);
+    g.b_trans = 1;
+    Plan p = get_plan(Kind::E4M3BF16, g, ctx, s, scale);
+    if (p.kernel != KernelId::E4m3Tc) return set_status(DNNOPT_STATUS_NOT_SUPPORTED);
+    int inj = check_injected_fault(2);
+    if (inj != DNNOPT_STATUS_SUCCESS) return set_status(inj);
+    const size_t tiles = static_cast<size_t>((g.N + 127) / 128);
+    Workspace* w = nullptr;
+    st = ensure_workspace(ctx, s, gemm_e4m3_tc_ws_floats(g, p.e4), tiles + 1,
+                          gemm_e4m3_tc_act_bytes(g), &w);
+    if (st != DNNOPT_STATUS_SUCCESS) return st;
+    AllGatherArgs a;
+    a.world = ag->world;
+    a.rank = ag->rank;
+    for (int q = 0; q < kAllGatherMaxRanks; ++q) {
+        a.out[q] = q < ag->world ? ag->out[q] : nullptr;
+        a.flag[q] = q < ag->world ? ag->flags[q] : nullptr;
+    }
+    a.done = w->counters + tiles;      // the tile tickets occupy counters[0, tiles)
+    a.epoch = ag->epoch;
+    cudaError_t e = launch_gemm_e4m3_tc(g, p.e4, scale, w->ws, w->counters, w->quant, w->err, s, &a);
+    note_launch(2);
+    if (e == cudaSuccess) {
+        e = launch_peer_wait(ag->flags[ag->rank], ag->world, ag->epoch, 2000000000ull /* 2 s */, w->err, s);
+        note_launch();
+    }
+    return cuda_status(e);
+}
+
+int dnnopt_cuda_peer_wait(const unsigned int* flags, int world, unsigned int epoch,
+                          unsigned int timeout_us, void* stream) {
+    if (!flags || world < 1 || world > DNNOPT_MAX_RANKS) return set_status(DNNOPT_STATUS_INVALID_VALUE);
+    int st;
+    DeviceContext* ctx = current_context(&st);
+    if (!ctx) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    Workspace* w = nullptr;
+    st = ensure_workspace(ctx, s, 0, 0, 0, &w);
+    if (st != DNNOPT_STATUS_SUCCESS) return st;
+    cudaError_t e = launch_peer_wait(flags, world, epoch, static_cast<uint64_t>(timeout_us) * 1000ull,
+                                     w->err, s);
+    note_launch();
+    return cuda_status(e);
+}
+
+int dnnopt_stream_status(void* stream) {
+    int st;
+    DeviceContext* ctx = current_context(&st);
+    if (!ctx) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_status(e);
+    auto it = ctx->ws.find(s);
+    if (it != ctx->ws.end() && it->second.err) {
+        uint32_t code = 0;
+        e = cudaMemcpy(&code, it->second.err, sizeof(code), cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) return cuda_status(e);
+        if (code != 0) {
+            cudaMemset(it->second.err, 0, sizeof(code));
+            return set_status(DNNOPT_STATUS_KERNEL_TIMEOUT);
+        }
+    }
+    return set_status(DNNOPT_STATUS_SUCCESS);
 }
 
 // ---- plan / autotune --------------------------------------------------------

@@ -21,6 +21,7 @@ enum KernelErrorCode : uint32_t {
     kKerrNone = 0,
     kKerrMbarTimeout = 1,      // an mbarrier wait exceeded its iteration limit
     kKerrTmemAlloc = 2,        // TMEM allocation returned an unusable address
+    kKerrPeerTimeout = 3,      // a peer GPU's flag did not arrive within the limit
 };
 
 __device__ __forceinline__ void record_kernel_error(uint32_t* err, uint32_t code) {
@@ -248,6 +249,26 @@ __device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t smem_addr) {
 __host__ __device__ constexpr uint32_t umma_idesc_bf16_f32(int m, int n) {
     return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
            (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// ---------------------------------------------------------------------------
+// Flag and counter accesses with explicit scope (peer GPUs signal each other
+// through mapped memory).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu_u32(uint32_t* p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
 }
 
 // ---------------------------------------------------------------------------

@@ -20,6 +20,14 @@
 // of each tile (atomic ticket), in split order, so the result is deterministic.
 // Roles: warp 0 TMA producer, warp 1 MMA issuer + TMEM owner, warps 2-5 drain
 // TMEM (tcgen05.ld) and write C.
+//
+// Fused all-gather (N-sharded over ranks, one process per GPU): the epilogue
+// stores each finished column into every rank's output buffer (peer memory
+// mapped through CUDA IPC, plain stores over NVLink), and the last tile of
+// the grid raises this rank's flag on every rank (release, system scope); a
+// one-CTA wait kernel then blocks the stream until every rank's flag has
+// arrived (bounded wait).  The transfer of a tile overlaps the MMAs of the
+// tiles still running.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -37,17 +45,27 @@ constexpr int kStage = kWStage + kActBlock;
 constexpr int kThreads = 192;
 constexpr int kMaxKc = 4096;            // K elements per CTA (activation operand 64 KB)
 constexpr size_t kSmemLimit = 227 * 1024;
+constexpr int kMaxPeers = kAllGatherMaxRanks;
 
 struct E4Params {
     int M, N, K;
     int kc, splits, stages;
     const float* inv_sigma;   // [8] from the prep kernel
     const float* scale;
-    uint16_t* C;
     int64_t ldc;
     float* ws;
     uint32_t* tickets;
     uint32_t* err;
+    // Outputs: nout copies of C (nout == 1: local C; nout == world: every
+    // rank's output buffer, this rank's column block already applied).
+    int nout;
+    uint16_t* out[kMaxPeers];
+    // All-gather signalling (done != nullptr): `done` counts finished tiles on this
+    // GPU; the last tile raises flag[q][rank] = epoch on every rank q.
+    uint32_t* done;
+    uint32_t* flag[kMaxPeers];
+    int rank;
+    uint32_t epoch;
 };
 
 // Instruction descriptor, kind::f8f6f4: A = B = E4M3 (format 0), D = F32,
@@ -216,10 +234,19 @@ gemm_e4m3_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
                 v[m] = (__uint_as_float(r[m]) + __uint_as_float(r[8 + m])) * p.inv_sigma[m];
         }
         const float sc = (n < p.N) ? p.scale[n] : 0.0f;
+        // Writes one finished column n (rows 0..M-1) into every output copy;
+        // the stores of a warp cover 64 contiguous bytes per row and copy.
+        auto write_col = [&](const float (&c)[8]) {
+            uint16_t bits[8];
+#pragma unroll
+            for (int m = 0; m < 8; ++m) bits[m] = __bfloat16_as_ushort(__float2bfloat16_rn(c[m] * sc));
+            for (int o = 0; o < p.nout; ++o)
+                for (int m = 0; m < p.M; ++m) p.out[o][(int64_t)m * p.ldc + n] = bits[m];
+        };
+        bool wrote = false;    // this CTA finished its tile (the epilogue group agrees)
         if (p.splits == 1) {
-            if (ok && n < p.N)
-                for (int m = 0; m < p.M; ++m)
-                    p.C[(int64_t)m * p.ldc + n] = __bfloat16_as_ushort(__float2bfloat16_rn(v[m] * sc));
+            if (ok && n < p.N) write_col(v);
+            wrote = true;
         } else {
             // Every epilogue thread takes both barriers, whatever `ok` says.
             if (ok) {
@@ -237,13 +264,36 @@ gemm_e4m3_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
             if (*s_last) {
                 __threadfence();
                 const float* wt = p.ws + (int64_t)tile * p.splits * (8 * BM);
-                if (ok && n < p.N)
-                    for (int m = 0; m < p.M; ++m) {
-                        float sum = 0.0f;
-                        for (int sp = 0; sp < p.splits; ++sp) sum += __ldcg(&wt[sp * 8 * BM + m * BM + nl]);
-                        p.C[(int64_t)m * p.ldc + n] = __bfloat16_as_ushort(__float2bfloat16_rn(sum * sc));
+                if (ok && n < p.N) {
+                    float sum[8];
+#pragma unroll
+                    for (int m = 0; m < 8; ++m) {
+                        sum[m] = 0.0f;
+                        if (m < p.M)
+                            for (int sp = 0; sp < p.splits; ++sp) sum[m] += __ldcg(&wt[sp * 8 * BM + m * BM + nl]);
                     }
+                    write_col(sum);
+                }
                 if (tid == 64) p.tickets[tile] = 0u;
+                wrote = true;
+            }
+        }
+        if (p.done && wrote) {
+            // All-gather completion.  After the epilogue barrier one thread
+            // counts the tile with an acq_rel atomic at GPU scope: its release
+            // covers the group's stores (ordered before it by the barrier),
+            // and the last tile's acquire gathers every tile's.  That thread
+            // then raises this rank's flag on every rank with a system-scope
+            // release store, which the peers read with system-scope acquire
+            // loads.  (A system-scope fence per tile measured 6 us slower.)
+            named_barrier_sync(1, 128);
+            if (tid == 64) {
+                const uint32_t ntiles = gridDim.x;
+                const uint32_t t = atom_add_acq_rel_gpu_u32(p.done, 1u);
+                if (t == ntiles - 1) {
+                    for (int q = 0; q < p.nout; ++q) st_release_sys_u32(&p.flag[q][p.rank], p.epoch);
+                    *p.done = 0u;   // ready for the next call on this stream
+                }
             }
         }
     }
@@ -300,13 +350,17 @@ E4m3TcPlan gemm_e4m3_tc_plan_splits(const GemmArgs& g, int splits, int stages) {
 }
 
 E4m3TcPlan gemm_e4m3_tc_plan(const GemmArgs& g, int num_sms) {
-    // Measured on B200: several CTAs per SM with a shallow ring (3 stages,
-    // 56 KB -> 4 CTAs per SM) stream the weights faster than one CTA with a
-    // deep ring, so split K until every SM holds at least two CTAs, no more.
+    // Measured on B200 (M = 8, K = 8192, N = 3584 .. 28672): several CTAs per
+    // SM with a shallow ring stream the weights faster than one CTA with a
+    // deep ring, and the best split count puts about three CTAs on every SM
+    // (tiles x splits ~ 3 x SMs); past 4 splits a 2-stage ring is as fast.
     const int tiles = (g.N + BM - 1) / BM;
-    int s = (2 * num_sms + tiles - 1) / tiles;
+    int s = (3 * num_sms + tiles / 2) / tiles;
+    const int max_s = g.K / KB > 1 ? g.K / KB : 1;
+    if (s > 16) s = 16;
+    if (s > max_s) s = max_s;
     if (s < 1) s = 1;
-    return gemm_e4m3_tc_plan_splits(g, s, 3);
+    return gemm_e4m3_tc_plan_splits(g, s, s > 4 ? 2 : 3);
 }
 
 size_t gemm_e4m3_tc_ws_floats(const GemmArgs& g, const E4m3TcPlan& p) {
@@ -321,10 +375,13 @@ size_t gemm_e4m3_tc_act_bytes(const GemmArgs& g) {
 
 cudaError_t launch_gemm_e4m3_tc(const GemmArgs& g, const E4m3TcPlan& plan, const float* scale,
                                 float* ws, uint32_t* tickets, void* act_buf, uint32_t* err,
-                                cudaStream_t s) {
+                                cudaStream_t s, const AllGatherArgs* ag) {
     if (!gemm_e4m3_tc_supported(g) || plan.kc <= 0 || plan.stages < 2 || !act_buf)
         return cudaErrorInvalidValue;
     if (plan.splits > 1 && (!ws || !tickets)) return cudaErrorInvalidValue;
+    if (ag && (ag->world < 1 || ag->world > kMaxPeers || ag->rank < 0 || ag->rank >= ag->world ||
+               !ag->done))
+        return cudaErrorInvalidValue;
     const int kpad = (g.K + KB - 1) / KB * KB;
     uint8_t* act = static_cast<uint8_t*>(act_buf);
     float* inv_sigma = reinterpret_cast<float*>(act + 16 * static_cast<size_t>(kpad));
@@ -379,8 +436,26 @@ cudaError_t launch_gemm_e4m3_tc(const GemmArgs& g, const E4m3TcPlan& plan, const
     p.kc = plan.kc; p.splits = plan.splits; p.stages = plan.stages;
     p.inv_sigma = inv_sigma;
     p.scale = scale;
-    p.C = static_cast<uint16_t*>(g.C); p.ldc = g.ldc;
+    p.ldc = g.ldc;
     p.ws = ws; p.tickets = tickets; p.err = err;
+    for (int q = 0; q < kMaxPeers; ++q) { p.out[q] = nullptr; p.flag[q] = nullptr; }
+    if (ag) {
+        p.nout = ag->world;
+        for (int q = 0; q < ag->world; ++q) {
+            if (!ag->out[q] || !ag->flag[q]) return cudaErrorInvalidValue;
+            p.out[q] = static_cast<uint16_t*>(ag->out[q]) + static_cast<int64_t>(ag->rank) * g.N;
+            p.flag[q] = ag->flag[q];
+        }
+        p.done = ag->done;
+        p.rank = ag->rank;
+        p.epoch = ag->epoch;
+    } else {
+        p.nout = 1;
+        p.out[0] = static_cast<uint16_t*>(g.C);
+        p.done = nullptr;
+        p.rank = 0;
+        p.epoch = 0;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((g.N + BM - 1) / BM, plan.splits, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);

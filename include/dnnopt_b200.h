@@ -173,6 +173,53 @@ int dnnopt_cuda_gemm_f32_noalloc(const dnnopt_gemm_desc* d, const float* A, cons
                                  float* C, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Multi-GPU (one process per GPU).  No reference counterpart: the reference
+ * is single-process CPU code.  Config 5's weight GEMM is N-sharded over the
+ * ranks and its output all-gathered inside the GEMM kernel over peer memory.
+ * ---------------------------------------------------------------------- */
+#define DNNOPT_MAX_RANKS 8
+
+/* Device buffers another process can map: zero-filled cudaMalloc memory on
+ * the current device, its 64-byte CUDA IPC handle, and the mapping of a
+ * peer's handle into this process (peer access over NVLink). */
+int dnnopt_peer_alloc(size_t bytes, void** ptr);
+int dnnopt_peer_free(void* ptr);
+int dnnopt_ipc_handle(const void* ptr, unsigned char handle[64]);
+int dnnopt_ipc_open(const unsigned char handle[64], void** ptr);
+int dnnopt_ipc_close(void* ptr);
+
+typedef struct {
+    int world;                                /* 1 .. DNNOPT_MAX_RANKS */
+    int rank;                                 /* this process's rank */
+    void* out[DNNOPT_MAX_RANKS];              /* rank q's output [M x ldc] bf16, mapped here */
+    unsigned int* flags[DNNOPT_MAX_RANKS];    /* rank q's flag array (world words), mapped here */
+    unsigned int epoch;                       /* same on every rank; +1 per call */
+} dnnopt_allgather_desc;
+
+/* Fused N-sharded e4m3 decode-FFN GEMM + all-gather.  d->N is this rank's
+ * shard width n and d->ldc the full output row length (>= world * n); W and
+ * scale hold this rank's n weight rows.  The kernel writes the rank's columns
+ * [rank*n, rank*n + n) of bf16(scale * A W^T) into every rank's out buffer,
+ * raises flags[q][rank] = epoch on every rank q once all of them are written,
+ * and the stream then waits (bounded, 2 s) until every rank's flag has reached
+ * epoch in this rank's array: work queued after the call on `stream` sees the
+ * full [M x world*n] result in out[rank].  M <= 8.  A rank must not overwrite
+ * an out buffer that peers may still read: alternate two buffers by epoch.
+ * A flag that does not arrive in time makes dnnopt_stream_status() return
+ * DNNOPT_STATUS_KERNEL_TIMEOUT. */
+int dnnopt_cuda_gemm_e4m3bf16_allgather(const dnnopt_gemm_desc* d, const uint16_t* A,
+                                        const uint8_t* W, const float* scale,
+                                        const dnnopt_allgather_desc* ag, void* stream);
+/* The bounded wait alone: blocks `stream` until flags[q] has reached epoch
+ * for every q < world, or until timeout_us has passed (then the stream's
+ * status becomes DNNOPT_STATUS_KERNEL_TIMEOUT). */
+int dnnopt_cuda_peer_wait(const unsigned int* flags, int world, unsigned int epoch,
+                          unsigned int timeout_us, void* stream);
+/* Synchronises `stream` and reports (then clears) a bounded wait that gave up
+ * in a kernel this library queued on it. */
+int dnnopt_stream_status(void* stream);
+
+/* ------------------------------------------------------------------------
  * Runtime control
  * ---------------------------------------------------------------------- */
 /* Stream used by the dnnopt_gemm_* (host-signature) entry points on the

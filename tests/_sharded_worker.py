@@ -15,6 +15,68 @@ sys.path.insert(0, ROOT)
 PKG = os.path.join(ROOT, "dnn-opt_b200")
 
 
+class _FakeLib:
+    """Stands in for the C ABI in the fused mode's host logic: addresses are
+    per-rank integers, IPC handles carry the address, and the fused GEMM call
+    records its descriptors."""
+
+    MAX_RANKS = 8
+
+    def __init__(self, mod, rank):
+        self.mod, self.rank = mod, rank
+        self.AllGatherDesc, self.desc = mod.AllGatherDesc, mod.desc
+        self.calls, self.closed, self.freed = [], [], []
+
+    def check(self, st, what=""):
+        assert st == 0, (st, what)
+
+    def peer_alloc(self, nbytes):
+        self.nbytes = nbytes
+        return (self.rank + 1) << 40
+
+    def ipc_handle(self, address):
+        return address.to_bytes(8, "little") + bytes(56)
+
+    def ipc_open(self, handle):
+        assert len(handle) == 64
+        return int.from_bytes(handle[:8], "little")
+
+    def ipc_close(self, address):
+        self.closed.append(address)
+
+    def peer_free(self, address):
+        self.freed.append(address)
+
+    def cuda_gemm_e4m3bf16_allgather(self, d, A, W, s, ag, stream):
+        self.calls.append((d.M, d.N, d.K, d.ldc, ag.world, ag.rank, ag.epoch,
+                           [ag.out[q] for q in range(ag.world)],
+                           [ag.flags[q] for q in range(ag.world)]))
+        return 0
+
+
+def fused_host_logic(mod, rank, world) -> bool:
+    """Peer-address exchange, per-call parity and epochs of the fused mode."""
+    from dnnopt_b200.sharded import FLAG_BYTES, ShardedE4M3Gemm
+    M, N, K = 8, 128 * world * 3, 256
+    fake = _FakeLib(mod, rank)
+    sh = ShardedE4M3Gemm(dist, N, K, rank, world, mode="fused", lib=fake,
+                         view=lambda address, shape: (address, shape))
+    bases = [(q + 1) << 40 for q in range(world)]
+    ok = sh.peer_base == bases and fake.nbytes == FLAG_BYTES + 2 * 8 * N * 2
+    A = torch.zeros((M, K), dtype=torch.int16)
+    for call in range(1, 4):
+        address, shape = sh.forward_fused(A, None, None, stream=0)
+        parity = call & 1
+        m, n, k, ldc, w, r, epoch, outs, flags = fake.calls[-1]
+        ok = ok and (m, n, k, ldc, w, r, epoch) == (M, N // world, K, N, world, rank, call)
+        ok = ok and outs == [b + FLAG_BYTES + parity * 8 * N * 2 for b in bases]
+        ok = ok and flags == bases and address == outs[rank] and shape == (M, N)
+    sh.close()
+    ok = ok and sorted(fake.closed) == sorted(b for q, b in enumerate(bases) if q != rank)
+    ok = ok and fake.freed == [bases[rank]]
+    return ok
+
+
 def main() -> None:
     spec = importlib.util.spec_from_file_location("dnnopt_b200", os.path.join(PKG, "__init__.py"),
                                                   submodule_search_locations=[PKG])
@@ -26,6 +88,12 @@ def main() -> None:
 
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     dist.init_process_group("gloo", rank=rank, world_size=world)
+    if os.environ.get("MODE") == "fused":
+        ok = fused_host_logic(mod, rank, world)
+        flag = torch.tensor([1 if ok else 0])
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        dist.destroy_process_group()
+        sys.exit(0 if int(flag.item()) == 1 else 3)
     M, N, K = int(os.environ["M"]), int(os.environ["N"]), int(os.environ["K"])
     orc = Oracle()
     A = bf16_bits(np.random.default_rng(42).standard_normal(M * K).astype(np.float32))

@@ -410,6 +410,57 @@ def test_e4m3_decode_ffn(gpu, dn, orc, shape):
         check_e4m3(Ch, ref64)
 
 
+# ------------------------------------------- fused all-gather, one GPU ----
+def test_peer_wait_times_out_and_recovers(gpu, dn):
+    """A flag that nothing sets: the bounded wait gives up after its limit,
+    the stream reports KERNEL_TIMEOUT, and the device keeps working."""
+    torch = gpu
+    flags = torch.tensor([1, 0], dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream()
+    dn.check(dn.cuda_peer_wait(flags, 2, 1, 200000, s))         # 0.2 s limit
+    assert dn.stream_status(s) == dn.KERNEL_TIMEOUT
+    assert dn.stream_status(s) == dn.SUCCESS                     # cleared
+    flags[1] = 1
+    dn.check(dn.cuda_peer_wait(flags, 2, 1, 200000, s))
+    assert dn.stream_status(s) == dn.SUCCESS
+    flags[0] = 5                                                 # a later epoch also passes
+    dn.check(dn.cuda_peer_wait(flags, 2, 1, 200000, s))
+    assert dn.stream_status(s) == dn.SUCCESS
+
+
+@pytest.mark.parametrize("M,N,K", [(8, 28672, 8192), (3, 1024, 1024)])
+def test_fused_allgather_single_rank(gpu, dn, orc, M, N, K):
+    """world = 1: the fused entry point writes the same bits as the plain
+    e4m3 GEMM, in alternating buffers, and raises its own flag each call."""
+    torch = gpu
+    A, q, s = e4m3_problem(orc, M, N, K)
+    dA = torch.from_numpy(A.view(np.int16)).cuda()
+    dW, ds = torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()
+    st = torch.cuda.current_stream()
+    plain = torch.zeros(M * N, dtype=torch.int16, device="cuda")
+    dn.check(dn.cuda_gemm("e4m3bf16", dn.desc(M, N, K, K, K, N), dA, dW, plain, st, scale=ds))
+    out_bytes = 8 * N * 2
+    base = dn.peer_alloc(256 + 2 * out_bytes)
+    try:
+        for epoch in (1, 2, 3):
+            ag = dn.AllGatherDesc()
+            ag.world, ag.rank, ag.epoch = 1, 0, epoch
+            ag.out[0] = base + 256 + (epoch & 1) * out_bytes
+            ag.flags[0] = base
+            dn.check(dn.cuda_gemm_e4m3bf16_allgather(dn.desc(M, N, K, K, K, N), dA, dW, ds, ag, st))
+            assert dn.stream_status(st) == dn.SUCCESS
+            got = torch.empty(M * N, dtype=torch.int16, device="cuda")
+            from dnnopt_b200.sharded import _cuda_view
+            got.copy_(_cuda_view(ag.out[0], (M * N,)))
+            flag_now = _cuda_view(base, (2,)).view(torch.int32)[0].item()
+            torch.cuda.synchronize()
+            assert torch.equal(got, plain), epoch
+            assert flag_now == epoch
+    finally:
+        torch.cuda.synchronize()
+        dn.peer_free(base)
+
+
 # -------------------------------------------------------- runtime paths ----
 def test_plan_selection_on_device(gpu, dn):
     assert dn.plan_describe(dn.KIND_F32, dn.desc(1, 4096, 4096, 4096, 4096, 4096)).startswith(

@@ -31,10 +31,9 @@ def test_shard_bounds(dn):
         shard_bounds(10, 0)
 
 
-@pytest.mark.parametrize("world,N", [(2, 512), (4, 1024)])
-def test_sharded_allgather_matches_single_process(dn, world, N):
+def _run_ranks(world, **extra):
     env = dict(os.environ, MASTER_ADDR="127.0.0.1", MASTER_PORT=str(_free_port()),
-               WORLD_SIZE=str(world), M="8", N=str(N), K="256", CUDA_VISIBLE_DEVICES="")
+               WORLD_SIZE=str(world), CUDA_VISIBLE_DEVICES="", **extra)
     procs = [subprocess.Popen([sys.executable, os.path.join(ROOT, "tests", "_sharded_worker.py")],
                               env=dict(env, RANK=str(r)), stdout=subprocess.PIPE,
                               stderr=subprocess.STDOUT, text=True) for r in range(world)]
@@ -48,6 +47,19 @@ def test_sharded_allgather_matches_single_process(dn, world, N):
         outs.append(out)
     codes = [p.returncode for p in procs]
     assert codes == [0] * world, (codes, outs)
+
+
+@pytest.mark.parametrize("world,N", [(2, 512), (4, 1024)])
+def test_sharded_allgather_matches_single_process(dn, world, N):
+    _run_ranks(world, M="8", N=str(N), K="256")
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_fused_mode_host_logic(dn, world):
+    """Fused mode: IPC-handle exchange maps every rank's buffer, each call
+    alternates output buffers by parity and carries the next epoch, close()
+    unmaps the peers and frees the own buffer."""
+    _run_ranks(world, MODE="fused")
 
 
 def test_uneven_split_rejected(dn):
