@@ -251,6 +251,14 @@ def capture(torch, stream, fn):
     return g
 
 
+# DRAM bytes (read + write) of one C2 sweep, summed over its 12 launches, from
+# one ncu capture:  ncu --clock-control none --metrics
+# dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum --csv
+# -k regex:gemv -s 12 -c 12 python bench.py --profile c2 --reps 2
+# (C is written into L2 and leaves it after the launch, so writes read 0).
+C2_DRAM_BYTES_PER_STEP = 117_940_000
+
+
 def bench_single(torch, dn, stream, fn_list, bytes_per_call, flops_per_call, iters=30):
     """Per-call device time of rotating calls: one CUDA graph holds 4 rounds
     over `fn_list` (so graph-launch overhead is amortised), replayed `iters`
@@ -516,8 +524,10 @@ def run_gpu_arm(args):
     # Dominant kernel: the split-K GEMV, all 12 launches of a step.
     achieved = bytes_step / (ms * 1e-3) / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / pk["hbm_gbs"], "traffic": None,
-                "kernel": "gemv_kn_kernel (12 launches per step, algorithmic bytes / step time)",
+                "frac": achieved / pk["hbm_gbs"], "traffic": C2_DRAM_BYTES_PER_STEP,
+                "traffic_unit": "bytes per step (12 launches), ncu dram__bytes_read.sum + dram__bytes_write.sum",
+                "algorithmic_bytes_per_step": bytes_step,
+                "kernel": "gemv_slab_kernel (12 launches per step, algorithmic bytes / step time)",
                 "peak_source": pk["source"]}
 
     # e2e: reference-signature host API, pinned host buffers, copies inside.
