@@ -108,7 +108,7 @@ int launch_plan(Kind kind, const GemmArgs& g, const Plan& p, const float* scales
             note_launch();
             break;
         case KernelId::GemvSlab:
-            e = launch_gemv_slab(in_a(kind), in_b(kind), g, p.kn.mt, s);
+            e = launch_gemv_slab(in_a(kind), in_b(kind), g, p.kn.mt, p.slab_w, s);
             note_launch();
             break;
         case KernelId::GemvNk:
@@ -219,10 +219,13 @@ Plan get_plan(Kind kind, const GemmArgs& g, DeviceContext* ctx, cudaStream_t s,
     Plan cands[kMaxCands];
     int nc = 0;
     if (is_kn(h.kernel)) {
-        Plan slab = h;
-        slab.kernel = KernelId::GemvSlab;
-        slab.kn = kn_plan_for(kind, g, info, 0, false);
-        cands[nc++] = slab;
+        for (int w : {8, 16}) {
+            Plan slab = h;
+            slab.kernel = KernelId::GemvSlab;
+            slab.kn = kn_plan_for(kind, g, info, 0, false);
+            slab.slab_w = w;
+            cands[nc++] = slab;
+        }
         const GemvKnPlan ws_plan = kn_plan_for(kind, g, info, 0, false);
         const int tries[6] = {h.kn.splits, h.kn.splits / 2, h.kn.splits * 2, 1,
                               ws_plan.splits, ws_plan.splits * 2};

@@ -33,9 +33,6 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kSlabW = 8;                     // columns per CTA
-constexpr int kRowsPerLoad = 32 / kSlabW;     // rows one warp load covers
-constexpr int kRowStep = kWarps * kRowsPerLoad;   // rows one CTA-wide load covers (32)
 constexpr int kBatch = 16;                    // rows per register batch (2 batches in flight)
 constexpr int kPassRows = 1024;               // K rows of A staged per pass
 
@@ -43,11 +40,14 @@ struct SlabParams {
     GemmArgs g;
 };
 
-template <In IA, In IB, int MT>
+template <In IA, In IB, int MT, int W>
 __global__ void __launch_bounds__(kThreads)
 gemv_slab_kernel(const SlabParams p) {
     using TA = typename Elem<IA>::T;
     using TB = typename Elem<IB>::T;
+    constexpr int kSlabW = W;                       // columns per CTA (8 or 16)
+    constexpr int kRowsPerLoad = 32 / kSlabW;       // rows one warp load covers
+    constexpr int kRowStep = kWarps * kRowsPerLoad; // rows one CTA-wide load covers
     extern __shared__ __align__(16) float sA[];          // [pass rows][MT]
     __shared__ float red[kWarps][MT][kSlabW];
 
@@ -161,11 +161,11 @@ gemv_slab_kernel(const SlabParams p) {
         }
     }
 
-    // Lanes l, l^8, l^16, l^24 hold the same column: fixed shuffle tree.
+    // Lanes l, l + W, ... hold the same column: fixed shuffle tree.
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
-        acc[m] += __shfl_xor_sync(0xFFFFFFFFu, acc[m], 8);
-        acc[m] += __shfl_xor_sync(0xFFFFFFFFu, acc[m], 16);
+#pragma unroll
+        for (int o = kSlabW; o < 32; o <<= 1) acc[m] += __shfl_xor_sync(0xFFFFFFFFu, acc[m], o);
     }
     if (rsub == 0) {
 #pragma unroll
@@ -181,27 +181,29 @@ gemv_slab_kernel(const SlabParams p) {
 }
 
 template <In IA, In IB, int MT>
-const void* slab_fn() {
-    return reinterpret_cast<const void*>(&gemv_slab_kernel<IA, IB, MT>);
+const void* slab_fn(int w) {
+    return w == 16 ? reinterpret_cast<const void*>(&gemv_slab_kernel<IA, IB, MT, 16>)
+                   : reinterpret_cast<const void*>(&gemv_slab_kernel<IA, IB, MT, 8>);
 }
 
 template <In IA, In IB>
-const void* slab_select_mt(int mt) {
+const void* slab_select_mt(int mt, int w) {
     switch (mt) {
-        case 1: return slab_fn<IA, IB, 1>();
-        case 2: return slab_fn<IA, IB, 2>();
-        case 4: return slab_fn<IA, IB, 4>();
-        case 8: return slab_fn<IA, IB, 8>();
+        case 1: return slab_fn<IA, IB, 1>(w);
+        case 2: return slab_fn<IA, IB, 2>(w);
+        case 4: return slab_fn<IA, IB, 4>(w);
+        case 8: return slab_fn<IA, IB, 8>(w);
         default: return nullptr;
     }
 }
 
-const void* slab_select(In ia, In ib, int mt) {
-    if (ia == In::F32 && ib == In::F32) return slab_select_mt<In::F32, In::F32>(mt);
-    if (ia == In::BF16 && ib == In::BF16) return slab_select_mt<In::BF16, In::BF16>(mt);
-    if (ia == In::F32R && ib == In::F32R) return slab_select_mt<In::F32R, In::F32R>(mt);
-    if (ia == In::RE4 && ib == In::RE5) return slab_select_mt<In::RE4, In::RE5>(mt);
-    if (ia == In::RE5 && ib == In::RE5) return slab_select_mt<In::RE5, In::RE5>(mt);
+const void* slab_select(In ia, In ib, int mt, int w) {
+    if (w != 8 && w != 16) return nullptr;
+    if (ia == In::F32 && ib == In::F32) return slab_select_mt<In::F32, In::F32>(mt, w);
+    if (ia == In::BF16 && ib == In::BF16) return slab_select_mt<In::BF16, In::BF16>(mt, w);
+    if (ia == In::F32R && ib == In::F32R) return slab_select_mt<In::F32R, In::F32R>(mt, w);
+    if (ia == In::RE4 && ib == In::RE5) return slab_select_mt<In::RE4, In::RE5>(mt, w);
+    if (ia == In::RE5 && ib == In::RE5) return slab_select_mt<In::RE5, In::RE5>(mt, w);
     return nullptr;
 }
 
@@ -212,24 +214,22 @@ size_t slab_smem_bytes(int mt, int K) {
 
 }  // namespace
 
-int gemv_slab_width() { return kSlabW; }
+int gemv_slab_ctas(int N, int w) { return (N + w - 1) / w; }
 
-int gemv_slab_ctas(int N) { return (N + kSlabW - 1) / kSlabW; }
-
-cudaError_t gemv_slab_occupancy(In ia, In ib, int mt, int K, int* blocks_per_sm) {
-    const void* fn = slab_select(ia, ib, mt);
+cudaError_t gemv_slab_occupancy(In ia, In ib, int mt, int w, int K, int* blocks_per_sm) {
+    const void* fn = slab_select(ia, ib, mt, w);
     if (!fn) return cudaErrorInvalidValue;
     return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, fn, kThreads,
                                                          slab_smem_bytes(mt, K));
 }
 
-cudaError_t launch_gemv_slab(In ia, In ib, const GemmArgs& g, int mt, cudaStream_t s) {
-    const void* fn = slab_select(ia, ib, mt);
+cudaError_t launch_gemv_slab(In ia, In ib, const GemmArgs& g, int mt, int w, cudaStream_t s) {
+    const void* fn = slab_select(ia, ib, mt, w);
     if (!fn || g.M > mt || g.M < 1 || g.N < 1 || g.K < 1) return cudaErrorInvalidValue;
     SlabParams sp;
     sp.g = g;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(gemv_slab_ctas(g.N)), 1, 1);
+    cfg.gridDim = dim3(static_cast<unsigned>(gemv_slab_ctas(g.N, w)), 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = slab_smem_bytes(mt, g.K);
     cfg.stream = s;

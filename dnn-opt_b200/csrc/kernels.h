@@ -59,12 +59,12 @@ cudaError_t launch_gemv_kn_cluster(In ia, In ib, const GemmArgs& g, const GemvKn
                                    cudaStream_t s);
 
 // ---- small-M column-slab GEMV, B is K x N -----------------------------------
-// One CTA per 8 consecutive columns over the whole K extent (reduced inside
-// the CTA: no workspace).  Launched with programmatic dependent launch.
-int gemv_slab_width();
-int gemv_slab_ctas(int N);
-cudaError_t gemv_slab_occupancy(In ia, In ib, int mt, int K, int* blocks_per_sm);
-cudaError_t launch_gemv_slab(In ia, In ib, const GemmArgs& g, int mt, cudaStream_t s);
+// One CTA per 8 or 16 consecutive columns over the whole K extent (reduced
+// inside the CTA: no workspace).  Launched with programmatic dependent launch.
+// `w` = columns per CTA (8 or 16).
+int gemv_slab_ctas(int N, int w);
+cudaError_t gemv_slab_occupancy(In ia, In ib, int mt, int w, int K, int* blocks_per_sm);
+cudaError_t launch_gemv_slab(In ia, In ib, const GemmArgs& g, int mt, int w, cudaStream_t s);
 
 // ---- small-M dot-form GEMV, B is N x K (K contiguous) ----------------------
 enum class DotKind : int {

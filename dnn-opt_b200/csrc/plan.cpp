@@ -78,6 +78,16 @@ int kn_occupancy(Kind kind, int mt, int vec4, const DeviceInfo& info) {
     return occ;
 }
 
+int slab_occupancy(Kind kind, int mt, int w, int K, const DeviceInfo& info) {
+    if (!info.have_device) return 8;   // no device: plan names only, 8-column slabs
+    int occ = 0;
+    if (gemv_slab_occupancy(in_a(kind), in_b(kind), mt, w, K, &occ) != cudaSuccess || occ < 1) {
+        cudaGetLastError();
+        occ = 1;
+    }
+    return occ;
+}
+
 int rows_occupancy(DotKind kind, int mt, int K, const DeviceInfo& info) {
     if (!info.have_device) return 4;
     int occ = 0;
@@ -232,7 +242,13 @@ Plan heuristic_plan(Kind kind, const GemmArgs& g, const DeviceInfo& info) {
         p.kernel = p.kn.cluster ? KernelId::GemvKnCluster : KernelId::GemvKn;
         // Measured on B200 (M <= 8, K = 1024, prime N of 1009-4093): the slab
         // form finishes in 0.4-0.8x the split-K time; at K = 4096 split-K wins.
-        if (g.K <= 2048 && g.N >= 512 && g.N <= 8192) p.kernel = KernelId::GemvSlab;
+        // 16-column slabs when 8-column ones would need more than one wave of
+        // resident CTAs (7 x 4093: 10.7 -> 8.5 us); 8 otherwise.
+        if (g.K <= 2048 && g.N >= 512 && g.N <= 8192) {
+            p.kernel = KernelId::GemvSlab;
+            const int occ8 = slab_occupancy(kind, p.kn.mt, 8, g.K, info);
+            p.slab_w = gemv_slab_ctas(g.N, 8) > occ8 * info.num_sms ? 16 : 8;
+        }
         return p;
     }
     if (kind == Kind::F32 && g.M <= 8 && g.b_trans && gemv_rows_supported(DotKind::F32, g)) {
@@ -275,8 +291,8 @@ std::string describe_plan(Kind, const GemmArgs& g, const Plan& p) {
                           p.e4.splits, p.e4.kc, p.e4.stages);
             break;
         case KernelId::GemvSlab:
-            std::snprintf(buf, sizeof(buf), "%s mt=%d ctas=%d%s", kernel_name(p.kernel), p.kn.mt,
-                          gemv_slab_ctas(g.N), p.tuned ? " tuned" : "");
+            std::snprintf(buf, sizeof(buf), "%s mt=%d w=%d ctas=%d%s", kernel_name(p.kernel), p.kn.mt,
+                          p.slab_w, gemv_slab_ctas(g.N, p.slab_w), p.tuned ? " tuned" : "");
             break;
         default:
             std::snprintf(buf, sizeof(buf), "%s", kernel_name(p.kernel));
@@ -337,8 +353,10 @@ bool cache_lookup(uint64_t key, Plan* out) {
     const Entry& e = it->second;
     out->kernel = static_cast<KernelId>(e.kernel);
     out->tuned = true;
-    if (out->kernel == KernelId::GemvKn || out->kernel == KernelId::GemvKnCluster ||
-        out->kernel == KernelId::GemvSlab) {
+    if (out->kernel == KernelId::GemvSlab) {
+        out->slab_w = e.p0 == 16 ? 16 : 8;
+        out->kn.mt = e.mt;
+    } else if (out->kernel == KernelId::GemvKn || out->kernel == KernelId::GemvKnCluster) {
         out->kn.splits = e.p0;
         out->kn.kchunk = e.p1;
         out->kn.mt = e.mt;
@@ -357,8 +375,9 @@ bool cache_lookup(uint64_t key, Plan* out) {
 void cache_store(uint64_t key, const Plan& p, float time_us) {
     Entry e;
     e.kernel = static_cast<int32_t>(p.kernel);
-    if (p.kernel == KernelId::GemvKn || p.kernel == KernelId::GemvKnCluster ||
-        p.kernel == KernelId::GemvSlab) {
+    if (p.kernel == KernelId::GemvSlab) {
+        e.p0 = p.slab_w; e.p1 = 0; e.mt = p.kn.mt;
+    } else if (p.kernel == KernelId::GemvKn || p.kernel == KernelId::GemvKnCluster) {
         e.p0 = p.kn.splits; e.p1 = p.kn.kchunk; e.mt = p.kn.mt;
     } else if (p.kernel == KernelId::E4m3Tc) {
         e.p0 = p.e4.splits; e.p1 = p.e4.kc; e.mt = p.e4.stages;

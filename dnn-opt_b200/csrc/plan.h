@@ -41,6 +41,7 @@ struct Plan {
     GemvKnPlan kn{};
     GemvNkPlan nk{};
     E4m3TcPlan e4{};
+    int slab_w = 8;      // GemvSlab: columns per CTA (8 or 16)
     bool tuned = false;
 };
 

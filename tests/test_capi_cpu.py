@@ -129,9 +129,9 @@ def test_plan_selection_without_device(dn):
     assert s.startswith("gemv_kn_splitk mt=1 vec4=1"), s
     # The irregular-N sweep (K = 1024): whole-K column slabs, no split-K reduction.
     s = dn.plan_describe(dn.KIND_F32, dn.desc(7, 4093, 1024, 1024, 4093, 4093, beta=0.5))
-    assert s == "gemv_kn_slab mt=8 ctas=512", s
+    assert s == "gemv_kn_slab mt=8 w=8 ctas=512", s
     s = dn.plan_describe(dn.KIND_F32, dn.desc(2, 1009, 1024, 1024, 1009, 1009))
-    assert s == "gemv_kn_slab mt=2 ctas=127", s
+    assert s == "gemv_kn_slab mt=2 w=8 ctas=127", s
     # Deeper K: split-K, one wave of resident CTAs, at most 16 splits.
     s = dn.plan_describe(dn.KIND_F32, dn.desc(7, 4093, 4096, 4096, 4093, 4093, beta=0.5))
     assert s.startswith("gemv_kn_splitk mt=8 vec4=0 splits=13 kchunk=320"), s   # prime N: scalar loads

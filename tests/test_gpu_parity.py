@@ -512,22 +512,26 @@ def _force_plan(dn, tmp_path, name, kind, M, N, K, lda, ldb, ldc, ta, tb, vec, e
 # outside its heuristic range (tiny N, K over several 1024-row passes, K not a
 # multiple of the 32-row step, transposed A, padded C).
 @pytest.mark.parametrize("M,N,K,alpha,beta,ta,ldc,force", [
-    (2, 1009, 1024, 1.0, 0.5, 0, None, False), (7, 4093, 1024, 1.0, 0.5, 0, None, False),
-    (5, 2039, 1000, 2.0, 0.0, 0, None, False), (8, 600, 2048, 1.0, -1.0, 0, 604, False),
-    (1, 7, 5, 1.0, 0.5, 0, None, True), (3, 100, 3000, 1.0, 0.25, 0, None, True),
-    (4, 520, 1030, 0.5, 0.5, 1, None, True), (6, 9000, 33, 1.0, 0.0, 0, None, True),
-    (1, 1024, 4097, 1.0, 0.5, 1, 1030, True)])
+    (2, 1009, 1024, 1.0, 0.5, 0, None, 0), (7, 4093, 1024, 1.0, 0.5, 0, None, 0),
+    (5, 2039, 1000, 2.0, 0.0, 0, None, 0), (8, 600, 2048, 1.0, -1.0, 0, 604, 0),
+    (1, 7, 5, 1.0, 0.5, 0, None, 8), (3, 100, 3000, 1.0, 0.25, 0, None, 8),
+    (4, 520, 1030, 0.5, 0.5, 1, None, 8), (6, 9000, 33, 1.0, 0.0, 0, None, 8),
+    (1, 1024, 4097, 1.0, 0.5, 1, 1030, 8), (1, 7, 5, 1.0, 0.5, 0, None, 16),
+    (3, 100, 3000, 1.0, 0.25, 0, None, 16), (7, 4093, 1024, 1.0, 0.5, 1, 4100, 16),
+    (8, 1030, 2000, 1.0, 0.0, 0, None, 16)])
 def test_slab_kernel(gpu, dn, orc, tmp_path, M, N, K, alpha, beta, ta, ldc, force):
+    """force = 0: heuristic plan (must be the slab kernel); 8 / 16: slab width
+    forced through an autotune-cache entry."""
     ldc = ldc or N
     lda = M if ta else K
     mt = 1 if M <= 1 else 2 if M <= 2 else 4 if M <= 4 else 8
     vec = 1 if N % 4 == 0 else 0
     if force:
-        _force_plan(dn, tmp_path, f"slab_{M}_{N}_{K}.bin", 0, M, N, K, lda, N, ldc, ta, 0, vec,
-                    (9, 0, 0, mt))
+        _force_plan(dn, tmp_path, f"slab_{M}_{N}_{K}_{force}.bin", 0, M, N, K, lda, N, ldc, ta, 0, vec,
+                    (9, force, 0, mt))
     else:
         assert dn.plan_describe(dn.KIND_F32, dn.desc(M, N, K, lda, N, ldc, alpha, beta, ta, 0)) \
-            == f"gemv_kn_slab mt={mt} ctas={(N + 7) // 8}"
+            .startswith(f"gemv_kn_slab mt={mt} w=")
     A, B = ref_uniform(M * K, 11), ref_uniform(K * N, 12)   # A is K x M when ta
     C0 = ref_uniform(M * ldc, 13)
     Ar = np.ascontiguousarray(A.reshape(K, M).T).reshape(-1) if ta else A
