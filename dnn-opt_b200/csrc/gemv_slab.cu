@@ -40,24 +40,20 @@ struct SlabParams {
     GemmArgs g;
 };
 
+// One slab (columns [slab*W, slab*W + W) of one GEMM) computed by the whole
+// CTA.  sA: dynamic shared memory of at least MT * min(K, kPassRows) floats.
 template <In IA, In IB, int MT, int W>
-__global__ void __launch_bounds__(kThreads)
-gemv_slab_kernel(const SlabParams p) {
+__device__ __forceinline__ void slab_body(const GemmArgs& g, int slab, float* sA,
+                                          float (&red)[kWarps][MT][W]) {
     using TA = typename Elem<IA>::T;
     using TB = typename Elem<IB>::T;
     constexpr int kSlabW = W;                       // columns per CTA (8 or 16)
     constexpr int kRowsPerLoad = 32 / kSlabW;       // rows one warp load covers
     constexpr int kRowStep = kWarps * kRowsPerLoad; // rows one CTA-wide load covers
-    extern __shared__ __align__(16) float sA[];          // [pass rows][MT]
-    __shared__ float red[kWarps][MT][kSlabW];
 
-    pdl_wait();
-    pdl_launch_dependents();
-
-    const GemmArgs& g = p.g;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int col = lane % kSlabW, rsub = lane / kSlabW;
-    const int n0 = blockIdx.x * kSlabW;
+    const int n0 = slab * kSlabW;
     const bool col_ok = n0 + col < g.N;
     const TA* A = static_cast<const TA*>(g.A);
     const TB* B = static_cast<const TB*>(g.B) + n0 + col;
@@ -178,6 +174,16 @@ gemv_slab_kernel(const SlabParams p) {
         for (int w = 0; w < kWarps; ++w) sum += red[w][wm][wc];
         C[(int64_t)wm * g.ldc + n0 + wc] = (g.beta == 0.0f) ? g.alpha * sum : fmaf(g.alpha, sum, g.beta * c_old);
     }
+}
+
+template <In IA, In IB, int MT, int W>
+__global__ void __launch_bounds__(kThreads)
+gemv_slab_kernel(const SlabParams p) {
+    extern __shared__ __align__(16) float sA[];          // [pass rows][MT]
+    __shared__ float red[kWarps][MT][W];
+    pdl_wait();
+    pdl_launch_dependents();
+    slab_body<IA, IB, MT, W>(p.g, blockIdx.x, sA, red);
 }
 
 template <In IA, In IB, int MT>
