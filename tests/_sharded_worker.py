@@ -77,6 +77,31 @@ def fused_host_logic(mod, rank, world) -> bool:
     return ok
 
 
+def dead_rank(rank, world) -> int:
+    """The last rank joins the group and leaves before the all-gather (between
+    calls, with nothing in flight); every other rank must get an error from
+    the collective within the short process-group timeout instead of hanging.
+    Exit 0 = this rank behaved as expected."""
+    import datetime
+    from dnnopt_b200.sharded import ShardedE4M3Gemm
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    if rank == world - 1:
+        return 0                      # leaves without a word
+    M, N, K = 2, 128 * world, 64
+
+    def compute(A_t, W_t, s_t, C_t):
+        C_t.zero_()
+
+    sh = ShardedE4M3Gemm(dist, N, K, rank, world, compute=compute)
+    try:
+        sh.forward(torch.zeros((M, K), dtype=torch.int16), None, None)
+    except Exception as e:            # gloo: connection closed or timed out
+        print(f"rank {rank}: peer loss detected: {type(e).__name__}", flush=True)
+        return 0
+    return 3
+
+
 def main() -> None:
     spec = importlib.util.spec_from_file_location("dnnopt_b200", os.path.join(PKG, "__init__.py"),
                                                   submodule_search_locations=[PKG])
@@ -87,6 +112,8 @@ def main() -> None:
     from oracle.oracle import Oracle, bf16_bits
 
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    if os.environ.get("MODE") == "dead_rank":
+        sys.exit(dead_rank(rank, world))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     if os.environ.get("MODE") == "fused":
         ok = fused_host_logic(mod, rank, world)

@@ -62,6 +62,13 @@ def test_fused_mode_host_logic(dn, world):
     _run_ranks(world, MODE="fused")
 
 
+@pytest.mark.parametrize("world", [2, 3])
+def test_dead_rank_detected(dn, world):
+    """Failure detection on the host: a rank that leaves between calls makes
+    the others' next all-gather fail within the process-group timeout."""
+    _run_ranks(world, MODE="dead_rank")
+
+
 def test_uneven_split_rejected(dn):
     from dnnopt_b200.sharded import ShardedE4M3Gemm
     with pytest.raises(ValueError):
