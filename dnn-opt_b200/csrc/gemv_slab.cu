@@ -23,6 +23,10 @@
 //     vector loads;
 //   * lanes of a column reduce with two shuffles, warps through shared memory
 //     in warp order: the result is deterministic.
+#include <mutex>
+#include <set>
+#include <utility>
+
 #include "common.cuh"
 #include "elem.cuh"
 #include "kernels.h"
@@ -229,9 +233,43 @@ cudaError_t gemv_slab_occupancy(In ia, In ib, int mt, int w, int K, int* blocks_
                                                          slab_smem_bytes(mt, K));
 }
 
+// Shared-memory carveout: just enough for the register-limited number of
+// CTAs per SM at the kernel's largest footprint (K >= kPassRows), the rest
+// stays L1.  Measured on B200: the default split can hold fewer CTAs than the
+// registers allow (start times spread over a second wave), while the largest
+// split leaves so little L1 that far fewer loads stay in flight (2-3x
+// slower).  Set once per device and kernel.
+cudaError_t set_carveout(const void* fn, int mt) {
+    static std::mutex mu;
+    static std::set<std::pair<int, const void*>> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(mu);
+    if (done.count({dev, fn})) return cudaSuccess;
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, fn);
+    if (e != cudaSuccess) return e;
+    int occ = 0;
+    const size_t dyn = slab_smem_bytes(mt, kPassRows);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kThreads, dyn);
+    if (e != cudaSuccess) return e;
+    int smem_per_sm = 0;
+    e = cudaDeviceGetAttribute(&smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    if (e != cudaSuccess) return e;
+    const size_t need = static_cast<size_t>(occ > 0 ? occ : 1) * (dyn + fa.sharedSizeBytes + 1024);
+    int pct = static_cast<int>((need * 100 + smem_per_sm - 1) / static_cast<size_t>(smem_per_sm)) + 2;
+    if (pct > 100) pct = 100;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, pct);
+    if (e == cudaSuccess) done.insert({dev, fn});
+    return e;
+}
+
 cudaError_t launch_gemv_slab(In ia, In ib, const GemmArgs& g, int mt, int w, cudaStream_t s) {
     const void* fn = slab_select(ia, ib, mt, w);
     if (!fn || g.M > mt || g.M < 1 || g.N < 1 || g.K < 1) return cudaErrorInvalidValue;
+    cudaError_t pe = set_carveout(fn, mt);
+    if (pe != cudaSuccess) return pe;
     SlabParams sp;
     sp.g = g;
     cudaLaunchConfig_t cfg = {};
