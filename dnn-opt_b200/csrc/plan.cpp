@@ -22,6 +22,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <functional>
 #include <map>
 #include <mutex>
 
@@ -78,34 +79,50 @@ int kn_occupancy(Kind kind, int mt, int vec4, const DeviceInfo& info) {
     return occ;
 }
 
-int slab_occupancy(Kind kind, int mt, int w, int K, const DeviceInfo& info) {
-    if (!info.have_device) return 8;   // no device: plan names only, 8-column slabs
+// Occupancy queries are memoised: the planner runs on every call, and the
+// CUDA occupancy calculator costs microseconds.  Keys hold everything the
+// answer depends on (kernel template arguments and the shared-memory size,
+// which is set by K up to the kernels' pass length).
+int memo_occupancy(int64_t key, const std::function<cudaError_t(int*)>& query) {
+    static std::mutex mu;
+    static std::map<int64_t, int> memo;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); return 1; }
+    key = key * 64 + dev;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = memo.find(key);
+        if (it != memo.end()) return it->second;
+    }
     int occ = 0;
-    if (gemv_slab_occupancy(in_a(kind), in_b(kind), mt, w, K, &occ) != cudaSuccess || occ < 1) {
+    if (query(&occ) != cudaSuccess || occ < 1) {
         cudaGetLastError();
         occ = 1;
     }
+    std::lock_guard<std::mutex> lk(mu);
+    memo[key] = occ;
     return occ;
+}
+
+int slab_occupancy(Kind kind, int mt, int w, int K, const DeviceInfo& info) {
+    if (!info.have_device) return 8;   // no device: plan names only, 8-column slabs
+    const int kk = K < 1024 ? K : 1024;
+    const int64_t key = ((static_cast<int64_t>(kind) * 16 + mt) * 32 + w) * 2048 + kk;
+    return memo_occupancy(key * 4 + 1, [&](int* occ) {
+        return gemv_slab_occupancy(in_a(kind), in_b(kind), mt, w, K, occ);
+    });
 }
 
 int rows_occupancy(DotKind kind, int mt, int K, const DeviceInfo& info) {
     if (!info.have_device) return 4;
-    int occ = 0;
-    if (gemv_rows_occupancy(kind, mt, K, &occ) != cudaSuccess || occ < 1) {
-        cudaGetLastError();
-        occ = 1;
-    }
-    return occ;
+    const int64_t key = (static_cast<int64_t>(kind) * 16 + mt) * (int64_t{1} << 31) + K;
+    return memo_occupancy(key * 4 + 2, [&](int* occ) { return gemv_rows_occupancy(kind, mt, K, occ); });
 }
 
 int nk_occupancy(DotKind kind, int mt, int vec, int K, const DeviceInfo& info) {
     if (!info.have_device) return 2;
-    int occ = 0;
-    if (gemv_nk_occupancy(kind, mt, vec, K, &occ) != cudaSuccess || occ < 1) {
-        cudaGetLastError();
-        occ = 1;
-    }
-    return occ;
+    const int64_t key = ((static_cast<int64_t>(kind) * 16 + mt) * 2 + vec) * (int64_t{1} << 31) + K;
+    return memo_occupancy(key * 4 + 3, [&](int* occ) { return gemv_nk_occupancy(kind, mt, vec, K, occ); });
 }
 
 }  // namespace
