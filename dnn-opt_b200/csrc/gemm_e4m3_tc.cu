@@ -158,8 +158,6 @@ gemm_e4m3_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-    pdl_wait();          // the activation operand comes from the prep kernel
-
     auto issue = [&](int kb, int s) {
         mbar_arrive_expect_tx(&full[s], kStage);
         tma_load_2d(sStage + s * kStage, &tmW, &full[s], k0 + kb * KB, n0);
@@ -173,8 +171,20 @@ gemm_e4m3_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
         fence_mbar_init();
         prefetch_tmap(&tmW);
         prefetch_tmap(&tmAct);
-        for (int kb = 0; kb < pre; ++kb) issue(kb, kb);
+        // The first ring of weights goes out before griddepcontrol.wait: the
+        // prep kernel does not write them, and every kernel before the prep
+        // kernel has completed when this grid starts (the prep kernel
+        // releases it only after its own wait).  The weight stream thus
+        // overlaps the prep kernel.
+        for (int kb = 0; kb < pre; ++kb) {
+            mbar_arrive_expect_tx(&full[kb], kStage);
+            tma_load_2d(sStage + kb * kStage, &tmW, &full[kb], k0 + kb * KB, n0);
+        }
     }
+    pdl_wait();          // the activation operand and 1/s come from the prep kernel
+    if (tid == 0)
+        for (int kb = 0; kb < pre; ++kb)
+            tma_load_2d(sStage + kb * kStage + kWStage, &tmAct, &full[kb], k0 + kb * KB, 0);
     if (warp == 1) {
         tmem_alloc(tmem_slot, 32);
         tmem_relinquish();
