@@ -63,7 +63,8 @@ class AllGatherDesc(ctypes.Structure):
         ("world", ctypes.c_int), ("rank", ctypes.c_int),
         ("out", ctypes.c_void_p * MAX_RANKS),
         ("flags", ctypes.c_void_p * MAX_RANKS),
-        ("epoch", ctypes.c_uint),
+        ("seq", ctypes.c_void_p),
+        ("out_stride", ctypes.c_size_t),
     ]
 
 

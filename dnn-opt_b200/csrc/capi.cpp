@@ -646,7 +646,8 @@ int dnnopt_ipc_close(void* ptr) {
 int dnnopt_cuda_gemm_e4m3bf16_allgather(const dnnopt_gemm_desc* d, const uint16_t* A,
                                         const uint8_t* W, const float* scale,
                                         const dnnopt_allgather_desc* ag, void* stream) {
-    if (!ag || ag->world < 1 || ag->world > DNNOPT_MAX_RANKS || ag->rank < 0 || ag->rank >= ag->world)
+    if (!ag || ag->world < 1 || ag->world > DNNOPT_MAX_RANKS || ag->rank < 0 || ag->rank >= ag->world ||
+        !ag->seq || ag->out_stride % 2 != 0)
         return set_status(DNNOPT_STATUS_INVALID_VALUE);
     for (int q = 0; q < ag->world; ++q)
         if (!ag->out[q] || !ag->flags[q]) return set_status(DNNOPT_STATUS_INVALID_VALUE);
@@ -678,11 +679,13 @@ int dnnopt_cuda_gemm_e4m3bf16_allgather(const dnnopt_gemm_desc* d, const uint16_
         a.flag[q] = q < ag->world ? ag->flags[q] : nullptr;
     }
     a.done = w->counters + tiles;      // the tile tickets occupy counters[0, tiles)
-    a.epoch = ag->epoch;
+    a.seq = ag->seq;
+    a.out_stride_elems = static_cast<int64_t>(ag->out_stride / 2);
     cudaError_t e = launch_gemm_e4m3_tc(g, p.e4, scale, w->ws, w->counters, w->quant, w->err, s, &a);
     note_launch(2);
     if (e == cudaSuccess) {
-        e = launch_peer_wait(ag->flags[ag->rank], ag->world, ag->epoch, 2000000000ull /* 2 s */, w->err, s);
+        e = launch_peer_wait(ag->flags[ag->rank], ag->world, 0u, ag->seq, 2000000000ull /* 2 s */,
+                             w->err, s);
         note_launch();
     }
     return cuda_status(e);
@@ -698,8 +701,8 @@ int dnnopt_cuda_peer_wait(const unsigned int* flags, int world, unsigned int epo
     Workspace* w = nullptr;
     st = ensure_workspace(ctx, s, 0, 0, 0, &w);
     if (st != DNNOPT_STATUS_SUCCESS) return st;
-    cudaError_t e = launch_peer_wait(flags, world, epoch, static_cast<uint64_t>(timeout_us) * 1000ull,
-                                     w->err, s);
+    cudaError_t e = launch_peer_wait(flags, world, epoch, nullptr,
+                                     static_cast<uint64_t>(timeout_us) * 1000ull, w->err, s);
     note_launch();
     return cuda_status(e);
 }

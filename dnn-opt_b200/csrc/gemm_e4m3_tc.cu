@@ -26,8 +26,8 @@
 // mapped through CUDA IPC, plain stores over NVLink), and the last tile of
 // the grid raises this rank's flag on every rank (release, system scope); a
 // one-CTA wait kernel then blocks the stream until every rank's flag has
-// arrived (bounded wait).  The transfer of a tile overlaps the MMAs of the
-// tiles still running.
+// arrived (bounded wait) and advances the device-side call counter.  The
+// transfer of a tile overlaps the MMAs of the tiles still running.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -60,12 +60,14 @@ struct E4Params {
     // rank's output buffer, this rank's column block already applied).
     int nout;
     uint16_t* out[kMaxPeers];
-    // All-gather signalling (done != nullptr): `done` counts finished tiles on this
-    // GPU; the last tile raises flag[q][rank] = epoch on every rank q.
+    // All-gather (done != nullptr): the call number is *seq + 1; output copy
+    // o goes to out[o] + (call & 1) * out_stride; `done` counts finished tiles
+    // on this GPU and the last tile raises flag[q][rank] = call on every rank q.
+    int64_t out_stride;
+    const uint32_t* seq;
     uint32_t* done;
     uint32_t* flag[kMaxPeers];
     int rank;
-    uint32_t epoch;
 };
 
 // Instruction descriptor, kind::f8f6f4: A = B = E4M3 (format 0), D = F32,
@@ -244,6 +246,8 @@ gemm_e4m3_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
                 v[m] = (__uint_as_float(r[m]) + __uint_as_float(r[8 + m])) * p.inv_sigma[m];
         }
         const float sc = (n < p.N) ? p.scale[n] : 0.0f;
+        const uint32_t call = p.seq ? *p.seq + 1u : 0u;
+        const int64_t obase = p.seq ? static_cast<int64_t>(call & 1u) * p.out_stride : 0;
         // Writes one finished column n (rows 0..M-1) into every output copy;
         // the stores of a warp cover 64 contiguous bytes per row and copy.
         auto write_col = [&](const float (&c)[8]) {
@@ -251,7 +255,7 @@ gemm_e4m3_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
 #pragma unroll
             for (int m = 0; m < 8; ++m) bits[m] = __bfloat16_as_ushort(__float2bfloat16_rn(c[m] * sc));
             for (int o = 0; o < p.nout; ++o)
-                for (int m = 0; m < p.M; ++m) p.out[o][(int64_t)m * p.ldc + n] = bits[m];
+                for (int m = 0; m < p.M; ++m) p.out[o][obase + (int64_t)m * p.ldc + n] = bits[m];
         };
         bool wrote = false;    // this CTA finished its tile (the epilogue group agrees)
         if (p.splits == 1) {
@@ -301,7 +305,7 @@ gemm_e4m3_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
                 const uint32_t ntiles = gridDim.x;
                 const uint32_t t = atom_add_acq_rel_gpu_u32(p.done, 1u);
                 if (t == ntiles - 1) {
-                    for (int q = 0; q < p.nout; ++q) st_release_sys_u32(&p.flag[q][p.rank], p.epoch);
+                    for (int q = 0; q < p.nout; ++q) st_release_sys_u32(&p.flag[q][p.rank], call);
                     *p.done = 0u;   // ready for the next call on this stream
                 }
             }
@@ -458,13 +462,16 @@ cudaError_t launch_gemm_e4m3_tc(const GemmArgs& g, const E4m3TcPlan& plan, const
         }
         p.done = ag->done;
         p.rank = ag->rank;
-        p.epoch = ag->epoch;
+        p.seq = ag->seq;
+        p.out_stride = ag->out_stride_elems;
+        if (!ag->seq) return cudaErrorInvalidValue;
     } else {
         p.nout = 1;
         p.out[0] = static_cast<uint16_t*>(g.C);
         p.done = nullptr;
         p.rank = 0;
-        p.epoch = 0;
+        p.seq = nullptr;
+        p.out_stride = 0;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((g.N + BM - 1) / BM, plan.splits, 1);

@@ -129,25 +129,29 @@ size_t gemm_e4m3_tc_ws_floats(const GemmArgs& g, const E4m3TcPlan& p);
 size_t gemm_e4m3_tc_act_bytes(const GemmArgs& g);
 // Two launches (activation prep, then the GEMM), both with programmatic
 // dependent launch.
-// Fused all-gather of an N-sharded e4m3 GEMM: out[q] is rank q's full output
-// [M x ldc] (mapped in this process), flag[q] rank q's flag array (kAllGather
-// MaxRanks words); `done` is a zeroed local counter.
+// Fused all-gather of an N-sharded e4m3 GEMM: out[q] is rank q's first
+// output buffer [M x ldc] (mapped in this process; the second starts
+// out_stride_elems later), flag[q] rank q's flag array; `seq` is this rank's
+// device-side call counter (call number = *seq + 1, advanced by the wait
+// kernel); `done` is a zeroed local counter.
 constexpr int kAllGatherMaxRanks = 8;
 struct AllGatherArgs {
     int world, rank;
     void* out[kAllGatherMaxRanks];
     uint32_t* flag[kAllGatherMaxRanks];
+    const uint32_t* seq;
+    int64_t out_stride_elems;
     uint32_t* done;
-    uint32_t epoch;
 };
 cudaError_t launch_gemm_e4m3_tc(const GemmArgs& g, const E4m3TcPlan& plan, const float* scale,
                                 float* ws, uint32_t* tickets, void* act_buf, uint32_t* err,
                                 cudaStream_t s, const AllGatherArgs* ag = nullptr);
 // One CTA: waits (bounded by timeout_ns of %globaltimer) until flag[q] has
-// reached `epoch` for every q < world; on timeout records
-// kKerrPeerTimeout in *err and returns.
-cudaError_t launch_peer_wait(const uint32_t* flag, int world, uint32_t epoch, uint64_t timeout_ns,
-                             uint32_t* err, cudaStream_t s);
+// reached the call number for every q < world; on timeout records
+// kKerrPeerTimeout in *err and returns.  The call number is *seq + 1 when
+// `seq` is given (then *seq is advanced to it after the wait), else `epoch`.
+cudaError_t launch_peer_wait(const uint32_t* flag, int world, uint32_t epoch, uint32_t* seq,
+                             uint64_t timeout_ns, uint32_t* err, cudaStream_t s);
 
 // err: device word that receives a KernelErrorCode when a bounded wait gives up.
 cudaError_t launch_gemm_bf16_tc(const GemmArgs& g, int num_sms, uint32_t* err, cudaStream_t s);

@@ -1,6 +1,6 @@
 // Peer-GPU plumbing for the fused all-gather (one process per GPU):
 //   * the bounded wait kernel that holds a stream until every rank's flag
-//     has reached the call's epoch;
+//     has reached the call's number;
 //   * device buffers that other processes can map (CUDA IPC handles).
 // Every wait here is bounded by %globaltimer; a flag that never arrives
 // turns into an error word and a DNNOPT_STATUS_KERNEL_TIMEOUT status, never a
@@ -21,14 +21,15 @@ namespace {
 // their griddepcontrol.wait) for this kernel's completion, which hides their
 // launch latency.
 __global__ void __launch_bounds__(32)
-peer_wait_kernel(const uint32_t* __restrict__ flag, int world, uint32_t epoch, uint64_t timeout_ns,
-                 uint32_t* err) {
+peer_wait_kernel(const uint32_t* __restrict__ flag, int world, uint32_t epoch, uint32_t* seq,
+                 uint64_t timeout_ns, uint32_t* err) {
     pdl_launch_dependents();
     const int q = threadIdx.x;
+    const uint32_t want = seq ? *seq + 1u : epoch;
     if (q < world) {
         const uint64_t t0 = global_timer_ns();
-        // Epochs increase by one per call; the signed difference tolerates wrap.
-        while (static_cast<int32_t>(ld_acquire_sys_u32(&flag[q]) - epoch) < 0) {
+        // Call numbers increase by one per call; the signed difference tolerates wrap.
+        while (static_cast<int32_t>(ld_acquire_sys_u32(&flag[q]) - want) < 0) {
             if (global_timer_ns() - t0 > timeout_ns) {
                 record_kernel_error(err, kKerrPeerTimeout);
                 break;
@@ -38,12 +39,13 @@ peer_wait_kernel(const uint32_t* __restrict__ flag, int world, uint32_t epoch, u
     }
     __syncwarp();
     pdl_wait();
+    if (seq && q == 0) *seq = want;   // read by the next call's GEMM (stream order)
 }
 
 }  // namespace
 
-cudaError_t launch_peer_wait(const uint32_t* flag, int world, uint32_t epoch, uint64_t timeout_ns,
-                             uint32_t* err, cudaStream_t s) {
+cudaError_t launch_peer_wait(const uint32_t* flag, int world, uint32_t epoch, uint32_t* seq,
+                             uint64_t timeout_ns, uint32_t* err, cudaStream_t s) {
     if (!flag || world < 1 || world > kAllGatherMaxRanks) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(1, 1, 1);
@@ -54,7 +56,7 @@ cudaError_t launch_peer_wait(const uint32_t* flag, int world, uint32_t epoch, ui
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, peer_wait_kernel, flag, world, epoch, timeout_ns, err);
+    return cudaLaunchKernelEx(&cfg, peer_wait_kernel, flag, world, epoch, seq, timeout_ns, err);
 }
 
 }  // namespace dnnopt_b200

@@ -10,9 +10,10 @@ C[M, N] = A[M, K] x W^T, and every rank ends up with the whole C.  Two ways:
   finished column block straight into every rank's output buffer (peer memory
   mapped through CUDA IPC, NVLink stores) and raises a per-rank flag; the
   stream then waits (bounded) for every rank's flag.  No collective library
-  is involved and the transfer overlaps the tiles still computing.  Output
-  buffers alternate by call parity so that a rank one call ahead never
-  overwrites a buffer its peers may still read.
+  is involved and the transfer overlaps the tiles still computing.  Calls are
+  numbered on the device, so the arguments never change and the call can be
+  captured in a CUDA graph; output buffers alternate by call parity so that a
+  rank one call ahead never overwrites a buffer its peers may still read.
 * ``mode="nccl"``: the shard GEMM (dnnopt_cuda_gemm_e4m3bf16) followed by an
   NCCL all-gather and a [G, M, n] -> [M, G*n] interleave (gloo in the CPU
   tests); kept as the library-collective comparison.
@@ -25,7 +26,8 @@ from __future__ import annotations
 
 from typing import Callable, Optional
 
-FLAG_BYTES = 256          # flag array at the start of each rank's shared buffer
+FLAG_BYTES = 256          # flag array + call counter at the start of each rank's buffer
+SEQ_OFFSET = 64           # this rank's device-side call counter (local use only)
 
 
 def shard_bounds(N: int, world: int, align: int = 128) -> list[int]:
@@ -80,7 +82,9 @@ class ShardedE4M3Gemm:
         self._view = view or _cuda_view
         self.base = None
         self.peer_base: list[int] = []
-        self.epoch = 0
+        self.calls = 0
+        self._ag = None
+        self._descs = {}
         if mode == "fused":
             if world > self.dn.MAX_RANKS:
                 raise ValueError(f"at most {self.dn.MAX_RANKS} ranks")
@@ -115,6 +119,14 @@ class ShardedE4M3Gemm:
         handles = self._exchange(dn.ipc_handle(self.base))
         self.peer_base = [self.base if q == self.rank else dn.ipc_open(handles[q])
                           for q in range(self.world)]
+        ag = dn.AllGatherDesc()
+        ag.world, ag.rank = self.world, self.rank
+        for q in range(self.world):
+            ag.out[q] = self.peer_base[q] + FLAG_BYTES
+            ag.flags[q] = self.peer_base[q]
+        ag.seq = self.base + SEQ_OFFSET
+        ag.out_stride = self.out_bytes
+        self._ag = ag                          # the same arguments for every call
         self.dist.barrier(group=self.group)   # every rank has mapped every buffer
 
     def out_address(self, q: int, parity: int) -> int:
@@ -123,25 +135,28 @@ class ShardedE4M3Gemm:
     def forward_fused(self, A, W_shard, s_shard, stream=None):
         """A: [M, K] bf16 bits (int16), M <= max_rows.  Returns C [M, N]
         (int16 bf16 bits), a view of this rank's output buffer that stays valid
-        until the call after next."""
+        until the call after next.  The c-th execution of the call (counting
+        from 1, graph replays included) writes buffer c & 1; this method counts
+        its own invocations to pick the view it returns."""
         dn = self.dn
         M = A.shape[0]
         if M > self.max_rows:
             raise ValueError(f"M={M} exceeds max_rows={self.max_rows}")
-        self.epoch = (self.epoch + 1) & 0xFFFFFFFF
-        parity = self.epoch & 1
-        ag = dn.AllGatherDesc()
-        ag.world, ag.rank, ag.epoch = self.world, self.rank, self.epoch
-        for q in range(self.world):
-            ag.out[q] = self.out_address(q, parity)
-            ag.flags[q] = self.peer_base[q]
-        d = dn.desc(M, self.n_local, self.K, self.K, self.K, self.N)
+        d = self._descs.get(M)
+        if d is None:
+            d = self._descs[M] = dn.desc(M, self.n_local, self.K, self.K, self.K, self.N)
         if stream is None:
             import torch
             stream = torch.cuda.current_stream()
-        dn.check(dn.cuda_gemm_e4m3bf16_allgather(d, A, W_shard, s_shard, ag, stream),
+        dn.check(dn.cuda_gemm_e4m3bf16_allgather(d, A, W_shard, s_shard, self._ag, stream),
                  "fused e4m3 all-gather GEMM")
-        return self._view(self.out_address(self.rank, parity), (M, self.N))
+        self.calls += 1
+        return self.output(self.calls & 1, M)
+
+    def output(self, parity: int, M: int | None = None):
+        """View of this rank's output buffer `parity` (the result of calls
+        with that parity)."""
+        return self._view(self.out_address(self.rank, parity), (M or self.max_rows, self.N))
 
     def close(self) -> None:
         """Unmaps the peers' buffers and frees this rank's (after a barrier, so

@@ -191,21 +191,26 @@ int dnnopt_ipc_close(void* ptr);
 typedef struct {
     int world;                                /* 1 .. DNNOPT_MAX_RANKS */
     int rank;                                 /* this process's rank */
-    void* out[DNNOPT_MAX_RANKS];              /* rank q's output [M x ldc] bf16, mapped here */
+    void* out[DNNOPT_MAX_RANKS];              /* rank q's first output buffer [M x ldc] bf16, mapped here */
     unsigned int* flags[DNNOPT_MAX_RANKS];    /* rank q's flag array (world words), mapped here */
-    unsigned int epoch;                       /* same on every rank; +1 per call */
+    unsigned int* seq;                        /* this rank's call counter (device word, starts at 0) */
+    size_t out_stride;                        /* bytes from each rank's first output buffer to its
+                                                 second; 0 = one buffer */
 } dnnopt_allgather_desc;
 
 /* Fused N-sharded e4m3 decode-FFN GEMM + all-gather.  d->N is this rank's
  * shard width n and d->ldc the full output row length (>= world * n); W and
- * scale hold this rank's n weight rows.  The kernel writes the rank's columns
- * [rank*n, rank*n + n) of bf16(scale * A W^T) into every rank's out buffer,
- * raises flags[q][rank] = epoch on every rank q once all of them are written,
- * and the stream then waits (bounded, 2 s) until every rank's flag has reached
- * epoch in this rank's array: work queued after the call on `stream` sees the
- * full [M x world*n] result in out[rank].  M <= 8.  A rank must not overwrite
- * an out buffer that peers may still read: alternate two buffers by epoch.
- * A flag that does not arrive in time makes dnnopt_stream_status() return
+ * scale hold this rank's n weight rows.  The call numbers itself on the
+ * device: call c = *seq + 1 writes the rank's columns [rank*n, rank*n + n) of
+ * bf16(scale * A W^T) into buffer (c & 1) of every rank (out[q] + (c & 1) *
+ * out_stride), raises flags[q][rank] = c on every rank q once all of them are
+ * written, and the stream then waits (bounded, 2 s) until every rank's flag
+ * has reached c in this rank's array and sets *seq = c: work queued after the
+ * call on `stream` sees the full [M x world*n] result.  Nothing in the
+ * arguments changes from call to call, so the call can be captured in a CUDA
+ * graph and replayed.  With two buffers a rank one call ahead never
+ * overwrites a buffer its peers may still read.  M <= 8.  A flag that does
+ * not arrive in time makes dnnopt_stream_status() return
  * DNNOPT_STATUS_KERNEL_TIMEOUT. */
 int dnnopt_cuda_gemm_e4m3bf16_allgather(const dnnopt_gemm_desc* d, const uint16_t* A,
                                         const uint8_t* W, const float* scale,

@@ -48,15 +48,16 @@ class _FakeLib:
         self.freed.append(address)
 
     def cuda_gemm_e4m3bf16_allgather(self, d, A, W, s, ag, stream):
-        self.calls.append((d.M, d.N, d.K, d.ldc, ag.world, ag.rank, ag.epoch,
+        self.calls.append((d.M, d.N, d.K, d.ldc, ag.world, ag.rank, ag.seq, ag.out_stride,
                            [ag.out[q] for q in range(ag.world)],
                            [ag.flags[q] for q in range(ag.world)]))
         return 0
 
 
 def fused_host_logic(mod, rank, world) -> bool:
-    """Peer-address exchange, per-call parity and epochs of the fused mode."""
-    from dnnopt_b200.sharded import FLAG_BYTES, ShardedE4M3Gemm
+    """Peer-address exchange, constant per-call arguments (device-side call
+    numbering) and the returned buffer's parity in the fused mode."""
+    from dnnopt_b200.sharded import FLAG_BYTES, SEQ_OFFSET, ShardedE4M3Gemm
     M, N, K = 8, 128 * world * 3, 256
     fake = _FakeLib(mod, rank)
     sh = ShardedE4M3Gemm(dist, N, K, rank, world, mode="fused", lib=fake,
@@ -67,10 +68,11 @@ def fused_host_logic(mod, rank, world) -> bool:
     for call in range(1, 4):
         address, shape = sh.forward_fused(A, None, None, stream=0)
         parity = call & 1
-        m, n, k, ldc, w, r, epoch, outs, flags = fake.calls[-1]
-        ok = ok and (m, n, k, ldc, w, r, epoch) == (M, N // world, K, N, world, rank, call)
-        ok = ok and outs == [b + FLAG_BYTES + parity * 8 * N * 2 for b in bases]
-        ok = ok and flags == bases and address == outs[rank] and shape == (M, N)
+        m, n, k, ldc, w, r, seq, stride, outs, flags = fake.calls[-1]
+        ok = ok and (m, n, k, ldc, w, r) == (M, N // world, K, N, world, rank)
+        ok = ok and seq == bases[rank] + SEQ_OFFSET and stride == 8 * N * 2
+        ok = ok and outs == [b + FLAG_BYTES for b in bases] and flags == bases
+        ok = ok and address == bases[rank] + FLAG_BYTES + parity * 8 * N * 2 and shape == (M, N)
     sh.close()
     ok = ok and sorted(fake.closed) == sorted(b for q, b in enumerate(bases) if q != rank)
     ok = ok and fake.freed == [bases[rank]]

@@ -431,31 +431,45 @@ def test_peer_wait_times_out_and_recovers(gpu, dn):
 @pytest.mark.parametrize("M,N,K", [(8, 28672, 8192), (3, 1024, 1024)])
 def test_fused_allgather_single_rank(gpu, dn, orc, M, N, K):
     """world = 1: the fused entry point writes the same bits as the plain
-    e4m3 GEMM, in alternating buffers, and raises its own flag each call."""
+    e4m3 GEMM into buffer (call & 1), raises its own flag to the call number
+    and advances the device-side counter -- eagerly and from a CUDA graph
+    replayed with unchanged arguments."""
     torch = gpu
+    from dnnopt_b200.sharded import _cuda_view
     A, q, s = e4m3_problem(orc, M, N, K)
     dA = torch.from_numpy(A.view(np.int16)).cuda()
     dW, ds = torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()
-    st = torch.cuda.current_stream()
+    st = torch.cuda.Stream()
     plain = torch.zeros(M * N, dtype=torch.int16, device="cuda")
     dn.check(dn.cuda_gemm("e4m3bf16", dn.desc(M, N, K, K, K, N), dA, dW, plain, st, scale=ds))
     out_bytes = 8 * N * 2
     base = dn.peer_alloc(256 + 2 * out_bytes)
     try:
-        for epoch in (1, 2, 3):
-            ag = dn.AllGatherDesc()
-            ag.world, ag.rank, ag.epoch = 1, 0, epoch
-            ag.out[0] = base + 256 + (epoch & 1) * out_bytes
-            ag.flags[0] = base
-            dn.check(dn.cuda_gemm_e4m3bf16_allgather(dn.desc(M, N, K, K, K, N), dA, dW, ds, ag, st))
+        ag = dn.AllGatherDesc()
+        ag.world, ag.rank = 1, 0
+        ag.out[0], ag.flags[0], ag.seq, ag.out_stride = base + 256, base, base + 64, out_bytes
+        d = dn.desc(M, N, K, K, K, N)
+        words = _cuda_view(base, (128,)).view(torch.int32)      # flags at 0, counter at 64 bytes
+        bufs = [_cuda_view(base + 256 + p * out_bytes, (M * N,)) for p in (0, 1)]
+        with torch.cuda.stream(st):
+            for call in (1, 2, 3):
+                dn.check(dn.cuda_gemm_e4m3bf16_allgather(d, dA, dW, ds, ag, st))
+                assert dn.stream_status(st) == dn.SUCCESS
+                assert torch.equal(bufs[call & 1], plain), call
+                assert words[0].item() == call and words[16].item() == call
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=st):
+                dn.check(dn.cuda_gemm_e4m3bf16_allgather(d, dA, dW, ds, ag, st))
+                dn.check(dn.cuda_gemm_e4m3bf16_allgather(d, dA, dW, ds, ag, st))
+            bufs[0].zero_(); bufs[1].zero_()
+            st.synchronize()
+            start = words[16].item()
+            graph.replay()
+            graph.replay()
             assert dn.stream_status(st) == dn.SUCCESS
-            got = torch.empty(M * N, dtype=torch.int16, device="cuda")
-            from dnnopt_b200.sharded import _cuda_view
-            got.copy_(_cuda_view(ag.out[0], (M * N,)))
-            flag_now = _cuda_view(base, (2,)).view(torch.int32)[0].item()
-            torch.cuda.synchronize()
-            assert torch.equal(got, plain), epoch
-            assert flag_now == epoch
+            assert words[16].item() == start + 4 and words[0].item() == start + 4
+            assert torch.equal(bufs[0], plain) and torch.equal(bufs[1], plain)
+            del graph
     finally:
         torch.cuda.synchronize()
         dn.peer_free(base)

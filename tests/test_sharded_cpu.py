@@ -56,9 +56,10 @@ def test_sharded_allgather_matches_single_process(dn, world, N):
 
 @pytest.mark.parametrize("world", [2, 4])
 def test_fused_mode_host_logic(dn, world):
-    """Fused mode: IPC-handle exchange maps every rank's buffer, each call
-    alternates output buffers by parity and carries the next epoch, close()
-    unmaps the peers and frees the own buffer."""
+    """Fused mode: IPC-handle exchange maps every rank's buffer, every call
+    passes the same arguments (the device numbers the calls), the returned
+    view alternates buffers by parity, close() unmaps the peers and frees the
+    own buffer."""
     _run_ranks(world, MODE="fused")
 
 
