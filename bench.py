@@ -256,7 +256,7 @@ def capture(torch, stream, fn):
 # dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum --csv
 # -k regex:gemv -s 12 -c 12 python bench.py --profile c2 --reps 2
 # (C is written into L2 and leaves it after the launch, so writes read 0).
-C2_DRAM_BYTES_PER_STEP = 117_940_000
+C2_DRAM_BYTES_PER_STEP = 117_954_304
 
 
 def bench_single(torch, dn, stream, fn_list, bytes_per_call, flops_per_call, iters=30):
