@@ -10,13 +10,15 @@
 // (4-17 MB) stream in under 3 us at HBM speed.
 //
 // B200 design, for latency:
-//   * a CTA owns a slab of kSlabW = 8 consecutive columns and the whole K
+//   * a CTA owns a slab of W = 8 (or 16) consecutive columns and the whole K
 //     extent, so each output is finished inside the CTA: no workspace, no
-//     atomic ticket, no second pass over memory;
-//   * lane l reads column l % 8 of rows l / 8 + 4 * warp + 32 * i: a warp load
-//     covers four 32-byte row segments (rows need no alignment, so prime N
-//     works), and every thread issues its first 2 x 16 row loads before it
-//     stages A, so one DRAM round trip covers most of a 1024-row slab;
+//     atomic ticket, no second pass over memory; the host picks W = 16 when
+//     8-column slabs would need more than one wave of resident CTAs;
+//   * lane l reads column l % W of rows l / W + (32 / W) * warp + 256 / W * i:
+//     a warp load covers 32 / W row segments of 4W bytes (rows need no
+//     alignment, so prime N works), and every thread issues its first 2 x 16
+//     row loads before it stages A, so one DRAM round trip covers most of a
+//     1024-row slab;
 //   * the A panel is staged in shared memory k-major, MT floats per row
 //     (thread t loads column t of A from every row m and writes its MT values
 //     as 16-byte stores), so a row's MT coefficients come back with MT/4
@@ -63,8 +65,8 @@ __device__ __forceinline__ void slab_body(const GemmArgs& g, int slab, float* sA
     const TB* B = static_cast<const TB*>(g.B) + n0 + col;
     float* C = static_cast<float*>(g.C);
 
-    // The threads that write C (tid < MT * kSlabW: m = tid / 8, column
-    // tid % 8) fetch their C element now, in the shadow of the B stream.
+    // The threads that write C (tid < MT * W: m = tid / W, column tid % W)
+    // fetch their C element now, in the shadow of the B stream.
     const int wm = tid / kSlabW, wc = tid % kSlabW;
     const bool writer = tid < MT * kSlabW && wm < g.M && n0 + wc < g.N;
     float c_old = 0.0f;
