@@ -260,11 +260,15 @@ Plan heuristic_plan(Kind kind, const GemmArgs& g, const DeviceInfo& info) {
         // Measured on B200 (M <= 8, K = 1024, prime N of 1009-4093): the slab
         // form finishes in 0.4-0.8x the split-K time; at K = 4096 split-K wins.
         // 16-column slabs when 8-column ones would need more than one wave of
-        // resident CTAs (7 x 4093: 10.7 -> 8.5 us); 8 otherwise.
+        // resident CTAs (7 x 4093: 10.7 -> 8.5 us), or for M <= 4 from 1536
+        // columns on (3 x 2039: 4.9 -> 3.8 us, 2 x 4093: 6.7 -> 6.1 us);
+        // 8 otherwise (narrower N keeps more CTAs: 2 x 1009 at 8 columns
+        // takes 2.8 us, at 16 3.7 us).
         if (g.K <= 2048 && g.N >= 512 && g.N <= 8192) {
             p.kernel = KernelId::GemvSlab;
             const int occ8 = slab_occupancy(kind, p.kn.mt, 8, g.K, info);
-            p.slab_w = gemv_slab_ctas(g.N, 8) > occ8 * info.num_sms ? 16 : 8;
+            const bool wide = gemv_slab_ctas(g.N, 8) > occ8 * info.num_sms || (p.kn.mt <= 4 && g.N >= 1536);
+            p.slab_w = wide ? 16 : 8;
         }
         return p;
     }

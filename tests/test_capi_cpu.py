@@ -132,6 +132,8 @@ def test_plan_selection_without_device(dn):
     assert s == "gemv_kn_slab mt=8 w=8 ctas=512", s
     s = dn.plan_describe(dn.KIND_F32, dn.desc(2, 1009, 1024, 1024, 1009, 1009))
     assert s == "gemv_kn_slab mt=2 w=8 ctas=127", s
+    s = dn.plan_describe(dn.KIND_F32, dn.desc(3, 2039, 1024, 1024, 2039, 2039))
+    assert s == "gemv_kn_slab mt=4 w=16 ctas=128", s   # M <= 4 from 1536 columns on: 16 wide
     # Deeper K: split-K, one wave of resident CTAs, at most 16 splits.
     s = dn.plan_describe(dn.KIND_F32, dn.desc(7, 4093, 4096, 4096, 4093, 4093, beta=0.5))
     assert s.startswith("gemv_kn_splitk mt=8 vec4=0 splits=13 kchunk=320"), s   # prime N: scalar loads
