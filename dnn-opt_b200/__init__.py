@@ -85,6 +85,11 @@ lib.dnnopt_gemm_int8_int8int8int32.argtypes = [_I, _I, _I, _P, _I, _P, _I, _P, _
 lib.dnnopt_gemm_e4m3_bf16.argtypes = [_I, _I, _I, _P, _I, _P, _I, _P, _P, _I]
 lib.dnnopt_gemm_f32_desc.argtypes = [ctypes.POINTER(GemmDesc), _P, _P, _P]
 lib.dnnopt_saxpy.argtypes = [_I, _F, _P, _I, _P, _I]
+_I64P, _FP = ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_float)
+_COLMAJOR_SIG = [ctypes.c_char_p, ctypes.c_char_p, _I64P, _I64P, _I64P, _FP, _P, _I64P, _P, _I64P,
+                 _FP, _P, _I64P, _P]
+lib.dnnopt_sgemm_colmajor.argtypes = _COLMAJOR_SIG
+lib.dnnopt_cuda_sgemm_colmajor.argtypes = _COLMAJOR_SIG + [_P]
 for _name in ("dnnopt_cuda_gemm_f32", "dnnopt_cuda_gemm_bf16f32", "dnnopt_cuda_gemm_f32_bf16round",
               "dnnopt_cuda_gemm_f32_s8quant", "dnnopt_cuda_gemm_s8s32",
               "dnnopt_cuda_gemm_refe4m3_e5m2", "dnnopt_cuda_gemm_refe5m2_e5m2",
@@ -192,6 +197,21 @@ def saxpy(N, alpha, X, incX, Y, incY) -> int:
     return lib.dnnopt_saxpy(N, alpha, ptr(X), incX, ptr(Y), incY)
 
 
+def _colmajor_args(transa, transb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, bias):
+    i64, f32 = ctypes.c_int64, ctypes.c_float
+    return (transa.encode() if isinstance(transa, str) else transa,
+            transb.encode() if isinstance(transb, str) else transb,
+            ctypes.byref(i64(M)), ctypes.byref(i64(N)), ctypes.byref(i64(K)), ctypes.byref(f32(alpha)),
+            ptr(A), ctypes.byref(i64(lda)), ptr(B), ctypes.byref(i64(ldb)), ctypes.byref(f32(beta)),
+            ptr(C), ctypes.byref(i64(ldc)), ptr(bias))
+
+
+def sgemm_colmajor(transa, transb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, bias=None) -> int:
+    """The oneDNN integration's dnnopt_sgemm: column-major, optional bias[i]."""
+    return lib.dnnopt_sgemm_colmajor(*_colmajor_args(transa, transb, M, N, K, alpha, A, lda, B, ldb,
+                                                     beta, C, ldc, bias))
+
+
 def has_fp8_support() -> bool:
     return bool(lib.dnnopt_has_fp8_support())
 
@@ -205,6 +225,12 @@ def cuda_gemm(kind: str, d: GemmDesc, A, B, C, stream=None, scale=None) -> int:
     if kind == "e4m3bf16":
         return fn(ctypes.byref(d), ptr(A), ptr(B), ptr(scale), ptr(C), s)
     return fn(ctypes.byref(d), ptr(A), ptr(B), ptr(C), s)
+
+
+def cuda_sgemm_colmajor(transa, transb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, bias=None,
+                        stream=None) -> int:
+    return lib.dnnopt_cuda_sgemm_colmajor(*_colmajor_args(transa, transb, M, N, K, alpha, A, lda, B,
+                                                          ldb, beta, C, ldc, bias), _stream(stream))
 
 
 def _stream(stream):

@@ -357,7 +357,10 @@ int host_entry(Kind kind, const dnnopt_gemm_desc* d, const void* A, const void* 
     const size_t eb = (kind == Kind::F32 || kind == Kind::F32BF16R || kind == Kind::F32S8Q) ? 4
                       : (kind == Kind::BF16F32) ? 2 : 1;
     const size_t ec = (kind == Kind::S8S32) ? 4 : (kind == Kind::E4M3BF16 ? 2 : 4);
-    const bool reads_c = kind != Kind::S8S32 && kind != Kind::E4M3BF16 && d->beta != 0.0f;
+    // C is staged in when beta != 0, and whenever its rows are padded (ldc > N):
+    // the whole span is copied back, so the padding must make the round trip.
+    const bool reads_c =
+        (kind != Kind::S8S32 && kind != Kind::E4M3BF16 && d->beta != 0.0f) || d->ldc > d->N;
     Operand ops[4] = {
         {A, ta ? span_bytes(d->K, d->M, d->lda, ea) : span_bytes(d->M, d->K, d->lda, ea), true, false},
         {B, tb ? span_bytes(d->N, d->K, d->ldb, eb) : span_bytes(d->K, d->N, d->ldb, eb), true, false},
@@ -416,6 +419,88 @@ dnnopt_gemm_desc make_desc(int M, int N, int K, float alpha, int lda, int ldb, f
 }
 
 int g_num_threads = 0;
+
+// ---- oneDNN entry (integration/onednn/0001-dnnopt-integration.patch:279-365) ----
+struct ColMajorArgs {
+    bool ta, tb;
+    int64_t M, N, K, lda, ldb, ldc;
+    float alpha, beta;
+};
+
+// Argument checks of the column-major entry.  Returns SUCCESS with *noop for
+// M == 0 or N == 0 (the entry's early return).
+int colmajor_parse(const char* transa, const char* transb, const int64_t* M, const int64_t* N,
+                   const int64_t* K, const float* alpha, const int64_t* lda, const int64_t* ldb,
+                   const float* beta, const int64_t* ldc, ColMajorArgs* a, bool* noop) {
+    *noop = false;
+    if (!transa || !transb || !M || !N || !K || !alpha || !lda || !ldb || !beta || !ldc)
+        return DNNOPT_STATUS_INVALID_VALUE;
+    // Packed operands: dnnl_unimplemented in the reference (:284-286).
+    if (*transa == 'P' || *transa == 'p' || *transb == 'P' || *transb == 'p')
+        return DNNOPT_STATUS_NOT_SUPPORTED;
+    if (*M < 0 || *N < 0 || *K < 0) return DNNOPT_STATUS_INVALID_VALUE;
+    if (*M == 0 || *N == 0) { *noop = true; return DNNOPT_STATUS_SUCCESS; }
+    a->ta = *transa == 'T' || *transa == 't';
+    a->tb = *transb == 'T' || *transb == 't';
+    a->M = *M; a->N = *N; a->K = *K;
+    a->lda = *lda; a->ldb = *ldb; a->ldc = *ldc;
+    a->alpha = *alpha; a->beta = *beta;
+    if (a->ldc < 1) return DNNOPT_STATUS_INVALID_VALUE;
+    if (a->K > 0) {
+        if (a->lda < (a->ta ? a->K : a->M) || a->ldb < (a->tb ? a->N : a->K))
+            return DNNOPT_STATUS_INVALID_VALUE;
+        const int64_t kIntMax = 2147483647;
+        if (a->M > kIntMax || a->N > kIntMax || a->K > kIntMax || a->lda > kIntMax ||
+            a->ldb > kIntMax)
+            return DNNOPT_STATUS_NOT_SUPPORTED;
+    }
+    return DNNOPT_STATUS_SUCCESS;
+}
+
+// Bytes each column-major operand spans.
+size_t colmajor_span(int64_t rows, int64_t cols, int64_t ld) {
+    if (rows <= 0 || cols <= 0) return 0;
+    return static_cast<size_t>((cols - 1) * ld + rows) * sizeof(float);
+}
+
+// Device pointers, stream-ordered.  The column-major GEMM is the row-major one
+// with the operands swapped, RowMajor(op B, op A, N, M, K, B, ldb, A, lda, C, ldc)
+// (:306-329); transposes are kernel flags, not copies.  ldc >= M: the bias is
+// fused into the GEMM's epilogue.  ldc < M (:330-353): the GEMM writes a dense
+// N x M scratch that is copied back in the entry's order.
+int colmajor_device(const ColMajorArgs& a, const float* A, const float* B, float* C,
+                    const float* bias, DeviceContext* ctx, cudaStream_t s) {
+    if (a.K == 0) {
+        cudaError_t e = launch_colmajor_k0(C, bias, a.M, a.N, a.ldc, a.beta, s);
+        note_launch();
+        return cuda_status(e);
+    }
+    GemmArgs g;
+    g.M = static_cast<int>(a.N); g.N = static_cast<int>(a.M); g.K = static_cast<int>(a.K);
+    g.alpha = a.alpha; g.beta = a.beta;
+    g.A = B; g.lda = a.ldb; g.a_trans = a.tb ? 1 : 0;
+    g.B = A; g.ldb = a.lda; g.b_trans = a.ta ? 1 : 0;
+    if (a.ldc >= a.M) {
+        g.C = C; g.ldc = a.ldc; g.bias = bias;
+        return run_device(Kind::F32, g, nullptr, ctx, s);
+    }
+    Workspace* w = nullptr;
+    const size_t tmp_bytes = static_cast<size_t>(a.M) * a.N * sizeof(float);
+    int st = ensure_workspace(ctx, s, 0, 0, tmp_bytes, &w);
+    if (st != DNNOPT_STATUS_SUCCESS) return st;
+    float* tmp = static_cast<float*>(w->quant);
+    if (a.beta != 0.0f) {
+        cudaError_t e = launch_colmajor_gather(tmp, C, a.M, a.N, a.ldc, s);
+        note_launch();
+        if (e != cudaSuccess) return cuda_status(e);
+    }
+    g.C = tmp; g.ldc = a.M;
+    st = run_device(Kind::F32, g, nullptr, ctx, s);
+    if (st != DNNOPT_STATUS_SUCCESS) return st;
+    cudaError_t e = launch_colmajor_writeback(C, tmp, a.M, bias, a.M, a.N, a.ldc, s);
+    note_launch();
+    return cuda_status(e);
+}
 
 }  // namespace
 
@@ -516,6 +601,60 @@ int dnnopt_gemm_f32_desc(const dnnopt_gemm_desc* d, const float* A, const float*
     return host_entry(Kind::F32, d, A, B, C, nullptr);
 }
 
+int dnnopt_sgemm_colmajor(const char* transa, const char* transb, const int64_t* M,
+                          const int64_t* N, const int64_t* K, const float* alpha, const float* A,
+                          const int64_t* lda, const float* B, const int64_t* ldb,
+                          const float* beta, float* C, const int64_t* ldc, const float* bias) {
+    ColMajorArgs a;
+    bool noop;
+    int st = colmajor_parse(transa, transb, M, N, K, alpha, lda, ldb, beta, ldc, &a, &noop);
+    if (st != DNNOPT_STATUS_SUCCESS || noop) return set_status(st);
+    if (!C || (a.K > 0 && (!A || !B))) return set_status(DNNOPT_STATUS_INVALID_VALUE);
+    DeviceContext* ctx = current_context(&st);
+    if (!ctx) return st;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    cudaStream_t s = ctx->user_stream_set ? ctx->user_stream : ctx->default_stream;
+    // The K == 0 path reads C whatever beta is; otherwise C is read for
+    // beta != 0, and staged in whenever its columns are padded (ldc > M) so
+    // that the padding survives the copy back of the whole span.
+    const bool reads_c = a.K == 0 || a.beta != 0.0f || a.ldc > a.M;
+    Operand ops[4] = {
+        {A, a.K > 0 ? (a.ta ? colmajor_span(a.K, a.M, a.lda) : colmajor_span(a.M, a.K, a.lda)) : 0,
+         true, false},
+        {B, a.K > 0 ? (a.tb ? colmajor_span(a.N, a.K, a.ldb) : colmajor_span(a.K, a.N, a.ldb)) : 0,
+         true, false},
+        {C, colmajor_span(a.M, a.N, a.ldc), reads_c, true},
+        {bias, bias ? static_cast<size_t>(a.M) * sizeof(float) : 0, true, false},
+    };
+    const void* dev[4] = {A, B, C, bias};
+    for (int i = 0; i < 4; ++i) {
+        if (!ops[i].user || ops[i].bytes == 0) continue;
+        if (classify_pointer(ops[i].user) == PtrKind::Device) continue;
+        void* buf = nullptr;
+        st = ensure_stage(ctx, i, ops[i].bytes, &buf);
+        if (st != DNNOPT_STATUS_SUCCESS) return st;
+        dev[i] = buf;
+        if (ops[i].in) {
+            cudaError_t e = cudaMemcpyAsync(buf, ops[i].user, ops[i].bytes, cudaMemcpyHostToDevice, s);
+            if (e != cudaSuccess) return cuda_status(e);
+        }
+    }
+    st = colmajor_device(a, static_cast<const float*>(dev[0]), static_cast<const float*>(dev[1]),
+                         static_cast<float*>(const_cast<void*>(dev[2])),
+                         static_cast<const float*>(dev[3]), ctx, s);
+    if (st != DNNOPT_STATUS_SUCCESS) {
+        cudaStreamSynchronize(s);
+        return set_status(st);
+    }
+    if (dev[2] != C) {
+        cudaError_t e = cudaMemcpyAsync(C, dev[2], ops[2].bytes, cudaMemcpyDeviceToHost, s);
+        if (e != cudaSuccess) return cuda_status(e);
+    }
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_status(e);
+    return set_status(DNNOPT_STATUS_SUCCESS);
+}
+
 int dnnopt_saxpy(int N, float alpha, const float* X, int incX, float* Y, int incY) {
     if (N <= 0 || alpha == 0.0f) return set_status(DNNOPT_STATUS_SUCCESS);   // reference early return
     if (!X || !Y || incX < 0 || incY < 0) return set_status(DNNOPT_STATUS_INVALID_VALUE);
@@ -559,6 +698,21 @@ void dnnopt_gemm_set_num_threads(int n) { g_num_threads = n < 0 ? 0 : n; }
 int dnnopt_gemm_get_num_threads(void) { return g_num_threads > 0 ? g_num_threads : 1; }
 
 // ---- device-pointer entry points ------------------------------------------
+int dnnopt_cuda_sgemm_colmajor(const char* transa, const char* transb, const int64_t* M,
+                               const int64_t* N, const int64_t* K, const float* alpha,
+                               const float* A, const int64_t* lda, const float* B,
+                               const int64_t* ldb, const float* beta, float* C, const int64_t* ldc,
+                               const float* bias, void* stream) {
+    ColMajorArgs a;
+    bool noop;
+    int st = colmajor_parse(transa, transb, M, N, K, alpha, lda, ldb, beta, ldc, &a, &noop);
+    if (st != DNNOPT_STATUS_SUCCESS || noop) return set_status(st);
+    if (!C || (a.K > 0 && (!A || !B))) return set_status(DNNOPT_STATUS_INVALID_VALUE);
+    DeviceContext* ctx = current_context(&st);
+    if (!ctx) return st;
+    return set_status(colmajor_device(a, A, B, C, bias, ctx, static_cast<cudaStream_t>(stream)));
+}
+
 int dnnopt_cuda_gemm_f32(const dnnopt_gemm_desc* d, const float* A, const float* B, float* C,
                          void* stream) {
     return device_entry(Kind::F32, d, A, B, C, nullptr, stream);

@@ -42,6 +42,13 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 // ---------------------------------------------------------------------------
 // Scalar conversions
 // ---------------------------------------------------------------------------
+// The bias pass of the oneDNN entry (integration/onednn/0001-dnnopt-integration.patch:355-362:
+// C[i,j] += bias[i] on the column-major C, i.e. bias[n] on the row-major view),
+// fused into the FP32 epilogues as its own rounding after alpha*acc + beta*C.
+__device__ __forceinline__ float add_bias(float v, const float* bias, int64_t n) {
+    return bias ? __fadd_rn(v, __ldg(bias + n)) : v;
+}
+
 __device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {
     return __uint_as_float(static_cast<uint32_t>(b) << 16);
 }

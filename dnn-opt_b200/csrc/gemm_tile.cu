@@ -108,7 +108,8 @@ __global__ void __launch_bounds__(kThreads) gemm_tile_f32_kernel(const GemmArgs 
             int gj = n0 + tx * 4 + c;
             if (gj >= g.N) continue;
             float* cp = C + (int64_t)gi * g.ldc + gj;
-            *cp = (g.beta == 0.0f) ? g.alpha * acc[r][c] : fmaf(g.alpha, acc[r][c], g.beta * *cp);
+            *cp = add_bias((g.beta == 0.0f) ? g.alpha * acc[r][c] : fmaf(g.alpha, acc[r][c], g.beta * *cp),
+                           g.bias, gj);
         }
     }
 }
@@ -342,6 +343,101 @@ cudaError_t launch_saxpy(int n, float alpha, const float* x, int incx, float* y,
     int blocks = (n + 255) / 256;
     if (blocks > 148 * 8) blocks = 148 * 8;
     saxpy_kernel<<<blocks, 256, 0, s>>>(n, alpha, x, incx, y, incy);
+    return cudaGetLastError();
+}
+
+// ---- column-major C of the oneDNN entry ------------------------------------
+// The entry (integration/onednn/0001-dnnopt-integration.patch:279-365) walks
+// the M x N column-major C column by column, j = 0..N-1, so when ldc < M the
+// columns overlap in memory and an address can belong to several (i, j)
+// pairs.  These kernels give every address of the footprint
+// [0, (N-1)*ldc + M) the value that sequential walk leaves: one thread per
+// address, pairs (j, i = a - j*ldc) visited in ascending j.  With ldc >= M an
+// address has at most one pair.
+
+__device__ __forceinline__ bool colmajor_pairs(int64_t a, int64_t M, int64_t N, int64_t ldc,
+                                               int64_t* jlo, int64_t* jhi) {
+    int64_t hi = a / ldc;
+    if (hi > N - 1) hi = N - 1;
+    const int64_t d = a - (M - 1);
+    int64_t lo = d <= 0 ? 0 : (d + ldc - 1) / ldc;
+    *jlo = lo;
+    *jhi = hi;
+    return lo <= hi;
+}
+
+// K == 0 (:288-303): C = 0 (beta == 0) or C * beta per pair (beta != 1),
+// then bias[i] added per pair.
+__global__ void colmajor_k0_kernel(float* C, const float* bias, int64_t M, int64_t N, int64_t ldc,
+                                   float beta) {
+    const int64_t total = (N - 1) * ldc + M;
+    for (int64_t a = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; a < total;
+         a += (int64_t)gridDim.x * blockDim.x) {
+        int64_t jlo, jhi;
+        if (!colmajor_pairs(a, M, N, ldc, &jlo, &jhi)) continue;
+        float v = C[a];
+        if (beta == 0.0f) {
+            v = 0.0f;
+        } else if (beta != 1.0f) {
+            for (int64_t j = jlo; j <= jhi; ++j) v = __fmul_rn(v, beta);
+        }
+        if (bias)
+            for (int64_t j = jlo; j <= jhi; ++j) v = __fadd_rn(v, bias[a - j * ldc]);
+        C[a] = v;
+    }
+}
+
+// ldc < M (:330-353): C was computed into tmp (rows j of M floats, ld tmp_ld)
+// and is copied back row by row, so the last pair's row wins; then the bias
+// pass (:355-362) adds bias[i] per pair.
+__global__ void colmajor_writeback_kernel(float* C, const float* tmp, int64_t tmp_ld,
+                                          const float* bias, int64_t M, int64_t N, int64_t ldc) {
+    const int64_t total = (N - 1) * ldc + M;
+    for (int64_t a = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; a < total;
+         a += (int64_t)gridDim.x * blockDim.x) {
+        int64_t jlo, jhi;
+        if (!colmajor_pairs(a, M, N, ldc, &jlo, &jhi)) continue;
+        float v = tmp[jhi * tmp_ld + (a - jhi * ldc)];
+        if (bias)
+            for (int64_t j = jlo; j <= jhi; ++j) v = __fadd_rn(v, bias[a - j * ldc]);
+        C[a] = v;
+    }
+}
+
+// Copy-in of the ldc < M path (:339-343): tmp[j][i] = C[j*ldc + i].
+__global__ void colmajor_gather_kernel(float* tmp, const float* C, int64_t M, int64_t N,
+                                       int64_t ldc) {
+    const int64_t total = N * M;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j = e / M, i = e - j * M;
+        tmp[e] = C[j * ldc + i];
+    }
+}
+
+namespace {
+int grid_for(int64_t n) {
+    int64_t b = (n + 255) / 256;
+    return static_cast<int>(b < 148 * 8 ? (b > 0 ? b : 1) : 148 * 8);
+}
+}  // namespace
+
+cudaError_t launch_colmajor_k0(float* C, const float* bias, int64_t M, int64_t N, int64_t ldc,
+                               float beta, cudaStream_t s) {
+    colmajor_k0_kernel<<<grid_for((N - 1) * ldc + M), 256, 0, s>>>(C, bias, M, N, ldc, beta);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_colmajor_writeback(float* C, const float* tmp, int64_t tmp_ld, const float* bias,
+                                      int64_t M, int64_t N, int64_t ldc, cudaStream_t s) {
+    colmajor_writeback_kernel<<<grid_for((N - 1) * ldc + M), 256, 0, s>>>(C, tmp, tmp_ld, bias, M,
+                                                                          N, ldc);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_colmajor_gather(float* tmp, const float* C, int64_t M, int64_t N, int64_t ldc,
+                                   cudaStream_t s) {
+    colmajor_gather_kernel<<<grid_for(N * M), 256, 0, s>>>(tmp, C, M, N, ldc);
     return cudaGetLastError();
 }
 

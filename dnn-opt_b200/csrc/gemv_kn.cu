@@ -193,7 +193,7 @@ gemv_kn_kernel(const KnParams p) {
     auto store = [&](int m, int j, float sum) {
         if (m < g.M && n0 + j < g.N) {
             float* cp = C + (int64_t)m * g.ldc + n0 + j;
-            *cp = (g.beta == 0.0f) ? g.alpha * sum : fmaf(g.alpha, sum, g.beta * *cp);
+            *cp = add_bias((g.beta == 0.0f) ? g.alpha * sum : fmaf(g.alpha, sum, g.beta * *cp), g.bias, n0 + j);
         }
     };
 
@@ -287,7 +287,8 @@ gemv_kn_kernel(const KnParams p) {
 #pragma unroll
             for (int u = 0; u < VW; ++u)
                 if (n0 + j0 + u < g.N)
-                    crow[u] = (g.beta == 0.0f) ? g.alpha * sum[u] : fmaf(g.alpha, sum[u], g.beta * cv[u]);
+                    crow[u] = add_bias((g.beta == 0.0f) ? g.alpha * sum[u] : fmaf(g.alpha, sum[u], g.beta * cv[u]),
+                                       g.bias, n0 + j0 + u);
         }
         if (tid == 0) p.counters[blockIdx.x] = 0u;   // ready for the next launch on this stream
     }

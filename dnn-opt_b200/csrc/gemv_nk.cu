@@ -175,7 +175,7 @@ gemv_nk_kernel(const NkParams p) {
             const int m = lane;
             if constexpr (KIND == DotKind::F32) {
                 float* cp = static_cast<float*>(g.C) + (int64_t)m * g.ldc + n;
-                *cp = (g.beta == 0.0f) ? g.alpha * s : fmaf(g.alpha, s, g.beta * *cp);
+                *cp = add_bias((g.beta == 0.0f) ? g.alpha * s : fmaf(g.alpha, s, g.beta * *cp), g.bias, n);
             } else if constexpr (KIND == DotKind::S8S32) {
                 static_cast<int32_t*>(g.C)[(int64_t)m * g.ldc + n] = s;
             } else if constexpr (KIND == DotKind::S8DQ) {
@@ -331,7 +331,7 @@ gemv_rows_kernel(const RowsParams p) {
             if (m < g.M && n < row_end) {
                 if constexpr (KIND == DotKind::F32) {
                     float* cp = static_cast<float*>(g.C) + (int64_t)m * g.ldc + n;
-                    *cp = (g.beta == 0.0f) ? g.alpha * t : fmaf(g.alpha, t, g.beta * *cp);
+                    *cp = add_bias((g.beta == 0.0f) ? g.alpha * t : fmaf(g.alpha, t, g.beta * *cp), g.bias, n);
                 } else if constexpr (KIND == DotKind::S8S32) {
                     static_cast<int32_t*>(g.C)[(int64_t)m * g.ldc + n] = t;
                 } else {

@@ -31,6 +31,9 @@ struct GemmArgs {
     int b_trans;
     void* C;
     int64_t ldc;
+    // FP32-output paths only: bias[n] added to C[m][n] after the alpha/beta
+    // epilogue (the oneDNN entry's bias pass); nullptr for none.
+    const float* bias = nullptr;
 };
 
 // ---- small-M FP32-output GEMV, B is K x N (N contiguous) -------------------
@@ -109,6 +112,15 @@ cudaError_t launch_quantize_s8(const GemmArgs& g, const uint32_t* absmax_bits, f
 // gemm_fp8 FP32 API: encode A with the reference e4m3 codec (dense M x K) and
 // B with the reference e5m2 codec (dense K x N).
 cudaError_t launch_quantize_ref_fp8(const GemmArgs& g, uint8_t* qa, uint8_t* qb, cudaStream_t s);
+
+// Column-major C fix-ups of the oneDNN entry (footprint [0, (N-1)*ldc + M),
+// overlapping columns handled in the entry's sequential order).
+cudaError_t launch_colmajor_k0(float* C, const float* bias, int64_t M, int64_t N, int64_t ldc,
+                               float beta, cudaStream_t s);
+cudaError_t launch_colmajor_writeback(float* C, const float* tmp, int64_t tmp_ld, const float* bias,
+                                      int64_t M, int64_t N, int64_t ldc, cudaStream_t s);
+cudaError_t launch_colmajor_gather(float* tmp, const float* C, int64_t M, int64_t N, int64_t ldc,
+                                   cudaStream_t s);
 
 cudaError_t launch_saxpy(int n, float alpha, const float* x, int incx, float* y, int incy,
                          cudaStream_t s);

@@ -123,6 +123,23 @@ int dnnopt_gemm_e4m3_bf16(int M, int N, int K, const uint16_t* A, int lda, const
  * src/blas/cblas_sgemm.cpp:67-99), without materialising transposes. */
 int dnnopt_gemm_f32_desc(const dnnopt_gemm_desc* d, const float* A, const float* B, float* C);
 
+/* Replaces the oneDNN integration's dnnopt_sgemm (reference
+ * integration/onednn/0001-dnnopt-integration.patch:279-365), the hook the
+ * patched extended_sgemm calls: column-major (Fortran) arguments by pointer,
+ * C(M x N, ldc) = alpha * op(A) * op(B) + beta * C, then C[i + j*ldc] +=
+ * bias[i] when bias is non-null.  transa / transb: 'T'/'t' transposed,
+ * 'P'/'p' (packed) -> DNNOPT_STATUS_NOT_SUPPORTED (dnnl_unimplemented),
+ * anything else not transposed.  M == 0 or N == 0: no-op; K == 0: C is
+ * scaled by beta (zeroed for beta == 0) and the bias added.  ldc < M (the
+ * reference's temporary-buffer path, :330-353) gives what its column-by-column
+ * copy-back leaves.  Host or device pointers, synchronous; transposes are
+ * kernel flags (no transposed copies) and the bias is fused into the GEMM
+ * epilogue. */
+int dnnopt_sgemm_colmajor(const char* transa, const char* transb, const int64_t* M,
+                          const int64_t* N, const int64_t* K, const float* alpha, const float* A,
+                          const int64_t* lda, const float* B, const int64_t* ldb,
+                          const float* beta, float* C, const int64_t* ldc, const float* bias);
+
 /* Replaces cblas_saxpy (reference src/blas/cblas_saxpy.cpp:13-50):
  * Y[i*incY] += alpha * X[i*incX] for i < N; N <= 0 or alpha == 0 is a no-op;
  * negative increments are rejected. */
@@ -139,6 +156,12 @@ int dnnopt_gemm_get_num_threads(void);
  * ---------------------------------------------------------------------- */
 int dnnopt_cuda_gemm_f32(const dnnopt_gemm_desc* d, const float* A, const float* B, float* C,
                          void* stream);
+/* dnnopt_sgemm_colmajor on device pointers, stream-ordered. */
+int dnnopt_cuda_sgemm_colmajor(const char* transa, const char* transb, const int64_t* M,
+                               const int64_t* N, const int64_t* K, const float* alpha,
+                               const float* A, const int64_t* lda, const float* B,
+                               const int64_t* ldb, const float* beta, float* C, const int64_t* ldc,
+                               const float* bias, void* stream);
 int dnnopt_cuda_gemm_bf16f32(const dnnopt_gemm_desc* d, const uint16_t* A, const uint16_t* B,
                              float* C, void* stream);
 /* FP32 operands rounded to bf16 on load (dnnopt_gemm_bf16 semantics). */

@@ -129,6 +129,66 @@ float oracle_refe5m2_to_f32(uint8_t b) {
     return u2f((sign << 31) | ((uint32_t)((int)e - 16 + 127) << 23) | (m << 21));
 }
 
+/* ---------------- oneDNN entry (0001-dnnopt-integration.patch:243-365) --------- */
+int oracle_sgemm_colmajor(char transa, char transb, int64_t M, int64_t N, int64_t K, float alpha,
+                          const float* A, int64_t lda, const float* B, int64_t ldb, float beta,
+                          float* C, int64_t ldc, const float* bias) {
+    if (transa == 'P' || transa == 'p' || transb == 'P' || transb == 'p') return -1;   /* :284-286 */
+    if (M == 0 || N == 0) return 0;                                                  /* :289 */
+    if (K == 0) {                                                                    /* :290-304 */
+        if (beta == 0.0f) {
+            for (int64_t j = 0; j < N; ++j) memset(C + j * ldc, 0, (size_t)M * sizeof(float));
+        } else if (beta != 1.0f) {
+            for (int64_t j = 0; j < N; ++j)
+                for (int64_t i = 0; i < M; ++i) C[j * ldc + i] *= beta;
+        }
+        if (bias)
+            for (int64_t j = 0; j < N; ++j)
+                for (int64_t i = 0; i < M; ++i) C[j * ldc + i] += bias[i];
+        return 0;
+    }
+    const int tA = transa == 'T' || transa == 't', tB = transb == 'T' || transb == 't';
+    /* Row-major view (:306-322): rm = op(B)^T-side first.  X (rm_M x K) is
+     * op(B) read row-major, Y (K x rm_N) is op(A) read row-major. */
+    const int rm_M = (int)N, rm_N = (int)M, rm_K = (int)K;
+    const float* X = B;
+    int ldx = (int)ldb;
+    float* xt = NULL;
+    if (tB) {            /* dnnopt_gemm_row_major transA: stored K x rm_M -> dense rm_M x K (:249-253) */
+        xt = (float*)malloc((size_t)rm_M * rm_K * sizeof(float));
+        for (int r = 0; r < rm_M; ++r)
+            for (int k = 0; k < rm_K; ++k) xt[(size_t)r * rm_K + k] = B[(size_t)k * ldb + r];
+        X = xt; ldx = rm_K;
+    }
+    const float* Y = A;
+    int ldy = (int)lda;
+    float* yt = NULL;
+    if (tA) {            /* transB: stored rm_N x K -> dense K x rm_N (:254-258) */
+        yt = (float*)malloc((size_t)rm_K * rm_N * sizeof(float));
+        for (int k = 0; k < rm_K; ++k)
+            for (int c = 0; c < rm_N; ++c) yt[(size_t)k * rm_N + c] = A[(size_t)c * lda + k];
+        Y = yt; ldy = rm_N;
+    }
+    if (ldc >= rm_N) {
+        oracle_gemm_f32_naive(rm_M, rm_N, rm_K, alpha, X, ldx, Y, ldy, beta, C, (int)ldc);
+    } else {             /* :330-353 */
+        float* tmp = (float*)calloc((size_t)rm_M * rm_N, sizeof(float));
+        if (beta != 0.0f)
+            for (int r = 0; r < rm_M; ++r)
+                for (int c = 0; c < rm_N; ++c) tmp[(size_t)r * rm_N + c] = C[(size_t)r * ldc + c];
+        oracle_gemm_f32_naive(rm_M, rm_N, rm_K, alpha, X, ldx, Y, ldy, beta, tmp, rm_N);
+        for (int r = 0; r < rm_M; ++r)
+            for (int c = 0; c < rm_N; ++c) C[(size_t)r * ldc + c] = tmp[(size_t)r * rm_N + c];
+        free(tmp);
+    }
+    free(xt);
+    free(yt);
+    if (bias)            /* :355-362, column by column */
+        for (int64_t j = 0; j < N; ++j)
+            for (int64_t i = 0; i < M; ++i) C[j * ldc + i] += bias[i];
+    return 0;
+}
+
 /* ---------------- FP32 (gemm.cpp:88-100) ---------------- */
 void oracle_gemm_f32_naive(int M, int N, int K, float alpha, const float* A, int lda,
                            const float* B, int ldb, float beta, float* C, int ldc) {

@@ -84,6 +84,17 @@ void oracle_gemm_refe4m3_refe5m2(int M, int N, int K, float alpha, const uint8_t
 void oracle_gemm_refe5m2_refe5m2(int M, int N, int K, float alpha, const uint8_t* A, int lda,
                                  const uint8_t* B, int ldb, float beta, float* C, int ldc);
 
+/* The oneDNN integration's dnnopt_sgemm (integration/onednn/
+ * 0001-dnnopt-integration.patch:279-365, with dnnopt_gemm_row_major
+ * :243-267): column-major arguments, C(M x N, ldc) = alpha*op(A)*op(B) +
+ * beta*C through RowMajor(op B, op A, N, M, K, B, ldb, A, lda, C, ldc) on
+ * dense transposed copies and the naive FP32 GEMM, the ldc < M temporary
+ * buffer and its copy-back, then C[i + j*ldc] += bias[i] (column by column).
+ * Returns 0, or -1 for packed ('P') operands. */
+int oracle_sgemm_colmajor(char transa, char transb, int64_t M, int64_t N, int64_t K, float alpha,
+                          const float* A, int64_t lda, const float* B, int64_t ldb, float beta,
+                          float* C, int64_t ldc, const float* bias);
+
 #ifdef __cplusplus
 }
 #endif

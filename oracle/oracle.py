@@ -44,6 +44,10 @@ def load_oracle():
     lib.oracle_gemm_bf16f32.argtypes = sig + [_P, _I]
     lib.oracle_gemm_e4m3bf16.argtypes = [_I, _I, _I, _P, _I, _P, _I, _P, _P, _I, _P, _I]
     lib.oracle_quantize_e4m3_rows.argtypes = [_I, _I, _P, _I, _P, _P, _I]
+    _L = ctypes.c_int64
+    lib.oracle_sgemm_colmajor.argtypes = [ctypes.c_char, ctypes.c_char, _L, _L, _L, _F, _P, _L, _P,
+                                          _L, _F, _P, _L, _P]
+    lib.oracle_sgemm_colmajor.restype = _I
     return lib
 
 
@@ -108,6 +112,10 @@ class Oracle:
 
     def gemm_f32(self, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc):
         self.lib.oracle_gemm_f32_naive(M, N, K, alpha, _p(A), lda, _p(B), ldb, beta, _p(C), ldc)
+
+    def sgemm_colmajor(self, transa, transb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, bias=None):
+        return self.lib.oracle_sgemm_colmajor(transa.encode(), transb.encode(), M, N, K, alpha, _p(A),
+                                              lda, _p(B), ldb, beta, _p(C), ldc, _p(bias))
 
     def gemm_f32_f64(self, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, threads=8):
         out = np.zeros(M * N, np.float64)

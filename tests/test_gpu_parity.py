@@ -175,6 +175,88 @@ def test_cblas_against_reference(gpu, dn, golden, size):
     assert np.max(np.abs(C - golden[f"fortran_{M}x{N}x{K}"])) <= fp32_tol(K)
 
 
+# ------------------------------------------------ oneDNN entry (col-major) ---
+COLMAJOR_CASES = [
+    # M, N, K, transa, transb, lda_pad, ldb_pad, ldc_pad, alpha, beta, bias
+    (4096, 1, 4096, "T", "N", 0, 0, 0, 1.0, 0.0, True),      # inner product, batch 1
+    (1009, 7, 1024, "T", "N", 0, 0, 0, 1.0, 0.5, True),      # small batch, prime OC
+    (2039, 3, 1024, "N", "N", 5, 0, 3, 0.75, 1.0, True),
+    (257, 5, 96, "N", "T", 3, 1, 2, 1.0, 0.0, False),
+    (300, 7, 128, "T", "T", 0, 4, 0, 1.0, -0.5, True),
+    (64, 33, 40, "N", "N", 0, 0, 0, 1.0, 1.0, True),         # M > 8 rows in the row-major view
+    (256, 256, 256, "N", "N", 0, 0, 0, 1.0, 0.0, True),
+]
+
+
+@pytest.mark.parametrize("case", COLMAJOR_CASES)
+def test_sgemm_colmajor_matches_oracle(gpu, dn, orc, case):
+    """dnnopt_sgemm_colmajor (host arrays) and dnnopt_cuda_sgemm_colmajor
+    (device tensors) against the oracle's restatement of the oneDNN entry."""
+    from tests.test_oracle_colmajor import operands
+    torch = gpu
+    M, N, K, ta, tb, pa, pb, pc, alpha, beta, with_bias = case
+    A, lda, B, ldb, C, ldc = operands(M, N, K, ta, tb, pa, pb, pc)
+    bias = ref_uniform(M, 5) if with_bias else None
+    ref = C.copy()
+    assert orc.sgemm_colmajor(ta, tb, M, N, K, alpha, A, lda, B, ldb, beta, ref, ldc, bias) == 0
+    host = C.copy()
+    dn.check(dn.sgemm_colmajor(ta, tb, M, N, K, alpha, A, lda, B, ldb, beta, host, ldc, bias))
+    assert np.max(np.abs(host - ref)) <= fp32_tol(K)
+    dA, dB, dC = (torch.from_numpy(x).cuda() for x in (A, B, C))
+    dbias = torch.from_numpy(bias).cuda() if with_bias else None
+    s = torch.cuda.current_stream()
+    dn.check(dn.cuda_sgemm_colmajor(ta, tb, M, N, K, alpha, dA, lda, dB, ldb, beta, dC, ldc, dbias, s))
+    torch.cuda.synchronize()
+    out = dC.cpu().numpy()
+    assert np.max(np.abs(out - ref)) <= fp32_tol(K)
+    # Padding between columns of C is left alone.
+    for j in range(N):
+        assert np.array_equal(out[j * ldc + M:(j + 1) * ldc], C[j * ldc + M:(j + 1) * ldc])
+
+
+def test_host_entry_keeps_c_padding(gpu, dn, orc):
+    """Host-pointer calls stage C's whole span (rows padded to ldc); with
+    beta == 0 the padding must still come back unchanged."""
+    M, N, K, ldc = 5, 257, 96, 260
+    A, B = ref_uniform(M * K, 1), ref_uniform(K * N, 2)
+    C = ref_uniform(M * ldc, 3)
+    ref = C.copy()
+    orc.gemm_f32(M, N, K, 1.0, A, K, B, N, 0.0, ref, ldc)
+    out = C.copy()
+    dn.check(dn.gemm_fp32(M, N, K, 1.0, A, K, B, N, 0.0, out, ldc))
+    assert np.max(np.abs(out - ref)) <= fp32_tol(K)
+    for m in range(M):
+        assert np.array_equal(out[m * ldc + N:(m + 1) * ldc], C[m * ldc + N:(m + 1) * ldc])
+
+
+def test_sgemm_colmajor_k0_and_overlapping_ldc(gpu, dn, orc):
+    torch = gpu
+    # K == 0: C scaled by beta (cleared for beta == 0, NaN included), bias added; bit-exact.
+    M, N, ldc = 37, 5, 40
+    for beta in (0.0, 1.0, 2.0):
+        C = ref_uniform(ldc * N, 3)
+        C[1] = np.nan if beta == 0.0 else C[1]
+        bias = ref_uniform(M, 4)
+        ref = C.copy()
+        orc.sgemm_colmajor("N", "N", M, N, 0, 1.0, None, M, None, 1, beta, ref, ldc, bias)
+        dC = torch.from_numpy(C).cuda()
+        dn.check(dn.cuda_sgemm_colmajor("N", "N", M, N, 0, 1.0, None, M, None, 1, beta, dC, ldc,
+                                        torch.from_numpy(bias).cuda(), torch.cuda.current_stream()))
+        torch.cuda.synchronize()
+        assert np.array_equal(dC.cpu().numpy().view(np.uint32), ref.view(np.uint32)), beta
+    # ldc < M: the temporary-buffer path with its column-by-column copy-back.
+    for (M, N, K, ldc, beta) in [(6, 4, 9, 4, 0.5), (20, 9, 33, 12, 0.0), (300, 3, 64, 128, 1.0)]:
+        from tests.test_oracle_colmajor import operands
+        A, lda, B, ldb, _, _ = operands(M, N, K, "N", "N")
+        C = ref_uniform((N - 1) * ldc + M, 11)
+        bias = ref_uniform(M, 12)
+        ref = C.copy()
+        orc.sgemm_colmajor("N", "N", M, N, K, 1.0, A, lda, B, ldb, beta, ref, ldc, bias)
+        host = C.copy()
+        dn.check(dn.sgemm_colmajor("N", "N", M, N, K, 1.0, A, lda, B, ldb, beta, host, ldc, bias))
+        assert np.max(np.abs(host - ref)) <= fp32_tol(K), (M, N, K, ldc)
+
+
 def test_cblas_256_all_orders(gpu, dn, orc):
     from tests.test_oracle_golden import cblas_by_oracle
     lib = cblas(dn)
