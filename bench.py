@@ -296,6 +296,23 @@ def per_config(torch, dn, stream, pk, world, rank, dist):
                                   "GB_s": r["GB_s"], "hbm_frac": r["GB_s"] / pk["hbm_gbs"],
                                   "kernel": dn.plan_describe(dn.KIND_F32, d)}
     del As, Bs, Cs
+    # The oneDNN entry on an inner-product pattern: column-major C (OC x batch)
+    # = W^T-stored weights x activations + bias, through dnnopt_cuda_sgemm_colmajor.
+    M, N, K = 4096, 1, 4096
+    Ws = [torch.from_numpy(ref_uniform(M * K, 52 + i)).cuda() for i in range(N_SETS)]
+    Xs = [torch.from_numpy(ref_uniform(K * N, 133 + i)).cuda() for i in range(N_SETS)]
+    Ys = [torch.zeros(M * N, device="cuda") for _ in range(N_SETS)]
+    bias = torch.from_numpy(ref_uniform(M, 7)).cuda()
+    fns = [lambda i=i: dn.cuda_sgemm_colmajor("T", "N", M, N, K, 1.0, Ws[i], K, Xs[i], K, 0.0, Ys[i], M,
+                                              bias, s) for i in range(N_SETS)]
+    for f in fns:
+        dn.check(f())
+    r = bench_single(torch, dn, s, fns, 4 * (M * K + K * N + M * N + M), 2.0 * M * N * K)
+    out["onednn_sgemm_T_N_4096x1x4096_bias"] = {
+        "GFLOP_s": r["TFLOP_s"] * 1e3, "us": r["us_per_call"], "GB_s": r["GB_s"],
+        "hbm_frac": r["GB_s"] / pk["hbm_gbs"],
+        "kernel": dn.plan_describe(dn.KIND_F32, dn.desc(N, M, K, K, K, M, trans_b=1)) + " + bias epilogue"}
+    del Ws, Xs, Ys
     # C3: INT8 4 x 11008 x 4096, B is [N, K].
     M, N, K = 4, 11008, 4096
     As = [torch.from_numpy(int8_uniform(M * K, 42 + i)).cuda() for i in range(N_SETS)]

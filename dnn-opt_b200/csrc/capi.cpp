@@ -108,6 +108,17 @@ int launch_plan(Kind kind, const GemmArgs& g, const Plan& p, const float* scales
             note_launch();
             break;
         case KernelId::GemvSlab:
+            if (g.bias) {
+                // The slab kernel has no bias epilogue; biased calls (the oneDNN
+                // entry) take the split-K kernel of the same plan family.
+                const GemvKnPlan kp = kn_plan_for(kind, g, info_of(ctx), 0, false);
+                st = ensure_workspace(ctx, s, gemv_kn_ws_floats(kp, g.N),
+                                      static_cast<size_t>(gemv_kn_tiles(g.N)), 0, &w);
+                if (st != DNNOPT_STATUS_SUCCESS) return st;
+                e = launch_gemv_kn(in_a(kind), in_b(kind), g, kp, w->ws, w->counters, s);
+                note_launch();
+                break;
+            }
             e = launch_gemv_slab(in_a(kind), in_b(kind), g, p.kn.mt, p.slab_w, s);
             note_launch();
             break;

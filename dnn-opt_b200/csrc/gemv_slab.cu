@@ -15,6 +15,9 @@
 //     atomic ticket, no second pass over memory; the host picks W = 16 when
 //     8-column slabs would need more than one wave of resident CTAs, or for
 //     M <= 4 from 1536 columns on;
+//   * no bias epilogue: it costs the no-bias form registers (63 -> 68 at
+//     M <= 2) and sweep time; calls with a bias vector take the split-K
+//     kernel instead;
 //   * lane l reads column l % W of rows l / W + (32 / W) * warp + 256 / W * i:
 //     a warp load covers 32 / W row segments of 4W bytes (rows need no
 //     alignment, so prime N works), and every thread issues its first 2 x 16
@@ -179,8 +182,7 @@ __device__ __forceinline__ void slab_body(const GemmArgs& g, int slab, float* sA
         float sum = 0.0f;
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) sum += red[w][wm][wc];
-        C[(int64_t)wm * g.ldc + n0 + wc] =
-            add_bias((g.beta == 0.0f) ? g.alpha * sum : fmaf(g.alpha, sum, g.beta * c_old), g.bias, n0 + wc);
+        C[(int64_t)wm * g.ldc + n0 + wc] = (g.beta == 0.0f) ? g.alpha * sum : fmaf(g.alpha, sum, g.beta * c_old);
     }
 }
 
@@ -194,26 +196,10 @@ gemv_slab_kernel(const SlabParams p) {
     slab_body<IA, IB, MT, W>(p.g, blockIdx.x, sA, red);
 }
 
-// The same body held to 64 registers (four CTAs per SM); used for FP32 with
-// MT == 2, which fits without spilling.
-template <In IA, In IB, int MT, int W>
-__global__ void __launch_bounds__(kThreads, 4)
-gemv_slab_kernel_occ4(const SlabParams p) {
-    extern __shared__ __align__(16) float sA[];
-    __shared__ float red[kWarps][MT][W];
-    pdl_wait();
-    pdl_launch_dependents();
-    slab_body<IA, IB, MT, W>(p.g, blockIdx.x, sA, red);
-}
-
 template <In IA, In IB, int MT>
 const void* slab_fn(int w) {
-    if constexpr (IA == In::F32 && IB == In::F32 && MT == 2)
-        return w == 16 ? reinterpret_cast<const void*>(&gemv_slab_kernel_occ4<IA, IB, MT, 16>)
-                       : reinterpret_cast<const void*>(&gemv_slab_kernel_occ4<IA, IB, MT, 8>);
-    else
-        return w == 16 ? reinterpret_cast<const void*>(&gemv_slab_kernel<IA, IB, MT, 16>)
-                       : reinterpret_cast<const void*>(&gemv_slab_kernel<IA, IB, MT, 8>);
+    return w == 16 ? reinterpret_cast<const void*>(&gemv_slab_kernel<IA, IB, MT, 16>)
+                   : reinterpret_cast<const void*>(&gemv_slab_kernel<IA, IB, MT, 8>);
 }
 
 template <In IA, In IB>
