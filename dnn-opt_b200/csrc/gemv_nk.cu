@@ -199,9 +199,14 @@ gemv_nk_kernel(const NkParams p) {
 // so each lane keeps its slice of A in registers for every row instead of
 // re-reading it from shared memory.  A CTA walks its contiguous row range R
 // rows at a time (R independent 16-byte loads in flight per chunk and lane),
-// accumulates MT x R partial dot products, and reduces them with a
-// 31-shuffle transpose-reduce (lane l ends with the warp total of value l),
-// then across the 8 warps through shared memory in warp order.
+// accumulates V = MT x R partial dot products, and reduces them with a
+// transpose-reduce over lane offsets V/2 .. 1 (lane l keeps value l % V)
+// followed by plain butterfly sums over offsets V .. 16, then across the 8
+// warps through shared memory in warp order.  V = 32 (MT x R = 4 x 8 or
+// 8 x 4) for K up to 512 chunks; V = 8 (MT = 2, R = 4, four chunks per lane)
+// carries M <= 2 rows of FP32 up to K = 4096 (inner products y = W x with W
+// stored row by row: 16 KB rows, A's 4096 values spread over the CTA's
+// registers).
 // ---------------------------------------------------------------------------
 template <DotKind KIND> struct Chunk;
 template <> struct Chunk<DotKind::F32> {
@@ -256,7 +261,8 @@ gemv_rows_kernel(const RowsParams p) {
     using C = Chunk<KIND>;
     using Acc = typename C::Acc;
     using TA = typename Tr<KIND>::TA;
-    static_assert(MT * R == 32, "one value per lane after the transpose-reduce");
+    constexpr int V = MT * R;
+    static_assert(V == 8 || V == 16 || V == 32, "V values per lane, a power of two up to 32");
     __shared__ Acc red[2][kWarps][32];
 
     pdl_wait();
@@ -299,7 +305,7 @@ gemv_rows_kernel(const RowsParams p) {
     int buf = 0;
     for (int r0 = row_begin; r0 < row_end; r0 += R, buf ^= 1) {
         if (r0 + R < row_end) load_rows(bn, r0 + R);
-        Acc v[32];
+        Acc v[V];
 #pragma unroll
         for (int m = 0; m < MT; ++m)
 #pragma unroll
@@ -310,9 +316,11 @@ gemv_rows_kernel(const RowsParams p) {
                 v[m * R + r] = acc;
             }
         // Transpose-reduce: after the step with offset s, a lane keeps the half
-        // selected by its bit s; lane l ends with the warp sum of value l.
+        // selected by its bit s; lane l ends with the sum of value l % V over
+        // the lanes that differ from it in bits below V, and the butterfly
+        // adds the lanes that differ above.
 #pragma unroll
-        for (int s = 16; s >= 1; s >>= 1) {
+        for (int s = V / 2; s >= 1; s >>= 1) {
             const bool upper = (lane & s) != 0;
 #pragma unroll
             for (int i = 0; i < s; ++i) {
@@ -321,9 +329,11 @@ gemv_rows_kernel(const RowsParams p) {
                 v[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, s);
             }
         }
+#pragma unroll
+        for (int o = V; o < 32; o <<= 1) v[0] += __shfl_xor_sync(0xFFFFFFFFu, v[0], o);
         red[buf][warp][lane] = v[0];
         __syncthreads();
-        if (warp == 0) {
+        if (warp == 0 && lane < V) {
             Acc t = red[buf][0][lane];
 #pragma unroll
             for (int w = 1; w < kWarps; ++w) t += red[buf][w][lane];
@@ -361,16 +371,25 @@ const void* rows_select_mt(int mt) {
     }
 }
 
-const void* rows_select(DotKind kind, int mt, int kch) {
+// Kernel and rows per step for `kch` 16-byte chunks per lane (1, 2, or 3-4
+// for the deep FP32 variant, M <= 2 only).
+struct RowsCfg {
+    const void* fn;
+    int R;
+};
+RowsCfg rows_cfg(DotKind kind, int mt, int kch) {
+    if (kch > 2) {
+        if (kind != DotKind::F32 || mt > 2 || kch > 4) return {nullptr, 0};
+        return {reinterpret_cast<const void*>(&gemv_rows_kernel<DotKind::F32, 2, 4, 4>), 4};
+    }
+    const int R = mt <= 4 ? 8 : 4;
     switch (kind) {
-        case DotKind::F32: return kch == 1 ? rows_select_mt<DotKind::F32, 1>(mt) : rows_select_mt<DotKind::F32, 2>(mt);
-        case DotKind::S8S32: return kch == 1 ? rows_select_mt<DotKind::S8S32, 1>(mt) : rows_select_mt<DotKind::S8S32, 2>(mt);
-        case DotKind::S8DQ: return kch == 1 ? rows_select_mt<DotKind::S8DQ, 1>(mt) : rows_select_mt<DotKind::S8DQ, 2>(mt);
-        default: return nullptr;
+        case DotKind::F32: return {kch == 1 ? rows_select_mt<DotKind::F32, 1>(mt) : rows_select_mt<DotKind::F32, 2>(mt), R};
+        case DotKind::S8S32: return {kch == 1 ? rows_select_mt<DotKind::S8S32, 1>(mt) : rows_select_mt<DotKind::S8S32, 2>(mt), R};
+        case DotKind::S8DQ: return {kch == 1 ? rows_select_mt<DotKind::S8DQ, 1>(mt) : rows_select_mt<DotKind::S8DQ, 2>(mt), R};
+        default: return {nullptr, 0};
     }
 }
-
-int rows_r(int mt) { return mt <= 4 ? 8 : 4; }
 
 template <DotKind KIND, int MT, bool VEC>
 const void* nk_fn() {
@@ -464,13 +483,14 @@ bool gemv_rows_supported(DotKind kind, const GemmArgs& g) {
     if (kind == DotKind::E4M3 || g.M < 1 || g.M > 8) return false;
     const int epc_ = epc(kind);
     const size_t eb = kind == DotKind::F32 ? 4 : 1;
-    if (g.K % epc_ != 0 || g.K / epc_ > 2 * kThreads) return false;
+    const int max_chunks = (kind == DotKind::F32 && g.M <= 2) ? 4 * kThreads : 2 * kThreads;
+    if (g.K % epc_ != 0 || g.K / epc_ > max_chunks) return false;
     return reinterpret_cast<uintptr_t>(g.B) % 16 == 0 && (static_cast<size_t>(g.ldb) * eb) % 16 == 0;
 }
 
 cudaError_t gemv_rows_occupancy(DotKind kind, int mt, int K, int* blocks_per_sm) {
     const int kch = (K / epc(kind) + kThreads - 1) / kThreads;
-    const void* fn = rows_select(kind, mt, kch <= 1 ? 1 : 2);
+    const void* fn = rows_cfg(kind, mt, kch <= 1 ? 1 : kch).fn;
     if (!fn) return cudaErrorInvalidValue;
     return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, fn, kThreads, 0);
 }
@@ -479,9 +499,10 @@ cudaError_t launch_gemv_rows(DotKind kind, const GemmArgs& g, int mt, int grid, 
                              cudaStream_t s) {
     if (!gemv_rows_supported(kind, g) || g.M > mt) return cudaErrorInvalidValue;
     const int kch = (g.K / epc(kind) + kThreads - 1) / kThreads;
-    const void* fn = rows_select(kind, mt, kch <= 1 ? 1 : 2);
+    const RowsCfg rc = rows_cfg(kind, mt, kch <= 1 ? 1 : kch);
+    const void* fn = rc.fn;
     if (!fn) return cudaErrorInvalidValue;
-    const int R = rows_r(mt);
+    const int R = rc.R;
     const int groups = (g.N + R - 1) / R;
     if (grid < 1) grid = 1;
     if (grid > groups) grid = groups;

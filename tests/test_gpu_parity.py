@@ -276,7 +276,10 @@ def test_cblas_256_all_orders(gpu, dn, orc):
 
 
 @pytest.mark.parametrize("M,N,K,beta", [(5, 777, 1024, 0.5), (1, 4096, 4096, 0.0), (8, 300, 8000, -1.0),
-                                         (3, 64, 30, 0.0)])
+                                         (3, 64, 30, 0.0),
+                                         # register-resident dot form, 3-4 chunks per lane (M <= 2)
+                                         (2, 4096, 4096, 0.5), (1, 1001, 3072, 1.0), (2, 37, 2052, 0.0),
+                                         (1, 3, 4092, 0.5)])
 def test_fp32_transposed_b_small_m(gpu, dn, orc, M, N, K, beta):
     """op(B) = B^T (B stored N x K): the dot-form kernels."""
     torch = gpu
