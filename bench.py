@@ -256,7 +256,7 @@ def capture(torch, stream, fn):
 # dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum --csv
 # -k regex:gemv -s 12 -c 12 python bench.py --profile c2 --reps 2
 # (C is written into L2 and leaves it after the launch, so writes read 0).
-C2_DRAM_BYTES_PER_STEP = 117_954_304
+C2_DRAM_BYTES_PER_STEP = 117_963_264
 
 
 def bench_single(torch, dn, stream, fn_list, bytes_per_call, flops_per_call, iters=30):
@@ -440,6 +440,15 @@ def run_profile(args):
             B = torch.from_numpy(ref_uniform(K * N, 123 + i)).cuda()
             C = torch.zeros(M * N, device="cuda")
             calls.append(lambda A=A, B=B, C=C: dn.cuda_gemm("f32", d, A, B, C, s))
+    elif name == "onednn":
+        M, N, K = 4096, 1, 4096
+        bias = torch.from_numpy(ref_uniform(M, 7)).cuda()
+        for i in range(N_SETS):
+            W = torch.from_numpy(ref_uniform(M * K, 52 + i)).cuda()
+            X = torch.from_numpy(ref_uniform(K * N, 133 + i)).cuda()
+            Y = torch.zeros(M * N, device="cuda")
+            calls.append(lambda W=W, X=X, Y=Y: dn.cuda_sgemm_colmajor("T", "N", M, N, K, 1.0, W, K, X, K,
+                                                                      0.0, Y, M, bias, s))
     elif name == "c3":
         M, N, K = 4, 11008, 4096
         d = dn.desc(M, N, K, K, K, N)
@@ -637,7 +646,7 @@ def main():
     ap.add_argument("--streams", type=int, default=SWEEP_STREAMS,
                     help="streams the 12 independent sweep GEMMs are spread over")
     ap.add_argument("--no-per-config", action="store_true", help="skip the per-config section")
-    ap.add_argument("--profile", choices=["c1", "c2", "c3", "c4", "c5"],
+    ap.add_argument("--profile", choices=["c1", "c2", "c3", "c4", "c5", "onednn"],
                     help="run one config's kernel --reps times for an ncu capture, no bench line")
     ap.add_argument("--reps", type=int, default=3)
     args = ap.parse_args()
