@@ -164,7 +164,7 @@ int launch_plan(Kind kind, const GemmArgs& g, const Plan& p, const float* scales
         case KernelId::TileF32:
             if (kind == Kind::E4M3BF16 || kind == Kind::S8S32 || kind == Kind::F32S8Q)
                 return set_status(DNNOPT_STATUS_NOT_SUPPORTED);
-            e = launch_gemm_tile_f32(in_a(kind), in_b(kind), g, s);
+            e = launch_gemm_simt(in_a(kind), in_b(kind), g, p.simt, s);
             note_launch();
             break;
         case KernelId::TileS8:

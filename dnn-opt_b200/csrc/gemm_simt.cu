@@ -1,0 +1,348 @@
+// General FP32-accumulate GEMM on the CUDA cores for everything the
+// specialised kernels do not take: M from 9 up (small-M bands above the GEMV
+// kernels' M <= 8), any transposition, any alignment, and the FP32-API
+// element encodings (FP32, BF16, FP32 rounded to BF16, the reference's fp8
+// codecs).  It replaces the reference's generic paths for these shapes:
+// gemm_fp32's adaptive-tile / packed registry range (src/gemm/gemm.cpp:295-347,
+// src/gemm/gemm_adaptive_tile_fp32.cpp:664-784) and gemm_driver_generic
+// (src/gemm/gemm_driver_generic.cpp:27-248) with C = alpha*A*B + beta*C.
+//
+// FP32 results must match the reference within 1e-5*K, so the products stay
+// FP32 FMAs (no TF32/BF16 tensor-core rounding).  Design:
+//   * CTA tile BM x 128 (BM = 16, 32 or 64 by M), 256 threads, each thread
+//     BM/8 rows x 4 consecutive columns; K in 32-deep slices staged in two
+//     shared-memory buffers, the next slice's global loads issued before the
+//     current slice's FMAs (register prefetch), one barrier per slice;
+//   * A is staged k-major (a thread's BM/8 row values come back as 16-byte
+//     broadcast loads), B n-major (one 16-byte load per thread and k);
+//   * small tile counts split K over up to 8 CTAs of one thread-block cluster;
+//     the partial tiles are summed through distributed shared memory in rank
+//     order (deterministic), each CTA finishing 1/S of the tile;
+//   * epilogue beta == 0 ? alpha*acc : fma(alpha, acc, beta*C), then + bias[n]
+//     when the oneDNN entry passes one.
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "common.cuh"
+#include "elem.cuh"
+#include "kernels.h"
+
+namespace dnnopt_b200 {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int BN = 128;
+constexpr int BK = 32;
+constexpr int kPadA = 4;      // keeps 16-byte alignment of k-major rows
+constexpr int kPadB = 4;
+constexpr int kMaxSplits = 8;
+
+struct SimtParams {
+    GemmArgs g;
+    int kchunk;     // K rows per split (multiple of BK)
+    int vec_b;      // 1: B is K x N with 16-byte aligned rows (4-wide loads)
+};
+
+template <int BM>
+constexpr size_t simt_smem_bytes() {
+    return 2 * (static_cast<size_t>(BK) * (BM + kPadA) + static_cast<size_t>(BK) * (BN + kPadB)) *
+           sizeof(float);
+}
+
+template <In IA, In IB, int BM>
+__global__ void __launch_bounds__(kThreads, 2)
+gemm_simt_kernel(const SimtParams p) {
+    using TA = typename Elem<IA>::T;
+    using TB = typename Elem<IB>::T;
+    constexpr int TM = BM / 8;                       // rows per thread
+    constexpr int LA = BM * BK / kThreads;           // A elements each thread stages per slice
+    constexpr int LB = BK * BN / kThreads;           // B elements (16)
+    constexpr int SA = BK * (BM + kPadA);            // floats per A buffer
+    constexpr int SB = BK * (BN + kPadB);
+    extern __shared__ __align__(16) float smem[];
+    float* sA = smem;                 // [2][BK][BM + kPadA]
+    float* sB = smem + 2 * SA;        // [2][BK][BN + kPadB]
+
+    pdl_wait();
+    pdl_launch_dependents();
+
+    const GemmArgs& g = p.g;
+    const int tid = threadIdx.x;
+    const int tx = tid & 31, ty = tid >> 5;          // columns 4*tx.., rows TM*ty..
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+    const int k_begin = blockIdx.z * p.kchunk;
+    const int k_end = min(g.K, k_begin + p.kchunk);
+    const int nslices = k_end > k_begin ? (k_end - k_begin + BK - 1) / BK : 0;
+    const TA* A = static_cast<const TA*>(g.A);
+    const TB* B = static_cast<const TB*>(g.B);
+
+    float ra[LA], rb[LB];
+    auto load_slice = [&](int k0) {
+#pragma unroll
+        for (int i = 0; i < LA; ++i) {
+            const int e = tid + i * kThreads;
+            int m, k;
+            if (g.a_trans) { m = e % BM; k = e / BM; } else { k = e % BK; m = e / BK; }
+            const int gm = m0 + m, gk = k0 + k;
+            ra[i] = (gm < g.M && gk < k_end)
+                        ? dec<IA>(A[g.a_trans ? (int64_t)gk * g.lda + gm : (int64_t)gm * g.lda + gk])
+                        : 0.0f;
+        }
+        if (!g.b_trans && p.vec_b) {
+#pragma unroll
+            for (int i = 0; i < LB / 4; ++i) {
+                const int e = tid + i * kThreads;
+                const int n4 = e % (BN / 4), k = e / (BN / 4);
+                const int gn = n0 + 4 * n4, gk = k0 + k;
+                float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                if (gk < k_end) {
+                    const TB* row = B + (int64_t)gk * g.ldb + gn;
+                    if (gn + 4 <= g.N) {
+                        load4<IB>(row, v);
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < 4; ++c)
+                            if (gn + c < g.N) v[c] = dec<IB>(row[c]);
+                    }
+                }
+#pragma unroll
+                for (int c = 0; c < 4; ++c) rb[4 * i + c] = v[c];
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < LB; ++i) {
+                const int e = tid + i * kThreads;
+                int n, k;
+                if (g.b_trans) { k = e % BK; n = e / BK; } else { n = e % BN; k = e / BN; }
+                const int gn = n0 + n, gk = k0 + k;
+                rb[i] = (gn < g.N && gk < k_end)
+                            ? dec<IB>(B[g.b_trans ? (int64_t)gn * g.ldb + gk : (int64_t)gk * g.ldb + gn])
+                            : 0.0f;
+            }
+        }
+    };
+    auto store_slice = [&](int buf) {
+        float* a = sA + buf * SA;
+        float* b = sB + buf * SB;
+#pragma unroll
+        for (int i = 0; i < LA; ++i) {
+            const int e = tid + i * kThreads;
+            int m, k;
+            if (g.a_trans) { m = e % BM; k = e / BM; } else { k = e % BK; m = e / BK; }
+            a[k * (BM + kPadA) + m] = ra[i];
+        }
+        if (!g.b_trans && p.vec_b) {
+#pragma unroll
+            for (int i = 0; i < LB / 4; ++i) {
+                const int e = tid + i * kThreads;
+                const int n4 = e % (BN / 4), k = e / (BN / 4);
+                *reinterpret_cast<float4*>(&b[k * (BN + kPadB) + 4 * n4]) =
+                    make_float4(rb[4 * i], rb[4 * i + 1], rb[4 * i + 2], rb[4 * i + 3]);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < LB; ++i) {
+                const int e = tid + i * kThreads;
+                int n, k;
+                if (g.b_trans) { k = e % BK; n = e / BK; } else { n = e % BN; k = e / BN; }
+                b[k * (BN + kPadB) + n] = rb[i];
+            }
+        }
+    };
+
+    float acc[TM][4];
+#pragma unroll
+    for (int r = 0; r < TM; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[r][c] = 0.0f;
+
+    if (nslices > 0) {
+        load_slice(k_begin);
+        store_slice(0);
+        __syncthreads();
+    }
+    for (int t = 0; t < nslices; ++t) {
+        const int buf = t & 1;
+        if (t + 1 < nslices) load_slice(k_begin + (t + 1) * BK);
+        const float* a = sA + buf * SA + ty * TM;
+        const float* b = sB + buf * SB + 4 * tx;
+#pragma unroll 8
+        for (int k = 0; k < BK; ++k) {
+            float av[TM];
+            if constexpr (TM >= 4) {
+#pragma unroll
+                for (int q = 0; q < TM / 4; ++q) {
+                    const float4 v = *reinterpret_cast<const float4*>(a + k * (BM + kPadA) + 4 * q);
+                    av[4 * q] = v.x; av[4 * q + 1] = v.y; av[4 * q + 2] = v.z; av[4 * q + 3] = v.w;
+                }
+            } else {
+                const float2 v = *reinterpret_cast<const float2*>(a + k * (BM + kPadA));
+                av[0] = v.x; av[1] = v.y;
+            }
+            const float4 bv = *reinterpret_cast<const float4*>(b + k * (BN + kPadB));
+#pragma unroll
+            for (int r = 0; r < TM; ++r) {
+                acc[r][0] = fmaf(av[r], bv.x, acc[r][0]);
+                acc[r][1] = fmaf(av[r], bv.y, acc[r][1]);
+                acc[r][2] = fmaf(av[r], bv.z, acc[r][2]);
+                acc[r][3] = fmaf(av[r], bv.w, acc[r][3]);
+            }
+        }
+        if (t + 1 < nslices) store_slice(buf ^ 1);
+        __syncthreads();
+    }
+
+    float* C = static_cast<float*>(g.C);
+    auto finish = [&](int gm, int gn, float sum) {
+        float* cp = C + (int64_t)gm * g.ldc + gn;
+        *cp = add_bias((g.beta == 0.0f) ? g.alpha * sum : fmaf(g.alpha, sum, g.beta * *cp), g.bias, gn);
+    };
+    if (gridDim.z == 1) {
+#pragma unroll
+        for (int r = 0; r < TM; ++r) {
+            const int gm = m0 + ty * TM + r;
+            if (gm >= g.M) continue;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int gn = n0 + 4 * tx + c;
+                if (gn < g.N) finish(gm, gn, acc[r][c]);
+            }
+        }
+        return;
+    }
+    // K split over the cluster: every CTA parks its partial tile in its own
+    // shared memory (the stage buffers are idle after the last barrier), then
+    // CTA q sums elements q, q + S, ... of the tile over ranks 0..S-1.
+    float* part = smem;                              // [BM][BN]
+#pragma unroll
+    for (int r = 0; r < TM; ++r)
+        *reinterpret_cast<float4*>(&part[(ty * TM + r) * BN + 4 * tx]) =
+            make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+    cluster_sync_all();
+    const uint32_t S = gridDim.z;
+    const uint32_t q = cluster_ctarank();
+    const uint32_t part_addr = smem_u32(part);
+    for (int e = static_cast<int>(q) * kThreads + tid; e < BM * BN; e += static_cast<int>(S) * kThreads) {
+        const int m = e / BN, n = e - m * BN;
+        const int gm = m0 + m, gn = n0 + n;
+        float v[kMaxSplits];
+#pragma unroll
+        for (int r = 0; r < kMaxSplits; ++r)
+            v[r] = r < static_cast<int>(S) ? ld_dsmem_f32(map_to_cta(part_addr + e * 4u, static_cast<uint32_t>(r)))
+                                           : 0.0f;
+        float sum = 0.0f;
+#pragma unroll
+        for (int r = 0; r < kMaxSplits; ++r)
+            if (r < static_cast<int>(S)) sum += v[r];
+        if (gm < g.M && gn < g.N) finish(gm, gn, sum);
+    }
+    cluster_sync_all();   // no CTA leaves while another still reads its tile
+}
+
+template <In IA, In IB>
+const void* simt_fn(int bm) {
+    switch (bm) {
+        case 16: return reinterpret_cast<const void*>(&gemm_simt_kernel<IA, IB, 16>);
+        case 32: return reinterpret_cast<const void*>(&gemm_simt_kernel<IA, IB, 32>);
+        case 64: return reinterpret_cast<const void*>(&gemm_simt_kernel<IA, IB, 64>);
+        default: return nullptr;
+    }
+}
+
+const void* simt_select(In ia, In ib, int bm) {
+    if (ia == In::F32 && ib == In::F32) return simt_fn<In::F32, In::F32>(bm);
+    if (ia == In::BF16 && ib == In::BF16) return simt_fn<In::BF16, In::BF16>(bm);
+    if (ia == In::F32R && ib == In::F32R) return simt_fn<In::F32R, In::F32R>(bm);
+    if (ia == In::RE4 && ib == In::RE5) return simt_fn<In::RE4, In::RE5>(bm);
+    if (ia == In::RE5 && ib == In::RE5) return simt_fn<In::RE5, In::RE5>(bm);
+    return nullptr;
+}
+
+size_t smem_for(int bm) {
+    switch (bm) {
+        case 16: return simt_smem_bytes<16>();
+        case 32: return simt_smem_bytes<32>();
+        default: return simt_smem_bytes<64>();
+    }
+}
+
+// Dynamic shared memory above 48 KB needs the attribute once per device and kernel.
+cudaError_t prepare(const void* fn, size_t smem) {
+    static std::mutex mu;
+    static std::set<std::pair<int, const void*>> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(mu);
+    if (done.count({dev, fn})) return cudaSuccess;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e == cudaSuccess) done.insert({dev, fn});
+    return e;
+}
+
+size_t elem_size(In i) {
+    switch (i) {
+        case In::F32:
+        case In::F32R: return 4;
+        case In::BF16: return 2;
+        default: return 1;
+    }
+}
+
+}  // namespace
+
+GemmSimtPlan gemm_simt_plan(const GemmArgs& g, int num_sms) {
+    GemmSimtPlan p;
+    p.bm = g.M <= 16 ? 16 : (g.M <= 32 ? 32 : 64);
+    const int64_t tiles = static_cast<int64_t>((g.N + BN - 1) / BN) * ((g.M + p.bm - 1) / p.bm);
+    const int64_t want = 2 * static_cast<int64_t>(num_sms > 0 ? num_sms : 148);
+    int s = static_cast<int>((want + tiles - 1) / tiles);
+    const int max_by_k = (g.K + 2 * BK - 1) / (2 * BK);      // at least two slices per split
+    if (s > max_by_k) s = max_by_k;
+    if (s > kMaxSplits) s = kMaxSplits;
+    if (s < 1) s = 1;
+    int kchunk = (g.K + s - 1) / s;
+    kchunk = (kchunk + BK - 1) / BK * BK;
+    p.splits = (g.K + kchunk - 1) / kchunk;
+    p.kchunk = kchunk;
+    return p;
+}
+
+cudaError_t launch_gemm_simt(In ia, In ib, const GemmArgs& g, const GemmSimtPlan& plan,
+                             cudaStream_t s) {
+    const void* fn = simt_select(ia, ib, plan.bm);
+    if (!fn || plan.splits < 1 || plan.splits > kMaxSplits || plan.kchunk < BK) return cudaErrorInvalidValue;
+    const size_t smem = smem_for(plan.bm);
+    cudaError_t e = prepare(fn, smem);
+    if (e != cudaSuccess) return e;
+    SimtParams sp;
+    sp.g = g;
+    sp.kchunk = plan.kchunk;
+    const size_t eb = elem_size(ib);
+    sp.vec_b = (!g.b_trans && reinterpret_cast<uintptr_t>(g.B) % (4 * eb) == 0 && g.ldb % 4 == 0) ? 1 : 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((g.N + BN - 1) / BN), static_cast<unsigned>((g.M + plan.bm - 1) / plan.bm),
+                       static_cast<unsigned>(plan.splits));
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    int na = 1;
+    if (plan.splits > 1) {
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = 1;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = static_cast<unsigned>(plan.splits);
+        na = 2;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    void* args[] = {&sp};
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+}  // namespace dnnopt_b200

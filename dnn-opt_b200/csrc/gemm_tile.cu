@@ -1,9 +1,7 @@
-// General-shape SIMT kernels: any M, N, K, leading dimensions and
-// transpositions.  They cover the shapes outside the small-M and tall-skinny
-// classes (the reference's adaptive-tile / packed registry range,
-// src/gemm/gemm_adaptive_tile_fp32.cpp:664-784, src/gemm/gemm_driver_generic.cpp:27-248)
-// so that every call the reference accepts has a GPU path.  FP32 arithmetic is
-// FFMA only (no TF32), matching the reference's FP32 accumulation class.
+// General-shape int8 SIMT kernel (any M, N, K, leading dimensions and
+// transpositions) for the int8 calls outside the dot-form GEMV class, so that
+// every int8 call the reference accepts has a GPU path (the FP32-accumulate
+// general kernel is gemm_simt.cu).
 //
 // Also here: the FP32-API int8 quantisation (per-tensor absmax / 127,
 // lrintf, clamp to [-128, 127]) of reference src/gemm/gemm_smallm_int8.cpp:198-236
@@ -17,102 +15,6 @@ namespace dnnopt_b200 {
 namespace {
 
 constexpr int BM = 64, BN = 64, BK = 16, kThreads = 256;
-
-template <In I> struct ElemT;
-template <> struct ElemT<In::F32> { using T = float; };
-template <> struct ElemT<In::BF16> { using T = uint16_t; };
-template <> struct ElemT<In::F32R> { using T = float; };
-template <> struct ElemT<In::RE4> { using T = uint8_t; };
-template <> struct ElemT<In::RE5> { using T = uint8_t; };
-
-__device__ __forceinline__ float dre4(uint32_t b) {
-    uint32_t s = (b >> 7) & 1u, e = (b >> 3) & 0xFu, m = b & 7u;
-    float v;
-    if (e == 0) v = static_cast<float>(m) * 0.001953125f;
-    else if (e == 0xF && m == 7) v = 448.0f;
-    else v = __uint_as_float(((e + 119u) << 23) | (m << 20));
-    return s ? -v : v;
-}
-__device__ __forceinline__ float dre5(uint32_t b) {
-    uint32_t s = (b >> 7) & 1u, e = (b >> 2) & 0x1Fu, m = b & 3u;
-    if (e == 0) {
-        float v = static_cast<float>(m) * 1.52587890625e-05f;
-        return s ? -v : v;
-    }
-    if (e == 0x1F) return __uint_as_float((s << 31) | (0xFFu << 23) | (m << 21));
-    return __uint_as_float((s << 31) | ((e + 111u) << 23) | (m << 21));
-}
-
-template <In I>
-__device__ __forceinline__ float decode(typename ElemT<I>::T v) {
-    if constexpr (I == In::F32) return v;
-    else if constexpr (I == In::BF16) return bf16_bits_to_f32(v);
-    else if constexpr (I == In::F32R) return round_to_bf16(v);
-    else if constexpr (I == In::RE4) return dre4(v);
-    else return dre5(v);
-}
-
-// 64 x 64 output tile per CTA, 4 x 4 per thread, K staged 16 at a time.
-template <In IA, In IB>
-__global__ void __launch_bounds__(kThreads) gemm_tile_f32_kernel(const GemmArgs g) {
-    using TA = typename ElemT<IA>::T;
-    using TB = typename ElemT<IB>::T;
-    __shared__ float sA[BK][BM + 4];
-    __shared__ float sB[BK][BN + 4];
-    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-    const TA* A = static_cast<const TA*>(g.A);
-    const TB* B = static_cast<const TB*>(g.B);
-    float acc[4][4] = {};
-    for (int k0 = 0; k0 < g.K; k0 += BK) {
-        for (int idx = tid; idx < BM * BK; idx += kThreads) {
-            int i, k;
-            if (g.a_trans) { i = idx % BM; k = idx / BM; } else { k = idx % BK; i = idx / BK; }
-            int gi = m0 + i, gk = k0 + k;
-            float v = 0.0f;
-            if (gi < g.M && gk < g.K)
-                v = decode<IA>(A[g.a_trans ? (int64_t)gk * g.lda + gi : (int64_t)gi * g.lda + gk]);
-            sA[k][i] = v;
-        }
-        for (int idx = tid; idx < BK * BN; idx += kThreads) {
-            int j, k;
-            if (g.b_trans) { k = idx % BK; j = idx / BK; } else { j = idx % BN; k = idx / BN; }
-            int gj = n0 + j, gk = k0 + k;
-            float v = 0.0f;
-            if (gj < g.N && gk < g.K)
-                v = decode<IB>(B[g.b_trans ? (int64_t)gj * g.ldb + gk : (int64_t)gk * g.ldb + gj]);
-            sB[k][j] = v;
-        }
-        __syncthreads();
-#pragma unroll
-        for (int k = 0; k < BK; ++k) {
-            float a[4], b[4];
-#pragma unroll
-            for (int r = 0; r < 4; ++r) a[r] = sA[k][ty * 4 + r];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) b[c] = sB[k][tx * 4 + c];
-#pragma unroll
-            for (int r = 0; r < 4; ++r)
-#pragma unroll
-                for (int c = 0; c < 4; ++c) acc[r][c] = fmaf(a[r], b[c], acc[r][c]);
-        }
-        __syncthreads();
-    }
-    float* C = static_cast<float*>(g.C);
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-        int gi = m0 + ty * 4 + r;
-        if (gi >= g.M) continue;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            int gj = n0 + tx * 4 + c;
-            if (gj >= g.N) continue;
-            float* cp = C + (int64_t)gi * g.ldc + gj;
-            *cp = add_bias((g.beta == 0.0f) ? g.alpha * acc[r][c] : fmaf(g.alpha, acc[r][c], g.beta * *cp),
-                           g.bias, gj);
-        }
-    }
-}
 
 // int8 x int8 -> int32 (exact) with A [M, K] and B [N, K]; optional dequant epilogue.
 template <bool DQ>
@@ -276,26 +178,7 @@ __global__ void quantize_ref_fp8_kernel(const GemmArgs g, uint8_t* qa, uint8_t* 
     }
 }
 
-template <In IA, In IB>
-const void* tile_fn() {
-    return reinterpret_cast<const void*>(&gemm_tile_f32_kernel<IA, IB>);
-}
-
 }  // namespace
-
-cudaError_t launch_gemm_tile_f32(In ia, In ib, const GemmArgs& g, cudaStream_t s) {
-    const void* fn = nullptr;
-    if (ia == In::F32 && ib == In::F32) fn = tile_fn<In::F32, In::F32>();
-    else if (ia == In::BF16 && ib == In::BF16) fn = tile_fn<In::BF16, In::BF16>();
-    else if (ia == In::F32R && ib == In::F32R) fn = tile_fn<In::F32R, In::F32R>();
-    else if (ia == In::RE4 && ib == In::RE5) fn = tile_fn<In::RE4, In::RE5>();
-    else if (ia == In::RE5 && ib == In::RE5) fn = tile_fn<In::RE5, In::RE5>();
-    if (!fn) return cudaErrorInvalidValue;
-    dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM);
-    GemmArgs a = g;
-    void* args[] = {&a};
-    return cudaLaunchKernel(fn, grid, dim3(kThreads), args, 0, s);
-}
 
 cudaError_t launch_gemm_tile_s8(DotKind kind, const GemmArgs& g, const float* scales,
                                 cudaStream_t s) {

@@ -98,7 +98,17 @@ cudaError_t launch_gemv_rows(DotKind kind, const GemmArgs& g, int mt, int grid, 
                              cudaStream_t s);
 
 // ---- general tiled SIMT kernels (any M, N, K, strides, transposes) ----------
-cudaError_t launch_gemm_tile_f32(In ia, In ib, const GemmArgs& g, cudaStream_t s);
+// General FP32-accumulate GEMM on the CUDA cores (gemm_simt.cu): BM x 128
+// tiles (BM = 16, 32, 64 by M), K split over up to 8 CTAs of a cluster when
+// the tiles alone would leave SMs idle.
+struct GemmSimtPlan {
+    int bm = 64;
+    int splits = 1;
+    int kchunk = 0;
+};
+GemmSimtPlan gemm_simt_plan(const GemmArgs& g, int num_sms);
+cudaError_t launch_gemm_simt(In ia, In ib, const GemmArgs& g, const GemmSimtPlan& plan,
+                             cudaStream_t s);
 // int8: A is M x K (lda), B is N x K (ldb); kind S8S32 or S8DQ (scales = {sA, sB} on device).
 cudaError_t launch_gemm_tile_s8(DotKind kind, const GemmArgs& g, const float* scales,
                                 cudaStream_t s);

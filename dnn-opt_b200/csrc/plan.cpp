@@ -155,7 +155,7 @@ const char* kernel_name(KernelId k) {
     switch (k) {
         case KernelId::GemvKn: return "gemv_kn_splitk";
         case KernelId::GemvNk: return "gemv_nk_dot";
-        case KernelId::TileF32: return "gemm_tile_f32";
+        case KernelId::TileF32: return "gemm_simt";
         case KernelId::TileS8: return "gemm_tile_s8";
         case KernelId::Bf16Tc: return "gemm_bf16_tcgen05";
         case KernelId::GemvNkRows: return "gemv_nk_dot_rowblocks";
@@ -289,6 +289,7 @@ Plan heuristic_plan(Kind kind, const GemmArgs& g, const DeviceInfo& info) {
         return p;
     }
     p.kernel = KernelId::TileF32;
+    p.simt = gemm_simt_plan(g, info.num_sms);
     return p;
 }
 
@@ -314,6 +315,10 @@ std::string describe_plan(Kind, const GemmArgs& g, const Plan& p) {
         case KernelId::GemvSlab:
             std::snprintf(buf, sizeof(buf), "%s mt=%d w=%d ctas=%d%s", kernel_name(p.kernel), p.kn.mt,
                           p.slab_w, gemv_slab_ctas(g.N, p.slab_w), p.tuned ? " tuned" : "");
+            break;
+        case KernelId::TileF32:
+            std::snprintf(buf, sizeof(buf), "%s bm=%d splits=%d kchunk=%d", kernel_name(p.kernel),
+                          p.simt.bm, p.simt.splits, p.simt.kchunk);
             break;
         default:
             std::snprintf(buf, sizeof(buf), "%s", kernel_name(p.kernel));

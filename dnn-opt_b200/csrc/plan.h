@@ -26,7 +26,7 @@ enum class Kind : int {
 enum class KernelId : int {
     GemvKn = 0,     // small-M split-K, B K x N
     GemvNk = 1,     // small-M dot form, B N x K
-    TileF32 = 2,    // general SIMT FP32-accumulate tile
+    TileF32 = 2,    // general SIMT FP32-accumulate GEMM (gemm_simt.cu)
     TileS8 = 3,     // general SIMT int8 tile
     Bf16Tc = 4,     // tcgen05 tall-skinny BF16
     GemvNkRows = 5, // dot form over 8-row blocks of A (M > 8)
@@ -41,6 +41,7 @@ struct Plan {
     GemvKnPlan kn{};
     GemvNkPlan nk{};
     E4m3TcPlan e4{};
+    GemmSimtPlan simt{};
     int slab_w = 8;      // GemvSlab: columns per CTA (8 or 16)
     bool tuned = false;
 };

@@ -295,6 +295,27 @@ def test_fp32_transposed_b_small_m(gpu, dn, orc, M, N, K, beta):
     assert np.max(np.abs(dC.cpu().numpy() - ref)) <= fp32_tol(K)
 
 
+@pytest.mark.parametrize("M,N,K,beta,ta,tb", [
+    (9, 4096, 1024, 0.5, 0, 0), (16, 1009, 2048, 0.0, 0, 0), (33, 777, 300, 1.0, 0, 1),
+    (64, 2048, 512, -0.5, 1, 0), (40, 130, 1000, 0.0, 1, 1), (128, 515, 96, 0.5, 0, 0)])
+def test_fp32_simt_small_m_bands(gpu, dn, orc, M, N, K, beta, ta, tb):
+    """M from 9 up on the general SIMT kernel (16/32/64-row tiles, K split
+    over a cluster), every transposition."""
+    torch = gpu
+    A, B, C0 = ref_uniform(M * K, 31), ref_uniform(K * N, 32), ref_uniform(M * N, 33)
+    ref = C0.copy()
+    orc.gemm_f32(M, N, K, 1.0, A, K, B, N, beta, ref, N)
+    Ad = np.ascontiguousarray(A.reshape(M, K).T).ravel() if ta else A
+    Bd = np.ascontiguousarray(B.reshape(K, N).T).ravel() if tb else B
+    d = dn.desc(M, N, K, M if ta else K, K if tb else N, N, 1.0, beta, ta, tb)
+    assert dn.plan_describe(dn.KIND_F32, d).startswith("gemm_simt")
+    dC = torch.from_numpy(C0.copy()).cuda()
+    dn.check(dn.cuda_gemm("f32", d, torch.from_numpy(Ad).cuda(), torch.from_numpy(Bd).cuda(), dC,
+                          torch.cuda.current_stream()))
+    torch.cuda.synchronize()
+    assert np.max(np.abs(dC.cpu().numpy() - ref)) <= fp32_tol(K)
+
+
 def test_saxpy(gpu, dn):
     X, Y = ref_uniform(1000, 1), ref_uniform(2000, 2)
     exp = Y.copy()
