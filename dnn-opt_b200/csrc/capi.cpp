@@ -82,6 +82,7 @@ DotKind dot_kind(Kind k) {
         case Kind::S8S32: return DotKind::S8S32;
         case Kind::F32S8Q: return DotKind::S8DQ;
         case Kind::E4M3BF16: return DotKind::E4M3;
+        case Kind::BF16F32: return DotKind::BF16;
         default: return DotKind::F32;
     }
 }

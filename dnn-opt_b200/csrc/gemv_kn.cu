@@ -43,6 +43,48 @@ struct KnParams {
     uint32_t* counters;
 };
 
+// Four B elements of one row as loaded: a 16-, 8- or 4-byte word for 4-, 2-
+// and 1-byte encodings (kept packed until the FMAs so that narrow types keep
+// as many rows in flight per register as FP32).
+template <size_t EB> struct RawWord;
+template <> struct RawWord<4> { using T = uint4; };
+template <> struct RawWord<2> { using T = uint2; };
+template <> struct RawWord<1> { using T = uint32_t; };
+
+template <In I>
+__device__ __forceinline__ void unpack4(const typename RawWord<sizeof(typename Elem<I>::T)>::T& w,
+                                        float (&o)[4]) {
+    using T = typename Elem<I>::T;
+    if constexpr (sizeof(T) == 4) {
+        o[0] = dec<I>(__uint_as_float(w.x)); o[1] = dec<I>(__uint_as_float(w.y));
+        o[2] = dec<I>(__uint_as_float(w.z)); o[3] = dec<I>(__uint_as_float(w.w));
+    } else if constexpr (sizeof(T) == 2) {
+        o[0] = dec<I>(static_cast<uint16_t>(w.x & 0xFFFFu)); o[1] = dec<I>(static_cast<uint16_t>(w.x >> 16));
+        o[2] = dec<I>(static_cast<uint16_t>(w.y & 0xFFFFu)); o[3] = dec<I>(static_cast<uint16_t>(w.y >> 16));
+    } else {
+        o[0] = dec<I>(static_cast<uint8_t>(w & 0xFFu)); o[1] = dec<I>(static_cast<uint8_t>((w >> 8) & 0xFFu));
+        o[2] = dec<I>(static_cast<uint8_t>((w >> 16) & 0xFFu)); o[3] = dec<I>(static_cast<uint8_t>(w >> 24));
+    }
+}
+
+// Element c of a packed word (scalar-load path).
+template <typename T, typename W>
+__device__ __forceinline__ void set_elem(W& w, int c, T v) {
+    if constexpr (sizeof(T) == 4) {
+        const uint32_t u = __float_as_uint(v);
+        if (c == 0) w.x = u; else if (c == 1) w.y = u; else if (c == 2) w.z = u; else w.w = u;
+    } else if constexpr (sizeof(T) == 2) {
+        const uint32_t u = static_cast<uint32_t>(v);
+        if (c == 0) w.x = (w.x & 0xFFFF0000u) | u;
+        else if (c == 1) w.x = (w.x & 0xFFFFu) | (u << 16);
+        else if (c == 2) w.y = (w.y & 0xFFFF0000u) | u;
+        else w.y = (w.y & 0xFFFFu) | (u << 16);
+    } else {
+        const uint32_t u = static_cast<uint32_t>(v);
+        w = (w & ~(0xFFu << (8 * c))) | (u << (8 * c));
+    }
+}
+
 // Column (within the 128-wide strip) held in accumulator slot c of `lane`.
 template <bool VEC4>
 __device__ __forceinline__ int slot_col(int lane, int c) {
@@ -71,7 +113,10 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 1)
 gemv_kn_kernel(const KnParams p) {
     using TA = typename Elem<IA>::T;
     using TB = typename Elem<IB>::T;
-    constexpr int U = 4;                          // rows per warp per batch (x2 in flight)
+    using Raw = typename RawWord<sizeof(TB)>::T;
+    // Rows per warp per batch (x2 in flight): 4 for FP32, 8 for 2-byte and 16
+    // for 1-byte encodings, i.e. the same 16 bytes per lane and row group.
+    constexpr int U = 16 / static_cast<int>(sizeof(TB));
     constexpr int kRowsPerBatch = kWarps * U;
 
     extern __shared__ __align__(16) float dsm[];
@@ -107,31 +152,32 @@ gemv_kn_kernel(const KnParams p) {
         const int kn = min(kPassRows, k_end - kp);
         const int nb = (kn + kRowsPerBatch - 1) / kRowsPerBatch;
 
-        auto load_batch = [&](float (&b)[U][4], int it) {
+        auto load_batch = [&](Raw (&b)[U], int it) {
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const int r = it * kRowsPerBatch + u * kWarps + warp;
-#pragma unroll
-                for (int c = 0; c < 4; ++c) b[u][c] = 0.0f;
+                b[u] = Raw{};
                 if (r < kn) {
                     const TB* row = B + (int64_t)(kp + r) * g.ldb + n0;
                     if (VEC4 && full_tile) {
-                        load4<IB>(row + 4 * lane, b[u]);
+                        b[u] = __ldg(reinterpret_cast<const Raw*>(row + 4 * lane));
                     } else {
 #pragma unroll
                         for (int c = 0; c < 4; ++c) {
                             int col = slot_col<VEC4>(lane, c);
-                            if (n0 + col < g.N) b[u][c] = dec<IB>(row[col]);
+                            if (n0 + col < g.N) set_elem<TB>(b[u], c, row[col]);
                         }
                     }
                 }
             }
         };
-        auto compute_batch = [&](const float (&b)[U][4], int it) {
+        auto compute_batch = [&](const Raw (&braw)[U], int it) {
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const int r = it * kRowsPerBatch + u * kWarps + warp;
                 if (r < kn) {
+                    float bu[4];
+                    unpack4<IB>(braw[u], bu);
                     float a[MT];
                     if constexpr (MT % 4 == 0) {
 #pragma unroll
@@ -146,12 +192,12 @@ gemv_kn_kernel(const KnParams p) {
 #pragma unroll
                     for (int m = 0; m < MT; ++m)
 #pragma unroll
-                        for (int c = 0; c < 4; ++c) acc[m][c] = fmaf(a[m], b[u][c], acc[m][c]);
+                        for (int c = 0; c < 4; ++c) acc[m][c] = fmaf(a[m], bu[c], acc[m][c]);
                 }
             }
         };
 
-        float b0[U][4], b1[U][4];
+        Raw b0[U], b1[U];
         if (nb > 0) load_batch(b0, 0);
         if (kp > k_begin) __syncthreads();   // the previous pass is done with sA
         for (int idx = tid; idx < kn * MT; idx += kThreads) {

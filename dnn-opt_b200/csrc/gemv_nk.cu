@@ -67,6 +67,11 @@ template <> struct Tr<DotKind::S8S32> {
 
 template <> struct Tr<DotKind::S8DQ> : Tr<DotKind::S8S32> {};
 
+// BF16 appears only in the register-resident rows kernel (A's element type).
+template <> struct Tr<DotKind::BF16> {
+    using TA = uint16_t; using TB = uint16_t; using Acc = float;
+};
+
 template <> struct Tr<DotKind::E4M3> {
     using TA = uint16_t; using TB = uint8_t; using Acc = float;
     static constexpr int EPC = 16;
@@ -232,6 +237,19 @@ template <> struct Chunk<DotKind::S8S32> {
     static constexpr int EPC = 16;
 };
 template <> struct Chunk<DotKind::S8DQ> : Chunk<DotKind::S8S32> {};
+template <> struct Chunk<DotKind::BF16> {
+    using Acc = float;
+    __device__ static float lo(uint32_t w) { return __uint_as_float(w << 16); }
+    __device__ static float hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+    __device__ static Acc dot(const uint4& b, const uint4& a, Acc acc) {
+        acc = fmaf(lo(a.x), lo(b.x), acc); acc = fmaf(hi(a.x), hi(b.x), acc);
+        acc = fmaf(lo(a.y), lo(b.y), acc); acc = fmaf(hi(a.y), hi(b.y), acc);
+        acc = fmaf(lo(a.z), lo(b.z), acc); acc = fmaf(hi(a.z), hi(b.z), acc);
+        acc = fmaf(lo(a.w), lo(b.w), acc); acc = fmaf(hi(a.w), hi(b.w), acc);
+        return acc;
+    }
+    static constexpr int EPC = 8;
+};
 
 struct RowsParams {
     GemmArgs g;
@@ -339,7 +357,7 @@ gemv_rows_kernel(const RowsParams p) {
             for (int w = 1; w < kWarps; ++w) t += red[buf][w][lane];
             const int m = lane / R, n = r0 + (lane % R);
             if (m < g.M && n < row_end) {
-                if constexpr (KIND == DotKind::F32) {
+                if constexpr (KIND == DotKind::F32 || KIND == DotKind::BF16) {
                     float* cp = static_cast<float*>(g.C) + (int64_t)m * g.ldc + n;
                     *cp = add_bias((g.beta == 0.0f) ? g.alpha * t : fmaf(g.alpha, t, g.beta * *cp), g.bias, n);
                 } else if constexpr (KIND == DotKind::S8S32) {
@@ -379,12 +397,15 @@ struct RowsCfg {
 };
 RowsCfg rows_cfg(DotKind kind, int mt, int kch) {
     if (kch > 2) {
-        if (kind != DotKind::F32 || mt > 2 || kch > 4) return {nullptr, 0};
-        return {reinterpret_cast<const void*>(&gemv_rows_kernel<DotKind::F32, 2, 4, 4>), 4};
+        if (mt > 2 || kch > 4) return {nullptr, 0};
+        if (kind == DotKind::F32) return {reinterpret_cast<const void*>(&gemv_rows_kernel<DotKind::F32, 2, 4, 4>), 4};
+        if (kind == DotKind::BF16) return {reinterpret_cast<const void*>(&gemv_rows_kernel<DotKind::BF16, 2, 4, 4>), 4};
+        return {nullptr, 0};
     }
     const int R = mt <= 4 ? 8 : 4;
     switch (kind) {
         case DotKind::F32: return {kch == 1 ? rows_select_mt<DotKind::F32, 1>(mt) : rows_select_mt<DotKind::F32, 2>(mt), R};
+        case DotKind::BF16: return {kch == 1 ? rows_select_mt<DotKind::BF16, 1>(mt) : rows_select_mt<DotKind::BF16, 2>(mt), R};
         case DotKind::S8S32: return {kch == 1 ? rows_select_mt<DotKind::S8S32, 1>(mt) : rows_select_mt<DotKind::S8S32, 2>(mt), R};
         case DotKind::S8DQ: return {kch == 1 ? rows_select_mt<DotKind::S8DQ, 1>(mt) : rows_select_mt<DotKind::S8DQ, 2>(mt), R};
         default: return {nullptr, 0};
@@ -413,6 +434,7 @@ const void* nk_select(DotKind kind, int mt, int vec) {
         case DotKind::S8S32: return nk_select_mt<DotKind::S8S32>(mt, vec);
         case DotKind::S8DQ: return nk_select_mt<DotKind::S8DQ>(mt, vec);
         case DotKind::E4M3: return nk_select_mt<DotKind::E4M3>(mt, vec);
+        default: break;   // BF16: rows kernel only
     }
     return nullptr;
 }
@@ -420,12 +442,13 @@ const void* nk_select(DotKind kind, int mt, int vec) {
 size_t elem_a_bytes(DotKind kind) {
     switch (kind) {
         case DotKind::F32: return 4;
-        case DotKind::E4M3: return 2;
+        case DotKind::E4M3:
+        case DotKind::BF16: return 2;
         default: return 1;
     }
 }
 
-int epc(DotKind kind) { return kind == DotKind::F32 ? 4 : 16; }
+int epc(DotKind kind) { return kind == DotKind::F32 ? 4 : (kind == DotKind::BF16 ? 8 : 16); }
 
 }  // namespace
 
@@ -482,8 +505,9 @@ cudaError_t launch_gemv_nk(DotKind kind, const GemmArgs& g, const GemvNkPlan& p,
 bool gemv_rows_supported(DotKind kind, const GemmArgs& g) {
     if (kind == DotKind::E4M3 || g.M < 1 || g.M > 8) return false;
     const int epc_ = epc(kind);
-    const size_t eb = kind == DotKind::F32 ? 4 : 1;
-    const int max_chunks = (kind == DotKind::F32 && g.M <= 2) ? 4 * kThreads : 2 * kThreads;
+    const size_t eb = kind == DotKind::F32 ? 4 : (kind == DotKind::BF16 ? 2 : 1);
+    const bool deep = (kind == DotKind::F32 || kind == DotKind::BF16) && g.M <= 2;
+    const int max_chunks = deep ? 4 * kThreads : 2 * kThreads;
     if (g.K % epc_ != 0 || g.K / epc_ > max_chunks) return false;
     return reinterpret_cast<uintptr_t>(g.B) % 16 == 0 && (static_cast<size_t>(g.ldb) * eb) % 16 == 0;
 }

@@ -75,6 +75,7 @@ enum class DotKind : int {
     S8S32 = 1,   // int8 x int8 -> int32 (exact), C overwritten
     E4M3 = 2,    // bf16 x OCP e4m3 * scale[n] -> bf16
     S8DQ = 3,    // int8 x int8 -> fp32 dequant: C = (alpha*sA*sB)*acc + beta*C
+    BF16 = 4,    // bf16 x bf16 -> fp32, alpha/beta epilogue (register-resident rows kernel)
 };
 struct GemvNkPlan {
     int mt;       // 1, 2, 4 or 8

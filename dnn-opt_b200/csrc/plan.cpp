@@ -56,6 +56,7 @@ DotKind dot_kind(Kind k) {
         case Kind::S8S32: return DotKind::S8S32;
         case Kind::F32S8Q: return DotKind::S8DQ;
         case Kind::E4M3BF16: return DotKind::E4M3;
+        case Kind::BF16F32: return DotKind::BF16;
         default: return DotKind::F32;
     }
 }
@@ -277,6 +278,13 @@ Plan heuristic_plan(Kind kind, const GemmArgs& g, const DeviceInfo& info) {
         p.nk.mt = mt_for(g.M);
         p.nk.vec = 1;
         p.nk.grid = rows_occupancy(DotKind::F32, p.nk.mt, g.K, info) * info.num_sms;
+        return p;
+    }
+    if (kind == Kind::BF16F32 && g.M <= 8 && g.b_trans && gemv_rows_supported(DotKind::BF16, g)) {
+        p.kernel = KernelId::GemvRows;
+        p.nk.mt = mt_for(g.M);
+        p.nk.vec = 1;
+        p.nk.grid = rows_occupancy(DotKind::BF16, p.nk.mt, g.K, info) * info.num_sms;
         return p;
     }
     if (kind == Kind::F32 && g.M <= 8 && g.b_trans && dot_fits) {

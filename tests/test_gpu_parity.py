@@ -447,6 +447,18 @@ def test_bf16_other_paths(gpu, dn, orc, shape):
     _bf16_case(dn, orc, gpu, M, N, K, 1.0, 0.25)
 
 
+@pytest.mark.parametrize("shape", [(1, 4096, 4096), (8, 1000, 2048), (2, 300, 8192), (5, 77, 96),
+                                   (3, 4096, 4096), (12, 500, 256)])
+def test_bf16_transposed_b(gpu, dn, orc, shape):
+    """B stored N x K (weights as [out, in]): the register-resident dot form
+    for M <= 8 with aligned rows, the SIMT kernel otherwise."""
+    M, N, K = shape
+    d = dn.desc(M, N, K, K, K, N, 1.0, 0.25, 0, 1)
+    if M <= 8:
+        assert dn.plan_describe(dn.KIND_BF16F32, d).startswith("gemv_rows_dot")
+    _bf16_case(dn, orc, gpu, M, N, K, 1.0, 0.25, b_layout="nk")
+
+
 @pytest.mark.parametrize("shape", GEMM_SHAPES)
 def test_bf16_fp32_api(gpu, dn, orc, golden, shape):
     M, N, K = shape
