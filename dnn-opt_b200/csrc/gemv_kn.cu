@@ -108,8 +108,11 @@ __device__ __forceinline__ int slot_col(int lane, int c) {
 //      in order.
 constexpr int kPassRows = 1024;   // K rows of A staged per pass
 
+// Register caps (measured on B200): MT = 1 at four CTAs per SM, MT = 2 at
+// three (2 x 4096 x 4096: 19.9 -> 17.6 us); MT = 4, 8 uncapped (three CTAs
+// per SM made 8 x 4096 x 4096 slower: more splits to reduce).
 template <In IA, In IB, int MT, bool VEC4, bool CLUSTER>
-__global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 1)
+__global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : (MT == 2 ? 3 : 1))
 gemv_kn_kernel(const KnParams p) {
     using TA = typename Elem<IA>::T;
     using TB = typename Elem<IB>::T;
