@@ -440,6 +440,14 @@ def run_profile(args):
             B = torch.from_numpy(ref_uniform(K * N, 123 + i)).cuda()
             C = torch.zeros(M * N, device="cuda")
             calls.append(lambda A=A, B=B, C=C: dn.cuda_gemm("f32", d, A, B, C, s))
+    elif name == "simt64":
+        M, N, K = 64, 4096, 4096
+        d = dn.desc(M, N, K, K, N, N)
+        for i in range(N_SETS):
+            A = torch.from_numpy(ref_uniform(M * K, 42 + i)).cuda()
+            B = torch.from_numpy(ref_uniform(K * N, 123 + i)).cuda()
+            C = torch.zeros(M * N, device="cuda")
+            calls.append(lambda A=A, B=B, C=C: dn.cuda_gemm("f32", d, A, B, C, s))
     elif name == "onednn":
         M, N, K = 4096, 1, 4096
         bias = torch.from_numpy(ref_uniform(M, 7)).cuda()
@@ -646,7 +654,7 @@ def main():
     ap.add_argument("--streams", type=int, default=SWEEP_STREAMS,
                     help="streams the 12 independent sweep GEMMs are spread over")
     ap.add_argument("--no-per-config", action="store_true", help="skip the per-config section")
-    ap.add_argument("--profile", choices=["c1", "c2", "c3", "c4", "c5", "onednn"],
+    ap.add_argument("--profile", choices=["c1", "c2", "c3", "c4", "c5", "onednn", "simt64"],
                     help="run one config's kernel --reps times for an ncu capture, no bench line")
     ap.add_argument("--reps", type=int, default=3)
     args = ap.parse_args()
