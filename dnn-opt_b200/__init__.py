@@ -88,6 +88,17 @@ lib.dnnopt_saxpy.argtypes = [_I, _F, _P, _I, _P, _I]
 _I64P, _FP = ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_float)
 _COLMAJOR_SIG = [ctypes.c_char_p, ctypes.c_char_p, _I64P, _I64P, _I64P, _FP, _P, _I64P, _P, _I64P,
                  _FP, _P, _I64P, _P]
+class Conv3DParams(ctypes.Structure):
+    """dnnopt_conv3d_params: N, IC, ID, IH, IW, OC, KD, KH, KW, strides d/h/w, pads d/h/w."""
+    _fields_ = [(n, ctypes.c_int) for n in ("N", "IC", "ID", "IH", "IW", "OC", "KD", "KH", "KW",
+                                             "stride_d", "stride_h", "stride_w",
+                                             "pad_d", "pad_h", "pad_w")]
+
+
+CONV3D_FP32, CONV3D_BF16, CONV3D_INT8 = 0, 1, 2
+POSTOP_NONE, POSTOP_RELU, POSTOP_RELU6 = 0, 1, 2
+lib.dnnopt_conv3d.argtypes = [_I, ctypes.POINTER(Conv3DParams), _P, _P, _P, _P, _I]
+lib.dnnopt_cuda_conv3d.argtypes = [_I, ctypes.POINTER(Conv3DParams), _P, _P, _P, _P, _I, _P]
 lib.dnnopt_sgemm_colmajor.argtypes = _COLMAJOR_SIG
 lib.dnnopt_cuda_sgemm_colmajor.argtypes = _COLMAJOR_SIG + [_P]
 for _name in ("dnnopt_cuda_gemm_f32", "dnnopt_cuda_gemm_bf16f32", "dnnopt_cuda_gemm_f32_bf16round",
@@ -212,6 +223,12 @@ def sgemm_colmajor(transa, transb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc,
                                                      beta, C, ldc, bias))
 
 
+def conv3d(precision, params, inp, flt, bias, out, post_op=0) -> int:
+    """params: Conv3DParams or the 15 ints in its field order."""
+    p = params if isinstance(params, Conv3DParams) else Conv3DParams(*params)
+    return lib.dnnopt_conv3d(precision, ctypes.byref(p), ptr(inp), ptr(flt), ptr(bias), ptr(out), post_op)
+
+
 def has_fp8_support() -> bool:
     return bool(lib.dnnopt_has_fp8_support())
 
@@ -231,6 +248,12 @@ def cuda_sgemm_colmajor(transa, transb, M, N, K, alpha, A, lda, B, ldb, beta, C,
                         stream=None) -> int:
     return lib.dnnopt_cuda_sgemm_colmajor(*_colmajor_args(transa, transb, M, N, K, alpha, A, lda, B,
                                                           ldb, beta, C, ldc, bias), _stream(stream))
+
+
+def cuda_conv3d(precision, params, inp, flt, bias, out, post_op=0, stream=None) -> int:
+    p = params if isinstance(params, Conv3DParams) else Conv3DParams(*params)
+    return lib.dnnopt_cuda_conv3d(precision, ctypes.byref(p), ptr(inp), ptr(flt), ptr(bias), ptr(out),
+                                  post_op, _stream(stream))
 
 
 def _stream(stream):

@@ -514,6 +514,90 @@ int colmajor_device(const ColMajorArgs& a, const float* A, const float* B, float
     return cuda_status(e);
 }
 
+// ---- Conv3D (reference src/conv/conv3d.cpp) --------------------------------
+// Geometry and argument checks; *noop for the reference's early return
+// (N, IC or OC <= 0) and for an empty output.
+int conv3d_geom(int precision, const dnnopt_conv3d_params* p, int post_op, Conv3dGeom* g, bool* noop) {
+    *noop = false;
+    if (!p || precision < DNNOPT_CONV3D_FP32 || precision > DNNOPT_CONV3D_INT8 ||
+        post_op < DNNOPT_POSTOP_NONE || post_op > DNNOPT_POSTOP_RELU6)
+        return DNNOPT_STATUS_INVALID_VALUE;
+    if (p->N <= 0 || p->OC <= 0 || p->IC <= 0) { *noop = true; return DNNOPT_STATUS_SUCCESS; }
+    if (p->ID < 0 || p->IH < 0 || p->IW < 0 || p->KD < 1 || p->KH < 1 || p->KW < 1 ||
+        p->stride_d < 1 || p->stride_h < 1 || p->stride_w < 1 || p->pad_d < 0 || p->pad_h < 0 ||
+        p->pad_w < 0)
+        return DNNOPT_STATUS_INVALID_VALUE;
+    Conv3dGeom q;
+    q.N = p->N; q.IC = p->IC; q.ID = p->ID; q.IH = p->IH; q.IW = p->IW; q.OC = p->OC;
+    q.KD = p->KD; q.KH = p->KH; q.KW = p->KW;
+    q.sd = p->stride_d; q.sh = p->stride_h; q.sw = p->stride_w;
+    q.pd = p->pad_d; q.ph = p->pad_h; q.pw = p->pad_w;
+    // Conv3DParams::OD/OH/OW (include/dnnopt/conv/conv3d.h:26-32), C integer division.
+    q.OD = (q.ID + 2 * q.pd - q.KD) / q.sd + 1;
+    q.OH = (q.IH + 2 * q.ph - q.KH) / q.sh + 1;
+    q.OW = (q.IW + 2 * q.pw - q.KW) / q.sw + 1;
+    if (q.OD <= 0 || q.OH <= 0 || q.OW <= 0) { *noop = true; return DNNOPT_STATUS_SUCCESS; }
+    const int64_t taps = static_cast<int64_t>(q.KD) * q.KH * q.KW;
+    q.M = static_cast<int64_t>(q.N) * q.OD * q.OH * q.OW;
+    q.K = taps * q.IC;
+    if (taps > kConv3dMaxTaps || q.M > 2147483647 || q.K > 2147483647)
+        return DNNOPT_STATUS_NOT_SUPPORTED;
+    *g = q;
+    return DNNOPT_STATUS_SUCCESS;
+}
+
+// Device pointers, stream-ordered: scales (INT8), column matrix and filter in
+// the compute precision, the library GEMM (FP32 / BF16 -> FP32 / INT8 ->
+// INT32, filter as the N x K operand), then bias, dequantisation and post-op.
+int conv3d_device(int precision, const Conv3dGeom& g, const float* in, const float* f, const float* bias,
+                  float* out, int op, DeviceContext* ctx, cudaStream_t s) {
+    const size_t eb = precision == DNNOPT_CONV3D_FP32 ? 4 : (precision == DNNOPT_CONV3D_BF16 ? 2 : 1);
+    auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+    const size_t col_b = up(static_cast<size_t>(g.M) * g.K * eb);
+    const size_t flt_b = precision ? up(static_cast<size_t>(g.OC) * g.K * eb) : 0;
+    const size_t acc_b = precision == DNNOPT_CONV3D_INT8 ? up(static_cast<size_t>(g.M) * g.OC * 4) : 0;
+    Workspace* w = nullptr;
+    int st = ensure_workspace(ctx, s, 0, 0, col_b + flt_b + acc_b, &w);
+    if (st != DNNOPT_STATUS_SUCCESS) return st;
+    char* base = static_cast<char*>(w->quant);
+    void* col = base;
+    void* fq = base + col_b;
+    int32_t* acc = reinterpret_cast<int32_t*>(base + col_b + flt_b);
+    const int64_t nin = static_cast<int64_t>(g.N) * g.ID * g.IH * g.IW * g.IC;
+    const int64_t nf = static_cast<int64_t>(g.OC) * g.K;
+    cudaError_t e = cudaSuccess;
+    if (precision == DNNOPT_CONV3D_INT8) {
+        e = launch_conv3d_scales(in, nin, f, nf, w->absmax, w->scales, s);
+        note_launch(2);
+        if (e != cudaSuccess) return cuda_status(e);
+    }
+    e = launch_conv3d_im2col(g, precision, in, col, w->scales, s);
+    note_launch();
+    if (e == cudaSuccess && precision != DNNOPT_CONV3D_FP32) {
+        e = launch_conv3d_filter(precision, f, fq, nf, w->scales, s);
+        note_launch();
+    }
+    if (e != cudaSuccess) return cuda_status(e);
+    GemmArgs ga;
+    ga.M = static_cast<int>(g.M); ga.N = g.OC; ga.K = static_cast<int>(g.K);
+    ga.alpha = 1.0f; ga.beta = 0.0f;
+    ga.A = col; ga.lda = g.K; ga.a_trans = 0;
+    ga.B = precision == DNNOPT_CONV3D_FP32 ? static_cast<const void*>(f) : fq;
+    ga.ldb = g.K; ga.b_trans = 1;
+    ga.C = precision == DNNOPT_CONV3D_INT8 ? static_cast<void*>(acc) : static_cast<void*>(out);
+    ga.ldc = g.OC;
+    const Kind kind = precision == DNNOPT_CONV3D_FP32 ? Kind::F32
+                      : (precision == DNNOPT_CONV3D_BF16 ? Kind::BF16F32 : Kind::S8S32);
+    st = run_device(kind, ga, nullptr, ctx, s);
+    if (st != DNNOPT_STATUS_SUCCESS) return st;
+    if (precision == DNNOPT_CONV3D_INT8 || bias || op != DNNOPT_POSTOP_NONE) {
+        e = launch_conv3d_post(out, precision == DNNOPT_CONV3D_INT8 ? acc : nullptr, w->scales, bias, g.M,
+                               g.OC, op, s);
+        note_launch();
+    }
+    return cuda_status(e);
+}
+
 }  // namespace
 
 extern "C" {
@@ -613,6 +697,53 @@ int dnnopt_gemm_f32_desc(const dnnopt_gemm_desc* d, const float* A, const float*
     return host_entry(Kind::F32, d, A, B, C, nullptr);
 }
 
+int dnnopt_conv3d(int precision, const dnnopt_conv3d_params* p, const float* input,
+                  const float* filter, const float* bias, float* output, int post_op) {
+    Conv3dGeom g;
+    bool noop;
+    int st = conv3d_geom(precision, p, post_op, &g, &noop);
+    if (st != DNNOPT_STATUS_SUCCESS || noop) return set_status(st);
+    if (!input || !filter || !output) return set_status(DNNOPT_STATUS_INVALID_VALUE);
+    DeviceContext* ctx = current_context(&st);
+    if (!ctx) return st;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    cudaStream_t s = ctx->user_stream_set ? ctx->user_stream : ctx->default_stream;
+    const size_t nin = static_cast<size_t>(g.N) * g.ID * g.IH * g.IW * g.IC;
+    Operand ops[4] = {
+        {input, nin * sizeof(float), true, false},
+        {filter, static_cast<size_t>(g.OC) * g.K * sizeof(float), true, false},
+        {bias, bias ? static_cast<size_t>(g.OC) * sizeof(float) : 0, true, false},
+        {output, static_cast<size_t>(g.M) * g.OC * sizeof(float), false, true},
+    };
+    const void* dev[4] = {input, filter, bias, output};
+    for (int i = 0; i < 4; ++i) {
+        if (!ops[i].user || ops[i].bytes == 0) continue;
+        if (classify_pointer(ops[i].user) == PtrKind::Device) continue;
+        void* buf = nullptr;
+        st = ensure_stage(ctx, i, ops[i].bytes, &buf);
+        if (st != DNNOPT_STATUS_SUCCESS) return st;
+        dev[i] = buf;
+        if (ops[i].in) {
+            cudaError_t e = cudaMemcpyAsync(buf, ops[i].user, ops[i].bytes, cudaMemcpyHostToDevice, s);
+            if (e != cudaSuccess) return cuda_status(e);
+        }
+    }
+    st = conv3d_device(precision, g, static_cast<const float*>(dev[0]), static_cast<const float*>(dev[1]),
+                       static_cast<const float*>(dev[2]), static_cast<float*>(const_cast<void*>(dev[3])),
+                       post_op, ctx, s);
+    if (st != DNNOPT_STATUS_SUCCESS) {
+        cudaStreamSynchronize(s);
+        return set_status(st);
+    }
+    if (dev[3] != output) {
+        cudaError_t e = cudaMemcpyAsync(output, dev[3], ops[3].bytes, cudaMemcpyDeviceToHost, s);
+        if (e != cudaSuccess) return cuda_status(e);
+    }
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_status(e);
+    return set_status(DNNOPT_STATUS_SUCCESS);
+}
+
 int dnnopt_sgemm_colmajor(const char* transa, const char* transb, const int64_t* M,
                           const int64_t* N, const int64_t* K, const float* alpha, const float* A,
                           const int64_t* lda, const float* B, const int64_t* ldb,
@@ -710,6 +841,20 @@ void dnnopt_gemm_set_num_threads(int n) { g_num_threads = n < 0 ? 0 : n; }
 int dnnopt_gemm_get_num_threads(void) { return g_num_threads > 0 ? g_num_threads : 1; }
 
 // ---- device-pointer entry points ------------------------------------------
+int dnnopt_cuda_conv3d(int precision, const dnnopt_conv3d_params* p, const float* input,
+                       const float* filter, const float* bias, float* output, int post_op,
+                       void* stream) {
+    Conv3dGeom g;
+    bool noop;
+    int st = conv3d_geom(precision, p, post_op, &g, &noop);
+    if (st != DNNOPT_STATUS_SUCCESS || noop) return set_status(st);
+    if (!input || !filter || !output) return set_status(DNNOPT_STATUS_INVALID_VALUE);
+    DeviceContext* ctx = current_context(&st);
+    if (!ctx) return st;
+    return set_status(conv3d_device(precision, g, input, filter, bias, output, post_op, ctx,
+                                    static_cast<cudaStream_t>(stream)));
+}
+
 int dnnopt_cuda_sgemm_colmajor(const char* transa, const char* transb, const int64_t* M,
                                const int64_t* N, const int64_t* K, const float* alpha,
                                const float* A, const int64_t* lda, const float* B,

@@ -124,6 +124,25 @@ cudaError_t launch_quantize_s8(const GemmArgs& g, const uint32_t* absmax_bits, f
 // B with the reference e5m2 codec (dense K x N).
 cudaError_t launch_quantize_ref_fp8(const GemmArgs& g, uint8_t* qa, uint8_t* qb, cudaStream_t s);
 
+// ---- Conv3D as an im2col GEMM (conv3d.cu) ------------------------------------
+constexpr int kConv3dMaxTaps = 1024;   // KD * KH * KW
+struct Conv3dGeom {
+    int N, IC, ID, IH, IW, OC, KD, KH, KW, sd, sh, sw, pd, ph, pw, OD, OH, OW;
+    int64_t M, K;   // column matrix: M = N*OD*OH*OW rows of K = KD*KH*KW*IC
+};
+// mode 0: FP32 columns, 1: BF16 (RNE), 2: INT8 quantised with 1/scales[2].
+cudaError_t launch_conv3d_im2col(const Conv3dGeom& g, int mode, const float* in, void* col,
+                                 const float* scales, cudaStream_t s);
+// Filter to BF16 (mode 1) or INT8 with 1/scales[3] (mode 2).
+cudaError_t launch_conv3d_filter(int mode, const float* f, void* out, int64_t n, const float* scales,
+                                 cudaStream_t s);
+// scales[0..3] = s_in, s_f, 1/s_in, 1/s_f from the per-tensor absmax (bits: 2 words).
+cudaError_t launch_conv3d_scales(const float* in, int64_t nin, const float* f, int64_t nf, uint32_t* bits,
+                                 float* scales, cudaStream_t s);
+// out = post_op(v + bias[oc]); v = out, or float(acc) * (scales[0] * scales[1]) when acc.
+cudaError_t launch_conv3d_post(float* out, const int32_t* acc, const float* scales, const float* bias,
+                               int64_t M, int OC, int op, cudaStream_t s);
+
 // Column-major C fix-ups of the oneDNN entry (footprint [0, (N-1)*ldc + M),
 // overlapping columns handled in the entry's sequential order).
 cudaError_t launch_colmajor_k0(float* C, const float* bias, int64_t M, int64_t N, int64_t ldc,

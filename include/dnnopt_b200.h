@@ -140,6 +140,30 @@ int dnnopt_sgemm_colmajor(const char* transa, const char* transb, const int64_t*
                           const int64_t* lda, const float* B, const int64_t* ldb,
                           const float* beta, float* C, const int64_t* ldc, const float* bias);
 
+/* ------------------------------------------------------------------------
+ * Conv3D (replaces dnnopt::conv3d_fp32 / conv3d_bf16 / conv3d_int8, reference
+ * include/dnnopt/conv/conv3d.h:52-127, src/conv/conv3d.cpp:151-525).
+ *   input  [N, ID, IH, IW, IC] (NDHWC), filter [OC, KD, KH, KW, IC],
+ *   bias [OC] or NULL, output [N, OD, OH, OW, OC], O* = (I* + 2*pad - K*) / stride + 1.
+ * precision: DNNOPT_CONV3D_FP32, _BF16 (input and filter rounded to bf16,
+ * FP32 accumulation: the reference's ARM BFMMLA path) or _INT8 (per-tensor
+ * absmax/127 quantisation, exact int32 sums, dequantised: its SMMLA path).
+ * post_op: DNNOPT_POSTOP_NONE, _RELU, _RELU6, applied after the bias.
+ * N, IC or OC <= 0, or an empty output: no-op (the reference's early return).
+ * KD*KH*KW is limited to 1024.  The column matrix (M x K in the compute
+ * precision, M = N*OD*OH*OW, K = KD*KH*KW*IC) is library scratch.
+ * ---------------------------------------------------------------------- */
+enum { DNNOPT_CONV3D_FP32 = 0, DNNOPT_CONV3D_BF16 = 1, DNNOPT_CONV3D_INT8 = 2 };
+enum { DNNOPT_POSTOP_NONE = 0, DNNOPT_POSTOP_RELU = 1, DNNOPT_POSTOP_RELU6 = 2 };
+typedef struct dnnopt_conv3d_params {
+    int N, IC, ID, IH, IW, OC, KD, KH, KW;
+    int stride_d, stride_h, stride_w;
+    int pad_d, pad_h, pad_w;
+} dnnopt_conv3d_params;
+/* Host or device pointers, synchronous. */
+int dnnopt_conv3d(int precision, const dnnopt_conv3d_params* p, const float* input,
+                  const float* filter, const float* bias, float* output, int post_op);
+
 /* Replaces cblas_saxpy (reference src/blas/cblas_saxpy.cpp:13-50):
  * Y[i*incY] += alpha * X[i*incX] for i < N; N <= 0 or alpha == 0 is a no-op;
  * negative increments are rejected. */
@@ -162,6 +186,10 @@ int dnnopt_cuda_sgemm_colmajor(const char* transa, const char* transb, const int
                                const float* A, const int64_t* lda, const float* B,
                                const int64_t* ldb, const float* beta, float* C, const int64_t* ldc,
                                const float* bias, void* stream);
+/* dnnopt_conv3d on device pointers, stream-ordered. */
+int dnnopt_cuda_conv3d(int precision, const dnnopt_conv3d_params* p, const float* input,
+                       const float* filter, const float* bias, float* output, int post_op,
+                       void* stream);
 int dnnopt_cuda_gemm_bf16f32(const dnnopt_gemm_desc* d, const uint16_t* A, const uint16_t* B,
                              float* C, void* stream);
 /* FP32 operands rounded to bf16 on load (dnnopt_gemm_bf16 semantics). */

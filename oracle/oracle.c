@@ -189,6 +189,78 @@ int oracle_sgemm_colmajor(char transa, char transb, int64_t M, int64_t N, int64_
     return 0;
 }
 
+/* ---------------- Conv3D (src/conv/conv3d.cpp) ---------------- */
+static float conv_post(float v, const float* bias, int oc, int op) {   /* :126-148 */
+    if (bias) v += bias[oc];
+    if (op == 1) v = v > 0 ? v : 0;
+    else if (op == 2) v = v > 0 ? (v < 6 ? v : 6) : 0;
+    return v;
+}
+static float absmax_scale(const float* x, size_t n) {                  /* :355-364 */
+    float m = 0.0f;
+    for (size_t i = 0; i < n; ++i) { float a = fabsf(x[i]); if (a > m) m = a; }
+    return m == 0.0f ? 1.0f : m / 127.0f;
+}
+static int8_t quant8(float x, float inv) {                             /* :366-377 */
+    int q = (int)roundf(x * inv);
+    if (q > 127) q = 127; else if (q < -128) q = -128;
+    return (int8_t)q;
+}
+void oracle_conv3d(int precision, const int* p, const float* input, const float* filter,
+                   const float* bias, float* output, int post_op, double* out64) {
+    const int N = p[0], IC = p[1], ID = p[2], IH = p[3], IW = p[4], OC = p[5];
+    const int KD = p[6], KH = p[7], KW = p[8], sd = p[9], sh = p[10], sw = p[11];
+    const int pd = p[12], ph = p[13], pw = p[14];
+    const int OD = (ID + 2 * pd - KD) / sd + 1, OH = (IH + 2 * ph - KH) / sh + 1;
+    const int OW = (IW + 2 * pw - KW) / sw + 1;
+    if (N <= 0 || OC <= 0 || IC <= 0) return;
+    const size_t nin = (size_t)N * ID * IH * IW * IC, nflt = (size_t)OC * KD * KH * KW * IC;
+    float s_in = 1.0f, s_f = 1.0f, inv_in = 1.0f, inv_f = 1.0f;
+    if (precision == 2) {
+        s_in = absmax_scale(input, nin); s_f = absmax_scale(filter, nflt);
+        inv_in = 1.0f / s_in; inv_f = 1.0f / s_f;
+    }
+    for (int n = 0; n < N; ++n)
+    for (int od = 0; od < OD; ++od)
+    for (int oh = 0; oh < OH; ++oh)
+    for (int ow = 0; ow < OW; ++ow) {
+        const size_t row = (((size_t)n * OD + od) * OH + oh) * OW + ow;
+        for (int oc = 0; oc < OC; ++oc) {
+            float acc = 0.0f;
+            double acc64 = 0.0;
+            int32_t acc8 = 0;
+            for (int kd = 0; kd < KD; ++kd)
+            for (int kh = 0; kh < KH; ++kh)
+            for (int kw = 0; kw < KW; ++kw)
+            for (int ic = 0; ic < IC; ++ic) {
+                const int id = od * sd - pd + kd, ih = oh * sh - ph + kh, iw = ow * sw - pw + kw;
+                const int inside = id >= 0 && id < ID && ih >= 0 && ih < IH && iw >= 0 && iw < IW;
+                const float x = inside ? input[((((size_t)n * ID + id) * IH + ih) * IW + iw) * IC + ic] : 0.0f;
+                const float w = filter[((((size_t)oc * KD + kd) * KH + kh) * KW + kw) * IC + ic];
+                if (precision == 0) {
+                    acc += x * w;                   /* im2col zeros included, column order */
+                } else if (precision == 1) {
+                    const float xb = oracle_bf16_to_f32(oracle_bf16_from_f32(x));
+                    const float wb = oracle_bf16_to_f32(oracle_bf16_from_f32(w));
+                    acc += xb * wb;
+                    acc64 += (double)xb * (double)wb;
+                } else {
+                    acc8 += (int32_t)quant8(x, inv_in) * (int32_t)quant8(w, inv_f);
+                }
+            }
+            float v = precision == 2 ? (float)acc8 * (s_in * s_f) : acc;
+            output[row * OC + oc] = conv_post(v, bias, oc, post_op);
+            if (out64) {
+                double d = precision == 1 ? acc64 : (double)v;
+                if (bias) d += bias[oc];
+                if (post_op == 1) d = d > 0 ? d : 0;
+                else if (post_op == 2) d = d > 0 ? (d < 6 ? d : 6) : 0;
+                out64[row * OC + oc] = d;
+            }
+        }
+    }
+}
+
 /* ---------------- FP32 (gemm.cpp:88-100) ---------------- */
 void oracle_gemm_f32_naive(int M, int N, int K, float alpha, const float* A, int lda,
                            const float* B, int ldb, float beta, float* C, int ldc) {

@@ -95,6 +95,22 @@ int oracle_sgemm_colmajor(char transa, char transb, int64_t M, int64_t N, int64_
                           const float* A, int64_t lda, const float* B, int64_t ldb, float beta,
                           float* C, int64_t ldc, const float* bias);
 
+/* Conv3D (reference src/conv/conv3d.cpp): NDHWC input, filter [OC, KD, KH,
+ * KW, IC], output [N, OD, OH, OW, OC]; p = N, IC, ID, IH, IW, OC, KD, KH, KW,
+ * stride d/h/w, pad d/h/w.  The GEMM view is im2col3d (:57-124, columns in
+ * (kd, kh, kw, ic) order, zeros for padding) times the filter, then
+ * apply_conv3d_postops (:126-148: + bias[oc], then relu / relu6).
+ *   precision 0: FP32, accumulated in column order exactly as im2col + the
+ *                naive GEMM does (bit-exact with the reference on x86);
+ *   precision 1: the ARM BF16 path (:290-340): input and filter rounded to
+ *                bf16 (RNE), products accumulated; out64 gets the float64 sum;
+ *   precision 2: the ARM INT8 path (:355-518): per-tensor scale absmax/127
+ *                (1 when all zero), q = clamp(round(x * (1/scale))), exact
+ *                int32 sums, float(acc) * (s_in * s_f), then bias / post-op.
+ * post_op: 0 none, 1 relu, 2 relu6.  out64 may be NULL. */
+void oracle_conv3d(int precision, const int* p, const float* input, const float* filter,
+                   const float* bias, float* output, int post_op, double* out64);
+
 #ifdef __cplusplus
 }
 #endif

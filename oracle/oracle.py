@@ -48,6 +48,7 @@ def load_oracle():
     lib.oracle_sgemm_colmajor.argtypes = [ctypes.c_char, ctypes.c_char, _L, _L, _L, _F, _P, _L, _P,
                                           _L, _F, _P, _L, _P]
     lib.oracle_sgemm_colmajor.restype = _I
+    lib.oracle_conv3d.argtypes = [_I, _P, _P, _P, _P, _P, _I, _P]
     return lib
 
 
@@ -65,6 +66,7 @@ def load_ref():
     lib.ref_gemm_int8_int8int8int32_mt.argtypes = [_I, _I, _I, _P, _I, _P, _I, _P, _I, _I]
     lib.cblas_sgemm.argtypes = [_I, _I, _I, _I, _I, _I, _F, _P, _I, _P, _I, _F, _P, _I]
     lib.sgemm_.argtypes = [_P] * 13
+    lib.ref_conv3d.argtypes = [_I, _P, _P, _P, _P, _P, _I]
     lib.ref_fill_random.argtypes = [_P, _SZ, ctypes.c_uint]
     lib.ref_bf16_from_f32.argtypes = [_F]
     lib.ref_bf16_from_f32.restype = ctypes.c_uint16
@@ -116,6 +118,13 @@ class Oracle:
     def sgemm_colmajor(self, transa, transb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, bias=None):
         return self.lib.oracle_sgemm_colmajor(transa.encode(), transb.encode(), M, N, K, alpha, _p(A),
                                               lda, _p(B), ldb, beta, _p(C), ldc, _p(bias))
+
+    def conv3d(self, precision, params, inp, flt, bias, out, post_op=0, want64=False):
+        """params: the 15 ints N, IC, ID, IH, IW, OC, KD, KH, KW, strides, pads."""
+        p = np.asarray(params, np.int32)
+        out64 = np.zeros(out.size, np.float64) if want64 else None
+        self.lib.oracle_conv3d(precision, _p(p), _p(inp), _p(flt), _p(bias), _p(out), post_op, _p(out64))
+        return out64
 
     def gemm_f32_f64(self, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, threads=8):
         out = np.zeros(M * N, np.float64)

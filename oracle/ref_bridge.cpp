@@ -7,6 +7,7 @@
 #include "dnnopt/gemm/gemm.h"
 #include "dnnopt/gemm/gemm_types.h"
 #include "dnnopt/blas/cblas.h"
+#include "dnnopt/conv/conv3d.h"
 
 #include <cstdint>
 #include <cstring>
@@ -113,6 +114,23 @@ void ref_gemm_int8_int8int8int32_mt(int M, int N, int K, const int8_t* A, int ld
         });
     }
     for (auto& th : pool) th.join();
+}
+
+// dnnopt::conv3d_fp32 / conv3d_bf16 / conv3d_int8 (reference
+// src/conv/conv3d.cpp:151-192, :290-345, :460-525).  p: N, IC, ID, IH, IW, OC,
+// KD, KH, KW, stride d/h/w, pad d/h/w.  precision 0/1/2 = fp32/bf16/int8; on
+// an x86 host the reference's bf16 and int8 entries fall back to conv3d_fp32.
+void ref_conv3d(int precision, const int* p, const float* input, const float* filter,
+                const float* bias, float* output, int post_op) {
+    dnnopt::Conv3DParams c;
+    c.N = p[0]; c.IC = p[1]; c.ID = p[2]; c.IH = p[3]; c.IW = p[4];
+    c.OC = p[5]; c.KD = p[6]; c.KH = p[7]; c.KW = p[8];
+    c.stride_d = p[9]; c.stride_h = p[10]; c.stride_w = p[11];
+    c.pad_d = p[12]; c.pad_h = p[13]; c.pad_w = p[14];
+    const auto op = static_cast<dnnopt::Conv3DPostOp>(post_op);
+    if (precision == 1) dnnopt::conv3d_bf16(c, input, filter, bias, output, op);
+    else if (precision == 2) dnnopt::conv3d_int8(c, input, filter, bias, output, op);
+    else dnnopt::conv3d_fp32(c, input, filter, bias, output, op);
 }
 
 }  // extern "C"

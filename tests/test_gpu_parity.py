@@ -316,6 +316,45 @@ def test_fp32_simt_small_m_bands(gpu, dn, orc, M, N, K, beta, ta, tb):
     assert np.max(np.abs(dC.cpu().numpy() - ref)) <= fp32_tol(K)
 
 
+# ----------------------------------------------------------------- Conv3D ---
+def _conv3d_shapes():
+    from tests.test_oracle_conv3d import CONV3D_SHAPES
+    # + a shape whose BF16 GEMM takes the tcgen05 kernel (K = 432, OC = 64, M = 1024)
+    return CONV3D_SHAPES + [(1, 16, 4, 16, 16, 64, 3, 3, 3, 1, 1, 1, 1, 1, 1)]
+
+
+@pytest.mark.parametrize("p", _conv3d_shapes())
+@pytest.mark.parametrize("precision", [0, 1, 2])
+def test_conv3d_matches_oracle(gpu, dn, orc, p, precision):
+    """dnnopt_conv3d (host arrays) and dnnopt_cuda_conv3d (device tensors)
+    against the oracle: FP32 within 1e-5*K, BF16 within FP32 accumulation of
+    the bf16 products (and the reference test's K*1e-2 of the exact result),
+    INT8 bit for bit (deterministic quantisation, exact int32 sums)."""
+    from tests.test_oracle_conv3d import conv3d_f64, conv3d_operands
+    torch = gpu
+    inp, flt, bias, n_out = conv3d_operands(p)
+    K = p[1] * p[6] * p[7] * p[8]
+    for post_op, b in ((0, None), (1, bias), (2, bias)):
+        ref = np.zeros(n_out, np.float32)
+        r64 = orc.conv3d(precision, p, inp, flt, b, ref, post_op, want64=True)
+        host = np.full(n_out, np.nan, np.float32)
+        dn.check(dn.conv3d(precision, p, inp, flt, b, host, post_op), "conv3d")
+        dC = torch.full((n_out,), float("nan"), device="cuda")
+        dn.check(dn.cuda_conv3d(precision, p, torch.from_numpy(inp).cuda(), torch.from_numpy(flt).cuda(),
+                                None if b is None else torch.from_numpy(b).cuda(), dC, post_op,
+                                torch.cuda.current_stream()), "cuda_conv3d")
+        torch.cuda.synchronize()
+        dev = dC.cpu().numpy()
+        for got in (host, dev):
+            if precision == 0:
+                assert np.max(np.abs(got - ref)) <= fp32_tol(K), (p, post_op)
+            elif precision == 1:
+                assert np.max(np.abs(got - r64)) <= fp32_tol(K), (p, post_op)
+                assert np.max(np.abs(got - conv3d_f64(p, inp, flt, b, post_op))) < K * 1e-2
+            else:
+                assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), (p, post_op)
+
+
 def test_saxpy(gpu, dn):
     X, Y = ref_uniform(1000, 1), ref_uniform(2000, 2)
     exp = Y.copy()
