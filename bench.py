@@ -313,6 +313,23 @@ def per_config(torch, dn, stream, pk, world, rank, dist):
         "hbm_frac": r["GB_s"] / pk["hbm_gbs"],
         "kernel": dn.plan_describe(dn.KIND_F32, dn.desc(N, M, K, K, K, M, trans_b=1)) + " + bias epilogue"}
     del Ws, Xs, Ys
+    # Conv3D (the in-tree caller of the BF16 / INT8 GEMMs), a video layer:
+    # N=1, IC=64, 8x56x56, OC=64, 3x3x3, stride 1, pad 1, bias + relu.
+    cp = (1, 64, 8, 56, 56, 64, 3, 3, 3, 1, 1, 1, 1, 1, 1)
+    nin, nflt, nout = 8 * 56 * 56 * 64, 64 * 27 * 64, 8 * 56 * 56 * 64
+    cin = torch.from_numpy(ref_uniform(nin, 3)).cuda()
+    cflt = torch.from_numpy(ref_uniform(nflt, 4)).cuda()
+    cbias = torch.from_numpy(ref_uniform(64, 5)).cuda()
+    cout = torch.zeros(nout, device="cuda")
+    flops = 2.0 * nout * 27 * 64
+    for prec, name in ((0, "fp32"), (1, "bf16"), (2, "int8")):
+        fns = [lambda prec=prec: dn.cuda_conv3d(prec, cp, cin, cflt, cbias, cout, dn.POSTOP_RELU, s)]
+        dn.check(fns[0](), "conv3d")
+        r = bench_single(torch, dn, s, fns, 4 * (nin + nflt + nout), flops, iters=10)
+        out[f"conv3d_{name}_1x64x8x56x56_oc64_k3"] = {
+            "TFLOP_s": r["TFLOP_s"], "us": r["us_per_call"],
+            "note": "im2col in the compute precision + library GEMM + bias/relu pass"}
+    del cin, cflt, cbias, cout
     # C3: INT8 4 x 11008 x 4096, B is [N, K].
     M, N, K = 4, 11008, 4096
     As = [torch.from_numpy(int8_uniform(M * K, 42 + i)).cuda() for i in range(N_SETS)]
