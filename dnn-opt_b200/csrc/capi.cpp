@@ -172,12 +172,24 @@ int launch_plan(Kind kind, const GemmArgs& g, const Plan& p, const float* scales
             e = launch_gemm_tile_s8(dot_kind(kind), g, scales, s);
             note_launch();
             break;
-        case KernelId::Bf16Tc:
+        case KernelId::Bf16Tc: {
             st = ensure_workspace(ctx, s, 0, 0, 0, &w);
             if (st != DNNOPT_STATUS_SUCCESS) return st;
-            e = launch_gemm_bf16_tc(g, ctx->num_sms, w->err, s);
-            note_launch();
+            // Deep K: chunks of kc rows, C accumulating (beta = 1 after the first).
+            const int kc = gemm_bf16_tc_kchunk(g);
+            if (kc < 1) return set_status(DNNOPT_STATUS_NOT_SUPPORTED);
+            for (int k0 = 0; k0 < g.K && e == cudaSuccess; k0 += kc) {
+                GemmArgs c = g;
+                c.K = g.K - k0 < kc ? g.K - k0 : kc;
+                c.A = static_cast<const uint16_t*>(g.A) + k0;
+                c.B = static_cast<const uint16_t*>(g.B) + (g.b_trans ? static_cast<int64_t>(k0)
+                                                                     : static_cast<int64_t>(k0) * g.ldb);
+                if (k0 > 0) c.beta = 1.0f;
+                e = launch_gemm_bf16_tc(c, ctx->num_sms, w->err, s);
+                note_launch();
+            }
             break;
+        }
     }
     return cuda_status(e);
 }

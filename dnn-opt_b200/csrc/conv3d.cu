@@ -29,10 +29,14 @@ __device__ __forceinline__ int8_t quant8(float x, float inv) {
     return static_cast<int8_t>(q);
 }
 
-// One CTA per output position (row of the column matrix); threads walk its K
-// columns, tap-major then input channel, so reads of a tap are contiguous in
-// IC and writes contiguous in K.
-template <int MODE>   // 0: FP32, 1: BF16 bits, 2: INT8
+// Grid-stride over groups of four output positions (rows of the column
+// matrix, four loads in flight per thread); each row's
+// K columns are walked as chunks of V input channels (V = 4 when IC % 4 == 0
+// and the input is 16-byte aligned: one 16-byte load and one 16/8/4-byte store
+// per chunk), tap-major then channel, so a tap's reads are contiguous in IC
+// and the writes contiguous in K.  A thread's (tap, chunk) position advances
+// by a fixed step per iteration, so the inner loop has no division.
+template <int MODE, int V>   // MODE 0: FP32, 1: BF16 bits, 2: INT8
 __global__ void __launch_bounds__(kThreads) im2col3d_kernel(const Conv3dGeom g, const float* __restrict__ in,
                                                             void* col, const float* scales) {
     __shared__ int s_tap[3 * kConv3dMaxTaps];
@@ -45,30 +49,84 @@ __global__ void __launch_bounds__(kThreads) im2col3d_kernel(const Conv3dGeom g, 
     }
     __syncthreads();
     const float inv = MODE == 2 ? scales[2] : 1.0f;
-    for (int64_t row = blockIdx.x; row < g.M; row += gridDim.x) {
-        const int ow = static_cast<int>(row % g.OW);
-        int64_t r = row / g.OW;
-        const int oh = static_cast<int>(r % g.OH);
-        r /= g.OH;
-        const int od = static_cast<int>(r % g.OD);
-        const int n = static_cast<int>(r / g.OD);
-        for (int k = threadIdx.x; k < g.K; k += kThreads) {
-            const int t = k / g.IC, ic = k - t * g.IC;
-            const int id = od * g.sd - g.pd + s_tap[3 * t];
-            const int ih = oh * g.sh - g.ph + s_tap[3 * t + 1];
-            const int iw = ow * g.sw - g.pw + s_tap[3 * t + 2];
-            float x = 0.0f;
-            if (id >= 0 && id < g.ID && ih >= 0 && ih < g.IH && iw >= 0 && iw < g.IW)
-                x = in[((((int64_t)n * g.ID + id) * g.IH + ih) * g.IW + iw) * g.IC + ic];
-            const int64_t o = row * g.K + k;
-            if constexpr (MODE == 0) static_cast<float*>(col)[o] = x;
-            else if constexpr (MODE == 1) static_cast<uint16_t*>(col)[o] = f32_to_bf16_bits_ref(x);
-            else static_cast<int8_t*>(col)[o] = quant8(x, inv);
+    const int cpr = g.IC / V;                      // chunks per tap
+    const int nchunks = taps * cpr;
+    const int t0 = threadIdx.x / cpr, c0 = threadIdx.x - t0 * cpr;
+    const int dt = kThreads / cpr, dc = kThreads - dt * cpr;
+    const int64_t plane = (int64_t)g.IH * g.IW * g.IC;
+    // R rows per pass: a thread keeps R independent loads in flight.
+    constexpr int R = 4;
+    for (int64_t row0 = (int64_t)blockIdx.x * R; row0 < g.M; row0 += (int64_t)gridDim.x * R) {
+        int od[R], oh[R], ow[R];
+        const float* src[R];
+        bool live[R];
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+            const int64_t row = row0 + q;
+            live[q] = row < g.M;
+            const int64_t rr = live[q] ? row : row0;
+            ow[q] = static_cast<int>(rr % g.OW);
+            int64_t r = rr / g.OW;
+            oh[q] = static_cast<int>(r % g.OH);
+            r /= g.OH;
+            od[q] = static_cast<int>(r % g.OD);
+            src[q] = in + (r / g.OD) * g.ID * plane;
+        }
+        int t = t0, c = c0;
+        for (int j = threadIdx.x; j < nchunks; j += kThreads) {
+            const int kd = s_tap[3 * t], kh = s_tap[3 * t + 1], kw = s_tap[3 * t + 2];
+            float x[R][V];
+#pragma unroll
+            for (int q = 0; q < R; ++q) {
+#pragma unroll
+                for (int v = 0; v < V; ++v) x[q][v] = 0.0f;
+                const int id = od[q] * g.sd - g.pd + kd;
+                const int ih = oh[q] * g.sh - g.ph + kh;
+                const int iw = ow[q] * g.sw - g.pw + kw;
+                if (live[q] && id >= 0 && id < g.ID && ih >= 0 && ih < g.IH && iw >= 0 && iw < g.IW) {
+                    const float* p = src[q] + id * plane + ((int64_t)ih * g.IW + iw) * g.IC + c * V;
+                    if constexpr (V == 4) {
+                        const float4 f4 = __ldg(reinterpret_cast<const float4*>(p));
+                        x[q][0] = f4.x; x[q][1] = f4.y; x[q][2] = f4.z; x[q][3] = f4.w;
+                    } else {
+                        x[q][0] = __ldg(p);
+                    }
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < R; ++q) {
+                if (!live[q]) continue;
+                const int64_t o = (row0 + q) * g.K + (int64_t)t * g.IC + c * V;
+                if constexpr (MODE == 0) {
+                    if constexpr (V == 4) *reinterpret_cast<float4*>(static_cast<float*>(col) + o) = make_float4(x[q][0], x[q][1], x[q][2], x[q][3]);
+                    else static_cast<float*>(col)[o] = x[q][0];
+                } else if constexpr (MODE == 1) {
+                    if constexpr (V == 4) {
+                        const uint32_t lo = f32_to_bf16_bits_ref(x[q][0]) | (static_cast<uint32_t>(f32_to_bf16_bits_ref(x[q][1])) << 16);
+                        const uint32_t hi = f32_to_bf16_bits_ref(x[q][2]) | (static_cast<uint32_t>(f32_to_bf16_bits_ref(x[q][3])) << 16);
+                        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(col) + o) = make_uint2(lo, hi);
+                    } else {
+                        static_cast<uint16_t*>(col)[o] = f32_to_bf16_bits_ref(x[q][0]);
+                    }
+                } else {
+                    if constexpr (V == 4) {
+                        uint32_t w = 0;
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) w |= static_cast<uint32_t>(static_cast<uint8_t>(quant8(x[q][v], inv))) << (8 * v);
+                        *reinterpret_cast<uint32_t*>(static_cast<int8_t*>(col) + o) = w;
+                    } else {
+                        static_cast<int8_t*>(col)[o] = quant8(x[q][0], inv);
+                    }
+                }
+            }
+            t += dt;
+            c += dc;
+            if (c >= cpr) { c -= cpr; ++t; }
         }
     }
 }
 
-// Filter [OC, K] in the GEMM precision: BF16 (RNE) or INT8 (scale scales[1]).
+// Filter [OC, K] in the GEMM precision: BF16 (RNE) or INT8 (times 1/s_f = scales[3]).
 template <int MODE>
 __global__ void conv3d_filter_kernel(const float* __restrict__ f, void* out, int64_t n, const float* scales) {
     const float inv = MODE == 2 ? scales[3] : 1.0f;
@@ -135,11 +193,16 @@ int grid_for(int64_t n) {
 cudaError_t launch_conv3d_im2col(const Conv3dGeom& g, int mode, const float* in, void* col,
                                  const float* scales, cudaStream_t s) {
     if (g.KD * g.KH * g.KW > kConv3dMaxTaps) return cudaErrorInvalidValue;
-    const int grid = static_cast<int>(g.M < 148 * 16 ? g.M : 148 * 16);
-    switch (mode) {
-        case 0: im2col3d_kernel<0><<<grid, kThreads, 0, s>>>(g, in, col, scales); break;
-        case 1: im2col3d_kernel<1><<<grid, kThreads, 0, s>>>(g, in, col, scales); break;
-        case 2: im2col3d_kernel<2><<<grid, kThreads, 0, s>>>(g, in, col, scales); break;
+    const int64_t passes = (g.M + 3) / 4;   // four rows per CTA pass
+    const int grid = static_cast<int>(passes < 148 * 16 ? passes : 148 * 16);
+    const bool v4 = g.IC % 4 == 0 && reinterpret_cast<uintptr_t>(in) % 16 == 0;
+    switch (mode * 2 + (v4 ? 1 : 0)) {
+        case 0: im2col3d_kernel<0, 1><<<grid, kThreads, 0, s>>>(g, in, col, scales); break;
+        case 1: im2col3d_kernel<0, 4><<<grid, kThreads, 0, s>>>(g, in, col, scales); break;
+        case 2: im2col3d_kernel<1, 1><<<grid, kThreads, 0, s>>>(g, in, col, scales); break;
+        case 3: im2col3d_kernel<1, 4><<<grid, kThreads, 0, s>>>(g, in, col, scales); break;
+        case 4: im2col3d_kernel<2, 1><<<grid, kThreads, 0, s>>>(g, in, col, scales); break;
+        case 5: im2col3d_kernel<2, 4><<<grid, kThreads, 0, s>>>(g, in, col, scales); break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();

@@ -376,12 +376,31 @@ bool encode_2d(CUtensorMap* m, CUtensorMapDataType t, const void* ptr, uint64_t 
 
 }  // namespace
 
-bool gemm_bf16_tc_supported(const GemmArgs& g) {
+namespace {
+bool shape_ok(const GemmArgs& g) {
     if (g.M < 1 || g.N < 1 || g.K < 1 || g.N > 256 || g.a_trans) return false;
     if (reinterpret_cast<uintptr_t>(g.A) % 16 || g.lda % 8 || g.lda < g.K) return false;
     if (reinterpret_cast<uintptr_t>(g.C) % 16 || g.ldc % 4 || g.ldc < g.N) return false;
-    if (get_encode_fn() == nullptr) return false;
-    return plan_layout(g).stages >= 2;
+    return get_encode_fn() != nullptr;
+}
+}  // namespace
+
+bool gemm_bf16_tc_supported(const GemmArgs& g) {
+    return shape_ok(g) && plan_layout(g).stages >= 2;
+}
+
+// B stays resident in shared memory, so a deep K (conv3d's im2col GEMMs:
+// K = 27*IC) may not fit: the caller then runs K in chunks of this many rows
+// (a multiple of the 64-row K-block), accumulating into C with beta = 1.
+int gemm_bf16_tc_kchunk(const GemmArgs& g) {
+    if (!shape_ok(g)) return 0;
+    if (plan_layout(g).stages >= 2) return g.K;
+    GemmArgs t = g;
+    for (int kc = (g.K - 1) / kKBlock * kKBlock; kc >= kKBlock; kc -= kKBlock) {
+        t.K = kc;
+        if (plan_layout(t).stages >= 2) return kc;
+    }
+    return 0;
 }
 
 cudaError_t launch_gemm_bf16_tc(const GemmArgs& g, int num_sms, uint32_t* err, cudaStream_t s) {

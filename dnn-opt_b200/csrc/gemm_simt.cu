@@ -9,8 +9,9 @@
 //
 // FP32 results must match the reference within 1e-5*K, so the products stay
 // FP32 FMAs (no TF32/BF16 tensor-core rounding).  Design:
-//   * CTA tile BM x 128 (BM = 16, 32 or 64 by M), 256 threads, each thread
-//     BM/8 rows x 4 consecutive columns; K in 32-deep slices staged in two
+//   * CTA tile BM x BN (BM = 16, 32 or 64 by M; BN = 128, or 64 when N <= 64 so
+//     narrow outputs such as conv3d's OC = 64 waste no columns), 256 threads,
+//     each thread BM*BN/1024 rows x 4 consecutive columns; K in 32-deep slices staged in two
 //     shared-memory buffers, the next slice's global loads issued before the
 //     current slice's FMAs (register prefetch), one barrier per slice;
 //   * A is staged k-major (a thread's BM/8 row values come back as 16-byte
@@ -33,7 +34,6 @@ namespace dnnopt_b200 {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int BN = 128;
 constexpr int BK = 32;
 constexpr int kPadA = 4;      // keeps 16-byte alignment of k-major rows
 constexpr int kPadB = 4;
@@ -45,18 +45,21 @@ struct SimtParams {
     int vec_b;      // 1: B is K x N with 16-byte aligned rows (4-wide loads)
 };
 
-template <int BM>
+template <int BM, int BN>
 constexpr size_t simt_smem_bytes() {
     return 2 * (static_cast<size_t>(BK) * (BM + kPadA) + static_cast<size_t>(BK) * (BN + kPadB)) *
            sizeof(float);
 }
 
-template <In IA, In IB, int BM>
+template <In IA, In IB, int BM, int BN>
 __global__ void __launch_bounds__(kThreads, 2)
 gemm_simt_kernel(const SimtParams p) {
     using TA = typename Elem<IA>::T;
     using TB = typename Elem<IB>::T;
-    constexpr int TM = BM / 8;                       // rows per thread
+    constexpr int kColGroups = BN / 4;               // threads across a tile row
+    constexpr int kRowGroups = kThreads / kColGroups;
+    constexpr int TM = BM / kRowGroups;              // rows per thread
+    static_assert(TM >= 1, "tile too small for 256 threads");
     constexpr int LA = BM * BK / kThreads;           // A elements each thread stages per slice
     constexpr int LB = BK * BN / kThreads;           // B elements (16)
     constexpr int SA = BK * (BM + kPadA);            // floats per A buffer
@@ -70,7 +73,7 @@ gemm_simt_kernel(const SimtParams p) {
 
     const GemmArgs& g = p.g;
     const int tid = threadIdx.x;
-    const int tx = tid & 31, ty = tid >> 5;          // columns 4*tx.., rows TM*ty..
+    const int tx = tid % kColGroups, ty = tid / kColGroups;   // columns 4*tx.., rows TM*ty..
     const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
     const int k_begin = blockIdx.z * p.kchunk;
     const int k_end = min(g.K, k_begin + p.kchunk);
@@ -177,9 +180,11 @@ gemm_simt_kernel(const SimtParams p) {
                     const float4 v = *reinterpret_cast<const float4*>(a + k * (BM + kPadA) + 4 * q);
                     av[4 * q] = v.x; av[4 * q + 1] = v.y; av[4 * q + 2] = v.z; av[4 * q + 3] = v.w;
                 }
-            } else {
+            } else if constexpr (TM == 2) {
                 const float2 v = *reinterpret_cast<const float2*>(a + k * (BM + kPadA));
                 av[0] = v.x; av[1] = v.y;
+            } else {
+                av[0] = a[k * (BM + kPadA)];
             }
             const float4 bv = *reinterpret_cast<const float4*>(b + k * (BN + kPadB));
 #pragma unroll
@@ -241,31 +246,33 @@ gemm_simt_kernel(const SimtParams p) {
     cluster_sync_all();   // no CTA leaves while another still reads its tile
 }
 
-template <In IA, In IB>
-const void* simt_fn(int bm) {
+template <In IA, In IB, int BN>
+const void* simt_fn_bn(int bm) {
     switch (bm) {
-        case 16: return reinterpret_cast<const void*>(&gemm_simt_kernel<IA, IB, 16>);
-        case 32: return reinterpret_cast<const void*>(&gemm_simt_kernel<IA, IB, 32>);
-        case 64: return reinterpret_cast<const void*>(&gemm_simt_kernel<IA, IB, 64>);
+        case 16: return reinterpret_cast<const void*>(&gemm_simt_kernel<IA, IB, 16, BN>);
+        case 32: return reinterpret_cast<const void*>(&gemm_simt_kernel<IA, IB, 32, BN>);
+        case 64: return reinterpret_cast<const void*>(&gemm_simt_kernel<IA, IB, 64, BN>);
         default: return nullptr;
     }
 }
 
-const void* simt_select(In ia, In ib, int bm) {
-    if (ia == In::F32 && ib == In::F32) return simt_fn<In::F32, In::F32>(bm);
-    if (ia == In::BF16 && ib == In::BF16) return simt_fn<In::BF16, In::BF16>(bm);
-    if (ia == In::F32R && ib == In::F32R) return simt_fn<In::F32R, In::F32R>(bm);
-    if (ia == In::RE4 && ib == In::RE5) return simt_fn<In::RE4, In::RE5>(bm);
-    if (ia == In::RE5 && ib == In::RE5) return simt_fn<In::RE5, In::RE5>(bm);
+template <In IA, In IB>
+const void* simt_fn(int bm, int bn) {
+    return bn == 64 ? simt_fn_bn<IA, IB, 64>(bm) : (bn == 128 ? simt_fn_bn<IA, IB, 128>(bm) : nullptr);
+}
+
+const void* simt_select(In ia, In ib, int bm, int bn) {
+    if (ia == In::F32 && ib == In::F32) return simt_fn<In::F32, In::F32>(bm, bn);
+    if (ia == In::BF16 && ib == In::BF16) return simt_fn<In::BF16, In::BF16>(bm, bn);
+    if (ia == In::F32R && ib == In::F32R) return simt_fn<In::F32R, In::F32R>(bm, bn);
+    if (ia == In::RE4 && ib == In::RE5) return simt_fn<In::RE4, In::RE5>(bm, bn);
+    if (ia == In::RE5 && ib == In::RE5) return simt_fn<In::RE5, In::RE5>(bm, bn);
     return nullptr;
 }
 
-size_t smem_for(int bm) {
-    switch (bm) {
-        case 16: return simt_smem_bytes<16>();
-        case 32: return simt_smem_bytes<32>();
-        default: return simt_smem_bytes<64>();
-    }
+size_t smem_for(int bm, int bn) {
+    if (bn == 64) return bm == 16 ? simt_smem_bytes<16, 64>() : (bm == 32 ? simt_smem_bytes<32, 64>() : simt_smem_bytes<64, 64>());
+    return bm == 16 ? simt_smem_bytes<16, 128>() : (bm == 32 ? simt_smem_bytes<32, 128>() : simt_smem_bytes<64, 128>());
 }
 
 // Dynamic shared memory above 48 KB needs the attribute once per device and kernel.
@@ -296,7 +303,8 @@ size_t elem_size(In i) {
 GemmSimtPlan gemm_simt_plan(const GemmArgs& g, int num_sms) {
     GemmSimtPlan p;
     p.bm = g.M <= 16 ? 16 : (g.M <= 32 ? 32 : 64);
-    const int64_t tiles = static_cast<int64_t>((g.N + BN - 1) / BN) * ((g.M + p.bm - 1) / p.bm);
+    p.bn = g.N <= 64 ? 64 : 128;
+    const int64_t tiles = static_cast<int64_t>((g.N + p.bn - 1) / p.bn) * ((g.M + p.bm - 1) / p.bm);
     const int64_t want = 2 * static_cast<int64_t>(num_sms > 0 ? num_sms : 148);
     int s = static_cast<int>((want + tiles - 1) / tiles);
     const int max_by_k = (g.K + 2 * BK - 1) / (2 * BK);      // at least two slices per split
@@ -312,9 +320,9 @@ GemmSimtPlan gemm_simt_plan(const GemmArgs& g, int num_sms) {
 
 cudaError_t launch_gemm_simt(In ia, In ib, const GemmArgs& g, const GemmSimtPlan& plan,
                              cudaStream_t s) {
-    const void* fn = simt_select(ia, ib, plan.bm);
+    const void* fn = simt_select(ia, ib, plan.bm, plan.bn);
     if (!fn || plan.splits < 1 || plan.splits > kMaxSplits || plan.kchunk < BK) return cudaErrorInvalidValue;
-    const size_t smem = smem_for(plan.bm);
+    const size_t smem = smem_for(plan.bm, plan.bn);
     cudaError_t e = prepare(fn, smem);
     if (e != cudaSuccess) return e;
     SimtParams sp;
@@ -323,7 +331,7 @@ cudaError_t launch_gemm_simt(In ia, In ib, const GemmArgs& g, const GemmSimtPlan
     const size_t eb = elem_size(ib);
     sp.vec_b = (!g.b_trans && reinterpret_cast<uintptr_t>(g.B) % (4 * eb) == 0 && g.ldb % 4 == 0) ? 1 : 0;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>((g.N + BN - 1) / BN), static_cast<unsigned>((g.M + plan.bm - 1) / plan.bm),
+    cfg.gridDim = dim3(static_cast<unsigned>((g.N + plan.bn - 1) / plan.bn), static_cast<unsigned>((g.M + plan.bm - 1) / plan.bm),
                        static_cast<unsigned>(plan.splits));
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;

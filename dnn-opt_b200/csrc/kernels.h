@@ -99,11 +99,12 @@ cudaError_t launch_gemv_rows(DotKind kind, const GemmArgs& g, int mt, int grid, 
                              cudaStream_t s);
 
 // ---- general tiled SIMT kernels (any M, N, K, strides, transposes) ----------
-// General FP32-accumulate GEMM on the CUDA cores (gemm_simt.cu): BM x 128
-// tiles (BM = 16, 32, 64 by M), K split over up to 8 CTAs of a cluster when
+// General FP32-accumulate GEMM on the CUDA cores (gemm_simt.cu): BM x BN
+// tiles (BM = 16, 32, 64 by M; BN = 64 for N <= 64, else 128), K split over up to 8 CTAs of a cluster when
 // the tiles alone would leave SMs idle.
 struct GemmSimtPlan {
     int bm = 64;
+    int bn = 128;
     int splits = 1;
     int kchunk = 0;
 };
@@ -157,6 +158,8 @@ cudaError_t launch_saxpy(int n, float alpha, const float* x, int incx, float* y,
 
 // ---- BF16 tall-skinny tcgen05 GEMM (A row-major K-contiguous, TMA) ----------
 bool gemm_bf16_tc_supported(const GemmArgs& g);
+// Rows of K one launch can take (g.K when B fits whole, 0 when the shape has no tcgen05 path).
+int gemm_bf16_tc_kchunk(const GemmArgs& g);
 // ---- config-5 e4m3 weight GEMM on tcgen05 (kind::f8f6f4), M <= 8 ------------
 struct E4m3TcPlan {
     int splits;   // K ranges (gridDim.y); > 1 reduces through ws + tickets

@@ -292,7 +292,7 @@ Plan heuristic_plan(Kind kind, const GemmArgs& g, const DeviceInfo& info) {
         p.nk = nk_plan_for(kind, g, info, 0);
         return p;
     }
-    if (kind == Kind::BF16F32 && g.M > 8 && info.have_device && gemm_bf16_tc_supported(g)) {
+    if (kind == Kind::BF16F32 && g.M > 8 && info.have_device && gemm_bf16_tc_kchunk(g) > 0) {
         p.kernel = KernelId::Bf16Tc;
         return p;
     }
@@ -325,8 +325,8 @@ std::string describe_plan(Kind, const GemmArgs& g, const Plan& p) {
                           p.slab_w, gemv_slab_ctas(g.N, p.slab_w), p.tuned ? " tuned" : "");
             break;
         case KernelId::TileF32:
-            std::snprintf(buf, sizeof(buf), "%s bm=%d splits=%d kchunk=%d", kernel_name(p.kernel),
-                          p.simt.bm, p.simt.splits, p.simt.kchunk);
+            std::snprintf(buf, sizeof(buf), "%s bm=%d bn=%d splits=%d kchunk=%d", kernel_name(p.kernel),
+                          p.simt.bm, p.simt.bn, p.simt.splits, p.simt.kchunk);
             break;
         default:
             std::snprintf(buf, sizeof(buf), "%s", kernel_name(p.kernel));

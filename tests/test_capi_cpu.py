@@ -146,9 +146,9 @@ def test_plan_selection_without_device(dn):
     s = dn.plan_describe(dn.KIND_E4M3BF16, dn.desc(8, 28672, 8192, 8192, 8192, 28672))
     assert s.startswith("gemv_nk_dot mt=8"), s
     s = dn.plan_describe(dn.KIND_F32, dn.desc(127, 127, 127, 127, 127, 127))
-    assert s == "gemm_simt bm=64 splits=2 kchunk=64", s      # 2 tiles: K split, two 32-deep slices per CTA
+    assert s == "gemm_simt bm=64 bn=128 splits=2 kchunk=64", s      # 2 tiles: K split, two 32-deep slices per CTA
     s = dn.plan_describe(dn.KIND_F32, dn.desc(16, 4096, 4096, 4096, 4096, 4096))
-    assert s == "gemm_simt bm=16 splits=8 kchunk=512", s      # M 9-16: 16-row tiles
+    assert s == "gemm_simt bm=16 bn=128 splits=8 kchunk=512", s      # M 9-16: 16-row tiles
     s = dn.plan_describe(dn.KIND_F32, dn.desc(3, 64, 32, 3, 32, 64, trans_a=1, trans_b=1))
     assert s.startswith("gemv_rows_dot"), s
     s = dn.plan_describe(dn.KIND_F32, dn.desc(3, 64, 30, 3, 30, 64, trans_a=1, trans_b=1))

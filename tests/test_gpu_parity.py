@@ -297,7 +297,9 @@ def test_fp32_transposed_b_small_m(gpu, dn, orc, M, N, K, beta):
 
 @pytest.mark.parametrize("M,N,K,beta,ta,tb", [
     (9, 4096, 1024, 0.5, 0, 0), (16, 1009, 2048, 0.0, 0, 0), (33, 777, 300, 1.0, 0, 1),
-    (64, 2048, 512, -0.5, 1, 0), (40, 130, 1000, 0.0, 1, 1), (128, 515, 96, 0.5, 0, 0)])
+    (64, 2048, 512, -0.5, 1, 0), (40, 130, 1000, 0.0, 1, 1), (128, 515, 96, 0.5, 0, 0),
+    # N <= 64: 64-column tiles
+    (200, 64, 300, 0.5, 0, 1), (37, 33, 129, 0.0, 1, 0), (16, 48, 1024, 1.0, 0, 0)])
 def test_fp32_simt_small_m_bands(gpu, dn, orc, M, N, K, beta, ta, tb):
     """M from 9 up on the general SIMT kernel (16/32/64-row tiles, K split
     over a cluster), every transposition."""
@@ -471,7 +473,9 @@ def test_bf16_tcgen05_shapes(gpu, dn, orc, M, N, K, alpha, beta, ldc):
 @pytest.mark.parametrize("M,N,K,beta,b_layout", [
     (1000, 40, 256, 0.0, "kn"), (777, 200, 192, 0.5, "kn"), (512, 256, 64, 0.0, "kn"),
     (300, 24, 136, 0.0, "kn"), (4096, 64, 256, 0.0, "nk"), (333, 48, 104, 0.5, "nk"),
-    (257, 200, 64, 0.0, "nk"), (2000, 64, 256, 0.0, "kn_pad1"), (129, 36, 72, 0.5, "kn_pad1")])
+    (257, 200, 64, 0.0, "nk"), (2000, 64, 256, 0.0, "kn_pad1"), (129, 36, 72, 0.5, "kn_pad1"),
+    # deep K: B does not fit shared memory whole, K runs in chunks accumulating into C
+    (2000, 64, 1728, 0.5, "nk"), (1500, 128, 2056, 0.0, "kn"), (777, 200, 1032, 0.5, "kn_pad1")])
 def test_bf16_tcgen05_b_layouts(gpu, dn, orc, M, N, K, beta, b_layout):
     ldb = {"kn": N, "nk": K, "kn_pad1": N + 1}[b_layout]
     d = dn.desc(M, N, K, K, ldb, N, 1.0, beta, 0, int(b_layout == "nk"))
