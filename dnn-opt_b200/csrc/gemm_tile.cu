@@ -1,7 +1,8 @@
-// General-shape int8 SIMT kernel (any M, N, K, leading dimensions and
-// transpositions) for the int8 calls outside the dot-form GEMV class, so that
-// every int8 call the reference accepts has a GPU path (the FP32-accumulate
-// general kernel is gemm_simt.cu).
+// General-shape int8 SIMT kernel (any M, N, K and leading dimensions) for the
+// int8 calls outside the dot-form GEMV class (M > 8, unaligned rows, conv3d's
+// column matrices), so that every int8 call the reference accepts has a GPU
+// path: dp4a on register tiles (the FP32-accumulate general kernel is
+// gemm_simt.cu).
 //
 // Also here: the FP32-API int8 quantisation (per-tensor absmax / 127,
 // lrintf, clamp to [-128, 127]) of reference src/gemm/gemm_smallm_int8.cpp:198-236
@@ -14,56 +15,147 @@ namespace dnnopt_b200 {
 
 namespace {
 
-constexpr int BM = 64, BN = 64, BK = 16, kThreads = 256;
+constexpr int kThreads = 256;
+constexpr int BM = 64, BN = 64;
+constexpr int BKB = 64;               // K bytes per slice
+constexpr int BKW = BKB / 4;          // 32-bit words (four int8 each) per slice
+constexpr int kPad = 4;
+constexpr int kMaxSplits = 8;
 
-// int8 x int8 -> int32 (exact) with A [M, K] and B [N, K]; optional dequant epilogue.
+struct S8Params {
+    GemmArgs g;
+    const float* scales;
+    int kchunk;     // K bytes per split (multiple of BKB)
+    int vec;        // 1: A and B rows 4-byte aligned (word loads)
+};
+
+// int8 x int8 -> int32 (exact) with A [M, K] and B [N, K] (K contiguous in
+// both); optional dequantising epilogue.  64 x 64 CTA tiles, 4 x 4 outputs per
+// thread, K in 64-byte slices through two shared-memory buffers (next slice's
+// words loaded before the current slice's dp4a), K split over up to 8 CTAs of
+// a cluster when the tiles alone leave SMs idle (int32 partials summed
+// through distributed shared memory: exact, so the order does not matter).
 template <bool DQ>
 __global__ void __launch_bounds__(kThreads)
-gemm_tile_s8_kernel(const GemmArgs g, const float* scales) {
-    __shared__ int32_t sA[BK][BM + 4];
-    __shared__ int32_t sB[BK][BN + 4];
+gemm_tile_s8_kernel(const S8Params p) {
+    // One array carved into the two operands' buffers, so that the split-K
+    // partial tile (BM x BN words) can reuse the whole of it.
+    __shared__ __align__(16) int32_t smem[2 * BKW * (BM + kPad) + 2 * BKW * (BN + kPad)];
+    static_assert(sizeof(smem) >= sizeof(int32_t) * BM * BN, "partial tile must fit");
+    auto sA = reinterpret_cast<int32_t (*)[BKW][BM + kPad]>(smem);
+    auto sB = reinterpret_cast<int32_t (*)[BKW][BN + kPad]>(smem + 2 * BKW * (BM + kPad));
+    pdl_wait();
+    pdl_launch_dependents();
+    const GemmArgs& g = p.g;
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
     const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int k_begin = blockIdx.z * p.kchunk;
+    const int k_end = min(g.K, k_begin + p.kchunk);
+    const int nslices = k_end > k_begin ? (k_end - k_begin + BKB - 1) / BKB : 0;
     const int8_t* A = static_cast<const int8_t*>(g.A);
     const int8_t* B = static_cast<const int8_t*>(g.B);
-    int32_t acc[4][4] = {};
-    for (int k0 = 0; k0 < g.K; k0 += BK) {
-        for (int idx = tid; idx < BM * BK; idx += kThreads) {
-            int k = idx % BK, i = idx / BK, gi = m0 + i, gk = k0 + k;
-            sA[k][i] = (gi < g.M && gk < g.K) ? A[(int64_t)gi * g.lda + gk] : 0;
-        }
-        for (int idx = tid; idx < BK * BN; idx += kThreads) {
-            int k = idx % BK, j = idx / BK, gj = n0 + j, gk = k0 + k;
-            sB[k][j] = (gj < g.N && gk < g.K) ? B[(int64_t)gj * g.ldb + gk] : 0;
-        }
-        __syncthreads();
+
+    // Word w (bytes 4w..4w+3 of the slice) of row r of a [rows, K] int8 matrix.
+    auto word = [&](const int8_t* X, int64_t ld, int row, int rows, int k) -> int32_t {
+        if (row >= rows || k >= k_end) return 0;
+        const int8_t* q = X + (int64_t)row * ld + k;
+        if (p.vec && k + 4 <= k_end) return *reinterpret_cast<const int32_t*>(q);
+        uint32_t w = 0;
 #pragma unroll
-        for (int k = 0; k < BK; ++k) {
+        for (int b = 0; b < 4; ++b)
+            if (k + b < k_end) w |= static_cast<uint32_t>(static_cast<uint8_t>(q[b])) << (8 * b);
+        return static_cast<int32_t>(w);
+    };
+    constexpr int LW = BM * BKW / kThreads;   // words per thread per operand (4)
+    int32_t ra[LW], rb[LW];
+    auto load_slice = [&](int k0) {
+#pragma unroll
+        for (int i = 0; i < LW; ++i) {
+            const int e = tid + i * kThreads;
+            const int r = e / BKW, w = e % BKW;
+            ra[i] = word(A, g.lda, m0 + r, g.M, k0 + 4 * w);
+            rb[i] = word(B, g.ldb, n0 + r, g.N, k0 + 4 * w);
+        }
+    };
+    auto store_slice = [&](int buf) {
+#pragma unroll
+        for (int i = 0; i < LW; ++i) {
+            const int e = tid + i * kThreads;
+            const int r = e / BKW, w = e % BKW;
+            sA[buf][w][r] = ra[i];
+            sB[buf][w][r] = rb[i];
+        }
+    };
+
+    int32_t acc[4][4] = {};
+    if (nslices > 0) {
+        load_slice(k_begin);
+        store_slice(0);
+        __syncthreads();
+    }
+    for (int t = 0; t < nslices; ++t) {
+        const int buf = t & 1;
+        if (t + 1 < nslices) load_slice(k_begin + (t + 1) * BKB);
+#pragma unroll 4
+        for (int w = 0; w < BKW; ++w) {
+            const int4 av = *reinterpret_cast<const int4*>(&sA[buf][w][4 * ty]);
+            const int4 bv = *reinterpret_cast<const int4*>(&sB[buf][w][4 * tx]);
+            const int a[4] = {av.x, av.y, av.z, av.w};
+            const int b[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
             for (int r = 0; r < 4; ++r)
 #pragma unroll
-                for (int c = 0; c < 4; ++c) acc[r][c] += sA[k][ty * 4 + r] * sB[k][tx * 4 + c];
+                for (int c = 0; c < 4; ++c) acc[r][c] = __dp4a(a[r], b[c], acc[r][c]);
         }
+        if (t + 1 < nslices) store_slice(buf ^ 1);
         __syncthreads();
     }
+
+    auto finish = [&](int gi, int gj, int32_t v) {
+        if constexpr (DQ) {
+            float* cp = static_cast<float*>(g.C) + (int64_t)gi * g.ldc + gj;
+            const float scale = __fmul_rn(g.alpha, __fmul_rn(p.scales[0], p.scales[1]));
+            const float c0 = (g.beta == 0.0f) ? 0.0f : __fmul_rn(g.beta, *cp);
+            *cp = __fadd_rn(c0, __fmul_rn(scale, static_cast<float>(v)));
+        } else {
+            static_cast<int32_t*>(g.C)[(int64_t)gi * g.ldc + gj] = v;
+        }
+    };
+    if (gridDim.z == 1) {
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-        int gi = m0 + ty * 4 + r;
-        if (gi >= g.M) continue;
+        for (int r = 0; r < 4; ++r) {
+            const int gi = m0 + 4 * ty + r;
+            if (gi >= g.M) continue;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            int gj = n0 + tx * 4 + c;
-            if (gj >= g.N) continue;
-            if constexpr (DQ) {
-                float* cp = static_cast<float*>(g.C) + (int64_t)gi * g.ldc + gj;
-                float scale = __fmul_rn(g.alpha, __fmul_rn(scales[0], scales[1]));
-                float c0 = (g.beta == 0.0f) ? 0.0f : __fmul_rn(g.beta, *cp);
-                *cp = __fadd_rn(c0, __fmul_rn(scale, static_cast<float>(acc[r][c])));
-            } else {
-                static_cast<int32_t*>(g.C)[(int64_t)gi * g.ldc + gj] = acc[r][c];
+            for (int c = 0; c < 4; ++c) {
+                const int gj = n0 + 4 * tx + c;
+                if (gj < g.N) finish(gi, gj, acc[r][c]);
             }
         }
+        return;
     }
+    // Cluster K split: partial tiles parked in this CTA's (idle) A buffers,
+    // CTA q finishes elements q*256 + tid, + S*256, ... over ranks 0..S-1.
+    int32_t* part = smem;           // [BM][BN]
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+        *reinterpret_cast<int4*>(&part[(4 * ty + r) * BN + 4 * tx]) = make_int4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+    cluster_sync_all();
+    const int S = static_cast<int>(gridDim.z);
+    const uint32_t q = cluster_ctarank();
+    const uint32_t part_addr = smem_u32(part);
+    for (int e = static_cast<int>(q) * kThreads + tid; e < BM * BN; e += S * kThreads) {
+        const int mm = e / BN, nn = e - mm * BN;
+        int32_t v[kMaxSplits];
+#pragma unroll
+        for (int r = 0; r < kMaxSplits; ++r)
+            v[r] = r < S ? __float_as_int(ld_dsmem_f32(map_to_cta(part_addr + e * 4u, static_cast<uint32_t>(r)))) : 0;
+        int32_t sum = 0;
+#pragma unroll
+        for (int r = 0; r < kMaxSplits; ++r) sum += v[r];
+        if (m0 + mm < g.M && n0 + nn < g.N) finish(m0 + mm, n0 + nn, sum);
+    }
+    cluster_sync_all();   // no CTA leaves while another still reads its tile
 }
 
 // Per-tensor absmax of op(A) (M x K) and B (K x N, or N x K when b_trans):
@@ -182,11 +274,50 @@ __global__ void quantize_ref_fp8_kernel(const GemmArgs g, uint8_t* qa, uint8_t* 
 
 cudaError_t launch_gemm_tile_s8(DotKind kind, const GemmArgs& g, const float* scales,
                                 cudaStream_t s) {
-    dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM);
-    if (kind == DotKind::S8S32) gemm_tile_s8_kernel<false><<<grid, kThreads, 0, s>>>(g, scales);
-    else if (kind == DotKind::S8DQ) gemm_tile_s8_kernel<true><<<grid, kThreads, 0, s>>>(g, scales);
-    else return cudaErrorInvalidValue;
-    return cudaGetLastError();
+    if (kind != DotKind::S8S32 && kind != DotKind::S8DQ) return cudaErrorInvalidValue;
+    int dev = 0, sms = 148;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) sms = 148;
+    S8Params sp;
+    sp.g = g;
+    sp.scales = scales;
+    sp.vec = (reinterpret_cast<uintptr_t>(g.A) % 4 == 0 && reinterpret_cast<uintptr_t>(g.B) % 4 == 0 &&
+              g.lda % 4 == 0 && g.ldb % 4 == 0) ? 1 : 0;
+    const int64_t tiles = static_cast<int64_t>((g.N + BN - 1) / BN) * ((g.M + BM - 1) / BM);
+    int splits = static_cast<int>((2 * static_cast<int64_t>(sms) + tiles - 1) / tiles);
+    const int max_by_k = (g.K + 2 * BKB - 1) / (2 * BKB);   // at least two slices per split
+    if (splits > max_by_k) splits = max_by_k;
+    if (splits > kMaxSplits) splits = kMaxSplits;
+    if (splits < 1) splits = 1;
+    int kchunk = (g.K + splits - 1) / splits;
+    kchunk = (kchunk + BKB - 1) / BKB * BKB;
+    if (kchunk < BKB) kchunk = BKB;
+    splits = (g.K + kchunk - 1) / kchunk;
+    if (splits < 1) splits = 1;
+    sp.kchunk = kchunk;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((g.N + BN - 1) / BN), static_cast<unsigned>((g.M + BM - 1) / BM),
+                       static_cast<unsigned>(splits));
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    int na = 1;
+    if (splits > 1) {
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = 1;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = static_cast<unsigned>(splits);
+        na = 2;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    void* args[] = {&sp};
+    const void* fn = kind == DotKind::S8S32 ? reinterpret_cast<const void*>(&gemm_tile_s8_kernel<false>)
+                                            : reinterpret_cast<const void*>(&gemm_tile_s8_kernel<true>);
+    return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
 cudaError_t launch_absmax2(const GemmArgs& g, uint32_t* absmax_bits, cudaStream_t s) {

@@ -385,7 +385,14 @@ def test_int8_edges_bitexact(gpu, dn, orc):
                                           (2, 5000, 127, 128, 127, 5000, 3),
                                           (8, 1000, 8192, 8192, 8192, 1000, 0),
                                           (3, 3001, 4112, 4112, 4128, 3001, 0),
-                                          (6, 17, 64, 80, 64, 17, 0)]:
+                                          (6, 17, 64, 80, 64, 17, 0),
+                                          # general dp4a tiles: split-K clusters, byte-wise
+                                          # loads for unaligned rows, K below one word
+                                          (100, 300, 1000, 1001, 1003, 300, 1),
+                                          (64, 64, 4096, 4096, 4096, 64, 0),
+                                          (200, 1000, 64, 64, 64, 1000, 0),
+                                          (17, 33, 3, 3, 3, 33, 0),
+                                          (130, 70, 1730, 1732, 1736, 72, 0)]:
         A = int8_uniform(M * lda, 7)
         Bb = int8_uniform(N * ldb + off, 8)
         ref = np.zeros(M * ldc, np.int32)
