@@ -10,12 +10,16 @@
 // FP32 results must match the reference within 1e-5*K, so the products stay
 // FP32 FMAs (no TF32/BF16 tensor-core rounding).  Design:
 //   * CTA tile BM x BN (BM = 16, 32 or 64 by M; BN = 128, or 64 when N <= 64 so
-//     narrow outputs such as conv3d's OC = 64 waste no columns), 256 threads,
+//     narrow outputs such as conv3d's OC = 64 waste no columns, with BM = 128
+//     when such an output has at least 128 rows per SM), 256 threads,
 //     each thread BM*BN/1024 rows x 4 consecutive columns; K in 32-deep slices staged in two
 //     shared-memory buffers, the next slice's global loads issued before the
 //     current slice's FMAs (register prefetch), one barrier per slice;
-//   * A is staged k-major (a thread's BM/8 row values come back as 16-byte
-//     broadcast loads), B n-major (one 16-byte load per thread and k);
+//   * both operands are staged k-major in shared memory (a thread's rows and
+//     its 4 columns come back as 16-byte loads), with the row index XOR-ed by
+//     k / 4 so that the transposing stores of k-contiguous operands (A not
+//     transposed, B transposed; 16-byte global loads along k) hit 32 distinct
+//     banks;
 //   * small tile counts split K over up to 8 CTAs of one thread-block cluster;
 //     the partial tiles are summed through distributed shared memory in rank
 //     order (deterministic), each CTA finishing 1/S of the tile;
@@ -42,13 +46,31 @@ constexpr int kMaxSplits = 8;
 struct SimtParams {
     GemmArgs g;
     int kchunk;     // K rows per split (multiple of BK)
-    int vec_b;      // 1: B is K x N with 16-byte aligned rows (4-wide loads)
+    int vec_a;      // 1: A's rows start on 4-element boundaries (4-wide loads when not transposed)
+    int vec_b;      // 1: B's rows start on 4-element boundaries (4-wide loads in either layout)
 };
 
 template <int BM, int BN>
 constexpr size_t simt_smem_bytes() {
     return 2 * (static_cast<size_t>(BK) * (BM + kPadA) + static_cast<size_t>(BK) * (BN + kPadB)) *
            sizeof(float);
+}
+
+// Four consecutive k of row `row` of a k-contiguous [rows, ld] operand (row
+// start and k on 4-element boundaries), zero past the row count and k_end.
+template <In I>
+__device__ __forceinline__ void load_krow4(const typename Elem<I>::T* X, int64_t ld, int row, int rows, int k,
+                                           int k_end, float (&v)[4]) {
+    v[0] = v[1] = v[2] = v[3] = 0.0f;
+    if (row >= rows || k >= k_end) return;
+    const typename Elem<I>::T* q = X + (int64_t)row * ld + k;
+    if (k + 4 <= k_end) {
+        load4<I>(q, v);
+    } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            if (k + c < k_end) v[c] = dec<I>(q[c]);
+    }
 }
 
 template <In IA, In IB, int BM, int BN>
@@ -81,19 +103,57 @@ gemm_simt_kernel(const SimtParams p) {
     const TA* A = static_cast<const TA*>(g.A);
     const TB* B = static_cast<const TB*>(g.B);
 
+    // Shared-memory layout: operand element (row, k) of a slice sits at
+    // k * (R + 4) + swz(row, k), where swz flips bits 2-4 of the row by k / 4.
+    // Groups of four rows stay contiguous (16-byte reads in the FMA loop), and
+    // the transposing stores of k-contiguous data (8 threads per 32-k row
+    // segment, 4 rows per warp) land in 32 distinct banks.
+    constexpr int kSwzA = BM / 4 - 1 < 7 ? BM / 4 - 1 : 7;
+    constexpr int kSwzB = BN / 4 - 1 < 7 ? BN / 4 - 1 : 7;
+    auto swz = [](int row, int k, int mask) { return row ^ (4 * ((k >> 2) & mask)); };
+    // k-contiguous operand (A not transposed, B transposed) with 4-element
+    // aligned rows: float4 e4 of a slice is row 4 * (e4 / 32) + lane / 8,
+    // k = 4 * (lane % 8), so a warp reads four whole 128-byte row segments.
+    auto kvec_coord = [](int e4, int& row, int& k) {
+        row = 4 * (e4 >> 5) + ((e4 & 31) >> 3);
+        k = 4 * (e4 & 7);
+    };
+    auto a_coord = [&](int e, int& m, int& k) {
+        if (g.a_trans) { m = e % BM; k = e / BM; } else { k = e % BK; m = e / BK; }
+    };
+    auto b_coord = [&](int e, int& n, int& k) {
+        if (g.b_trans) { k = e % BK; n = e / BK; } else { n = e % BN; k = e / BN; }
+    };
+    const bool vec_a = BM >= 32 && !g.a_trans && p.vec_a;
+    const bool vec_bt = g.b_trans && p.vec_b;
+    const bool vec_bn = !g.b_trans && p.vec_b;
     float ra[LA], rb[LB];
     auto load_slice = [&](int k0) {
+        if constexpr (BM >= 32) {
+            if (vec_a) {
 #pragma unroll
-        for (int i = 0; i < LA; ++i) {
-            const int e = tid + i * kThreads;
-            int m, k;
-            if (g.a_trans) { m = e % BM; k = e / BM; } else { k = e % BK; m = e / BK; }
-            const int gm = m0 + m, gk = k0 + k;
-            ra[i] = (gm < g.M && gk < k_end)
-                        ? dec<IA>(A[g.a_trans ? (int64_t)gk * g.lda + gm : (int64_t)gm * g.lda + gk])
-                        : 0.0f;
+                for (int i = 0; i < LA / 4; ++i) {
+                    int m, k;
+                    kvec_coord(tid + i * kThreads, m, k);
+                    float v[4];
+                    load_krow4<IA>(A, g.lda, m0 + m, g.M, k0 + k, k_end, v);
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) ra[4 * i + c] = v[c];
+                }
+            }
         }
-        if (!g.b_trans && p.vec_b) {
+        if (!vec_a) {
+#pragma unroll
+            for (int i = 0; i < LA; ++i) {
+                int m, k;
+                a_coord(tid + i * kThreads, m, k);
+                const int gm = m0 + m, gk = k0 + k;
+                ra[i] = (gm < g.M && gk < k_end)
+                            ? dec<IA>(A[g.a_trans ? (int64_t)gk * g.lda + gm : (int64_t)gm * g.lda + gk])
+                            : 0.0f;
+            }
+        }
+        if (vec_bn) {
 #pragma unroll
             for (int i = 0; i < LB / 4; ++i) {
                 const int e = tid + i * kThreads;
@@ -113,12 +173,21 @@ gemm_simt_kernel(const SimtParams p) {
 #pragma unroll
                 for (int c = 0; c < 4; ++c) rb[4 * i + c] = v[c];
             }
+        } else if (vec_bt) {
+#pragma unroll
+            for (int i = 0; i < LB / 4; ++i) {
+                int n, k;
+                kvec_coord(tid + i * kThreads, n, k);
+                float v[4];
+                load_krow4<IB>(B, g.ldb, n0 + n, g.N, k0 + k, k_end, v);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) rb[4 * i + c] = v[c];
+            }
         } else {
 #pragma unroll
             for (int i = 0; i < LB; ++i) {
-                const int e = tid + i * kThreads;
                 int n, k;
-                if (g.b_trans) { k = e % BK; n = e / BK; } else { n = e % BN; k = e / BN; }
+                b_coord(tid + i * kThreads, n, k);
                 const int gn = n0 + n, gk = k0 + k;
                 rb[i] = (gn < g.N && gk < k_end)
                             ? dec<IB>(B[g.b_trans ? (int64_t)gn * g.ldb + gk : (int64_t)gk * g.ldb + gn])
@@ -129,28 +198,49 @@ gemm_simt_kernel(const SimtParams p) {
     auto store_slice = [&](int buf) {
         float* a = sA + buf * SA;
         float* b = sB + buf * SB;
+        if constexpr (BM >= 32) {
+            if (vec_a) {
 #pragma unroll
-        for (int i = 0; i < LA; ++i) {
-            const int e = tid + i * kThreads;
-            int m, k;
-            if (g.a_trans) { m = e % BM; k = e / BM; } else { k = e % BK; m = e / BK; }
-            a[k * (BM + kPadA) + m] = ra[i];
+                for (int i = 0; i < LA / 4; ++i) {
+                    int m, k;
+                    kvec_coord(tid + i * kThreads, m, k);
+                    const int col = swz(m, k, kSwzA);     // same for k .. k + 3
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) a[(k + c) * (BM + kPadA) + col] = ra[4 * i + c];
+                }
+            }
         }
-        if (!g.b_trans && p.vec_b) {
+        if (!vec_a) {
+#pragma unroll
+            for (int i = 0; i < LA; ++i) {
+                int m, k;
+                a_coord(tid + i * kThreads, m, k);
+                a[k * (BM + kPadA) + swz(m, k, kSwzA)] = ra[i];
+            }
+        }
+        if (vec_bn) {
 #pragma unroll
             for (int i = 0; i < LB / 4; ++i) {
                 const int e = tid + i * kThreads;
                 const int n4 = e % (BN / 4), k = e / (BN / 4);
-                *reinterpret_cast<float4*>(&b[k * (BN + kPadB) + 4 * n4]) =
+                *reinterpret_cast<float4*>(&b[k * (BN + kPadB) + swz(4 * n4, k, kSwzB)]) =
                     make_float4(rb[4 * i], rb[4 * i + 1], rb[4 * i + 2], rb[4 * i + 3]);
+            }
+        } else if (vec_bt) {
+#pragma unroll
+            for (int i = 0; i < LB / 4; ++i) {
+                int n, k;
+                kvec_coord(tid + i * kThreads, n, k);
+                const int col = swz(n, k, kSwzB);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) b[(k + c) * (BN + kPadB) + col] = rb[4 * i + c];
             }
         } else {
 #pragma unroll
             for (int i = 0; i < LB; ++i) {
-                const int e = tid + i * kThreads;
                 int n, k;
-                if (g.b_trans) { k = e % BK; n = e / BK; } else { n = e % BN; k = e / BN; }
-                b[k * (BN + kPadB) + n] = rb[i];
+                b_coord(tid + i * kThreads, n, k);
+                b[k * (BN + kPadB) + swz(n, k, kSwzB)] = rb[i];
             }
         }
     };
@@ -169,24 +259,25 @@ gemm_simt_kernel(const SimtParams p) {
     for (int t = 0; t < nslices; ++t) {
         const int buf = t & 1;
         if (t + 1 < nslices) load_slice(k_begin + (t + 1) * BK);
-        const float* a = sA + buf * SA + ty * TM;
-        const float* b = sB + buf * SB + 4 * tx;
-#pragma unroll 8
+        const float* a = sA + buf * SA;
+        const float* b = sB + buf * SB;
+#pragma unroll
         for (int k = 0; k < BK; ++k) {
             float av[TM];
             if constexpr (TM >= 4) {
 #pragma unroll
                 for (int q = 0; q < TM / 4; ++q) {
-                    const float4 v = *reinterpret_cast<const float4*>(a + k * (BM + kPadA) + 4 * q);
+                    const float4 v = *reinterpret_cast<const float4*>(
+                        a + k * (BM + kPadA) + swz(ty * TM + 4 * q, k, kSwzA));
                     av[4 * q] = v.x; av[4 * q + 1] = v.y; av[4 * q + 2] = v.z; av[4 * q + 3] = v.w;
                 }
             } else if constexpr (TM == 2) {
-                const float2 v = *reinterpret_cast<const float2*>(a + k * (BM + kPadA));
+                const float2 v = *reinterpret_cast<const float2*>(a + k * (BM + kPadA) + swz(ty * 2, k, kSwzA));
                 av[0] = v.x; av[1] = v.y;
             } else {
-                av[0] = a[k * (BM + kPadA)];
+                av[0] = a[k * (BM + kPadA) + swz(ty, k, kSwzA)];
             }
-            const float4 bv = *reinterpret_cast<const float4*>(b + k * (BN + kPadB));
+            const float4 bv = *reinterpret_cast<const float4*>(b + k * (BN + kPadB) + swz(4 * tx, k, kSwzB));
 #pragma unroll
             for (int r = 0; r < TM; ++r) {
                 acc[r][0] = fmaf(av[r], bv.x, acc[r][0]);
@@ -252,6 +343,9 @@ const void* simt_fn_bn(int bm) {
         case 16: return reinterpret_cast<const void*>(&gemm_simt_kernel<IA, IB, 16, BN>);
         case 32: return reinterpret_cast<const void*>(&gemm_simt_kernel<IA, IB, 32, BN>);
         case 64: return reinterpret_cast<const void*>(&gemm_simt_kernel<IA, IB, 64, BN>);
+        case 128:
+            if constexpr (BN == 64) return reinterpret_cast<const void*>(&gemm_simt_kernel<IA, IB, 128, 64>);
+            return nullptr;
         default: return nullptr;
     }
 }
@@ -271,7 +365,10 @@ const void* simt_select(In ia, In ib, int bm, int bn) {
 }
 
 size_t smem_for(int bm, int bn) {
-    if (bn == 64) return bm == 16 ? simt_smem_bytes<16, 64>() : (bm == 32 ? simt_smem_bytes<32, 64>() : simt_smem_bytes<64, 64>());
+    if (bn == 64)
+        return bm == 16 ? simt_smem_bytes<16, 64>()
+                        : (bm == 32 ? simt_smem_bytes<32, 64>()
+                                    : (bm == 64 ? simt_smem_bytes<64, 64>() : simt_smem_bytes<128, 64>()));
     return bm == 16 ? simt_smem_bytes<16, 128>() : (bm == 32 ? simt_smem_bytes<32, 128>() : simt_smem_bytes<64, 128>());
 }
 
@@ -304,6 +401,10 @@ GemmSimtPlan gemm_simt_plan(const GemmArgs& g, int num_sms) {
     GemmSimtPlan p;
     p.bm = g.M <= 16 ? 16 : (g.M <= 32 ? 32 : 64);
     p.bn = g.N <= 64 ? 64 : 128;
+    // Narrow outputs with many rows (conv3d's im2col GEMM: N = OC, M = output
+    // positions): 128 x 64 tiles give each thread 8 x 4 outputs, as the 64 x
+    // 128 tiles do for wide N, instead of 4 x 4.
+    if (p.bn == 64 && g.M >= 128 * static_cast<int64_t>(num_sms > 0 ? num_sms : 148)) p.bm = 128;
     const int64_t tiles = static_cast<int64_t>((g.N + p.bn - 1) / p.bn) * ((g.M + p.bm - 1) / p.bm);
     const int64_t want = 2 * static_cast<int64_t>(num_sms > 0 ? num_sms : 148);
     int s = static_cast<int>((want + tiles - 1) / tiles);
@@ -329,7 +430,9 @@ cudaError_t launch_gemm_simt(In ia, In ib, const GemmArgs& g, const GemmSimtPlan
     sp.g = g;
     sp.kchunk = plan.kchunk;
     const size_t eb = elem_size(ib);
-    sp.vec_b = (!g.b_trans && reinterpret_cast<uintptr_t>(g.B) % (4 * eb) == 0 && g.ldb % 4 == 0) ? 1 : 0;
+    sp.vec_b = (reinterpret_cast<uintptr_t>(g.B) % (4 * eb) == 0 && g.ldb % 4 == 0) ? 1 : 0;
+    const size_t ea = elem_size(ia);
+    sp.vec_a = (reinterpret_cast<uintptr_t>(g.A) % (4 * ea) == 0 && g.lda % 4 == 0) ? 1 : 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>((g.N + plan.bn - 1) / plan.bn), static_cast<unsigned>((g.M + plan.bm - 1) / plan.bm),
                        static_cast<unsigned>(plan.splits));

@@ -149,6 +149,8 @@ def test_plan_selection_without_device(dn):
     assert s == "gemm_simt bm=64 bn=128 splits=2 kchunk=64", s      # 2 tiles: K split, two 32-deep slices per CTA
     s = dn.plan_describe(dn.KIND_F32, dn.desc(16, 4096, 4096, 4096, 4096, 4096))
     assert s == "gemm_simt bm=16 bn=128 splits=8 kchunk=512", s      # M 9-16: 16-row tiles
+    s = dn.plan_describe(dn.KIND_F32, dn.desc(25088, 64, 1728, 1728, 1728, 64, trans_b=1))
+    assert s == "gemm_simt bm=128 bn=64 splits=2 kchunk=864", s     # conv3d im2col GEMM: 128 x 64 tiles
     s = dn.plan_describe(dn.KIND_F32, dn.desc(3, 64, 32, 3, 32, 64, trans_a=1, trans_b=1))
     assert s.startswith("gemv_rows_dot"), s
     s = dn.plan_describe(dn.KIND_F32, dn.desc(3, 64, 30, 3, 30, 64, trans_a=1, trans_b=1))

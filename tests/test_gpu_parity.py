@@ -299,7 +299,10 @@ def test_fp32_transposed_b_small_m(gpu, dn, orc, M, N, K, beta):
     (9, 4096, 1024, 0.5, 0, 0), (16, 1009, 2048, 0.0, 0, 0), (33, 777, 300, 1.0, 0, 1),
     (64, 2048, 512, -0.5, 1, 0), (40, 130, 1000, 0.0, 1, 1), (128, 515, 96, 0.5, 0, 0),
     # N <= 64: 64-column tiles
-    (200, 64, 300, 0.5, 0, 1), (37, 33, 129, 0.0, 1, 0), (16, 48, 1024, 1.0, 0, 0)])
+    (200, 64, 300, 0.5, 0, 1), (37, 33, 129, 0.0, 1, 0), (16, 48, 1024, 1.0, 0, 0),
+    # N <= 64 with >= 128 rows per SM: 128 x 64 tiles (conv3d's im2col GEMM)
+    (20000, 64, 300, 0.5, 0, 1), (19000, 50, 129, 0.0, 1, 0), (20011, 37, 1000, 1.0, 0, 0),
+    (19000, 64, 200, 0.0, 1, 1)])
 def test_fp32_simt_small_m_bands(gpu, dn, orc, M, N, K, beta, ta, tb):
     """M from 9 up on the general SIMT kernel (16/32/64-row tiles, K split
     over a cluster), every transposition."""
