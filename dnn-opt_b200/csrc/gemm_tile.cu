@@ -27,6 +27,8 @@ struct S8Params {
     const float* scales;
     int kchunk;     // K bytes per split (multiple of BKB)
     int vec;        // 1: A and B rows 4-byte aligned (word loads)
+    int vec16a;     // 1: A rows 16-byte aligned (16-byte loads)
+    int vec16b;     // 1: B rows 16-byte aligned
 };
 
 // int8 x int8 -> int32 (exact) with A [M, K] and B [N, K] (K contiguous in
@@ -67,23 +69,52 @@ gemm_tile_s8_kernel(const S8Params p) {
         return static_cast<int32_t>(w);
     };
     constexpr int LW = BM * BKW / kThreads;   // words per thread per operand (4)
+    static_assert(BM == BN && LW == 4, "one 16-byte segment per thread and operand");
+    // Word w of row r sits at [w][swz(r, w)]: bits 2-4 of the row flipped by
+    // w / 4, so the transposing stores of 16-byte row segments (4 threads per
+    // 64-byte row, 8 rows per warp) hit 32 distinct banks while the dp4a loop
+    // still reads four consecutive rows as one 16-byte load.
+    auto swz = [](int r, int w) { return r ^ (4 * ((w >> 2) & 7)); };
+    const int vrow = tid >> 2, vq = tid & 3;  // 16-byte path: row, segment
     int32_t ra[LW], rb[LW];
-    auto load_slice = [&](int k0) {
+    // Words 4q .. 4q + 3 of row `row` (16-byte aligned rows), zero past the ends.
+    auto seg16 = [&](const int8_t* X, int64_t ld, int row, int rows, int k, int32_t (&v)[4]) {
+        if (row < rows && k + 16 <= k_end) {
+            const int4 x = __ldg(reinterpret_cast<const int4*>(X + (int64_t)row * ld + k));
+            v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+        } else {
 #pragma unroll
-        for (int i = 0; i < LW; ++i) {
-            const int e = tid + i * kThreads;
-            const int r = e / BKW, w = e % BKW;
-            ra[i] = word(A, g.lda, m0 + r, g.M, k0 + 4 * w);
-            rb[i] = word(B, g.ldb, n0 + r, g.N, k0 + 4 * w);
+            for (int j = 0; j < 4; ++j) v[j] = word(X, ld, row, rows, k + 4 * j);
+        }
+    };
+    auto load_slice = [&](int k0) {
+        if (p.vec16a) {
+            seg16(A, g.lda, m0 + vrow, g.M, k0 + 16 * vq, ra);
+        } else {
+#pragma unroll
+            for (int i = 0; i < LW; ++i) {
+                const int e = tid + i * kThreads;
+                ra[i] = word(A, g.lda, m0 + e / BKW, g.M, k0 + 4 * (e % BKW));
+            }
+        }
+        if (p.vec16b) {
+            seg16(B, g.ldb, n0 + vrow, g.N, k0 + 16 * vq, rb);
+        } else {
+#pragma unroll
+            for (int i = 0; i < LW; ++i) {
+                const int e = tid + i * kThreads;
+                rb[i] = word(B, g.ldb, n0 + e / BKW, g.N, k0 + 4 * (e % BKW));
+            }
         }
     };
     auto store_slice = [&](int buf) {
 #pragma unroll
         for (int i = 0; i < LW; ++i) {
             const int e = tid + i * kThreads;
-            const int r = e / BKW, w = e % BKW;
-            sA[buf][w][r] = ra[i];
-            sB[buf][w][r] = rb[i];
+            const int ra_r = p.vec16a ? vrow : e / BKW, ra_w = p.vec16a ? 4 * vq + i : e % BKW;
+            const int rb_r = p.vec16b ? vrow : e / BKW, rb_w = p.vec16b ? 4 * vq + i : e % BKW;
+            sA[buf][ra_w][swz(ra_r, ra_w)] = ra[i];
+            sB[buf][rb_w][swz(rb_r, rb_w)] = rb[i];
         }
     };
 
@@ -96,10 +127,10 @@ gemm_tile_s8_kernel(const S8Params p) {
     for (int t = 0; t < nslices; ++t) {
         const int buf = t & 1;
         if (t + 1 < nslices) load_slice(k_begin + (t + 1) * BKB);
-#pragma unroll 4
+#pragma unroll
         for (int w = 0; w < BKW; ++w) {
-            const int4 av = *reinterpret_cast<const int4*>(&sA[buf][w][4 * ty]);
-            const int4 bv = *reinterpret_cast<const int4*>(&sB[buf][w][4 * tx]);
+            const int4 av = *reinterpret_cast<const int4*>(&sA[buf][w][swz(4 * ty, w)]);
+            const int4 bv = *reinterpret_cast<const int4*>(&sB[buf][w][swz(4 * tx, w)]);
             const int a[4] = {av.x, av.y, av.z, av.w};
             const int b[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
@@ -284,6 +315,8 @@ cudaError_t launch_gemm_tile_s8(DotKind kind, const GemmArgs& g, const float* sc
     sp.scales = scales;
     sp.vec = (reinterpret_cast<uintptr_t>(g.A) % 4 == 0 && reinterpret_cast<uintptr_t>(g.B) % 4 == 0 &&
               g.lda % 4 == 0 && g.ldb % 4 == 0) ? 1 : 0;
+    sp.vec16a = (reinterpret_cast<uintptr_t>(g.A) % 16 == 0 && g.lda % 16 == 0) ? 1 : 0;
+    sp.vec16b = (reinterpret_cast<uintptr_t>(g.B) % 16 == 0 && g.ldb % 16 == 0) ? 1 : 0;
     const int64_t tiles = static_cast<int64_t>((g.N + BN - 1) / BN) * ((g.M + BM - 1) / BM);
     int splits = static_cast<int>((2 * static_cast<int64_t>(sms) + tiles - 1) / tiles);
     const int max_by_k = (g.K + 2 * BKB - 1) / (2 * BKB);   // at least two slices per split
