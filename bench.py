@@ -465,6 +465,16 @@ def run_profile(args):
             B = torch.from_numpy(ref_uniform(K * N, 123 + i)).cuda()
             C = torch.zeros(M * N, device="cuda")
             calls.append(lambda A=A, B=B, C=C: dn.cuda_gemm("f32", d, A, B, C, s))
+    elif name in ("conv3d_fp32", "conv3d_int8"):
+        # The bench's Conv3D layer: im2col, the GEMM and the post pass per call.
+        cp = (1, 64, 8, 56, 56, 64, 3, 3, 3, 1, 1, 1, 1, 1, 1)
+        nin, nflt, nout = 8 * 56 * 56 * 64, 64 * 27 * 64, 8 * 56 * 56 * 64
+        cin = torch.from_numpy(ref_uniform(nin, 3)).cuda()
+        cflt = torch.from_numpy(ref_uniform(nflt, 4)).cuda()
+        cbias = torch.from_numpy(ref_uniform(64, 5)).cuda()
+        cout = torch.zeros(nout, device="cuda")
+        prec = 0 if name == "conv3d_fp32" else 2
+        calls.append(lambda: dn.cuda_conv3d(prec, cp, cin, cflt, cbias, cout, dn.POSTOP_RELU, s))
     elif name == "onednn":
         M, N, K = 4096, 1, 4096
         bias = torch.from_numpy(ref_uniform(M, 7)).cuda()
@@ -671,7 +681,8 @@ def main():
     ap.add_argument("--streams", type=int, default=SWEEP_STREAMS,
                     help="streams the 12 independent sweep GEMMs are spread over")
     ap.add_argument("--no-per-config", action="store_true", help="skip the per-config section")
-    ap.add_argument("--profile", choices=["c1", "c2", "c3", "c4", "c5", "onednn", "simt64"],
+    ap.add_argument("--profile", choices=["c1", "c2", "c3", "c4", "c5", "onednn", "simt64",
+                                         "conv3d_fp32", "conv3d_int8"],
                     help="run one config's kernel --reps times for an ncu capture, no bench line")
     ap.add_argument("--reps", type=int, default=3)
     args = ap.parse_args()

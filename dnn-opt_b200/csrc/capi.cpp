@@ -568,14 +568,19 @@ int conv3d_device(int precision, const Conv3dGeom& g, const float* in, const flo
     const size_t col_b = up(static_cast<size_t>(g.M) * g.K * eb);
     const size_t flt_b = precision ? up(static_cast<size_t>(g.OC) * g.K * eb) : 0;
     const size_t acc_b = precision == DNNOPT_CONV3D_INT8 ? up(static_cast<size_t>(g.M) * g.OC * 4) : 0;
+    const int64_t nin = static_cast<int64_t>(g.N) * g.ID * g.IH * g.IW * g.IC;
+    // BF16 / INT8 with whole 16-byte channel chunks: the input is converted
+    // once into the workspace and im2col copies its chunks.
+    const bool copy = precision != DNNOPT_CONV3D_FP32 && conv3d_copy_im2col_ok(g, precision);
+    const size_t in_b = copy ? up(static_cast<size_t>(nin) * eb) : 0;
     Workspace* w = nullptr;
-    int st = ensure_workspace(ctx, s, 0, 0, col_b + flt_b + acc_b, &w);
+    int st = ensure_workspace(ctx, s, 0, 0, col_b + flt_b + acc_b + in_b, &w);
     if (st != DNNOPT_STATUS_SUCCESS) return st;
     char* base = static_cast<char*>(w->quant);
     void* col = base;
     void* fq = base + col_b;
     int32_t* acc = reinterpret_cast<int32_t*>(base + col_b + flt_b);
-    const int64_t nin = static_cast<int64_t>(g.N) * g.ID * g.IH * g.IW * g.IC;
+    void* inq = base + col_b + flt_b + acc_b;
     const int64_t nf = static_cast<int64_t>(g.OC) * g.K;
     cudaError_t e = cudaSuccess;
     if (precision == DNNOPT_CONV3D_INT8) {
@@ -583,7 +588,13 @@ int conv3d_device(int precision, const Conv3dGeom& g, const float* in, const flo
         note_launch(2);
         if (e != cudaSuccess) return cuda_status(e);
     }
-    e = launch_conv3d_im2col(g, precision, in, col, w->scales, s);
+    if (copy) {
+        e = launch_conv3d_filter(precision, in, inq, nin, w->scales, s, 2);
+        note_launch();
+        if (e == cudaSuccess) e = launch_conv3d_im2col_copy(g, precision, inq, col, s);
+    } else {
+        e = launch_conv3d_im2col(g, precision, in, col, w->scales, s);
+    }
     note_launch();
     if (e == cudaSuccess && precision != DNNOPT_CONV3D_FP32) {
         e = launch_conv3d_filter(precision, f, fq, nf, w->scales, s);

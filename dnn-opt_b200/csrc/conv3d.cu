@@ -126,10 +126,79 @@ __global__ void __launch_bounds__(kThreads) im2col3d_kernel(const Conv3dGeom g, 
     }
 }
 
-// Filter [OC, K] in the GEMM precision: BF16 (RNE) or INT8 (times 1/s_f = scales[3]).
+// im2col of an input already converted to the GEMM precision T (BF16 bits or
+// INT8): the same walk as im2col3d_kernel, but every chunk is 16 bytes of one
+// tap's channels (IC a multiple of 16 / sizeof(T)) copied as is, so the
+// conversion runs once per input element instead of once per tap.  The block
+// is sized to a row's chunk count (rounded up to a warp), not a fixed 256, so
+// short INT8 rows (K / 16 chunks) leave few threads idle.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) im2col3d_copy_kernel(const Conv3dGeom g, const T* __restrict__ in,
+                                                                 T* __restrict__ col) {
+    constexpr int V = 16 / static_cast<int>(sizeof(T));
+    __shared__ int s_tap[3 * kConv3dMaxTaps];
+    const int taps = g.KD * g.KH * g.KW;
+    const int nt = static_cast<int>(blockDim.x);   // a multiple of 32, at most kThreads
+    for (int t = threadIdx.x; t < taps; t += nt) {
+        const int kw = t % g.KW, r = t / g.KW;
+        s_tap[3 * t] = r / g.KH;
+        s_tap[3 * t + 1] = r % g.KH;
+        s_tap[3 * t + 2] = kw;
+    }
+    __syncthreads();
+    const int cpr = g.IC / V;
+    const int nchunks = taps * cpr;
+    const int t0 = threadIdx.x / cpr, c0 = threadIdx.x - t0 * cpr;
+    const int dt = nt / cpr, dc = nt - dt * cpr;
+    const int64_t plane = (int64_t)g.IH * g.IW * g.IC;
+    constexpr int R = 4;
+    for (int64_t row0 = (int64_t)blockIdx.x * R; row0 < g.M; row0 += (int64_t)gridDim.x * R) {
+        int od[R], oh[R], ow[R];
+        const T* src[R];
+        bool live[R];
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+            const int64_t row = row0 + q;
+            live[q] = row < g.M;
+            const int64_t rr = live[q] ? row : row0;
+            ow[q] = static_cast<int>(rr % g.OW);
+            int64_t r = rr / g.OW;
+            oh[q] = static_cast<int>(r % g.OH);
+            r /= g.OH;
+            od[q] = static_cast<int>(r % g.OD);
+            src[q] = in + (r / g.OD) * g.ID * plane;
+        }
+        int t = t0, c = c0;
+        for (int j = threadIdx.x; j < nchunks; j += nt) {
+            const int kd = s_tap[3 * t], kh = s_tap[3 * t + 1], kw = s_tap[3 * t + 2];
+            int4 x[R];
+#pragma unroll
+            for (int q = 0; q < R; ++q) {
+                x[q] = make_int4(0, 0, 0, 0);
+                const int id = od[q] * g.sd - g.pd + kd;
+                const int ih = oh[q] * g.sh - g.ph + kh;
+                const int iw = ow[q] * g.sw - g.pw + kw;
+                if (live[q] && id >= 0 && id < g.ID && ih >= 0 && ih < g.IH && iw >= 0 && iw < g.IW)
+                    x[q] = __ldg(reinterpret_cast<const int4*>(src[q] + id * plane +
+                                                               ((int64_t)ih * g.IW + iw) * g.IC + c * V));
+            }
+#pragma unroll
+            for (int q = 0; q < R; ++q)
+                if (live[q])
+                    *reinterpret_cast<int4*>(col + (row0 + q) * g.K + (int64_t)t * g.IC + c * V) = x[q];
+            t += dt;
+            c += dc;
+            if (c >= cpr) { c -= cpr; ++t; }
+        }
+    }
+}
+
+// Filter [OC, K] or input in the GEMM precision: BF16 (RNE) or INT8 (times
+// 1/s = scales[inv_idx]: 3 for the filter, 2 for the input).
 template <int MODE>
-__global__ void conv3d_filter_kernel(const float* __restrict__ f, void* out, int64_t n, const float* scales) {
-    const float inv = MODE == 2 ? scales[3] : 1.0f;
+__global__ void conv3d_filter_kernel(const float* __restrict__ f, void* out, int64_t n, const float* scales,
+                                     int inv_idx) {
+    const float inv = MODE == 2 ? scales[inv_idx] : 1.0f;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         if constexpr (MODE == 1) static_cast<uint16_t*>(out)[i] = f32_to_bf16_bits_ref(f[i]);
         else static_cast<int8_t*>(out)[i] = quant8(f[i], inv);
@@ -151,9 +220,25 @@ __global__ void conv3d_absmax_kernel(const float* __restrict__ in, int64_t nin, 
         m0 = max(m0, __shfl_xor_sync(0xFFFFFFFFu, m0, o));
         m1 = max(m1, __shfl_xor_sync(0xFFFFFFFFu, m1, o));
     }
-    if ((threadIdx.x & 31) == 0) {
-        atomicMax(&bits[0], m0);
-        atomicMax(&bits[1], m1);
+    // One atomic per CTA and value (per-warp atomics on the same two words
+    // serialise in L2).
+    __shared__ uint32_t s_m[2][kThreads / 32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) { s_m[0][warp] = m0; s_m[1][warp] = m1; }
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = static_cast<int>(blockDim.x >> 5);
+        m0 = lane < nw ? s_m[0][lane] : 0u;
+        m1 = lane < nw ? s_m[1][lane] : 0u;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            m0 = max(m0, __shfl_xor_sync(0xFFFFFFFFu, m0, o));
+            m1 = max(m1, __shfl_xor_sync(0xFFFFFFFFu, m1, o));
+        }
+        if (lane == 0) {
+            atomicMax(&bits[0], m0);
+            atomicMax(&bits[1], m1);
+        }
     }
 }
 
@@ -209,10 +294,34 @@ cudaError_t launch_conv3d_im2col(const Conv3dGeom& g, int mode, const float* in,
 }
 
 cudaError_t launch_conv3d_filter(int mode, const float* f, void* out, int64_t n, const float* scales,
-                                 cudaStream_t s) {
-    if (mode == 1) conv3d_filter_kernel<1><<<grid_for(n), kThreads, 0, s>>>(f, out, n, scales);
-    else if (mode == 2) conv3d_filter_kernel<2><<<grid_for(n), kThreads, 0, s>>>(f, out, n, scales);
+                                 cudaStream_t s, int inv_idx) {
+    if (mode == 1) conv3d_filter_kernel<1><<<grid_for(n), kThreads, 0, s>>>(f, out, n, scales, inv_idx);
+    else if (mode == 2) conv3d_filter_kernel<2><<<grid_for(n), kThreads, 0, s>>>(f, out, n, scales, inv_idx);
     else return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
+bool conv3d_copy_im2col_ok(const Conv3dGeom& g, int mode) {
+    const int v = mode == 1 ? 8 : (mode == 2 ? 16 : 0);
+    return v > 0 && g.IC % v == 0 && g.KD * g.KH * g.KW <= kConv3dMaxTaps;
+}
+
+cudaError_t launch_conv3d_im2col_copy(const Conv3dGeom& g, int mode, const void* in_conv, void* col,
+                                      cudaStream_t s) {
+    if (!conv3d_copy_im2col_ok(g, mode) || reinterpret_cast<uintptr_t>(in_conv) % 16 != 0 ||
+        reinterpret_cast<uintptr_t>(col) % 16 != 0)
+        return cudaErrorInvalidValue;
+    const int64_t nchunks = g.K * (mode == 1 ? 2 : 1) / 16;
+    const int threads = static_cast<int>(nchunks >= kThreads ? kThreads : (nchunks + 31) / 32 * 32);
+    const int64_t passes = (g.M + 3) / 4;
+    const int64_t cap = 148LL * 16 * (kThreads / threads);
+    const int grid = static_cast<int>(passes < cap ? passes : cap);
+    if (mode == 1)
+        im2col3d_copy_kernel<uint16_t><<<grid, threads, 0, s>>>(g, static_cast<const uint16_t*>(in_conv),
+                                                                static_cast<uint16_t*>(col));
+    else
+        im2col3d_copy_kernel<int8_t><<<grid, threads, 0, s>>>(g, static_cast<const int8_t*>(in_conv),
+                                                              static_cast<int8_t*>(col));
     return cudaGetLastError();
 }
 
@@ -220,7 +329,9 @@ cudaError_t launch_conv3d_scales(const float* in, int64_t nin, const float* f, i
                                  float* scales, cudaStream_t s) {
     cudaError_t e = cudaMemsetAsync(bits, 0, 2 * sizeof(uint32_t), s);
     if (e != cudaSuccess) return e;
-    conv3d_absmax_kernel<<<grid_for(nin + nf), kThreads, 0, s>>>(in, nin, f, nf, bits);
+    const int64_t blocks = (nin + nf + 4 * kThreads - 1) / (4 * kThreads);
+    const int grid = static_cast<int>(blocks < 148 * 4 ? (blocks > 0 ? blocks : 1) : 148 * 4);
+    conv3d_absmax_kernel<<<grid, kThreads, 0, s>>>(in, nin, f, nf, bits);
     conv3d_scales_kernel<<<1, 32, 0, s>>>(bits, scales);
     return cudaGetLastError();
 }

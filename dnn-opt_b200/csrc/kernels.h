@@ -134,9 +134,16 @@ struct Conv3dGeom {
 // mode 0: FP32 columns, 1: BF16 (RNE), 2: INT8 quantised with 1/scales[2].
 cudaError_t launch_conv3d_im2col(const Conv3dGeom& g, int mode, const float* in, void* col,
                                  const float* scales, cudaStream_t s);
-// Filter to BF16 (mode 1) or INT8 with 1/scales[3] (mode 2).
+// Filter (or input) to BF16 (mode 1) or INT8 with 1/scales[inv_idx] (mode 2;
+// 3 for the filter, 2 for the input).
 cudaError_t launch_conv3d_filter(int mode, const float* f, void* out, int64_t n, const float* scales,
-                                 cudaStream_t s);
+                                 cudaStream_t s, int inv_idx = 3);
+// im2col of an input already in the GEMM precision (mode 1: BF16 bits, 2:
+// INT8), 16-byte channel chunks copied as is; needs IC % (16 / element size)
+// == 0 (conv3d_copy_im2col_ok) and 16-byte aligned buffers.
+bool conv3d_copy_im2col_ok(const Conv3dGeom& g, int mode);
+cudaError_t launch_conv3d_im2col_copy(const Conv3dGeom& g, int mode, const void* in_conv, void* col,
+                                      cudaStream_t s);
 // scales[0..3] = s_in, s_f, 1/s_in, 1/s_f from the per-tensor absmax (bits: 2 words).
 cudaError_t launch_conv3d_scales(const float* in, int64_t nin, const float* f, int64_t nf, uint32_t* bits,
                                  float* scales, cudaStream_t s);

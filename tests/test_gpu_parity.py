@@ -324,8 +324,12 @@ def test_fp32_simt_small_m_bands(gpu, dn, orc, M, N, K, beta, ta, tb):
 # ----------------------------------------------------------------- Conv3D ---
 def _conv3d_shapes():
     from tests.test_oracle_conv3d import CONV3D_SHAPES
-    # + a shape whose BF16 GEMM takes the tcgen05 kernel (K = 432, OC = 64, M = 1024)
-    return CONV3D_SHAPES + [(1, 16, 4, 16, 16, 64, 3, 3, 3, 1, 1, 1, 1, 1, 1)]
+    # + a shape whose BF16 GEMM takes the tcgen05 kernel (K = 432, OC = 64, M = 1024),
+    # + batch / stride / uneven padding with IC a multiple of 16 (the convert-once
+    # input and 16-byte chunk im2col of the BF16 and INT8 paths)
+    return CONV3D_SHAPES + [(1, 16, 4, 16, 16, 64, 3, 3, 3, 1, 1, 1, 1, 1, 1),
+                            (2, 32, 4, 9, 9, 24, 3, 3, 3, 2, 2, 2, 1, 1, 1),
+                            (1, 48, 3, 7, 7, 16, 1, 3, 3, 1, 1, 1, 0, 1, 1)]
 
 
 @pytest.mark.parametrize("p", _conv3d_shapes())
