@@ -563,6 +563,17 @@ int conv3d_geom(int precision, const dnnopt_conv3d_params* p, int post_op, Conv3
 // INT32, filter as the N x K operand), then bias, dequantisation and post-op.
 int conv3d_device(int precision, const Conv3dGeom& g, const float* in, const float* f, const float* bias,
                   float* out, int op, DeviceContext* ctx, cudaStream_t s) {
+    // FP32 with IC % 4 == 0: one implicit-GEMM launch that gathers the column
+    // matrix tile by tile from the input (no M x K scratch), then the post pass.
+    if (precision == DNNOPT_CONV3D_FP32 && gemm_simt_conv_ok(g, in, f)) {
+        cudaError_t e = launch_gemm_simt_conv(g, in, f, out, ctx->num_sms, s);
+        note_launch();
+        if (e == cudaSuccess && (bias || op != DNNOPT_POSTOP_NONE)) {
+            e = launch_conv3d_post(out, nullptr, nullptr, bias, g.M, g.OC, op, s);
+            note_launch();
+        }
+        return cuda_status(e);
+    }
     const size_t eb = precision == DNNOPT_CONV3D_FP32 ? 4 : (precision == DNNOPT_CONV3D_BF16 ? 2 : 1);
     auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
     const size_t col_b = up(static_cast<size_t>(g.M) * g.K * eb);

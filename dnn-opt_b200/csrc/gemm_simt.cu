@@ -48,6 +48,10 @@ struct SimtParams {
     int kchunk;     // K rows per split (multiple of BK)
     int vec_a;      // 1: A's rows start on 4-element boundaries (4-wide loads when not transposed)
     int vec_b;      // 1: B's rows start on 4-element boundaries (4-wide loads in either layout)
+    // Implicit im2col (CONV kernels only): A[m][k] is the NDHWC input at
+    // output position m, tap k / IC, channel k % IC, zero in the padding.
+    Conv3dGeom conv;
+    const float* conv_in;
 };
 
 template <int BM, int BN>
@@ -73,7 +77,7 @@ __device__ __forceinline__ void load_krow4(const typename Elem<I>::T* X, int64_t
     }
 }
 
-template <In IA, In IB, int BM, int BN>
+template <In IA, In IB, int BM, int BN, bool CONV = false>
 __global__ void __launch_bounds__(kThreads, 2)
 gemm_simt_kernel(const SimtParams p) {
     using TA = typename Elem<IA>::T;
@@ -127,9 +131,68 @@ gemm_simt_kernel(const SimtParams p) {
     const bool vec_a = BM >= 32 && !g.a_trans && p.vec_a;
     const bool vec_bt = g.b_trans && p.vec_b;
     const bool vec_bn = !g.b_trans && p.vec_b;
+    // CONV: the tile's output positions (id0, ih0, iw0, batch or -1) and the
+    // tap table (kd << 20 | kh << 10 | kw) decoded once, behind the stage buffers.
+    const int4* s_rows = nullptr;
+    const int* s_tap = nullptr;
+    if constexpr (CONV) {
+        int4* rows = reinterpret_cast<int4*>(smem + 2 * SA + 2 * SB);
+        int* tab = reinterpret_cast<int*>(rows + BM);
+        const Conv3dGeom& cg = p.conv;
+        for (int r = tid; r < BM; r += kThreads) {
+            const int64_t m = static_cast<int64_t>(m0) + r;
+            int4 v = make_int4(0, 0, 0, -1);
+            if (m < g.M) {
+                const int ow = static_cast<int>(m % cg.OW);
+                int64_t t = m / cg.OW;
+                const int oh = static_cast<int>(t % cg.OH);
+                t /= cg.OH;
+                const int od = static_cast<int>(t % cg.OD);
+                v = make_int4(od * cg.sd - cg.pd, oh * cg.sh - cg.ph, ow * cg.sw - cg.pw, static_cast<int>(t / cg.OD));
+            }
+            rows[r] = v;
+        }
+        const int taps = cg.KD * cg.KH * cg.KW;
+        for (int t = tid; t < taps; t += kThreads) {
+            const int kw = t % cg.KW, r2 = t / cg.KW;
+            tab[t] = ((r2 / cg.KH) << 20) | ((r2 % cg.KH) << 10) | kw;
+        }
+        __syncthreads();
+        s_rows = rows;
+        s_tap = tab;
+    }
     float ra[LA], rb[LB];
     auto load_slice = [&](int k0) {
-        if constexpr (BM >= 32) {
+        if constexpr (CONV) {
+            // k (a multiple of 4) is the same for all of a thread's rows; the
+            // four channels of a float4 belong to one tap as IC % 4 == 0.
+            const Conv3dGeom& cg = p.conv;
+            int m, k;
+            kvec_coord(tid, m, k);
+            const int gk = k0 + k;
+            const bool kin = gk < k_end;
+            int kd = 0, kh = 0, kw = 0, c = 0;
+            if (kin) {
+                const int tap = gk / cg.IC;
+                c = gk - tap * cg.IC;
+                const int pk = s_tap[tap];
+                kd = pk >> 20;
+                kh = (pk >> 10) & 1023;
+                kw = pk & 1023;
+            }
+#pragma unroll
+            for (int i = 0; i < LA / 4; ++i) {
+                int mi, ki;
+                kvec_coord(tid + i * kThreads, mi, ki);
+                const int4 ri = s_rows[mi];
+                const int id = ri.x + kd, ih = ri.y + kh, iw = ri.z + kw;
+                float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (kin && ri.w >= 0 && id >= 0 && id < cg.ID && ih >= 0 && ih < cg.IH && iw >= 0 && iw < cg.IW)
+                    v = __ldg(reinterpret_cast<const float4*>(
+                        p.conv_in + (((static_cast<int64_t>(ri.w) * cg.ID + id) * cg.IH + ih) * cg.IW + iw) * cg.IC + c));
+                ra[4 * i] = v.x; ra[4 * i + 1] = v.y; ra[4 * i + 2] = v.z; ra[4 * i + 3] = v.w;
+            }
+        } else if constexpr (BM >= 32) {
             if (vec_a) {
 #pragma unroll
                 for (int i = 0; i < LA / 4; ++i) {
@@ -142,7 +205,7 @@ gemm_simt_kernel(const SimtParams p) {
                 }
             }
         }
-        if (!vec_a) {
+        if (!CONV && !vec_a) {
 #pragma unroll
             for (int i = 0; i < LA; ++i) {
                 int m, k;
@@ -364,6 +427,14 @@ const void* simt_select(In ia, In ib, int bm, int bn) {
     return nullptr;
 }
 
+// Implicit-im2col FP32 kernels (conv3d): the tile shapes the plan picks for M >= 64.
+const void* simt_conv_select(int bm, int bn) {
+    if (bm == 64 && bn == 64) return reinterpret_cast<const void*>(&gemm_simt_kernel<In::F32, In::F32, 64, 64, true>);
+    if (bm == 128 && bn == 64) return reinterpret_cast<const void*>(&gemm_simt_kernel<In::F32, In::F32, 128, 64, true>);
+    if (bm == 64 && bn == 128) return reinterpret_cast<const void*>(&gemm_simt_kernel<In::F32, In::F32, 64, 128, true>);
+    return nullptr;
+}
+
 size_t smem_for(int bm, int bn) {
     if (bn == 64)
         return bm == 16 ? simt_smem_bytes<16, 64>()
@@ -419,20 +490,10 @@ GemmSimtPlan gemm_simt_plan(const GemmArgs& g, int num_sms) {
     return p;
 }
 
-cudaError_t launch_gemm_simt(In ia, In ib, const GemmArgs& g, const GemmSimtPlan& plan,
-                             cudaStream_t s) {
-    const void* fn = simt_select(ia, ib, plan.bm, plan.bn);
-    if (!fn || plan.splits < 1 || plan.splits > kMaxSplits || plan.kchunk < BK) return cudaErrorInvalidValue;
-    const size_t smem = smem_for(plan.bm, plan.bn);
-    cudaError_t e = prepare(fn, smem);
-    if (e != cudaSuccess) return e;
-    SimtParams sp;
-    sp.g = g;
-    sp.kchunk = plan.kchunk;
-    const size_t eb = elem_size(ib);
-    sp.vec_b = (reinterpret_cast<uintptr_t>(g.B) % (4 * eb) == 0 && g.ldb % 4 == 0) ? 1 : 0;
-    const size_t ea = elem_size(ia);
-    sp.vec_a = (reinterpret_cast<uintptr_t>(g.A) % (4 * ea) == 0 && g.lda % 4 == 0) ? 1 : 0;
+namespace {
+
+cudaError_t launch_simt(const void* fn, SimtParams& sp, const GemmSimtPlan& plan, size_t smem, cudaStream_t s) {
+    const GemmArgs& g = sp.g;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>((g.N + plan.bn - 1) / plan.bn), static_cast<unsigned>((g.M + plan.bm - 1) / plan.bm),
                        static_cast<unsigned>(plan.splits));
@@ -454,6 +515,64 @@ cudaError_t launch_gemm_simt(In ia, In ib, const GemmArgs& g, const GemmSimtPlan
     cfg.numAttrs = na;
     void* args[] = {&sp};
     return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+}  // namespace
+
+cudaError_t launch_gemm_simt(In ia, In ib, const GemmArgs& g, const GemmSimtPlan& plan,
+                             cudaStream_t s) {
+    const void* fn = simt_select(ia, ib, plan.bm, plan.bn);
+    if (!fn || plan.splits < 1 || plan.splits > kMaxSplits || plan.kchunk < BK) return cudaErrorInvalidValue;
+    const size_t smem = smem_for(plan.bm, plan.bn);
+    cudaError_t e = prepare(fn, smem);
+    if (e != cudaSuccess) return e;
+    SimtParams sp = {};
+    sp.g = g;
+    sp.kchunk = plan.kchunk;
+    const size_t eb = elem_size(ib);
+    sp.vec_b = (reinterpret_cast<uintptr_t>(g.B) % (4 * eb) == 0 && g.ldb % 4 == 0) ? 1 : 0;
+    const size_t ea = elem_size(ia);
+    sp.vec_a = (reinterpret_cast<uintptr_t>(g.A) % (4 * ea) == 0 && g.lda % 4 == 0) ? 1 : 0;
+    return launch_simt(fn, sp, plan, smem, s);
+}
+
+bool gemm_simt_conv_ok(const Conv3dGeom& cg, const float* in, const float* filter) {
+    return cg.IC % 4 == 0 && cg.M >= 64 && cg.M <= INT32_MAX && cg.K <= INT32_MAX &&
+           cg.KD * cg.KH * cg.KW <= kConv3dMaxTaps && cg.KD < 1024 && cg.KH < 1024 && cg.KW < 1024 &&
+           reinterpret_cast<uintptr_t>(in) % 16 == 0 && reinterpret_cast<uintptr_t>(filter) % 16 == 0;
+}
+
+cudaError_t launch_gemm_simt_conv(const Conv3dGeom& cg, const float* in, const float* filter, float* out,
+                                  int num_sms, cudaStream_t s) {
+    if (!gemm_simt_conv_ok(cg, in, filter)) return cudaErrorInvalidValue;
+    GemmArgs g;
+    g.M = static_cast<int>(cg.M);
+    g.N = cg.OC;
+    g.K = static_cast<int>(cg.K);
+    g.alpha = 1.0f;
+    g.beta = 0.0f;
+    g.A = in;                 // not read: the CONV kernel gathers from conv_in
+    g.lda = cg.K;
+    g.a_trans = 0;
+    g.B = filter;             // [OC, K]
+    g.ldb = cg.K;
+    g.b_trans = 1;
+    g.C = out;                // [M, OC]
+    g.ldc = cg.OC;
+    const GemmSimtPlan plan = gemm_simt_plan(g, num_sms);
+    const void* fn = simt_conv_select(plan.bm, plan.bn);
+    if (!fn || plan.splits < 1 || plan.splits > kMaxSplits || plan.kchunk < BK) return cudaErrorInvalidValue;
+    const size_t base = smem_for(plan.bm, plan.bn) + static_cast<size_t>(plan.bm) * sizeof(int4);
+    cudaError_t e = prepare(fn, base + kConv3dMaxTaps * sizeof(int));
+    if (e != cudaSuccess) return e;
+    SimtParams sp = {};
+    sp.g = g;
+    sp.kchunk = plan.kchunk;
+    sp.vec_a = 1;
+    sp.vec_b = 1;
+    sp.conv = cg;
+    sp.conv_in = in;
+    return launch_simt(fn, sp, plan, base + static_cast<size_t>(cg.KD * cg.KH * cg.KW) * sizeof(int), s);
 }
 
 }  // namespace dnnopt_b200

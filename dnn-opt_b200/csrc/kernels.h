@@ -147,6 +147,13 @@ cudaError_t launch_conv3d_im2col_copy(const Conv3dGeom& g, int mode, const void*
 // scales[0..3] = s_in, s_f, 1/s_in, 1/s_f from the per-tensor absmax (bits: 2 words).
 cudaError_t launch_conv3d_scales(const float* in, int64_t nin, const float* f, int64_t nf, uint32_t* bits,
                                  float* scales, cudaStream_t s);
+// FP32 conv3d as one implicit-GEMM launch of the SIMT kernel (gemm_simt.cu):
+// out[M, OC] = im2col(in) x filter^T with the column matrix gathered tile by
+// tile from the NDHWC input (never materialised).  Needs IC % 4 == 0, M >= 64,
+// 16-byte aligned input and filter, at most kConv3dMaxTaps taps.
+bool gemm_simt_conv_ok(const Conv3dGeom& g, const float* in, const float* filter);
+cudaError_t launch_gemm_simt_conv(const Conv3dGeom& g, const float* in, const float* filter, float* out,
+                                  int num_sms, cudaStream_t s);
 // out = post_op(v + bias[oc]); v = out, or float(acc) * (scales[0] * scales[1]) when acc.
 cudaError_t launch_conv3d_post(float* out, const int32_t* acc, const float* scales, const float* bias,
                                int64_t M, int OC, int op, cudaStream_t s);
