@@ -576,7 +576,11 @@ int conv3d_device(int precision, const Conv3dGeom& g, const float* in, const flo
     }
     const size_t eb = precision == DNNOPT_CONV3D_FP32 ? 4 : (precision == DNNOPT_CONV3D_BF16 ? 2 : 1);
     auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
-    const size_t col_b = up(static_cast<size_t>(g.M) * g.K * eb);
+    // INT8 with IC % 16 == 0 and M >= 64: the dp4a kernel gathers 16-byte
+    // channel segments from the quantised input, so no column matrix (the
+    // workspace buffers are 256-byte aligned, so only the geometry decides).
+    const bool implicit8 = precision == DNNOPT_CONV3D_INT8 && gemm_tile_s8_conv_ok(g, nullptr, nullptr);
+    const size_t col_b = implicit8 ? 0 : up(static_cast<size_t>(g.M) * g.K * eb);
     const size_t flt_b = precision ? up(static_cast<size_t>(g.OC) * g.K * eb) : 0;
     const size_t acc_b = precision == DNNOPT_CONV3D_INT8 ? up(static_cast<size_t>(g.M) * g.OC * 4) : 0;
     const int64_t nin = static_cast<int64_t>(g.N) * g.ID * g.IH * g.IW * g.IC;
@@ -602,16 +606,25 @@ int conv3d_device(int precision, const Conv3dGeom& g, const float* in, const flo
     if (copy) {
         e = launch_conv3d_filter(precision, in, inq, nin, w->scales, s, 2);
         note_launch();
-        if (e == cudaSuccess) e = launch_conv3d_im2col_copy(g, precision, inq, col, s);
+        if (e == cudaSuccess && !implicit8) e = launch_conv3d_im2col_copy(g, precision, inq, col, s);
     } else {
         e = launch_conv3d_im2col(g, precision, in, col, w->scales, s);
     }
-    note_launch();
+    if (!implicit8) note_launch();
     if (e == cudaSuccess && precision != DNNOPT_CONV3D_FP32) {
         e = launch_conv3d_filter(precision, f, fq, nf, w->scales, s);
         note_launch();
     }
     if (e != cudaSuccess) return cuda_status(e);
+    if (implicit8) {
+        e = launch_gemm_tile_s8_conv(g, static_cast<const int8_t*>(inq), static_cast<const int8_t*>(fq), acc, s);
+        note_launch();
+        if (e == cudaSuccess) {
+            e = launch_conv3d_post(out, acc, w->scales, bias, g.M, g.OC, op, s);
+            note_launch();
+        }
+        return cuda_status(e);
+    }
     GemmArgs ga;
     ga.M = static_cast<int>(g.M); ga.N = g.OC; ga.K = static_cast<int>(g.K);
     ga.alpha = 1.0f; ga.beta = 0.0f;

@@ -29,6 +29,10 @@ struct S8Params {
     int vec;        // 1: A and B rows 4-byte aligned (word loads)
     int vec16a;     // 1: A rows 16-byte aligned (16-byte loads)
     int vec16b;     // 1: B rows 16-byte aligned
+    // Implicit im2col (CONV kernels only): A[m][k] is the quantised NDHWC
+    // input at output position m, tap k / IC, channel k % IC, zero in the padding.
+    Conv3dGeom conv;
+    const int8_t* conv_in;
 };
 
 // int8 x int8 -> int32 (exact) with A [M, K] and B [N, K] (K contiguous in
@@ -37,7 +41,7 @@ struct S8Params {
 // words loaded before the current slice's dp4a), K split over up to 8 CTAs of
 // a cluster when the tiles alone leave SMs idle (int32 partials summed
 // through distributed shared memory: exact, so the order does not matter).
-template <bool DQ>
+template <bool DQ, bool CONV = false>
 __global__ void __launch_bounds__(kThreads)
 gemm_tile_s8_kernel(const S8Params p) {
     // One array carved into the two operands' buffers, so that the split-K
@@ -87,8 +91,46 @@ gemm_tile_s8_kernel(const S8Params p) {
             for (int j = 0; j < 4; ++j) v[j] = word(X, ld, row, rows, k + 4 * j);
         }
     };
+    // CONV: this thread's output position (id0, ih0, iw0, batch or -1) and the
+    // tap table (kd << 20 | kh << 10 | kw), decoded once.
+    __shared__ int s_tap[CONV ? kConv3dMaxTaps : 1];
+    int4 crow = make_int4(0, 0, 0, -1);
+    if constexpr (CONV) {
+        const Conv3dGeom& cg = p.conv;
+        const int taps = cg.KD * cg.KH * cg.KW;
+        for (int t = tid; t < taps; t += kThreads) {
+            const int kw = t % cg.KW, r2 = t / cg.KW;
+            s_tap[t] = ((r2 / cg.KH) << 20) | ((r2 % cg.KH) << 10) | kw;
+        }
+        const int64_t m = static_cast<int64_t>(m0) + vrow;
+        if (m < g.M) {
+            const int ow = static_cast<int>(m % cg.OW);
+            int64_t t = m / cg.OW;
+            const int oh = static_cast<int>(t % cg.OH);
+            t /= cg.OH;
+            const int od = static_cast<int>(t % cg.OD);
+            crow = make_int4(od * cg.sd - cg.pd, oh * cg.sh - cg.ph, ow * cg.sw - cg.pw, static_cast<int>(t / cg.OD));
+        }
+        __syncthreads();
+    }
     auto load_slice = [&](int k0) {
-        if (p.vec16a) {
+        if constexpr (CONV) {
+            // 16 channels of one tap (IC % 16 == 0, so K % 16 == 0 and a
+            // segment that starts below k_end ends within it).
+            const Conv3dGeom& cg = p.conv;
+            const int k = k0 + 16 * vq;
+            ra[0] = ra[1] = ra[2] = ra[3] = 0;
+            if (k < k_end && crow.w >= 0) {
+                const int tap = k / cg.IC, c = k - tap * cg.IC;
+                const int pk = s_tap[tap];
+                const int id = crow.x + (pk >> 20), ih = crow.y + ((pk >> 10) & 1023), iw = crow.z + (pk & 1023);
+                if (id >= 0 && id < cg.ID && ih >= 0 && ih < cg.IH && iw >= 0 && iw < cg.IW) {
+                    const int4 x = __ldg(reinterpret_cast<const int4*>(
+                        p.conv_in + (((static_cast<int64_t>(crow.w) * cg.ID + id) * cg.IH + ih) * cg.IW + iw) * cg.IC + c));
+                    ra[0] = x.x; ra[1] = x.y; ra[2] = x.z; ra[3] = x.w;
+                }
+            }
+        } else if (p.vec16a) {
             seg16(A, g.lda, m0 + vrow, g.M, k0 + 16 * vq, ra);
         } else {
 #pragma unroll
@@ -303,20 +345,14 @@ __global__ void quantize_ref_fp8_kernel(const GemmArgs g, uint8_t* qa, uint8_t* 
 
 }  // namespace
 
-cudaError_t launch_gemm_tile_s8(DotKind kind, const GemmArgs& g, const float* scales,
-                                cudaStream_t s) {
-    if (kind != DotKind::S8S32 && kind != DotKind::S8DQ) return cudaErrorInvalidValue;
+namespace {
+
+cudaError_t launch_s8(const void* fn, S8Params& sp, cudaStream_t s) {
+    const GemmArgs& g = sp.g;
     int dev = 0, sms = 148;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) sms = 148;
-    S8Params sp;
-    sp.g = g;
-    sp.scales = scales;
-    sp.vec = (reinterpret_cast<uintptr_t>(g.A) % 4 == 0 && reinterpret_cast<uintptr_t>(g.B) % 4 == 0 &&
-              g.lda % 4 == 0 && g.ldb % 4 == 0) ? 1 : 0;
-    sp.vec16a = (reinterpret_cast<uintptr_t>(g.A) % 16 == 0 && g.lda % 16 == 0) ? 1 : 0;
-    sp.vec16b = (reinterpret_cast<uintptr_t>(g.B) % 16 == 0 && g.ldb % 16 == 0) ? 1 : 0;
     const int64_t tiles = static_cast<int64_t>((g.N + BN - 1) / BN) * ((g.M + BM - 1) / BM);
     int splits = static_cast<int>((2 * static_cast<int64_t>(sms) + tiles - 1) / tiles);
     const int max_by_k = (g.K + 2 * BKB - 1) / (2 * BKB);   // at least two slices per split
@@ -348,9 +384,57 @@ cudaError_t launch_gemm_tile_s8(DotKind kind, const GemmArgs& g, const float* sc
     cfg.attrs = attr;
     cfg.numAttrs = na;
     void* args[] = {&sp};
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+}  // namespace
+
+cudaError_t launch_gemm_tile_s8(DotKind kind, const GemmArgs& g, const float* scales,
+                                cudaStream_t s) {
+    if (kind != DotKind::S8S32 && kind != DotKind::S8DQ) return cudaErrorInvalidValue;
+    S8Params sp = {};
+    sp.g = g;
+    sp.scales = scales;
+    sp.vec = (reinterpret_cast<uintptr_t>(g.A) % 4 == 0 && reinterpret_cast<uintptr_t>(g.B) % 4 == 0 &&
+              g.lda % 4 == 0 && g.ldb % 4 == 0) ? 1 : 0;
+    sp.vec16a = (reinterpret_cast<uintptr_t>(g.A) % 16 == 0 && g.lda % 16 == 0) ? 1 : 0;
+    sp.vec16b = (reinterpret_cast<uintptr_t>(g.B) % 16 == 0 && g.ldb % 16 == 0) ? 1 : 0;
     const void* fn = kind == DotKind::S8S32 ? reinterpret_cast<const void*>(&gemm_tile_s8_kernel<false>)
                                             : reinterpret_cast<const void*>(&gemm_tile_s8_kernel<true>);
-    return cudaLaunchKernelExC(&cfg, fn, args);
+    return launch_s8(fn, sp, s);
+}
+
+bool gemm_tile_s8_conv_ok(const Conv3dGeom& cg, const int8_t* in_q, const int8_t* filter_q) {
+    return cg.IC % 16 == 0 && cg.M >= 64 && cg.M <= INT32_MAX && cg.K <= INT32_MAX &&
+           cg.KD * cg.KH * cg.KW <= kConv3dMaxTaps && cg.KD < 1024 && cg.KH < 1024 && cg.KW < 1024 &&
+           reinterpret_cast<uintptr_t>(in_q) % 16 == 0 && reinterpret_cast<uintptr_t>(filter_q) % 16 == 0;
+}
+
+cudaError_t launch_gemm_tile_s8_conv(const Conv3dGeom& cg, const int8_t* in_q, const int8_t* filter_q,
+                                     int32_t* acc, cudaStream_t s) {
+    if (!gemm_tile_s8_conv_ok(cg, in_q, filter_q)) return cudaErrorInvalidValue;
+    S8Params sp = {};
+    GemmArgs& g = sp.g;
+    g.M = static_cast<int>(cg.M);
+    g.N = cg.OC;
+    g.K = static_cast<int>(cg.K);
+    g.alpha = 1.0f;
+    g.beta = 0.0f;
+    g.A = in_q;               // not read: the CONV kernel gathers from conv_in
+    g.lda = cg.K;
+    g.a_trans = 0;
+    g.B = filter_q;           // [OC, K]
+    g.ldb = cg.K;
+    g.b_trans = 1;
+    g.C = acc;                // [M, OC] int32
+    g.ldc = cg.OC;
+    sp.scales = nullptr;
+    sp.vec = 1;
+    sp.vec16a = 1;            // store mapping of 16-byte row segments
+    sp.vec16b = 1;
+    sp.conv = cg;
+    sp.conv_in = in_q;
+    return launch_s8(reinterpret_cast<const void*>(&gemm_tile_s8_kernel<false, true>), sp, s);
 }
 
 cudaError_t launch_absmax2(const GemmArgs& g, uint32_t* absmax_bits, cudaStream_t s) {
