@@ -564,14 +564,11 @@ int conv3d_geom(int precision, const dnnopt_conv3d_params* p, int post_op, Conv3
 int conv3d_device(int precision, const Conv3dGeom& g, const float* in, const float* f, const float* bias,
                   float* out, int op, DeviceContext* ctx, cudaStream_t s) {
     // FP32 with IC % 4 == 0: one implicit-GEMM launch that gathers the column
-    // matrix tile by tile from the input (no M x K scratch), then the post pass.
+    // matrix tile by tile from the input (no M x K scratch), bias and post-op
+    // in its epilogue.
     if (precision == DNNOPT_CONV3D_FP32 && gemm_simt_conv_ok(g, in, f)) {
-        cudaError_t e = launch_gemm_simt_conv(g, in, f, out, ctx->num_sms, s);
+        const cudaError_t e = launch_gemm_simt_conv(g, in, f, bias, op, out, ctx->num_sms, s);
         note_launch();
-        if (e == cudaSuccess && (bias || op != DNNOPT_POSTOP_NONE)) {
-            e = launch_conv3d_post(out, nullptr, nullptr, bias, g.M, g.OC, op, s);
-            note_launch();
-        }
         return cuda_status(e);
     }
     const size_t eb = precision == DNNOPT_CONV3D_FP32 ? 4 : (precision == DNNOPT_CONV3D_BF16 ? 2 : 1);
@@ -582,7 +579,7 @@ int conv3d_device(int precision, const Conv3dGeom& g, const float* in, const flo
     const bool implicit8 = precision == DNNOPT_CONV3D_INT8 && gemm_tile_s8_conv_ok(g, nullptr, nullptr);
     const size_t col_b = implicit8 ? 0 : up(static_cast<size_t>(g.M) * g.K * eb);
     const size_t flt_b = precision ? up(static_cast<size_t>(g.OC) * g.K * eb) : 0;
-    const size_t acc_b = precision == DNNOPT_CONV3D_INT8 ? up(static_cast<size_t>(g.M) * g.OC * 4) : 0;
+    const size_t acc_b = precision == DNNOPT_CONV3D_INT8 && !implicit8 ? up(static_cast<size_t>(g.M) * g.OC * 4) : 0;
     const int64_t nin = static_cast<int64_t>(g.N) * g.ID * g.IH * g.IW * g.IC;
     // BF16 / INT8 with whole 16-byte channel chunks: the input is converted
     // once into the workspace and im2col copies its chunks.
@@ -616,13 +613,10 @@ int conv3d_device(int precision, const Conv3dGeom& g, const float* in, const flo
         note_launch();
     }
     if (e != cudaSuccess) return cuda_status(e);
-    if (implicit8) {
-        e = launch_gemm_tile_s8_conv(g, static_cast<const int8_t*>(inq), static_cast<const int8_t*>(fq), acc, s);
+    if (implicit8) {   // dequantisation, bias and post-op in the GEMM's epilogue
+        e = launch_gemm_tile_s8_conv(g, static_cast<const int8_t*>(inq), static_cast<const int8_t*>(fq), w->scales,
+                                     bias, op, out, s);
         note_launch();
-        if (e == cudaSuccess) {
-            e = launch_conv3d_post(out, acc, w->scales, bias, g.M, g.OC, op, s);
-            note_launch();
-        }
         return cuda_status(e);
     }
     GemmArgs ga;

@@ -52,6 +52,7 @@ struct SimtParams {
     // output position m, tap k / IC, channel k % IC, zero in the padding.
     Conv3dGeom conv;
     const float* conv_in;
+    int conv_op;    // post-op after the bias: 0 none, 1 relu, 2 relu6
 };
 
 template <int BM, int BN>
@@ -356,7 +357,12 @@ gemm_simt_kernel(const SimtParams p) {
     float* C = static_cast<float*>(g.C);
     auto finish = [&](int gm, int gn, float sum) {
         float* cp = C + (int64_t)gm * g.ldc + gn;
-        *cp = add_bias((g.beta == 0.0f) ? g.alpha * sum : fmaf(g.alpha, sum, g.beta * *cp), g.bias, gn);
+        float v = add_bias((g.beta == 0.0f) ? g.alpha * sum : fmaf(g.alpha, sum, g.beta * *cp), g.bias, gn);
+        if constexpr (CONV) {
+            if (p.conv_op == 1) v = v > 0.0f ? v : 0.0f;
+            else if (p.conv_op == 2) v = v > 0.0f ? (v < 6.0f ? v : 6.0f) : 0.0f;
+        }
+        *cp = v;
     };
     if (gridDim.z == 1) {
 #pragma unroll
@@ -542,8 +548,8 @@ bool gemm_simt_conv_ok(const Conv3dGeom& cg, const float* in, const float* filte
            reinterpret_cast<uintptr_t>(in) % 16 == 0 && reinterpret_cast<uintptr_t>(filter) % 16 == 0;
 }
 
-cudaError_t launch_gemm_simt_conv(const Conv3dGeom& cg, const float* in, const float* filter, float* out,
-                                  int num_sms, cudaStream_t s) {
+cudaError_t launch_gemm_simt_conv(const Conv3dGeom& cg, const float* in, const float* filter, const float* bias,
+                                  int op, float* out, int num_sms, cudaStream_t s) {
     if (!gemm_simt_conv_ok(cg, in, filter)) return cudaErrorInvalidValue;
     GemmArgs g;
     g.M = static_cast<int>(cg.M);
@@ -559,6 +565,7 @@ cudaError_t launch_gemm_simt_conv(const Conv3dGeom& cg, const float* in, const f
     g.b_trans = 1;
     g.C = out;                // [M, OC]
     g.ldc = cg.OC;
+    g.bias = bias;            // per output channel, then the post-op, in the epilogue
     const GemmSimtPlan plan = gemm_simt_plan(g, num_sms);
     const void* fn = simt_conv_select(plan.bm, plan.bn);
     if (!fn || plan.splits < 1 || plan.splits > kMaxSplits || plan.kchunk < BK) return cudaErrorInvalidValue;
@@ -572,6 +579,7 @@ cudaError_t launch_gemm_simt_conv(const Conv3dGeom& cg, const float* in, const f
     sp.vec_b = 1;
     sp.conv = cg;
     sp.conv_in = in;
+    sp.conv_op = op;
     return launch_simt(fn, sp, plan, base + static_cast<size_t>(cg.KD * cg.KH * cg.KW) * sizeof(int), s);
 }
 

@@ -33,6 +33,8 @@ struct S8Params {
     // input at output position m, tap k / IC, channel k % IC, zero in the padding.
     Conv3dGeom conv;
     const int8_t* conv_in;
+    const float* conv_bias;   // CONV epilogue: float(acc) * (s_in * s_f) [+ bias] [relu / relu6]
+    int conv_op;
 };
 
 // int8 x int8 -> int32 (exact) with A [M, K] and B [N, K] (K contiguous in
@@ -190,6 +192,12 @@ gemm_tile_s8_kernel(const S8Params p) {
             const float scale = __fmul_rn(g.alpha, __fmul_rn(p.scales[0], p.scales[1]));
             const float c0 = (g.beta == 0.0f) ? 0.0f : __fmul_rn(g.beta, *cp);
             *cp = __fadd_rn(c0, __fmul_rn(scale, static_cast<float>(v)));
+        } else if constexpr (CONV) {
+            float x = __fmul_rn(static_cast<float>(v), __fmul_rn(p.scales[0], p.scales[1]));
+            if (p.conv_bias) x = __fadd_rn(x, p.conv_bias[gj]);
+            if (p.conv_op == 1) x = x > 0.0f ? x : 0.0f;
+            else if (p.conv_op == 2) x = x > 0.0f ? (x < 6.0f ? x : 6.0f) : 0.0f;
+            static_cast<float*>(g.C)[(int64_t)gi * g.ldc + gj] = x;
         } else {
             static_cast<int32_t*>(g.C)[(int64_t)gi * g.ldc + gj] = v;
         }
@@ -411,7 +419,8 @@ bool gemm_tile_s8_conv_ok(const Conv3dGeom& cg, const int8_t* in_q, const int8_t
 }
 
 cudaError_t launch_gemm_tile_s8_conv(const Conv3dGeom& cg, const int8_t* in_q, const int8_t* filter_q,
-                                     int32_t* acc, cudaStream_t s) {
+                                     const float* scales, const float* bias, int op, float* out,
+                                     cudaStream_t s) {
     if (!gemm_tile_s8_conv_ok(cg, in_q, filter_q)) return cudaErrorInvalidValue;
     S8Params sp = {};
     GemmArgs& g = sp.g;
@@ -426,9 +435,11 @@ cudaError_t launch_gemm_tile_s8_conv(const Conv3dGeom& cg, const int8_t* in_q, c
     g.B = filter_q;           // [OC, K]
     g.ldb = cg.K;
     g.b_trans = 1;
-    g.C = acc;                // [M, OC] int32
+    g.C = out;                // [M, OC] float, dequantised in the epilogue
     g.ldc = cg.OC;
-    sp.scales = nullptr;
+    sp.scales = scales;       // device: s_in, s_f, 1/s_in, 1/s_f
+    sp.conv_bias = bias;
+    sp.conv_op = op;
     sp.vec = 1;
     sp.vec16a = 1;            // store mapping of 16-byte row segments
     sp.vec16b = 1;

@@ -149,18 +149,21 @@ cudaError_t launch_conv3d_scales(const float* in, int64_t nin, const float* f, i
                                  float* scales, cudaStream_t s);
 // FP32 conv3d as one implicit-GEMM launch of the SIMT kernel (gemm_simt.cu):
 // out[M, OC] = im2col(in) x filter^T with the column matrix gathered tile by
-// tile from the NDHWC input (never materialised).  Needs IC % 4 == 0, M >= 64,
-// 16-byte aligned input and filter, at most kConv3dMaxTaps taps.
+// tile from the NDHWC input (never materialised), bias and post-op (0 none,
+// 1 relu, 2 relu6) in the epilogue.  Needs IC % 4 == 0, M >= 64, 16-byte
+// aligned input and filter, at most kConv3dMaxTaps taps.
 bool gemm_simt_conv_ok(const Conv3dGeom& g, const float* in, const float* filter);
-cudaError_t launch_gemm_simt_conv(const Conv3dGeom& g, const float* in, const float* filter, float* out,
-                                  int num_sms, cudaStream_t s);
+cudaError_t launch_gemm_simt_conv(const Conv3dGeom& g, const float* in, const float* filter, const float* bias,
+                                  int op, float* out, int num_sms, cudaStream_t s);
 // INT8 conv3d as one implicit-GEMM launch of the dp4a tile kernel
-// (gemm_tile.cu): acc[M, OC] = im2col(in_q) x filter_q^T (exact int32) with
-// 16-byte channel segments gathered from the quantised NDHWC input.  Needs
-// IC % 16 == 0, M >= 64, 16-byte aligned operands, at most kConv3dMaxTaps taps.
+// (gemm_tile.cu): out[M, OC] = post(float(im2col(in_q) x filter_q^T) *
+// (scales[0] * scales[1]) + bias) with exact int32 sums and 16-byte channel
+// segments gathered from the quantised NDHWC input.  Needs IC % 16 == 0,
+// M >= 64, 16-byte aligned operands, at most kConv3dMaxTaps taps.
 bool gemm_tile_s8_conv_ok(const Conv3dGeom& g, const int8_t* in_q, const int8_t* filter_q);
 cudaError_t launch_gemm_tile_s8_conv(const Conv3dGeom& g, const int8_t* in_q, const int8_t* filter_q,
-                                     int32_t* acc, cudaStream_t s);
+                                     const float* scales, const float* bias, int op, float* out,
+                                     cudaStream_t s);
 // out = post_op(v + bias[oc]); v = out, or float(acc) * (scales[0] * scales[1]) when acc.
 cudaError_t launch_conv3d_post(float* out, const int32_t* acc, const float* scales, const float* bias,
                                int64_t M, int OC, int op, cudaStream_t s);
