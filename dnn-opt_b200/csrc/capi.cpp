@@ -595,6 +595,17 @@ int conv3d_device(int precision, const Conv3dGeom& g, const float* in, const flo
     void* inq = base + col_b + flt_b + acc_b;
     const int64_t nf = static_cast<int64_t>(g.OC) * g.K;
     cudaError_t e = cudaSuccess;
+    if (implicit8) {   // absmax; scales + quantised input and filter; GEMM with the epilogue
+        e = launch_conv3d_absmax_quant(in, nin, f, nf, w->absmax, w->scales, static_cast<int8_t*>(inq),
+                                       static_cast<int8_t*>(fq), s);
+        note_launch(2);
+        if (e == cudaSuccess) {
+            e = launch_gemm_tile_s8_conv(g, static_cast<const int8_t*>(inq), static_cast<const int8_t*>(fq),
+                                         w->scales, bias, op, out, s);
+            note_launch();
+        }
+        return cuda_status(e);
+    }
     if (precision == DNNOPT_CONV3D_INT8) {
         e = launch_conv3d_scales(in, nin, f, nf, w->absmax, w->scales, s);
         note_launch(2);
@@ -603,22 +614,16 @@ int conv3d_device(int precision, const Conv3dGeom& g, const float* in, const flo
     if (copy) {
         e = launch_conv3d_filter(precision, in, inq, nin, w->scales, s, 2);
         note_launch();
-        if (e == cudaSuccess && !implicit8) e = launch_conv3d_im2col_copy(g, precision, inq, col, s);
+        if (e == cudaSuccess) e = launch_conv3d_im2col_copy(g, precision, inq, col, s);
     } else {
         e = launch_conv3d_im2col(g, precision, in, col, w->scales, s);
     }
-    if (!implicit8) note_launch();
+    note_launch();
     if (e == cudaSuccess && precision != DNNOPT_CONV3D_FP32) {
         e = launch_conv3d_filter(precision, f, fq, nf, w->scales, s);
         note_launch();
     }
     if (e != cudaSuccess) return cuda_status(e);
-    if (implicit8) {   // dequantisation, bias and post-op in the GEMM's epilogue
-        e = launch_gemm_tile_s8_conv(g, static_cast<const int8_t*>(inq), static_cast<const int8_t*>(fq), w->scales,
-                                     bias, op, out, s);
-        note_launch();
-        return cuda_status(e);
-    }
     GemmArgs ga;
     ga.M = static_cast<int>(g.M); ga.N = g.OC; ga.K = static_cast<int>(g.K);
     ga.alpha = 1.0f; ga.beta = 0.0f;

@@ -253,6 +253,28 @@ __global__ void conv3d_scales_kernel(const uint32_t* bits, float* scales) {
     }
 }
 
+// The scales from the absmax bits (as conv3d_scales_kernel computes them),
+// then input and filter quantised in one grid-stride pass; block 0 also stores
+// the scales for the GEMM's dequantising epilogue.
+__global__ void conv3d_quant_both_kernel(const float* __restrict__ in, int64_t nin, const float* __restrict__ f,
+                                         int64_t nf, const uint32_t* bits, float* scales, int8_t* inq,
+                                         int8_t* fq) {
+    const float m0 = __uint_as_float(bits[0]), m1 = __uint_as_float(bits[1]);
+    const float s0 = m0 == 0.0f ? 1.0f : __fdiv_rn(m0, 127.0f);
+    const float s1 = m1 == 0.0f ? 1.0f : __fdiv_rn(m1, 127.0f);
+    const float inv0 = __fdiv_rn(1.0f, s0), inv1 = __fdiv_rn(1.0f, s1);
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        scales[0] = s0;
+        scales[1] = s1;
+        scales[2] = inv0;
+        scales[3] = inv1;
+    }
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nin + nf; i += (int64_t)gridDim.x * blockDim.x) {
+        if (i < nin) inq[i] = quant8(in[i], inv0);
+        else fq[i - nin] = quant8(f[i - nin], inv1);
+    }
+}
+
 // output = post(v + bias[oc]), v = the GEMM result, or float(acc) * (s_in*s_f)
 // for INT8 (dequantize_int32_to_fp32_3d :379-386, apply_conv3d_postops).
 __global__ void conv3d_post_kernel(float* out, const int32_t* acc, const float* scales, const float* bias,
@@ -333,6 +355,17 @@ cudaError_t launch_conv3d_scales(const float* in, int64_t nin, const float* f, i
     const int grid = static_cast<int>(blocks < 148 * 4 ? (blocks > 0 ? blocks : 1) : 148 * 4);
     conv3d_absmax_kernel<<<grid, kThreads, 0, s>>>(in, nin, f, nf, bits);
     conv3d_scales_kernel<<<1, 32, 0, s>>>(bits, scales);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_conv3d_absmax_quant(const float* in, int64_t nin, const float* f, int64_t nf, uint32_t* bits,
+                                       float* scales, int8_t* inq, int8_t* fq, cudaStream_t s) {
+    cudaError_t e = cudaMemsetAsync(bits, 0, 2 * sizeof(uint32_t), s);
+    if (e != cudaSuccess) return e;
+    const int64_t blocks = (nin + nf + 4 * kThreads - 1) / (4 * kThreads);
+    const int grid = static_cast<int>(blocks < 148 * 4 ? (blocks > 0 ? blocks : 1) : 148 * 4);
+    conv3d_absmax_kernel<<<grid, kThreads, 0, s>>>(in, nin, f, nf, bits);
+    conv3d_quant_both_kernel<<<grid_for(nin + nf), kThreads, 0, s>>>(in, nin, f, nf, bits, scales, inq, fq);
     return cudaGetLastError();
 }
 

@@ -144,6 +144,9 @@ cudaError_t launch_conv3d_filter(int mode, const float* f, void* out, int64_t n,
 bool conv3d_copy_im2col_ok(const Conv3dGeom& g, int mode);
 cudaError_t launch_conv3d_im2col_copy(const Conv3dGeom& g, int mode, const void* in_conv, void* col,
                                       cudaStream_t s);
+// Absmax, then scales[0..3] and the INT8 input and filter in one pass (two launches).
+cudaError_t launch_conv3d_absmax_quant(const float* in, int64_t nin, const float* f, int64_t nf, uint32_t* bits,
+                                       float* scales, int8_t* inq, int8_t* fq, cudaStream_t s);
 // scales[0..3] = s_in, s_f, 1/s_in, 1/s_f from the per-tensor absmax (bits: 2 words).
 cudaError_t launch_conv3d_scales(const float* in, int64_t nin, const float* f, int64_t nf, uint32_t* bits,
                                  float* scales, cudaStream_t s);
