@@ -42,6 +42,9 @@ METRIC = "GFLOP/s (TOPS int8/fp8) and % of HBM/tensor roofline per shape vs refe
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 N_SETS = 3
 SWEEP_STREAMS = 6
+# One workload string for both arms, so their lines name the same config.
+WORKLOAD = ("C2 FP32 sweep: M{2,3,5,7} x N{1009,2039,4093} x K1024, alpha=1, beta=0.5 "
+            "(12 GEMMs per step)")
 
 
 def load_dnnopt():
@@ -186,7 +189,7 @@ def run_reference_arm(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded uniform[-1,1], reference test generator)",
-        "config": {"workload": "C2 FP32 sweep M{2,3,5,7} x N{1009,2039,4093} x K1024, beta=0.5"},
+        "config": {"workload": WORKLOAD},
         "cpu_baseline": {"value": v, "unit": "GFLOP/s", "cores": cores, "kind": kind, "sample": sample},
         "e2e": {"value": v, "unit": "GFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -647,8 +650,7 @@ def run_gpu_arm(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded uniform[-1,1], the reference tests' std::mt19937 stream)",
             "config": {
-                "workload": "C2 FP32 sweep: M{2,3,5,7} x N{1009,2039,4093} x K1024, alpha=1, beta=0.5 "
-                            "(12 GEMMs per step)",
+                "workload": WORKLOAD,
                 "api": f"dnnopt_cuda_gemm_f32 (device pointers); the 12 independent GEMMs on {args.streams} "
                        "streams forked/joined inside one CUDA graph per input set",
                 "l2": f"{N_SETS} rotating input sets ({N_SETS * bytes_step / 1e6:.0f} MB > 126 MB L2)",

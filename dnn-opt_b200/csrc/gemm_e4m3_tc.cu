@@ -9,9 +9,12 @@
 // are the UMMA M dimension, the activations the N dimension.  A small prep
 // kernel first splits the bf16 activations into two e4m3 operands,
 // hi = e4m3(a*s) and lo = e4m3(a*s - hi), with s a power of two per row
-// (max |a*s| in [128, 256)); hi + lo reproduces a*s exactly whenever the
-// residual is in e4m3's normal range, i.e. for all but values more than 2^18
-// below the row maximum.  UMMA N = 16 holds the 8 hi rows and 8 lo rows (one
+// (max |a*s| in [128, 256)).  a*s carries bf16's 8 significant bits, hi the
+// top 4 and lo the rest, so hi + lo reproduces a*s exactly while the
+// residual's last bit is at least e4m3's subnormal step 2^-9, i.e. for
+// |a*s| >= 2^-2, values down to 2^9-2^10 below the row maximum; smaller values
+// are off by at most 2^-10, about 2^-17-2^-18 of the row maximum, well inside
+// the bf16 output rounding.  UMMA N = 16 holds the 8 hi rows and 8 lo rows (one
 // 2 KB TMA box per K-block, loaded with the weight box), so
 // D[:, m] + D[:, 8+m] is the full-precision product sum, undone by 1/s.
 //

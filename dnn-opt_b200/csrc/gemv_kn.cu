@@ -27,6 +27,7 @@
 #include "dnnopt_b200.h"
 #include "elem.cuh"
 #include "kernels.h"
+#include "plan.h"
 
 namespace dnnopt_b200 {
 
@@ -486,9 +487,11 @@ cudaError_t launch_gemv_kn(In ia, In ib, const GemmArgs& g, const GemvKnPlan& p,
 // accounting and out-of-memory handling), serving loops that forbid any
 // allocation after warm-up because cudaMalloc can synchronise the device, and
 // runtimes that fix their memory budget at start-up.  For them this entry
-// point runs the same small-M split-K GEMV kernel as dnnopt_cuda_gemm_f32
-// but takes its scratch (split-K partial strips and the per-strip tickets)
-// from the file-scope device array below instead of the per-stream workspace.
+// point runs the small-M split-K GEMV kernel with the planner's split rule
+// (dnnopt_cuda_gemm_f32 may pick the slab or cluster kernel for the same
+// shape; results then agree within FP32 rounding, not bitwise) and takes its
+// scratch (split-K partial strips and the per-strip tickets) from the
+// file-scope device array below instead of the per-stream workspace.
 //
 // * Capacity: kNoAllocTicketWords strips of 128 columns (N <= 131072) and
 //   kNoAllocPartialFloats partial floats (4 MiB); larger requests are
@@ -496,8 +499,10 @@ cudaError_t launch_gemv_kn(In ia, In ib, const GemmArgs& g, const GemvKnPlan& p,
 //   is held by every GPU that loads the library until the process exits.
 // * The first call on a device looks up the array's device address with
 //   cudaGetSymbolAddress (host code cannot use the symbol itself: on the host
-//   it names a stand-in, not device memory); make that first call before any
-//   stream capture.
+//   it names a stand-in, not device memory) and loads the eight FP32 kernel
+//   instantiations; make that first call before any stream capture.  The
+//   address is cached for the life of the process: after cudaDeviceReset the
+//   entry point must not be called again.
 // * Every call shares the array and it keeps the last call's contents: the
 //   tickets are cleared on the call's stream before each launch, the partials
 //   are fully rewritten before they are read.  Calls that overlap on the GPU
@@ -515,11 +520,49 @@ constexpr size_t kNoAllocScratchBytes = kNoAllocTicketWords * 4 + kNoAllocPartia
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 constexpr int kNoAllocMaxDevices = 64;
+// Per-device set-up, done once under g_noalloc_mu by the first call on that
+// device: the scratch array's device address, the SM count and the resident
+// CTAs per SM of each of the eight FP32 instantiations (M class 1/2/4/8 x
+// vector width), which also loads every one of them, so that later calls make
+// no driver query and load no code.
+struct NoAllocDevice {
+    void* scratch = nullptr;
+    int sms = 0;
+    int occ[4][2] = {};
+};
 std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
-int g_noalloc_sms[kNoAllocMaxDevices] = {};
+NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
 
 int noalloc_mt(int M) { return M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8)); }
+int noalloc_mt_index(int mt) { return mt == 1 ? 0 : (mt == 2 ? 1 : (mt == 4 ? 2 : 3)); }
+
+int noalloc_setup(int dev, NoAllocDevice* out) {
+    NoAllocDevice d;
+    if (cudaGetSymbolAddress(&d.scratch, g_noalloc_scratch) != cudaSuccess || !d.scratch) {
+        cudaGetLastError();
+        return DNNOPT_STATUS_CUDA_ERROR;
+    }
+    if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+        cudaGetLastError();
+        return DNNOPT_STATUS_CUDA_ERROR;
+    }
+    const int mts[4] = {1, 2, 4, 8};
+    for (int i = 0; i < 4; ++i) {
+        for (int v = 0; v < 2; ++v) {
+            const void* fn = kn_select(In::F32, In::F32, mts[i], v);
+            cudaFuncAttributes fa;
+            int occ = 0;
+            if (!fn || cudaFuncGetAttributes(&fa, fn) != cudaSuccess ||
+                gemv_kn_occupancy(In::F32, In::F32, mts[i], v, &occ) != cudaSuccess) {
+                cudaGetLastError();
+                return DNNOPT_STATUS_CUDA_ERROR;
+            }
+            d.occ[i][v] = occ < 1 ? 1 : occ;
+        }
+    }
+    *out = d;
+    return DNNOPT_STATUS_SUCCESS;
+}
 
 }  // namespace
 }  // namespace dnnopt_b200
@@ -542,27 +585,16 @@ extern "C" __attribute__((visibility("default"))) int dnnopt_cuda_gemm_f32_noall
         return DNNOPT_STATUS_NO_DEVICE;
     }
     if (dev < 0 || dev >= kNoAllocMaxDevices) return DNNOPT_STATUS_NOT_SUPPORTED;
-    void* scratch = nullptr;
-    int sms = 0;
+    NoAllocDevice nd;
     {
         std::lock_guard<std::mutex> lk(g_noalloc_mu);
-        if (!g_noalloc_ptr[dev]) {
-            void* p = nullptr;
-            if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
-                cudaGetLastError();
-                return DNNOPT_STATUS_CUDA_ERROR;
-            }
-            int n = 0;
-            if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
-                cudaGetLastError();
-                return DNNOPT_STATUS_CUDA_ERROR;
-            }
-            g_noalloc_ptr[dev] = p;
-            g_noalloc_sms[dev] = n;
+        if (!g_noalloc_dev[dev].scratch) {
+            const int st = noalloc_setup(dev, &g_noalloc_dev[dev]);
+            if (st != DNNOPT_STATUS_SUCCESS) return st;
         }
-        scratch = g_noalloc_ptr[dev];
-        sms = g_noalloc_sms[dev];
+        nd = g_noalloc_dev[dev];
     }
+    void* scratch = nd.scratch;
 
     GemmArgs g;
     g.M = d->M; g.N = d->N; g.K = d->K;
@@ -571,25 +603,20 @@ extern "C" __attribute__((visibility("default"))) int dnnopt_cuda_gemm_f32_noall
     g.B = B; g.ldb = d->ldb; g.b_trans = 0;
     g.C = C; g.ldc = d->ldc;
 
-    // Same split-K choice as the allocating path, capped by the scratch size.
-    GemvKnPlan p;
-    p.mt = noalloc_mt(g.M);
-    p.vec4 = (reinterpret_cast<uintptr_t>(B) % 16 == 0 && g.ldb % 4 == 0) ? 1 : 0;
-    int occ = 1;
-    if (gemv_kn_occupancy(In::F32, In::F32, p.mt, p.vec4, &occ) != cudaSuccess || occ < 1) {
-        cudaGetLastError();
-        occ = 1;
-    }
-    int splits = (occ * sms) / tiles;
-    const int max_splits = g.K / 32 > 1 ? g.K / 32 : 1;
-    splits = splits > max_splits ? max_splits : splits;
-    splits = splits < 1 ? 1 : splits;
+    // The planner's split-K rule for this kernel (kn_plan_rule, the one
+    // dnnopt_cuda_gemm_f32 uses when it picks the split-K kernel), then fewer
+    // splits if the partial strips would not fit the fixed array.  The rule
+    // keeps splits x strips within one wave of resident CTAs, at most 8 x 128
+    // x 3 x 148 floats, so the clamp is a guard that B200 shapes do not reach.
+    const int mt = noalloc_mt(g.M);
+    const int vec4 = (reinterpret_cast<uintptr_t>(B) % 16 == 0 && g.ldb % 4 == 0) ? 1 : 0;
+    GemvKnPlan p = kn_plan_rule(g, mt, vec4, nd.occ[noalloc_mt_index(mt)][vec4], nd.sms, 0, false);
     const size_t per_split = static_cast<size_t>(p.mt) * tiles * 128;
-    while (splits > 1 && static_cast<size_t>(splits) * per_split > kNoAllocPartialFloats) --splits;
-    int kchunk = (g.K + splits - 1) / splits;
-    kchunk = (kchunk + 7) / 8 * 8;
-    p.kchunk = kchunk;
-    p.splits = (g.K + kchunk - 1) / kchunk;
+    if (p.splits > 1 && static_cast<size_t>(p.splits) * per_split > kNoAllocPartialFloats) {
+        int splits = p.splits;
+        while (splits > 1 && static_cast<size_t>(splits) * per_split > kNoAllocPartialFloats) --splits;
+        p = kn_plan_rule(g, mt, vec4, 1, nd.sms, splits, false);
+    }
     if (p.splits > 1 && static_cast<size_t>(p.splits) * per_split > kNoAllocPartialFloats)
         return DNNOPT_STATUS_EXCEEDS_SCRATCH;
 

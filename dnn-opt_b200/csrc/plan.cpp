@@ -23,8 +23,12 @@
 #include <cstdlib>
 #include <cstring>
 #include <functional>
+#include <list>
 #include <map>
 #include <mutex>
+#include <unordered_map>
+#include <utility>
+#include <vector>
 
 namespace dnnopt_b200 {
 
@@ -168,12 +172,11 @@ const char* kernel_name(KernelId k) {
     return "?";
 }
 
-GemvKnPlan kn_plan_for(Kind kind, const GemmArgs& g, const DeviceInfo& info, int splits_hint,
-                       bool allow_cluster) {
+GemvKnPlan kn_plan_rule(const GemmArgs& g, int mt, int vec4, int occ, int num_sms, int splits_hint,
+                        bool allow_cluster) {
     GemvKnPlan p;
-    p.mt = mt_for(g.M);
-    const size_t eb = static_cast<size_t>(elem_bytes_b(kind));
-    p.vec4 = (aligned(g.B, 4 * eb) && g.ldb % 4 == 0) ? 1 : 0;
+    p.mt = mt;
+    p.vec4 = vec4;
     p.cluster = 0;
     const int tiles = gemv_kn_tiles(g.N);
     const int max_splits = g.K / 32 > 1 ? g.K / 32 : 1;
@@ -182,8 +185,7 @@ GemvKnPlan kn_plan_for(Kind kind, const GemmArgs& g, const DeviceInfo& info, int
     if (splits <= 0) {
         // One wave of resident CTAs, at most 16 splits of at least 64 rows:
         // measured on B200, more splits only add reduction latency.
-        const int occ = kn_occupancy(kind, p.mt, p.vec4, info);
-        splits = (occ * info.num_sms) / tiles;
+        splits = (occ * num_sms) / tiles;
         if (splits > 16) splits = 16;
         if (splits > g.K / 64) splits = g.K / 64;
     }
@@ -202,6 +204,15 @@ GemvKnPlan kn_plan_for(Kind kind, const GemmArgs& g, const DeviceInfo& info, int
     p.kchunk = kchunk;
     p.splits = (g.K + kchunk - 1) / kchunk;
     return p;
+}
+
+GemvKnPlan kn_plan_for(Kind kind, const GemmArgs& g, const DeviceInfo& info, int splits_hint,
+                       bool allow_cluster) {
+    const int mt = mt_for(g.M);
+    const size_t eb = static_cast<size_t>(elem_bytes_b(kind));
+    const int vec4 = (aligned(g.B, 4 * eb) && g.ldb % 4 == 0) ? 1 : 0;
+    const int occ = splits_hint <= 0 ? kn_occupancy(kind, mt, vec4, info) : 1;
+    return kn_plan_rule(g, mt, vec4, occ, info.num_sms, splits_hint, allow_cluster);
 }
 
 GemvNkPlan nk_plan_for(Kind kind, const GemmArgs& g, const DeviceInfo& info, int grid_hint) {
@@ -344,19 +355,49 @@ struct Entry {
     float time_us;
 };
 
+// LRU of kCacheCapacity plans (the reference's ShapeCache keeps 256 entries,
+// include/dnnopt/autotune/shape_cache.h:139-146): `g_lru` lists keys from the
+// most to the least recently used; a lookup hit or a store moves the key to
+// the front, a store into a full cache evicts the back.
+constexpr size_t kCacheCapacity = 256;
+struct Slot {
+    Entry e;
+    std::list<uint64_t>::iterator pos;
+};
 std::mutex g_cache_mu;
-std::map<uint64_t, Entry> g_cache;
+std::unordered_map<uint64_t, Slot> g_cache;
+std::list<uint64_t> g_lru;
 int g_autotune = -1;   // -1: read DNNOPT_AUTOTUNE on first query
 
+// Inserts or refreshes `key` (caller holds g_cache_mu).
+void cache_put_locked(uint64_t key, const Entry& e) {
+    auto it = g_cache.find(key);
+    if (it != g_cache.end()) {
+        it->second.e = e;
+        g_lru.splice(g_lru.begin(), g_lru, it->second.pos);
+        return;
+    }
+    while (g_cache.size() >= kCacheCapacity && !g_lru.empty()) {
+        g_cache.erase(g_lru.back());
+        g_lru.pop_back();
+    }
+    g_lru.push_front(key);
+    g_cache[key] = Slot{e, g_lru.begin()};
+}
+
+// FNV-1a, 64-bit (offset basis 14695981039346656037, prime 1099511628211),
+// the hash of the reference's shape keys (src/autotune/shape_cache.cpp:15-24).
 uint64_t fnv1a(const void* data, size_t n) {
     const unsigned char* p = static_cast<const unsigned char*>(data);
-    uint64_t h = 1469598103934665603ull;
+    uint64_t h = 14695981039346656037ull;
     for (size_t i = 0; i < n; ++i) { h ^= p[i]; h *= 1099511628211ull; }
     return h;
 }
 
 constexpr char kMagic[8] = {'D', 'N', 'N', 'A', 'U', 'T', 'O', '\0'};
-constexpr uint32_t kVersion = 4;   // reference files are v1-v3 (CPU blocking choices)
+// Reference files are v1-v3 (CPU blocking choices); v4 files of this library
+// were keyed with a mistyped offset basis, so v5 marks the FNV-1a keys.
+constexpr uint32_t kVersion = 5;
 
 }  // namespace
 
@@ -384,7 +425,8 @@ bool cache_lookup(uint64_t key, Plan* out) {
     std::lock_guard<std::mutex> lk(g_cache_mu);
     auto it = g_cache.find(key);
     if (it == g_cache.end()) return false;
-    const Entry& e = it->second;
+    g_lru.splice(g_lru.begin(), g_lru, it->second.pos);
+    const Entry& e = it->second.e;
     out->kernel = static_cast<KernelId>(e.kernel);
     out->tuned = true;
     if (out->kernel == KernelId::GemvSlab) {
@@ -419,8 +461,7 @@ void cache_store(uint64_t key, const Plan& p, float time_us) {
     else { e.p0 = p.nk.grid; e.p1 = 0; e.mt = p.nk.mt; }
     e.time_us = time_us;
     std::lock_guard<std::mutex> lk(g_cache_mu);
-    if (g_cache.size() >= 4096) g_cache.erase(g_cache.begin());
-    g_cache[key] = e;
+    cache_put_locked(key, e);
 }
 
 int cache_save(const char* path) {
@@ -430,8 +471,11 @@ int cache_save(const char* path) {
     uint32_t n = static_cast<uint32_t>(g_cache.size());
     bool ok = std::fwrite(kMagic, 1, 8, f) == 8 && std::fwrite(&kVersion, 4, 1, f) == 1 &&
               std::fwrite(&n, 4, 1, f) == 1;
-    for (const auto& kv : g_cache) {
-        ok = ok && std::fwrite(&kv.first, 8, 1, f) == 1 && std::fwrite(&kv.second, sizeof(Entry), 1, f) == 1;
+    // Least recently used first: loading the file re-inserts in this order,
+    // so the recency order survives a save / load round trip.
+    for (auto it = g_lru.rbegin(); it != g_lru.rend(); ++it) {
+        const Entry& e = g_cache[*it].e;
+        ok = ok && std::fwrite(&*it, 8, 1, f) == 1 && std::fwrite(&e, sizeof(Entry), 1, f) == 1;
     }
     ok = (std::fclose(f) == 0) && ok;
     return ok ? static_cast<int>(n) : -1;
@@ -448,7 +492,8 @@ int cache_load(const char* path) {
         std::fclose(f);
         return -1;
     }
-    std::map<uint64_t, Entry> loaded;
+    std::vector<std::pair<uint64_t, Entry>> loaded;
+    loaded.reserve(n);
     for (uint32_t i = 0; i < n; ++i) {
         uint64_t key;
         Entry e;
@@ -456,11 +501,13 @@ int cache_load(const char* path) {
             std::fclose(f);
             return -1;
         }
-        loaded[key] = e;
+        loaded.emplace_back(key, e);
     }
     std::fclose(f);
+    // File order is least recently used first; past the capacity the oldest
+    // entries are evicted as they would have been.
     std::lock_guard<std::mutex> lk(g_cache_mu);
-    for (const auto& kv : loaded) g_cache[kv.first] = kv.second;
+    for (const auto& kv : loaded) cache_put_locked(kv.first, kv.second);
     return static_cast<int>(loaded.size());
 }
 

@@ -55,6 +55,12 @@ struct DeviceInfo {
 // (splits <= 16, kchunk <= gemv_kn_cluster_max_chunk()).
 GemvKnPlan kn_plan_for(Kind kind, const GemmArgs& g, const DeviceInfo& info, int splits_hint,
                        bool allow_cluster = true);
+// The split rule behind kn_plan_for as a pure function of the shape, the M
+// class, the B vector width, the kernel's resident CTAs per SM and the SM
+// count (shared with the allocation-free entry point, which caches its own
+// occupancy figures).
+GemvKnPlan kn_plan_rule(const GemmArgs& g, int mt, int vec4, int occ, int num_sms, int splits_hint,
+                        bool allow_cluster);
 GemvNkPlan nk_plan_for(Kind kind, const GemmArgs& g, const DeviceInfo& info, int grid_hint);
 
 // Heuristic plan (no timing).  Needs no device when info.have_device is false
@@ -63,7 +69,8 @@ Plan heuristic_plan(Kind kind, const GemmArgs& g, const DeviceInfo& info);
 const char* kernel_name(KernelId k);
 std::string describe_plan(Kind kind, const GemmArgs& g, const Plan& p);
 
-// Autotune cache (FNV-1a keyed, persisted as "DNNAUTO" version 4).
+// Autotune cache: LRU of 256 plans keyed by FNV-1a, persisted as "DNNAUTO"
+// version 5.
 bool autotune_enabled();
 void set_autotune_enabled(bool on);
 uint64_t plan_key(Kind kind, const GemmArgs& g, int vec);

@@ -213,13 +213,18 @@ int dnnopt_cuda_gemm_refe5m2_e5m2(const dnnopt_gemm_desc* d, const uint8_t* A, c
 /* Allocation-free FP32 small-M GEMM (no counterpart in the reference).  For
  * callers that cannot call cudaMalloc -- code whose device memory belongs to
  * a framework's caching allocator, serving loops that allow no allocation
- * after warm-up, runtimes with a memory budget fixed at start-up.  Same
- * arithmetic and kernel as dnnopt_cuda_gemm_f32 for M <= 8 with B stored
- * K x N (otherwise DNNOPT_STATUS_NOT_SUPPORTED); its split-K scratch is a
- * fixed 4 MiB device array inside the library (N <= 131072, larger requests
- * return DNNOPT_STATUS_EXCEEDS_SCRATCH).  The first call on a device looks up
- * that array; make it before any stream capture.  All calls share the array:
- * calls that overlap on the GPU race and must be serialised by the caller. */
+ * after warm-up, runtimes with a memory budget fixed at start-up.  M <= 8
+ * with B stored K x N (otherwise DNNOPT_STATUS_NOT_SUPPORTED), on the split-K
+ * GEMV kernel with the planner's split rule.  dnnopt_cuda_gemm_f32 may pick
+ * the column-slab or cluster kernel for the same shape, which sum in another
+ * order: results agree within FP32 rounding, not bit for bit.  The split-K
+ * scratch is a fixed 4 MiB device array inside the library (N <= 131072,
+ * larger requests return DNNOPT_STATUS_EXCEEDS_SCRATCH).  The first call on a
+ * device looks up that array and loads the kernel; make it before any stream
+ * capture.  The looked-up address belongs to the device's primary context:
+ * after cudaDeviceReset the entry point must not be called again in this
+ * process.  All calls share the array: calls that overlap on the GPU race and
+ * must be serialised by the caller. */
 int dnnopt_cuda_gemm_f32_noalloc(const dnnopt_gemm_desc* d, const float* A, const float* B,
                                  float* C, void* stream);
 

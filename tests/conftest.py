@@ -50,6 +50,34 @@ def load_dnnopt():
     return mod
 
 
+# Autotune-cache files ("DNNAUTO" v5): a plan key is the 64-bit FNV-1a hash
+# (offset basis 14695981039346656037, prime 1099511628211) of ten
+# little-endian int64 fields; an entry is the key plus (kernel id, p0, p1, mt,
+# time_us).
+PLAN_FILE_VERSION = 5
+
+
+def fnv1a64(data: bytes) -> int:
+    h = 14695981039346656037
+    for b in data:
+        h = ((h ^ b) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+    return h
+
+
+def plan_key(kind, M, N, K, lda, ldb, ldc, ta, tb, vec):
+    import struct
+    return fnv1a64(struct.pack("<10q", kind, M, N, K, lda, ldb, ldc, ta, tb, vec))
+
+
+def plan_file_bytes(entries, version=PLAN_FILE_VERSION):
+    """entries: [(key, (kernel, p0, p1, mt))], least recently used first."""
+    import struct
+    out = b"DNNAUTO\x00" + struct.pack("<II", version, len(entries))
+    for key, e in entries:
+        out += struct.pack("<Q", key) + struct.pack("<iiiif", *e, 0.0)
+    return out
+
+
 @pytest.fixture(scope="session")
 def dn():
     return load_dnnopt()

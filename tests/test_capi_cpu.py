@@ -11,6 +11,8 @@ import subprocess
 import numpy as np
 import pytest
 
+from tests.conftest import fnv1a64, plan_file_bytes
+
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
@@ -167,14 +169,56 @@ def test_autotune_cache_files(dn, tmp_path):
     with open(p, "rb") as f:
         head = f.read(16)
     assert head[:8] == b"DNNAUTO\x00"
-    assert struct.unpack("<II", head[8:16]) == (4, n)
+    assert struct.unpack("<II", head[8:16]) == (5, n)
     assert dn.lib.dnnopt_autotune_load(p) == n
     bad = tmp_path / "bad.bin"
     bad.write_bytes(b"DNNAUTO\x00" + struct.pack("<II", 3, 0))   # reference v3 file: rejected
     assert dn.lib.dnnopt_autotune_load(str(bad).encode()) == -1
+    bad.write_bytes(plan_file_bytes([(1, (0, 1, 8, 1))], version=4))   # mistyped-basis keys: rejected
+    assert dn.lib.dnnopt_autotune_load(str(bad).encode()) == -1
     bad.write_bytes(b"garbage")
     assert dn.lib.dnnopt_autotune_load(str(bad).encode()) == -1
     assert dn.lib.dnnopt_autotune_load(b"/nonexistent/file") == -1
+
+
+def _saved_keys(dn, path):
+    assert dn.lib.dnnopt_autotune_save(str(path).encode()) >= 0
+    raw = path.read_bytes()
+    n = struct.unpack("<I", raw[12:16])[0]
+    return [struct.unpack("<Q", raw[16 + 28 * i:24 + 28 * i])[0] for i in range(n)]
+
+
+def test_autotune_cache_is_lru_of_256(dn, tmp_path):
+    """The plan cache keeps the 256 most recently used plans, like the
+    reference's ShapeCache (include/dnnopt/autotune/shape_cache.h:139-146):
+    inserting past the capacity evicts the least recently used key, and
+    re-inserting a key refreshes it.  Saved files list keys least recent
+    first, so a load restores the order."""
+    base = 1 << 40
+    first = [(base + i, (0, 1, 8, 1)) for i in range(300)]
+    f1 = tmp_path / "many.bin"
+    f1.write_bytes(plan_file_bytes(first))
+    assert dn.lib.dnnopt_autotune_load(str(f1).encode()) == 300
+    assert dn.lib.dnnopt_autotune_entries() == 256
+    keys = _saved_keys(dn, tmp_path / "s1.bin")
+    assert keys == [base + i for i in range(44, 300)]
+    # Refresh the oldest survivor, then insert a new key: the next oldest goes.
+    f2 = tmp_path / "two.bin"
+    f2.write_bytes(plan_file_bytes([(base + 44, (0, 2, 8, 1)), (base + 1000, (0, 1, 8, 1))]))
+    assert dn.lib.dnnopt_autotune_load(str(f2).encode()) == 2
+    keys = _saved_keys(dn, tmp_path / "s2.bin")
+    assert len(keys) == 256
+    assert base + 45 not in keys and keys[-2:] == [base + 44, base + 1000]
+    assert keys[0] == base + 46
+
+
+def test_plan_key_hash_is_fnv1a():
+    """Known-answer values of 64-bit FNV-1a for the key helper that the GPU
+    tests use to force plans (a forced plan is found only when the library
+    hashes its keys the same way)."""
+    for b, want in ((b"", 0xCBF29CE484222325), (b"a", 0xAF63DC4C8601EC8C),
+                    (b"foobar", 0x85944171F73967E8)):
+        assert fnv1a64(b) == want
 
 
 def test_thread_count_plumbing(dn):

@@ -15,6 +15,7 @@ import numpy as np
 import pytest
 
 from oracle.oracle import bf16_bits, bf16_to_f32, int8_uniform, ref_uniform
+from tests.conftest import plan_file_bytes, plan_key
 
 pytestmark = pytest.mark.gpu
 
@@ -664,18 +665,13 @@ def test_plan_selection_on_device(gpu, dn):
 def test_cluster_variant_forced(gpu, dn, orc, tmp_path, splits):
     """The cluster (DSMEM-reduction) variant, forced through an autotune-cache
     entry, against the oracle on a prime-N shape and an aligned shape."""
-    import struct
     for (M, N, K, vec) in [(3, 2039, 1024, 0), (8, 1024, 2048, 1)]:
         kchunk = ((K + splits - 1) // splits + 7) // 8 * 8
         se = (K + kchunk - 1) // kchunk
         mt = 1 if M <= 1 else 2 if M <= 2 else 4 if M <= 4 else 8
-        key_src = struct.pack("<10q", 0, M, N, K, K, N, N, 0, 0, vec)
-        h = 1469598103934665603
-        for b in key_src:
-            h = ((h ^ b) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+        h = plan_key(0, M, N, K, K, N, N, 0, 0, vec)
         path = tmp_path / f"cl_{splits}_{M}.bin"
-        path.write_bytes(b"DNNAUTO\x00" + struct.pack("<II", 4, 1) + struct.pack("<Q", h) +
-                         struct.pack("<iiiif", 6, se, kchunk, mt, 0.0))
+        path.write_bytes(plan_file_bytes([(h, (6, se, kchunk, mt))]))
         assert dn.lib.dnnopt_autotune_load(str(path).encode()) == 1
         d = dn.desc(M, N, K, K, N, N, 1.0, 0.5)
         assert dn.plan_describe(dn.KIND_F32, d).startswith("gemv_kn_")  # heuristic view
@@ -688,14 +684,9 @@ def test_cluster_variant_forced(gpu, dn, orc, tmp_path, splits):
 
 def _force_plan(dn, tmp_path, name, kind, M, N, K, lda, ldb, ldc, ta, tb, vec, entry):
     """Load an autotune-cache file holding one plan for this exact call."""
-    import struct
-    key_src = struct.pack("<10q", kind, M, N, K, lda, ldb, ldc, ta, tb, vec)
-    h = 1469598103934665603
-    for b in key_src:
-        h = ((h ^ b) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+    h = plan_key(kind, M, N, K, lda, ldb, ldc, ta, tb, vec)
     path = tmp_path / name
-    path.write_bytes(b"DNNAUTO\x00" + struct.pack("<II", 4, 1) + struct.pack("<Q", h) +
-                     struct.pack("<iiiif", *entry, 0.0))
+    path.write_bytes(plan_file_bytes([(h, tuple(entry))]))
     assert dn.lib.dnnopt_autotune_load(str(path).encode()) == 1
 
 
