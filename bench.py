@@ -68,6 +68,13 @@ def peaks():
     return dict(FALLBACK_PEAKS, source="fallback")
 
 
+def rotating_sets(bytes_per_set, floor=3):
+    """Input sets to rotate between timed calls: at least `floor` and at least
+    ~3x the 126 MB L2 in all (384 MB), so that no call finds its operands in
+    L2 left over from an earlier call."""
+    return max(floor, -(-384_000_000 // int(bytes_per_set)))
+
+
 def gemm_bytes(M, N, K, beta, eb=4):
     return eb * (M * K + K * N + M * N * (2 if beta != 0 else 1))
 
@@ -287,27 +294,29 @@ def per_config(torch, dn, stream, pk, world, rank, dist):
     s = stream
     # C1: FP32 1 x 4096 x 4096.
     M, N, K = 1, 4096, 4096
-    As = [torch.from_numpy(ref_uniform(M * K, 42 + i)).cuda() for i in range(N_SETS)]
-    Bs = [torch.from_numpy(ref_uniform(K * N, 123 + i)).cuda() for i in range(N_SETS)]
-    Cs = [torch.zeros(M * N, device="cuda") for _ in range(N_SETS)]
+    ns = rotating_sets(gemm_bytes(M, N, K, 0.0))
+    As = [torch.from_numpy(ref_uniform(M * K, 42 + i)).cuda() for i in range(ns)]
+    Bs = [torch.from_numpy(ref_uniform(K * N, 123 + i)).cuda() for i in range(ns)]
+    Cs = [torch.zeros(M * N, device="cuda") for _ in range(ns)]
     d = dn.desc(M, N, K, K, N, N)
-    for i in range(N_SETS):
+    for i in range(ns):
         dn.check(dn.cuda_gemm("f32", d, As[i], Bs[i], Cs[i], s))
-    fns = [lambda i=i: dn.cuda_gemm("f32", d, As[i], Bs[i], Cs[i], s) for i in range(N_SETS)]
+    fns = [lambda i=i: dn.cuda_gemm("f32", d, As[i], Bs[i], Cs[i], s) for i in range(ns)]
     r = bench_single(torch, dn, s, fns, gemm_bytes(M, N, K, 0.0), 2.0 * M * N * K)
     out["c1_fp32_1x4096x4096"] = {"GFLOP_s": r["TFLOP_s"] * 1e3, "us": r["us_per_call"],
                                   "GB_s": r["GB_s"], "hbm_frac": r["GB_s"] / pk["hbm_gbs"],
-                                  "kernel": dn.plan_describe(dn.KIND_F32, d)}
+                                  "input_sets": ns, "kernel": dn.plan_describe(dn.KIND_F32, d)}
     del As, Bs, Cs
     # The oneDNN entry on an inner-product pattern: column-major C (OC x batch)
     # = W^T-stored weights x activations + bias, through dnnopt_cuda_sgemm_colmajor.
     M, N, K = 4096, 1, 4096
-    Ws = [torch.from_numpy(ref_uniform(M * K, 52 + i)).cuda() for i in range(N_SETS)]
-    Xs = [torch.from_numpy(ref_uniform(K * N, 133 + i)).cuda() for i in range(N_SETS)]
-    Ys = [torch.zeros(M * N, device="cuda") for _ in range(N_SETS)]
+    ns = rotating_sets(4 * (M * K + K * N + M * N))
+    Ws = [torch.from_numpy(ref_uniform(M * K, 52 + i)).cuda() for i in range(ns)]
+    Xs = [torch.from_numpy(ref_uniform(K * N, 133 + i)).cuda() for i in range(ns)]
+    Ys = [torch.zeros(M * N, device="cuda") for _ in range(ns)]
     bias = torch.from_numpy(ref_uniform(M, 7)).cuda()
     fns = [lambda i=i: dn.cuda_sgemm_colmajor("T", "N", M, N, K, 1.0, Ws[i], K, Xs[i], K, 0.0, Ys[i], M,
-                                              bias, s) for i in range(N_SETS)]
+                                              bias, s) for i in range(ns)]
     for f in fns:
         dn.check(f())
     r = bench_single(torch, dn, s, fns, 4 * (M * K + K * N + M * N + M), 2.0 * M * N * K)
@@ -335,33 +344,35 @@ def per_config(torch, dn, stream, pk, world, rank, dist):
     del cin, cflt, cbias, cout
     # C3: INT8 4 x 11008 x 4096, B is [N, K].
     M, N, K = 4, 11008, 4096
-    As = [torch.from_numpy(int8_uniform(M * K, 42 + i)).cuda() for i in range(N_SETS)]
-    Bs = [torch.from_numpy(int8_uniform(N * K, 123 + i)).cuda() for i in range(N_SETS)]
-    Cs = [torch.zeros(M * N, dtype=torch.int32, device="cuda") for _ in range(N_SETS)]
+    ns = rotating_sets(M * K + N * K + 4 * M * N)
+    As = [torch.from_numpy(int8_uniform(M * K, 42 + i)).cuda() for i in range(ns)]
+    Bs = [torch.from_numpy(int8_uniform(N * K, 123 + i)).cuda() for i in range(ns)]
+    Cs = [torch.zeros(M * N, dtype=torch.int32, device="cuda") for _ in range(ns)]
     d = dn.desc(M, N, K, K, K, N)
-    for i in range(N_SETS):
+    for i in range(ns):
         dn.check(dn.cuda_gemm("s8s32", d, As[i], Bs[i], Cs[i], s))
-    fns = [lambda i=i: dn.cuda_gemm("s8s32", d, As[i], Bs[i], Cs[i], s) for i in range(N_SETS)]
+    fns = [lambda i=i: dn.cuda_gemm("s8s32", d, As[i], Bs[i], Cs[i], s) for i in range(ns)]
     r = bench_single(torch, dn, s, fns, M * K + N * K + 4 * M * N, 2.0 * M * N * K)
     out["c3_int8_4x11008x4096"] = {"TOPS": r["TFLOP_s"], "us": r["us_per_call"], "GB_s": r["GB_s"],
-                                   "hbm_frac": r["GB_s"] / pk["hbm_gbs"],
+                                   "hbm_frac": r["GB_s"] / pk["hbm_gbs"], "input_sets": ns,
                                    "kernel": dn.plan_describe(dn.KIND_S8S32, d)}
     del As, Bs, Cs
     # C4: BF16 65536 x 64 x 256 -> FP32.
     M, N, K = 65536, 64, 256
+    ns = rotating_sets(2 * (M * K + K * N) + 4 * M * N)
     rng = np.random.default_rng(42)
     As = [torch.from_numpy(bf16_bits(rng.standard_normal(M * K).astype(np.float32)).view(np.int16)).cuda()
-          for _ in range(N_SETS)]
+          for _ in range(ns)]
     Bs = [torch.from_numpy(bf16_bits(rng.standard_normal(K * N).astype(np.float32)).view(np.int16)).cuda()
-          for _ in range(N_SETS)]
-    Cs = [torch.zeros(M * N, device="cuda") for _ in range(N_SETS)]
+          for _ in range(ns)]
+    Cs = [torch.zeros(M * N, device="cuda") for _ in range(ns)]
     d = dn.desc(M, N, K, K, N, N)
-    for i in range(N_SETS):
+    for i in range(ns):
         dn.check(dn.cuda_gemm("bf16f32", d, As[i], Bs[i], Cs[i], s))
-    fns = [lambda i=i: dn.cuda_gemm("bf16f32", d, As[i], Bs[i], Cs[i], s) for i in range(N_SETS)]
+    fns = [lambda i=i: dn.cuda_gemm("bf16f32", d, As[i], Bs[i], Cs[i], s) for i in range(ns)]
     r = bench_single(torch, dn, s, fns, 2 * (M * K + K * N) + 4 * M * N, 2.0 * M * N * K)
     out["c4_bf16_65536x64x256"] = {"TFLOP_s": r["TFLOP_s"], "us": r["us_per_call"], "GB_s": r["GB_s"],
-                                   "hbm_frac": r["GB_s"] / pk["hbm_gbs"],
+                                   "hbm_frac": r["GB_s"] / pk["hbm_gbs"], "input_sets": ns,
                                    "tensor_frac": r["TFLOP_s"] / pk["bf16_tflops"],
                                    "kernel": dn.plan_describe(dn.KIND_BF16F32, d)}
     del As, Bs, Cs
@@ -382,10 +393,40 @@ def per_config(torch, dn, stream, pk, world, rank, dist):
     out["c5_e4m3_8x28672x8192"] = {"TFLOP_s": r["TFLOP_s"], "us": r["us_per_call"], "GB_s": r["GB_s"],
                                    "hbm_frac": r["GB_s"] / pk["hbm_gbs"],
                                    "kernel": dn.plan_describe(dn.KIND_E4M3BF16, d)}
-    # C5 sharded over the ranks when world > 1: the fused GEMM + all-gather
-    # (peer-memory stores inside the GEMM kernel) and, for comparison, the
-    # shard GEMM followed by an NCCL all-gather.
-    if world > 1:
+    # C5 N-sharded over the ranks (BASELINE: 1/2/4/8 GPUs): the fused GEMM +
+    # all-gather (peer-memory stores inside the GEMM kernel), the shard GEMM
+    # followed by an NCCL all-gather, the shard GEMM alone, and the full GEMM
+    # on one GPU, all timed the same way, so that speed-up and efficiency
+    # against one GPU come from one run.
+    def queued_us(call, n=100):
+        """Device time per call of n back-to-back calls: the stream first
+        spins for ~20 ms so that the host has queued every call before the
+        first event (an eager Python call costs more host time than the GPU
+        work at 4-8 ranks), max over ranks."""
+        for _ in range(3):
+            call(0)
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(40_000_000)
+        e0.record()
+        for i in range(n):
+            call(i)
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / n], device="cuda")
+        if dist is not None:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item()) * 1e3
+
+    full_us = queued_us(lambda i: dn.check(dn.cuda_gemm("e4m3bf16", d, A, W, C, s, scale=scale)))
+    sharded = {"ranks": world, "full_1gpu_us": full_us,
+               "timing": "device time per call, 100 calls queued behind a GPU sleep, max over ranks"}
+    if world == 1:
+        sharded.update({"us": full_us, "speedup_vs_1gpu": 1.0, "efficiency": 1.0,
+                        "kernel": dn.plan_describe(dn.KIND_E4M3BF16, d)})
+    else:
         from dnnopt_b200.sharded import ShardedE4M3Gemm  # noqa: E402
         Am = A.view(M, K)
         res = {}
@@ -402,38 +443,31 @@ def per_config(torch, dn, stream, pk, world, rank, dist):
                 bufs = dict(C_local=torch.empty((M, sh.n_local), dtype=torch.int16, device="cuda"),
                             gathered=torch.empty((world, M, sh.n_local), dtype=torch.int16, device="cuda"),
                             out=torch.empty((M, N), dtype=torch.int16, device="cuda"))
-            for i in range(3):
-                outC = sh.forward(Am, Ws[i % n_copies], sl, **bufs)
-            torch.cuda.synchronize()
-            dist.barrier()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            # Device time of 100 back-to-back calls: the stream first spins for
-            # ~20 ms so that the host has queued every call before the first
-            # event (the eager Python call costs more host time than the GPU
-            # work at 4-8 ranks; the single-GPU configs are timed in graphs).
-            # The ranks' skew at the end of the spin is paid once.
-            torch.cuda._sleep(40_000_000)
-            e0.record()
-            for i in range(100):
-                outC = sh.forward(Am, Ws[i % n_copies], sl, **bufs)
-            e1.record()
-            torch.cuda.synchronize()
-            t = torch.tensor([e0.elapsed_time(e1) / 100], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            res[mode] = (float(t.item()) * 1e3, outC.reshape(-1).clone())
+            holder = {}
+
+            def call(i, sh=sh, Ws=Ws, sl=sl, bufs=bufs, holder=holder, n_copies=n_copies):
+                holder["out"] = sh.forward(Am, Ws[i % n_copies], sl, **bufs)
+            res[mode] = (queued_us(call), holder["out"].reshape(-1).clone())
             if mode == "fused":
                 ok_status = dn.stream_status(torch.cuda.current_stream()) == dn.SUCCESS
+                # The shard GEMM alone (no all-gather), same rotating shards.
+                ds = dn.desc(M, r1 - r0, K, K, K, r1 - r0)
+                Cl = torch.empty(M * (r1 - r0), dtype=torch.int16, device="cuda")
+                shard_us = queued_us(lambda i: dn.check(dn.cuda_gemm("e4m3bf16", ds, A, Ws[i % n_copies], Cl, s,
+                                                                     scale=sl)))
             sh.close()
             del Ws
         us = res["fused"][0]
-        out["c5_sharded"] = {
-            "ranks": world, "us": us, "TFLOP_s": 2.0 * M * N * K / us / 1e6,
+        sharded.update({
+            "us": us, "TFLOP_s": 2.0 * M * N * K / us / 1e6,
+            "speedup_vs_1gpu": full_us / us, "efficiency": full_us / us / world,
             "GB_s_per_gpu": (N * K / world + 4 * N / world + 2 * M * K + 2 * M * N) / us / 1e3,
             "kernel": "gemm_e4m3_tcgen05 with peer-memory all-gather epilogue + bounded flag wait",
-            "nccl_allgather_us": res["nccl"][0],
+            "nccl_allgather_us": res["nccl"][0], "nccl_speedup_vs_1gpu": full_us / res["nccl"][0],
+            "shard_gemm_alone_us": shard_us,
             "matches_nccl_path": bool(torch.equal(res["fused"][1], res["nccl"][1])) and ok_status,
-            "timing": "device time per call, 100 calls queued behind a GPU sleep, max over ranks",
-            "shard_plan": dn.plan_describe(dn.KIND_E4M3BF16, dn.desc(M, N // world, K, K, K, N // world))}
+            "shard_plan": dn.plan_describe(dn.KIND_E4M3BF16, dn.desc(M, N // world, K, K, K, N // world))})
+    out["c5_sharded"] = sharded
     return out
 
 

@@ -50,8 +50,12 @@ DeviceInfo info_of(const DeviceContext* ctx) {
 }
 
 // Kernels for a K x N B with M <= 8 (one plan family: interchangeable under autotune).
+// Dot-form kernels with A in registers (interchangeable under autotune).
+bool is_rows(KernelId k) { return k == KernelId::GemvRows || k == KernelId::GemvRowsBulk; }
+
 bool is_kn(KernelId k) {
-    return k == KernelId::GemvKn || k == KernelId::GemvKnCluster || k == KernelId::GemvSlab;
+    return k == KernelId::GemvKn || k == KernelId::GemvKnCluster || k == KernelId::GemvSlab ||
+           k == KernelId::GemvPanel;
 }
 
 int vec_of(const Plan& p) {
@@ -123,12 +127,29 @@ int launch_plan(Kind kind, const GemmArgs& g, const Plan& p, const float* scales
             e = launch_gemv_slab(in_a(kind), in_b(kind), g, p.kn.mt, p.slab_w, s);
             note_launch();
             break;
+        case KernelId::GemvPanel: {
+            GemvKnPlan kp = p.kn;
+            if (kind != Kind::F32 || !gemv_panel_supported(g, kp.mt, p.panel_w, p.panel_splits))
+                return set_status(DNNOPT_STATUS_NOT_SUPPORTED);
+            st = ensure_workspace(ctx, s, gemv_panel_ws_floats(g.N, kp.mt, p.panel_w, p.panel_splits),
+                                  static_cast<size_t>(gemv_panel_tickets(g.N, p.panel_w)), 0, &w);
+            if (st != DNNOPT_STATUS_SUCCESS) return st;
+            e = launch_gemv_panel(g, kp.mt, p.panel_w, p.panel_splits, w->ws, w->counters, s);
+            note_launch();
+            break;
+        }
         case KernelId::GemvNk:
             e = launch_gemv_nk(dot_kind(kind), g, p.nk, scales, s);
             note_launch();
             break;
         case KernelId::GemvRows:
             e = launch_gemv_rows(dot_kind(kind), g, p.nk.mt, p.nk.grid, scales, s);
+            note_launch();
+            break;
+        case KernelId::GemvRowsBulk:
+            st = ensure_workspace(ctx, s, 0, 0, 0, &w);
+            if (st != DNNOPT_STATUS_SUCCESS) return st;
+            e = launch_gemv_rows_bulk(dot_kind(kind), g, p.nk.mt, p.nk.grid, scales, w->err, s);
             note_launch();
             break;
         case KernelId::GemvNkRows: {
@@ -225,24 +246,42 @@ Plan get_plan(Kind kind, const GemmArgs& g, DeviceContext* ctx, cudaStream_t s,
               const float* scales) {
     const DeviceInfo info = info_of(ctx);
     Plan h = heuristic_plan(kind, g, info);
-    const bool tunable = is_kn(h.kernel) || h.kernel == KernelId::GemvNk ||
+    const bool tunable = is_kn(h.kernel) || h.kernel == KernelId::GemvNk || h.kernel == KernelId::GemvRowsBulk ||
                          h.kernel == KernelId::E4m3Tc;
     if (!tunable) return h;
     const uint64_t key = plan_key(kind, g, vec_of(h));
     Plan c = h;
-    if (cache_lookup(key, &c) && (c.kernel == h.kernel || (is_kn(c.kernel) && is_kn(h.kernel)))) {
+    if (cache_lookup(key, &c) && (c.kernel == h.kernel || (is_kn(c.kernel) && is_kn(h.kernel)) ||
+                                  (is_rows(c.kernel) && is_rows(h.kernel)))) {
         // Layout-derived fields come from the current call.
         if (is_kn(c.kernel)) c.kn.vec4 = h.kn.vec4;
         else if (c.kernel != KernelId::E4m3Tc) c.nk.vec = h.nk.vec;
+        // A loaded plan that does not fit this call (a hand-written or stale
+        // file) gives way to the heuristic one.
+        if (c.kernel == KernelId::GemvPanel &&
+            (kind != Kind::F32 || !gemv_panel_supported(g, c.kn.mt, c.panel_w, c.panel_splits)))
+            return h;
         return c;
     }
     if (!autotune_enabled() || !ctx) return h;
 
     // Candidates around the heuristic choice.
-    constexpr int kMaxCands = 16;
+    constexpr int kMaxCands = 24;
     Plan cands[kMaxCands];
     int nc = 0;
     if (is_kn(h.kernel)) {
+        if (kind == Kind::F32) {
+            for (int pw : {64, 128})
+                for (int ps : {1, 2, 4, 8}) {
+                    if (!gemv_panel_supported(g, h.kn.mt, pw, ps) || nc >= kMaxCands - 8) continue;
+                    Plan q = h;
+                    q.kernel = KernelId::GemvPanel;
+                    q.kn = kn_plan_for(kind, g, info, 0, false);
+                    q.panel_w = pw;
+                    q.panel_splits = ps;
+                    cands[nc++] = q;
+                }
+        }
         for (int w : {8, 16}) {
             Plan slab = h;
             slab.kernel = KernelId::GemvSlab;
@@ -283,6 +322,27 @@ Plan get_plan(Kind kind, const GemmArgs& g, DeviceContext* ctx, cudaStream_t s,
                     dup = dup || (cands[i].e4.splits == q.e4.splits && cands[i].e4.stages == q.e4.stages);
                 if (!dup && nc < kMaxCands) cands[nc++] = q;
             }
+    } else if (h.kernel == KernelId::GemvRowsBulk) {
+        // Bulk-copy rows kernel at its occupancy grid and half of it, and the
+        // register-load rows kernel at its own occupancy grid.
+        const int g0 = h.nk.grid;
+        for (int t : {g0, g0 / 2}) {
+            if (t < 1) continue;
+            Plan q = h;
+            q.nk.grid = t;
+            cands[nc++] = q;
+        }
+        if (gemv_rows_supported(dot_kind(kind), g)) {
+            Plan q = h;
+            q.kernel = KernelId::GemvRows;
+            int occ = 1;
+            if (gemv_rows_occupancy(dot_kind(kind), h.nk.mt, g.K, &occ) != cudaSuccess || occ < 1) {
+                cudaGetLastError();
+                occ = 1;
+            }
+            q.nk.grid = occ * info.num_sms;
+            cands[nc++] = q;
+        }
     } else {
         const int g0 = h.nk.grid;
         const int tries[3] = {g0, g0 / 2, g0 * 2};

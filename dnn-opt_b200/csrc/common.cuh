@@ -140,6 +140,17 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, ui
         : "memory");
 }
 
+// Untiled bulk copy global -> this CTA's shared memory, completing on `bar`
+// (complete_tx).  Both addresses 16-byte aligned, `bytes` a multiple of 16.
+// Efficient for copies of a few KB; at ~0.5 KB the per-copy cost dominates.
+__device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* gsrc, uint32_t bytes,
+                                             uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_u32(smem_dst)), "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ void tma_store_2d(const void* tmap, const void* smem_src, int32_t x,
                                              int32_t y) {
     asm volatile(

@@ -378,6 +378,182 @@ gemv_rows_kernel(const RowsParams p) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// Bulk-copy variant of the register-resident dot form (gemv_rows_bulk): the
+// same lane -> 16-byte K-chunk ownership (A in registers) and the same
+// transpose-reduce, but B's rows reach the CTA through a ring of shared-memory
+// stages of R rows, filled by a ninth (producer) warp with cp.async.bulk: one
+// copy per stage when the rows are dense in memory (ldb == K), else one per
+// row.  The bytes in flight then cost no registers (two CTAs per SM keep up
+// to six stages, 192 KB, in flight per SM), and the consumer warps release a
+// stage on an mbarrier as soon as their reads of it are done, before the
+// reduction.  Every wait is bounded (kMbarTimeoutNs); a timeout records an
+// error word and the remaining waits give up.
+// ---------------------------------------------------------------------------
+constexpr int kBulkThreads = kThreads + 32;   // 8 consumer warps + 1 producer warp
+constexpr int kBulkMaxStages = 6;
+
+struct RowsBulkParams {
+    GemmArgs g;
+    int rows_per_cta;      // multiple of R
+    int stages;            // ring depth (2..kBulkMaxStages)
+    uint32_t row_bytes;    // K * element size (a multiple of 16)
+    const float* scales;
+    uint32_t* err;
+};
+
+template <DotKind KIND, int MT, int R, int KCH>
+__global__ void __launch_bounds__(kBulkThreads, 1)
+gemv_rows_bulk_kernel(const RowsBulkParams p) {
+    using C = Chunk<KIND>;
+    using Acc = typename C::Acc;
+    using TA = typename Tr<KIND>::TA;
+    constexpr int V = MT * R;
+    static_assert(V == 8 || V == 16 || V == 32, "V values per lane, a power of two up to 32");
+    extern __shared__ __align__(128) unsigned char stage_mem[];
+    __shared__ __align__(8) uint64_t full[kBulkMaxStages];
+    __shared__ __align__(8) uint64_t empty[kBulkMaxStages];
+    __shared__ Acc red[2][kWarps][32];
+    __shared__ uint32_t abort_flag;
+
+    const GemmArgs& g = p.g;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int row_begin = blockIdx.x * p.rows_per_cta;
+    const int row_end = min(g.N, row_begin + p.rows_per_cta);
+    const int ngroups = row_begin < row_end ? (row_end - row_begin + R - 1) / R : 0;
+    const uint32_t stage_bytes = static_cast<uint32_t>(R) * p.row_bytes;
+
+    if (tid == 0) {
+        for (int s = 0; s < p.stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kWarps);
+        }
+        abort_flag = 0u;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    pdl_wait();
+    pdl_launch_dependents();
+
+    if (warp == kWarps) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            const unsigned char* Bb = static_cast<const unsigned char*>(g.B);
+            const int64_t ldb_bytes = g.ldb * static_cast<int64_t>(sizeof(typename Tr<KIND>::TB));
+            const bool dense = ldb_bytes == static_cast<int64_t>(p.row_bytes);
+            for (int j = 0; j < ngroups; ++j) {
+                const int s = j % p.stages;
+                if (j >= p.stages &&
+                    !mbar_wait(&empty[s], static_cast<uint32_t>(j / p.stages - 1) & 1u, &abort_flag, p.err))
+                    break;
+                const int r0 = row_begin + j * R;
+                const int nr = min(R, row_end - r0);
+                mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nr) * p.row_bytes);
+                unsigned char* dst = stage_mem + static_cast<size_t>(s) * stage_bytes;
+                if (dense) {
+                    bulk_load_1d(dst, Bb + r0 * ldb_bytes, static_cast<uint32_t>(nr) * p.row_bytes, &full[s]);
+                } else {
+                    for (int r = 0; r < nr; ++r)
+                        bulk_load_1d(dst + static_cast<size_t>(r) * p.row_bytes, Bb + (r0 + r) * ldb_bytes,
+                                     p.row_bytes, &full[s]);
+                }
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumers (warps 0..7) ----------------
+    const int nchunks = g.K / C::EPC;
+    const TA* A = static_cast<const TA*>(g.A);
+    uint4 a[KCH][MT];
+#pragma unroll
+    for (int j = 0; j < KCH; ++j) {
+        const int ch = tid + j * kThreads;
+#pragma unroll
+        for (int m = 0; m < MT; ++m)
+            a[j][m] = (m < g.M && ch < nchunks)
+                          ? load_a_chunk<TA>(A, g.lda, g.a_trans, m, ch * C::EPC, g.K)
+                          : make_uint4(0u, 0u, 0u, 0u);
+    }
+    int buf = 0;
+    for (int j = 0; j < ngroups; ++j, buf ^= 1) {
+        const int s = j % p.stages;
+        const bool ok = mbar_wait(&full[s], static_cast<uint32_t>(j / p.stages) & 1u, &abort_flag, p.err);
+        const int r0 = row_begin + j * R;
+        Acc v[V];
+#pragma unroll
+        for (int i = 0; i < V; ++i) v[i] = Acc(0);
+        if (ok) {
+            const unsigned char* st = stage_mem + static_cast<size_t>(s) * stage_bytes;
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                uint4 b[KCH];
+#pragma unroll
+                for (int kc = 0; kc < KCH; ++kc) {
+                    const int ch = tid + kc * kThreads;
+                    b[kc] = ch < nchunks ? *reinterpret_cast<const uint4*>(st + r * p.row_bytes + ch * 16)
+                                         : make_uint4(0u, 0u, 0u, 0u);
+                }
+#pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                    Acc acc = Acc(0);
+#pragma unroll
+                    for (int kc = 0; kc < KCH; ++kc) acc = C::dot(b[kc], a[kc][m], acc);
+                    v[m * R + r] = acc;
+                }
+            }
+        }
+        // This warp is done with the stage.
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+        for (int sh = V / 2; sh >= 1; sh >>= 1) {
+            const bool upper = (lane & sh) != 0;
+#pragma unroll
+            for (int i = 0; i < sh; ++i) {
+                Acc send = upper ? v[i] : v[i + sh];
+                Acc keep = upper ? v[i + sh] : v[i];
+                v[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, sh);
+            }
+        }
+#pragma unroll
+        for (int o = V; o < 32; o <<= 1) v[0] += __shfl_xor_sync(0xFFFFFFFFu, v[0], o);
+        red[buf][warp][lane] = v[0];
+        named_barrier_sync(1, kThreads);
+        if (warp == 0 && lane < V && ok) {
+            Acc t = red[buf][0][lane];
+#pragma unroll
+            for (int w = 1; w < kWarps; ++w) t += red[buf][w][lane];
+            const int m = lane / R, n = r0 + (lane % R);
+            if (m < g.M && n < row_end) {
+                if constexpr (KIND == DotKind::F32 || KIND == DotKind::BF16) {
+                    float* cp = static_cast<float*>(g.C) + (int64_t)m * g.ldc + n;
+                    *cp = add_bias((g.beta == 0.0f) ? g.alpha * t : fmaf(g.alpha, t, g.beta * *cp), g.bias, n);
+                } else if constexpr (KIND == DotKind::S8S32) {
+                    static_cast<int32_t*>(g.C)[(int64_t)m * g.ldc + n] = t;
+                } else {
+                    float* cp = static_cast<float*>(g.C) + (int64_t)m * g.ldc + n;
+                    float scale = __fmul_rn(g.alpha, __fmul_rn(p.scales[0], p.scales[1]));
+                    float c0 = (g.beta == 0.0f) ? 0.0f : __fmul_rn(g.beta, *cp);
+                    *cp = __fadd_rn(c0, __fmul_rn(scale, static_cast<float>(t)));
+                }
+            }
+        }
+        // red[buf] is rewritten two groups later, after the next barrier.
+    }
+}
+
+template <DotKind KIND, int KCH>
+const void* rows_bulk_select_mt(int mt) {
+    switch (mt) {
+        case 1:
+        case 2:
+        case 4: return reinterpret_cast<const void*>(&gemv_rows_bulk_kernel<KIND, 4, 8, KCH>);
+        case 8: return reinterpret_cast<const void*>(&gemv_rows_bulk_kernel<KIND, 8, 4, KCH>);
+        default: return nullptr;
+    }
+}
+
 template <DotKind KIND, int KCH>
 const void* rows_select_mt(int mt) {
     switch (mt) {
@@ -548,6 +724,105 @@ cudaError_t launch_gemv_rows(DotKind kind, const GemmArgs& g, int mt, int grid, 
     cfg.numAttrs = 1;
     void* args[] = {&rp};
     return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+// ---- bulk-copy rows kernel -------------------------------------------------
+namespace {
+
+struct RowsBulkCfg {
+    const void* fn;
+    int R;
+    int stages;
+    uint32_t row_bytes;
+    size_t smem;
+};
+
+// K of at most 2 x 256 chunks; stage depth for two CTAs per SM (96 KB each)
+// when a stage is at most 48 KB, else one CTA per SM (200 KB).
+RowsBulkCfg rows_bulk_cfg(DotKind kind, int mt, int K) {
+    RowsBulkCfg c{nullptr, 0, 0, 0, 0};
+    const int kch = (K / epc(kind) + kThreads - 1) / kThreads;
+    if (kch < 1 || kch > 2) return c;
+    switch (kind) {
+        case DotKind::F32: c.fn = kch == 1 ? rows_bulk_select_mt<DotKind::F32, 1>(mt) : rows_bulk_select_mt<DotKind::F32, 2>(mt); break;
+        case DotKind::BF16: c.fn = kch == 1 ? rows_bulk_select_mt<DotKind::BF16, 1>(mt) : rows_bulk_select_mt<DotKind::BF16, 2>(mt); break;
+        case DotKind::S8S32: c.fn = kch == 1 ? rows_bulk_select_mt<DotKind::S8S32, 1>(mt) : rows_bulk_select_mt<DotKind::S8S32, 2>(mt); break;
+        case DotKind::S8DQ: c.fn = kch == 1 ? rows_bulk_select_mt<DotKind::S8DQ, 1>(mt) : rows_bulk_select_mt<DotKind::S8DQ, 2>(mt); break;
+        default: return c;
+    }
+    if (!c.fn) return c;
+    c.R = mt <= 4 ? 8 : 4;
+    const size_t eb = kind == DotKind::F32 ? 4 : (kind == DotKind::BF16 ? 2 : 1);
+    c.row_bytes = static_cast<uint32_t>(static_cast<size_t>(K) * eb);
+    const size_t stage = static_cast<size_t>(c.R) * c.row_bytes;
+    const size_t budget = stage <= 48 * 1024 ? 96 * 1024 : 200 * 1024;
+    int st = static_cast<int>(budget / stage);
+    st = st > kBulkMaxStages ? kBulkMaxStages : st;
+    if (st < 2) { c.fn = nullptr; return c; }
+    c.stages = st;
+    c.smem = static_cast<size_t>(st) * stage;
+    return c;
+}
+
+cudaError_t prepare_rows_bulk(const void* fn) {
+    static std::mutex mu;
+    static std::set<std::pair<int, const void*>> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(mu);
+    if (done.count({dev, fn})) return cudaSuccess;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e == cudaSuccess) done.insert({dev, fn});
+    return e;
+}
+
+}  // namespace
+
+bool gemv_rows_bulk_supported(DotKind kind, const GemmArgs& g) {
+    return gemv_rows_supported(kind, g) && rows_bulk_cfg(kind, 8, g.K).fn != nullptr &&
+           rows_bulk_cfg(kind, 4, g.K).fn != nullptr;
+}
+
+cudaError_t gemv_rows_bulk_occupancy(DotKind kind, int mt, int K, int* blocks_per_sm) {
+    const RowsBulkCfg c = rows_bulk_cfg(kind, mt, K);
+    if (!c.fn) return cudaErrorInvalidValue;
+    cudaError_t e = prepare_rows_bulk(c.fn);
+    if (e != cudaSuccess) return e;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, c.fn, kBulkThreads, c.smem);
+}
+
+cudaError_t launch_gemv_rows_bulk(DotKind kind, const GemmArgs& g, int mt, int grid, const float* scales,
+                                  uint32_t* err, cudaStream_t s) {
+    if (!gemv_rows_bulk_supported(kind, g) || g.M > mt) return cudaErrorInvalidValue;
+    const RowsBulkCfg c = rows_bulk_cfg(kind, mt, g.K);
+    if (!c.fn) return cudaErrorInvalidValue;
+    cudaError_t e = prepare_rows_bulk(c.fn);
+    if (e != cudaSuccess) return e;
+    const int groups = (g.N + c.R - 1) / c.R;
+    if (grid < 1) grid = 1;
+    if (grid > groups) grid = groups;
+    const int per = (groups + grid - 1) / grid;
+    RowsBulkParams rp;
+    rp.g = g;
+    rp.rows_per_cta = per * c.R;
+    rp.stages = c.stages;
+    rp.row_bytes = c.row_bytes;
+    rp.scales = scales;
+    rp.err = err;
+    const int blocks = (g.N + rp.rows_per_cta - 1) / rp.rows_per_cta;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks, 1, 1);
+    cfg.blockDim = dim3(kBulkThreads, 1, 1);
+    cfg.dynamicSmemBytes = c.smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void* args[] = {&rp};
+    return cudaLaunchKernelExC(&cfg, c.fn, args);
 }
 
 }  // namespace dnnopt_b200

@@ -69,6 +69,22 @@ int gemv_slab_ctas(int N, int w);
 cudaError_t gemv_slab_occupancy(In ia, In ib, int mt, int w, int K, int* blocks_per_sm);
 cudaError_t launch_gemv_slab(In ia, In ib, const GemmArgs& g, int mt, int w, cudaStream_t s);
 
+// ---- small-M row-panel GEMV, FP32, B is K x N ------------------------------
+// A CTA owns a panel of `w` (64 or 128) columns and one of `splits` (1, 2,
+// 4, 8) K-ranges of gemv_panel_rows(K, splits) rows, read as whole row
+// segments (4w bytes) per warp.  splits > 1: partial panels go to `ws`
+// (gemv_panel_ws_floats) and the last CTA of each panel (ticket in
+// `counters`, gemv_panel_tickets of them, zero on entry and left zero) sums
+// them in split order.  Launched with programmatic dependent launch.
+int gemv_panel_rows(int K, int splits);
+bool gemv_panel_supported(const GemmArgs& g, int mt, int w, int splits);
+int gemv_panel_ctas(int N, int w, int splits);
+size_t gemv_panel_ws_floats(int N, int mt, int w, int splits);
+int gemv_panel_tickets(int N, int w);
+cudaError_t gemv_panel_occupancy(int mt, int w, int rows, int* blocks_per_sm);
+cudaError_t launch_gemv_panel(const GemmArgs& g, int mt, int w, int splits, float* ws, uint32_t* counters,
+                              cudaStream_t s);
+
 // ---- small-M dot-form GEMV, B is N x K (K contiguous) ----------------------
 enum class DotKind : int {
     F32 = 0,     // fp32 x fp32 -> fp32, alpha/beta epilogue
@@ -97,6 +113,16 @@ bool gemv_rows_supported(DotKind kind, const GemmArgs& g);
 cudaError_t gemv_rows_occupancy(DotKind kind, int mt, int K, int* blocks_per_sm);
 cudaError_t launch_gemv_rows(DotKind kind, const GemmArgs& g, int mt, int grid, const float* scales,
                              cudaStream_t s);
+
+// Bulk-copy variant of the register-resident dot form (F32 / BF16 / S8S32 /
+// S8DQ, same preconditions, K of at most 2 x 256 chunks): B rows reach the
+// CTA through a ring of shared-memory stages filled with cp.async.bulk by a
+// producer warp.  `err` receives a KernelErrorCode when a bounded wait gives
+// up (may be null).
+bool gemv_rows_bulk_supported(DotKind kind, const GemmArgs& g);
+cudaError_t gemv_rows_bulk_occupancy(DotKind kind, int mt, int K, int* blocks_per_sm);
+cudaError_t launch_gemv_rows_bulk(DotKind kind, const GemmArgs& g, int mt, int grid, const float* scales,
+                                  uint32_t* err, cudaStream_t s);
 
 // ---- general tiled SIMT kernels (any M, N, K, strides, transposes) ----------
 // General FP32-accumulate GEMM on the CUDA cores (gemm_simt.cu): BM x BN

@@ -2,6 +2,10 @@
 //
 // Dispatch rules (B200 re-statement of src/gemm/gemm.cpp:168-455, where the
 // reference routes by M < small_m_bound (8), N >= wide_n_bound and K):
+//   * FP32, M <= 8, B stored K x N, N >= 512, K <= 2048
+//                                    -> GemvPanel (128-column panels, row
+//                                      segments by bulk copy, K ranges reduced
+//                                      in a cluster)
 //   * M <= 8 and B stored K x N      -> GemvSlab (whole K per 8-column CTA) for
 //                                      K <= 2048 and 512 <= N <= 8192, where a
 //                                      split-K reduction costs more than the B
@@ -10,7 +14,10 @@
 //                                      CTA) or, when autotune measures it faster,
 //                                      GemvKnCluster (splits reduced in a
 //                                      thread-block cluster) or GemvSlab
-//   * M <= 8 and B stored N x K      -> GemvNk  (dot-form GEMV; all int8 calls)
+//   * int8, M <= 8, B stored N x K, 16-byte rows of at most 512 chunks
+//                                    -> GemvRowsBulk (dot form, A in registers,
+//                                      B rows by bulk copy into a shared ring)
+//   * M <= 8 and B stored N x K      -> GemvRows / GemvNk (dot-form GEMV)
 //   * BF16, large M, N <= 256        -> Bf16Tc  (tcgen05 tall-skinny)
 //   * config-5 e4m3 with M > 8       -> GemvNkRows (dot form per 8-row block)
 //   * anything else                  -> TileF32 / TileS8 (general SIMT tiles)
@@ -118,6 +125,12 @@ int slab_occupancy(Kind kind, int mt, int w, int K, const DeviceInfo& info) {
     });
 }
 
+int rows_bulk_occupancy(DotKind kind, int mt, int K, const DeviceInfo& info) {
+    if (!info.have_device) return 2;
+    const int64_t key = (static_cast<int64_t>(kind) * 16 + mt) * (int64_t{1} << 31) + K;
+    return memo_occupancy(key * 8 + 5, [&](int* occ) { return gemv_rows_bulk_occupancy(kind, mt, K, occ); });
+}
+
 int rows_occupancy(DotKind kind, int mt, int K, const DeviceInfo& info) {
     if (!info.have_device) return 4;
     const int64_t key = (static_cast<int64_t>(kind) * 16 + mt) * (int64_t{1} << 31) + K;
@@ -128,6 +141,20 @@ int nk_occupancy(DotKind kind, int mt, int vec, int K, const DeviceInfo& info) {
     if (!info.have_device) return 2;
     const int64_t key = ((static_cast<int64_t>(kind) * 16 + mt) * 2 + vec) * (int64_t{1} << 31) + K;
     return memo_occupancy(key * 4 + 3, [&](int* occ) { return gemv_nk_occupancy(kind, mt, vec, K, occ); });
+}
+
+// Row-panel GEMV (FP32, B K x N): 128-column panels and the K extent split
+// into power-of-two ranges of about 128 rows (at most 8, one cluster), so a
+// 1024-row B gives 8 CTAs per panel that each keep three 32-row stages of
+// bulk copies in flight.  Deep K (above 2048) stays with split-K.
+bool panel_plan(const GemmArgs& g, int* w, int* splits) {
+    if (g.K > 2048) return false;   // deep K: the split-K kernel (measured at K = 4096)
+    int s = 1;
+    while (s < 8 && g.K / (2 * s) >= 128) s *= 2;
+    if (!gemv_panel_supported(g, mt_for(g.M), 128, s)) return false;
+    *w = 128;
+    *splits = s;
+    return true;
 }
 
 }  // namespace
@@ -168,6 +195,8 @@ const char* kernel_name(KernelId k) {
         case KernelId::GemvRows: return "gemv_rows_dot";
         case KernelId::E4m3Tc: return "gemm_e4m3_tcgen05";
         case KernelId::GemvSlab: return "gemv_kn_slab";
+        case KernelId::GemvPanel: return "gemv_panel";
+        case KernelId::GemvRowsBulk: return "gemv_rows_bulk";
     }
     return "?";
 }
@@ -235,7 +264,12 @@ Plan heuristic_plan(Kind kind, const GemmArgs& g, const DeviceInfo& info) {
     switch (kind) {
         case Kind::S8S32:
         case Kind::F32S8Q:
-            if (g.M <= 8 && gemv_rows_supported(dot_kind(kind), g)) {
+            if (g.M <= 8 && gemv_rows_bulk_supported(dot_kind(kind), g)) {
+                p.kernel = KernelId::GemvRowsBulk;
+                p.nk.mt = mt_for(g.M);
+                p.nk.vec = 1;
+                p.nk.grid = rows_bulk_occupancy(dot_kind(kind), p.nk.mt, g.K, info) * info.num_sms;
+            } else if (g.M <= 8 && gemv_rows_supported(dot_kind(kind), g)) {
                 p.kernel = KernelId::GemvRows;
                 p.nk.mt = mt_for(g.M);
                 p.nk.vec = 1;
@@ -276,7 +310,9 @@ Plan heuristic_plan(Kind kind, const GemmArgs& g, const DeviceInfo& info) {
         // columns on (3 x 2039: 4.9 -> 3.8 us, 2 x 4093: 6.7 -> 6.1 us);
         // 8 otherwise (narrower N keeps more CTAs: 2 x 1009 at 8 columns
         // takes 2.8 us, at 16 3.7 us).
-        if (g.K <= 2048 && g.N >= 512 && g.N <= 8192) {
+        if (kind == Kind::F32 && g.N >= 512 && panel_plan(g, &p.panel_w, &p.panel_splits)) {
+            p.kernel = KernelId::GemvPanel;
+        } else if (g.K <= 2048 && g.N >= 512 && g.N <= 8192) {
             p.kernel = KernelId::GemvSlab;
             const int occ8 = slab_occupancy(kind, p.kn.mt, 8, g.K, info);
             const bool wide = gemv_slab_ctas(g.N, 8) > occ8 * info.num_sms || (p.kn.mt <= 4 && g.N >= 1536);
@@ -324,6 +360,7 @@ std::string describe_plan(Kind, const GemmArgs& g, const Plan& p) {
         case KernelId::GemvNk:
         case KernelId::GemvNkRows:
         case KernelId::GemvRows:
+        case KernelId::GemvRowsBulk:
             std::snprintf(buf, sizeof(buf), "%s mt=%d vec=%d grid=%d%s", kernel_name(p.kernel),
                           p.nk.mt, p.nk.vec, p.nk.grid, p.tuned ? " tuned" : "");
             break;
@@ -334,6 +371,11 @@ std::string describe_plan(Kind, const GemmArgs& g, const Plan& p) {
         case KernelId::GemvSlab:
             std::snprintf(buf, sizeof(buf), "%s mt=%d w=%d ctas=%d%s", kernel_name(p.kernel), p.kn.mt,
                           p.slab_w, gemv_slab_ctas(g.N, p.slab_w), p.tuned ? " tuned" : "");
+            break;
+        case KernelId::GemvPanel:
+            std::snprintf(buf, sizeof(buf), "%s mt=%d w=%d splits=%d ctas=%d%s", kernel_name(p.kernel), p.kn.mt,
+                          p.panel_w, p.panel_splits, gemv_panel_ctas(g.N, p.panel_w, p.panel_splits),
+                          p.tuned ? " tuned" : "");
             break;
         case KernelId::TileF32:
             std::snprintf(buf, sizeof(buf), "%s bm=%d bn=%d splits=%d kchunk=%d", kernel_name(p.kernel),
@@ -432,6 +474,10 @@ bool cache_lookup(uint64_t key, Plan* out) {
     if (out->kernel == KernelId::GemvSlab) {
         out->slab_w = e.p0 == 16 ? 16 : 8;
         out->kn.mt = e.mt;
+    } else if (out->kernel == KernelId::GemvPanel) {
+        out->panel_w = e.p0 == 64 ? 64 : 128;
+        out->panel_splits = e.p1;
+        out->kn.mt = e.mt;
     } else if (out->kernel == KernelId::GemvKn || out->kernel == KernelId::GemvKnCluster) {
         out->kn.splits = e.p0;
         out->kn.kchunk = e.p1;
@@ -453,6 +499,8 @@ void cache_store(uint64_t key, const Plan& p, float time_us) {
     e.kernel = static_cast<int32_t>(p.kernel);
     if (p.kernel == KernelId::GemvSlab) {
         e.p0 = p.slab_w; e.p1 = 0; e.mt = p.kn.mt;
+    } else if (p.kernel == KernelId::GemvPanel) {
+        e.p0 = p.panel_w; e.p1 = p.panel_splits; e.mt = p.kn.mt;
     } else if (p.kernel == KernelId::GemvKn || p.kernel == KernelId::GemvKnCluster) {
         e.p0 = p.kn.splits; e.p1 = p.kn.kchunk; e.mt = p.kn.mt;
     } else if (p.kernel == KernelId::E4m3Tc) {

@@ -34,6 +34,8 @@ enum class KernelId : int {
     GemvRows = 7,   // small-M dot form with A in registers (aligned B rows, K <= 512 chunks)
     E4m3Tc = 8,     // config-5 e4m3 weights on tcgen05 (kind::f8f6f4), 8-row blocks of A
     GemvSlab = 9,   // small-M column slab, B K x N: whole K per CTA, no split-K reduction
+    GemvPanel = 10, // small-M FP32 row panels, B K x N: 512-byte row segments, cluster K reduction
+    GemvRowsBulk = 11,  // GemvRows with B rows staged by bulk copies in a shared-memory ring
 };
 
 struct Plan {
@@ -43,6 +45,8 @@ struct Plan {
     E4m3TcPlan e4{};
     GemmSimtPlan simt{};
     int slab_w = 8;      // GemvSlab: columns per CTA (8 or 16)
+    int panel_w = 128;   // GemvPanel: columns per CTA (128 or 256)
+    int panel_splits = 8;  // GemvPanel: K-ranges per panel = cluster size (1, 2, 4, 8)
     bool tuned = false;
 };
 

@@ -129,12 +129,18 @@ def test_plan_selection_without_device(dn):
     # Dispatch classes of the reference's shape router (src/gemm/gemm.cpp:168-455).
     s = dn.plan_describe(dn.KIND_F32, dn.desc(1, 4096, 4096, 4096, 4096, 4096))
     assert s.startswith("gemv_kn_splitk mt=1 vec4=1"), s
-    # The irregular-N sweep (K = 1024): whole-K column slabs, no split-K reduction.
+    # The irregular-N sweep (K = 1024): 128-column row panels, K in 8 ranges
+    # of 128 rows reduced in a cluster.
     s = dn.plan_describe(dn.KIND_F32, dn.desc(7, 4093, 1024, 1024, 4093, 4093, beta=0.5))
-    assert s == "gemv_kn_slab mt=8 w=8 ctas=512", s
+    assert s == "gemv_panel mt=8 w=128 splits=8 ctas=256", s
     s = dn.plan_describe(dn.KIND_F32, dn.desc(2, 1009, 1024, 1024, 1009, 1009))
-    assert s == "gemv_kn_slab mt=2 w=8 ctas=127", s
-    s = dn.plan_describe(dn.KIND_F32, dn.desc(3, 2039, 1024, 1024, 2039, 2039))
+    assert s == "gemv_panel mt=2 w=128 splits=8 ctas=64", s
+    s = dn.plan_describe(dn.KIND_F32, dn.desc(3, 2039, 600, 600, 2039, 2039))
+    assert s == "gemv_panel mt=4 w=128 splits=4 ctas=64", s   # 600 rows: 4 ranges of 160
+    # Other encodings of the same shapes keep the whole-K column slabs.
+    s = dn.plan_describe(dn.KIND_BF16F32, dn.desc(7, 4093, 1024, 1024, 4093, 4093, beta=0.5))
+    assert s == "gemv_kn_slab mt=8 w=8 ctas=512", s
+    s = dn.plan_describe(dn.KIND_BF16F32, dn.desc(3, 2039, 1024, 1024, 2039, 2039))
     assert s == "gemv_kn_slab mt=4 w=16 ctas=128", s   # M <= 4 from 1536 columns on: 16 wide
     # Deeper K: split-K, one wave of resident CTAs, at most 16 splits.
     s = dn.plan_describe(dn.KIND_F32, dn.desc(7, 4093, 4096, 4096, 4093, 4093, beta=0.5))
@@ -142,7 +148,7 @@ def test_plan_selection_without_device(dn):
     s = dn.plan_describe(dn.KIND_F32, dn.desc(2, 1009, 4096, 4096, 1009, 1009))
     assert s.startswith("gemv_kn_splitk mt=2 vec4=0 splits=16 kchunk=256"), s
     s = dn.plan_describe(dn.KIND_S8S32, dn.desc(4, 11008, 4096, 4096, 4096, 11008))
-    assert s.startswith("gemv_rows_dot mt=4 vec=1"), s
+    assert s.startswith("gemv_rows_bulk mt=4 vec=1"), s
     s = dn.plan_describe(dn.KIND_S8S32, dn.desc(4, 11008, 4100, 4100, 4100, 11008))
     assert s.startswith("gemv_nk_dot mt=4 vec=0"), s      # rows not 16-byte aligned
     s = dn.plan_describe(dn.KIND_E4M3BF16, dn.desc(8, 28672, 8192, 8192, 8192, 28672))

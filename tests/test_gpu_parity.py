@@ -415,6 +415,61 @@ def test_int8_edges_bitexact(gpu, dn, orc):
         assert np.array_equal(got, ref.reshape(M, ldc)[:, :N]), (M, N, K)
 
 
+# Both dot-form kernels with A in registers, forced through autotune-cache
+# entries: the bulk-copy ring (dense rows: one copy per stage; padded rows: one
+# per row) and the register-load form, on int8 (bit-exact) and on FP32 / BF16
+# with B stored N x K.
+@pytest.mark.parametrize("kernel", [7, 11])
+@pytest.mark.parametrize("case", [
+    ("s8s32", 4, 11008, 4096, 4096, 30), ("s8s32", 1, 1009, 4096, 4096, 7),
+    ("s8s32", 8, 1000, 8192, 8192, 300), ("s8s32", 3, 3001, 4112, 4128, 150),
+    ("s8s32", 6, 17, 64, 64, 5), ("s8s32", 2, 777, 512, 528, 296),
+    ("f32", 3, 1000, 1024, 1024, 296), ("f32", 8, 257, 2048, 2052, 64),
+    ("bf16f32", 5, 999, 2048, 2048, 148), ("bf16f32", 2, 4096, 4096, 4104, 296)])
+def test_rows_kernels_forced(gpu, dn, orc, tmp_path, kernel, case):
+    kind_name, M, N, K, ldb, grid = case
+    torch = gpu
+    mt = 1 if M <= 1 else 2 if M <= 2 else 4 if M <= 4 else 8
+    kind = {"s8s32": dn.KIND_S8S32, "f32": dn.KIND_F32, "bf16f32": dn.KIND_BF16F32}[kind_name]
+    _force_plan(dn, tmp_path, f"rows_{kernel}_{kind_name}_{M}_{N}.bin", kind, M, N, K, K, ldb, N, 0, 1, 1,
+                (kernel, grid, 0, mt))
+    s = torch.cuda.current_stream()
+    if kind_name == "s8s32":
+        A, Bb = int8_uniform(M * K, 17), int8_uniform(N * ldb, 18)
+        ref = np.zeros(M * N, np.int32)
+        orc.gemm_s8s32(M, N, K, A, K, Bb, ldb, ref, N)
+        dC = torch.zeros(M * N, dtype=torch.int32, device="cuda")
+        dn.check(dn.cuda_gemm("s8s32", dn.desc(M, N, K, K, ldb, N), torch.from_numpy(A).cuda(),
+                              torch.from_numpy(Bb).cuda(), dC, s))
+        torch.cuda.synchronize()
+        assert np.array_equal(dC.cpu().numpy(), ref)
+        return
+    if kind_name == "f32":
+        A, Bb, C0 = ref_uniform(M * K, 17), ref_uniform(N * ldb, 18), ref_uniform(M * N, 19)
+        Bt = np.ascontiguousarray(Bb.reshape(N, ldb)[:, :K].T).reshape(-1)
+        ref = C0.copy()
+        orc.gemm_f32(M, N, K, 1.0, A, K, Bt, N, 0.5, ref, N)
+        dC = torch.from_numpy(C0.copy()).cuda()
+        dn.check(dn.cuda_gemm("f32", dn.desc(M, N, K, K, ldb, N, 1.0, 0.5, 0, 1), torch.from_numpy(A).cuda(),
+                              torch.from_numpy(Bb).cuda(), dC, s))
+        torch.cuda.synchronize()
+        assert np.max(np.abs(dC.cpu().numpy() - ref)) <= fp32_tol(K)
+        return
+    rng = np.random.default_rng(20)
+    Ab = bf16_bits(rng.standard_normal(M * K).astype(np.float32))
+    Bb = bf16_bits(rng.standard_normal(N * ldb).astype(np.float32))
+    Bt = np.ascontiguousarray(Bb.reshape(N, ldb)[:, :K].T).reshape(-1)
+    ref = np.zeros(M * N, np.float32)
+    r64 = orc.gemm_bf16f32(M, N, K, 1.0, Ab, K, Bt, N, 0.0, ref, N, want64=True)
+    dC = torch.zeros(M * N, device="cuda")
+    dn.check(dn.cuda_gemm("bf16f32", dn.desc(M, N, K, K, ldb, N, 1.0, 0.0, 0, 1),
+                          torch.from_numpy(Ab.view(np.int16)).cuda(), torch.from_numpy(Bb.view(np.int16)).cuda(),
+                          dC, s))
+    torch.cuda.synchronize()
+    got = dC.cpu().numpy()
+    assert np.max(np.abs(got - r64)) <= 2e-6 * K * max(1.0, float(np.max(np.abs(r64))))
+
+
 @pytest.mark.parametrize("shape", [(1, 128, 64), (7, 13, 5), (5, 7, 11), (4, 1009, 1024),
                                    (8, 4096, 512), (32, 48, 64), (13, 17, 19)])
 def test_int8_fp32_api_bitexact(gpu, dn, orc, shape):
@@ -658,7 +713,7 @@ def test_plan_selection_on_device(gpu, dn):
     assert dn.plan_describe(dn.KIND_F32, dn.desc(1, 4096, 4096, 4096, 4096, 4096)).startswith(
         "gemv_kn_splitk mt=1 vec4=1 splits=16")
     assert dn.plan_describe(dn.KIND_S8S32, dn.desc(4, 11008, 4096, 4096, 4096, 11008)).startswith(
-        "gemv_rows_dot mt=4 vec=1")
+        "gemv_rows_bulk mt=4 vec=1")
 
 
 @pytest.mark.parametrize("splits", [2, 5, 8, 16])
@@ -674,7 +729,7 @@ def test_cluster_variant_forced(gpu, dn, orc, tmp_path, splits):
         path.write_bytes(plan_file_bytes([(h, (6, se, kchunk, mt))]))
         assert dn.lib.dnnopt_autotune_load(str(path).encode()) == 1
         d = dn.desc(M, N, K, K, N, N, 1.0, 0.5)
-        assert dn.plan_describe(dn.KIND_F32, d).startswith("gemv_kn_")  # heuristic view
+        assert dn.plan_describe(dn.KIND_F32, d).startswith(("gemv_kn_", "gemv_panel"))  # heuristic view
         A, B, C = ref_uniform(M * K, 5), ref_uniform(K * N, 6), ref_uniform(M * N, 7)
         ref = C.copy()
         orc.gemm_f32(M, N, K, 1.0, A, K, B, N, 0.5, ref, N)
@@ -690,12 +745,13 @@ def _force_plan(dn, tmp_path, name, kind, M, N, K, lda, ldb, ldc, ta, tb, vec, e
     assert dn.lib.dnnopt_autotune_load(str(path).encode()) == 1
 
 
-# Column-slab kernel: heuristic shapes and, through a forced plan, shapes
-# outside its heuristic range (tiny N, K over several 1024-row passes, K not a
-# multiple of the 32-row step, transposed A, padded C).
+# Column-slab kernel through a forced plan: the sweep shapes (FP32 now plans
+# row panels for them), and shapes outside its heuristic range (tiny N, K over
+# several 1024-row passes, K not a multiple of the 32-row step, transposed A,
+# padded C).
 @pytest.mark.parametrize("M,N,K,alpha,beta,ta,ldc,force", [
-    (2, 1009, 1024, 1.0, 0.5, 0, None, 0), (7, 4093, 1024, 1.0, 0.5, 0, None, 0),
-    (5, 2039, 1000, 2.0, 0.0, 0, None, 0), (8, 600, 2048, 1.0, -1.0, 0, 604, 0),
+    (2, 1009, 1024, 1.0, 0.5, 0, None, 8), (7, 4093, 1024, 1.0, 0.5, 0, None, 16),
+    (5, 2039, 1000, 2.0, 0.0, 0, None, 16), (8, 600, 2048, 1.0, -1.0, 0, 604, 8),
     (1, 7, 5, 1.0, 0.5, 0, None, 8), (3, 100, 3000, 1.0, 0.25, 0, None, 8),
     (4, 520, 1030, 0.5, 0.5, 1, None, 8), (6, 9000, 33, 1.0, 0.0, 0, None, 8),
     (1, 1024, 4097, 1.0, 0.5, 1, 1030, 8), (1, 7, 5, 1.0, 0.5, 0, None, 16),
@@ -728,6 +784,84 @@ def test_slab_kernel(gpu, dn, orc, tmp_path, M, N, K, alpha, beta, ta, ldc, forc
     got = dC.cpu().numpy().reshape(M, ldc)
     assert np.max(np.abs(got[:, :N] - ref_full[:, :N])) <= fp32_tol(K), (M, N, K)
     assert np.array_equal(got[:, N:], C0.reshape(M, ldc)[:, N:])
+
+
+# Row-panel kernel (FP32, B K x N): heuristic shapes, then every panel width
+# and K-range count forced through an autotune-cache entry on prime N, K not a
+# multiple of the 32-row stage, K ranges that leave the last CTA short, M = 1..8,
+# transposed A, padded C, beta = 0 over NaN, and a B base that is only 4-byte
+# aligned (every row segment then starts mid-chunk).
+PANEL_CASES = [
+    (2, 1009, 1024, 1.0, 0.5, 0, None, 0, 0, 0), (7, 4093, 1024, 1.0, 0.5, 0, None, 0, 0, 0),
+    (5, 2039, 1000, 2.0, 0.0, 0, None, 0, 0, 0), (8, 600, 2048, 1.0, -1.0, 0, 604, 0, 0, 0),
+    (1, 4093, 1024, 1.0, 0.0, 0, None, 0, 0, 0), (3, 513, 777, 0.5, 0.25, 1, 520, 0, 0, 1),
+]
+for _w in (64, 128):
+    for _s in (1, 2, 4, 8):
+        PANEL_CASES += [(7, 1031, 999, 1.0, 0.5, 0, None, _w, _s, 0),
+                        (4, 300, 520, 1.5, 0.0, 1, 301, _w, _s, 1),
+                        (8, 2039, 1024, 1.0, 0.5, 0, 2048, _w, _s, 1)]
+PANEL_CASES += [(6, 9000, 33, 1.0, 0.5, 0, None, 128, 1, 0), (1, 5, 70, 1.0, 0.5, 0, None, 128, 2, 0),
+                (2, 4096, 2048, 1.0, 0.5, 0, None, 128, 8, 1), (5, 131, 4096, 1.0, 0.5, 1, None, 128, 8, 0)]
+
+
+@pytest.mark.parametrize("M,N,K,alpha,beta,ta,ldc,w,splits,boff", PANEL_CASES)
+def test_panel_kernel(gpu, dn, orc, tmp_path, M, N, K, alpha, beta, ta, ldc, w, splits, boff):
+    """w = 0: heuristic plan (must be the panel kernel); else (w, splits)
+    forced.  boff = 1 offsets B's base by one float."""
+    ldc = ldc or N
+    lda = M if ta else K
+    mt = 1 if M <= 1 else 2 if M <= 2 else 4 if M <= 4 else 8
+    Bbuf = ref_uniform(K * N + 1, 12)
+    Bhost = Bbuf[boff:boff + K * N]
+    vec = 1 if (N % 4 == 0 and boff == 0) else 0
+    d = dn.desc(M, N, K, lda, N, ldc, alpha, beta, ta, 0)
+    if w:
+        _force_plan(dn, tmp_path, f"panel_{M}_{N}_{K}_{w}_{splits}_{boff}.bin", 0, M, N, K, lda, N, ldc, ta,
+                    0, vec, (10, w, splits, mt))
+    else:
+        assert dn.plan_describe(dn.KIND_F32, d).startswith(f"gemv_panel mt={mt} w="), (M, N, K)
+    A = ref_uniform(M * K, 11)   # K x M when ta
+    C0 = ref_uniform(M * ldc, 13)
+    if beta == 0.0:
+        C0[::3] = np.nan         # never read when beta == 0
+    Ar = np.ascontiguousarray(A.reshape(K, M).T).reshape(-1) if ta else A
+    tmp = np.ascontiguousarray(C0.reshape(M, ldc)[:, :N]).reshape(-1).copy()
+    tmp = np.nan_to_num(tmp) if beta == 0.0 else tmp
+    orc.gemm_f32(M, N, K, alpha, Ar, K, Bhost.copy(), N, beta, tmp, N)
+    dA, dC = gpu.from_numpy(A).cuda(), gpu.from_numpy(C0.copy()).cuda()
+    dBbuf = gpu.from_numpy(Bbuf).cuda()
+    dB = dBbuf[boff:boff + K * N]
+    dn.check(dn.cuda_gemm("f32", d, dA, dB, dC, gpu.cuda.current_stream()))
+    gpu.cuda.synchronize()
+    got = dC.cpu().numpy().reshape(M, ldc)
+    assert np.max(np.abs(got[:, :N] - tmp.reshape(M, N))) <= fp32_tol(K), (M, N, K, w, splits)
+    assert np.array_equal(got[:, N:], C0.reshape(M, ldc)[:, N:], equal_nan=True)
+    # Deterministic: a second call gives the same bits.
+    dC2 = gpu.from_numpy(C0.copy()).cuda()
+    dn.check(dn.cuda_gemm("f32", d, dA, dB, dC2, gpu.cuda.current_stream()))
+    gpu.cuda.synchronize()
+    assert np.array_equal(dC2.cpu().numpy().view(np.uint32), dC.cpu().numpy().view(np.uint32))
+
+
+def test_panel_kernel_bias_through_onednn_entry(gpu, dn, orc):
+    """The oneDNN entry with both operands untransposed maps onto a small-M
+    K x N GEMM with the bias in the epilogue: C (OC x batch, column-major) =
+    W (OC x K) x X (K x batch) + bias."""
+    from tests.test_oracle_colmajor import operands
+    torch = gpu
+    M, N, K = 1000, 3, 512     # OC, batch, K
+    A, lda, B, ldb, C, ldc = operands(M, N, K, "N", "N", 0, 0, 0)
+    bias = ref_uniform(M, 5)
+    assert dn.plan_describe(dn.KIND_F32, dn.desc(N, M, K, ldb, lda, ldc)).startswith("gemv_panel")
+    ref = C.copy()
+    assert orc.sgemm_colmajor("N", "N", M, N, K, 1.0, A, lda, B, ldb, 0.5, ref, ldc, bias) == 0
+    dA, dB, dC = (torch.from_numpy(x).cuda() for x in (A, B, C))
+    s = torch.cuda.current_stream()
+    dn.check(dn.cuda_sgemm_colmajor("N", "N", M, N, K, 1.0, dA, lda, dB, ldb, 0.5, dC, ldc,
+                                    torch.from_numpy(bias).cuda(), s))
+    torch.cuda.synchronize()
+    assert np.max(np.abs(dC.cpu().numpy() - ref)) <= fp32_tol(K)
 
 
 def test_autotune_roundtrip(gpu, dn, orc, tmp_path):
