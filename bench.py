@@ -68,6 +68,20 @@ def peaks():
     return dict(FALLBACK_PEAKS, source="fallback")
 
 
+def lpt_assignment(sizes, n_streams):
+    """Longest-processing-time assignment of independent jobs to streams:
+    returns (issue order, stream index per job), largest job first, each onto
+    the stream with the fewest bytes so far."""
+    order = sorted(range(len(sizes)), key=lambda i: -sizes[i])
+    load = [0] * n_streams
+    stream_of = {}
+    for i in order:
+        k = min(range(n_streams), key=lambda j: load[j])
+        stream_of[i] = k
+        load[k] += sizes[i]
+    return order, stream_of
+
+
 def rotating_sets(bytes_per_set, floor=3):
     """Input sets to rotate between timed calls: at least `floor` and at least
     ~3x the 126 MB L2 in all (384 MB), so that no call finds its operands in
@@ -580,11 +594,13 @@ def run_gpu_arm(args):
     sets = make_sweep_sets(torch, dev)
     flops = sum(2.0 * M * N * K for (M, N, K) in C2_SHAPES)
     bytes_step = sum(gemm_bytes(M, N, K, 0.5) for (M, N, K) in C2_SHAPES)
-    # The 12 GEMMs are independent: issue them on SWEEP_STREAMS streams
-    # (largest first, round-robin) forked from and joined back into `stream`,
-    # so their latencies overlap; each stream has its own library workspace.
+    # The 12 GEMMs are independent: issue them on SWEEP_STREAMS streams forked
+    # from and joined back into `stream`, so their latencies overlap; each
+    # stream has its own library workspace.  Streams are loaded by bytes,
+    # largest GEMM first onto the least-loaded stream (longest-processing-time
+    # order), so that no stream carries much more than its share.
     side = [torch.cuda.Stream(device=dev) for _ in range(args.streams)]
-    order = sorted(range(len(C2_SHAPES)), key=lambda i: -gemm_bytes(*C2_SHAPES[i], 0.5))
+    order, stream_of = lpt_assignment([gemm_bytes(M, N, K, 0.5) for (M, N, K) in C2_SHAPES], args.streams)
 
     def sweep(items, streams):
         if streams is None or len(streams) == 1:
@@ -597,10 +613,10 @@ def run_gpu_arm(args):
         fork.record(stream)
         for st in streams:
             st.wait_event(fork)
-        for j, i in enumerate(order):
+        for i in order:
             (M, N, K, A, B, C) = items[i]
             dn.check(dn.cuda_gemm("f32", dn.desc(M, N, K, K, N, N, 1.0, 0.5), A, B, C,
-                                  streams[j % len(streams)]), "sweep GEMM")
+                                  streams[stream_of[i]]), "sweep GEMM")
         for st in streams:
             join = torch.cuda.Event()
             join.record(st)
@@ -686,7 +702,8 @@ def run_gpu_arm(args):
             "config": {
                 "workload": WORKLOAD,
                 "api": f"dnnopt_cuda_gemm_f32 (device pointers); the 12 independent GEMMs on {args.streams} "
-                       "streams forked/joined inside one CUDA graph per input set",
+                       "streams (largest first onto the least-loaded stream) forked/joined inside one CUDA "
+                       "graph per input set",
                 "l2": f"{N_SETS} rotating input sets ({N_SETS * bytes_step / 1e6:.0f} MB > 126 MB L2)",
                 "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
             },

@@ -183,6 +183,17 @@ int launch_plan(Kind kind, const GemmArgs& g, const Plan& p, const float* scales
             }
             break;
         }
+        case KernelId::GemmTc: {
+            const TcKind tk = kind == Kind::BF16F32 ? TcKind::BF16 : TcKind::I8;
+            if (kind != Kind::BF16F32 && kind != Kind::S8S32 && kind != Kind::F32S8Q)
+                return set_status(DNNOPT_STATUS_NOT_SUPPORTED);
+            const size_t wsb = gemm_tc_ws_bytes(g, p.tc);
+            st = ensure_workspace(ctx, s, (wsb + 3) / 4, static_cast<size_t>(gemm_tc_tickets(g, p.tc)), 0, &w);
+            if (st != DNNOPT_STATUS_SUCCESS) return st;
+            e = launch_gemm_tc(tk, dot_kind(kind), g, p.tc, scales, w->ws, w->counters, w->err, ctx->num_sms, s);
+            note_launch();
+            break;
+        }
         case KernelId::TileF32:
             if (kind == Kind::E4M3BF16 || kind == Kind::S8S32 || kind == Kind::F32S8Q)
                 return set_status(DNNOPT_STATUS_NOT_SUPPORTED);

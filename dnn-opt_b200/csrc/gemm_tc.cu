@@ -1,0 +1,518 @@
+// General GEMM on the 5th-generation tensor cores (tcgen05 + TMEM), both
+// operands streamed by TMA, for the shapes the GEMV kernels and the
+// tall-skinny BF16 kernel do not take:
+//   * INT8 x INT8 -> INT32 (gemm_int8_int8int8int32, reference
+//     src/gemm/gemm_int8_native.cpp:37-181, the 8x8 SMMLA tile) and the
+//     FP32-API gemm_int8 after quantisation (dequantising epilogue,
+//     src/gemm/gemm_driver_generic.cpp:49-67) for M > 8: tcgen05.mma.kind::i8,
+//     int32 accumulators (exact, so bit-identical to the reference's sums);
+//   * BF16 x BF16 -> FP32 (gemm_bf16_bf16bf16f32, reference
+//     src/gemm/gemm_driver_bf16.cpp:134-218) for M > 8 and N > 256:
+//     tcgen05.mma.kind::f16, FP32 accumulators, the reference epilogue
+//     beta == 0 ? alpha*acc : fma(alpha, acc, beta*C).
+//
+// Layout: A [M, K] K-major (lda); B either [N, K] K-major (INT8 always, BF16
+// with trans_b) or [K, N] MN-major (BF16 without trans_b).  Every K-block is
+// 128 bytes of K (64 bf16 or 128 int8), staged by TMA with the 128-byte
+// swizzle straight into the UMMA operand layout; four MMAs of 32 bytes of K
+// consume it (K = 16 bf16 or K = 32 int8 per instruction).
+//
+// Work units are (split, m-tile, n-tile) with 128-row m-tiles and n-tiles of
+// n_mma <= 256 columns; persistent CTAs (one per SM: a 4-stage 48 KB ring)
+// walk the units.  Roles: warp 0 issues TMA loads, warp 1 owns TMEM and
+// issues the MMAs into one of two accumulators (so the epilogue of a unit
+// overlaps the MMAs of the next), warps 2-5 drain TMEM with tcgen05.ld (warp
+// q owns TMEM lanes / tile rows 32(q%4) ...) and write C directly.  With a
+// K split (units of one tile in different CTAs) the epilogue writes its
+// partial tile to the workspace; the last CTA of the tile (atomic ticket)
+// sums the splits in split order and writes C.
+//
+// Every TMA load targets this CTA's own shared memory.  Every mbarrier wait is
+// bounded (kMbarTimeoutNs); a timeout records an error word and makes the
+// other roles give up.
+#include <cuda.h>
+
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace dnnopt_b200 {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int kKBytes = 128;                       // bytes of K per K-block
+constexpr int kThreads = 192;
+constexpr int kStages = 4;
+constexpr int kMaxN = 256;
+constexpr int kABytes = BM * kKBytes;              // 16 KB
+constexpr int kBBytesMax = kMaxN * kKBytes;        // 32 KB
+constexpr int kStageBytes = kABytes + kBBytesMax;  // 48 KB
+constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * kStageBytes + 256;
+
+enum TcOp : int {
+    kOpBf16K = 0,    // bf16, B [N, K] K-major
+    kOpBf16MN = 1,   // bf16, B [K, N] MN-major
+    kOpI8 = 2,       // int8, B [N, K] K-major
+};
+enum TcEpi : int {
+    kEpiF32 = 0,     // C fp32 = beta == 0 ? alpha*acc : fma(alpha, acc, beta*C)
+    kEpiS32 = 1,     // C int32 = acc
+    kEpiS8DQ = 2,    // C fp32 = (beta*C) + (alpha*sA*sB) * float(acc)
+};
+
+struct TcGemmParams {
+    int M, N, K;
+    int n_mma, num_kb, kb_per_split, splits;
+    int m_tiles, n_tiles, units;
+    int op, epi;
+    float alpha, beta;
+    void* C;
+    int64_t ldc;
+    const float* scales;   // {sA, sB} for kEpiS8DQ
+    int c_vec;             // 1: C 16-byte aligned with ldc % 4 == 0 (vector epilogue)
+    void* ws;              // [tiles][splits][BM][n_mma] partials (splits > 1)
+    uint32_t* tickets;     // one per tile, zero on entry, left zero
+    uint32_t* err;
+};
+
+__device__ __forceinline__ void umma_i8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Instruction descriptor (tcgen05 .kind::f16 / .kind::i8): D format bits
+// 4-5 (1 = F32, 2 = S32), A / B format bits 7-9 / 10-12 (BF16 = 1, signed
+// 8-bit = 1), B major bit 16 (1 = MN-major), N >> 3 at 17, M >> 4 at 24.
+__host__ __device__ constexpr uint32_t tc_idesc(int op, int m, int n) {
+    const uint32_t dfmt = op == kOpI8 ? 2u : 1u;
+    return (dfmt << 4) | (1u << 7) | (1u << 10) | ((op == kOpBf16MN ? 1u : 0u) << 16) |
+           (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// MN-major operand in the 128-byte swizzled layout: 64 bf16 along N per
+// 128-byte row, 8 K rows per 1024-byte atom, 64-column chunks `lbo` bytes apart.
+__device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t smem_addr, uint32_t lbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>(1024u >> 4) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    d |= static_cast<uint64_t>(2u) << 61;
+    return d;
+}
+
+// Epilogue of four consecutive outputs (row, col .. col+3) from raw
+// accumulator words: int32 as is, FP32 with alpha / beta, or the int8
+// dequantisation float(acc) * (alpha * sA * sB) (+ beta * C) with the
+// reference's rounding order.  16-byte accesses when C allows and the four
+// columns are inside N.
+__device__ __forceinline__ void store4(const TcGemmParams& p, int row, int col, const uint32_t* w) {
+    const int64_t off = static_cast<int64_t>(row) * p.ldc + col;
+    const bool vec = p.c_vec && col + 3 < p.N;
+    if (p.epi == kEpiS32) {
+        int32_t* cp = static_cast<int32_t*>(p.C) + off;
+        if (vec) {
+            *reinterpret_cast<int4*>(cp) = make_int4(static_cast<int>(w[0]), static_cast<int>(w[1]),
+                                                     static_cast<int>(w[2]), static_cast<int>(w[3]));
+        } else {
+            for (int j = 0; j < 4 && col + j < p.N; ++j) cp[j] = static_cast<int32_t>(w[j]);
+        }
+        return;
+    }
+    float* cp = static_cast<float*>(p.C) + off;
+    float old[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (p.beta != 0.0f) {
+        if (vec) {
+            const float4 t = *reinterpret_cast<const float4*>(cp);
+            old[0] = t.x; old[1] = t.y; old[2] = t.z; old[3] = t.w;
+        } else {
+            for (int j = 0; j < 4 && col + j < p.N; ++j) old[j] = cp[j];
+        }
+    }
+    float v[4];
+    if (p.epi == kEpiF32) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float acc = __uint_as_float(w[j]);
+            v[j] = (p.beta == 0.0f) ? p.alpha * acc : fmaf(p.alpha, acc, p.beta * old[j]);
+        }
+    } else {
+        const float scale = __fmul_rn(p.alpha, __fmul_rn(p.scales[0], p.scales[1]));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float c_0 = (p.beta == 0.0f) ? 0.0f : __fmul_rn(p.beta, old[j]);
+            v[j] = __fadd_rn(c_0, __fmul_rn(scale, static_cast<float>(static_cast<int32_t>(w[j]))));
+        }
+    }
+    if (vec) {
+        *reinterpret_cast<float4*>(cp) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+        for (int j = 0; j < 4 && col + j < p.N; ++j) cp[j] = v[j];
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const TcGemmParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t* stages = base;
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + kStages * kStageBytes);
+    uint64_t* empty = full + kStages;
+    uint64_t* tfull = empty + kStages;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+    volatile uint32_t* last_flag = tmem_slot + 2;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t b_bytes = static_cast<uint32_t>(p.n_mma) * kKBytes;
+    const uint32_t tmem_cols = static_cast<uint32_t>(2 * p.n_mma) <= 32 ? 32u
+                             : (static_cast<uint32_t>(2 * p.n_mma) <= 64 ? 64u
+                             : (static_cast<uint32_t>(2 * p.n_mma) <= 128 ? 128u
+                             : (static_cast<uint32_t>(2 * p.n_mma) <= 256 ? 256u : 512u)));
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int b = 0; b < 2; ++b) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], 4); }
+        *abort_flag = 0u;
+        fence_mbar_init();
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, tmem_cols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();
+
+    // Unit u -> (split, m-tile, n-tile); the splits of a tile are adjacent
+    // unit indices so that they run at the same time.
+    auto unit_coords = [&](int u, int& split, int& mt, int& nt) {
+        split = u % p.splits;
+        const int t = u / p.splits;
+        mt = t % p.m_tiles;
+        nt = t / p.m_tiles;
+    };
+    auto unit_kbs = [&](int split, int& kb0, int& nkb) {
+        kb0 = split * p.kb_per_split;
+        nkb = min(p.kb_per_split, p.num_kb - kb0);
+    };
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            uint32_t it = 0;
+            for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
+                int split, mt, nt, kb0, nkb;
+                unit_coords(u, split, mt, nt);
+                unit_kbs(split, kb0, nkb);
+                for (int kb = kb0; kb < kb0 + nkb; ++kb, ++it) {
+                    const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
+                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.err)) break;
+                    uint8_t* sa = stages + s * kStageBytes;
+                    uint8_t* sb = sa + kABytes;
+                    mbar_arrive_expect_tx(&full[s], kABytes + b_bytes);
+                    const int kx = p.op == kOpI8 ? kb * kKBytes : kb * (kKBytes / 2);   // elements
+                    tma_load_2d(sa, &tmA, &full[s], kx, mt * BM);
+                    if (p.op == kOpBf16MN) {
+                        // 64-column chunks of 64 K rows: chunk j at j * 8 KB.
+                        for (int j = 0; j < p.n_mma / 64; ++j)
+                            tma_load_2d(sb + j * 8192, &tmB, &full[s], nt * p.n_mma + j * 64, kx);
+                    } else {
+                        tma_load_2d(sb, &tmB, &full[s], kx, nt * p.n_mma);
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint32_t idesc = tc_idesc(p.op, BM, p.n_mma);
+            uint32_t it = 0, titer = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; ok && u < p.units && !*abort_flag; u += gridDim.x, ++titer) {
+                int split, mt, nt, kb0, nkb;
+                unit_coords(u, split, mt, nt);
+                unit_kbs(split, kb0, nkb);
+                const uint32_t buf = titer & 1u, tph = (titer >> 1) & 1u;
+                if (!mbar_wait(&tempty[buf], tph ^ 1u, abort_flag, p.err)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + buf * static_cast<uint32_t>(p.n_mma);
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
+                    if (!mbar_wait(&full[s], ph, abort_flag, p.err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(stages + s * kStageBytes);
+                    const uint32_t b_addr = a_addr + kABytes;
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        // 32 bytes of K per MMA: +32 B along a K-major 128-byte
+                        // row; two 1024-B atoms (16 K rows) down an MN-major chunk.
+                        const uint64_t adesc = umma_desc_k_sw128(a_addr + kk * 32);
+                        const uint64_t bdesc = p.op == kOpBf16MN ? desc_mn_sw128(b_addr + kk * 2048, 8192)
+                                                                 : umma_desc_k_sw128(b_addr + kk * 32);
+                        const uint32_t accum = (kb | kk) != 0 ? 1u : 0u;
+                        if (p.op == kOpI8) umma_i8_ss(d_tmem, adesc, bdesc, idesc, accum);
+                        else umma_f16_ss(d_tmem, adesc, bdesc, idesc, accum);
+                    }
+                    umma_commit(&empty[s]);   // stage free once these MMAs retire
+                }
+                if (!ok) break;
+                umma_commit(&tfull[buf]);     // accumulator ready for the epilogue
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int q = warp & 3;           // TMEM lanes 32q .. 32q+31 (warp id mod 4)
+        const int ep_tid = tid - 64;      // 0..127
+        uint32_t titer = 0;
+        for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x, ++titer) {
+            int split, mt, nt;
+            unit_coords(u, split, mt, nt);
+            const uint32_t buf = titer & 1u, tph = (titer >> 1) & 1u;
+            const bool ok = mbar_wait(&tfull[buf], tph, abort_flag, p.err);
+            tc_fence_after();
+            const int row_in = q * 32 + lane;
+            const int row = mt * BM + row_in;
+            const int col0 = nt * p.n_mma;
+            const int tile = mt + nt * p.m_tiles;
+            const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * static_cast<uint32_t>(p.n_mma);
+            const bool partial = p.splits > 1;
+            // Drain the accumulator 32 columns at a time: to C, or (split-K) to
+            // this split's partial tile in the workspace.
+            uint32_t* wrow = partial ? static_cast<uint32_t*>(p.ws) +
+                                           ((static_cast<int64_t>(tile) * p.splits + split) * BM + row_in) * p.n_mma
+                                     : nullptr;
+            for (int c0 = 0; c0 < p.n_mma; c0 += 32) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x16(t_addr + c0, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+                tmem_ld_32x32b_x16(t_addr + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
+                tmem_ld_wait();
+                if (!ok) continue;
+                if (partial) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4)
+                        __stcg(reinterpret_cast<uint4*>(wrow + c0 + j), make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]));
+                } else if (row < p.M) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) {
+                        const int col = col0 + c0 + j;
+                        if (col >= p.N) break;
+                        store4(p, row, col, &r[j]);
+                    }
+                }
+            }
+            // Accumulator drained: the next unit's MMAs may reuse it.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
+            if (!partial || !ok) continue;
+            // Split-K: publish, then the last split of the tile sums all splits
+            // in split order (int32: exact; FP32: a fixed order).
+            __threadfence();
+            named_barrier_sync(1, 128);
+            if (ep_tid == 0) {
+                const uint32_t t = atomicAdd(&p.tickets[tile], 1u);
+                *last_flag = t == static_cast<uint32_t>(p.splits - 1) ? 1u : 0u;
+            }
+            named_barrier_sync(1, 128);
+            const bool last = *last_flag != 0u;
+            named_barrier_sync(1, 128);   // everyone has read last_flag before the next unit rewrites it
+            if (!last) continue;
+            __threadfence();
+            if (row < p.M) {
+                const uint32_t* trow = static_cast<const uint32_t*>(p.ws) +
+                                       (static_cast<int64_t>(tile) * p.splits * BM + row_in) * p.n_mma;
+                const int64_t sstride = static_cast<int64_t>(BM) * p.n_mma;
+                for (int c0 = 0; c0 < p.n_mma; c0 += 4) {
+                    if (col0 + c0 >= p.N) break;
+                    int32_t si[4] = {0, 0, 0, 0};
+                    float sf[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    for (int sp = 0; sp < p.splits; ++sp) {
+                        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(trow + sp * sstride + c0));
+                        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            si[j] += static_cast<int32_t>(w[j]);
+                            sf[j] += __uint_as_float(w[j]);
+                        }
+                    }
+                    uint32_t w[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) w[j] = p.epi == kEpiF32 ? __float_as_uint(sf[j]) : static_cast<uint32_t>(si[j]);
+                    store4(p, row, col0 + c0, w);
+                }
+            }
+            if (ep_tid == 0) p.tickets[tile] = 0u;   // ready for the next launch on this stream
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    pdl_launch_dependents();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, tmem_cols);
+    }
+}
+
+// ---- host helpers ----------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<EncodeTiledFn>(nullptr);
+        return reinterpret_cast<EncodeTiledFn>(ptr);
+    }();
+    return fn;
+}
+
+bool encode(CUtensorMap* m, CUtensorMapDataType t, const void* ptr, uint64_t d0, uint64_t d1, uint64_t row_bytes,
+            uint32_t b0, uint32_t b1) {
+    cuuint64_t dims[2] = {d0, d1};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {b0, b1};
+    cuuint32_t estr[2] = {1, 1};
+    return encode_fn()(m, t, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+}  // namespace
+
+bool gemm_tc_supported(TcKind kind, const GemmArgs& g) {
+    if (g.M < 1 || g.N < 1 || g.K < 1 || g.a_trans || !encode_fn()) return false;
+    const size_t eb = kind == TcKind::BF16 ? 2 : 1;
+    if (!aligned16(g.A) || (static_cast<size_t>(g.lda) * eb) % 16 != 0) return false;
+    if (!aligned16(g.B) || (static_cast<size_t>(g.ldb) * eb) % 16 != 0) return false;
+    if (kind != TcKind::BF16 && !g.b_trans) return false;   // int8 B is always [N, K]
+    if (kind == TcKind::BF16 && !g.b_trans && g.N < 64) return false;
+    return !g.bias;
+}
+
+// Tile width, K split and grid for a shape: n_mma up to 256 (a multiple of 64
+// for MN-major B, else of 32: the epilogue drains 32 columns at a time); the K extent split so that units ~ SMs when the
+// output tiles alone leave most SMs idle, at least 4 K-blocks per split.
+TcPlan gemm_tc_plan(TcKind kind, const GemmArgs& g, int num_sms) {
+    TcPlan pl{};
+    const bool mn = kind == TcKind::BF16 && !g.b_trans;
+    int n = g.N < kMaxN ? g.N : kMaxN;
+    n = mn ? (n + 63) / 64 * 64 : (n + 31) / 32 * 32;
+    pl.n_mma = n;
+    const int m_tiles = (g.M + BM - 1) / BM, n_tiles = (g.N + n - 1) / n;
+    const int elems = kind == TcKind::BF16 ? kKBytes / 2 : kKBytes;
+    const int num_kb = (g.K + elems - 1) / elems;
+    const int tiles = m_tiles * n_tiles;
+    int splits = 1;
+    while (tiles * splits * 2 <= num_sms && num_kb / (splits * 2) >= 4 && splits < 16) splits *= 2;
+    pl.kb_per_split = (num_kb + splits - 1) / splits;
+    pl.splits = (num_kb + pl.kb_per_split - 1) / pl.kb_per_split;
+    return pl;
+}
+
+size_t gemm_tc_ws_bytes(const GemmArgs& g, const TcPlan& pl) {
+    if (pl.splits <= 1) return 0;
+    const int m_tiles = (g.M + BM - 1) / BM, n_tiles = (g.N + pl.n_mma - 1) / pl.n_mma;
+    return static_cast<size_t>(m_tiles) * n_tiles * pl.splits * BM * pl.n_mma * 4;
+}
+
+int gemm_tc_tickets(const GemmArgs& g, const TcPlan& pl) {
+    return ((g.M + BM - 1) / BM) * ((g.N + pl.n_mma - 1) / pl.n_mma);
+}
+
+cudaError_t launch_gemm_tc(TcKind kind, DotKind epi, const GemmArgs& g, const TcPlan& pl, const float* scales,
+                           void* ws, uint32_t* tickets, uint32_t* err, int num_sms, cudaStream_t s) {
+    if (!gemm_tc_supported(kind, g) || pl.n_mma < 16 || pl.n_mma > kMaxN) return cudaErrorInvalidValue;
+    if (pl.splits > 1 && (!ws || !tickets)) return cudaErrorInvalidValue;
+    const bool mn = kind == TcKind::BF16 && !g.b_trans;
+    const int op = kind == TcKind::BF16 ? (mn ? kOpBf16MN : kOpBf16K) : kOpI8;
+    CUtensorMap tmA, tmB;
+    if (kind == TcKind::BF16) {
+        if (!encode(&tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, g.A, g.K, g.M, static_cast<uint64_t>(g.lda) * 2, 64, BM))
+            return cudaErrorInvalidValue;
+        if (mn) {
+            if (!encode(&tmB, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, g.B, g.N, g.K, static_cast<uint64_t>(g.ldb) * 2, 64, 64))
+                return cudaErrorInvalidValue;
+        } else if (!encode(&tmB, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, g.B, g.K, g.N, static_cast<uint64_t>(g.ldb) * 2, 64,
+                           static_cast<uint32_t>(pl.n_mma))) {
+            return cudaErrorInvalidValue;
+        }
+    } else {
+        if (!encode(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.A, g.K, g.M, static_cast<uint64_t>(g.lda), 128, BM) ||
+            !encode(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.B, g.K, g.N, static_cast<uint64_t>(g.ldb), 128,
+                    static_cast<uint32_t>(pl.n_mma)))
+            return cudaErrorInvalidValue;
+    }
+    TcGemmParams p;
+    p.M = g.M; p.N = g.N; p.K = g.K;
+    p.n_mma = pl.n_mma;
+    const int elems = kind == TcKind::BF16 ? kKBytes / 2 : kKBytes;
+    p.num_kb = (g.K + elems - 1) / elems;
+    p.kb_per_split = pl.kb_per_split;
+    p.splits = pl.splits;
+    p.m_tiles = (g.M + BM - 1) / BM;
+    p.n_tiles = (g.N + pl.n_mma - 1) / pl.n_mma;
+    p.units = p.m_tiles * p.n_tiles * p.splits;
+    p.op = op;
+    p.epi = epi == DotKind::S8S32 ? kEpiS32 : (epi == DotKind::S8DQ ? kEpiS8DQ : kEpiF32);
+    p.alpha = g.alpha; p.beta = g.beta;
+    p.C = g.C; p.ldc = g.ldc;
+    p.scales = scales;
+    p.c_vec = aligned16(g.C) && g.ldc % 4 == 0 ? 1 : 0;
+    p.ws = ws;
+    p.tickets = tickets;
+    p.err = err;
+
+    static std::mutex mu;
+    static std::set<int> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!done.count(dev)) {
+            e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(kSmem));
+            if (e != cudaSuccess) return e;
+            done.insert(dev);
+        }
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(p.units < num_sms ? p.units : num_sms));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, tmA, tmB, p);
+}
+
+}  // namespace dnnopt_b200

@@ -209,6 +209,27 @@ cudaError_t launch_colmajor_gather(float* tmp, const float* C, int64_t M, int64_
 cudaError_t launch_saxpy(int n, float alpha, const float* x, int incx, float* y, int incy,
                          cudaStream_t s);
 
+// ---- general tcgen05 GEMM, both operands by TMA (gemm_tc.cu) ----------------
+// INT8 (A [M,K], B [N,K], int32 accumulators: S8S32 or the S8DQ dequantising
+// epilogue with scales = {sA, sB}) or BF16 (A [M,K], B [K,N] or [N,K] with
+// b_trans, FP32 accumulators, alpha / beta).  Operands 16-byte aligned with
+// 16-byte row strides, A not transposed, no bias.  Units = 128-row x n_mma
+// tiles x K splits; splits > 1 reduce through `ws` (gemm_tc_ws_bytes) with one
+// ticket per tile in `tickets` (zero on entry, left zero).  `err` receives a
+// KernelErrorCode when a bounded wait gives up.
+enum class TcKind : int { I8 = 0, BF16 = 1 };
+struct TcPlan {
+    int n_mma;          // columns per tile (<= 256)
+    int kb_per_split;   // 128-byte K-blocks per split
+    int splits;
+};
+bool gemm_tc_supported(TcKind kind, const GemmArgs& g);
+TcPlan gemm_tc_plan(TcKind kind, const GemmArgs& g, int num_sms);
+size_t gemm_tc_ws_bytes(const GemmArgs& g, const TcPlan& pl);
+int gemm_tc_tickets(const GemmArgs& g, const TcPlan& pl);
+cudaError_t launch_gemm_tc(TcKind kind, DotKind epi, const GemmArgs& g, const TcPlan& pl, const float* scales,
+                           void* ws, uint32_t* tickets, uint32_t* err, int num_sms, cudaStream_t s);
+
 // ---- BF16 tall-skinny tcgen05 GEMM (A row-major K-contiguous, TMA) ----------
 bool gemm_bf16_tc_supported(const GemmArgs& g);
 // Rows of K one launch can take (g.K when B fits whole, 0 when the shape has no tcgen05 path).

@@ -18,7 +18,9 @@
 //                                    -> GemvRowsBulk (dot form, A in registers,
 //                                      B rows by bulk copy into a shared ring)
 //   * M <= 8 and B stored N x K      -> GemvRows / GemvNk (dot-form GEMV)
-//   * BF16, large M, N <= 256        -> Bf16Tc  (tcgen05 tall-skinny)
+//   * BF16, large M, N <= 256        -> Bf16Tc  (tcgen05 tall-skinny, B resident)
+//   * BF16 M > 8 otherwise, int8 M > 8 (TMA-aligned operands)
+//                                    -> GemmTc  (tcgen05, both operands by TMA)
 //   * config-5 e4m3 with M > 8       -> GemvNkRows (dot form per 8-row block)
 //   * anything else                  -> TileF32 / TileS8 (general SIMT tiles)
 // The split-K factor is chosen so that the grid is one wave of resident CTAs
@@ -197,6 +199,7 @@ const char* kernel_name(KernelId k) {
         case KernelId::GemvSlab: return "gemv_kn_slab";
         case KernelId::GemvPanel: return "gemv_panel";
         case KernelId::GemvRowsBulk: return "gemv_rows_bulk";
+        case KernelId::GemmTc: return "gemm_tcgen05";
     }
     return "?";
 }
@@ -277,6 +280,9 @@ Plan heuristic_plan(Kind kind, const GemmArgs& g, const DeviceInfo& info) {
             } else if (g.M <= 8 && dot_fits) {
                 p.kernel = KernelId::GemvNk;
                 p.nk = nk_plan_for(kind, g, info, 0);
+            } else if (gemm_tc_supported(TcKind::I8, g)) {
+                p.kernel = KernelId::GemmTc;
+                p.tc = gemm_tc_plan(TcKind::I8, g, info.num_sms);
             } else {
                 p.kernel = KernelId::TileS8;
             }
@@ -343,6 +349,11 @@ Plan heuristic_plan(Kind kind, const GemmArgs& g, const DeviceInfo& info) {
         p.kernel = KernelId::Bf16Tc;
         return p;
     }
+    if (kind == Kind::BF16F32 && g.M > 8 && gemm_tc_supported(TcKind::BF16, g)) {
+        p.kernel = KernelId::GemmTc;
+        p.tc = gemm_tc_plan(TcKind::BF16, g, info.num_sms);
+        return p;
+    }
     p.kernel = KernelId::TileF32;
     p.simt = gemm_simt_plan(g, info.num_sms);
     return p;
@@ -376,6 +387,10 @@ std::string describe_plan(Kind, const GemmArgs& g, const Plan& p) {
             std::snprintf(buf, sizeof(buf), "%s mt=%d w=%d splits=%d ctas=%d%s", kernel_name(p.kernel), p.kn.mt,
                           p.panel_w, p.panel_splits, gemv_panel_ctas(g.N, p.panel_w, p.panel_splits),
                           p.tuned ? " tuned" : "");
+            break;
+        case KernelId::GemmTc:
+            std::snprintf(buf, sizeof(buf), "%s n=%d splits=%d kblocks=%d", kernel_name(p.kernel), p.tc.n_mma,
+                          p.tc.splits, p.tc.kb_per_split);
             break;
         case KernelId::TileF32:
             std::snprintf(buf, sizeof(buf), "%s bm=%d bn=%d splits=%d kchunk=%d", kernel_name(p.kernel),

@@ -36,6 +36,7 @@ enum class KernelId : int {
     GemvSlab = 9,   // small-M column slab, B K x N: whole K per CTA, no split-K reduction
     GemvPanel = 10, // small-M FP32 row panels, B K x N: 512-byte row segments, cluster K reduction
     GemvRowsBulk = 11,  // GemvRows with B rows staged by bulk copies in a shared-memory ring
+    GemmTc = 12,    // general tcgen05 GEMM, both operands by TMA (int8 kind::i8, bf16 kind::f16)
 };
 
 struct Plan {
@@ -44,6 +45,7 @@ struct Plan {
     GemvNkPlan nk{};
     E4m3TcPlan e4{};
     GemmSimtPlan simt{};
+    TcPlan tc{};
     int slab_w = 8;      // GemvSlab: columns per CTA (8 or 16)
     int panel_w = 128;   // GemvPanel: columns per CTA (128 or 256)
     int panel_splits = 8;  // GemvPanel: K-ranges per panel = cluster size (1, 2, 4, 8)

@@ -521,6 +521,58 @@ def _bf16_case(dn, orc, torch, M, N, K, alpha=1.0, beta=0.0, ldc=None, seed=42, 
     return got
 
 
+# General tcgen05 GEMM (both operands by TMA): M > 8 int8 (kind::i8, exact
+# int32 sums, so bit-identical to the oracle) and BF16 with N > 256
+# (kind::f16), B as [K, N] (MN-major operand) or [N, K] (K-major).  Cases cover
+# one and many 128 x 256 tiles, K split across CTAs (ticketed in-order
+# reduction), K not a multiple of the 128-byte K-block (TMA zero fill), M and
+# N not multiples of the tile, padded ldc, beta != 0.
+@pytest.mark.parametrize("M,N,K,ldc", [
+    (2048, 2048, 2048, None), (64, 4096, 4096, None), (300, 1000, 4096, 1004), (129, 257, 160, None),
+    (9, 4096, 1024, None), (200, 1000, 64, None), (1000, 64, 1728, None), (777, 333, 4112, None)])
+def test_gemm_tc_int8_bitexact(gpu, dn, orc, M, N, K, ldc):
+    torch = gpu
+    ldc = ldc or N
+    d = dn.desc(M, N, K, K, K, ldc)
+    assert dn.plan_describe(dn.KIND_S8S32, d).startswith("gemm_tcgen05"), dn.plan_describe(dn.KIND_S8S32, d)
+    A, B = int8_uniform(M * K, 31), int8_uniform(N * K, 32)
+    ref = np.zeros(M * ldc, np.int32)
+    orc.gemm_s8s32(M, N, K, A, K, B, K, ref, ldc)
+    dC = torch.full((M * ldc,), 7, dtype=torch.int32, device="cuda")
+    for _ in range(2):   # the split-K tickets must be left at zero for the second call
+        dn.check(dn.cuda_gemm("s8s32", d, torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda(), dC,
+                              torch.cuda.current_stream()))
+        torch.cuda.synchronize()
+        got = dC.cpu().numpy().reshape(M, ldc)
+        assert np.array_equal(got[:, :N], ref.reshape(M, ldc)[:, :N]), (M, N, K)
+        assert np.all(got[:, N:] == 7)
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 512, 1024), (130, 300, 256), (1000, 4096, 512)])
+def test_gemm_tc_int8_fp32_api_bitexact(gpu, dn, orc, M, N, K):
+    """The FP32-API gemm_int8 (absmax quantisation) on the tcgen05 kernel's
+    dequantising epilogue, bit-exact against the oracle's restatement."""
+    for alpha, beta in [(1.0, 0.0), (1.5, 0.5)]:
+        A, B, C = ref_uniform(M * K, 42), ref_uniform(K * N, 43), ref_uniform(M * N, 44)
+        ref = C.copy()
+        orc.gemm_int8_f32api(M, N, K, alpha, A, K, B, N, beta, ref, N)
+        dn.check(dn.gemm_int8(M, N, K, alpha, A, K, B, N, beta, C, N))
+        assert np.array_equal(C.view(np.uint32), ref.view(np.uint32)), (M, N, K, alpha, beta)
+
+
+@pytest.mark.parametrize("M,N,K,alpha,beta,ldc,layout", [
+    (64, 4096, 4096, 1.0, 0.0, None, "kn"), (16, 4096, 4096, 1.0, 0.0, None, "kn"),
+    (300, 1000, 512, 1.0, 0.5, None, "kn"), (200, 600, 1024, 2.0, 0.0, None, "nk"),
+    (9, 4093, 768, 1.0, -1.0, 4100, "nk"), (1024, 1024, 1024, 1.0, 0.0, None, "kn"),
+    (129, 320, 100, 0.5, 0.25, None, "kn"), (513, 2000, 2048, 1.0, 0.0, None, "nk")])
+def test_gemm_tc_bf16(gpu, dn, orc, M, N, K, alpha, beta, ldc, layout):
+    ldc_ = ldc or N
+    ldb = K if layout == "nk" else N
+    d = dn.desc(M, N, K, K, ldb, ldc_, alpha, beta, 0, 1 if layout == "nk" else 0)
+    assert dn.plan_describe(dn.KIND_BF16F32, d).startswith("gemm_tcgen05"), dn.plan_describe(dn.KIND_BF16F32, d)
+    _bf16_case(dn, orc, gpu, M, N, K, alpha, beta, ldc, b_layout=layout)
+
+
 def test_bf16_config4_full(gpu, dn, orc):
     d = dn.desc(65536, 64, 256, 256, 64, 64)
     assert dn.plan_describe(dn.KIND_BF16F32, d) == "gemm_bf16_tcgen05"
