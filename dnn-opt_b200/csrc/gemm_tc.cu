@@ -18,8 +18,8 @@
 // consume it (K = 16 bf16 or K = 32 int8 per instruction).
 //
 // Work units are (split, m-tile, n-tile) with 128-row m-tiles and n-tiles of
-// n_mma <= 256 columns; persistent CTAs (one per SM: a 4-stage 48 KB ring)
-// walk the units.  Roles: warp 0 issues TMA loads, warp 1 owns TMEM and
+// n_mma <= 256 columns; persistent CTAs (one per SM: a 192 KB ring of 4
+// stages at n_mma = 256, up to 8 for narrower tiles) walk the units.  Roles: warp 0 issues TMA loads, warp 1 owns TMEM and
 // issues the MMAs into one of two accumulators (so the epilogue of a unit
 // overlaps the MMAs of the next), warps 2-5 drain TMEM with tcgen05.ld (warp
 // q owns TMEM lanes / tile rows 32(q%4) ...) and write C directly.  With a
@@ -46,12 +46,12 @@ namespace {
 constexpr int BM = 128;
 constexpr int kKBytes = 128;                       // bytes of K per K-block
 constexpr int kThreads = 192;
-constexpr int kStages = 4;
+constexpr int kMaxStages = 8;
+constexpr int kRingBytes = 4 * (128 * 128 + 256 * 128);   // 192 KB of stages
 constexpr int kMaxN = 256;
+constexpr int kMaxSplits = 8;
 constexpr int kABytes = BM * kKBytes;              // 16 KB
-constexpr int kBBytesMax = kMaxN * kKBytes;        // 32 KB
-constexpr int kStageBytes = kABytes + kBBytesMax;  // 48 KB
-constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * kStageBytes + 256;
+constexpr size_t kSmem = 1024 + static_cast<size_t>(kRingBytes) + 256;
 
 enum TcOp : int {
     kOpBf16K = 0,    // bf16, B [N, K] K-major
@@ -67,6 +67,7 @@ enum TcEpi : int {
 struct TcGemmParams {
     int M, N, K;
     int n_mma, num_kb, kb_per_split, splits;
+    int stages;            // ring depth: kRingBytes / (A block + B block), at most kMaxStages
     int m_tiles, n_tiles, units;
     int op, epi;
     float alpha, beta;
@@ -167,9 +168,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint8_t* base = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint8_t* stages = base;
-    uint64_t* full = reinterpret_cast<uint64_t*>(base + kStages * kStageBytes);
-    uint64_t* empty = full + kStages;
-    uint64_t* tfull = empty + kStages;
+    const int kStages = p.stages;
+    const uint32_t kStageBytes = static_cast<uint32_t>(kABytes) + static_cast<uint32_t>(p.n_mma) * kKBytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + kRingBytes);
+    uint64_t* empty = full + kMaxStages;
+    uint64_t* tfull = empty + kMaxStages;
     uint64_t* tempty = tfull + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
     volatile uint32_t* abort_flag = tmem_slot + 1;
@@ -305,6 +308,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 tmem_ld_wait();
                 if (!ok) continue;
                 if (partial) {
+                    if (row >= p.M) continue;   // rows past M are never summed
 #pragma unroll
                     for (int j = 0; j < 32; j += 4)
                         __stcg(reinterpret_cast<uint4*>(wrow + c0 + j), make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]));
@@ -335,27 +339,51 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             named_barrier_sync(1, 128);   // everyone has read last_flag before the next unit rewrites it
             if (!last) continue;
             __threadfence();
-            if (row < p.M) {
-                const uint32_t* trow = static_cast<const uint32_t*>(p.ws) +
-                                       (static_cast<int64_t>(tile) * p.splits * BM + row_in) * p.n_mma;
+            {
+                // The tile's valid rows x n_mma/4 column quads, row-major over
+                // the 128 epilogue threads (coalesced 16-byte loads), two quads
+                // per thread per round with every split's load in flight.
+                const uint32_t* tbase = static_cast<const uint32_t*>(p.ws) +
+                                        static_cast<int64_t>(tile) * p.splits * BM * p.n_mma;
                 const int64_t sstride = static_cast<int64_t>(BM) * p.n_mma;
-                for (int c0 = 0; c0 < p.n_mma; c0 += 4) {
-                    if (col0 + c0 >= p.N) break;
-                    int32_t si[4] = {0, 0, 0, 0};
-                    float sf[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                    for (int sp = 0; sp < p.splits; ++sp) {
-                        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(trow + sp * sstride + c0));
-                        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+                const int mrows = min(BM, p.M - mt * BM);
+                const int quads = p.n_mma / 4;
+                const int items = mrows * quads;
+                for (int i0 = ep_tid; i0 < items; i0 += 2 * 128) {
+                    uint4 v[2][kMaxSplits];
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            si[j] += static_cast<int32_t>(w[j]);
-                            sf[j] += __uint_as_float(w[j]);
-                        }
+                    for (int h = 0; h < 2; ++h) {
+                        const int item = i0 + h * 128;
+#pragma unroll
+                        for (int sp = 0; sp < kMaxSplits; ++sp)
+                            if (item < items && sp < p.splits)
+                                v[h][sp] = __ldcg(reinterpret_cast<const uint4*>(
+                                    tbase + sp * sstride + (item / quads) * p.n_mma + (item % quads) * 4));
                     }
-                    uint32_t w[4];
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) w[j] = p.epi == kEpiF32 ? __float_as_uint(sf[j]) : static_cast<uint32_t>(si[j]);
-                    store4(p, row, col0 + c0, w);
+                    for (int h = 0; h < 2; ++h) {
+                        const int item = i0 + h * 128;
+                        if (item >= items) break;
+                        const int r_in = item / quads, c4 = (item % quads) * 4;
+                        if (col0 + c4 >= p.N) continue;
+                        int32_t si[4] = {0, 0, 0, 0};
+                        float sf[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                        for (int sp = 0; sp < kMaxSplits; ++sp) {
+                            if (sp >= p.splits) break;
+                            const uint32_t w4[4] = {v[h][sp].x, v[h][sp].y, v[h][sp].z, v[h][sp].w};
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                si[j] += static_cast<int32_t>(w4[j]);
+                                sf[j] += __uint_as_float(w4[j]);
+                            }
+                        }
+                        uint32_t w[4];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            w[j] = p.epi == kEpiF32 ? __float_as_uint(sf[j]) : static_cast<uint32_t>(si[j]);
+                        store4(p, mt * BM + r_in, col0 + c4, w);
+                    }
                 }
             }
             if (ep_tid == 0) p.tickets[tile] = 0u;   // ready for the next launch on this stream
@@ -423,13 +451,18 @@ TcPlan gemm_tc_plan(TcKind kind, const GemmArgs& g, int num_sms) {
     const bool mn = kind == TcKind::BF16 && !g.b_trans;
     int n = g.N < kMaxN ? g.N : kMaxN;
     n = mn ? (n + 63) / 64 * 64 : (n + 31) / 32 * 32;
+    const int m_tiles = (g.M + BM - 1) / BM;
+    // Narrower tiles before a K split: a split tile's last CTA sums every
+    // split's partial tile alone, so more tiles (B columns read by more CTAs,
+    // A re-read from L2) cost less than deep splits.
+    while (n > 64 && m_tiles * ((g.N + n - 1) / n) * 2 <= num_sms) n /= 2;
     pl.n_mma = n;
-    const int m_tiles = (g.M + BM - 1) / BM, n_tiles = (g.N + n - 1) / n;
+    const int n_tiles = (g.N + n - 1) / n;
     const int elems = kind == TcKind::BF16 ? kKBytes / 2 : kKBytes;
     const int num_kb = (g.K + elems - 1) / elems;
     const int tiles = m_tiles * n_tiles;
     int splits = 1;
-    while (tiles * splits * 2 <= num_sms && num_kb / (splits * 2) >= 4 && splits < 16) splits *= 2;
+    while (tiles * splits * 2 <= num_sms && num_kb / (splits * 2) >= 4 && splits < kMaxSplits) splits *= 2;
     pl.kb_per_split = (num_kb + splits - 1) / splits;
     pl.splits = (num_kb + pl.kb_per_split - 1) / pl.kb_per_split;
     return pl;
@@ -448,7 +481,7 @@ int gemm_tc_tickets(const GemmArgs& g, const TcPlan& pl) {
 cudaError_t launch_gemm_tc(TcKind kind, DotKind epi, const GemmArgs& g, const TcPlan& pl, const float* scales,
                            void* ws, uint32_t* tickets, uint32_t* err, int num_sms, cudaStream_t s) {
     if (!gemm_tc_supported(kind, g) || pl.n_mma < 16 || pl.n_mma > kMaxN) return cudaErrorInvalidValue;
-    if (pl.splits > 1 && (!ws || !tickets)) return cudaErrorInvalidValue;
+    if (pl.splits > kMaxSplits || (pl.splits > 1 && (!ws || !tickets))) return cudaErrorInvalidValue;
     const bool mn = kind == TcKind::BF16 && !g.b_trans;
     const int op = kind == TcKind::BF16 ? (mn ? kOpBf16MN : kOpBf16K) : kOpI8;
     CUtensorMap tmA, tmB;
@@ -482,6 +515,8 @@ cudaError_t launch_gemm_tc(TcKind kind, DotKind epi, const GemmArgs& g, const Tc
     p.epi = epi == DotKind::S8S32 ? kEpiS32 : (epi == DotKind::S8DQ ? kEpiS8DQ : kEpiF32);
     p.alpha = g.alpha; p.beta = g.beta;
     p.C = g.C; p.ldc = g.ldc;
+    p.stages = kRingBytes / (kABytes + pl.n_mma * kKBytes);
+    if (p.stages > kMaxStages) p.stages = kMaxStages;
     p.scales = scales;
     p.c_vec = aligned16(g.C) && g.ldc % 4 == 0 ? 1 : 0;
     p.ws = ws;

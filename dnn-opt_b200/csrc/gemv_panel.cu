@@ -57,7 +57,7 @@ struct PanelParams {
 };
 
 template <int MT, int U, int kPanel>
-__global__ void __launch_bounds__(kThreads, kPanel == 64 ? 3 : 2)
+__global__ void __launch_bounds__(kThreads, (kPanel == 64 && U <= 8) ? 3 : 2)
 gemv_panel_kernel(const PanelParams p) {
     constexpr int kQ = kPanel / 32;                        // columns per lane
     constexpr int kMaxOut = (MT * kPanel + kThreads - 1) / kThreads;
@@ -270,20 +270,23 @@ gemv_panel_kernel(const PanelParams p) {
 }
 
 // Rows per warp batch (two batches in flight): 4 for 128-column panels, 8
-// for 64-column ones, i.e. 16 KB of loads in flight per CTA either way.
+// for 64-column ones (16 KB of loads in flight per CTA either way), 16 for
+// 64-column panels over the whole K (one CTA streams a 64-column panel alone,
+// so it keeps 32 KB in flight).
 template <int MT>
-const void* panel_fn(int w) {
-    return w == 64 ? reinterpret_cast<const void*>(&gemv_panel_kernel<MT, 8, 64>)
-                   : reinterpret_cast<const void*>(&gemv_panel_kernel<MT, 4, 128>);
+const void* panel_fn(int w, int splits) {
+    if (w == 64) return splits == 1 ? reinterpret_cast<const void*>(&gemv_panel_kernel<MT, 16, 64>)
+                                    : reinterpret_cast<const void*>(&gemv_panel_kernel<MT, 8, 64>);
+    return reinterpret_cast<const void*>(&gemv_panel_kernel<MT, 4, 128>);
 }
 
-const void* panel_select(int mt, int w) {
+const void* panel_select(int mt, int w, int splits) {
     if (w != 64 && w != 128) return nullptr;
     switch (mt) {
-        case 1: return panel_fn<1>(w);
-        case 2: return panel_fn<2>(w);
-        case 4: return panel_fn<4>(w);
-        case 8: return panel_fn<8>(w);
+        case 1: return panel_fn<1>(w, splits);
+        case 2: return panel_fn<2>(w, splits);
+        case 4: return panel_fn<4>(w, splits);
+        case 8: return panel_fn<8>(w, splits);
         default: return nullptr;
     }
 }
@@ -315,7 +318,7 @@ int gemv_panel_rows(int K, int splits) {
 }
 
 bool gemv_panel_supported(const GemmArgs& g, int mt, int w, int splits) {
-    if (!panel_select(mt, w) || g.M < 1 || g.M > mt || g.N < 1 || g.K < 1 || g.b_trans) return false;
+    if (!panel_select(mt, w, splits) || g.M < 1 || g.M > mt || g.N < 1 || g.K < 1 || g.b_trans) return false;
     if (splits != 1 && splits != 2 && splits != 4 && splits != 8) return false;
     const int rows = gemv_panel_rows(g.K, splits);
     // Every split holds at least one row and at most kMaxRows.
@@ -324,8 +327,8 @@ bool gemv_panel_supported(const GemmArgs& g, int mt, int w, int splits) {
 
 int gemv_panel_ctas(int N, int w, int splits) { return (N + w - 1) / w * splits; }
 
-cudaError_t gemv_panel_occupancy(int mt, int w, int rows, int* blocks_per_sm) {
-    const void* fn = panel_select(mt, w);
+cudaError_t gemv_panel_occupancy(int mt, int w, int splits, int rows, int* blocks_per_sm) {
+    const void* fn = panel_select(mt, w, splits);
     if (!fn) return cudaErrorInvalidValue;
     cudaError_t e = panel_prepare(fn);
     if (e != cudaSuccess) return e;
@@ -344,7 +347,7 @@ cudaError_t launch_gemv_panel(const GemmArgs& g, int mt, int w, int splits, floa
                               cudaStream_t s) {
     if (!gemv_panel_supported(g, mt, w, splits)) return cudaErrorInvalidValue;
     if (splits > 1 && (!ws || !counters)) return cudaErrorInvalidValue;
-    const void* fn = panel_select(mt, w);
+    const void* fn = panel_select(mt, w, splits);
     cudaError_t e = panel_prepare(fn);
     if (e != cudaSuccess) return e;
     PanelParams pp;

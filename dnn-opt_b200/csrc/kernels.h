@@ -81,7 +81,7 @@ bool gemv_panel_supported(const GemmArgs& g, int mt, int w, int splits);
 int gemv_panel_ctas(int N, int w, int splits);
 size_t gemv_panel_ws_floats(int N, int mt, int w, int splits);
 int gemv_panel_tickets(int N, int w);
-cudaError_t gemv_panel_occupancy(int mt, int w, int rows, int* blocks_per_sm);
+cudaError_t gemv_panel_occupancy(int mt, int w, int splits, int rows, int* blocks_per_sm);
 cudaError_t launch_gemv_panel(const GemmArgs& g, int mt, int w, int splits, float* ws, uint32_t* counters,
                               cudaStream_t s);
 

@@ -3,9 +3,9 @@
 // Dispatch rules (B200 re-statement of src/gemm/gemm.cpp:168-455, where the
 // reference routes by M < small_m_bound (8), N >= wide_n_bound and K):
 //   * FP32, M <= 8, B stored K x N, N >= 512, K <= 2048
-//                                    -> GemvPanel (128-column panels, row
-//                                      segments by bulk copy, K ranges reduced
-//                                      in a cluster)
+//                                    -> GemvPanel (64-column panels read as
+//                                      whole row segments, K ranges summed by
+//                                      the last CTA of each panel)
 //   * M <= 8 and B stored K x N      -> GemvSlab (whole K per 8-column CTA) for
 //                                      K <= 2048 and 512 <= N <= 8192, where a
 //                                      split-K reduction costs more than the B
@@ -145,16 +145,18 @@ int nk_occupancy(DotKind kind, int mt, int vec, int K, const DeviceInfo& info) {
     return memo_occupancy(key * 4 + 3, [&](int* occ) { return gemv_nk_occupancy(kind, mt, vec, K, occ); });
 }
 
-// Row-panel GEMV (FP32, B K x N): 128-column panels and the K extent split
-// into power-of-two ranges of about 128 rows (at most 8, one cluster), so a
-// 1024-row B gives 8 CTAs per panel that each keep three 32-row stages of
-// bulk copies in flight.  Deep K (above 2048) stays with split-K.
+// Row-panel GEMV (FP32, B K x N): 64-column panels and the K extent split
+// into power-of-two ranges of about 256 rows (at most 8), so a 1024-row B
+// gives 4 CTAs per panel.  Measured on B200 on the irregular-N sweep (12
+// GEMMs, K = 1024, one stream each, graph replay): 38.1 us against 46.7 for
+// the column slabs, 43.1 for 128-column panels in 4 ranges, 44.8 in 8.  Deep
+// K (above 2048) stays with split-K.
 bool panel_plan(const GemmArgs& g, int* w, int* splits) {
-    if (g.K > 2048) return false;   // deep K: the split-K kernel (measured at K = 4096)
+    if (g.K > 2048) return false;
     int s = 1;
-    while (s < 8 && g.K / (2 * s) >= 128) s *= 2;
-    if (!gemv_panel_supported(g, mt_for(g.M), 128, s)) return false;
-    *w = 128;
+    while (s < 8 && g.K / (2 * s) >= 256) s *= 2;
+    if (!gemv_panel_supported(g, mt_for(g.M), 64, s)) return false;
+    *w = 64;
     *splits = s;
     return true;
 }

@@ -129,14 +129,14 @@ def test_plan_selection_without_device(dn):
     # Dispatch classes of the reference's shape router (src/gemm/gemm.cpp:168-455).
     s = dn.plan_describe(dn.KIND_F32, dn.desc(1, 4096, 4096, 4096, 4096, 4096))
     assert s.startswith("gemv_kn_splitk mt=1 vec4=1"), s
-    # The irregular-N sweep (K = 1024): 128-column row panels, K in 8 ranges
-    # of 128 rows reduced in a cluster.
+    # The irregular-N sweep (K = 1024): 64-column row panels, K in 4 ranges
+    # of 256 rows, reduced by the last CTA of each panel.
     s = dn.plan_describe(dn.KIND_F32, dn.desc(7, 4093, 1024, 1024, 4093, 4093, beta=0.5))
-    assert s == "gemv_panel mt=8 w=128 splits=8 ctas=256", s
+    assert s == "gemv_panel mt=8 w=64 splits=4 ctas=256", s
     s = dn.plan_describe(dn.KIND_F32, dn.desc(2, 1009, 1024, 1024, 1009, 1009))
-    assert s == "gemv_panel mt=2 w=128 splits=8 ctas=64", s
+    assert s == "gemv_panel mt=2 w=64 splits=4 ctas=64", s
     s = dn.plan_describe(dn.KIND_F32, dn.desc(3, 2039, 600, 600, 2039, 2039))
-    assert s == "gemv_panel mt=4 w=128 splits=4 ctas=64", s   # 600 rows: 4 ranges of 160
+    assert s == "gemv_panel mt=4 w=64 splits=2 ctas=64", s   # 600 rows: 2 ranges of 304
     # Other encodings of the same shapes keep the whole-K column slabs.
     s = dn.plan_describe(dn.KIND_BF16F32, dn.desc(7, 4093, 1024, 1024, 4093, 4093, beta=0.5))
     assert s == "gemv_kn_slab mt=8 w=8 ctas=512", s
