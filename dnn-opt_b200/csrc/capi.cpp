@@ -647,7 +647,19 @@ int conv3d_device(int precision, const Conv3dGeom& g, const float* in, const flo
     // INT8 with IC % 16 == 0 and M >= 64: the dp4a kernel gathers 16-byte
     // channel segments from the quantised input, so no column matrix (the
     // workspace buffers are 256-byte aligned, so only the geometry decides).
-    const bool implicit8 = precision == DNNOPT_CONV3D_INT8 && gemm_tile_s8_conv_ok(g, nullptr, nullptr);
+    // When the column matrix can feed the tcgen05 GEMM (dense int8 rows of a
+    // 16-byte multiple), materialising it and running kind::i8 beats the
+    // dp4a implicit GEMM (the column matrix write costs less than the dp4a
+    // arithmetic), so the implicit form is kept for the other shapes.
+    GemmArgs probe{};
+    probe.M = static_cast<int>(g.M); probe.N = g.OC; probe.K = static_cast<int>(g.K);
+    // The column matrix and the quantised filter live in the 256-byte aligned
+    // workspace: only the geometry decides (the address is never dereferenced).
+    const void* ws_like = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
+    probe.A = ws_like; probe.lda = g.K; probe.B = ws_like; probe.ldb = g.K; probe.b_trans = 1;
+    probe.C = out; probe.ldc = g.OC;
+    const bool tc8 = precision == DNNOPT_CONV3D_INT8 && g.M > 8 && gemm_tc_supported(TcKind::I8, probe);
+    const bool implicit8 = precision == DNNOPT_CONV3D_INT8 && !tc8 && gemm_tile_s8_conv_ok(g, nullptr, nullptr);
     const size_t col_b = implicit8 ? 0 : up(static_cast<size_t>(g.M) * g.K * eb);
     const size_t flt_b = precision ? up(static_cast<size_t>(g.OC) * g.K * eb) : 0;
     const size_t acc_b = precision == DNNOPT_CONV3D_INT8 && !implicit8 ? up(static_cast<size_t>(g.M) * g.OC * 4) : 0;

@@ -347,13 +347,20 @@ Plan heuristic_plan(Kind kind, const GemmArgs& g, const DeviceInfo& info) {
         p.nk = nk_plan_for(kind, g, info, 0);
         return p;
     }
-    if (kind == Kind::BF16F32 && g.M > 8 && info.have_device && gemm_bf16_tc_kchunk(g) > 0) {
+    // BF16 with large M: the tall-skinny kernel while B stays resident in
+    // shared memory (N <= 256, K whole); otherwise the streaming tcgen05 GEMM
+    // (the tall-skinny kernel would run K in chunks, re-reading C each time).
+    if (kind == Kind::BF16F32 && g.M > 8 && info.have_device && gemm_bf16_tc_kchunk(g) == g.K) {
         p.kernel = KernelId::Bf16Tc;
         return p;
     }
     if (kind == Kind::BF16F32 && g.M > 8 && gemm_tc_supported(TcKind::BF16, g)) {
         p.kernel = KernelId::GemmTc;
         p.tc = gemm_tc_plan(TcKind::BF16, g, info.num_sms);
+        return p;
+    }
+    if (kind == Kind::BF16F32 && g.M > 8 && info.have_device && gemm_bf16_tc_kchunk(g) > 0) {
+        p.kernel = KernelId::Bf16Tc;   // K in chunks (unaligned operands for the streaming kernel)
         return p;
     }
     p.kernel = KernelId::TileF32;
