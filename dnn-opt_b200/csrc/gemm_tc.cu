@@ -49,9 +49,12 @@ constexpr int kThreads = 192;
 constexpr int kMaxStages = 8;
 constexpr int kRingBytes = 4 * (128 * 128 + 256 * 128);   // 192 KB of stages
 constexpr int kMaxN = 256;
-constexpr int kMaxSplits = 8;
+constexpr int kMaxSplits = 4;
+constexpr int kRedItems = 4;                       // column quads per thread per reduction round
 constexpr int kABytes = BM * kKBytes;              // 16 KB
-constexpr size_t kSmem = 1024 + static_cast<size_t>(kRingBytes) + 256;
+constexpr int kCStageBytes = 32 * 128;                // one 32 x 32 4-byte store block
+constexpr int kCStaging = 4 * 2 * kCStageBytes;       // 4 epilogue warps x 2 buffers
+constexpr size_t kSmem = 1024 + static_cast<size_t>(kRingBytes) + kCStaging + 256;
 
 enum TcOp : int {
     kOpBf16K = 0,    // bf16, B [N, K] K-major
@@ -75,6 +78,7 @@ struct TcGemmParams {
     int64_t ldc;
     const float* scales;   // {sA, sB} for kEpiS8DQ
     int c_vec;             // 1: C 16-byte aligned with ldc % 4 == 0 (vector epilogue)
+    int c_tma;             // 1: unsplit tiles with beta == 0 go out by TMA stores (tmC)
     void* ws;              // [tiles][splits][BM][n_mma] partials (splits > 1)
     uint32_t* tickets;     // one per tile, zero on entry, left zero
     uint32_t* err;
@@ -163,14 +167,15 @@ __device__ __forceinline__ void store4(const TcGemmParams& p, int row, int col, 
 
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const TcGemmParams p) {
+               const __grid_constant__ CUtensorMap tmC, const TcGemmParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint8_t* stages = base;
     const int kStages = p.stages;
     const uint32_t kStageBytes = static_cast<uint32_t>(kABytes) + static_cast<uint32_t>(p.n_mma) * kKBytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(base + kRingBytes);
+    uint8_t* sC = base + kRingBytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + kRingBytes + kCStaging);
     uint64_t* empty = full + kMaxStages;
     uint64_t* tfull = empty + kMaxStages;
     uint64_t* tempty = tfull + 2;
@@ -192,6 +197,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         fence_mbar_init();
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
+        if (p.c_tma) prefetch_tmap(&tmC);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, tmem_cols);
@@ -244,11 +250,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
+        // One instruction form per operand kind, hoisted out of the K loop:
+        // 32 bytes of K per MMA, +32 B along a K-major 128-byte row, or two
+        // 1024-B atoms (16 K rows) down an MN-major chunk.
         if (lane == 0) {
             const uint32_t idesc = tc_idesc(p.op, BM, p.n_mma);
             uint32_t it = 0, titer = 0;
             bool ok = true;
-            for (int u = blockIdx.x; ok && u < p.units && !*abort_flag; u += gridDim.x, ++titer) {
+            for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++titer) {
                 int split, mt, nt, kb0, nkb;
                 unit_coords(u, split, mt, nt);
                 unit_kbs(split, kb0, nkb);
@@ -262,16 +271,21 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(stages + s * kStageBytes);
                     const uint32_t b_addr = a_addr + kABytes;
+                    if (p.op == kOpI8) {
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        // 32 bytes of K per MMA: +32 B along a K-major 128-byte
-                        // row; two 1024-B atoms (16 K rows) down an MN-major chunk.
-                        const uint64_t adesc = umma_desc_k_sw128(a_addr + kk * 32);
-                        const uint64_t bdesc = p.op == kOpBf16MN ? desc_mn_sw128(b_addr + kk * 2048, 8192)
-                                                                 : umma_desc_k_sw128(b_addr + kk * 32);
-                        const uint32_t accum = (kb | kk) != 0 ? 1u : 0u;
-                        if (p.op == kOpI8) umma_i8_ss(d_tmem, adesc, bdesc, idesc, accum);
-                        else umma_f16_ss(d_tmem, adesc, bdesc, idesc, accum);
+                        for (int kk = 0; kk < 4; ++kk)
+                            umma_i8_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32), umma_desc_k_sw128(b_addr + kk * 32),
+                                       idesc, (kb | kk) != 0);
+                    } else if (p.op == kOpBf16MN) {
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            umma_f16_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32), desc_mn_sw128(b_addr + kk * 2048, 8192),
+                                        idesc, (kb | kk) != 0);
+                    } else {
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            umma_f16_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32), umma_desc_k_sw128(b_addr + kk * 32),
+                                        idesc, (kb | kk) != 0);
                     }
                     umma_commit(&empty[s]);   // stage free once these MMAs retire
                 }
@@ -283,12 +297,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         // ---------------- epilogue (warps 2..5) ----------------
         const int q = warp & 3;           // TMEM lanes 32q .. 32q+31 (warp id mod 4)
         const int ep_tid = tid - 64;      // 0..127
-        uint32_t titer = 0;
+        uint32_t titer = 0, cgrp = 0;
         for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x, ++titer) {
             int split, mt, nt;
             unit_coords(u, split, mt, nt);
             const uint32_t buf = titer & 1u, tph = (titer >> 1) & 1u;
-            const bool ok = mbar_wait(&tfull[buf], tph, abort_flag, p.err);
+            const bool ok = mbar_wait_warp(&tfull[buf], tph, abort_flag, p.err);
             tc_fence_after();
             const int row_in = q * 32 + lane;
             const int row = mt * BM + row_in;
@@ -312,6 +326,35 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
                     for (int j = 0; j < 32; j += 4)
                         __stcg(reinterpret_cast<uint4*>(wrow + c0 + j), make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]));
+                } else if (p.c_tma) {
+                    // beta == 0: the 32 x 32 block (rows 32q.., columns c0..)
+                    // through 128-byte-swizzled shared memory and one TMA store
+                    // (rows >= M, columns >= N clipped by the tensor map).
+                    if (col0 + c0 >= p.N) continue;
+                    uint8_t* sbuf = sC + (q * 2 + (cgrp & 1u)) * kCStageBytes;
+                    if (lane == 0) tma_store_wait_read<1>();   // this buffer's previous store has read it
+                    __syncwarp();
+                    const float dq = p.epi == kEpiS8DQ ? __fmul_rn(p.alpha, __fmul_rn(p.scales[0], p.scales[1])) : 0.0f;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const uint32_t raw = r[c * 4 + j];
+                            w[j] = p.epi == kEpiS32 ? raw
+                                 : (p.epi == kEpiF32 ? __float_as_uint(p.alpha * __uint_as_float(raw))
+                                                     : __float_as_uint(__fadd_rn(0.0f, __fmul_rn(dq, static_cast<float>(static_cast<int32_t>(raw))))));
+                        }
+                        *reinterpret_cast<uint4*>(sbuf + lane * 128 + ((c ^ (lane & 7)) * 16)) =
+                            make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmC, sbuf, col0 + c0, mt * BM + q * 32);
+                        tma_store_commit();
+                    }
+                    ++cgrp;
                 } else if (row < p.M) {
 #pragma unroll
                     for (int j = 0; j < 32; j += 4) {
@@ -341,18 +384,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             __threadfence();
             {
                 // The tile's valid rows x n_mma/4 column quads, row-major over
-                // the 128 epilogue threads (coalesced 16-byte loads), two quads
-                // per thread per round with every split's load in flight.
+                // the 128 epilogue threads (coalesced 16-byte loads),
+                // kRedItems quads per thread per round with every split's load
+                // in flight.
                 const uint32_t* tbase = static_cast<const uint32_t*>(p.ws) +
                                         static_cast<int64_t>(tile) * p.splits * BM * p.n_mma;
                 const int64_t sstride = static_cast<int64_t>(BM) * p.n_mma;
                 const int mrows = min(BM, p.M - mt * BM);
                 const int quads = p.n_mma / 4;
                 const int items = mrows * quads;
-                for (int i0 = ep_tid; i0 < items; i0 += 2 * 128) {
-                    uint4 v[2][kMaxSplits];
+                for (int i0 = ep_tid; i0 < items; i0 += kRedItems * 128) {
+                    uint4 v[kRedItems][kMaxSplits];
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
+                    for (int h = 0; h < kRedItems; ++h) {
                         const int item = i0 + h * 128;
 #pragma unroll
                         for (int sp = 0; sp < kMaxSplits; ++sp)
@@ -361,7 +405,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                                     tbase + sp * sstride + (item / quads) * p.n_mma + (item % quads) * 4));
                     }
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
+                    for (int h = 0; h < kRedItems; ++h) {
                         const int item = i0 + h * 128;
                         if (item >= items) break;
                         const int r_in = item / quads, c4 = (item % quads) * 4;
@@ -388,6 +432,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             }
             if (ep_tid == 0) p.tickets[tile] = 0u;   // ready for the next launch on this stream
         }
+        if (p.c_tma && lane == 0) tma_store_wait_all<0>();   // staging must outlive the stores' reads
     }
 
     tc_fence_before();
@@ -501,7 +546,15 @@ cudaError_t launch_gemm_tc(TcKind kind, DotKind epi, const GemmArgs& g, const Tc
                     static_cast<uint32_t>(pl.n_mma)))
             return cudaErrorInvalidValue;
     }
+    // Unsplit tiles with beta == 0 store C by TMA when C's rows are 16-byte
+    // strided and aligned.
+    CUtensorMap tmC = tmA;
+    const bool c_tma = pl.splits == 1 && g.beta == 0.0f && aligned16(g.C) && (g.ldc * 4) % 16 == 0 &&
+                       encode(&tmC, epi == DotKind::S8S32 ? CU_TENSOR_MAP_DATA_TYPE_INT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                              g.C, g.N, g.M, static_cast<uint64_t>(g.ldc) * 4, 32, 32);
+    if (!c_tma) tmC = tmA;   // unused
     TcGemmParams p;
+    p.c_tma = c_tma ? 1 : 0;
     p.M = g.M; p.N = g.N; p.K = g.K;
     p.n_mma = pl.n_mma;
     const int elems = kind == TcKind::BF16 ? kKBytes / 2 : kKBytes;
@@ -547,7 +600,7 @@ cudaError_t launch_gemm_tc(TcKind kind, DotKind epi, const GemmArgs& g, const Tc
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, tmA, tmB, p);
+    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, tmA, tmB, tmC, p);
 }
 
 }  // namespace dnnopt_b200
