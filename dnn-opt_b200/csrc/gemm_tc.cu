@@ -70,7 +70,8 @@ enum TcEpi : int {
 struct TcGemmParams {
     int M, N, K;
     int n_mma, num_kb, kb_per_split, splits;
-    int stages;            // ring depth: kRingBytes / (A block + B block), at most kMaxStages
+    int kbs;               // 128-byte K-blocks per ring stage (2 for tiles of <= 128 columns)
+    int stages;            // ring depth: kRingBytes / stage bytes, at most kMaxStages
     int m_tiles, n_tiles, units;
     int op, epi;
     float alpha, beta;
@@ -173,7 +174,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint8_t* stages = base;
     const int kStages = p.stages;
-    const uint32_t kStageBytes = static_cast<uint32_t>(kABytes) + static_cast<uint32_t>(p.n_mma) * kKBytes;
+    const uint32_t kSubBytes = static_cast<uint32_t>(kABytes) + static_cast<uint32_t>(p.n_mma) * kKBytes;
+    const uint32_t kStageBytes = static_cast<uint32_t>(p.kbs) * kSubBytes;   // [A kb][B kb] per K-block
     uint8_t* sC = base + kRingBytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(base + kRingBytes + kCStaging);
     uint64_t* empty = full + kMaxStages;
@@ -230,20 +232,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 int split, mt, nt, kb0, nkb;
                 unit_coords(u, split, mt, nt);
                 unit_kbs(split, kb0, nkb);
-                for (int kb = kb0; kb < kb0 + nkb; ++kb, ++it) {
+                for (int kb = kb0; kb < kb0 + nkb; kb += p.kbs, ++it) {
                     const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
                     if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.err)) break;
-                    uint8_t* sa = stages + s * kStageBytes;
-                    uint8_t* sb = sa + kABytes;
-                    mbar_arrive_expect_tx(&full[s], kABytes + b_bytes);
-                    const int kx = p.op == kOpI8 ? kb * kKBytes : kb * (kKBytes / 2);   // elements
-                    tma_load_2d(sa, &tmA, &full[s], kx, mt * BM);
-                    if (p.op == kOpBf16MN) {
-                        // 64-column chunks of 64 K rows: chunk j at j * 8 KB.
-                        for (int j = 0; j < p.n_mma / 64; ++j)
-                            tma_load_2d(sb + j * 8192, &tmB, &full[s], nt * p.n_mma + j * 64, kx);
-                    } else {
-                        tma_load_2d(sb, &tmB, &full[s], kx, nt * p.n_mma);
+                    const int nsub = min(p.kbs, kb0 + nkb - kb);
+                    mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nsub) * (kABytes + b_bytes));
+                    for (int sub = 0; sub < nsub; ++sub) {
+                        uint8_t* sa = stages + s * kStageBytes + sub * kSubBytes;
+                        uint8_t* sb = sa + kABytes;
+                        const int kx = p.op == kOpI8 ? (kb + sub) * kKBytes : (kb + sub) * (kKBytes / 2);   // elements
+                        tma_load_2d(sa, &tmA, &full[s], kx, mt * BM);
+                        if (p.op == kOpBf16MN) {
+                            // 64-column chunks of 64 K rows: chunk j at j * 8 KB.
+                            for (int j = 0; j < p.n_mma / 64; ++j)
+                                tma_load_2d(sb + j * 8192, &tmB, &full[s], nt * p.n_mma + j * 64, kx);
+                        } else {
+                            tma_load_2d(sb, &tmB, &full[s], kx, nt * p.n_mma);
+                        }
                     }
                 }
             }
@@ -265,27 +270,31 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 if (!mbar_wait(&tempty[buf], tph ^ 1u, abort_flag, p.err)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + buf * static_cast<uint32_t>(p.n_mma);
-                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                for (int kb = 0; kb < nkb; kb += p.kbs, ++it) {
                     const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
                     if (!mbar_wait(&full[s], ph, abort_flag, p.err)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_u32(stages + s * kStageBytes);
-                    const uint32_t b_addr = a_addr + kABytes;
-                    if (p.op == kOpI8) {
+                    const int nsub = min(p.kbs, nkb - kb);
+                    for (int sub = 0; sub < nsub; ++sub) {
+                        const uint32_t a_addr = smem_u32(stages + s * kStageBytes + sub * kSubBytes);
+                        const uint32_t b_addr = a_addr + kABytes;
+                        const int kl = kb + sub;
+                        if (p.op == kOpI8) {
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
-                            umma_i8_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32), umma_desc_k_sw128(b_addr + kk * 32),
-                                       idesc, (kb | kk) != 0);
-                    } else if (p.op == kOpBf16MN) {
+                            for (int kk = 0; kk < 4; ++kk)
+                                umma_i8_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32),
+                                           umma_desc_k_sw128(b_addr + kk * 32), idesc, (kl | kk) != 0);
+                        } else if (p.op == kOpBf16MN) {
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
-                            umma_f16_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32), desc_mn_sw128(b_addr + kk * 2048, 8192),
-                                        idesc, (kb | kk) != 0);
-                    } else {
+                            for (int kk = 0; kk < 4; ++kk)
+                                umma_f16_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32),
+                                            desc_mn_sw128(b_addr + kk * 2048, 8192), idesc, (kl | kk) != 0);
+                        } else {
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
-                            umma_f16_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32), umma_desc_k_sw128(b_addr + kk * 32),
-                                        idesc, (kb | kk) != 0);
+                            for (int kk = 0; kk < 4; ++kk)
+                                umma_f16_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32),
+                                            umma_desc_k_sw128(b_addr + kk * 32), idesc, (kl | kk) != 0);
+                        }
                     }
                     umma_commit(&empty[s]);   // stage free once these MMAs retire
                 }
@@ -568,7 +577,10 @@ cudaError_t launch_gemm_tc(TcKind kind, DotKind epi, const GemmArgs& g, const Tc
     p.epi = epi == DotKind::S8S32 ? kEpiS32 : (epi == DotKind::S8DQ ? kEpiS8DQ : kEpiF32);
     p.alpha = g.alpha; p.beta = g.beta;
     p.C = g.C; p.ldc = g.ldc;
-    p.stages = kRingBytes / (kABytes + pl.n_mma * kKBytes);
+    // Narrow tiles carry two K-blocks per stage: the cost of a stage (barrier
+    // round trips, commit) is then paid once per 256 bytes of K.
+    p.kbs = pl.n_mma <= 128 ? 2 : 1;
+    p.stages = kRingBytes / (p.kbs * (kABytes + pl.n_mma * kKBytes));
     if (p.stages > kMaxStages) p.stages = kMaxStages;
     p.scales = scales;
     p.c_vec = aligned16(g.C) && g.ldc % 4 == 0 ? 1 : 0;
