@@ -257,7 +257,7 @@ Plan get_plan(Kind kind, const GemmArgs& g, DeviceContext* ctx, cudaStream_t s,
               const float* scales) {
     const DeviceInfo info = info_of(ctx);
     Plan h = heuristic_plan(kind, g, info);
-    const bool tunable = is_kn(h.kernel) || h.kernel == KernelId::GemvNk || h.kernel == KernelId::GemvRowsBulk ||
+    const bool tunable = is_kn(h.kernel) || h.kernel == KernelId::GemvNk || is_rows(h.kernel) ||
                          h.kernel == KernelId::E4m3Tc;
     if (!tunable) return h;
     const uint64_t key = plan_key(kind, g, vec_of(h));
@@ -333,9 +333,9 @@ Plan get_plan(Kind kind, const GemmArgs& g, DeviceContext* ctx, cudaStream_t s,
                     dup = dup || (cands[i].e4.splits == q.e4.splits && cands[i].e4.stages == q.e4.stages);
                 if (!dup && nc < kMaxCands) cands[nc++] = q;
             }
-    } else if (h.kernel == KernelId::GemvRowsBulk) {
-        // Bulk-copy rows kernel at its occupancy grid and half of it, and the
-        // register-load rows kernel at its own occupancy grid.
+    } else if (is_rows(h.kernel)) {
+        // Register-load rows kernel at its occupancy grid and half of it, and
+        // the bulk-copy ring at its own occupancy grid.
         const int g0 = h.nk.grid;
         for (int t : {g0, g0 / 2}) {
             if (t < 1) continue;
@@ -343,11 +343,11 @@ Plan get_plan(Kind kind, const GemmArgs& g, DeviceContext* ctx, cudaStream_t s,
             q.nk.grid = t;
             cands[nc++] = q;
         }
-        if (gemv_rows_supported(dot_kind(kind), g)) {
+        if (gemv_rows_bulk_supported(dot_kind(kind), g)) {
             Plan q = h;
-            q.kernel = KernelId::GemvRows;
+            q.kernel = KernelId::GemvRowsBulk;
             int occ = 1;
-            if (gemv_rows_occupancy(dot_kind(kind), h.nk.mt, g.K, &occ) != cudaSuccess || occ < 1) {
+            if (gemv_rows_bulk_occupancy(dot_kind(kind), h.nk.mt, g.K, &occ) != cudaSuccess || occ < 1) {
                 cudaGetLastError();
                 occ = 1;
             }

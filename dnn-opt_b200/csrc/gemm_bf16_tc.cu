@@ -204,16 +204,21 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                     if (!mbar_wait(&full[s], ph, abort_flag, p.err)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(sA + s * kStageBytes);
+                    // K step of 16: 32 bytes along a K-major row, or two
+                    // 1024-byte 8-row atoms down an MN-major chunk (the B
+                    // layout branch taken once per K-block).
+                    if (p.b_mode == kBTmaMN) {
 #pragma unroll
-                    for (int kk = 0; kk < kKBlock / 16; ++kk) {
-                        // K step of 16: 32 bytes along a K-major row, or two
-                        // 1024-byte 8-row atoms down an MN-major chunk.
-                        const uint64_t bdesc =
-                            p.b_mode == kBTmaMN
-                                ? umma_desc_mn_sw128(sb_addr + (kb * 8 + kk * 2) * 1024, lbo)
-                                : umma_desc_k_sw128(sb_addr + kb * p.n_mma * 128 + kk * 32);
-                        umma_f16_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32), bdesc, idesc,
-                                    (kb | kk) != 0 ? 1u : 0u);
+                        for (int kk = 0; kk < kKBlock / 16; ++kk)
+                            umma_f16_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32),
+                                        umma_desc_mn_sw128(sb_addr + (kb * 8 + kk * 2) * 1024, lbo), idesc,
+                                        (kb | kk) != 0 ? 1u : 0u);
+                    } else {
+#pragma unroll
+                        for (int kk = 0; kk < kKBlock / 16; ++kk)
+                            umma_f16_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32),
+                                        umma_desc_k_sw128(sb_addr + kb * p.n_mma * 128 + kk * 32), idesc,
+                                        (kb | kk) != 0 ? 1u : 0u);
                     }
                     umma_commit(&empty[s]);   // stage is free once these MMAs retire
                 }
@@ -234,7 +239,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         uint32_t titer = 0, gcount = 0;
         for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x, ++titer) {
             const uint32_t buf = titer & 1u, tph = (titer >> 1) & 1u;
-            if (!mbar_wait(&tfull[buf], tph, abort_flag, p.err)) break;
+            if (!mbar_wait_warp(&tfull[buf], tph, abort_flag, p.err)) break;
             tc_fence_after();
             const int row = tile * BM + q * 32 + lane;
             const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * p.n_mma;

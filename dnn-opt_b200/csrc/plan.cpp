@@ -14,10 +14,9 @@
 //                                      CTA) or, when autotune measures it faster,
 //                                      GemvKnCluster (splits reduced in a
 //                                      thread-block cluster) or GemvSlab
-//   * int8, M <= 8, B stored N x K, 16-byte rows of at most 512 chunks
-//                                    -> GemvRowsBulk (dot form, A in registers,
-//                                      B rows by bulk copy into a shared ring)
-//   * M <= 8 and B stored N x K      -> GemvRows / GemvNk (dot-form GEMV)
+//   * M <= 8 and B stored N x K      -> GemvRows (dot form, A in registers;
+//                                      autotune also times GemvRowsBulk, B rows
+//                                      by bulk copy into a shared ring) / GemvNk
 //   * BF16, large M, N <= 256        -> Bf16Tc  (tcgen05 tall-skinny, B resident)
 //   * BF16 M > 8 otherwise, int8 M > 8 (TMA-aligned operands)
 //                                    -> GemmTc  (tcgen05, both operands by TMA)
@@ -125,12 +124,6 @@ int slab_occupancy(Kind kind, int mt, int w, int K, const DeviceInfo& info) {
     return memo_occupancy(key * 4 + 1, [&](int* occ) {
         return gemv_slab_occupancy(in_a(kind), in_b(kind), mt, w, K, occ);
     });
-}
-
-int rows_bulk_occupancy(DotKind kind, int mt, int K, const DeviceInfo& info) {
-    if (!info.have_device) return 2;
-    const int64_t key = (static_cast<int64_t>(kind) * 16 + mt) * (int64_t{1} << 31) + K;
-    return memo_occupancy(key * 8 + 5, [&](int* occ) { return gemv_rows_bulk_occupancy(kind, mt, K, occ); });
 }
 
 int rows_occupancy(DotKind kind, int mt, int K, const DeviceInfo& info) {
@@ -269,12 +262,10 @@ Plan heuristic_plan(Kind kind, const GemmArgs& g, const DeviceInfo& info) {
     switch (kind) {
         case Kind::S8S32:
         case Kind::F32S8Q:
-            if (g.M <= 8 && gemv_rows_bulk_supported(dot_kind(kind), g)) {
-                p.kernel = KernelId::GemvRowsBulk;
-                p.nk.mt = mt_for(g.M);
-                p.nk.vec = 1;
-                p.nk.grid = rows_bulk_occupancy(dot_kind(kind), p.nk.mt, g.K, info) * info.num_sms;
-            } else if (g.M <= 8 && gemv_rows_supported(dot_kind(kind), g)) {
+            // Dot form with A in registers: the register-load kernel (config
+            // 3: 10.3 us against 10.5 for the bulk-copy ring, which autotune
+            // also times).
+            if (g.M <= 8 && gemv_rows_supported(dot_kind(kind), g)) {
                 p.kernel = KernelId::GemvRows;
                 p.nk.mt = mt_for(g.M);
                 p.nk.vec = 1;

@@ -148,7 +148,7 @@ def test_plan_selection_without_device(dn):
     s = dn.plan_describe(dn.KIND_F32, dn.desc(2, 1009, 4096, 4096, 1009, 1009))
     assert s.startswith("gemv_kn_splitk mt=2 vec4=0 splits=16 kchunk=256"), s
     s = dn.plan_describe(dn.KIND_S8S32, dn.desc(4, 11008, 4096, 4096, 4096, 11008))
-    assert s.startswith("gemv_rows_bulk mt=4 vec=1"), s
+    assert s.startswith("gemv_rows_dot mt=4 vec=1"), s
     s = dn.plan_describe(dn.KIND_S8S32, dn.desc(4, 11008, 4100, 4100, 4100, 11008))
     assert s.startswith("gemv_nk_dot mt=4 vec=0"), s      # rows not 16-byte aligned
     s = dn.plan_describe(dn.KIND_E4M3BF16, dn.desc(8, 28672, 8192, 8192, 8192, 28672))

@@ -768,7 +768,7 @@ def test_plan_selection_on_device(gpu, dn):
     assert dn.plan_describe(dn.KIND_F32, dn.desc(1, 4096, 4096, 4096, 4096, 4096)).startswith(
         "gemv_kn_splitk mt=1 vec4=1 splits=16")
     assert dn.plan_describe(dn.KIND_S8S32, dn.desc(4, 11008, 4096, 4096, 4096, 11008)).startswith(
-        "gemv_rows_bulk mt=4 vec=1")
+        "gemv_rows_dot mt=4 vec=1")
 
 
 @pytest.mark.parametrize("splits", [2, 5, 8, 16])
