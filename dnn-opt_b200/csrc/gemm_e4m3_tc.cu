@@ -101,6 +101,28 @@ __device__ __forceinline__ float e4m3_byte_to_f32(uint32_t b) {
 
 // Activation operand: one CTA per activation row m (8 rows; rows >= M are
 // zero).  act is [16][kpad] e4m3 (row m = hi, row 8+m = lo), K-tail zero.
+// Each thread owns 16-byte chunks (8 bf16) c = tid + 256 i of its row: with
+// 16-byte aligned rows and K <= 16384 every chunk is loaded once, all loads
+// in flight together, and kept in registers for both the row maximum and the
+// split (one memory round trip); otherwise elements are read one at a time,
+// twice.  Either way the scale and the conversions are the same.
+constexpr int kPrepChunks = 8;   // chunks per thread held in registers (K <= 256 * 8 * 8)
+
+__device__ __forceinline__ void act_split8(const float (&x)[8], float sigma, uint2& hi, uint2& lo) {
+    float v[8], r[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = x[j] * sigma;
+    hi.x = f32x2_to_e4m3x2(v[0], v[1]) | (f32x2_to_e4m3x2(v[2], v[3]) << 16);
+    hi.y = f32x2_to_e4m3x2(v[4], v[5]) | (f32x2_to_e4m3x2(v[6], v[7]) << 16);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        r[j] = v[j] - e4m3_byte_to_f32(hi.x >> (8 * j));
+        r[4 + j] = v[4 + j] - e4m3_byte_to_f32(hi.y >> (8 * j));
+    }
+    lo.x = f32x2_to_e4m3x2(r[0], r[1]) | (f32x2_to_e4m3x2(r[2], r[3]) << 16);
+    lo.y = f32x2_to_e4m3x2(r[4], r[5]) | (f32x2_to_e4m3x2(r[6], r[7]) << 16);
+}
+
 __global__ void __launch_bounds__(256)
 e4m3_act_prep_kernel(const uint16_t* __restrict__ A, int64_t lda, int M, int K, int kpad,
                      uint8_t* __restrict__ act, float* __restrict__ inv_sigma) {
@@ -110,9 +132,32 @@ e4m3_act_prep_kernel(const uint16_t* __restrict__ A, int64_t lda, int M, int K, 
     const int m = blockIdx.x, tid = threadIdx.x;
     const bool live = m < M;
     const uint16_t* arow = A + (int64_t)m * lda;
+    const int nch = kpad / 8;   // kpad is a multiple of 128
+    const bool vec = (reinterpret_cast<uintptr_t>(arow) & 15u) == 0 && nch <= 256 * kPrepChunks;
+    float x[kPrepChunks][8];
     float amax = 0.0f;
-    if (live)
+    if (vec) {
+#pragma unroll
+        for (int i = 0; i < kPrepChunks; ++i) {
+            const int c = tid + 256 * i;
+            uint4 w = make_uint4(0u, 0u, 0u, 0u);
+            if (live && c < nch && c * 8 + 8 <= K) w = __ldg(reinterpret_cast<const uint4*>(arow) + c);
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                x[i][2 * j] = __uint_as_float(ww[j] << 16);
+                x[i][2 * j + 1] = __uint_as_float(ww[j] & 0xFFFF0000u);
+            }
+            if (live && c < nch && c * 8 < K && c * 8 + 8 > K) {   // the K tail chunk
+#pragma unroll
+                for (int j = 0; j < 8; ++j) x[i][j] = c * 8 + j < K ? bf16_bits_to_f32(arow[c * 8 + j]) : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(x[i][j]));
+        }
+    } else if (live) {
         for (int k = tid; k < K; k += 256) amax = fmaxf(amax, fabsf(bf16_bits_to_f32(arow[k])));
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
     if ((tid & 31) == 0) wmax[tid >> 5] = amax;
@@ -126,18 +171,26 @@ e4m3_act_prep_kernel(const uint16_t* __restrict__ A, int64_t lda, int M, int K, 
     e = max(-100, min(100, 8 - e));
     const float sigma = ldexpf(1.0f, e);
     if (tid == 0) inv_sigma[m] = ldexpf(1.0f, -e);
-    for (int k4 = tid * 4; k4 < kpad; k4 += 1024) {
-        float x[4];
+    if (vec) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-            x[j] = (live && k4 + j < K) ? bf16_bits_to_f32(arow[k4 + j]) * sigma : 0.0f;
-        uint32_t hi = f32x2_to_e4m3x2(x[0], x[1]) | (f32x2_to_e4m3x2(x[2], x[3]) << 16);
-        float r[4];
+        for (int i = 0; i < kPrepChunks; ++i) {
+            const int c = tid + 256 * i;
+            if (c >= nch) break;
+            uint2 hi, lo;
+            act_split8(x[i], sigma, hi, lo);
+            *reinterpret_cast<uint2*>(act + (int64_t)m * kpad + c * 8) = hi;
+            *reinterpret_cast<uint2*>(act + (int64_t)(8 + m) * kpad + c * 8) = lo;
+        }
+        return;
+    }
+    for (int c = tid; c < nch; c += 256) {
+        float xx[8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) r[j] = x[j] - e4m3_byte_to_f32(hi >> (8 * j));
-        uint32_t lo = f32x2_to_e4m3x2(r[0], r[1]) | (f32x2_to_e4m3x2(r[2], r[3]) << 16);
-        *reinterpret_cast<uint32_t*>(act + (int64_t)m * kpad + k4) = hi;
-        *reinterpret_cast<uint32_t*>(act + (int64_t)(8 + m) * kpad + k4) = lo;
+        for (int j = 0; j < 8; ++j) xx[j] = (live && c * 8 + j < K) ? bf16_bits_to_f32(arow[c * 8 + j]) : 0.0f;
+        uint2 hi, lo;
+        act_split8(xx, sigma, hi, lo);
+        *reinterpret_cast<uint2*>(act + (int64_t)m * kpad + c * 8) = hi;
+        *reinterpret_cast<uint2*>(act + (int64_t)(8 + m) * kpad + c * 8) = lo;
     }
 }
 
