@@ -275,12 +275,13 @@ def capture(torch, stream, fn):
     return g
 
 
-# DRAM bytes (read + write) of one C2 sweep, summed over its 12 launches, from
-# one ncu capture:  ncu --clock-control none --metrics
+# DRAM bytes (read + write) of one C2 sweep, summed over its 12 launches of
+# the row-panel GEMV, from one ncu capture:  ncu --clock-control none --metrics
 # dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum --csv
 # -k regex:gemv -s 12 -c 12 python bench.py --profile c2 --reps 2
-# (C is written into L2 and leaves it after the launch, so writes read 0).
-C2_DRAM_BYTES_PER_STEP = 117_963_264
+# (C and the split partials are written into L2 and leave it after the launch,
+# so writes read 0).
+C2_DRAM_BYTES_PER_STEP = 117_945_344
 
 
 def bench_single(torch, dn, stream, fn_list, bytes_per_call, flops_per_call, iters=30):
@@ -552,6 +553,15 @@ def run_profile(args):
             B = torch.from_numpy(bf16_bits(rng.standard_normal(K * N).astype(np.float32)).view(np.int16)).cuda()
             C = torch.zeros(M * N, device="cuda")
             calls.append(lambda A=A, B=B, C=C: dn.cuda_gemm("bf16f32", d, A, B, C, s))
+    elif name == "tc_i8":
+        # The general tcgen05 GEMM (kind::i8) on int8 2048^3, B stored [N, K].
+        M, N, K = 2048, 2048, 2048
+        d = dn.desc(M, N, K, K, K, N)
+        C = torch.zeros(M * N, dtype=torch.int32, device="cuda")
+        for i in range(4):
+            A = torch.randint(-127, 128, (M * K,), dtype=torch.int8, device="cuda")
+            B = torch.randint(-127, 128, (N * K,), dtype=torch.int8, device="cuda")
+            calls.append(lambda A=A, B=B: dn.cuda_gemm("s8s32", d, A, B, C, s))
     elif name == "c5":
         M, N, K = 8, 28672, 8192
         d = dn.desc(M, N, K, K, K, N)
@@ -736,7 +746,7 @@ def main():
     ap.add_argument("--streams", type=int, default=SWEEP_STREAMS,
                     help="streams the 12 independent sweep GEMMs are spread over")
     ap.add_argument("--no-per-config", action="store_true", help="skip the per-config section")
-    ap.add_argument("--profile", choices=["c1", "c2", "c3", "c4", "c5", "onednn", "simt64",
+    ap.add_argument("--profile", choices=["c1", "c2", "c3", "c4", "c5", "onednn", "simt64", "tc_i8",
                                          "conv3d_fp32", "conv3d_int8"],
                     help="run one config's kernel --reps times for an ncu capture, no bench line")
     ap.add_argument("--reps", type=int, default=3)
