@@ -487,14 +487,33 @@ int host_entry(Kind kind, const dnnopt_gemm_desc* d, const void* A, const void* 
         cudaError_t e = cudaMemcpyAsync(C, dev[2], ops[2].bytes, cudaMemcpyDeviceToHost, s);
         if (e != cudaSuccess) return cuda_status(e);
     }
+    // Bounded in-kernel waits report through the stream's error word: read it
+    // in the same stream, into a pinned word, so the call synchronises once.
+    auto it = ctx->ws.find(s);
+    const bool check_err = it != ctx->ws.end() && it->second.err;
+    if (check_err && !ctx->host_err) {
+        void* h = nullptr;
+        if (cudaHostAlloc(&h, sizeof(uint32_t), cudaHostAllocDefault) != cudaSuccess) {
+            cudaGetLastError();
+            h = nullptr;
+        }
+        ctx->host_err = static_cast<uint32_t*>(h);
+    }
+    uint32_t code = 0;
+    if (check_err && ctx->host_err) {
+        *ctx->host_err = 0u;
+        cudaError_t e = cudaMemcpyAsync(ctx->host_err, it->second.err, sizeof(uint32_t), cudaMemcpyDeviceToHost, s);
+        if (e != cudaSuccess) return cuda_status(e);
+    }
     cudaError_t e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_status(e);
-    // Bounded in-kernel waits report through the stream's error word.
-    auto it = ctx->ws.find(s);
-    if (it != ctx->ws.end() && it->second.err) {
-        uint32_t code = 0;
-        e = cudaMemcpy(&code, it->second.err, sizeof(code), cudaMemcpyDeviceToHost);
-        if (e != cudaSuccess) return cuda_status(e);
+    if (check_err) {
+        if (ctx->host_err) {
+            code = *ctx->host_err;
+        } else {
+            e = cudaMemcpy(&code, it->second.err, sizeof(code), cudaMemcpyDeviceToHost);
+            if (e != cudaSuccess) return cuda_status(e);
+        }
         if (code != 0) {
             cudaMemset(it->second.err, 0, sizeof(code));
             return set_status(DNNOPT_STATUS_KERNEL_TIMEOUT);

@@ -41,6 +41,9 @@ struct DeviceContext {
     // Device staging for host-pointer calls (host API).
     void* stage[4] = {nullptr, nullptr, nullptr, nullptr};
     size_t stage_bytes[4] = {0, 0, 0, 0};
+    // Pinned host word that receives the stream's kernel error word in the
+    // same stream as the result copy (host API), so a call syncs once.
+    uint32_t* host_err = nullptr;
 };
 
 // Returns the context of the current device (creating it), or nullptr with
