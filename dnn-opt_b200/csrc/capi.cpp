@@ -663,6 +663,27 @@ int conv3d_device(int precision, const Conv3dGeom& g, const float* in, const flo
     }
     const size_t eb = precision == DNNOPT_CONV3D_FP32 ? 4 : (precision == DNNOPT_CONV3D_BF16 ? 2 : 1);
     auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+    // BF16 / INT8 with stride 1 and channel rows of a 32-byte multiple: the
+    // operands converted (or quantised) once, then one implicit tcgen05 launch
+    // with bias, dequantisation and post-op in its epilogue.
+    if (precision != DNNOPT_CONV3D_FP32 && conv3d_tc_ok(g, precision)) {
+        const size_t cb = precision == DNNOPT_CONV3D_BF16 ? 2 : 1;
+        const int64_t cin = static_cast<int64_t>(g.N) * g.ID * g.IH * g.IW * g.IC;
+        const int64_t cf = static_cast<int64_t>(g.OC) * g.K;
+        const size_t in_b = up(static_cast<size_t>(cin) * cb), f_b = up(static_cast<size_t>(cf) * cb);
+        Workspace* w = nullptr;
+        int st = ensure_workspace(ctx, s, 0, 0, in_b + f_b + up(conv3d_tc_part_bytes()), &w);
+        if (st != DNNOPT_STATUS_SUCCESS) return st;
+        char* base = static_cast<char*>(w->quant);
+        cudaError_t e = launch_conv3d_tc_prep(precision, in, cin, f, cf, base, base + in_b, base + in_b + f_b,
+                                              w->scales, s);
+        note_launch(precision == DNNOPT_CONV3D_INT8 ? 2 : 1);
+        if (e == cudaSuccess) {
+            e = launch_conv3d_tc(g, precision, base, base + in_b, w->scales, bias, op, out, w->err, ctx->num_sms, s);
+            note_launch();
+        }
+        return cuda_status(e);
+    }
     // INT8 with IC % 16 == 0 and M >= 64: the dp4a kernel gathers 16-byte
     // channel segments from the quantised input, so no column matrix (the
     // workspace buffers are 256-byte aligned, so only the geometry decides).

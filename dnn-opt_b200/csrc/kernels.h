@@ -193,6 +193,21 @@ bool gemm_tile_s8_conv_ok(const Conv3dGeom& g, const int8_t* in_q, const int8_t*
 cudaError_t launch_gemm_tile_s8_conv(const Conv3dGeom& g, const int8_t* in_q, const int8_t* filter_q,
                                      const float* scales, const float* bias, int op, float* out,
                                      cudaStream_t s);
+// BF16 / INT8 conv3d with stride 1 as an implicit GEMM on tcgen05
+// (conv3d_tc.cu): TMA boxes of the NDHWC input shifted per filter tap are the
+// A tiles (no column matrix), the filter resident in shared memory when it
+// fits, bias / dequantisation / post-op in the epilogue.  Needs IC * element
+// size a multiple of 32 bytes.  mode 1: BF16, 2: INT8.
+bool conv3d_tc_ok(const Conv3dGeom& g, int mode);
+// Bytes of the absmax partials the INT8 preparation needs.
+size_t conv3d_tc_part_bytes();
+// Operands for launch_conv3d_tc: BF16 bits of input and filter (one launch),
+// or INT8 (per-CTA absmax partials, then scales[0..3] and the quantised input
+// and filter: two launches).  inq / fq 16-byte aligned.
+cudaError_t launch_conv3d_tc_prep(int mode, const float* in, int64_t nin, const float* f, int64_t nf, void* inq,
+                                  void* fq, void* part, float* scales, cudaStream_t s);
+cudaError_t launch_conv3d_tc(const Conv3dGeom& g, int mode, const void* inq, const void* fq, const float* scales,
+                             const float* bias, int op, float* out, uint32_t* err, int num_sms, cudaStream_t s);
 // out = post_op(v + bias[oc]); v = out, or float(acc) * (scales[0] * scales[1]) when acc.
 cudaError_t launch_conv3d_post(float* out, const int32_t* acc, const float* scales, const float* bias,
                                int64_t M, int OC, int op, cudaStream_t s);

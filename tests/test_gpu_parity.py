@@ -328,9 +328,19 @@ def _conv3d_shapes():
     # + a shape whose BF16 GEMM takes the tcgen05 kernel (K = 432, OC = 64, M = 1024),
     # + batch / stride / uneven padding with IC a multiple of 16 (the convert-once
     # input and 16-byte chunk im2col of the BF16 and INT8 paths)
+    # + stride-1 shapes of the implicit tcgen05 conv: 32 / 64 / 128-byte
+    # channel chunks (IC 32, 64, 96, 128 in INT8 and BF16), tiles ragged in
+    # every dimension (batch, OW 11 and 130, OC 24 and 300: two channel tiles
+    # with the filter streamed), asymmetric kernels and padding.
     return CONV3D_SHAPES + [(1, 16, 4, 16, 16, 64, 3, 3, 3, 1, 1, 1, 1, 1, 1),
                             (2, 32, 4, 9, 9, 24, 3, 3, 3, 2, 2, 2, 1, 1, 1),
-                            (1, 48, 3, 7, 7, 16, 1, 3, 3, 1, 1, 1, 0, 1, 1)]
+                            (1, 48, 3, 7, 7, 16, 1, 3, 3, 1, 1, 1, 0, 1, 1),
+                            (1, 64, 4, 14, 14, 64, 3, 3, 3, 1, 1, 1, 1, 1, 1),
+                            (2, 32, 3, 9, 11, 24, 3, 3, 3, 1, 1, 1, 1, 1, 1),
+                            (1, 96, 2, 6, 6, 300, 1, 3, 3, 1, 1, 1, 0, 1, 1),
+                            (3, 128, 2, 5, 5, 40, 3, 1, 3, 1, 1, 1, 1, 0, 1),
+                            (1, 16, 6, 7, 7, 16, 5, 3, 3, 1, 1, 1, 2, 1, 1),
+                            (1, 32, 1, 2, 130, 32, 1, 1, 3, 1, 1, 1, 0, 0, 1)]
 
 
 @pytest.mark.parametrize("p", _conv3d_shapes())
