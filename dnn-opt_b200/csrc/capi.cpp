@@ -515,7 +515,9 @@ int host_entry(Kind kind, const dnnopt_gemm_desc* d, const void* A, const void* 
             if (e != cudaSuccess) return cuda_status(e);
         }
         if (code != 0) {
-            cudaMemset(it->second.err, 0, sizeof(code));
+            // Clears the error word and the conv prep's grid-barrier and
+            // absmax words (a timed-out barrier may have left them set).
+            cudaMemset(it->second.err, 0, 16 * sizeof(uint32_t));
             return set_status(DNNOPT_STATUS_KERNEL_TIMEOUT);
         }
     }
@@ -668,16 +670,18 @@ int conv3d_device(int precision, const Conv3dGeom& g, const float* in, const flo
     // with bias, dequantisation and post-op in its epilogue.
     if (precision != DNNOPT_CONV3D_FP32 && conv3d_tc_ok(g, precision)) {
         const size_t cb = precision == DNNOPT_CONV3D_BF16 ? 2 : 1;
-        const int64_t cin = static_cast<int64_t>(g.N) * g.ID * g.IH * g.IW * g.IC;
         const int64_t cf = static_cast<int64_t>(g.OC) * g.K;
-        const size_t in_b = up(static_cast<size_t>(cin) * cb), f_b = up(static_cast<size_t>(cf) * cb);
+        const size_t in_b = up(conv3d_tc_input_bytes(g, precision)), f_b = up(static_cast<size_t>(cf) * cb);
         Workspace* w = nullptr;
-        int st = ensure_workspace(ctx, s, 0, 0, in_b + f_b + up(conv3d_tc_part_bytes()), &w);
+        int st = ensure_workspace(ctx, s, 0, 0, in_b + f_b, &w);
         if (st != DNNOPT_STATUS_SUCCESS) return st;
         char* base = static_cast<char*>(w->quant);
-        cudaError_t e = launch_conv3d_tc_prep(precision, in, cin, f, cf, base, base + in_b, base + in_b + f_b,
-                                              w->scales, s);
-        note_launch(precision == DNNOPT_CONV3D_INT8 ? 2 : 1);
+        // INT8 prep: grid-barrier words = the two spare absmax words, absmax
+        // slots = the four words after the scales.
+        cudaError_t e = launch_conv3d_tc_prep(g, precision, in, f, base, base + in_b, w->absmax + 2,
+                                              reinterpret_cast<uint32_t*>(w->scales) + 4, w->scales, w->err,
+                                              ctx->num_sms, s);
+        note_launch();
         if (e == cudaSuccess) {
             e = launch_conv3d_tc(g, precision, base, base + in_b, w->scales, bias, op, out, w->err, ctx->num_sms, s);
             note_launch();
@@ -1200,7 +1204,9 @@ int dnnopt_stream_status(void* stream) {
         e = cudaMemcpy(&code, it->second.err, sizeof(code), cudaMemcpyDeviceToHost);
         if (e != cudaSuccess) return cuda_status(e);
         if (code != 0) {
-            cudaMemset(it->second.err, 0, sizeof(code));
+            // Clears the error word and the conv prep's grid-barrier and
+            // absmax words (a timed-out barrier may have left them set).
+            cudaMemset(it->second.err, 0, 16 * sizeof(uint32_t));
             return set_status(DNNOPT_STATUS_KERNEL_TIMEOUT);
         }
     }

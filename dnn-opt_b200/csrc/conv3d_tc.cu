@@ -2,35 +2,39 @@
 // the B200 path of the reference's conv3d_bf16 / conv3d_int8
 // (src/conv/conv3d.cpp), which materialise im2col columns
 // (im2col3d_nhwc_* :389-457) and call the library GEMMs.  Here the column
-// matrix is never written: for each filter tap (kd, kh, kw) and chunk of
-// input channels, a TMA box of the NDHWC input, shifted by the tap, is the
-// A tile of that K-block, and the hardware's out-of-bounds zero fill is the
-// convolution padding.
+// matrix is never written.  The operands are prepared once: the input
+// converted (BF16, RNE) or quantised (INT8, per-tensor scale, round half
+// away, quantize_fp32_to_int8_3d :366-377) into a zero-padded NDHWC copy
+// [N, ID+2pd, IH+2ph, IW+2pw, IC], the filter likewise.  In the padded copy,
+// viewed as rows of IC channels, output position (n, od, oh, ow) is row
+//   P = ((n*Dp + od)*Hp + oh)*Wp + ow
+// and its filter tap (kd, kh, kw) reads row P + (kd*Hp + kh)*Wp + kw, so the
+// A tile of a K-block (one tap, one chunk of channels) for 128 consecutive
+// rows P is ONE 2-D TMA box.  Rows P that are not output positions (the
+// padding columns / planes) are computed and dropped.
 //
-//   output [N, OD, OH, OW, OC] = sum_k A[pixel, k] * filter[oc, k],
+//   output [N, OD, OH, OW, OC] = sum_k A[P, k] * filter[oc, k],
 //   k = ((kd*KH + kh)*KW + kw)*IC + ic (the reference's column order)
 //
-// INT8: both operands quantised per tensor first (conv3d_int8's
-// quantize_fp32_to_int8_3d :366-377, round half away, clamp), int32
-// accumulators in TMEM (exact), dequantisation float(acc) * (s_in*s_f), then
-// bias and relu / relu6 in the epilogue with the reference's rounding order
-// (dequantize_int32_to_fp32_3d :379-386, apply_conv3d_postops :126-148).
-// BF16: operands rounded to bf16 (RNE) once, FP32 accumulators.
+// INT8: int32 accumulators in TMEM (exact), dequantisation float(acc) *
+// (s_in*s_f), then bias and relu / relu6 in the epilogue with the reference's
+// rounding order (dequantize_int32_to_fp32_3d :379-386, apply_conv3d_postops
+// :126-148).  BF16: FP32 accumulators, then bias and post-op.
 //
-// Tiles: 128 output positions, a box of bw x bh x bd x bn positions (powers
-// of two, product 128; positions past the output are computed and dropped),
-// by n_mma <= 256 output channels.  A K-block is cb = 32, 64 or 128 bytes of
-// channels of one tap, staged with the matching TMA swizzle straight into the
-// UMMA K-major layout.  With one channel tile the whole filter stays resident
-// in shared memory (loaded with the CTA's first tile), so the ring streams
-// only input boxes, which L2 serves (each input position is read once per
-// tap).  Roles as in the general tcgen05 GEMM: warp 0 TMA, warp 1 TMEM +
-// MMA issue into two accumulators, warps 2-5 epilogue.  Every mbarrier wait
-// is bounded; every TMA load targets this CTA's own shared memory.
+// A K-block is cb = 32, 64 or 128 bytes of channels of one tap, staged with
+// the matching TMA swizzle straight into the UMMA K-major layout; each ring
+// stage carries several K-blocks (32-64 KB: on B200 a stage costs a roughly
+// fixed mbarrier round trip of about 0.3 us, and a 128-row box about 0.12 us
+// more).  With one channel tile (OC <= 256) the whole filter stays resident
+// in shared memory, loaded with the CTA's first tile.  Roles: warp 0 TMA,
+// warp 1 TMEM + MMA issue into two accumulators, warps 2-5 epilogue (32 x 32
+// blocks transposed through swizzled shared memory into whole 128-byte row
+// stores).  Every mbarrier wait and the prep kernel's grid barrier are
+// bounded; every TMA load targets this CTA's own shared memory.
 #include <cuda.h>
 
 #include <mutex>
-#include <set>
+#include <unordered_map>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -43,40 +47,32 @@ constexpr int BM = 128;
 constexpr int kThreads = 192;
 constexpr int kMaxStages = 8;
 constexpr int kMaxN = 256;
-constexpr size_t kSmemCap = 232448;   // 227 KB dynamic shared memory per CTA
+constexpr size_t kSmemCap = 232448;       // 227 KB dynamic shared memory per CTA
 constexpr size_t kSmemMin = 120 * 1024;   // keeps one CTA per SM (TMEM of up to 512 columns)
 constexpr int kBarBytes = 256;
-constexpr int kPartMax = 512;          // absmax partials (CTAs of the first INT8 prep kernel)
-constexpr int kPrepThreads = 256;
+constexpr int kStaging = 4 * 4096;        // one 32 x 32 fp32 block per epilogue warp
+constexpr int kPrepThreads = 256;         // BF16 conversion
+constexpr int kQuantThreads = 1024;       // INT8 prep: one CTA per SM (cooperative)
 
 struct ConvTcParams {
     int N, OD, OH, OW, OC;
+    int Dp, Hp, Wp;             // padded input extents
     int KH, KW;
-    int pd, ph, pw;
-    int bw, bh, bd, bn;         // output positions per tile along W, H, D, N
-    int tw, th, td;             // tiles along W, H, D
     int m_tiles, n_tiles, units;
+    int p_last;                 // padded row of the last output position
     int cb, celems, cpt, num_kb;   // K-block bytes / elements, K-blocks per tap, total
     int n_mma, stages, b_res;
-    int i8;                     // 1: kind::i8 (int32 accumulators), 0: kind::f16 (bf16, f32)
+    int kbs;                    // K-blocks per ring stage
     int post;                   // 0 none, 1 relu, 2 relu6
     uint32_t a_bytes, b_bytes;  // one K-block of A (128 rows) and of B (n_mma rows)
-    uint32_t stage_bytes, ring_off, bar_off;
+    uint32_t stage_bytes;       // kbs A blocks, then kbs B blocks unless the filter is resident
+    uint32_t ring_off, stg_off, bar_off;
     const float* scales;        // INT8: {s_in, s_f}
     const float* bias;
     float* out;
     int out_vec;                // 16-byte output stores (OC % 4 == 0, aligned)
     uint32_t* err;
 };
-
-__device__ __forceinline__ void tma_load_5d(void* smem_dst, const void* tmap, uint64_t* bar, int32_t c0,
-                                            int32_t c1, int32_t c2, int32_t c3, int32_t c4) {
-    asm volatile(
-        "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(smem_dst)),
-        "l"(tmap), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
-        : "memory");
-}
 
 __device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                         uint32_t accumulate) {
@@ -115,6 +111,10 @@ __device__ __forceinline__ float conv_post(float v, const float* bias, int oc, i
     return v;
 }
 
+// I8: kind::i8 with int32 accumulators (INT8), else kind::f16 (BF16, FP32
+// accumulators).  A compile-time choice: a run-time branch between the two MMA
+// forms in the issue loop measured twice the issue time per MMA on B200.
+template <bool I8>
 __global__ void __launch_bounds__(kThreads, 1)
 conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const ConvTcParams p) {
@@ -150,7 +150,7 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    pdl_wait();   // the quantised / converted operands come from the previous launch
+    pdl_wait();   // the prepared operands come from the previous launch
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
@@ -159,29 +159,34 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             bool first = true;
             for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
                 const int mt = u % p.m_tiles, nt = u / p.m_tiles;
-                int r = mt;
-                const int iw = r % p.tw; r /= p.tw;
-                const int ih = r % p.th; r /= p.th;
-                const int id = r % p.td;
-                const int in = r / p.td;
-                const int x1 = iw * p.bw - p.pw, x2 = ih * p.bh - p.ph, x3 = id * p.bd - p.pd, x4 = in * p.bn;
+                const int p0 = mt * BM;
                 const bool load_b = !p.b_res || first;
-                int c = 0, kw = 0, kh = 0, kd = 0;
+                // Tap walk: off = (kd*Hp + kh)*Wp + kw, channel chunk c fastest.
+                int c = 0, kw = 0, kh = 0, off = 0;
                 bool ok = true;
-                for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+                for (int kb = 0; kb < p.num_kb; kb += p.kbs, ++it) {
                     const uint32_t s = it % p.stages, ph = (it / p.stages) & 1u;
                     if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
                     uint8_t* sa = ring + s * p.stage_bytes;
-                    mbar_arrive_expect_tx(&full[s], p.a_bytes + (load_b ? p.b_bytes : 0u));
-                    tma_load_5d(sa, &tmA, &full[s], c * p.celems, x1 + kw, x2 + kh, x3 + kd, x4);
-                    if (load_b)
-                        tma_load_2d(p.b_res ? bres + static_cast<uint32_t>(kb) * p.b_bytes : sa + p.a_bytes, &tmB,
-                                    &full[s], kb * p.celems, nt * p.n_mma);
-                    if (++c == p.cpt) {
-                        c = 0;
-                        if (++kw == p.KW) {
-                            kw = 0;
-                            if (++kh == p.KH) { kh = 0; ++kd; }
+                    const int nsub = min(p.kbs, p.num_kb - kb);
+                    mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nsub) * (p.a_bytes + (load_b ? p.b_bytes : 0u)));
+                    for (int sub = 0; sub < nsub; ++sub) {
+                        tma_load_2d(sa + sub * p.a_bytes, &tmA, &full[s], c * p.celems, p0 + off);
+                        if (load_b)
+                            tma_load_2d(p.b_res ? bres + static_cast<uint32_t>(kb + sub) * p.b_bytes
+                                                : sa + p.kbs * p.a_bytes + sub * p.b_bytes,
+                                        &tmB, &full[s], (kb + sub) * p.celems, nt * p.n_mma);
+                        if (++c == p.cpt) {
+                            c = 0;
+                            ++off;
+                            if (++kw == p.KW) {
+                                kw = 0;
+                                off += p.Wp - p.KW;
+                                if (++kh == p.KH) {
+                                    kh = 0;
+                                    off += (p.Hp - p.KH) * p.Wp;
+                                }
+                            }
                         }
                     }
                 }
@@ -192,7 +197,7 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            const uint32_t idesc = conv_idesc(p.i8, p.n_mma);
+            const uint32_t idesc = conv_idesc(I8 ? 1 : 0, p.n_mma);
             const int ksteps = p.cb / 32;   // 32 bytes of K per MMA (K = 32 int8 or 16 bf16)
             uint32_t it = 0, titer = 0;
             bool ok = true;
@@ -201,18 +206,25 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 if (!mbar_wait(&tempty[buf], tph ^ 1u, abort_flag, p.err)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + buf * static_cast<uint32_t>(p.n_mma);
-                for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+                for (int kb = 0; kb < p.num_kb; kb += p.kbs, ++it) {
                     const uint32_t s = it % p.stages, ph = (it / p.stages) & 1u;
                     if (!mbar_wait(&full[s], ph, abort_flag, p.err)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_u32(ring + s * p.stage_bytes);
-                    const uint32_t b_addr = p.b_res ? smem_u32(bres) + static_cast<uint32_t>(kb) * p.b_bytes
-                                                    : a_addr + p.a_bytes;
-                    for (int kk = 0; kk < ksteps; ++kk) {
-                        const uint64_t da = desc_k_swizzled(a_addr + kk * 32, p.cb);
-                        const uint64_t db = desc_k_swizzled(b_addr + kk * 32, p.cb);
-                        if (p.i8) umma_i8(d_tmem, da, db, idesc, (kb | kk) != 0);
-                        else umma_f16_ss(d_tmem, da, db, idesc, (kb | kk) != 0);
+                    const uint32_t st_addr = smem_u32(ring + s * p.stage_bytes);
+                    const int nsub = min(p.kbs, p.num_kb - kb);
+                    // Branch-free issue loop: B blocks are b_bytes apart in
+                    // both the resident copy and the stage.
+                    const uint32_t b_base = p.b_res ? smem_u32(bres) + static_cast<uint32_t>(kb) * p.b_bytes
+                                                    : st_addr + p.kbs * p.a_bytes;
+                    for (int sub = 0; sub < nsub; ++sub) {
+                        const uint32_t a_addr = st_addr + sub * p.a_bytes;
+                        const uint32_t b_addr = b_base + sub * p.b_bytes;
+                        for (int kk = 0; kk < ksteps; ++kk) {
+                            const uint64_t da = desc_k_swizzled(a_addr + kk * 32, p.cb);
+                            const uint64_t db = desc_k_swizzled(b_addr + kk * 32, p.cb);
+                            if constexpr (I8) umma_i8(d_tmem, da, db, idesc, ((kb + sub) | kk) != 0);
+                            else umma_f16_ss(d_tmem, da, db, idesc, ((kb + sub) | kk) != 0);
+                        }
                     }
                     umma_commit(&empty[s]);
                 }
@@ -222,53 +234,67 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         }
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
-        const int q = warp & 3;            // TMEM lanes 32q .. 32q+31
-        const int row_in = q * 32 + lane;
-        const int ww = row_in % p.bw;
-        const int hh = (row_in / p.bw) % p.bh;
-        const int dd = (row_in / (p.bw * p.bh)) % p.bd;
-        const int nn = row_in / (p.bw * p.bh * p.bd);
-        const float dq = p.i8 ? __fmul_rn(p.scales[0], p.scales[1]) : 1.0f;
+        const int q = warp & 3;            // TMEM lanes 32q .. 32q+31 = tile rows
+        uint8_t* stg = base + p.stg_off + q * 4096;
+        const float dq = I8 ? __fmul_rn(p.scales[0], p.scales[1]) : 1.0f;
+        const int plane = p.Hp * p.Wp, vol = p.Dp * plane;
         uint32_t titer = 0;
         for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x, ++titer) {
             const int mt = u % p.m_tiles, nt = u / p.m_tiles;
-            int r = mt;
-            const int iw = r % p.tw; r /= p.tw;
-            const int ih = r % p.th; r /= p.th;
-            const int id = r % p.td;
-            const int in = r / p.td;
-            const int ow = iw * p.bw + ww, oh = ih * p.bh + hh, od = id * p.bd + dd, on = in * p.bn + nn;
-            const bool live = ow < p.OW && oh < p.OH && od < p.OD && on < p.N;
-            const int64_t pix = ((static_cast<int64_t>(on) * p.OD + od) * p.OH + oh) * p.OW + ow;
-            float* orow = p.out + pix * p.OC;
+            // This lane's row: padded position P -> output position (or none).
+            const int P = mt * BM + q * 32 + lane;
+            const int n = P / vol;
+            int r = P - n * vol;
+            const int d = r / plane;
+            r -= d * plane;
+            const int h = r / p.Wp, w = r - h * p.Wp;
+            const int live = P <= p.p_last && d < p.OD && h < p.OH && w < p.OW;
+            const int64_t pix = ((static_cast<int64_t>(n) * p.OD + d) * p.OH + h) * p.OW + w;
             const uint32_t buf = titer & 1u, tph = (titer >> 1) & 1u;
             const bool ok = mbar_wait_warp(&tfull[buf], tph, abort_flag, p.err);
             tc_fence_after();
             const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * static_cast<uint32_t>(p.n_mma);
             const int col0 = nt * p.n_mma;
             for (int c0 = 0; c0 < p.n_mma; c0 += 32) {
-                if (col0 + c0 >= p.OC) break;   // uniform across the warp
+                const int cbase = col0 + c0;
+                if (cbase >= p.OC) break;   // uniform across the warp
                 uint32_t v[32];
                 tmem_ld_32x32b_x16(t_addr + c0, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
                 tmem_ld_32x32b_x16(t_addr + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
                 tmem_ld_wait();
-                if (!ok || !live) continue;
-                float f[32];
+                // Row `lane` into the staging block: 16-byte chunk j of the
+                // row at chunk position j ^ (lane % 8) (conflict-free both ways).
+                __syncwarp();   // the previous block's reads are done
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const float a = p.i8 ? __fmul_rn(static_cast<float>(static_cast<int32_t>(v[j])), dq)
-                                         : __uint_as_float(v[j]);
-                    f[j] = conv_post(a, p.bias, min(col0 + c0 + j, p.OC - 1), p.post);
+                for (int j = 0; j < 8; ++j) {
+                    float f[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int col = cbase + 4 * j + e;
+                        const float a = I8 ? __fmul_rn(static_cast<float>(static_cast<int32_t>(v[4 * j + e])), dq)
+                                           : __uint_as_float(v[4 * j + e]);
+                        f[e] = conv_post(a, p.bias, min(col, p.OC - 1), p.post);
+                    }
+                    *reinterpret_cast<float4*>(stg + lane * 128 + ((j ^ (lane & 7)) * 16)) =
+                        make_float4(f[0], f[1], f[2], f[3]);
                 }
-                const int cbase = col0 + c0;
-                if (p.out_vec && cbase + 32 <= p.OC) {
+                __syncwarp();
+                // Whole rows out: eight lanes per 128-byte row, four rows per step.
 #pragma unroll
-                    for (int j = 0; j < 32; j += 4)
-                        *reinterpret_cast<float4*>(orow + cbase + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (cbase + j < p.OC) orow[cbase + j] = f[j];
+                for (int rd = 0; rd < 8; ++rd) {
+                    const int row = rd * 4 + (lane >> 3), ch = lane & 7;
+                    const int64_t prow = __shfl_sync(0xFFFFFFFFu, pix, row);
+                    const int lrow = __shfl_sync(0xFFFFFFFFu, live, row);
+                    const float4 val = *reinterpret_cast<const float4*>(stg + row * 128 + ((ch ^ (row & 7)) * 16));
+                    const int col = cbase + ch * 4;
+                    if (!ok || !lrow || col >= p.OC) continue;
+                    float* dst = p.out + prow * p.OC + col;
+                    if (p.out_vec) {
+                        *reinterpret_cast<float4*>(dst) = val;
+                    } else {
+                        const float vv[4] = {val.x, val.y, val.z, val.w};
+                        for (int e = 0; e < 4 && col + e < p.OC; ++e) dst[e] = vv[e];
+                    }
                 }
             }
             tc_fence_before();
@@ -287,6 +313,16 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 }
 
 // ---- operand preparation -------------------------------------------------------
+struct PrepGeom {
+    int N, ID, IH, IW, IC;
+    int pd, ph, pw, Dp, Hp, Wp;
+    int cpp;          // 16-byte chunks per padded pixel
+    int64_t nin, nf;  // input / filter elements
+    int64_t nchunks;  // 16-byte chunks of the padded input
+    int in_vec;       // input 16-byte aligned
+    int f_vec;        // filter 16-byte aligned
+};
+
 // Reference round-half-away quantisation (quantize_fp32_to_int8_3d :366-377).
 __device__ __forceinline__ uint32_t quant8_bits(float x, float inv) {
     int q = static_cast<int>(roundf(x * inv));
@@ -294,41 +330,116 @@ __device__ __forceinline__ uint32_t quant8_bits(float x, float inv) {
     return static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(q)));
 }
 
+__device__ __forceinline__ uint32_t quant8x4(float4 v, float inv) {
+    return quant8_bits(v.x, inv) | (quant8_bits(v.y, inv) << 8) | (quant8_bits(v.z, inv) << 16) |
+           (quant8_bits(v.w, inv) << 24);
+}
+
 __device__ __forceinline__ uint32_t abs_bits(float x) {
     const float a = fabsf(x);
     return a == a ? __float_as_uint(a) : 0u;   // NaN never wins, as in `a > max`
 }
 
-// Per-CTA absmax of the input (x) and the filter (y) as float bit patterns
-// (non-negative floats order like unsigned integers), one partial per CTA:
-// no atomics, nothing to reset between calls.  Vector loads over the
-// 16-byte aligned body of each tensor, scalar loads for the rest.
-__global__ void __launch_bounds__(kPrepThreads) conv3d_absmax_part_kernel(const float* __restrict__ in, int64_t nin,
-                                                                          const float* __restrict__ f, int64_t nf,
-                                                                          uint2* part) {
-    uint32_t m[2] = {0u, 0u};
+__device__ __forceinline__ uint32_t abs_bits4(float4 v) {
+    return max(max(abs_bits(v.x), abs_bits(v.y)), max(abs_bits(v.z), abs_bits(v.w)));
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Source of padded chunk `ch` (16 bytes of the padded copy, `per` input
+// elements), or nullptr for a padding chunk.
+// 32-bit index arithmetic: the padded copy has fewer than 2^31 rows.
+__device__ __forceinline__ const float* pad_source(const PrepGeom& g, const float* in, int64_t ch, int per) {
+    const uint32_t c32 = static_cast<uint32_t>(ch);
+    const uint32_t pixel = c32 / static_cast<uint32_t>(g.cpp);
+    const int cc = static_cast<int>(c32 - pixel * static_cast<uint32_t>(g.cpp));
+    uint32_t t = pixel;
+    const int wp = static_cast<int>(t % static_cast<uint32_t>(g.Wp)); t /= static_cast<uint32_t>(g.Wp);
+    const int hp = static_cast<int>(t % static_cast<uint32_t>(g.Hp)); t /= static_cast<uint32_t>(g.Hp);
+    const int dp = static_cast<int>(t % static_cast<uint32_t>(g.Dp));
+    const int64_t n = t / static_cast<uint32_t>(g.Dp);
+    const int d = dp - g.pd, h = hp - g.ph, w = wp - g.pw;
+    if (d < 0 || d >= g.ID || h < 0 || h >= g.IH || w < 0 || w >= g.IW) return nullptr;
+    return in + (((n * g.ID + d) * g.IH + h) * static_cast<int64_t>(g.IW) + w) * g.IC + static_cast<int64_t>(cc) * per;
+}
+
+// Grid barrier for a cooperative launch: arrive, the last CTA clears the two
+// words `clear2` (the other call parity's absmax slot), resets the count and
+// advances the generation; the others wait (bounded, about 2 s of SM clocks)
+// for the generation to move.  false: timed out (error recorded).
+__device__ bool grid_barrier(uint32_t* count, uint32_t* gen, uint32_t* clear2, uint32_t* err) {
+    __shared__ uint32_t s_ok;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t ok = 1u;
+        const uint32_t g0 = ld_acquire_gpu_u32(gen);
+        __threadfence();
+        const uint32_t t = atomicAdd(count, 1u);
+        if (t == gridDim.x - 1) {
+            clear2[0] = 0u;
+            clear2[1] = 0u;
+            atomicExch(count, 0u);
+            __threadfence();
+            atomicAdd(gen, 1u);
+        } else {
+            long long t0;
+            asm volatile("mov.u64 %0, %%clock64;" : "=l"(t0));
+            for (;;) {
+                if (ld_acquire_gpu_u32(gen) != g0) break;
+                long long t1;
+                asm volatile("mov.u64 %0, %%clock64;" : "=l"(t1));
+                if (t1 - t0 > (4LL << 30)) {
+                    record_kernel_error(err, kKerrMbarTimeout);
+                    ok = 0u;
+                    break;
+                }
+            }
+        }
+        __threadfence();
+        s_ok = ok;
+    }
+    __syncthreads();
+    return s_ok != 0u;
+}
+
+// INT8 operands in one cooperative launch of one CTA per SM: absmax of input
+// and filter (float bit patterns: non-negative floats order like unsigned
+// integers), folded per CTA into this call's slot of `maxslots` (two slots
+// alternating with the barrier generation's parity, so the slot is clean
+// without a reset launch), grid barrier, the scales (s = max_abs / 127, 1
+// when all zero, compute_quant_scale_3d :355-364; scales[0..3] = s_in, s_f,
+// 1/s_in, 1/s_f), then the padded input (zero padding written too) and the
+// filter quantised; the second read of the input is served by L2.
+__global__ void __launch_bounds__(kQuantThreads) conv3d_quant_pad_kernel(const float* __restrict__ in,
+                                                                         const float* __restrict__ f, const PrepGeom g,
+                                                                         uint32_t* sync, uint32_t* maxslots,
+                                                                         float* scales, int8_t* inq, int8_t* fq,
+                                                                         uint32_t* err) {
+    __shared__ uint32_t s_m[2][kQuantThreads / 32];
+    __shared__ float s_inv[2];
+    __shared__ uint32_t s_slot;
+    // This call's slot: the generation cannot move before every CTA arrived.
+    if (threadIdx.x == 0) s_slot = ld_acquire_gpu_u32(sync + 1) & 1u;
     const int64_t gt = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const int64_t gs = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    uint32_t m[2] = {0u, 0u};
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
         const float* x = t == 0 ? in : f;
-        const int64_t n = t == 0 ? nin : nf;
-        const int64_t head = (reinterpret_cast<uintptr_t>(x) % 16 == 0) ? 0 : n;   // unaligned: all scalar
-        const int64_t nv = (n - head) / 4;
+        const int64_t n = t == 0 ? g.nin : g.nf;
+        const int64_t nv = (t == 0 ? g.in_vec : g.f_vec) ? n / 4 : 0;
         const float4* x4 = reinterpret_cast<const float4*>(x);
         uint32_t acc = 0u;
-        int64_t i = gt;
-        for (; i + 3 * gs < nv; i += 4 * gs) {
+        for (int64_t i0 = gt; i0 < nv; i0 += 4 * gs) {
             float4 v[4];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) v[k] = __ldg(x4 + i + k * gs);
+            for (int k = 0; k < 4; ++k) v[k] = i0 + k * gs < nv ? __ldg(x4 + i0 + k * gs) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-                acc = max(acc, max(max(abs_bits(v[k].x), abs_bits(v[k].y)), max(abs_bits(v[k].z), abs_bits(v[k].w))));
-        }
-        for (; i < nv; i += gs) {
-            const float4 v = __ldg(x4 + i);
-            acc = max(acc, max(max(abs_bits(v.x), abs_bits(v.y)), max(abs_bits(v.z), abs_bits(v.w))));
+            for (int k = 0; k < 4; ++k) acc = max(acc, abs_bits4(v[k]));
         }
         for (int64_t j = nv * 4 + gt; j < n; j += gs) acc = max(acc, abs_bits(__ldg(x + j)));
         m[t] = acc;
@@ -338,46 +449,20 @@ __global__ void __launch_bounds__(kPrepThreads) conv3d_absmax_part_kernel(const 
         m[0] = max(m[0], __shfl_xor_sync(0xFFFFFFFFu, m[0], o));
         m[1] = max(m[1], __shfl_xor_sync(0xFFFFFFFFu, m[1], o));
     }
-    __shared__ uint32_t s_m[2][kPrepThreads / 32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (lane == 0) { s_m[0][warp] = m[0]; s_m[1][warp] = m[1]; }
     __syncthreads();
+    const uint32_t slot = s_slot;
     if (threadIdx.x == 0) {
         uint32_t a = 0u, b = 0u;
-        for (int w = 0; w < kPrepThreads / 32; ++w) { a = max(a, s_m[0][w]); b = max(b, s_m[1][w]); }
-        part[blockIdx.x] = make_uint2(a, b);
+        for (int w = 0; w < kQuantThreads / 32; ++w) { a = max(a, s_m[0][w]); b = max(b, s_m[1][w]); }
+        atomicMax(maxslots + 2 * slot, a);
+        atomicMax(maxslots + 2 * slot + 1, b);
     }
-    pdl_launch_dependents();
-}
-
-// Scales from the absmax partials (s = max_abs / 127, 1 when all zero,
-// compute_quant_scale_3d :355-364; scales[0..3] = s_in, s_f, 1/s_in, 1/s_f),
-// then input and filter quantised: four elements per 32-bit store.
-__global__ void __launch_bounds__(kPrepThreads) conv3d_quant_kernel(const float* __restrict__ in, int64_t nin,
-                                                                    const float* __restrict__ f, int64_t nf,
-                                                                    const uint2* part, int nparts, float* scales,
-                                                                    int8_t* inq, int8_t* fq) {
-    pdl_wait();
-    uint32_t m0 = 0u, m1 = 0u;
-    for (int i = threadIdx.x; i < nparts; i += blockDim.x) {
-        const uint2 v = part[i];
-        m0 = max(m0, v.x);
-        m1 = max(m1, v.y);
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-        m0 = max(m0, __shfl_xor_sync(0xFFFFFFFFu, m0, o));
-        m1 = max(m1, __shfl_xor_sync(0xFFFFFFFFu, m1, o));
-    }
-    __shared__ uint32_t s_m[2][kPrepThreads / 32];
-    __shared__ float s_inv[2];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) { s_m[0][warp] = m0; s_m[1][warp] = m1; }
-    __syncthreads();
+    grid_barrier(sync, sync + 1, maxslots + 2 * (slot ^ 1u), err);
     if (threadIdx.x == 0) {
-        uint32_t a = 0u, b = 0u;
-        for (int w = 0; w < kPrepThreads / 32; ++w) { a = max(a, s_m[0][w]); b = max(b, s_m[1][w]); }
-        const float ma = __uint_as_float(a), mb = __uint_as_float(b);
+        const float ma = __uint_as_float(__ldcg(maxslots + 2 * slot));
+        const float mb = __uint_as_float(__ldcg(maxslots + 2 * slot + 1));
         const float sa = ma == 0.0f ? 1.0f : __fdiv_rn(ma, 127.0f);
         const float sb = mb == 0.0f ? 1.0f : __fdiv_rn(mb, 127.0f);
         s_inv[0] = __fdiv_rn(1.0f, sa);
@@ -391,50 +476,71 @@ __global__ void __launch_bounds__(kPrepThreads) conv3d_quant_kernel(const float*
     }
     __syncthreads();
     pdl_launch_dependents();
-    const int64_t gt = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const int64_t gs = static_cast<int64_t>(gridDim.x) * blockDim.x;
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-        const float* x = t == 0 ? in : f;
-        int8_t* y = t == 0 ? inq : fq;
-        const int64_t n = t == 0 ? nin : nf;
-        const float inv = s_inv[t];
-        // y is 256-byte aligned (workspace); vector groups need x aligned too.
-        const int64_t nv = reinterpret_cast<uintptr_t>(x) % 16 == 0 ? n / 4 : 0;
-        const float4* x4 = reinterpret_cast<const float4*>(x);
-        uint32_t* y4 = reinterpret_cast<uint32_t*>(y);
-        for (int64_t i = gt; i < nv; i += gs) {
-            const float4 v = __ldg(x4 + i);
-            y4[i] = quant8_bits(v.x, inv) | (quant8_bits(v.y, inv) << 8) | (quant8_bits(v.z, inv) << 16) |
-                    (quant8_bits(v.w, inv) << 24);
+    const float inv0 = s_inv[0], inv1 = s_inv[1];
+    // Padded input: 16 int8 per chunk.
+    uint4* out4 = reinterpret_cast<uint4*>(inq);
+    for (int64_t ch = gt; ch < g.nchunks; ch += gs) {
+        const float* src = pad_source(g, in, ch, 16);
+        uint4 o = make_uint4(0u, 0u, 0u, 0u);
+        if (src) {
+            if (g.in_vec) {
+                const float4* s4 = reinterpret_cast<const float4*>(src);
+                o.x = quant8x4(__ldg(s4), inv0);
+                o.y = quant8x4(__ldg(s4 + 1), inv0);
+                o.z = quant8x4(__ldg(s4 + 2), inv0);
+                o.w = quant8x4(__ldg(s4 + 3), inv0);
+            } else {
+                uint32_t wv[4];
+                for (int k = 0; k < 4; ++k)
+                    wv[k] = quant8x4(make_float4(__ldg(src + 4 * k), __ldg(src + 4 * k + 1), __ldg(src + 4 * k + 2),
+                                                 __ldg(src + 4 * k + 3)), inv0);
+                o = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            }
         }
-        for (int64_t j = nv * 4 + gt; j < n; j += gs)
-            y[j] = static_cast<int8_t>(static_cast<uint8_t>(quant8_bits(__ldg(x + j), inv)));
+        out4[ch] = o;
     }
+    // Filter [OC, K]: four elements per 32-bit store (fq is 16-byte aligned).
+    const int64_t nfv = g.f_vec ? g.nf / 4 : 0;
+    for (int64_t i = gt; i < nfv; i += gs)
+        reinterpret_cast<uint32_t*>(fq)[i] = quant8x4(__ldg(reinterpret_cast<const float4*>(f) + i), inv1);
+    for (int64_t j = nfv * 4 + gt; j < g.nf; j += gs)
+        fq[j] = static_cast<int8_t>(static_cast<uint8_t>(quant8_bits(__ldg(f + j), inv1)));
 }
 
-// Input and filter to bf16 bits (RNE, the reference's bfloat16_t(float)):
-// four elements per 8-byte store.
-__global__ void __launch_bounds__(kPrepThreads) conv3d_bf16_prep_kernel(const float* __restrict__ in, int64_t nin,
-                                                                        const float* __restrict__ f, int64_t nf,
-                                                                        uint16_t* inb, uint16_t* fb) {
+__device__ __forceinline__ uint32_t bf16x2(float a, float b) {
+    return f32_to_bf16_bits_ref(a) | (static_cast<uint32_t>(f32_to_bf16_bits_ref(b)) << 16);
+}
+
+// BF16 operands: the padded input (8 bf16 per 16-byte chunk, zero padding
+// written too) and the filter, RNE as the reference's bfloat16_t(float).
+__global__ void __launch_bounds__(kPrepThreads) conv3d_bf16_pad_kernel(const float* __restrict__ in,
+                                                                       const float* __restrict__ f, const PrepGeom g,
+                                                                       uint16_t* inb, uint16_t* fb) {
     const int64_t gt = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const int64_t gs = static_cast<int64_t>(gridDim.x) * blockDim.x;
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-        const float* x = t == 0 ? in : f;
-        uint16_t* y = t == 0 ? inb : fb;
-        const int64_t n = t == 0 ? nin : nf;
-        const int64_t nv = reinterpret_cast<uintptr_t>(x) % 16 == 0 ? n / 4 : 0;
-        const float4* x4 = reinterpret_cast<const float4*>(x);
-        uint2* y4 = reinterpret_cast<uint2*>(y);
-        for (int64_t i = gt; i < nv; i += gs) {
-            const float4 v = __ldg(x4 + i);
-            y4[i] = make_uint2(f32_to_bf16_bits_ref(v.x) | (static_cast<uint32_t>(f32_to_bf16_bits_ref(v.y)) << 16),
-                               f32_to_bf16_bits_ref(v.z) | (static_cast<uint32_t>(f32_to_bf16_bits_ref(v.w)) << 16));
+    uint4* out4 = reinterpret_cast<uint4*>(inb);
+    for (int64_t ch = gt; ch < g.nchunks; ch += gs) {
+        const float* src = pad_source(g, in, ch, 8);
+        uint4 o = make_uint4(0u, 0u, 0u, 0u);
+        if (src) {
+            float x[8];
+            if (g.in_vec) {
+                const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+                const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+                x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+            } else {
+                for (int k = 0; k < 8; ++k) x[k] = __ldg(src + k);
+            }
+            o = make_uint4(bf16x2(x[0], x[1]), bf16x2(x[2], x[3]), bf16x2(x[4], x[5]), bf16x2(x[6], x[7]));
         }
-        for (int64_t j = nv * 4 + gt; j < n; j += gs) y[j] = f32_to_bf16_bits_ref(__ldg(x + j));
+        out4[ch] = o;
     }
+    const int64_t nfv = g.f_vec ? g.nf / 4 : 0;
+    for (int64_t i = gt; i < nfv; i += gs) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(f) + i);
+        reinterpret_cast<uint2*>(fb)[i] = make_uint2(bf16x2(v.x, v.y), bf16x2(v.z, v.w));
+    }
+    for (int64_t j = nfv * 4 + gt; j < g.nf; j += gs) fb[j] = f32_to_bf16_bits_ref(__ldg(f + j));
     pdl_launch_dependents();
 }
 
@@ -456,21 +562,16 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-int pow2_at_least(int x, int cap) {
-    int p = 1;
-    while (p < x && p < cap) p *= 2;
-    return p;
-}
-
 int chunk_bytes(const Conv3dGeom& g, int mode) {
     const int64_t icb = static_cast<int64_t>(g.IC) * (mode == 1 ? 2 : 1);
     return icb % 128 == 0 ? 128 : (icb % 64 == 0 ? 64 : (icb % 32 == 0 ? 32 : 0));
 }
 
 struct ConvTcLayout {
-    int bw, bh, bd, bn, tw, th, td, tn, cb, n_mma, n_tiles, num_kb, stages, b_res;
+    int Dp, Hp, Wp, cb, n_mma, n_tiles, num_kb, stages, b_res, kbs, m_tiles;
+    int64_t rows, p_last;
     size_t smem;
-    uint32_t a_bytes, b_bytes, stage_bytes, ring_off, bar_off;
+    uint32_t a_bytes, b_bytes, stage_bytes, ring_off, stg_off, bar_off;
 };
 
 bool conv_layout(const Conv3dGeom& g, int mode, ConvTcLayout* L) {
@@ -478,34 +579,42 @@ bool conv_layout(const Conv3dGeom& g, int mode, ConvTcLayout* L) {
     if (cb == 0) return false;
     const int eb = mode == 1 ? 2 : 1;
     L->cb = cb;
-    L->bw = pow2_at_least(g.OW, BM);
-    L->bh = pow2_at_least(g.OH, BM / L->bw);
-    L->bd = pow2_at_least(g.OD, BM / (L->bw * L->bh));
-    L->bn = BM / (L->bw * L->bh * L->bd);
-    L->tw = (g.OW + L->bw - 1) / L->bw;
-    L->th = (g.OH + L->bh - 1) / L->bh;
-    L->td = (g.OD + L->bd - 1) / L->bd;
-    L->tn = (g.N + L->bn - 1) / L->bn;
-    int n = g.OC < kMaxN ? g.OC : kMaxN;
+    L->Dp = g.ID + 2 * g.pd;
+    L->Hp = g.IH + 2 * g.ph;
+    L->Wp = g.IW + 2 * g.pw;
+    L->rows = static_cast<int64_t>(g.N) * L->Dp * L->Hp * L->Wp;
+    L->p_last = ((static_cast<int64_t>(g.N - 1) * L->Dp + g.OD - 1) * L->Hp + g.OH - 1) * L->Wp + g.OW - 1;
+    // Row indices (tile rows plus the largest tap offset) stay in int32.
+    const int64_t max_off = (static_cast<int64_t>(g.KD - 1) * L->Hp + g.KH - 1) * L->Wp + g.KW - 1;
+    if (L->rows + max_off + BM >= (int64_t(1) << 31)) return false;
+    L->m_tiles = static_cast<int>((L->p_last + BM) / BM);
+    const int n = g.OC < kMaxN ? g.OC : kMaxN;
     L->n_mma = (n + 31) / 32 * 32;
     L->n_tiles = (g.OC + L->n_mma - 1) / L->n_mma;
     const int64_t cpt = static_cast<int64_t>(g.IC) * eb / cb;
     L->num_kb = static_cast<int>(cpt * g.KD * g.KH * g.KW);
     L->a_bytes = static_cast<uint32_t>(BM * cb);
     L->b_bytes = static_cast<uint32_t>(L->n_mma * cb);
-    const size_t fixed = 1024 + kBarBytes;
+    const size_t fixed = 1024 + kBarBytes + kStaging;
     const size_t bres = static_cast<size_t>(L->num_kb) * L->b_bytes;
     // The filter stays resident when it leaves room for a ring of at least
-    // four input stages.
+    // four input K-blocks.
     L->b_res = L->n_tiles == 1 && fixed + bres + 4 * static_cast<size_t>(L->a_bytes) <= kSmemCap ? 1 : 0;
-    L->stage_bytes = L->a_bytes + (L->b_res ? 0u : L->b_bytes);
+    // Several K-blocks per ring stage (32-64 KB), at least three stages.
+    const uint32_t per_kb = L->a_bytes + (L->b_res ? 0u : L->b_bytes);
     const size_t avail = kSmemCap - fixed - (L->b_res ? bres : 0);
+    L->kbs = 1;
+    for (int k = 8; k > 1; --k)
+        if (k * per_kb <= 65536u && avail / (k * per_kb) >= 3) { L->kbs = k; break; }
+    if (L->kbs > L->num_kb) L->kbs = L->num_kb;
+    L->stage_bytes = static_cast<uint32_t>(L->kbs) * per_kb;
     int st = static_cast<int>(avail / L->stage_bytes);
     if (st > kMaxStages) st = kMaxStages;
     if (st < 2) return false;
     L->stages = st;
     L->ring_off = static_cast<uint32_t>(L->b_res ? bres : 0);
-    L->bar_off = L->ring_off + static_cast<uint32_t>(st) * L->stage_bytes;
+    L->stg_off = L->ring_off + static_cast<uint32_t>(st) * L->stage_bytes;
+    L->bar_off = L->stg_off + kStaging;
     L->smem = 1024 + L->bar_off + kBarBytes;
     if (L->smem < kSmemMin) L->smem = kSmemMin;
     return L->smem <= kSmemCap;
@@ -515,9 +624,36 @@ CUtensorMapSwizzle swizzle_for(int cb) {
     return cb == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : (cb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
 }
 
-int prep_grid(int64_t n4) {
-    const int64_t b = (n4 + kPrepThreads - 1) / kPrepThreads;
-    return static_cast<int>(b < 1 ? 1 : (b > 148 * 4 ? 148 * 4 : b));
+PrepGeom prep_geom(const Conv3dGeom& g, int mode, const float* in, const float* f) {
+    PrepGeom pg;
+    pg.N = g.N; pg.ID = g.ID; pg.IH = g.IH; pg.IW = g.IW; pg.IC = g.IC;
+    pg.pd = g.pd; pg.ph = g.ph; pg.pw = g.pw;
+    pg.Dp = g.ID + 2 * g.pd; pg.Hp = g.IH + 2 * g.ph; pg.Wp = g.IW + 2 * g.pw;
+    pg.cpp = g.IC * (mode == 1 ? 2 : 1) / 16;
+    pg.nin = static_cast<int64_t>(g.N) * g.ID * g.IH * g.IW * g.IC;
+    pg.nf = static_cast<int64_t>(g.OC) * g.K;
+    pg.nchunks = static_cast<int64_t>(g.N) * pg.Dp * pg.Hp * pg.Wp * pg.cpp;
+    pg.in_vec = reinterpret_cast<uintptr_t>(in) % 16 == 0 ? 1 : 0;
+    pg.f_vec = reinterpret_cast<uintptr_t>(f) % 16 == 0 ? 1 : 0;
+    return pg;
+}
+
+// CTAs of the INT8 prep kernel: one per SM when one 1024-thread CTA fits
+// (cooperative launch), else 0.
+int coop_grid(int num_sms) {
+    static std::mutex mu;
+    static std::unordered_map<int, int> per_sm;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = per_sm.find(dev);
+    if (it == per_sm.end()) {
+        int nb = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, conv3d_quant_pad_kernel, kQuantThreads, 0) != cudaSuccess)
+            nb = 0;
+        it = per_sm.emplace(dev, nb).first;
+    }
+    return it->second >= 1 ? num_sms : 0;
 }
 
 }  // namespace
@@ -530,33 +666,46 @@ bool conv3d_tc_ok(const Conv3dGeom& g, int mode) {
     return conv_layout(g, mode, &L);
 }
 
-size_t conv3d_tc_part_bytes() { return static_cast<size_t>(kPartMax) * sizeof(uint2); }
+size_t conv3d_tc_input_bytes(const Conv3dGeom& g, int mode) {
+    return static_cast<size_t>(g.N) * (g.ID + 2 * g.pd) * (g.IH + 2 * g.ph) * (g.IW + 2 * g.pw) * g.IC *
+           (mode == 1 ? 2 : 1);
+}
 
-cudaError_t launch_conv3d_tc_prep(int mode, const float* in, int64_t nin, const float* f, int64_t nf, void* inq,
-                                  void* fq, void* part, float* scales, cudaStream_t s) {
+cudaError_t launch_conv3d_tc_prep(const Conv3dGeom& g, int mode, const float* in, const float* f, void* inq, void* fq,
+                                  uint32_t* sync, uint32_t* maxslots, float* scales, uint32_t* err, int num_sms,
+                                  cudaStream_t s) {
+    if (!conv3d_tc_ok(g, mode)) return cudaErrorInvalidValue;
     if (reinterpret_cast<uintptr_t>(inq) % 16 || reinterpret_cast<uintptr_t>(fq) % 16) return cudaErrorInvalidValue;
+    const PrepGeom pg = prep_geom(g, mode, in, f);
     if (mode == 1) {
-        conv3d_bf16_prep_kernel<<<prep_grid((nin + nf) / 4), kPrepThreads, 0, s>>>(
-            in, nin, f, nf, static_cast<uint16_t*>(inq), static_cast<uint16_t*>(fq));
+        const int64_t work = pg.nchunks > pg.nf / 4 ? pg.nchunks : pg.nf / 4;
+        int64_t grid = (work + kPrepThreads - 1) / kPrepThreads;
+        if (grid > 4LL * num_sms) grid = 4LL * num_sms;
+        if (grid < 1) grid = 1;
+        conv3d_bf16_pad_kernel<<<static_cast<unsigned>(grid), kPrepThreads, 0, s>>>(
+            in, f, pg, static_cast<uint16_t*>(inq), static_cast<uint16_t*>(fq));
         return cudaGetLastError();
     }
-    if (mode != 2 || !part || !scales) return cudaErrorInvalidValue;
-    int parts = prep_grid((nin + nf) / 16);   // about four float4 per thread
-    if (parts > kPartMax) parts = kPartMax;
-    conv3d_absmax_part_kernel<<<parts, kPrepThreads, 0, s>>>(in, nin, f, nf, static_cast<uint2*>(part));
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    if (!sync || !maxslots || !scales) return cudaErrorInvalidValue;
+    int grid = coop_grid(num_sms);
+    if (grid < 1) return cudaErrorNotSupported;
+    // Fewer CTAs for small tensors: four float4 per thread for the absmax,
+    // one 16-byte chunk per thread for the quantisation.
+    const int64_t w1 = (pg.nin / 4 + 4 * kQuantThreads - 1) / (4 * kQuantThreads);
+    const int64_t w2 = (pg.nchunks + kQuantThreads - 1) / kQuantThreads;
+    const int64_t need = w1 > w2 ? w1 : w2;
+    if (need < grid) grid = static_cast<int>(need > 0 ? need : 1);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(prep_grid((nin + nf) / 4)));
-    cfg.blockDim = dim3(kPrepThreads);
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(kQuantThreads);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, conv3d_quant_kernel, in, nin, f, nf, static_cast<const uint2*>(part), parts,
-                              scales, static_cast<int8_t*>(inq), static_cast<int8_t*>(fq));
+    return cudaLaunchKernelEx(&cfg, conv3d_quant_pad_kernel, in, f, pg, sync, maxslots, scales,
+                              static_cast<int8_t*>(inq), static_cast<int8_t*>(fq), err);
 }
 
 cudaError_t launch_conv3d_tc(const Conv3dGeom& g, int mode, const void* inq, const void* fq, const float* scales,
@@ -570,14 +719,12 @@ cudaError_t launch_conv3d_tc(const Conv3dGeom& g, int mode, const void* inq, con
     const CUtensorMapSwizzle sw = swizzle_for(L.cb);
     CUtensorMap tmA, tmB;
     {
-        const cuuint64_t ic = static_cast<cuuint64_t>(g.IC);
-        cuuint64_t dims[5] = {ic, static_cast<cuuint64_t>(g.IW), static_cast<cuuint64_t>(g.IH),
-                              static_cast<cuuint64_t>(g.ID), static_cast<cuuint64_t>(g.N)};
-        cuuint64_t strides[4] = {ic * eb, ic * eb * g.IW, ic * eb * g.IW * g.IH, ic * eb * g.IW * g.IH * g.ID};
-        cuuint32_t box[5] = {static_cast<cuuint32_t>(L.cb / eb), static_cast<cuuint32_t>(L.bw),
-                             static_cast<cuuint32_t>(L.bh), static_cast<cuuint32_t>(L.bd), static_cast<cuuint32_t>(L.bn)};
-        cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-        if (encode_fn()(&tmA, dt, 5, const_cast<void*>(inq), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+        // Padded input as rows of IC channels; box: one K-block x 128 rows.
+        cuuint64_t dims[2] = {static_cast<cuuint64_t>(g.IC), static_cast<cuuint64_t>(L.rows)};
+        cuuint64_t strides[1] = {static_cast<cuuint64_t>(g.IC) * eb};
+        cuuint32_t box[2] = {static_cast<cuuint32_t>(L.cb / eb), static_cast<cuuint32_t>(BM)};
+        cuuint32_t estr[2] = {1, 1};
+        if (encode_fn()(&tmA, dt, 2, const_cast<void*>(inq), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return cudaErrorInvalidValue;
     }
@@ -592,13 +739,12 @@ cudaError_t launch_conv3d_tc(const Conv3dGeom& g, int mode, const void* inq, con
     }
     ConvTcParams p;
     p.N = g.N; p.OD = g.OD; p.OH = g.OH; p.OW = g.OW; p.OC = g.OC;
+    p.Dp = L.Dp; p.Hp = L.Hp; p.Wp = L.Wp;
     p.KH = g.KH; p.KW = g.KW;
-    p.pd = g.pd; p.ph = g.ph; p.pw = g.pw;
-    p.bw = L.bw; p.bh = L.bh; p.bd = L.bd; p.bn = L.bn;
-    p.tw = L.tw; p.th = L.th; p.td = L.td;
-    p.m_tiles = L.tw * L.th * L.td * L.tn;
+    p.m_tiles = L.m_tiles;
     p.n_tiles = L.n_tiles;
     p.units = p.m_tiles * p.n_tiles;
+    p.p_last = static_cast<int>(L.p_last);
     p.cb = L.cb;
     p.celems = L.cb / eb;
     p.cpt = static_cast<int>(static_cast<int64_t>(g.IC) * eb / L.cb);
@@ -606,12 +752,13 @@ cudaError_t launch_conv3d_tc(const Conv3dGeom& g, int mode, const void* inq, con
     p.n_mma = L.n_mma;
     p.stages = L.stages;
     p.b_res = L.b_res;
-    p.i8 = mode == 2 ? 1 : 0;
+    p.kbs = L.kbs;
     p.post = op;
     p.a_bytes = L.a_bytes;
     p.b_bytes = L.b_bytes;
     p.stage_bytes = L.stage_bytes;
     p.ring_off = L.ring_off;
+    p.stg_off = L.stg_off;
     p.bar_off = L.bar_off;
     p.scales = scales;
     p.bias = bias;
@@ -620,17 +767,20 @@ cudaError_t launch_conv3d_tc(const Conv3dGeom& g, int mode, const void* inq, con
     p.err = err;
 
     static std::mutex mu;
-    static std::set<int> done;
+    static std::unordered_map<int, bool> done;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     {
         std::lock_guard<std::mutex> lk(mu);
         if (!done.count(dev)) {
-            e = cudaFuncSetAttribute(conv3d_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            e = cudaFuncSetAttribute(conv3d_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(kSmemCap));
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(conv3d_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kSmemCap));
             if (e != cudaSuccess) return e;
-            done.insert(dev);
+            done[dev] = true;
         }
     }
     cudaLaunchConfig_t cfg = {};
@@ -643,7 +793,8 @@ cudaError_t launch_conv3d_tc(const Conv3dGeom& g, int mode, const void* inq, con
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, conv3d_tc_kernel, tmA, tmB, p);
+    return mode == 2 ? cudaLaunchKernelEx(&cfg, conv3d_tc_kernel<true>, tmA, tmB, p)
+                     : cudaLaunchKernelEx(&cfg, conv3d_tc_kernel<false>, tmA, tmB, p);
 }
 
 }  // namespace dnnopt_b200

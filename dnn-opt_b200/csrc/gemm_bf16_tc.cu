@@ -54,6 +54,7 @@ enum BMode : int {
 struct TcParams {
     int M, N, K;
     int n_mma, num_kb, kpad, n_chunks, num_tiles, stages, b_mode;
+    int kbs, groups;   // A K-blocks per ring stage, stages per tile
     uint32_t sb_bytes;
     float alpha, beta;
     const uint16_t* B;
@@ -87,7 +88,8 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint8_t* sB = base;
     uint8_t* sA = sB + p.sb_bytes;
-    uint8_t* sC = sA + p.stages * kStageBytes;
+    const uint32_t stage_bytes = static_cast<uint32_t>(p.kbs) * kStageBytes;
+    uint8_t* sC = sA + p.stages * stage_bytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(sC + kCStagingBytes);
     uint64_t* empty = full + p.stages;
     uint64_t* tfull = empty + p.stages;
@@ -99,16 +101,20 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     // Tiles of this CTA: blockIdx.x, +gridDim.x, ...; producer iteration i
-    // loads K-block (i % num_kb) of the (i / num_kb)-th of them.
+    // loads K-block group (i % groups) of the (i / groups)-th of them: kbs
+    // K-blocks per stage (a stage costs a roughly fixed mbarrier round trip,
+    // so larger stages stream faster).
     const int my_tiles = (p.num_tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
                          static_cast<int>(gridDim.x);
-    const uint32_t total_iters = static_cast<uint32_t>(my_tiles > 0 ? my_tiles : 0) * p.num_kb;
+    const uint32_t total_iters = static_cast<uint32_t>(my_tiles > 0 ? my_tiles : 0) * p.groups;
     auto issue_load = [&](uint32_t i) {
         const uint32_t s = i % p.stages;
-        const int tile = static_cast<int>(blockIdx.x) + static_cast<int>(i / p.num_kb) * static_cast<int>(gridDim.x);
-        const int kb = static_cast<int>(i % p.num_kb);
-        mbar_arrive_expect_tx(&full[s], kStageBytes);
-        tma_load_2d(sA + s * kStageBytes, &tmA, &full[s], kb * kKBlock, tile * BM);
+        const int tile = static_cast<int>(blockIdx.x) + static_cast<int>(i / p.groups) * static_cast<int>(gridDim.x);
+        const int kb0 = static_cast<int>(i % p.groups) * p.kbs;
+        const int nsub = min(p.kbs, p.num_kb - kb0);
+        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nsub) * kStageBytes);
+        for (int sub = 0; sub < nsub; ++sub)
+            tma_load_2d(sA + s * stage_bytes + sub * kStageBytes, &tmA, &full[s], (kb0 + sub) * kKBlock, tile * BM);
     };
     const uint32_t pre = total_iters < static_cast<uint32_t>(p.stages) ? total_iters
                                                                        : static_cast<uint32_t>(p.stages);
@@ -199,26 +205,31 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 if (!mbar_wait(&tempty[buf], tph ^ 1u, abort_flag, p.err)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + buf * p.n_mma;
-                for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+                for (int grp = 0; grp < p.groups; ++grp, ++it) {
                     const uint32_t s = it % p.stages, ph = (it / p.stages) & 1u;
                     if (!mbar_wait(&full[s], ph, abort_flag, p.err)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_u32(sA + s * kStageBytes);
-                    // K step of 16: 32 bytes along a K-major row, or two
-                    // 1024-byte 8-row atoms down an MN-major chunk (the B
-                    // layout branch taken once per K-block).
-                    if (p.b_mode == kBTmaMN) {
+                    const int kb0 = grp * p.kbs;
+                    const int nsub = min(p.kbs, p.num_kb - kb0);
+                    for (int sub = 0; sub < nsub; ++sub) {
+                        const int kb = kb0 + sub;
+                        const uint32_t a_addr = smem_u32(sA + s * stage_bytes + sub * kStageBytes);
+                        // K step of 16: 32 bytes along a K-major row, or two
+                        // 1024-byte 8-row atoms down an MN-major chunk (the B
+                        // layout branch taken once per K-block).
+                        if (p.b_mode == kBTmaMN) {
 #pragma unroll
-                        for (int kk = 0; kk < kKBlock / 16; ++kk)
-                            umma_f16_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32),
-                                        umma_desc_mn_sw128(sb_addr + (kb * 8 + kk * 2) * 1024, lbo), idesc,
-                                        (kb | kk) != 0 ? 1u : 0u);
-                    } else {
+                            for (int kk = 0; kk < kKBlock / 16; ++kk)
+                                umma_f16_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32),
+                                            umma_desc_mn_sw128(sb_addr + (kb * 8 + kk * 2) * 1024, lbo), idesc,
+                                            (kb | kk) != 0 ? 1u : 0u);
+                        } else {
 #pragma unroll
-                        for (int kk = 0; kk < kKBlock / 16; ++kk)
-                            umma_f16_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32),
-                                        umma_desc_k_sw128(sb_addr + kb * p.n_mma * 128 + kk * 32), idesc,
-                                        (kb | kk) != 0 ? 1u : 0u);
+                            for (int kk = 0; kk < kKBlock / 16; ++kk)
+                                umma_f16_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32),
+                                            umma_desc_k_sw128(sb_addr + kb * p.n_mma * 128 + kk * 32), idesc,
+                                            (kb | kk) != 0 ? 1u : 0u);
+                        }
                     }
                     umma_commit(&empty[s]);   // stage is free once these MMAs retire
                 }
@@ -325,7 +336,7 @@ EncodeTiledFn get_encode_fn() {
 }
 
 struct Layout {
-    int b_mode, n_mma, num_kb, kpad, n_chunks, stages, ctas_per_sm;
+    int b_mode, n_mma, num_kb, kpad, n_chunks, stages, ctas_per_sm, kbs;
     uint32_t sb_bytes, tmem_cols;
     size_t smem;
 };
@@ -355,6 +366,7 @@ Layout plan_layout(const GemmArgs& g) {
     const size_t fixed = 1024 + static_cast<size_t>(L.sb_bytes) + kCStagingBytes + 256;
     const size_t per_cta2 = kSmemPerSm / 2 - 1024;
     const int st2 = fixed < per_cta2 ? static_cast<int>((per_cta2 - fixed) / kStageBytes) : 0;
+    L.kbs = 1;
     if (st2 >= 2 && 2 * L.tmem_cols <= 512) {
         L.stages = st2 > 4 ? 4 : st2;
         L.ctas_per_sm = 2;
@@ -363,7 +375,7 @@ Layout plan_layout(const GemmArgs& g) {
         L.stages = st > kMaxStages ? kMaxStages : st;
         L.ctas_per_sm = 1;
     }
-    L.smem = fixed + static_cast<size_t>(L.stages) * kStageBytes;
+    L.smem = fixed + static_cast<size_t>(L.stages) * L.kbs * kStageBytes;
     return L;
 }
 
@@ -438,6 +450,7 @@ cudaError_t launch_gemm_bf16_tc(const GemmArgs& g, int num_sms, uint32_t* err, c
     p.n_mma = L.n_mma; p.num_kb = L.num_kb; p.kpad = L.kpad; p.n_chunks = L.n_chunks;
     p.num_tiles = (g.M + BM - 1) / BM;
     p.stages = L.stages; p.b_mode = L.b_mode; p.sb_bytes = L.sb_bytes;
+    p.kbs = L.kbs; p.groups = (L.num_kb + L.kbs - 1) / L.kbs;
     p.alpha = g.alpha; p.beta = g.beta;
     p.B = static_cast<const uint16_t*>(g.B); p.ldb = g.ldb; p.b_trans = g.b_trans;
     p.C = static_cast<const float*>(g.C); p.ldc = g.ldc;

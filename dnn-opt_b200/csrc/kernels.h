@@ -194,18 +194,22 @@ cudaError_t launch_gemm_tile_s8_conv(const Conv3dGeom& g, const int8_t* in_q, co
                                      const float* scales, const float* bias, int op, float* out,
                                      cudaStream_t s);
 // BF16 / INT8 conv3d with stride 1 as an implicit GEMM on tcgen05
-// (conv3d_tc.cu): TMA boxes of the NDHWC input shifted per filter tap are the
-// A tiles (no column matrix), the filter resident in shared memory when it
-// fits, bias / dequantisation / post-op in the epilogue.  Needs IC * element
-// size a multiple of 32 bytes.  mode 1: BF16, 2: INT8.
+// (conv3d_tc.cu): the input prepared once into a zero-padded NDHWC copy, in
+// which every filter tap of 128 consecutive output rows is one 2-D TMA box
+// (no column matrix); the filter resident in shared memory when it fits;
+// bias / dequantisation / post-op in the epilogue.  Needs IC * element size a
+// multiple of 32 bytes.  mode 1: BF16, 2: INT8.
 bool conv3d_tc_ok(const Conv3dGeom& g, int mode);
-// Bytes of the absmax partials the INT8 preparation needs.
-size_t conv3d_tc_part_bytes();
-// Operands for launch_conv3d_tc: BF16 bits of input and filter (one launch),
-// or INT8 (per-CTA absmax partials, then scales[0..3] and the quantised input
-// and filter: two launches).  inq / fq 16-byte aligned.
-cudaError_t launch_conv3d_tc_prep(int mode, const float* in, int64_t nin, const float* f, int64_t nf, void* inq,
-                                  void* fq, void* part, float* scales, cudaStream_t s);
+// Bytes of the padded input copy.
+size_t conv3d_tc_input_bytes(const Conv3dGeom& g, int mode);
+// Operands for launch_conv3d_tc: BF16 bits of the padded input and the
+// filter, or INT8 in one cooperative launch (absmax into this call's slot of
+// the four zero-initialised words `maxslots`, grid barrier on the two
+// zero-initialised words `sync`, scales[0..3], quantised padded input and
+// filter).  inq / fq 16-byte aligned.
+cudaError_t launch_conv3d_tc_prep(const Conv3dGeom& g, int mode, const float* in, const float* f, void* inq, void* fq,
+                                  uint32_t* sync, uint32_t* maxslots, float* scales, uint32_t* err, int num_sms,
+                                  cudaStream_t s);
 cudaError_t launch_conv3d_tc(const Conv3dGeom& g, int mode, const void* inq, const void* fq, const float* scales,
                              const float* bias, int op, float* out, uint32_t* err, int num_sms, cudaStream_t s);
 // out = post_op(v + bias[oc]); v = out, or float(acc) * (scales[0] * scales[1]) when acc.

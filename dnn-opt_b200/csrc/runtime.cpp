@@ -103,7 +103,10 @@ int ensure_workspace(DeviceContext* ctx, cudaStream_t stream, size_t ws_floats, 
     Workspace& w = ctx->ws[stream];
     cudaError_t e;
     if (!w.err) {
-        // err, absmax[2], scales[2] share one small allocation.
+        // err (word 0), absmax (words 4-5), the conv prep's grid-barrier
+        // count and generation (words 6-7), scales (words 8-11) and the conv
+        // prep's two absmax slots (words 12-15) share one small
+        // zero-initialised allocation.
         void* small = nullptr;
         e = cudaMalloc(&small, 64);
         if (e != cudaSuccess) return cuda_status(e);

@@ -24,7 +24,7 @@ struct Workspace {
     uint32_t* counters = nullptr;   // split-K tickets (kept zero between launches)
     size_t n_counters = 0;
     uint32_t* err = nullptr;        // bounded-wait error word
-    uint32_t* absmax = nullptr;     // [2] absmax bit patterns (FP32-API int8)
+    uint32_t* absmax = nullptr;     // [2] absmax bit patterns (FP32-API int8), [2..3] grid-barrier words
     float* scales = nullptr;        // [2] sA, sB
     void* quant = nullptr;          // quantised copies of A and B
     size_t quant_bytes = 0;
