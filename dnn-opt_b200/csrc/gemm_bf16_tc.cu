@@ -8,9 +8,9 @@
 // Shape physics: at N=64, K=256 the GEMM does 43 flop per HBM byte, far below
 // the BF16 ridge (~250 flop/B), so the kernel streams A and C at HBM speed and
 // keeps the tensor cores a few percent busy.  Design:
-//   * persistent CTAs walk 128-row tiles of A; two CTAs per SM when shared
-//     memory and TMEM allow (a shallow ring each: measured faster than one CTA
-//     with a deep ring);
+//   * persistent CTAs walk 128-row tiles of A: one CTA per SM with four
+//     K-blocks per ring stage when K spans four or more K-blocks, else two
+//     CTAs per SM when shared memory and TMEM allow;
 //   * one thread issues every TMA load: B once per CTA, straight into the UMMA
 //     operand layout (MN-major 128-byte swizzle when B is K x N, K-major when B
 //     is N x K; an element gather only when B's rows are not 16-byte aligned),
@@ -80,6 +80,10 @@ __device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t smem_addr, uint3
     return d;
 }
 
+// MN: B in the MN-major layout (kBTmaMN), else K-major.  A compile-time
+// choice: a run-time branch between MMA forms in the issue loop measured twice
+// the issue time per MMA on B200.
+template <bool MN>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmC, const TcParams p) {
@@ -195,7 +199,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             uint32_t idesc = umma_idesc_bf16_f32(BM, p.n_mma);
-            if (p.b_mode == kBTmaMN) idesc |= 1u << 16;          // B operand MN-major
+            if constexpr (MN) idesc |= 1u << 16;                 // B operand MN-major
             const uint32_t sb_addr = smem_u32(sB);
             const uint32_t lbo = static_cast<uint32_t>(p.kpad) * 128u;
             bool ok = p.b_mode == kBGather || mbar_wait(bfull, 0, abort_flag, p.err);
@@ -217,7 +221,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                         // K step of 16: 32 bytes along a K-major row, or two
                         // 1024-byte 8-row atoms down an MN-major chunk (the B
                         // layout branch taken once per K-block).
-                        if (p.b_mode == kBTmaMN) {
+                        if constexpr (MN) {
 #pragma unroll
                             for (int kk = 0; kk < kKBlock / 16; ++kk)
                                 umma_f16_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32),
@@ -341,9 +345,11 @@ struct Layout {
     size_t smem;
 };
 
-// B operand mode, shared-memory plan and CTAs per SM.  Measured on B200: two
-// CTAs per SM with a 2-4 stage ring stream A faster than one CTA with a deep
-// ring; one CTA per SM (up to 8 stages) when B or TMEM leaves no room for two.
+// B operand mode, shared-memory plan and CTAs per SM.  Measured on B200: one
+// CTA per SM with four K-blocks per stage streams A fastest when K has four
+// or more K-blocks; for shallower K two CTAs per SM with a 2-4 stage ring beat
+// one CTA with a deep ring of single K-blocks; one CTA per SM (up to 8 stages)
+// when B or TMEM leaves no room for two.
 Layout plan_layout(const GemmArgs& g) {
     Layout L;
     const bool b_aligned = reinterpret_cast<uintptr_t>(g.B) % 16 == 0 && g.ldb % 8 == 0;
@@ -367,7 +373,16 @@ Layout plan_layout(const GemmArgs& g) {
     const size_t per_cta2 = kSmemPerSm / 2 - 1024;
     const int st2 = fixed < per_cta2 ? static_cast<int>((per_cta2 - fixed) / kStageBytes) : 0;
     L.kbs = 1;
-    if (st2 >= 2 && 2 * L.tmem_cols <= 512) {
+    // Four or more K-blocks per tile: one CTA per SM with four K-blocks per
+    // ring stage (a stage costs a roughly fixed mbarrier round trip; measured
+    // on 65536 x 64 x 256: 11.9 us against 12.8 us for two CTAs per SM with
+    // one K-block per stage).  Shallower K: two CTAs per SM.
+    const int st4 = fixed < kSmemLimit ? static_cast<int>((kSmemLimit - fixed) / (4 * kStageBytes)) : 0;
+    if (L.num_kb >= 4 && st4 >= 2) {
+        L.kbs = 4;
+        L.stages = st4 > kMaxStages ? kMaxStages : st4;
+        L.ctas_per_sm = 1;
+    } else if (st2 >= 2 && 2 * L.tmem_cols <= 512) {
         L.stages = st2 > 4 ? 4 : st2;
         L.ctas_per_sm = 2;
     } else {
@@ -464,8 +479,11 @@ cudaError_t launch_gemm_bf16_tc(const GemmArgs& g, int num_sms, uint32_t* err, c
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev != smem_set_dev) {
-        e = cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(kSmemLimit));
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(kSmemLimit));
         if (e != cudaSuccess) return e;
         smem_set_dev = dev;
     }
@@ -480,7 +498,8 @@ cudaError_t launch_gemm_bf16_tc(const GemmArgs& g, int num_sms, uint32_t* err, c
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemm_bf16_tc_kernel, tmA, tmB, tmC, p);
+    return L.b_mode == kBTmaMN ? cudaLaunchKernelEx(&cfg, gemm_bf16_tc_kernel<true>, tmA, tmB, tmC, p)
+                               : cudaLaunchKernelEx(&cfg, gemm_bf16_tc_kernel<false>, tmA, tmB, tmC, p);
 }
 
 }  // namespace dnnopt_b200

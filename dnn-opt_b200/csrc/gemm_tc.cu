@@ -18,8 +18,9 @@
 // consume it (K = 16 bf16 or K = 32 int8 per instruction).
 //
 // Work units are (split, m-tile, n-tile) with 128-row m-tiles and n-tiles of
-// n_mma <= 256 columns; persistent CTAs (one per SM: a 192 KB ring of 4
-// stages at n_mma = 256, up to 8 for narrower tiles) walk the units.  Roles: warp 0 issues TMA loads, warp 1 owns TMEM and
+// n_mma <= 256 columns; persistent CTAs (one per SM, a 192 KB ring of stages
+// of up to 64 KB: one K-block at n_mma = 256, several for narrower tiles or
+// small M, whose A blocks hold only M rows) walk the units.  Roles: warp 0 issues TMA loads, warp 1 owns TMEM and
 // issues the MMAs into one of two accumulators (so the epilogue of a unit
 // overlaps the MMAs of the next), warps 2-5 drain TMEM with tcgen05.ld (warp
 // q owns TMEM lanes / tile rows 32(q%4) ...) and write C directly.  With a
@@ -49,9 +50,9 @@ constexpr int kThreads = 192;
 constexpr int kMaxStages = 8;
 constexpr int kRingBytes = 4 * (128 * 128 + 256 * 128);   // 192 KB of stages
 constexpr int kMaxN = 256;
-constexpr int kMaxSplits = 4;
+constexpr int kMaxSplits = 4;                      // K splits reduced through the global workspace
+constexpr int kMaxClusterSplits = 8;               // K splits reduced inside a cluster (portable size)
 constexpr int kRedItems = 4;                       // column quads per thread per reduction round
-constexpr int kABytes = BM * kKBytes;              // 16 KB
 constexpr int kCStageBytes = 32 * 128;                // one 32 x 32 4-byte store block
 constexpr int kCStaging = 4 * 2 * kCStageBytes;       // 4 epilogue warps x 2 buffers
 constexpr size_t kSmem = 1024 + static_cast<size_t>(kRingBytes) + kCStaging + 256;
@@ -70,8 +71,10 @@ enum TcEpi : int {
 struct TcGemmParams {
     int M, N, K;
     int n_mma, num_kb, kb_per_split, splits;
-    int kbs;               // 128-byte K-blocks per ring stage (2 for tiles of <= 128 columns)
+    int kbs;               // 128-byte K-blocks per ring stage (stages of up to 64 KB)
     int stages;            // ring depth: kRingBytes / stage bytes, at most kMaxStages
+    int a_rows;            // A rows loaded per K-block: 128, or M rounded up to 8 when M < 128
+    uint32_t a_bytes, sub_bytes;   // a_rows * 128; one K-block of A and B
     int m_tiles, n_tiles, units;
     int op, epi;
     float alpha, beta;
@@ -80,7 +83,8 @@ struct TcGemmParams {
     const float* scales;   // {sA, sB} for kEpiS8DQ
     int c_vec;             // 1: C 16-byte aligned with ldc % 4 == 0 (vector epilogue)
     int c_tma;             // 1: unsplit tiles with beta == 0 go out by TMA stores (tmC)
-    void* ws;              // [tiles][splits][BM][n_mma] partials (splits > 1)
+    int cluster;           // 1: the splits of a tile are one thread-block cluster (one unit per CTA)
+    void* ws;              // [tiles][splits][BM][n_mma] partials (splits > 1, not cluster)
     uint32_t* tickets;     // one per tile, zero on entry, left zero
     uint32_t* err;
 };
@@ -114,6 +118,12 @@ __device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t smem_addr, uint32_t l
     d |= static_cast<uint64_t>(1u) << 46;
     d |= static_cast<uint64_t>(2u) << 61;
     return d;
+}
+
+__device__ __forceinline__ void st_dsmem_v4(uint32_t cluster_addr, uint4 v) {
+    asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w)
+                 : "memory");
 }
 
 // Epilogue of four consecutive outputs (row, col .. col+3) from raw
@@ -166,6 +176,9 @@ __device__ __forceinline__ void store4(const TcGemmParams& p, int row, int col, 
     }
 }
 
+// OP is a template parameter: a run-time branch between MMA forms in the
+// issue loop measured twice the issue time per MMA on B200.
+template <int OP>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, const TcGemmParams p) {
@@ -174,8 +187,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint8_t* stages = base;
     const int kStages = p.stages;
-    const uint32_t kSubBytes = static_cast<uint32_t>(kABytes) + static_cast<uint32_t>(p.n_mma) * kKBytes;
-    const uint32_t kStageBytes = static_cast<uint32_t>(p.kbs) * kSubBytes;   // [A kb][B kb] per K-block
+    // Stage = kbs x [A K-block (a_rows rows)][B K-block].  With a_rows < 128
+    // the MMA's M = 128 rows read past the loaded A rows into neighbouring
+    // shared memory: those accumulator rows are >= M and never stored.
+    const uint32_t kSubBytes = p.sub_bytes;
+    const uint32_t kStageBytes = static_cast<uint32_t>(p.kbs) * kSubBytes;
     uint8_t* sC = base + kRingBytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(base + kRingBytes + kCStaging);
     uint64_t* empty = full + kMaxStages;
@@ -186,7 +202,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     volatile uint32_t* last_flag = tmem_slot + 2;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t b_bytes = static_cast<uint32_t>(p.n_mma) * kKBytes;
     const uint32_t tmem_cols = static_cast<uint32_t>(2 * p.n_mma) <= 32 ? 32u
                              : (static_cast<uint32_t>(2 * p.n_mma) <= 64 ? 64u
                              : (static_cast<uint32_t>(2 * p.n_mma) <= 128 ? 128u
@@ -236,13 +251,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
                     if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.err)) break;
                     const int nsub = min(p.kbs, kb0 + nkb - kb);
-                    mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nsub) * (kABytes + b_bytes));
+                    mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nsub) * kSubBytes);
                     for (int sub = 0; sub < nsub; ++sub) {
                         uint8_t* sa = stages + s * kStageBytes + sub * kSubBytes;
-                        uint8_t* sb = sa + kABytes;
-                        const int kx = p.op == kOpI8 ? (kb + sub) * kKBytes : (kb + sub) * (kKBytes / 2);   // elements
+                        uint8_t* sb = sa + p.a_bytes;
+                        const int kx = OP == kOpI8 ? (kb + sub) * kKBytes : (kb + sub) * (kKBytes / 2);   // elements
                         tma_load_2d(sa, &tmA, &full[s], kx, mt * BM);
-                        if (p.op == kOpBf16MN) {
+                        if constexpr (OP == kOpBf16MN) {
                             // 64-column chunks of 64 K rows: chunk j at j * 8 KB.
                             for (int j = 0; j < p.n_mma / 64; ++j)
                                 tma_load_2d(sb + j * 8192, &tmB, &full[s], nt * p.n_mma + j * 64, kx);
@@ -259,7 +274,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         // 32 bytes of K per MMA, +32 B along a K-major 128-byte row, or two
         // 1024-B atoms (16 K rows) down an MN-major chunk.
         if (lane == 0) {
-            const uint32_t idesc = tc_idesc(p.op, BM, p.n_mma);
+            const uint32_t idesc = tc_idesc(OP, BM, p.n_mma);
             uint32_t it = 0, titer = 0;
             bool ok = true;
             for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++titer) {
@@ -277,14 +292,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     const int nsub = min(p.kbs, nkb - kb);
                     for (int sub = 0; sub < nsub; ++sub) {
                         const uint32_t a_addr = smem_u32(stages + s * kStageBytes + sub * kSubBytes);
-                        const uint32_t b_addr = a_addr + kABytes;
+                        const uint32_t b_addr = a_addr + p.a_bytes;
                         const int kl = kb + sub;
-                        if (p.op == kOpI8) {
+                        if constexpr (OP == kOpI8) {
 #pragma unroll
                             for (int kk = 0; kk < 4; ++kk)
                                 umma_i8_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32),
                                            umma_desc_k_sw128(b_addr + kk * 32), idesc, (kl | kk) != 0);
-                        } else if (p.op == kOpBf16MN) {
+                        } else if constexpr (OP == kOpBf16MN) {
 #pragma unroll
                             for (int kk = 0; kk < 4; ++kk)
                                 umma_f16_ss(d_tmem, umma_desc_k_sw128(a_addr + kk * 32),
@@ -307,7 +322,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int q = warp & 3;           // TMEM lanes 32q .. 32q+31 (warp id mod 4)
         const int ep_tid = tid - 64;      // 0..127
         uint32_t titer = 0, cgrp = 0;
-        for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x, ++titer) {
+        if (p.cluster) {
+            // Cluster split-K: this CTA's one unit is done once its
+            // accumulator is complete; the rows leave TMEM after the cluster
+            // barrier below.
+            if (!mbar_wait_warp(&tfull[0], 0u, abort_flag, p.err) && lane == 0) *abort_flag = 1u;
+        }
+        for (int u = blockIdx.x; !p.cluster && u < p.units && !*abort_flag; u += gridDim.x, ++titer) {
             int split, mt, nt;
             unit_coords(u, split, mt, nt);
             const uint32_t buf = titer & 1u, tph = (titer >> 1) & 1u;
@@ -446,6 +467,71 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
     tc_fence_before();
     __syncthreads();
+    if (p.cluster) {
+        // Barrier A: every CTA of the cluster has its accumulator complete, so
+        // every ring is idle.  Each split then pushes its partial rows from
+        // TMEM into the owning CTA's ring with remote (fire-and-forget)
+        // stores: CTA `rank` owns tile rows [rank*per, (rank+1)*per), laid
+        // out [split][row][n_mma + 4] (16-byte chunks of consecutive rows in
+        // different banks).  Barrier B makes them visible; the owner sums its
+        // rows over the splits in split order (int32: exact; FP32: a fixed
+        // order) from its own shared memory and applies the epilogue.
+        cluster_sync_all();
+        int split, mt, nt;
+        unit_coords(static_cast<int>(blockIdx.x), split, mt, nt);
+        const int mrows = min(BM, p.M - mt * BM);
+        const int per = (mrows + p.splits - 1) / p.splits;
+        const int pstride = p.n_mma + 4;
+        const uint32_t part0 = smem_u32(stages);
+        if (warp >= 2) {
+            tc_fence_after();
+            const int q = warp & 3;
+            const int row_in = q * 32 + lane;
+            const int owner = row_in < mrows ? row_in / per : 0;
+            const uint32_t dst = map_to_cta(
+                part0 + static_cast<uint32_t>(((split * per) + (row_in - owner * per)) * pstride) * 4u,
+                static_cast<uint32_t>(owner));
+            const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+            for (int c0 = 0; c0 < p.n_mma; c0 += 32) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x16(t_addr + c0, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+                tmem_ld_32x32b_x16(t_addr + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
+                tmem_ld_wait();
+                if (row_in >= mrows) continue;
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    st_dsmem_v4(dst + static_cast<uint32_t>(c0 + j) * 4u, make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]));
+            }
+        }
+        cluster_sync_all();
+        const uint32_t rank = cluster_ctarank();
+        const int r0 = static_cast<int>(rank) * per;
+        const int r1 = min(mrows, r0 + per);
+        const int quads = p.n_mma / 4;
+        const int col0 = nt * p.n_mma;
+        const int items = r0 < r1 ? (r1 - r0) * quads : 0;
+        const uint32_t* part = reinterpret_cast<const uint32_t*>(stages);
+        for (int item = tid; item < items; item += kThreads) {
+            const int lr = item / quads, c4 = (item % quads) * 4;
+            if (col0 + c4 >= p.N) continue;
+            int32_t si[4] = {0, 0, 0, 0};
+            float sf[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (int k = 0; k < p.splits; ++k) {
+                const uint4 v = *reinterpret_cast<const uint4*>(part + ((k * per) + lr) * pstride + c4);
+                const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    si[j] += static_cast<int32_t>(w4[j]);
+                    sf[j] += __uint_as_float(w4[j]);
+                }
+            }
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                w[j] = p.epi == kEpiF32 ? __float_as_uint(sf[j]) : static_cast<uint32_t>(si[j]);
+            if (!*abort_flag) store4(p, mt * BM + r0 + lr, col0 + c4, w);
+        }
+    }
     pdl_launch_dependents();
     if (warp == 1) {
         tc_fence_after();
@@ -509,14 +595,19 @@ TcPlan gemm_tc_plan(TcKind kind, const GemmArgs& g, int num_sms) {
     // Narrower tiles before a K split: a split tile's last CTA sums every
     // split's partial tile alone, so more tiles (B columns read by more CTAs,
     // A re-read from L2) cost less than deep splits.
-    while (n > 64 && m_tiles * ((g.N + n - 1) / n) * 2 <= num_sms) n /= 2;
+    // Narrow no further than 128 columns: every MMA instruction and every ring
+    // stage has a roughly fixed cost (measured on B200), so a K split keeps
+    // more work per MMA than a narrower tile does.
+    while (n > 128 && m_tiles * ((g.N + n - 1) / n) * 2 <= num_sms) n /= 2;
     pl.n_mma = n;
     const int n_tiles = (g.N + n - 1) / n;
     const int elems = kind == TcKind::BF16 ? kKBytes / 2 : kKBytes;
     const int num_kb = (g.K + elems - 1) / elems;
     const int tiles = m_tiles * n_tiles;
+    // Splits double while every unit still gets its own CTA, so a split tile
+    // is reduced inside its thread-block cluster (up to 8 CTAs).
     int splits = 1;
-    while (tiles * splits * 2 <= num_sms && num_kb / (splits * 2) >= 4 && splits < kMaxSplits) splits *= 2;
+    while (tiles * splits * 2 <= num_sms && num_kb / (splits * 2) >= 4 && splits < kMaxClusterSplits) splits *= 2;
     pl.kb_per_split = (num_kb + splits - 1) / splits;
     pl.splits = (num_kb + pl.kb_per_split - 1) / pl.kb_per_split;
     return pl;
@@ -535,12 +626,20 @@ int gemm_tc_tickets(const GemmArgs& g, const TcPlan& pl) {
 cudaError_t launch_gemm_tc(TcKind kind, DotKind epi, const GemmArgs& g, const TcPlan& pl, const float* scales,
                            void* ws, uint32_t* tickets, uint32_t* err, int num_sms, cudaStream_t s) {
     if (!gemm_tc_supported(kind, g) || pl.n_mma < 16 || pl.n_mma > kMaxN) return cudaErrorInvalidValue;
-    if (pl.splits > kMaxSplits || (pl.splits > 1 && (!ws || !tickets))) return cudaErrorInvalidValue;
+    const int units = ((g.M + BM - 1) / BM) * ((g.N + pl.n_mma - 1) / pl.n_mma) * pl.splits;
+    // Split tiles are reduced inside a cluster when every unit has its own CTA,
+    // else through the workspace by a ticketed last CTA.
+    const bool cluster = pl.splits > 1 && units <= num_sms && pl.splits <= kMaxClusterSplits;
+    if (!cluster && (pl.splits > kMaxSplits || (pl.splits > 1 && (!ws || !tickets)))) return cudaErrorInvalidValue;
     const bool mn = kind == TcKind::BF16 && !g.b_trans;
     const int op = kind == TcKind::BF16 ? (mn ? kOpBf16MN : kOpBf16K) : kOpI8;
     CUtensorMap tmA, tmB;
+    // A rows per K-block: the whole 128-row tile, or only M (rounded up to 8)
+    // when M < 128, so a small-M GEMM loads no zero rows.
+    const int a_rows = g.M >= BM ? BM : (g.M + 7) / 8 * 8;
     if (kind == TcKind::BF16) {
-        if (!encode(&tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, g.A, g.K, g.M, static_cast<uint64_t>(g.lda) * 2, 64, BM))
+        if (!encode(&tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, g.A, g.K, g.M, static_cast<uint64_t>(g.lda) * 2, 64,
+                    static_cast<uint32_t>(a_rows)))
             return cudaErrorInvalidValue;
         if (mn) {
             if (!encode(&tmB, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, g.B, g.N, g.K, static_cast<uint64_t>(g.ldb) * 2, 64, 64))
@@ -550,7 +649,8 @@ cudaError_t launch_gemm_tc(TcKind kind, DotKind epi, const GemmArgs& g, const Tc
             return cudaErrorInvalidValue;
         }
     } else {
-        if (!encode(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.A, g.K, g.M, static_cast<uint64_t>(g.lda), 128, BM) ||
+        if (!encode(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.A, g.K, g.M, static_cast<uint64_t>(g.lda), 128,
+                    static_cast<uint32_t>(a_rows)) ||
             !encode(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.B, g.K, g.N, static_cast<uint64_t>(g.ldb), 128,
                     static_cast<uint32_t>(pl.n_mma)))
             return cudaErrorInvalidValue;
@@ -577,13 +677,17 @@ cudaError_t launch_gemm_tc(TcKind kind, DotKind epi, const GemmArgs& g, const Tc
     p.epi = epi == DotKind::S8S32 ? kEpiS32 : (epi == DotKind::S8DQ ? kEpiS8DQ : kEpiF32);
     p.alpha = g.alpha; p.beta = g.beta;
     p.C = g.C; p.ldc = g.ldc;
-    // Narrow tiles carry two K-blocks per stage: the cost of a stage (barrier
-    // round trips, commit) is then paid once per 256 bytes of K.
-    p.kbs = pl.n_mma <= 128 ? 2 : 1;
-    p.stages = kRingBytes / (p.kbs * (kABytes + pl.n_mma * kKBytes));
+    // Up to 64 KB per ring stage: a stage's cost (barrier round trips, commit)
+    // is roughly fixed, so small K-blocks travel several to a stage.
+    p.a_rows = a_rows;
+    p.a_bytes = static_cast<uint32_t>(a_rows) * kKBytes;
+    p.sub_bytes = p.a_bytes + static_cast<uint32_t>(pl.n_mma) * kKBytes;
+    p.kbs = 4 * p.sub_bytes <= 65536u ? 4 : (2 * p.sub_bytes <= 65536u ? 2 : 1);
+    p.stages = kRingBytes / (p.kbs * static_cast<int>(p.sub_bytes));
     if (p.stages > kMaxStages) p.stages = kMaxStages;
     p.scales = scales;
     p.c_vec = aligned16(g.C) && g.ldc % 4 == 0 ? 1 : 0;
+    p.cluster = cluster ? 1 : 0;
     p.ws = ws;
     p.tickets = tickets;
     p.err = err;
@@ -596,8 +700,14 @@ cudaError_t launch_gemm_tc(TcKind kind, DotKind epi, const GemmArgs& g, const Tc
     {
         std::lock_guard<std::mutex> lk(mu);
         if (!done.count(dev)) {
-            e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            e = cudaFuncSetAttribute(gemm_tc_kernel<kOpBf16K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(kSmem));
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(gemm_tc_kernel<kOpBf16MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kSmem));
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(gemm_tc_kernel<kOpI8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kSmem));
             if (e != cudaSuccess) return e;
             done.insert(dev);
         }
@@ -607,12 +717,22 @@ cudaError_t launch_gemm_tc(TcKind kind, DotKind epi, const GemmArgs& g, const Tc
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = kSmem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, tmA, tmB, tmC, p);
+    if (cluster) {
+        cfg.gridDim = dim3(static_cast<unsigned>(p.units));
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = static_cast<unsigned>(pl.splits);
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        cfg.numAttrs = 2;
+    }
+    if (op == kOpI8) return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<kOpI8>, tmA, tmB, tmC, p);
+    if (op == kOpBf16MN) return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<kOpBf16MN>, tmA, tmB, tmC, p);
+    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<kOpBf16K>, tmA, tmB, tmC, p);
 }
 
 }  // namespace dnnopt_b200
