@@ -391,6 +391,24 @@ def per_config(torch, dn, stream, pk, world, rank, dist):
                                    "tensor_frac": r["TFLOP_s"] / pk["bf16_tflops"],
                                    "kernel": dn.plan_describe(dn.KIND_BF16F32, d)}
     del As, Bs, Cs
+    # Small-M BF16 on the general tcgen05 GEMM (B [K, N], K split across the
+    # CTAs of a thread-block cluster): the M >= 9 band above the GEMV kernels.
+    for M in (64, 16):
+        N, K = 4096, 4096
+        byts = 2 * (M * K + K * N) + 4 * M * N
+        ns = rotating_sets(byts)
+        As = [torch.randn(M * K, device="cuda").to(torch.bfloat16).view(torch.int16) for _ in range(ns)]
+        Bs = [torch.randn(K * N, device="cuda").to(torch.bfloat16).view(torch.int16) for _ in range(ns)]
+        Cs = [torch.zeros(M * N, device="cuda") for _ in range(ns)]
+        d = dn.desc(M, N, K, K, N, N)
+        for i in range(ns):
+            dn.check(dn.cuda_gemm("bf16f32", d, As[i], Bs[i], Cs[i], s))
+        fns = [lambda i=i: dn.cuda_gemm("bf16f32", d, As[i], Bs[i], Cs[i], s) for i in range(ns)]
+        r = bench_single(torch, dn, s, fns, byts, 2.0 * M * N * K)
+        out[f"bf16_{M}x{N}x{K}"] = {"TFLOP_s": r["TFLOP_s"], "us": r["us_per_call"], "GB_s": r["GB_s"],
+                                    "hbm_frac": r["GB_s"] / pk["hbm_gbs"], "input_sets": ns,
+                                    "kernel": dn.plan_describe(dn.KIND_BF16F32, d)}
+        del As, Bs, Cs
     # C5: e4m3 decode-FFN 8 x 28672 x 8192 (W 235 MB > L2).
     M, N, K = 8, 28672, 8192
     A = torch.from_numpy(bf16_bits(np.random.default_rng(42).standard_normal(M * K)
@@ -517,15 +535,15 @@ def run_profile(args):
             B = torch.from_numpy(ref_uniform(K * N, 123 + i)).cuda()
             C = torch.zeros(M * N, device="cuda")
             calls.append(lambda A=A, B=B, C=C: dn.cuda_gemm("f32", d, A, B, C, s))
-    elif name in ("conv3d_fp32", "conv3d_int8"):
-        # The bench's Conv3D layer: im2col, the GEMM and the post pass per call.
+    elif name in ("conv3d_fp32", "conv3d_bf16", "conv3d_int8"):
+        # The bench's Conv3D layer (BF16 / INT8: operand prep + implicit tcgen05 conv).
         cp = (1, 64, 8, 56, 56, 64, 3, 3, 3, 1, 1, 1, 1, 1, 1)
         nin, nflt, nout = 8 * 56 * 56 * 64, 64 * 27 * 64, 8 * 56 * 56 * 64
         cin = torch.from_numpy(ref_uniform(nin, 3)).cuda()
         cflt = torch.from_numpy(ref_uniform(nflt, 4)).cuda()
         cbias = torch.from_numpy(ref_uniform(64, 5)).cuda()
         cout = torch.zeros(nout, device="cuda")
-        prec = 0 if name == "conv3d_fp32" else 2
+        prec = {"conv3d_fp32": 0, "conv3d_bf16": 1, "conv3d_int8": 2}[name]
         calls.append(lambda: dn.cuda_conv3d(prec, cp, cin, cflt, cbias, cout, dn.POSTOP_RELU, s))
     elif name == "onednn":
         M, N, K = 4096, 1, 4096
@@ -562,6 +580,16 @@ def run_profile(args):
             A = torch.randint(-127, 128, (M * K,), dtype=torch.int8, device="cuda")
             B = torch.randint(-127, 128, (N * K,), dtype=torch.int8, device="cuda")
             calls.append(lambda A=A, B=B: dn.cuda_gemm("s8s32", d, A, B, C, s))
+    elif name == "tc_bf16_small":
+        # The general tcgen05 GEMM on small-M BF16 64 x 4096 x 4096 (B [K, N]):
+        # K split across the CTAs of a thread-block cluster.
+        M, N, K = 64, 4096, 4096
+        d = dn.desc(M, N, K, K, N, N)
+        for i in range(N_SETS):
+            A = torch.randn(M * K, device="cuda").to(torch.bfloat16).view(torch.int16)
+            B = torch.randn(K * N, device="cuda").to(torch.bfloat16).view(torch.int16)
+            C = torch.zeros(M * N, device="cuda")
+            calls.append(lambda A=A, B=B, C=C: dn.cuda_gemm("bf16f32", d, A, B, C, s))
     elif name == "c5":
         M, N, K = 8, 28672, 8192
         d = dn.desc(M, N, K, K, K, N)
@@ -747,7 +775,7 @@ def main():
                     help="streams the 12 independent sweep GEMMs are spread over")
     ap.add_argument("--no-per-config", action="store_true", help="skip the per-config section")
     ap.add_argument("--profile", choices=["c1", "c2", "c3", "c4", "c5", "onednn", "simt64", "tc_i8",
-                                         "conv3d_fp32", "conv3d_int8"],
+                                         "conv3d_fp32", "conv3d_bf16", "conv3d_int8", "tc_bf16_small"],
                     help="run one config's kernel --reps times for an ncu capture, no bench line")
     ap.add_argument("--reps", type=int, default=3)
     args = ap.parse_args()
