@@ -594,7 +594,9 @@ def test_bf16_config4_full(gpu, dn, orc):
     (333, 48, 100, 1.0, 0.5, None), (4096, 256, 128, 0.5, 0.0, None), (257, 128, 320, 1.0, -1.0, 132),
     (129, 80, 8, 1.0, 0.0, None), (9, 64, 256, 1.0, 0.0, None),
     # One and two waves of 128-row tiles on 148 SMs.
-    (18944, 64, 256, 1.0, 0.5, None), (37888, 48, 64, 1.0, 0.0, None)])
+    (18944, 64, 256, 1.0, 0.5, None), (37888, 48, 64, 1.0, 0.0, None),
+    # A partial last round of tiles (one and two CTAs per SM), ragged last tile.
+    (25600, 48, 320, 1.0, 0.0, None), (25563, 64, 256, 1.0, 0.5, None), (51195, 64, 128, 2.0, 0.0, None)])
 def test_bf16_tcgen05_shapes(gpu, dn, orc, M, N, K, alpha, beta, ldc):
     _bf16_case(dn, orc, gpu, M, N, K, alpha, beta, ldc)
 
