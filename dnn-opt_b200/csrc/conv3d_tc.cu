@@ -9,9 +9,12 @@
 // viewed as rows of IC channels, output position (n, od, oh, ow) is row
 //   P = ((n*Dp + od)*Hp + oh)*Wp + ow
 // and its filter tap (kd, kh, kw) reads row P + (kd*Hp + kh)*Wp + kw, so the
-// A tile of a K-block (one tap, one chunk of channels) for 128 consecutive
-// rows P is ONE 2-D TMA box.  Rows P that are not output positions (the
-// padding columns / planes) are computed and dropped.
+// A tiles of the KW taps kw = 0 .. KW-1 of one (kd, kh) and chunk of channels
+// for 128 consecutive rows P are rows kw .. kw+127 of ONE 2-D TMA box of
+// 128 + KW - 1 rows (a window): each tap's UMMA descriptor starts kw rows
+// into it, which the swizzled layout allows (the swizzle follows the absolute
+// shared-memory address; checked on B200).  Rows P that are not output
+// positions (the padding columns / planes) are computed and dropped.
 //
 //   output [N, OD, OH, OW, OC] = sum_k A[P, k] * filter[oc, k],
 //   k = ((kd*KH + kh)*KW + kw)*IC + ic (the reference's column order)
@@ -23,9 +26,9 @@
 //
 // A K-block is cb = 32, 64 or 128 bytes of channels of one tap, staged with
 // the matching TMA swizzle straight into the UMMA K-major layout; each ring
-// stage carries several K-blocks (32-64 KB: on B200 a stage costs a roughly
+// stage carries several windows (up to 64 KB: on B200 a stage costs a roughly
 // fixed mbarrier round trip of about 0.3 us, and a 128-row box about 0.12 us
-// more).  With one channel tile (OC <= 256) the whole filter stays resident
+// more, so one window box instead of KW tap boxes cuts the TMA rows ~KW-fold).  With one channel tile (OC <= 256) the whole filter stays resident
 // in shared memory, loaded with the CTA's first tile.  Roles: warp 0 TMA,
 // warp 1 TMEM + MMA issue into two accumulators, warps 2-5 epilogue (32 x 32
 // blocks transposed through swizzled shared memory into whole 128-byte row
@@ -62,10 +65,15 @@ struct ConvTcParams {
     int p_last;                 // padded row of the last output position
     int cb, celems, cpt, num_kb;   // K-block bytes / elements, K-blocks per tap, total
     int n_mma, stages, b_res;
-    int kbs;                    // K-blocks per ring stage
+    // Windows: one A box of rows_win = 128 + KW - 1 (rounded up to 8) rows
+    // per (kd, kh, channel chunk) serves the KW taps kw = 0 .. KW-1, whose A
+    // operands start kw rows into it (the UMMA descriptor may start at any
+    // row of a swizzled tile: the swizzle follows the absolute address).
+    int num_win, kws;           // windows per tile (KD*KH*cpt), windows per ring stage
+    uint32_t a_slot, win_bytes; // A box slot (1024-byte multiple); A slot + KW B blocks unless resident
     int post;                   // 0 none, 1 relu, 2 relu6
-    uint32_t a_bytes, b_bytes;  // one K-block of A (128 rows) and of B (n_mma rows)
-    uint32_t stage_bytes;       // kbs A blocks, then kbs B blocks unless the filter is resident
+    uint32_t a_bytes, b_bytes;  // one A window box (rows_win rows) and one B K-block (n_mma rows)
+    uint32_t stage_bytes;       // kws windows
     uint32_t ring_off, stg_off, bar_off;
     const float* scales;        // INT8: {s_in, s_f}
     const float* bias;
@@ -161,31 +169,34 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 const int mt = u % p.m_tiles, nt = u / p.m_tiles;
                 const int p0 = mt * BM;
                 const bool load_b = !p.b_res || first;
-                // Tap walk: off = (kd*Hp + kh)*Wp + kw, channel chunk c fastest.
-                int c = 0, kw = 0, kh = 0, off = 0;
+                // Window walk: off = (kd*Hp + kh)*Wp, tap0 = (kd*KH + kh)*KW,
+                // channel chunk c fastest.
+                int c = 0, kh = 0, off = 0, tap0 = 0;
                 bool ok = true;
-                for (int kb = 0; kb < p.num_kb; kb += p.kbs, ++it) {
+                const uint32_t b_load = load_b ? static_cast<uint32_t>(p.KW) * p.b_bytes : 0u;
+                for (int w = 0; w < p.num_win; w += p.kws, ++it) {
                     const uint32_t s = it % p.stages, ph = (it / p.stages) & 1u;
                     if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
                     uint8_t* sa = ring + s * p.stage_bytes;
-                    const int nsub = min(p.kbs, p.num_kb - kb);
-                    mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nsub) * (p.a_bytes + (load_b ? p.b_bytes : 0u)));
+                    const int nsub = min(p.kws, p.num_win - w);
+                    mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nsub) * (p.a_bytes + b_load));
                     for (int sub = 0; sub < nsub; ++sub) {
-                        tma_load_2d(sa + sub * p.a_bytes, &tmA, &full[s], c * p.celems, p0 + off);
+                        uint8_t* wb = sa + sub * p.win_bytes;
+                        tma_load_2d(wb, &tmA, &full[s], c * p.celems, p0 + off);
                         if (load_b)
-                            tma_load_2d(p.b_res ? bres + static_cast<uint32_t>(kb + sub) * p.b_bytes
-                                                : sa + p.kbs * p.a_bytes + sub * p.b_bytes,
-                                        &tmB, &full[s], (kb + sub) * p.celems, nt * p.n_mma);
+                            for (int kw = 0; kw < p.KW; ++kw) {
+                                const int kb = (tap0 + kw) * p.cpt + c;
+                                tma_load_2d(p.b_res ? bres + static_cast<uint32_t>(kb) * p.b_bytes
+                                                    : wb + p.a_slot + kw * p.b_bytes,
+                                            &tmB, &full[s], kb * p.celems, nt * p.n_mma);
+                            }
                         if (++c == p.cpt) {
                             c = 0;
-                            ++off;
-                            if (++kw == p.KW) {
-                                kw = 0;
-                                off += p.Wp - p.KW;
-                                if (++kh == p.KH) {
-                                    kh = 0;
-                                    off += (p.Hp - p.KH) * p.Wp;
-                                }
+                            off += p.Wp;
+                            tap0 += p.KW;
+                            if (++kh == p.KH) {
+                                kh = 0;
+                                off += (p.Hp - p.KH) * p.Wp;
                             }
                         }
                     }
@@ -206,24 +217,38 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 if (!mbar_wait(&tempty[buf], tph ^ 1u, abort_flag, p.err)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + buf * static_cast<uint32_t>(p.n_mma);
-                for (int kb = 0; kb < p.num_kb; kb += p.kbs, ++it) {
+                int c = 0, kh = 0, tap0 = 0;
+                uint32_t acc = 0u;   // 0 until the tile's first MMA
+                const uint32_t bres_addr = smem_u32(bres);
+                // B block of tap kw: resident copy (cpt blocks per tap) or the
+                // window's own KW blocks; chosen once per window so that the
+                // issue loop is branch-free.
+                const uint32_t b_step = p.b_res ? static_cast<uint32_t>(p.cpt) * p.b_bytes : p.b_bytes;
+                for (int w = 0; w < p.num_win; w += p.kws, ++it) {
                     const uint32_t s = it % p.stages, ph = (it / p.stages) & 1u;
                     if (!mbar_wait(&full[s], ph, abort_flag, p.err)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t st_addr = smem_u32(ring + s * p.stage_bytes);
-                    const int nsub = min(p.kbs, p.num_kb - kb);
-                    // Branch-free issue loop: B blocks are b_bytes apart in
-                    // both the resident copy and the stage.
-                    const uint32_t b_base = p.b_res ? smem_u32(bres) + static_cast<uint32_t>(kb) * p.b_bytes
-                                                    : st_addr + p.kbs * p.a_bytes;
+                    const int nsub = min(p.kws, p.num_win - w);
                     for (int sub = 0; sub < nsub; ++sub) {
-                        const uint32_t a_addr = st_addr + sub * p.a_bytes;
-                        const uint32_t b_addr = b_base + sub * p.b_bytes;
-                        for (int kk = 0; kk < ksteps; ++kk) {
-                            const uint64_t da = desc_k_swizzled(a_addr + kk * 32, p.cb);
-                            const uint64_t db = desc_k_swizzled(b_addr + kk * 32, p.cb);
-                            if constexpr (I8) umma_i8(d_tmem, da, db, idesc, ((kb + sub) | kk) != 0);
-                            else umma_f16_ss(d_tmem, da, db, idesc, ((kb + sub) | kk) != 0);
+                        const uint32_t win = st_addr + sub * p.win_bytes;
+                        const uint32_t b0 = p.b_res ? bres_addr + static_cast<uint32_t>(tap0 * p.cpt + c) * p.b_bytes
+                                                    : win + p.a_slot;
+                        for (int kw = 0; kw < p.KW; ++kw) {
+                            const uint32_t a_addr = win + static_cast<uint32_t>(kw * p.cb);
+                            const uint32_t b_addr = b0 + kw * b_step;
+                            for (int kk = 0; kk < ksteps; ++kk) {
+                                const uint64_t da = desc_k_swizzled(a_addr + kk * 32, p.cb);
+                                const uint64_t db = desc_k_swizzled(b_addr + kk * 32, p.cb);
+                                if constexpr (I8) umma_i8(d_tmem, da, db, idesc, acc);
+                                else umma_f16_ss(d_tmem, da, db, idesc, acc);
+                                acc = 1u;
+                            }
+                        }
+                        if (++c == p.cpt) {
+                            c = 0;
+                            tap0 += p.KW;
+                            if (++kh == p.KH) kh = 0;
                         }
                     }
                     umma_commit(&empty[s]);
@@ -568,7 +593,9 @@ int chunk_bytes(const Conv3dGeom& g, int mode) {
 }
 
 struct ConvTcLayout {
-    int Dp, Hp, Wp, cb, n_mma, n_tiles, num_kb, stages, b_res, kbs, m_tiles;
+    int Dp, Hp, Wp, cb, n_mma, n_tiles, num_kb, stages, b_res, m_tiles;
+    int rows_win, num_win, kws;
+    uint32_t a_slot, win_bytes;
     int64_t rows, p_last;
     size_t smem;
     uint32_t a_bytes, b_bytes, stage_bytes, ring_off, stg_off, bar_off;
@@ -593,21 +620,26 @@ bool conv_layout(const Conv3dGeom& g, int mode, ConvTcLayout* L) {
     L->n_tiles = (g.OC + L->n_mma - 1) / L->n_mma;
     const int64_t cpt = static_cast<int64_t>(g.IC) * eb / cb;
     L->num_kb = static_cast<int>(cpt * g.KD * g.KH * g.KW);
-    L->a_bytes = static_cast<uint32_t>(BM * cb);
+    // One A window per (kd, kh, chunk): 128 + KW - 1 rows, rounded up to 8.
+    L->rows_win = (BM + g.KW - 1 + 7) / 8 * 8;
+    if (L->rows_win > 256) return false;   // TMA box limit
+    L->num_win = static_cast<int>(cpt * g.KD * g.KH);
+    L->a_bytes = static_cast<uint32_t>(L->rows_win * cb);
+    L->a_slot = (L->a_bytes + 1023u) / 1024u * 1024u;
     L->b_bytes = static_cast<uint32_t>(L->n_mma * cb);
     const size_t fixed = 1024 + kBarBytes + kStaging;
     const size_t bres = static_cast<size_t>(L->num_kb) * L->b_bytes;
     // The filter stays resident when it leaves room for a ring of at least
-    // four input K-blocks.
-    L->b_res = L->n_tiles == 1 && fixed + bres + 4 * static_cast<size_t>(L->a_bytes) <= kSmemCap ? 1 : 0;
-    // Several K-blocks per ring stage (32-64 KB), at least three stages.
-    const uint32_t per_kb = L->a_bytes + (L->b_res ? 0u : L->b_bytes);
+    // three input windows.
+    L->b_res = L->n_tiles == 1 && fixed + bres + 3 * static_cast<size_t>(L->a_slot) <= kSmemCap ? 1 : 0;
+    L->win_bytes = L->a_slot + (L->b_res ? 0u : static_cast<uint32_t>(g.KW) * L->b_bytes);
+    // Several windows per ring stage (up to 64 KB), preferably three stages.
     const size_t avail = kSmemCap - fixed - (L->b_res ? bres : 0);
-    L->kbs = 1;
+    L->kws = 1;
     for (int k = 8; k > 1; --k)
-        if (k * per_kb <= 65536u && avail / (k * per_kb) >= 3) { L->kbs = k; break; }
-    if (L->kbs > L->num_kb) L->kbs = L->num_kb;
-    L->stage_bytes = static_cast<uint32_t>(L->kbs) * per_kb;
+        if (k * L->win_bytes <= 65536u && avail / (k * L->win_bytes) >= 3) { L->kws = k; break; }
+    if (L->kws > L->num_win) L->kws = L->num_win;
+    L->stage_bytes = static_cast<uint32_t>(L->kws) * L->win_bytes;
     int st = static_cast<int>(avail / L->stage_bytes);
     if (st > kMaxStages) st = kMaxStages;
     if (st < 2) return false;
@@ -719,10 +751,10 @@ cudaError_t launch_conv3d_tc(const Conv3dGeom& g, int mode, const void* inq, con
     const CUtensorMapSwizzle sw = swizzle_for(L.cb);
     CUtensorMap tmA, tmB;
     {
-        // Padded input as rows of IC channels; box: one K-block x 128 rows.
+        // Padded input as rows of IC channels; box: one chunk x rows_win rows.
         cuuint64_t dims[2] = {static_cast<cuuint64_t>(g.IC), static_cast<cuuint64_t>(L.rows)};
         cuuint64_t strides[1] = {static_cast<cuuint64_t>(g.IC) * eb};
-        cuuint32_t box[2] = {static_cast<cuuint32_t>(L.cb / eb), static_cast<cuuint32_t>(BM)};
+        cuuint32_t box[2] = {static_cast<cuuint32_t>(L.cb / eb), static_cast<cuuint32_t>(L.rows_win)};
         cuuint32_t estr[2] = {1, 1};
         if (encode_fn()(&tmA, dt, 2, const_cast<void*>(inq), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
@@ -752,7 +784,10 @@ cudaError_t launch_conv3d_tc(const Conv3dGeom& g, int mode, const void* inq, con
     p.n_mma = L.n_mma;
     p.stages = L.stages;
     p.b_res = L.b_res;
-    p.kbs = L.kbs;
+    p.num_win = L.num_win;
+    p.kws = L.kws;
+    p.a_slot = L.a_slot;
+    p.win_bytes = L.win_bytes;
     p.post = op;
     p.a_bytes = L.a_bytes;
     p.b_bytes = L.b_bytes;
