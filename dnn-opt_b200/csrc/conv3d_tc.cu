@@ -69,7 +69,8 @@ struct ConvTcParams {
     // per (kd, kh, channel chunk) serves the KW taps kw = 0 .. KW-1, whose A
     // operands start kw rows into it (the UMMA descriptor may start at any
     // row of a swizzled tile: the swizzle follows the absolute address).
-    int num_win, kws;           // windows per tile (KD*KH*cpt), windows per ring stage
+    int num_win, kws;           // windows per tile (KD*(KH/hwin)*cpt), windows per ring stage
+    int hwin;                   // filter rows per window: KH when 128 + (KH-1)*Wp + KW - 1 <= 256 rows, else 1
     uint32_t a_slot, win_bytes; // A box slot (1024-byte multiple); A slot + KW B blocks unless resident
     int post;                   // 0 none, 1 relu, 2 relu6
     uint32_t a_bytes, b_bytes;  // one A window box (rows_win rows) and one B K-block (n_mma rows)
@@ -169,11 +170,13 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 const int mt = u % p.m_tiles, nt = u / p.m_tiles;
                 const int p0 = mt * BM;
                 const bool load_b = !p.b_res || first;
-                // Window walk: off = (kd*Hp + kh)*Wp, tap0 = (kd*KH + kh)*KW,
-                // channel chunk c fastest.
+                // Window walk: off = (kd*Hp + kh0)*Wp, tap0 = (kd*KH + kh0)*KW
+                // with kh0 the window's first filter row, channel chunk c
+                // fastest.
                 int c = 0, kh = 0, off = 0, tap0 = 0;
                 bool ok = true;
-                const uint32_t b_load = load_b ? static_cast<uint32_t>(p.KW) * p.b_bytes : 0u;
+                const int wtaps = p.hwin * p.KW;   // taps per window
+                const uint32_t b_load = load_b ? static_cast<uint32_t>(wtaps) * p.b_bytes : 0u;
                 for (int w = 0; w < p.num_win; w += p.kws, ++it) {
                     const uint32_t s = it % p.stages, ph = (it / p.stages) & 1u;
                     if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
@@ -184,17 +187,18 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                         uint8_t* wb = sa + sub * p.win_bytes;
                         tma_load_2d(wb, &tmA, &full[s], c * p.celems, p0 + off);
                         if (load_b)
-                            for (int kw = 0; kw < p.KW; ++kw) {
-                                const int kb = (tap0 + kw) * p.cpt + c;
+                            for (int t = 0; t < wtaps; ++t) {
+                                const int kb = (tap0 + t) * p.cpt + c;
                                 tma_load_2d(p.b_res ? bres + static_cast<uint32_t>(kb) * p.b_bytes
-                                                    : wb + p.a_slot + kw * p.b_bytes,
+                                                    : wb + p.a_slot + t * p.b_bytes,
                                             &tmB, &full[s], kb * p.celems, nt * p.n_mma);
                             }
                         if (++c == p.cpt) {
                             c = 0;
-                            off += p.Wp;
-                            tap0 += p.KW;
-                            if (++kh == p.KH) {
+                            off += p.hwin * p.Wp;
+                            tap0 += wtaps;
+                            kh += p.hwin;
+                            if (kh == p.KH) {
                                 kh = 0;
                                 off += (p.Hp - p.KH) * p.Wp;
                             }
@@ -217,7 +221,8 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 if (!mbar_wait(&tempty[buf], tph ^ 1u, abort_flag, p.err)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + buf * static_cast<uint32_t>(p.n_mma);
-                int c = 0, kh = 0, tap0 = 0;
+                int c = 0, tap0 = 0;
+                const int wtaps = p.hwin * p.KW;
                 uint32_t acc = 0u;   // 0 until the tile's first MMA
                 const uint32_t bres_addr = smem_u32(bres);
                 // B block of tap kw: resident copy (cpt blocks per tap) or the
@@ -234,21 +239,24 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                         const uint32_t win = st_addr + sub * p.win_bytes;
                         const uint32_t b0 = p.b_res ? bres_addr + static_cast<uint32_t>(tap0 * p.cpt + c) * p.b_bytes
                                                     : win + p.a_slot;
-                        for (int kw = 0; kw < p.KW; ++kw) {
-                            const uint32_t a_addr = win + static_cast<uint32_t>(kw * p.cb);
-                            const uint32_t b_addr = b0 + kw * b_step;
-                            for (int kk = 0; kk < ksteps; ++kk) {
-                                const uint64_t da = desc_k_swizzled(a_addr + kk * 32, p.cb);
-                                const uint64_t db = desc_k_swizzled(b_addr + kk * 32, p.cb);
-                                if constexpr (I8) umma_i8(d_tmem, da, db, idesc, acc);
-                                else umma_f16_ss(d_tmem, da, db, idesc, acc);
-                                acc = 1u;
+                        // Tap (kh_i, kw) of the window: A starts kh_i*Wp + kw rows in.
+                        for (int kh_i = 0; kh_i < p.hwin; ++kh_i) {
+                            for (int kw = 0; kw < p.KW; ++kw) {
+                                const int t = kh_i * p.KW + kw;
+                                const uint32_t a_addr = win + static_cast<uint32_t>((kh_i * p.Wp + kw) * p.cb);
+                                const uint32_t b_addr = b0 + t * b_step;
+                                for (int kk = 0; kk < ksteps; ++kk) {
+                                    const uint64_t da = desc_k_swizzled(a_addr + kk * 32, p.cb);
+                                    const uint64_t db = desc_k_swizzled(b_addr + kk * 32, p.cb);
+                                    if constexpr (I8) umma_i8(d_tmem, da, db, idesc, acc);
+                                    else umma_f16_ss(d_tmem, da, db, idesc, acc);
+                                    acc = 1u;
+                                }
                             }
                         }
                         if (++c == p.cpt) {
                             c = 0;
-                            tap0 += p.KW;
-                            if (++kh == p.KH) kh = 0;
+                            tap0 += wtaps;
                         }
                     }
                     umma_commit(&empty[s]);
@@ -594,7 +602,7 @@ int chunk_bytes(const Conv3dGeom& g, int mode) {
 
 struct ConvTcLayout {
     int Dp, Hp, Wp, cb, n_mma, n_tiles, num_kb, stages, b_res, m_tiles;
-    int rows_win, num_win, kws;
+    int rows_win, num_win, kws, hwin;
     uint32_t a_slot, win_bytes;
     int64_t rows, p_last;
     size_t smem;
@@ -620,10 +628,14 @@ bool conv_layout(const Conv3dGeom& g, int mode, ConvTcLayout* L) {
     L->n_tiles = (g.OC + L->n_mma - 1) / L->n_mma;
     const int64_t cpt = static_cast<int64_t>(g.IC) * eb / cb;
     L->num_kb = static_cast<int>(cpt * g.KD * g.KH * g.KW);
-    // One A window per (kd, kh, chunk): 128 + KW - 1 rows, rounded up to 8.
-    L->rows_win = (BM + g.KW - 1 + 7) / 8 * 8;
+    // One A window per (kd, chunk) covering all KH x KW taps when
+    // 128 + (KH-1)*Wp + KW - 1 rows fit a TMA box (256 rows), else one per
+    // (kd, kh, chunk) of 128 + KW - 1 rows; rounded up to 8 rows.
+    const int64_t full_rows = BM + static_cast<int64_t>(g.KH - 1) * L->Wp + g.KW - 1;
+    L->hwin = full_rows <= 256 ? g.KH : 1;
+    L->rows_win = static_cast<int>(((L->hwin == g.KH ? full_rows : BM + g.KW - 1) + 7) / 8 * 8);
     if (L->rows_win > 256) return false;   // TMA box limit
-    L->num_win = static_cast<int>(cpt * g.KD * g.KH);
+    L->num_win = static_cast<int>(cpt * g.KD * (g.KH / L->hwin));
     L->a_bytes = static_cast<uint32_t>(L->rows_win * cb);
     L->a_slot = (L->a_bytes + 1023u) / 1024u * 1024u;
     L->b_bytes = static_cast<uint32_t>(L->n_mma * cb);
@@ -632,7 +644,7 @@ bool conv_layout(const Conv3dGeom& g, int mode, ConvTcLayout* L) {
     // The filter stays resident when it leaves room for a ring of at least
     // three input windows.
     L->b_res = L->n_tiles == 1 && fixed + bres + 3 * static_cast<size_t>(L->a_slot) <= kSmemCap ? 1 : 0;
-    L->win_bytes = L->a_slot + (L->b_res ? 0u : static_cast<uint32_t>(g.KW) * L->b_bytes);
+    L->win_bytes = L->a_slot + (L->b_res ? 0u : static_cast<uint32_t>(L->hwin * g.KW) * L->b_bytes);
     // Several windows per ring stage (up to 64 KB), preferably three stages.
     const size_t avail = kSmemCap - fixed - (L->b_res ? bres : 0);
     L->kws = 1;
@@ -785,6 +797,7 @@ cudaError_t launch_conv3d_tc(const Conv3dGeom& g, int mode, const void* inq, con
     p.stages = L.stages;
     p.b_res = L.b_res;
     p.num_win = L.num_win;
+    p.hwin = L.hwin;
     p.kws = L.kws;
     p.a_slot = L.a_slot;
     p.win_bytes = L.win_bytes;

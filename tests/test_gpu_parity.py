@@ -340,7 +340,10 @@ def _conv3d_shapes():
                             (1, 96, 2, 6, 6, 300, 1, 3, 3, 1, 1, 1, 0, 1, 1),
                             (3, 128, 2, 5, 5, 40, 3, 1, 3, 1, 1, 1, 1, 0, 1),
                             (1, 16, 6, 7, 7, 16, 5, 3, 3, 1, 1, 1, 2, 1, 1),
-                            (1, 32, 1, 2, 130, 32, 1, 1, 3, 1, 1, 1, 0, 0, 1)]
+                            (1, 32, 1, 2, 130, 32, 1, 1, 3, 1, 1, 1, 0, 0, 1),
+                            # padded width 72: a window of all 3 x 3 taps would
+                            # exceed 256 rows, so one window per filter row
+                            (1, 32, 3, 4, 70, 32, 3, 3, 3, 1, 1, 1, 1, 1, 1)]
 
 
 @pytest.mark.parametrize("p", _conv3d_shapes())
