@@ -9,12 +9,14 @@
 // viewed as rows of IC channels, output position (n, od, oh, ow) is row
 //   P = ((n*Dp + od)*Hp + oh)*Wp + ow
 // and its filter tap (kd, kh, kw) reads row P + (kd*Hp + kh)*Wp + kw, so the
-// A tiles of the KW taps kw = 0 .. KW-1 of one (kd, kh) and chunk of channels
-// for 128 consecutive rows P are rows kw .. kw+127 of ONE 2-D TMA box of
-// 128 + KW - 1 rows (a window): each tap's UMMA descriptor starts kw rows
-// into it, which the swizzled layout allows (the swizzle follows the absolute
-// shared-memory address; checked on B200).  Rows P that are not output
-// positions (the padding columns / planes) are computed and dropped.
+// A tiles of all KH x KW taps of one depth slice kd and one chunk of channels,
+// for 128 consecutive rows P, are 128-row windows at offsets kh*Wp + kw of
+// ONE 2-D TMA box of 128 + (KH-1)*Wp + KW - 1 rows (one box per filter row,
+// 128 + KW - 1 rows, when that exceeds the 256-row box limit): each tap's
+// UMMA descriptor starts that many rows into the box, which the swizzled
+// layout allows (the swizzle follows the absolute shared-memory address;
+// checked on B200).  Rows P that are not output positions (the padding
+// columns / planes) are computed and dropped.
 //
 //   output [N, OD, OH, OW, OC] = sum_k A[P, k] * filter[oc, k],
 //   k = ((kd*KH + kh)*KW + kw)*IC + ic (the reference's column order)
@@ -26,9 +28,11 @@
 //
 // A K-block is cb = 32, 64 or 128 bytes of channels of one tap, staged with
 // the matching TMA swizzle straight into the UMMA K-major layout; each ring
-// stage carries several windows (up to 64 KB: on B200 a stage costs a roughly
-// fixed mbarrier round trip of about 0.3 us, and a 128-row box about 0.12 us
-// more, so one window box instead of KW tap boxes cuts the TMA rows ~KW-fold).  With one channel tile (OC <= 256) the whole filter stays resident
+// stage carries one or more window boxes (up to 64 KB: on B200 a stage costs
+// a roughly fixed mbarrier round trip of about 0.3 us and a 128-row box about
+// 0.12 us more, so one window box instead of a box per tap cuts the TMA rows
+// several-fold).  With one channel tile (OC <= 256) the whole filter stays
+// resident
 // in shared memory, loaded with the CTA's first tile.  Roles: warp 0 TMA,
 // warp 1 TMEM + MMA issue into two accumulators, warps 2-5 epilogue (32 x 32
 // blocks transposed through swizzled shared memory into whole 128-byte row
@@ -65,10 +69,11 @@ struct ConvTcParams {
     int p_last;                 // padded row of the last output position
     int cb, celems, cpt, num_kb;   // K-block bytes / elements, K-blocks per tap, total
     int n_mma, stages, b_res;
-    // Windows: one A box of rows_win = 128 + KW - 1 (rounded up to 8) rows
-    // per (kd, kh, channel chunk) serves the KW taps kw = 0 .. KW-1, whose A
-    // operands start kw rows into it (the UMMA descriptor may start at any
-    // row of a swizzled tile: the swizzle follows the absolute address).
+    // Windows: one A box of rows_win rows (128 + (hwin-1)*Wp + KW - 1,
+    // rounded up to 8) per (kd, group of hwin filter rows, channel chunk)
+    // serves hwin*KW taps, whose A operands start kh*Wp + kw rows into it
+    // (the UMMA descriptor may start at any row of a swizzled tile: the
+    // swizzle follows the absolute address).
     int num_win, kws;           // windows per tile (KD*(KH/hwin)*cpt), windows per ring stage
     int hwin;                   // filter rows per window: KH when 128 + (KH-1)*Wp + KW - 1 <= 256 rows, else 1
     uint32_t a_slot, win_bytes; // A box slot (1024-byte multiple); A slot + KW B blocks unless resident
