@@ -355,7 +355,10 @@ def per_config(torch, dn, stream, pk, world, rank, dist):
         r = bench_single(torch, dn, s, fns, 4 * (nin + nflt + nout), flops, iters=10)
         out[f"conv3d_{name}_1x64x8x56x56_oc64_k3"] = {
             "TFLOP_s": r["TFLOP_s"], "us": r["us_per_call"],
-            "note": "im2col in the compute precision + library GEMM + bias/relu pass"}
+            "note": {"fp32": "SIMT implicit GEMM gathering A from the input, bias/relu in its epilogue",
+                     "bf16": "padded BF16 copy + implicit tcgen05 kind::f16 conv (window boxes), bias/relu in its epilogue",
+                     "int8": "cooperative absmax/quantised padded copy + implicit tcgen05 kind::i8 conv, "
+                             "dequant/bias/relu in its epilogue"}[name]}
     del cin, cflt, cbias, cout
     # C3: INT8 4 x 11008 x 4096, B is [N, K].
     M, N, K = 4, 11008, 4096

@@ -126,9 +126,14 @@ __device__ __forceinline__ float conv_post(float v, const float* bias, int oc, i
 }
 
 // I8: kind::i8 with int32 accumulators (INT8), else kind::f16 (BF16, FP32
-// accumulators).  A compile-time choice: a run-time branch between the two MMA
-// forms in the issue loop measured twice the issue time per MMA on B200.
-template <bool I8>
+// accumulators).  KS: MMAs per tap and channel chunk (cb / 32).  Both
+// compile-time: on B200 one thread issuing tcgen05.mma at N = 64 is bound by
+// its own instruction stream (a straight-line sequence measured ~54 cycles
+// per MMA, the math ~32), and every run-time branch in the loop adds to it — a
+// branch between the two MMA forms doubled the cost, nested tap / K-step
+// loops made the conv kernel ~20 % (INT8) and ~27 % (BF16) slower than this
+// flat loop.
+template <bool I8, int KS>
 __global__ void __launch_bounds__(kThreads, 1)
 conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const ConvTcParams p) {
@@ -218,7 +223,6 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             const uint32_t idesc = conv_idesc(I8 ? 1 : 0, p.n_mma);
-            const int ksteps = p.cb / 32;   // 32 bytes of K per MMA (K = 32 int8 or 16 bf16)
             uint32_t it = 0, titer = 0;
             bool ok = true;
             for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++titer) {
@@ -233,7 +237,10 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 // B block of tap kw: resident copy (cpt blocks per tap) or the
                 // window's own KW blocks; chosen once per window so that the
                 // issue loop is branch-free.
-                const uint32_t b_step = p.b_res ? static_cast<uint32_t>(p.cpt) * p.b_bytes : p.b_bytes;
+                const uint32_t b_step16 = (p.b_res ? static_cast<uint32_t>(p.cpt) * p.b_bytes : p.b_bytes) >> 4;
+                constexpr uint32_t cb16 = 2u * KS;   // one row of the chunk, in 16-byte units
+                // From tap (kh, KW-1) to tap (kh+1, 0): Wp - KW + 1 rows down.
+                const uint32_t a_wrap = static_cast<uint32_t>(p.Wp - p.KW + 1) * cb16;
                 for (int w = 0; w < p.num_win; w += p.kws, ++it) {
                     const uint32_t s = it % p.stages, ph = (it / p.stages) & 1u;
                     if (!mbar_wait(&full[s], ph, abort_flag, p.err)) { ok = false; break; }
@@ -244,20 +251,31 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                         const uint32_t win = st_addr + sub * p.win_bytes;
                         const uint32_t b0 = p.b_res ? bres_addr + static_cast<uint32_t>(tap0 * p.cpt + c) * p.b_bytes
                                                     : win + p.a_slot;
-                        // Tap (kh_i, kw) of the window: A starts kh_i*Wp + kw rows in.
-                        for (int kh_i = 0; kh_i < p.hwin; ++kh_i) {
-                            for (int kw = 0; kw < p.KW; ++kw) {
-                                const int t = kh_i * p.KW + kw;
-                                const uint32_t a_addr = win + static_cast<uint32_t>((kh_i * p.Wp + kw) * p.cb);
-                                const uint32_t b_addr = b0 + t * b_step;
-                                for (int kk = 0; kk < ksteps; ++kk) {
-                                    const uint64_t da = desc_k_swizzled(a_addr + kk * 32, p.cb);
-                                    const uint64_t db = desc_k_swizzled(b_addr + kk * 32, p.cb);
-                                    if constexpr (I8) umma_i8(d_tmem, da, db, idesc, acc);
-                                    else umma_f16_ss(d_tmem, da, db, idesc, acc);
-                                    acc = 1u;
-                                }
+                        // Descriptors of the window's first tap; tap (kh_i, kw)
+                        // starts kh_i*Wp + kw rows into the A box and K step kk
+                        // 32 bytes further.  The start address field holds
+                        // address >> 4 in bits 0-13 and shared-memory addresses
+                        // stay below 2^18, so these offsets (in 16-byte units)
+                        // are added to the descriptor without a carry.
+                        const uint64_t da0 = desc_k_swizzled(win, KS * 32);
+                        const uint64_t db0 = desc_k_swizzled(b0, KS * 32);
+                        // Taps in (kh_i, kw) order as one flat loop; the step to
+                        // the next tap's A rows is a select, not a nested loop.
+                        uint32_t a_off = 0u, b_off = 0u;
+                        int kw = 0;
+                        for (int t = 0; t < wtaps; ++t) {
+#pragma unroll
+                            for (int kk = 0; kk < KS; ++kk) {
+                                const uint64_t da = da0 + (a_off + 2u * kk);
+                                const uint64_t db = db0 + (b_off + 2u * kk);
+                                if constexpr (I8) umma_i8(d_tmem, da, db, idesc, acc);
+                                else umma_f16_ss(d_tmem, da, db, idesc, acc);
+                                acc = 1u;
                             }
+                            const bool wrap = ++kw == p.KW;
+                            kw = wrap ? 0 : kw;
+                            a_off += wrap ? a_wrap : cb16;
+                            b_off += b_step16;
                         }
                         if (++c == p.cpt) {
                             c = 0;
@@ -827,12 +845,16 @@ cudaError_t launch_conv3d_tc(const Conv3dGeom& g, int mode, const void* inq, con
     {
         std::lock_guard<std::mutex> lk(mu);
         if (!done.count(dev)) {
-            e = cudaFuncSetAttribute(conv3d_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(kSmemCap));
-            if (e == cudaSuccess)
-                e = cudaFuncSetAttribute(conv3d_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kSmemCap));
-            if (e != cudaSuccess) return e;
+            const void* fns[6] = {reinterpret_cast<const void*>(conv3d_tc_kernel<true, 1>),
+                                  reinterpret_cast<const void*>(conv3d_tc_kernel<true, 2>),
+                                  reinterpret_cast<const void*>(conv3d_tc_kernel<true, 4>),
+                                  reinterpret_cast<const void*>(conv3d_tc_kernel<false, 1>),
+                                  reinterpret_cast<const void*>(conv3d_tc_kernel<false, 2>),
+                                  reinterpret_cast<const void*>(conv3d_tc_kernel<false, 4>)};
+            for (const void* fn : fns) {
+                e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemCap));
+                if (e != cudaSuccess) return e;
+            }
             done[dev] = true;
         }
     }
@@ -846,8 +868,14 @@ cudaError_t launch_conv3d_tc(const Conv3dGeom& g, int mode, const void* inq, con
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return mode == 2 ? cudaLaunchKernelEx(&cfg, conv3d_tc_kernel<true>, tmA, tmB, p)
-                     : cudaLaunchKernelEx(&cfg, conv3d_tc_kernel<false>, tmA, tmB, p);
+    // MMAs per tap and chunk: cb / 32 (cb is 32, 64 or 128).
+    if (mode == 2)
+        return L.cb == 128 ? cudaLaunchKernelEx(&cfg, conv3d_tc_kernel<true, 4>, tmA, tmB, p)
+             : L.cb == 64  ? cudaLaunchKernelEx(&cfg, conv3d_tc_kernel<true, 2>, tmA, tmB, p)
+                           : cudaLaunchKernelEx(&cfg, conv3d_tc_kernel<true, 1>, tmA, tmB, p);
+    return L.cb == 128 ? cudaLaunchKernelEx(&cfg, conv3d_tc_kernel<false, 4>, tmA, tmB, p)
+         : L.cb == 64  ? cudaLaunchKernelEx(&cfg, conv3d_tc_kernel<false, 2>, tmA, tmB, p)
+                       : cudaLaunchKernelEx(&cfg, conv3d_tc_kernel<false, 1>, tmA, tmB, p);
 }
 
 }  // namespace dnnopt_b200
